@@ -1,0 +1,762 @@
+// BF16 GEMM on the sm_100a tensor cores: C = epilogue(A . W^T).
+//
+// One persistent kernel family serves every dense projection of the decoders (the packed
+// q/k/v projection, the output projection, gate/up with its SwiGLU, down, and the vocabulary
+// head). It replaces the reference's Tensor-Unit contractions
+// (crates/furiosa-opt-models/src/ops/linear/{mod,kernel,rows}.rs, ops/swiglu/mod.rs:1-8) with a
+// design for Blackwell:
+//
+// - Warp roles, 192 threads: warp 0 issues TMA loads (one elected thread), warp 1 allocates TMEM
+//   and issues tcgen05.mma (one elected thread), warps 2-5 drain the FP32 accumulators from TMEM
+//   with tcgen05.ld and apply the epilogue in registers.
+// - Operands are staged by TMA with 128-byte swizzling into a ring of shared-memory stages
+//   guarded by full/empty mbarriers; MMAs read them through K-major shared-memory descriptors.
+// - Accumulators live in TMEM, double-buffered where they fit, so the epilogue of one tile
+//   overlaps the MMAs of the next.
+// - Two operand mappings: "rows" (activations on the MMA's M side, 128 x 256 tiles) for prefill
+//   and "swap" (weight rows on M, the few activation rows on N) for decode, where a 64-row batch
+//   would waste half of a 128-row MMA.
+// - Split-K for launches with fewer tiles than SMs: each split writes FP32 partials to scratch and
+//   the last split of a tile (an arrival counter) adds them in split order, so the result does not
+//   depend on which split finishes first.
+//
+// Numerics: FP32 accumulation, one rounding to BF16 (after the residual add where there is one),
+// as the reference's contractions round once (ops/pointwise/add.rs:1).
+
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "sm100.cuh"
+#include "tmap.cuh"
+
+namespace foa {
+namespace {
+
+constexpr int kBlockK = 64;  // 64 BF16 = 128 bytes: one swizzled row
+constexpr int kThreads = 192;
+
+struct KParams {
+  int Mp, Nq;                 // rows of the M-side and N-side operands
+  int tiles_p, tiles_q;       // tile counts along M and N
+  int splits, kblocks, kb_per_split;
+  int units;                  // tiles * splits
+  int swap;                   // 1: C[j, i] (N-side rows are output rows)
+  void* c;
+  long ldc;
+  const __nv_bfloat16* res;
+  long ldr;
+  float* ws;
+  int* counters;
+  int* status;
+  int out_rows, out_cols;     // logical output shape
+};
+
+template <int kMB, int kBN, int kStages, int kAcc>
+struct Cfg {
+  static constexpr int kPRows = 128 * kMB;
+  static constexpr int kPBytes = kPRows * 128;
+  static constexpr int kQBytes = kBN * 128;
+  static constexpr int kStageBytes = kPBytes + kQBytes;
+  static constexpr int kAccCols = kMB * kBN;
+  static constexpr int kColsRaw = kAcc * kAccCols;
+  static constexpr int kTmemCols = kColsRaw <= 32    ? 32
+                                   : kColsRaw <= 64  ? 64
+                                   : kColsRaw <= 128 ? 128
+                                   : kColsRaw <= 256 ? 256
+                                                     : 512;
+  static constexpr int kBarrierBytes = 256;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static_assert(kColsRaw <= 512, "accumulators exceed TMEM");
+  static_assert(kSmemBytes <= 232448, "stages exceed shared memory");
+  static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "invalid MMA N");
+};
+
+__device__ __forceinline__ void epi_barrier() {
+  asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__device__ __forceinline__ float silu_bf16_times(float g_acc, float u_acc) {
+  // Rounded as the reference's SwiGLU rounds: each projection to BF16, SiLU(gate) to BF16, then
+  // the product to BF16 by the caller.
+  const float g = __bfloat162float(__float2bfloat16_rn(g_acc));
+  const float u = __bfloat162float(__float2bfloat16_rn(u_acc));
+  const float s = __bfloat162float(__float2bfloat16_rn(g / (1.0f + __expf(-g))));
+  return s * u;
+}
+
+// Stores 16 consecutive output values of one output row (rows mapping) or one output column
+// (swap mapping), applying the residual add and the output type of the epilogue.
+template <int kEpi>
+__device__ __forceinline__ void store16(const KParams& p, int row, int col, const float (&v)[16],
+                                        bool along_row) {
+  // along_row: the 16 values are C[row, col + t]; otherwise C[row + t, col].
+  if (kEpi == kEpiF32) {
+    float* c = static_cast<float*>(p.c);
+    if (along_row) {
+      if (row >= p.out_rows) return;
+      float* dst = c + (long)row * p.ldc + col;
+      if (col + 16 <= p.out_cols) {
+#pragma unroll
+        for (int t = 0; t < 16; t += 4)
+          *reinterpret_cast<float4*>(dst + t) = make_float4(v[t], v[t + 1], v[t + 2], v[t + 3]);
+      } else {
+        for (int t = 0; t < 16 && col + t < p.out_cols; ++t) dst[t] = v[t];
+      }
+    } else {
+      if (col >= p.out_cols) return;
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        if (row + t < p.out_rows) c[(long)(row + t) * p.ldc + col] = v[t];
+    }
+    return;
+  }
+  __nv_bfloat16* c = static_cast<__nv_bfloat16*>(p.c);
+  if (along_row) {
+    if (row >= p.out_rows) return;
+    float w[16];
+#pragma unroll
+    for (int t = 0; t < 16; ++t) w[t] = v[t];
+    if (p.res != nullptr) {
+      const __nv_bfloat16* r = p.res + (long)row * p.ldr + col;
+      for (int t = 0; t < 16; ++t)
+        if (col + t < p.out_cols) w[t] += __bfloat162float(r[t]);
+    }
+    __nv_bfloat16* dst = c + (long)row * p.ldc + col;
+    if (col + 16 <= p.out_cols) {
+      uint4 lo = make_uint4(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]),
+                            pack_bf16x2(w[4], w[5]), pack_bf16x2(w[6], w[7]));
+      uint4 hi = make_uint4(pack_bf16x2(w[8], w[9]), pack_bf16x2(w[10], w[11]),
+                            pack_bf16x2(w[12], w[13]), pack_bf16x2(w[14], w[15]));
+      reinterpret_cast<uint4*>(dst)[0] = lo;
+      reinterpret_cast<uint4*>(dst)[1] = hi;
+    } else {
+      for (int t = 0; t < 16 && col + t < p.out_cols; ++t) dst[t] = __float2bfloat16_rn(w[t]);
+    }
+  } else {
+    if (col >= p.out_cols) return;
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int r = row + t;
+      if (r < p.out_rows) {
+        float x = v[t];
+        if (p.res != nullptr) x += __bfloat162float(p.res[(long)r * p.ldr + col]);
+        c[(long)r * p.ldc + col] = __float2bfloat16_rn(x);
+      }
+    }
+  }
+}
+
+// kRed: how K splits meet. kRedNone: one split. kRedGlobal: FP32 partials in global scratch, the
+// last split of a tile (arrival counter) adds them in split order. kRedCluster: the splits of a tile
+// form one thread-block cluster; each stages its partial in its own shared memory and every CTA
+// reduces a slice of the tile's rows over distributed shared memory, in split order.
+enum : int { kRedNone = 0, kRedGlobal = 1, kRedCluster = 2 };
+
+template <int kEpi>
+__device__ __forceinline__ void store_one(const KParams& p, int row, int col, float v) {
+  if (row >= p.out_rows || col >= p.out_cols) return;
+  if (kEpi == kEpiF32) {
+    static_cast<float*>(p.c)[(long)row * p.ldc + col] = v;
+    return;
+  }
+  if (p.res != nullptr) v += __bfloat162float(p.res[(long)row * p.ldr + col]);
+  static_cast<__nv_bfloat16*>(p.c)[(long)row * p.ldc + col] = __float2bfloat16_rn(v);
+}
+
+template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP,
+                     const __grid_constant__ CUtensorMap tmQ, const KParams p) {
+  using C = Cfg<kMB, kBN, kStages, kAcc>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint64_t* empty = full + kStages;
+  uint64_t* tfull = empty + kStages;
+  uint64_t* tempty = tfull + kAcc;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kAcc);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < kAcc; ++b) {
+      mbar_init(tfull + b, 1);
+      mbar_init(tempty + b, 128);
+    }
+    *abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmP);
+    tma_prefetch_desc(&tmQ);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ----------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const int tile = u / p.splits, split = u % p.splits;
+        const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(empty + s, ph ^ 1, p.status, kTimeoutSmemEmpty, abort)) {
+            ok = false;
+            break;
+          }
+          uint8_t* st = smem + s * C::kStageBytes;
+          mbar_arrive_expect_tx(full + s, C::kStageBytes);
+          tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
+          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+        }
+      }
+      if (!ok) {
+        // Drain: let every load issued into the ring land before the CTA exits.
+        const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0;
+        for (uint32_t j = first; j < it; ++j)
+          mbar_wait(full + (j % kStages), (j / kStages) & 1, p.status, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ----------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, kBN);
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++tc) {
+        const int split = u % p.splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+        const int b = tc % kAcc;
+        const uint32_t aph = (tc / kAcc) & 1;
+        if (!mbar_wait(tempty + b, aph ^ 1, p.status, kTimeoutTmemEmpty, abort)) break;
+        tc_fence_after();
+        const uint32_t d0 = tmem_base + b * C::kAccCols;
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          if (!mbar_wait(full + s, ph, p.status, kTimeoutTmaFull, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint8_t* st = smem + s * C::kStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBlockK / 16; ++kk) {
+            const uint64_t bdesc = sdesc_kmajor_sw128(st + C::kPBytes + kk * 32);
+#pragma unroll
+            for (int mb = 0; mb < kMB; ++mb) {
+              const uint64_t adesc = sdesc_kmajor_sw128(st + mb * 16384 + kk * 32);
+              mma_bf16(d0 + mb * kBN, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+            }
+          }
+          mma_commit(empty + s);
+        }
+        if (ok) mma_commit(tfull + b);
+      }
+    }
+  } else {
+    // ----------------------------------------------------------------- epilogue (4 warps)
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int lrow = q * 32 + lane;
+    uint32_t tc = 0;
+    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tc) {
+      const int tile = u / p.splits, split = u % p.splits;
+      const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
+      const int b = tc % kAcc;
+      const uint32_t aph = (tc / kAcc) & 1;
+      if (!mbar_wait(tfull + b, aph, p.status, kTimeoutTmemFull, abort)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols;
+
+      auto tmem16 = [&](int mb, int c0, float (&v)[16]) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(tbase + mb * kBN + c0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = __uint_as_float(r[t]);
+      };
+      // Partials are stored column-major ([col][row]) so a warp's 32 rows are 128 contiguous bytes.
+      const long tile_elems = (long)C::kPRows * kBN;
+      auto ws_at = [&](int s, int mb, int c) {
+        return p.ws + ((long)tile * p.splits + s) * tile_elems + (long)c * C::kPRows + mb * 128 + lrow;
+      };
+      if (kRed == kRedCluster) continue;  // pushed after the cluster barrier below
+      bool from_ws = false;
+      if (kRed == kRedGlobal && p.splits > 1) {
+        for (int mb = 0; mb < kMB; ++mb)
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            float v[16];
+            tmem16(mb, c0, v);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) __stcg(ws_at(split, mb, c0 + t), v[t]);
+          }
+        tc_fence_before();
+        mbar_arrive(tempty + b);
+        __threadfence();
+        epi_barrier();
+        if (lrow == 0) {
+          const int old = atomicAdd(p.counters + tile, 1);
+          const int last = (old == p.splits - 1);
+          if (last) p.counters[tile] = 0;
+          *last_flag = last;
+        }
+        epi_barrier();
+        if (!*last_flag) continue;
+        __threadfence();
+        from_ws = true;
+      }
+      auto get16 = [&](int mb, int c0, float (&v)[16]) {
+        if (!from_ws) {
+          tmem16(mb, c0, v);
+          return;
+        }
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] = 0.f;
+        for (int s = 0; s < p.splits; ++s) {
+          float x[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) x[t] = __ldcg(ws_at(s, mb, c0 + t));
+#pragma unroll
+          for (int t = 0; t < 16; ++t) v[t] += x[t];
+        }
+      };
+
+      if (kEpi == kEpiSwiGLU) {
+        if (!p.swap) {
+          // Rows mapping: the tile's first kBN/2 columns are gate rows, the rest up rows.
+          const int row = tp * C::kPRows + lrow;
+          for (int c0 = 0; c0 < kBN / 2; c0 += 16) {
+            float g[16], v[16];
+            get16(0, c0, g);
+            get16(0, c0 + kBN / 2, v);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = silu_bf16_times(g[t], v[t]);
+            store16<kEpiBf16>(p, row, tq * (kBN / 2) + c0, v, true);
+          }
+        } else {
+          // Swap mapping: M block 0 holds gate rows, block 1 the up rows of the same features.
+          const int feature = tp * 128 + lrow;
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            float g[16], v[16];
+            get16(0, c0, g);
+            get16(1, c0, v);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) v[t] = silu_bf16_times(g[t], v[t]);
+            store16<kEpiBf16>(p, tq * kBN + c0, feature, v, false);
+          }
+        }
+      } else {
+        for (int mb = 0; mb < kMB; ++mb) {
+          const int i = tp * C::kPRows + mb * 128 + lrow;
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            float v[16];
+            get16(mb, c0, v);
+            const int j = tq * kBN + c0;
+            if (!p.swap)
+              store16<kEpi>(p, i, j, v, true);
+            else
+              store16<kEpi>(p, j, i, v, false);
+          }
+        }
+      }
+      if (!from_ws) {
+        tc_fence_before();
+        mbar_arrive(tempty + b);
+      }
+    }
+  }
+
+  if (kRed == kRedCluster) {
+    // 1. Every CTA of the cluster has drained its MMAs (its epilogue saw the accumulator
+    //    complete), so every operand ring is idle and may receive partials.
+    cluster_sync();
+    // 2. Push this split's partial into the shared memory of the CTA that reduces each row;
+    //    DSMEM stores do not stall. Receive layout per CTA: [split][half][col][row of slice].
+    if (warp >= 2 && !*abort) {
+      const int q = warp & 3;
+      const int lrow = q * 32 + lane;
+      const int S = p.splits;
+      const int split = blockIdx.x % S;
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16);
+      const uint32_t red = smem_u32(smem);
+      for (int mb = 0; mb < kMB; ++mb) {
+        int owner, rl, rs, half;
+        if (kEpi == kEpiSwiGLU) {
+          rs = (128 + S - 1) / S;
+          owner = lrow / rs;
+          rl = lrow % rs;
+          half = mb;
+        } else {
+          rs = (C::kPRows + S - 1) / S;
+          const int r = mb * 128 + lrow;
+          owner = r / rs;
+          rl = r % rs;
+          half = 0;
+        }
+        const int halves = kEpi == kEpiSwiGLU ? 2 : 1;
+        const uint32_t base =
+            dsmem_addr(red, owner) + 4u * (uint32_t)(((split * halves + half) * kBN) * rs + rl);
+        for (int c0 = 0; c0 < kBN; c0 += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tbase + mb * kBN + c0, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            dsmem_st_f32(base + 4u * (uint32_t)((c0 + t) * rs), __uint_as_float(r[t]));
+        }
+      }
+      tc_fence_before();
+    }
+    // 3. Every partial has landed; each CTA adds its slice in split order.
+    cluster_sync();
+    if (warp >= 2) {
+      const int tid = threadIdx.x - 64;
+      const int S = p.splits;
+      const int rank = (int)cluster_rank();
+      const int tile = blockIdx.x / S;
+      const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
+      const float* red = reinterpret_cast<const float*>(smem);
+      if (kEpi == kEpiSwiGLU) {
+        const int rs = (128 + S - 1) / S;
+        for (int e = tid; e < rs * kBN; e += 128) {
+          const int rl = e % rs, c = e / rs;
+          const int f = rank * rs + rl;
+          if (f >= 128) continue;
+          float g = 0.f, u = 0.f;
+          for (int s = 0; s < S; ++s) {
+            g += red[((s * 2 + 0) * kBN + c) * rs + rl];
+            u += red[((s * 2 + 1) * kBN + c) * rs + rl];
+          }
+          store_one<kEpiBf16>(p, tq * kBN + c, tp * 128 + f, silu_bf16_times(g, u));
+        }
+      } else {
+        const int rs = (C::kPRows + S - 1) / S;
+        for (int e = tid; e < rs * kBN; e += 128) {
+          const int rl = e % rs, c = e / rs;
+          const int r = rank * rs + rl;
+          if (r >= C::kPRows) continue;
+          float v = 0.f;
+          for (int s = 0; s < S; ++s) v += red[(s * kBN + c) * rs + rl];
+          store_one<kEpi>(p, tq * kBN + c, tp * C::kPRows + r, v);
+        }
+      }
+    }
+  } else {
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------------------ host side
+
+int g_num_sms[64] = {0};
+
+int device_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (g_num_sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms[dev] = n > 0 ? n : 148;
+  }
+  return g_num_sms[dev];
+}
+
+struct Plan {
+  int swap, kbn, mb, red;
+  int tiles_p, tiles_q, splits, kb_per_split, kblocks, units, grid;
+};
+
+int pick_swap_bn(int m) {
+  if (m <= 16) return 16;
+  if (m <= 32) return 32;
+  if (m <= 64) return 64;
+  if (m <= 128) return 128;
+  return 256;
+}
+
+// Shared-memory bytes of the operand ring of a swap-mapping configuration (see launch_swap).
+int swap_ring_bytes(int mb, int kbn) {
+  const int stage = 128 * mb * 128 + kbn * 128;
+  int stages = 0;
+  if (mb == 1) stages = kbn <= 32 ? 8 : kbn == 64 ? 8 : kbn == 128 ? 6 : 4;
+  else stages = kbn <= 32 ? 6 : kbn == 64 ? 5 : kbn == 128 ? 4 : 3;
+  return stage * stages;
+}
+
+using ClusterLimit = int (*)(int mb, int kbn, int epilogue, int size);
+int cluster_limit_of(int mb, int kbn, int epi, int size);
+
+Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len,
+               ClusterLimit cluster_limit = cluster_limit_of) {
+  Plan pl{};
+  const bool swap = a.mode == kModeSwap || (a.mode == kModeAuto && a.M <= 256);
+  pl.swap = swap;
+  pl.kblocks = (a.K + kBlockK - 1) / kBlockK;
+  if (!swap) {
+    pl.mb = 1;
+    pl.kbn = 256;
+    pl.tiles_p = (a.M + 127) / 128;
+    pl.tiles_q = (a.N + 255) / 256;
+  } else {
+    pl.mb = a.epilogue == kEpiSwiGLU ? 2 : 1;
+    pl.kbn = pick_swap_bn(a.M);
+    pl.tiles_p = (a.N + 128 * pl.mb - 1) / (128 * pl.mb);
+    pl.tiles_q = (a.M + pl.kbn - 1) / pl.kbn;
+  }
+  const int tiles = pl.tiles_p * pl.tiles_q;
+  int splits = a.splits;
+  if (splits <= 0) {
+    splits = 1;
+    if (tiles * 2 <= num_sms) splits = std::min(8, num_sms / tiles);
+    splits = std::min(splits, std::max(1, pl.kblocks / 2));
+  }
+  splits = std::max(1, std::min(splits, pl.kblocks));
+  const size_t red_bytes = (size_t)128 * pl.mb * pl.kbn * sizeof(float);
+  const size_t recv_bytes = (size_t)(128 * pl.mb + 2 * splits) * pl.kbn * sizeof(float);
+  const bool cluster_fits =
+      pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn);
+  pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
+  if (pl.red == 1) {
+    // Global scratch bounds the split count.
+    while (splits > 1 && ((size_t)tiles * splits * red_bytes > ws_bytes || tiles > counters_len))
+      --splits;
+    if (splits == 1) pl.red = 0;
+  }
+  pl.kb_per_split = (pl.kblocks + splits - 1) / splits;
+  pl.splits = (pl.kblocks + pl.kb_per_split - 1) / pl.kb_per_split;
+  if (pl.splits == 1) pl.red = 0;
+  if (pl.red == 2 && cluster_limit != nullptr) {
+    // All clusters must be resident in one wave: shrink the split count until they are.
+    while (pl.splits > 1 && tiles > cluster_limit(pl.mb, pl.kbn, a.epilogue, pl.splits)) {
+      const int want = pl.splits - 1;
+      pl.kb_per_split = (pl.kblocks + want - 1) / want;
+      pl.splits = (pl.kblocks + pl.kb_per_split - 1) / pl.kb_per_split;
+    }
+    if (pl.splits == 1) pl.red = 0;
+  }
+  pl.units = tiles * pl.splits;
+  pl.grid = pl.red == 2 ? pl.units : std::min(pl.units, num_sms);
+  return pl;
+}
+
+template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed>
+int launch(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, const Plan& pl,
+           cudaStream_t stream) {
+  using C = Cfg<kMB, kBN, kStages, kAcc>;
+  auto kernel = gemm_bf16_kernel<kMB, kBN, kStages, kAcc, kEpi, kRed>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!configured[dev & 63]) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    configured[dev & 63] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(pl.grid);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = C::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  if (kRed == kRedCluster) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = pl.splits;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, tp, tq, kp);
+  return err == cudaSuccess ? 0 : -5;
+}
+
+// Clusters of `size` CTAs of this configuration that the device holds at once (cached).
+template <int kMB, int kBN, int kStages, int kAcc, int kEpi>
+int max_active_clusters(int size) {
+  using C = Cfg<kMB, kBN, kStages, kAcc>;
+  static int cache[64][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& slot = cache[dev & 63][size];
+  if (slot == 0) {
+    auto kernel = gemm_bf16_kernel<kMB, kBN, kStages, kAcc, kEpi, kRedCluster>;
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(size * 64);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = C::kSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = size;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kernel, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 148 / size;
+    }
+    slot = n;
+  }
+  return slot;
+}
+
+template <int kMB, int kBN, int kStages, int kAcc, int kEpi>
+int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, const Plan& pl,
+               cudaStream_t stream) {
+  switch (pl.red) {
+    case kRedNone:
+      return launch<kMB, kBN, kStages, kAcc, kEpi, kRedNone>(tp, tq, kp, pl, stream);
+    case kRedGlobal:
+      return launch<kMB, kBN, kStages, kAcc, kEpi, kRedGlobal>(tp, tq, kp, pl, stream);
+    default:
+      if constexpr (kMB * kBN * 128 * 4 <= 232448 - 2048)
+        return launch<kMB, kBN, kStages, kAcc, kEpi, kRedCluster>(tp, tq, kp, pl, stream);
+      return -2;
+  }
+}
+
+template <int kMB, int kBN, int kStages, int kAcc>
+int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp,
+                     const Plan& pl, cudaStream_t stream) {
+  if (epi == kEpiBf16) return launch_red<kMB, kBN, kStages, kAcc, kEpiBf16>(tp, tq, kp, pl, stream);
+  if (epi == kEpiF32) return launch_red<kMB, kBN, kStages, kAcc, kEpiF32>(tp, tq, kp, pl, stream);
+  return -2;
+}
+
+int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp,
+                const Plan& pl, cudaStream_t stream) {
+  if (pl.mb == 2) {
+    if (epi != kEpiSwiGLU) return -2;
+    switch (pl.kbn) {
+      case 16: return launch_red<2, 16, 6, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+      case 32: return launch_red<2, 32, 6, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+      case 64: return launch_red<2, 64, 5, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+      case 128: return launch_red<2, 128, 4, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+      default: return launch_red<2, 256, 3, 1, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+    }
+  }
+  switch (pl.kbn) {
+    case 16: return launch_plain_epi<1, 16, 8, 2>(epi, tp, tq, kp, pl, stream);
+    case 32: return launch_plain_epi<1, 32, 8, 2>(epi, tp, tq, kp, pl, stream);
+    case 64: return launch_plain_epi<1, 64, 8, 2>(epi, tp, tq, kp, pl, stream);
+    case 128: return launch_plain_epi<1, 128, 6, 2>(epi, tp, tq, kp, pl, stream);
+    default: return launch_plain_epi<1, 256, 4, 2>(epi, tp, tq, kp, pl, stream);
+  }
+}
+
+int cluster_limit_of(int mb, int kbn, int epi, int size) {
+  if (mb == 2) {
+    switch (kbn) {
+      case 16: return max_active_clusters<2, 16, 6, 2, kEpiSwiGLU>(size);
+      case 32: return max_active_clusters<2, 32, 6, 2, kEpiSwiGLU>(size);
+      case 64: return max_active_clusters<2, 64, 5, 2, kEpiSwiGLU>(size);
+      default: return max_active_clusters<2, 128, 4, 2, kEpiSwiGLU>(size);
+    }
+  }
+  const bool f32 = epi == kEpiF32;
+  switch (kbn) {
+    case 16: return f32 ? max_active_clusters<1, 16, 8, 2, kEpiF32>(size) : max_active_clusters<1, 16, 8, 2, kEpiBf16>(size);
+    case 32: return f32 ? max_active_clusters<1, 32, 8, 2, kEpiF32>(size) : max_active_clusters<1, 32, 8, 2, kEpiBf16>(size);
+    case 64: return f32 ? max_active_clusters<1, 64, 8, 2, kEpiF32>(size) : max_active_clusters<1, 64, 8, 2, kEpiBf16>(size);
+    case 128: return f32 ? max_active_clusters<1, 128, 6, 2, kEpiF32>(size) : max_active_clusters<1, 128, 6, 2, kEpiBf16>(size);
+    default: return f32 ? max_active_clusters<1, 256, 4, 2, kEpiF32>(size) : max_active_clusters<1, 256, 4, 2, kEpiBf16>(size);
+  }
+}
+
+}  // namespace
+
+void gemm_bf16_scratch(const GemmArgs& args, size_t* workspace_bytes, int* counters) {
+  const int sms = args.num_sms > 0 ? args.num_sms : device_sms();
+  Plan pl = make_plan(args, sms, ~size_t(0) >> 1, 1 << 30, nullptr);
+  const bool global = pl.red == 1;
+  *workspace_bytes =
+      global ? (size_t)pl.tiles_p * pl.tiles_q * pl.splits * 128 * pl.mb * pl.kbn * 4 : 0;
+  *counters = global ? pl.tiles_p * pl.tiles_q : 0;
+}
+
+int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return -2;
+  if (a.K % 8 != 0 || a.lda % 8 != 0 || a.ldw % 8 != 0) return -1;
+  if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15)) return -1;
+  if (a.epilogue == kEpiSwiGLU && (a.N % 256 != 0 || a.residual != nullptr)) return -2;
+  if (a.epilogue != kEpiF32 && (a.ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
+  if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
+  if (a.residual != nullptr && a.epilogue != kEpiBf16) return -2;
+
+  const int sms = a.num_sms > 0 ? a.num_sms : device_sms();
+  const Plan pl = make_plan(a, sms, a.workspace ? a.workspace_bytes : 0,
+                            a.counters ? a.counters_len : 0);
+
+  KParams kp{};
+  kp.tiles_p = pl.tiles_p;
+  kp.tiles_q = pl.tiles_q;
+  kp.splits = pl.splits;
+  kp.kblocks = pl.kblocks;
+  kp.kb_per_split = pl.kb_per_split;
+  kp.units = pl.units;
+  kp.swap = pl.swap;
+  kp.c = a.c;
+  kp.ldc = a.ldc;
+  kp.res = static_cast<const __nv_bfloat16*>(a.residual);
+  kp.ldr = a.ldr;
+  kp.ws = a.workspace;
+  kp.counters = a.counters;
+  kp.status = a.status;
+  kp.out_rows = a.M;
+  kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
+  if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
+
+  CUtensorMap tp, tq;
+  const int prow_box = 128 * pl.mb;
+  if (!pl.swap) {
+    kp.Mp = a.M;
+    kp.Nq = a.N;
+    if (!encode_tmap_bf16_kmajor(&tp, a.a, a.M, a.K, a.lda, prow_box)) return -4;
+    if (!encode_tmap_bf16_kmajor(&tq, a.w, a.N, a.K, a.ldw, pl.kbn)) return -4;
+    if (pl.red == 2) return -2;
+    switch (a.epilogue) {
+      case kEpiBf16: return launch_red<1, 256, 4, 2, kEpiBf16>(tp, tq, kp, pl, stream);
+      case kEpiF32: return launch_red<1, 256, 4, 2, kEpiF32>(tp, tq, kp, pl, stream);
+      case kEpiSwiGLU: return launch_red<1, 256, 4, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+    }
+    return -2;
+  }
+  kp.Mp = a.N;
+  kp.Nq = a.M;
+  if (!encode_tmap_bf16_kmajor(&tp, a.w, a.N, a.K, a.ldw, prow_box)) return -4;
+  if (!encode_tmap_bf16_kmajor(&tq, a.a, a.M, a.K, a.lda, pl.kbn)) return -4;
+  return launch_swap(a.epilogue, tp, tq, kp, pl, stream);
+}
+
+}  // namespace foa

@@ -1,0 +1,55 @@
+// Host-visible interface of the BF16 tcgen05 GEMM family.
+#pragma once
+
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace foa {
+
+// What the epilogue does with each FP32 accumulator value.
+enum GemmEpilogue : int {
+  kEpiBf16 = 0,        // C = bf16(acc)                  (+ residual: C = bf16(acc + res))
+  kEpiF32 = 1,         // C = acc as FP32
+  kEpiSwiGLU = 2,      // weights interleave gate/up in 128-row blocks; C = bf16(bf16(silu(bf16 g)) * bf16 u)
+};
+
+// Which operand feeds the MMA's M side.
+enum GemmMode : int {
+  kModeAuto = 0,
+  kModeRows = 1,   // activations on M (large row counts: prefill)
+  kModeSwap = 2,   // weights on M, activations on N (few rows: decode)
+};
+
+struct GemmArgs {
+  const void* a = nullptr;  // activations [M, K] BF16, row stride lda elements
+  long lda = 0;
+  const void* w = nullptr;  // weights [N, K] BF16, row stride ldw elements
+  long ldw = 0;
+  int M = 0, N = 0, K = 0;
+  void* c = nullptr;  // output [M, N'] (N' = N, or N/2 for SwiGLU), row stride ldc elements
+  long ldc = 0;
+  const void* residual = nullptr;  // optional BF16 [M, N] added before rounding (kEpiBf16 only)
+  long ldr = 0;
+  int epilogue = kEpiBf16;
+  int mode = kModeAuto;
+  int splits = 0;  // K splits; 0 chooses
+  // Scratch for split-K partial sums: FP32 partials and one arrival counter per output tile.
+  // The counters must be zero before the first launch; every launch leaves them zero.
+  float* workspace = nullptr;
+  size_t workspace_bytes = 0;
+  int* counters = nullptr;
+  int counters_len = 0;
+  int* status = nullptr;  // device status word (see sm100.cuh)
+  int num_sms = 0;        // 0: query the device
+};
+
+// Plans and launches one GEMM on `stream`. Returns 0, or a negative code for a rejected argument
+// (no launch happens then): -1 misaligned pointer/stride, -2 bad shape, -3 scratch too small,
+// -4 tensor-map encoding failed, -5 launch failed.
+int gemm_bf16(const GemmArgs& args, cudaStream_t stream);
+
+// Scratch the launch of `args` needs: FP32 workspace bytes and counter entries.
+void gemm_bf16_scratch(const GemmArgs& args, size_t* workspace_bytes, int* counters);
+
+}  // namespace foa

@@ -1,0 +1,330 @@
+// Memory-bound kernels of the decoder step: RMSNorm with the residual add, the embedding gather,
+// the attention front (QK-norm, RoPE, paged KV write) and the greedy readout.
+//
+// Reference contracts: RMSNorm `ops/normalization/rms_norm.rs:15-20` (FP32 statistics, one
+// rounding), residual add `ops/pointwise/add.rs:1` (FP32 sum rounded once), QK-norm
+// `ops/attention/full/head.rs:41`, RoPE `ops/rotary.rs:55-57` (half-split pairs), KV store
+// `ops/index/scatter.rs:30`, greedy head `ops/reduction.rs:73-77` (first maximum wins).
+
+#include <cfloat>
+#include <climits>
+
+#include "ops.cuh"
+#include "sm100.cuh"
+
+namespace foa {
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// ------------------------------------------------------------------------------------ RMSNorm
+// One CTA of 128 threads per row; each thread keeps up to kVec 8-element vectors in registers.
+template <int kVec>
+__global__ void __launch_bounds__(128) rmsnorm_kernel(
+    const __nv_bfloat16* __restrict__ x, long ldx, const __nv_bfloat16* __restrict__ residual,
+    long ldr, const __nv_bfloat16* __restrict__ weight, __nv_bfloat16* __restrict__ out, long ldo,
+    __nv_bfloat16* residual_out, long ldro, int cols, float eps) {
+  const int row = blockIdx.x;
+  const int nvec = cols / 8;
+  float h[kVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = threadIdx.x + i * 128;
+    if (v < nvec) {
+      const uint4 xv = *reinterpret_cast<const uint4*>(x + (long)row * ldx + v * 8);
+      const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        h[i][2 * t] = bf16_lo(xw[t]);
+        h[i][2 * t + 1] = bf16_hi(xw[t]);
+      }
+      if (residual != nullptr) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(residual + (long)row * ldr + v * 8);
+        const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          h[i][2 * t] += bf16_lo(rw[t]);
+          h[i][2 * t + 1] += bf16_hi(rw[t]);
+        }
+      }
+      // The residual stream is BF16: the norm reads the rounded sum.
+      uint32_t packed[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        packed[t] = pack_bf16x2(h[i][2 * t], h[i][2 * t + 1]);
+        h[i][2 * t] = bf16_lo(packed[t]);
+        h[i][2 * t + 1] = bf16_hi(packed[t]);
+        ss += h[i][2 * t] * h[i][2 * t] + h[i][2 * t + 1] * h[i][2 * t + 1];
+      }
+      if (residual_out != nullptr)
+        *reinterpret_cast<uint4*>(residual_out + (long)row * ldro + v * 8) =
+            make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  }
+  __shared__ float red[4];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  const float total = red[0] + red[1] + red[2] + red[3];
+  const float inv = rsqrtf(total / (float)cols + eps);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = threadIdx.x + i * 128;
+    if (v < nvec) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(weight + v * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        o[t] = pack_bf16x2(h[i][2 * t] * inv * bf16_lo(ww[t]), h[i][2 * t + 1] * inv * bf16_hi(ww[t]));
+      *reinterpret_cast<uint4*>(out + (long)row * ldo + v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------ embedding
+__global__ void embedding_kernel(const int32_t* __restrict__ ids,
+                                 const __nv_bfloat16* __restrict__ table, long ldt,
+                                 int row_begin, int row_end, __nv_bfloat16* __restrict__ out,
+                                 long ldo, int cols) {
+  const int row = blockIdx.x;
+  const int id = ids[row];
+  const bool local = id >= row_begin && id < row_end;
+  const int nvec = cols / 8;
+  for (int v = threadIdx.x; v < nvec; v += blockDim.x) {
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (local) val = *reinterpret_cast<const uint4*>(table + (long)(id - row_begin) * ldt + v * 8);
+    *reinterpret_cast<uint4*>(out + (long)row * ldo + v * 8) = val;
+  }
+}
+
+// ------------------------------------------------------------------------------------ argmax
+__device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, long ld,
+                                                     int cols, int valid, int base,
+                                                     int32_t* out_index, float* out_value) {
+  const int row = blockIdx.x;
+  const float* src = logits + (long)row * ld;
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  const int n = min(cols, valid);
+  const int n4 = (ld % 4 == 0) ? n / 4 : 0;
+  for (int v = threadIdx.x; v < n4; v += blockDim.x) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(src) + v);
+    better(bv, bi, x.x, 4 * v);
+    better(bv, bi, x.y, 4 * v + 1);
+    better(bv, bi, x.z, 4 * v + 2);
+    better(bv, bi, x.w, 4 * v + 3);
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) better(bv, bi, src[i], i);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    better(bv, bi, ov, oi);
+  }
+  __shared__ float sv[16];
+  __shared__ int si[16];
+  if ((threadIdx.x & 31) == 0) {
+    sv[threadIdx.x >> 5] = bv;
+    si[threadIdx.x >> 5] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    if (bi == INT_MAX) bi = 0;
+    out_index[row] = bi + base;
+    if (out_value != nullptr) out_value[row] = bv;
+  }
+}
+
+__global__ void argmax_merge_kernel(const float* values, const int32_t* indices, int ranks,
+                                    int rows, int32_t* out) {
+  const int row = blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float bv = -INFINITY;
+  int bi = INT_MAX;
+  for (int r = 0; r < ranks; ++r) better(bv, bi, values[(long)r * rows + row], indices[(long)r * rows + row]);
+  out[row] = bi == INT_MAX ? 0 : bi;
+}
+
+// ------------------------------------------------------------------------------------ attention front
+// One warp per (row, head) of the packed projection. A lane holds elements
+// [lane*E, lane*E+E) of the first half of the head and the same offsets of the second half, so
+// each rotated pair (j, j + d/2) stays in one lane.
+template <int kHD>
+__global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
+    const __nv_bfloat16* __restrict__ qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
+    const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float eps,
+    const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, float attn_factor,
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
+    const int32_t* __restrict__ slots) {
+  constexpr int E = kHD / 64;  // elements per lane in each half
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int heads = q_heads + 2 * kv_heads;
+  const int task = blockIdx.x * 4 + warp;
+  if (task >= rows * heads) return;
+  const int row = task / heads, head = task % heads;
+  const __nv_bfloat16* src = qkv + (long)row * ld_qkv + (long)head * kHD;
+  float a[E], b[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    a[e] = __bfloat162float(src[lane * E + e]);
+    b[e] = __bfloat162float(src[kHD / 2 + lane * E + e]);
+  }
+  const bool is_q = head < q_heads;
+  const bool is_k = !is_q && head < q_heads + kv_heads;
+  if (is_q || is_k) {
+    const __nv_bfloat16* nw = is_q ? q_norm : k_norm;
+    if (nw != nullptr) {
+      float ss = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss += a[e] * a[e] + b[e] * b[e];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / (float)kHD + eps);
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        a[e] = __bfloat162float(__float2bfloat16_rn(a[e] * inv * __bfloat162float(nw[lane * E + e])));
+        b[e] = __bfloat162float(
+            __float2bfloat16_rn(b[e] * inv * __bfloat162float(nw[kHD / 2 + lane * E + e])));
+      }
+    }
+    const float pos = (float)positions[row];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      float s, c;
+      sincosf(pos * inv_freq[lane * E + e], &s, &c);
+      c *= attn_factor;
+      s *= attn_factor;
+      const float x1 = a[e], x2 = b[e];
+      a[e] = x1 * c - x2 * s;
+      b[e] = x2 * c + x1 * s;
+    }
+  }
+  if (is_q) {
+    __nv_bfloat16* dst = q_out + ((long)row * q_heads + head) * kHD;
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+      dst[lane * E + e] = __float2bfloat16_rn(a[e]);
+      dst[kHD / 2 + lane * E + e] = __float2bfloat16_rn(b[e]);
+    }
+    return;
+  }
+  const int slot = slots[row];
+  if (slot < 0) return;
+  const int kvh = is_k ? head - q_heads : head - q_heads - kv_heads;
+  const long page = 2L * kv_heads * 16 * kHD;
+  __nv_bfloat16* dst = cache + (long)(slot / 16) * page + (is_k ? 0 : (long)kv_heads * 16 * kHD) +
+                       ((long)kvh * 16 + slot % 16) * kHD;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    dst[lane * E + e] = __float2bfloat16_rn(a[e]);
+    dst[kHD / 2 + lane * E + e] = __float2bfloat16_rn(b[e]);
+  }
+}
+
+}  // namespace
+
+int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, long ldr,
+            const __nv_bfloat16* weight, __nv_bfloat16* out, long ldo,
+            __nv_bfloat16* residual_out, long ldro, int rows, int cols, float eps,
+            cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (cols % 8 != 0 || cols > 16384) return -2;
+  const int vec = (cols / 8 + 127) / 128;
+#define FOA_RMS(V)                                                                          \
+  case V:                                                                                   \
+    rmsnorm_kernel<V><<<rows, 128, 0, stream>>>(x, ldx, residual, ldr, weight, out, ldo,    \
+                                                residual_out, ldro, cols, eps);             \
+    break;
+  switch (vec) {
+    FOA_RMS(1)
+    FOA_RMS(2)
+    FOA_RMS(3)
+    FOA_RMS(4)
+    FOA_RMS(5)
+    FOA_RMS(6)
+    FOA_RMS(7)
+    FOA_RMS(8)
+    FOA_RMS(9)
+    FOA_RMS(10)
+    FOA_RMS(11)
+    FOA_RMS(12)
+    FOA_RMS(13)
+    FOA_RMS(14)
+    FOA_RMS(15)
+    FOA_RMS(16)
+    default:
+      return -2;
+  }
+#undef FOA_RMS
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int embedding(const int32_t* ids, const __nv_bfloat16* table, long ldt, int row_begin,
+              int row_end, __nv_bfloat16* out, long ldo, int rows, int cols,
+              cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (cols % 8 != 0) return -2;
+  embedding_kernel<<<rows, 128, 0, stream>>>(ids, table, ldt, row_begin, row_end, out, ldo, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int argmax_rows(const float* logits, long ld, int rows, int cols, int valid_cols, int index_base,
+                int32_t* out_index, float* out_value, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  argmax_kernel<<<rows, 512, 0, stream>>>(logits, ld, cols, valid_cols, index_base, out_index,
+                                          out_value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int argmax_merge(const float* values, const int32_t* indices, int ranks, int rows,
+                 int32_t* out_tokens, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  argmax_merge_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(values, indices, ranks, rows,
+                                                              out_tokens);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
+                       int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
+                       float eps, const int32_t* positions, RopeTable rope,
+                       __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slots,
+                       cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  const long tasks = (long)rows * (q_heads + 2 * kv_heads);
+  const int grid = (int)((tasks + 3) / 4);
+  switch (head_dim) {
+    case 64:
+      qk_norm_rope_cache_kernel<64><<<grid, 128, 0, stream>>>(
+          qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
+          rope.attention_factor, q_out, cache, slots);
+      break;
+    case 128:
+      qk_norm_rope_cache_kernel<128><<<grid, 128, 0, stream>>>(
+          qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
+          rope.attention_factor, q_out, cache, slots);
+      break;
+    case 256:
+      qk_norm_rope_cache_kernel<256><<<grid, 128, 0, stream>>>(
+          qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
+          rope.attention_factor, q_out, cache, slots);
+      break;
+    default:
+      return -2;
+  }
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+}  // namespace foa

@@ -1,0 +1,55 @@
+// Host-visible interface of the engine's non-GEMM kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace foa {
+
+// h = x (+ residual), FP32 sum rounded once to BF16 into residual_out (when given);
+// out = BF16(h * weight / sqrt(mean(h^2) + eps)) with FP32 statistics and one rounding.
+// `residual` and `residual_out` may be null; `residual_out` may alias `residual` or `x`.
+int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, long ldr,
+            const __nv_bfloat16* weight, __nv_bfloat16* out, long ldo,
+            __nv_bfloat16* residual_out, long ldro, int rows, int cols, float eps,
+            cudaStream_t stream);
+
+// out[r, :] = table[ids[r], :] for r < rows, BF16 rows of `cols` elements. Rows of the table
+// outside [row_begin, row_end) (a vocabulary shard) give zeros, and ids are shifted by row_begin.
+int embedding(const int32_t* ids, const __nv_bfloat16* table, long ldt, int row_begin,
+              int row_end, __nv_bfloat16* out, long ldo, int rows, int cols, cudaStream_t stream);
+
+// For each of `rows` FP32 rows of `cols` logits: the first index of the maximum (NaN never wins)
+// and its value. Padded vocabulary columns >= `valid_cols` never win. `index_base` is added to
+// every index (a vocabulary shard's offset).
+int argmax_rows(const float* logits, long ld, int rows, int cols, int valid_cols, int index_base,
+                int32_t* out_index, float* out_value, cudaStream_t stream);
+
+// Merges per-rank (value, index) argmax candidates [ranks, rows] into tokens: the largest value,
+// the lowest index among equal values.
+int argmax_merge(const float* values, const int32_t* indices, int ranks, int rows,
+                 int32_t* out_tokens, cudaStream_t stream);
+
+// Rotary embedding parameters: inverse frequencies for the `head_dim/2` rotated pairs, and the
+// attention factor YaRN scales cos/sin by.
+struct RopeTable {
+  const float* inv_freq;  // [head_dim / 2]
+  float attention_factor;
+};
+
+// Attention front of one call: splits the packed q/k/v projection rows, applies the per-head
+// RMSNorm to q and k (when q_norm/k_norm are given), rotates q and k by position (half-split
+// pairs j, j + d/2), writes rotated q to `q_out` [rows, q_heads, head_dim] and k/v into the paged
+// cache slot of each row.
+//
+// Cache layout per layer: block b is `page_bytes` bytes holding K[kv_heads][16][head_dim] then
+// V[kv_heads][16][head_dim] in BF16. slot_mapping[r] = block * 16 + offset, or -1 to skip.
+int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
+                       int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
+                       float eps, const int32_t* positions, RopeTable rope,
+                       __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slot_mapping,
+                       cudaStream_t stream);
+
+}  // namespace foa

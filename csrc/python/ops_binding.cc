@@ -1,0 +1,141 @@
+// Raw launchers of the engine's kernels for Python: every tensor crosses as a device address and
+// its strides, every launch as a CUDA stream handle. The engine's own model code calls the same
+// launchers from C++; this surface exists so tests and tools can drive one kernel at a time.
+#include <pybind11/pybind11.h>
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+
+#include "kernels/gemm.cuh"
+#include "kernels/ops.cuh"
+
+namespace py = pybind11;
+
+namespace {
+
+cudaStream_t as_stream(uint64_t s) { return reinterpret_cast<cudaStream_t>(s); }
+template <class T>
+T* as_ptr(uint64_t p) {
+  return reinterpret_cast<T*>(p);
+}
+
+void check(int rc, const char* what) {
+  if (rc != 0) throw std::runtime_error(std::string(what) + " launch rejected: code " + std::to_string(rc));
+}
+
+}  // namespace
+
+void bind_ops(py::module_& m) {
+  m.def(
+      "gemm",
+      [](uint64_t a, long lda, uint64_t w, long ldw, int M, int N, int K, uint64_t c, long ldc,
+         uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
+         uint64_t counters, int counters_len, uint64_t status, uint64_t stream) {
+        foa::GemmArgs g;
+        g.a = as_ptr<void>(a);
+        g.lda = lda;
+        g.w = as_ptr<void>(w);
+        g.ldw = ldw;
+        g.M = M;
+        g.N = N;
+        g.K = K;
+        g.c = as_ptr<void>(c);
+        g.ldc = ldc;
+        g.residual = as_ptr<void>(res);
+        g.ldr = ldr;
+        g.epilogue = epilogue;
+        g.mode = mode;
+        g.splits = splits;
+        g.workspace = as_ptr<float>(ws);
+        g.workspace_bytes = ws_bytes;
+        g.counters = as_ptr<int>(counters);
+        g.counters_len = counters_len;
+        g.status = as_ptr<int>(status);
+        py::gil_scoped_release nogil;
+        check(foa::gemm_bf16(g, as_stream(stream)), "gemm");
+      },
+      py::arg("a"), py::arg("lda"), py::arg("w"), py::arg("ldw"), py::arg("M"), py::arg("N"),
+      py::arg("K"), py::arg("c"), py::arg("ldc"), py::arg("res"), py::arg("ldr"),
+      py::arg("epilogue"), py::arg("mode"), py::arg("splits"), py::arg("ws"),
+      py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
+      py::arg("stream"));
+
+  m.def(
+      "gemm_scratch",
+      [](int M, int N, int K, int epilogue, int mode, int splits) {
+        foa::GemmArgs g;
+        g.M = M;
+        g.N = N;
+        g.K = K;
+        g.epilogue = epilogue;
+        g.mode = mode;
+        g.splits = splits;
+        size_t bytes = 0;
+        int counters = 0;
+        foa::gemm_bf16_scratch(g, &bytes, &counters);
+        return py::make_tuple(bytes, counters);
+      },
+      py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epilogue"), py::arg("mode"),
+      py::arg("splits"));
+
+  m.def(
+      "rmsnorm",
+      [](uint64_t x, long ldx, uint64_t residual, long ldr, uint64_t weight, uint64_t out,
+         long ldo, uint64_t residual_out, long ldro, int rows, int cols, float eps,
+         uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::rmsnorm(as_ptr<const __nv_bfloat16>(x), ldx,
+                           as_ptr<const __nv_bfloat16>(residual), ldr,
+                           as_ptr<const __nv_bfloat16>(weight), as_ptr<__nv_bfloat16>(out), ldo,
+                           as_ptr<__nv_bfloat16>(residual_out), ldro, rows, cols, eps,
+                           as_stream(stream)),
+              "rmsnorm");
+      },
+      py::arg("x"), py::arg("ldx"), py::arg("residual"), py::arg("ldr"), py::arg("weight"),
+      py::arg("out"), py::arg("ldo"), py::arg("residual_out"), py::arg("ldro"), py::arg("rows"),
+      py::arg("cols"), py::arg("eps"), py::arg("stream"));
+  m.def(
+      "embedding",
+      [](uint64_t ids, uint64_t table, long ldt, int row_begin, int row_end, uint64_t out,
+         long ldo, int rows, int cols, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::embedding(as_ptr<const int32_t>(ids), as_ptr<const __nv_bfloat16>(table), ldt,
+                             row_begin, row_end, as_ptr<__nv_bfloat16>(out), ldo, rows, cols,
+                             as_stream(stream)),
+              "embedding");
+      });
+
+  m.def("argmax",
+        [](uint64_t logits, long ld, int rows, int cols, int valid, int base, uint64_t idx,
+           uint64_t val, uint64_t stream) {
+          py::gil_scoped_release nogil;
+          check(foa::argmax_rows(as_ptr<const float>(logits), ld, rows, cols, valid, base,
+                                 as_ptr<int32_t>(idx), as_ptr<float>(val), as_stream(stream)),
+                "argmax");
+        });
+
+  m.def("argmax_merge", [](uint64_t values, uint64_t indices, int ranks, int rows, uint64_t out,
+                           uint64_t stream) {
+    py::gil_scoped_release nogil;
+    check(foa::argmax_merge(as_ptr<const float>(values), as_ptr<const int32_t>(indices), ranks,
+                            rows, as_ptr<int32_t>(out), as_stream(stream)),
+          "argmax_merge");
+  });
+
+  m.def("qk_norm_rope_cache",
+        [](uint64_t qkv, long ld_qkv, int rows, int q_heads, int kv_heads, int head_dim,
+           uint64_t q_norm, uint64_t k_norm, float eps, uint64_t positions, uint64_t inv_freq,
+           float attention_factor, uint64_t q_out, uint64_t cache, uint64_t slots,
+           uint64_t stream) {
+          py::gil_scoped_release nogil;
+          foa::RopeTable rope{as_ptr<const float>(inv_freq), attention_factor};
+          check(foa::qk_norm_rope_cache(
+                    as_ptr<const __nv_bfloat16>(qkv), ld_qkv, rows, q_heads, kv_heads, head_dim,
+                    as_ptr<const __nv_bfloat16>(q_norm), as_ptr<const __nv_bfloat16>(k_norm), eps,
+                    as_ptr<const int32_t>(positions), rope, as_ptr<__nv_bfloat16>(q_out),
+                    as_ptr<__nv_bfloat16>(cache), as_ptr<const int32_t>(slots),
+                    as_stream(stream)),
+                "qk_norm_rope_cache");
+        });
+}

@@ -1,0 +1,21 @@
+"""Python handles on the engine's sm_100a kernels.
+
+Each function takes CUDA torch tensors, checks shapes and layouts, and calls the raw launcher of
+the native extension on the current stream. The launchers fail loudly: a missing extension on a
+GPU host raises, so no test or benchmark silently runs a PyTorch fallback.
+"""
+
+from .native import native, scratch  # noqa: F401
+from .kernels import (  # noqa: F401
+    EPI_BF16,
+    EPI_F32,
+    EPI_SWIGLU,
+    MODE_AUTO,
+    MODE_ROWS,
+    MODE_SWAP,
+    argmax,
+    embedding,
+    gemm,
+    qk_norm_rope_cache,
+    rmsnorm,
+)
