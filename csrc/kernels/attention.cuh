@@ -1,0 +1,52 @@
+// Host-visible interface of the paged attention kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace foa {
+
+// One sequence's rows in a call: rows [row_start, row_start + len) of the call append positions
+// cached .. cached + len - 1; the sequence's block IDs are table[table_start .. table_start +
+// nblocks). The same five fields the reference's compact history encodes per segment.
+struct Segment {
+  int32_t row_start;
+  int32_t len;
+  int32_t cached;
+  int32_t table_start;
+  int32_t nblocks;
+};
+
+struct PagedAttention {
+  const __nv_bfloat16* q = nullptr;  // [rows, q_heads, head_dim]
+  __nv_bfloat16* o = nullptr;        // [rows, q_heads, head_dim]
+  const __nv_bfloat16* cache = nullptr;  // layer pages: K[kv_heads][16][d] then V[kv_heads][16][d]
+  const int32_t* table = nullptr;        // block IDs
+  const Segment* segments = nullptr;
+  int num_segments = 0;
+  int q_heads = 0, kv_heads = 0, head_dim = 128;
+  float scale = 0.f;  // softmax scale (1/sqrt(head_dim) by default)
+  // Decode split scratch: FP32 partial outputs and log-sum-exps of every (row, head, split).
+  float* partial_o = nullptr;
+  float* partial_lse = nullptr;
+  size_t partial_capacity = 0;  // elements of partial_lse (partial_o holds head_dim times more)
+  int max_keys = 0;             // longest history of any segment (bounds the split count)
+  int keys_per_split = 512;     // fixed split width: each row's tiling depends on its own length
+  int* status = nullptr;
+};
+
+// Decode: every segment appends one row (len == 1) and attends its whole history.
+int paged_decode(const PagedAttention& args, cudaStream_t stream);
+
+// Prefill / chunks: segments of any length attend their history plus their own rows causally.
+// `work` lists (segment, query tile) pairs, `num_work` of them; a tile is 64 (token, head) rows
+// of one key/value head.
+int paged_prefill(const PagedAttention& args, const int32_t* work, int num_work,
+                  cudaStream_t stream);
+
+// Query tiles of a segment of `len` rows with `group` query heads per key/value head.
+inline int prefill_tiles(int len, int group) { return (len * group + 63) / 64; }
+
+}  // namespace foa

@@ -9,6 +9,7 @@
 
 #include "kernels/gemm.cuh"
 #include "kernels/ops.cuh"
+#include "kernels/attention.cuh"
 
 namespace py = pybind11;
 
@@ -137,5 +138,49 @@ void bind_ops(py::module_& m) {
                     as_ptr<__nv_bfloat16>(cache), as_ptr<const int32_t>(slots),
                     as_stream(stream)),
                 "qk_norm_rope_cache");
+        });
+  auto make_attn = [](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
+                      int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
+                      uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
+                      int keys_per_split, uint64_t status) {
+    foa::PagedAttention a;
+    a.q = as_ptr<const __nv_bfloat16>(q);
+    a.o = as_ptr<__nv_bfloat16>(o);
+    a.cache = as_ptr<const __nv_bfloat16>(cache);
+    a.table = as_ptr<const int32_t>(table);
+    a.segments = as_ptr<const foa::Segment>(segments);
+    a.num_segments = num_segments;
+    a.q_heads = q_heads;
+    a.kv_heads = kv_heads;
+    a.head_dim = head_dim;
+    a.scale = scale;
+    a.partial_o = as_ptr<float>(partial_o);
+    a.partial_lse = as_ptr<float>(partial_lse);
+    a.partial_capacity = capacity;
+    a.max_keys = max_keys;
+    a.keys_per_split = keys_per_split;
+    a.status = as_ptr<int>(status);
+    return a;
+  };
+  m.def("paged_decode",
+        [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
+                    int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
+                    uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
+                    int keys_per_split, uint64_t status, uint64_t stream) {
+          auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
+                             head_dim, scale, partial_o, partial_lse, capacity, max_keys,
+                             keys_per_split, status);
+          py::gil_scoped_release nogil;
+          check(foa::paged_decode(a, as_stream(stream)), "paged_decode");
+        });
+  m.def("paged_prefill",
+        [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
+                    int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
+                    uint64_t work, int num_work, uint64_t status, uint64_t stream) {
+          auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
+                             head_dim, scale, 0, 0, 0, 1, 512, status);
+          py::gil_scoped_release nogil;
+          check(foa::paged_prefill(a, as_ptr<const int32_t>(work), num_work, as_stream(stream)),
+                "paged_prefill");
         });
 }

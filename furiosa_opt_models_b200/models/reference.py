@@ -52,3 +52,38 @@ def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
     """``bf16(silu(bf16 gate)) * bf16 up`` in FP32."""
     g = gate.bfloat16().float()
     return torch.nn.functional.silu(g).bfloat16().float() * up.bfloat16().float()
+
+
+def gather_kv(cache: torch.Tensor, table, table_start: int, keys: int):
+    """K and V [keys, kv_heads, d] of one sequence from a paged layer ``cache``
+    [blocks, 2, kv_heads, 16, d]."""
+    nb = (keys + 15) // 16
+    ids = [int(x) for x in table[table_start : table_start + nb]]
+    pages = cache[ids]  # [nb, 2, H, 16, d]
+    k = pages[:, 0].permute(0, 2, 1, 3).reshape(nb * 16, cache.shape[2], cache.shape[4])[:keys]
+    v = pages[:, 1].permute(0, 2, 1, 3).reshape(nb * 16, cache.shape[2], cache.shape[4])[:keys]
+    return k.float(), v.float()
+
+
+def paged_attention(q: torch.Tensor, cache: torch.Tensor, table, segments, scale: float | None = None):
+    """Causal GQA attention of every segment's rows over its paged history, in FP32.
+
+    ``q`` [rows, q_heads, d]; ``segments`` rows of (row_start, len, cached, table_start, nblocks).
+    Row i of a segment is position cached + i and attends keys 0..cached + i."""
+    rows, q_heads, d = q.shape
+    kv_heads = cache.shape[2]
+    group = q_heads // kv_heads
+    scale = d ** -0.5 if scale is None else scale
+    out = torch.zeros(rows, q_heads, d, dtype=torch.float32)
+    for row_start, length, cached, table_start, _ in [tuple(int(x) for x in s) for s in segments]:
+        keys = cached + length
+        k, v = gather_kv(cache, table, table_start, keys)
+        k = k.repeat_interleave(group, dim=1)  # [keys, q_heads, d]
+        v = v.repeat_interleave(group, dim=1)
+        qs = q[row_start : row_start + length].float()  # [len, q_heads, d]
+        s = torch.einsum("lhd,khd->hlk", qs, k) * scale
+        pos = torch.arange(length)[:, None] + cached
+        mask = torch.arange(keys)[None, :] <= pos
+        s = s.masked_fill(~mask[None], float("-inf"))
+        out[row_start : row_start + length] = torch.einsum("hlk,khd->lhd", torch.softmax(s, -1), v)
+    return out

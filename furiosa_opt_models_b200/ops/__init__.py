@@ -18,4 +18,7 @@ from .kernels import (  # noqa: F401
     gemm,
     qk_norm_rope_cache,
     rmsnorm,
+    paged_decode,
+    paged_prefill,
+    prefill_work,
 )

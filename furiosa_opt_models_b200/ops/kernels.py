@@ -109,3 +109,48 @@ def qk_norm_rope_cache(qkv, q_heads, kv_heads, head_dim, q_norm, k_norm, eps, po
         _ptr(k_norm), float(eps), positions.data_ptr(), inv_freq.data_ptr(),
         float(attention_factor), q.data_ptr(), cache.data_ptr(), slots.data_ptr(), _stream())
     return q
+
+
+def _attn_common(segments: torch.Tensor) -> None:
+    if segments.dtype != torch.int32 or segments.dim() != 2 or segments.shape[1] != 5:
+        raise ValueError("segments are int32 [n, 5]: row_start, len, cached, table_start, nblocks")
+
+
+def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys_per_split=512, out=None):
+    """Flash-decoding of one-row segments over the paged cache. q: [rows, q_heads, d]."""
+    _attn_common(segments)
+    rows, q_heads, d = q.shape
+    out = torch.empty_like(q) if out is None else out
+    s = scratch(q.device)
+    n = segments.shape[0]
+    splits = (max_keys + keys_per_split - 1) // keys_per_split
+    need = n * q_heads * splits
+    po = torch.empty(need * d if splits > 1 else 1, dtype=torch.float32, device=q.device)
+    pl = torch.empty(need if splits > 1 else 1, dtype=torch.float32, device=q.device)
+    native().ops.paged_decode(
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(), n,
+        q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5), po.data_ptr(),
+        pl.data_ptr(), need, int(max_keys), keys_per_split, s.status.data_ptr(), _stream())
+    return out
+
+
+def prefill_work(segments_cpu, group: int) -> torch.Tensor:
+    """(segment, query tile) pairs of the prefill kernel, as int32 [n, 2]."""
+    work = []
+    for i, (_, length, _, _, _) in enumerate(segments_cpu.tolist()):
+        for tile in range((length * group + 63) // 64):
+            work.append((i, tile))
+    return torch.tensor(work, dtype=torch.int32).reshape(-1, 2)
+
+
+def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=None):
+    """Causal attention of segments' rows over their history and themselves."""
+    _attn_common(segments)
+    rows, q_heads, d = q.shape
+    out = torch.empty_like(q) if out is None else out
+    s = scratch(q.device)
+    native().ops.paged_prefill(
+        q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(),
+        segments.shape[0], q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5),
+        work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream())
+    return out

@@ -1,0 +1,53 @@
+"""Paged decode and prefill attention against the FP32 PyTorch reference."""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _setup(lengths, cached, q_heads, kv_heads, d, blocks=512, seed=0):
+    torch.manual_seed(seed)
+    cache = torch.randn(blocks, 2, kv_heads, 16, d, dtype=torch.bfloat16) * 0.5
+    perm = torch.randperm(blocks).tolist()
+    table, segs, row = [], [], 0
+    for n, c in zip(lengths, cached):
+        nb = (c + n + 15) // 16
+        start = len(table)
+        table += perm[:nb]
+        perm = perm[nb:]
+        segs.append((row, n, c, start, nb))
+        row += n
+    q = torch.randn(row, q_heads, d, dtype=torch.bfloat16)
+    return q, cache, torch.tensor(table, dtype=torch.int32), torch.tensor(segs, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("q_heads,kv_heads,d", [(16, 8, 128), (32, 8, 128), (8, 8, 64), (64, 8, 128)])
+def test_paged_decode(q_heads, kv_heads, d):
+    from furiosa_opt_models_b200 import ops
+    from furiosa_opt_models_b200.models import reference
+
+    cached = [0, 5, 15, 16, 100, 511, 512, 1000, 2047, 3000]
+    q, cache, table, segs = _setup([1] * len(cached), cached, q_heads, kv_heads, d)
+    ref = reference.paged_attention(q, cache, table, segs)
+    out = ops.paged_decode(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), kv_heads,
+                           max_keys=max(cached) + 1)
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
+
+
+@pytest.mark.parametrize("q_heads,kv_heads,d", [(16, 8, 128), (32, 8, 128), (8, 8, 64)])
+def test_paged_prefill(q_heads, kv_heads, d):
+    from furiosa_opt_models_b200 import ops
+    from furiosa_opt_models_b200.models import reference
+
+    lengths = [7, 16, 33, 64, 130, 1]
+    cached = [0, 0, 20, 100, 0, 40]
+    q, cache, table, segs = _setup(lengths, cached, q_heads, kv_heads, d)
+    ref = reference.paged_attention(q, cache, table, segs)
+    work = ops.prefill_work(segs, q_heads // kv_heads)
+    out = ops.paged_prefill(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), kv_heads, work.cuda())
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
