@@ -1,0 +1,517 @@
+#include "model.h"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "kernels/attention.cuh"
+#include "kernels/gemm.cuh"
+#include "kernels/ops.cuh"
+
+namespace foa::engine {
+
+namespace {
+constexpr size_t kAlign = 256;
+size_t align_up(size_t v) { return (v + kAlign - 1) / kAlign * kAlign; }
+int64_t next_pow2(int64_t v) {
+  int64_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+__nv_bfloat16* bf(const HbmBuffer& b) { return static_cast<__nv_bfloat16*>(b.data()); }
+int32_t* i32(const HbmBuffer& b, size_t off = 0) {
+  return reinterpret_cast<int32_t*>(static_cast<char*>(b.data()) + off);
+}
+}  // namespace
+
+// ------------------------------------------------------------------------------------ RoPE
+std::vector<float> rope_inv_freq(const RopeSpec& r, int d, float* attention_factor) {
+  const int half = d / 2;
+  std::vector<double> base(half);
+  for (int j = 0; j < half; ++j) base[j] = 1.0 / std::pow(r.theta, (2.0 * j) / d);
+  std::vector<double> out = base;
+  double attn = 1.0;
+  if (r.type == "linear") {
+    for (auto& f : out) f /= r.factor;
+  } else if (r.type == "llama3") {
+    const double old = r.original_max_positions;
+    const double low_wl = old / r.low_freq_factor, high_wl = old / r.high_freq_factor;
+    for (int j = 0; j < half; ++j) {
+      const double f = base[j], wl = 2.0 * M_PI / f;
+      if (wl < high_wl) {
+        out[j] = f;
+      } else if (wl > low_wl) {
+        out[j] = f / r.factor;
+      } else {
+        const double smooth = (old / wl - r.low_freq_factor) / (r.high_freq_factor - r.low_freq_factor);
+        out[j] = (1.0 - smooth) * f / r.factor + smooth * f;
+      }
+    }
+  } else if (r.type == "yarn") {
+    const double old = r.original_max_positions;
+    auto corr_dim = [&](double rot) {
+      return (d * std::log(old / (rot * 2.0 * M_PI))) / (2.0 * std::log(r.theta));
+    };
+    double low = corr_dim(r.beta_fast), high = corr_dim(r.beta_slow);
+    if (r.truncate) {
+      low = std::floor(low);
+      high = std::ceil(high);
+    }
+    low = std::max(low, 0.0);
+    high = std::min(high, double(d - 1));
+    if (low == high) high += 0.001;
+    for (int j = 0; j < half; ++j) {
+      const double ramp = std::clamp((j - low) / (high - low), 0.0, 1.0);
+      const double extrap = 1.0 - ramp;
+      out[j] = (base[j] / r.factor) * (1.0 - extrap) + base[j] * extrap;
+    }
+    auto mscale = [](double s, double m) { return s <= 1.0 ? 1.0 : 0.1 * m * std::log(s) + 1.0; };
+    if (r.attention_factor > 0)
+      attn = r.attention_factor;
+    else if (r.mscale_all_dim > 0)
+      attn = mscale(r.factor, r.mscale) / mscale(r.factor, r.mscale_all_dim);
+    else
+      attn = mscale(r.factor, 1.0);
+  }
+  if (attention_factor) *attention_factor = static_cast<float>(attn);
+  return std::vector<float>(out.begin(), out.end());
+}
+
+// ------------------------------------------------------------------------------------ model
+DecoderModel::DecoderModel(const Device& device, ModelConfig cfg, int tp, int rank)
+    : device_(device), cfg_(std::move(cfg)), tp_(tp), rank_(rank) {
+  if (cfg_.q_heads % tp_ != 0) throw Unsupported("query heads do not split evenly over the chips");
+  qh_l_ = cfg_.q_heads / tp_;
+  qh_first_ = rank_ * qh_l_;
+  if (cfg_.kv_heads >= tp_) {
+    if (cfg_.kv_heads % tp_ != 0) throw Unsupported("key/value heads do not split evenly over the chips");
+    kvh_l_ = cfg_.kv_heads / tp_;
+    kvh_first_ = rank_ * kvh_l_;
+  } else {
+    // Fewer key/value heads than chips: each chip holds a replica of the head its queries read.
+    if (tp_ % cfg_.kv_heads != 0) throw Unsupported("key/value heads do not split evenly over the chips");
+    kvh_l_ = 1;
+    kvh_first_ = rank_ * cfg_.kv_heads / tp_;
+  }
+  const int inter = cfg_.experts > 0 ? 0 : cfg_.intermediate;
+  if (inter % tp_ != 0 || (inter / tp_) % 128 != 0)
+    throw Unsupported("the intermediate width does not split into 128-row blocks over the chips");
+  inter_l_ = inter / tp_;
+  vocab_l_ = (cfg_.vocab + tp_ - 1) / tp_;
+  vocab_l_ = (vocab_l_ + 7) / 8 * 8;
+  vocab_begin_ = rank_ * vocab_l_;
+  vocab_end_ = std::min(cfg_.vocab, vocab_begin_ + vocab_l_);
+  inv_freq_host_ = rope_inv_freq(cfg_.rope, cfg_.head_dim, &attention_factor_);
+  allocate_weights();
+  auto st = device_.state();
+  inv_freq_ = HbmBuffer(device_, inv_freq_host_.size() * sizeof(float));
+  st->check_cuda(cudaMemcpy(inv_freq_.data(), inv_freq_host_.data(), inv_freq_.size(),
+                            cudaMemcpyHostToDevice),
+                 "rope table");
+  for (auto& e : stage_done_) st->check_cuda(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+}
+
+DecoderModel::~DecoderModel() {
+  device_.state()->activate();
+  cudaStreamSynchronize(device_.state()->stream);
+  clear_graphs();
+  for (auto& e : stage_done_)
+    if (e) cudaEventDestroy(e);
+}
+
+void DecoderModel::clear_graphs() {
+  for (auto& g : graphs_)
+    if (g.second.exec) cudaGraphExecDestroy(g.second.exec);
+  graphs_.clear();
+}
+
+Limits DecoderModel::limits() const {
+  Limits l;
+  l.window = cfg_.window;
+  l.rows = cfg_.rows;
+  Pool pool;
+  pool.block = 16;
+  pool.bytes = 2LL * kvh_l_ * 16 * cfg_.head_dim * 2;
+  l.cache.pools.push_back(pool);
+  Group g;
+  g.pool = 0;
+  g.layers_begin = 0;
+  g.layers_end = cfg_.layers;
+  l.cache.groups.push_back(g);
+  l.adapters = 0;
+  return l;
+}
+
+void DecoderModel::allocate_weights() {
+  const int H = cfg_.hidden, D = cfg_.head_dim;
+  std::vector<std::pair<std::string, std::vector<int64_t>>> plan;
+  // The embedding is whole on every chip, padded to the chips' head shards; the head is the
+  // chip's vocabulary shard (a view into the embedding when they are tied).
+  plan.push_back({"embed", {static_cast<int64_t>(vocab_l_) * tp_, H}});
+  if (!cfg_.tied) plan.push_back({"lm_head", {vocab_l_, H}});
+  plan.push_back({"final_norm", {H}});
+  if (cfg_.output == Output::Scores) plan.push_back({"score", {cfg_.labels, H}});
+  for (int l = 0; l < cfg_.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    plan.push_back({p + "in_norm", {H}});
+    plan.push_back({p + "qkv", {(qh_l_ + 2 * kvh_l_) * D, H}});
+    if (cfg_.qk_norm) {
+      plan.push_back({p + "q_norm", {D}});
+      plan.push_back({p + "k_norm", {D}});
+    }
+    plan.push_back({p + "o", {H, qh_l_ * D}});
+    plan.push_back({p + "post_norm", {H}});
+    if (cfg_.experts == 0) {
+      plan.push_back({p + "gate_up", {2 * inter_l_, H}});
+      plan.push_back({p + "down", {H, inter_l_}});
+    }
+  }
+  size_t total = 0;
+  std::vector<size_t> offs;
+  for (auto& e : plan) {
+    offs.push_back(total);
+    size_t n = 1;
+    for (auto s : e.second) n *= static_cast<size_t>(s);
+    total = align_up(total + n * 2);
+  }
+  arena_ = HbmBuffer(device_, std::max<size_t>(total, 256));
+  arena_bytes_ = total;
+  for (size_t i = 0; i < plan.size(); ++i) {
+    WeightSlot w;
+    w.ptr = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(arena_.data()) + offs[i]);
+    w.shape = plan[i].second;
+    weights_[plan[i].first] = w;
+  }
+  if (cfg_.tied) {
+    WeightSlot head = weights_["embed"];
+    head.ptr += static_cast<size_t>(vocab_begin_) * H;
+    head.shape = {vocab_l_, H};
+    weights_["lm_head"] = head;
+  }
+}
+
+void DecoderModel::init_random(uint64_t seed, float stdv) {
+  auto st = device_.state();
+  st->activate();
+  uint64_t k = 0;
+  for (auto& [name, w] : weights_) {
+    if (name == "lm_head" && cfg_.tied) continue;
+    long n = 1;
+    for (auto s : w.shape) n *= s;
+    const bool norm = name.find("norm") != std::string::npos;
+    int rc = norm ? foa::fill_bf16(w.ptr, n, 1.0f, st->stream)
+                  : foa::init_normal_bf16(w.ptr, n, stdv, seed * 1315423911ull + (++k), st->stream);
+    if (rc != 0) st->fail("weight initialisation launch failed");
+  }
+  st->check_cuda(cudaStreamSynchronize(st->stream), "weight initialisation");
+}
+
+void DecoderModel::ensure_workspace(int64_t rows, int64_t kept, int64_t splits, int64_t decode_rows) {
+  const int H = cfg_.hidden, D = cfg_.head_dim;
+  bool changed = false;
+  if (rows > ws_rows_) {
+    const int64_t R = std::max<int64_t>(256, next_pow2(rows));
+    ws_x_ = HbmBuffer(device_, R * H * 2);
+    ws_h_ = HbmBuffer(device_, R * H * 2);
+    ws_qkv_ = HbmBuffer(device_, R * (qh_l_ + 2 * kvh_l_) * D * 2);
+    ws_q_ = HbmBuffer(device_, R * qh_l_ * D * 2);
+    ws_attn_ = HbmBuffer(device_, R * qh_l_ * D * 2);
+    ws_act_ = HbmBuffer(device_, std::max<int64_t>(R * inter_l_ * 2, 256));
+    ws_rows_ = R;
+    changed = true;
+  }
+  if (kept > ws_kept_) {
+    const int64_t K = std::max<int64_t>(64, next_pow2(kept));
+    ws_hk_ = HbmBuffer(device_, K * H * 2);
+    const int64_t cols = cfg_.output == Output::Scores ? cfg_.labels : vocab_l_;
+    ws_logits_ = HbmBuffer(device_, K * std::max<int64_t>(cols, 8) * 4);
+    ws_idx_ = HbmBuffer(device_, K * 4);
+    ws_val_ = HbmBuffer(device_, K * 4);
+    ws_tokens_ = HbmBuffer(device_, K * 4);
+    ws_kept_ = K;
+    changed = true;
+  }
+  if (splits > ws_splits_ || decode_rows > ws_decode_) {
+    const int64_t S = std::max(splits, ws_splits_), Rd = std::max<int64_t>(std::max(decode_rows, ws_decode_), 64);
+    ws_part_o_ = HbmBuffer(device_, Rd * qh_l_ * S * D * 4);
+    ws_part_lse_ = HbmBuffer(device_, Rd * qh_l_ * S * 4);
+    ws_splits_ = S;
+    ws_decode_ = Rd;
+    changed = true;
+  }
+  if (!ws_gemm_.valid()) {
+    ws_gemm_ = HbmBuffer(device_, 64 << 20);
+    ws_counters_ = HbmBuffer(device_, 65536 * 4);
+    auto st = device_.state();
+    st->check_cuda(cudaMemsetAsync(ws_counters_.data(), 0, ws_counters_.size(), st->stream), "zero");
+    changed = true;
+  }
+  if (changed) clear_graphs();
+}
+
+int64_t DecoderModel::graph_bucket(int64_t rows) const {
+  static const int64_t kBuckets[] = {1, 2, 4, 8, 16, 32, 48, 64, 96, 128, 192, 256, 384, 512};
+  for (int64_t b : kBuckets)
+    if (rows <= b) return b;
+  return 0;
+}
+
+HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cache) {
+  auto st = device_.state();
+  st->check();
+  st->activate();
+  const Limits lim = limits();
+  // Decode-only calls whose every request keeps its last row run as CUDA graphs of padded size.
+  bool graphable = graphs_enabled_;
+  int64_t rows = 0;
+  for (const auto& r : requests) {
+    rows += r.length;
+    graphable = graphable && r.length == 1 && r.keep.kind == KeepKind::Last;
+  }
+  const int64_t bucket = graphable ? graph_bucket(rows) : 0;
+  if (bucket == 0) graphable = false;
+
+  cache.lend();
+  struct GiveBack {
+    Cache& c;
+    ~GiveBack() { c.give_back(); }
+  } give_back{cache};
+
+  const int group = qh_l_ / kvh_l_;
+  // Host staging ring: wait until the slot's previous copy has left the pinned buffer.
+  const int slot = stage_slot_;
+  stage_slot_ ^= 1;
+  st->check_cuda(cudaEventSynchronize(stage_done_[slot]), "staging wait");
+  Plan plan = plan_call(requests, lim, cache, 0, {}, group, graphable ? bucket : 0, host_stage_);
+  if (pinned_stage_[slot].size() < plan.staged.bytes)
+    pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
+  std::memcpy(pinned_stage_[slot].data(), host_stage_.data(), plan.staged.bytes);
+
+  const int64_t splits_needed = plan.decode > 0 ? (plan.max_keys + 511) / 512 : 1;
+  const int64_t splits = next_pow2(splits_needed);
+  ensure_workspace(plan.rows_padded, std::max<int64_t>(plan.kept_padded, 1), splits,
+                   plan.segments_padded);
+  if (!ws_stage_.valid() || ws_stage_.size() < plan.staged.bytes) {
+    ws_stage_ = HbmBuffer(device_, std::max<size_t>(plan.staged.bytes * 2, 1 << 20));
+    clear_graphs();
+  }
+  st->check_cuda(cudaMemcpyAsync(ws_stage_.data(), pinned_stage_[slot].data(), plan.staged.bytes,
+                                 cudaMemcpyHostToDevice, st->stream),
+                 "stage operands");
+  st->check_cuda(cudaEventRecord(stage_done_[slot], st->stream), "staging event");
+  plan.max_keys = splits * 512;  // the decode grid covers the bucket's splits
+
+  if (graphable) {
+    const GraphKey key{bucket, splits};
+    const void* cache_id = cache.layers().empty() ? nullptr : cache.layers()[0].data();
+    auto it = graphs_.find(key);
+    if (it != graphs_.end() && it->second.cache != cache_id) {
+      // The graph reads another cache's layers: capture it again.
+      if (it->second.exec) cudaGraphExecDestroy(it->second.exec);
+      graphs_.erase(it);
+      it = graphs_.end();
+    }
+    if (it != graphs_.end() && it->second.exec != nullptr) {
+      st->check_cuda(cudaGraphLaunch(it->second.exec, st->stream), "graph launch");
+      launches_ += it->second.kernels;
+    } else if (it == graphs_.end()) {
+      // First sight of the shape: run eagerly (configures every kernel), capture next time.
+      launches_ += launch(plan, cache);
+      GraphEntry e;
+      e.cache = cache_id;
+      graphs_[key] = e;
+    } else {
+      cudaGraph_t graph = nullptr;
+      st->check_cuda(cudaStreamBeginCapture(st->stream, cudaStreamCaptureModeThreadLocal), "capture");
+      const int kernels = launch(plan, cache);
+      st->check_cuda(cudaStreamEndCapture(st->stream, &graph), "capture");
+      cudaGraphExec_t exec = nullptr;
+      st->check_cuda(cudaGraphInstantiate(&exec, graph, 0), "graph instantiate");
+      cudaGraphDestroy(graph);
+      it->second.exec = exec;
+      it->second.kernels = kernels;
+      st->check_cuda(cudaGraphLaunch(exec, st->stream), "graph launch");
+      launches_ += kernels;
+    }
+  } else {
+    launches_ += launch(plan, cache);
+  }
+
+  // The kept rows' output in its own buffer, so later calls do not overwrite it.
+  const int H = cfg_.hidden;
+  HbmTensor result = [&]() {
+    if (cfg_.output == Output::Tokens) {
+      HbmBuffer out(device_, std::max<int64_t>(plan.kept * 4, 8));
+      if (plan.kept)
+        st->check_cuda(cudaMemcpyAsync(out.data(), ws_tokens_.data(), plan.kept * 4,
+                                       cudaMemcpyDeviceToDevice, st->stream),
+                       "output copy");
+      return HbmTensor(out, {plan.kept}, DType::I32);
+    }
+    if (cfg_.output == Output::Hidden) {
+      HbmBuffer out(device_, std::max<int64_t>(plan.kept * H * 2, 8));
+      if (plan.kept)
+        st->check_cuda(cudaMemcpyAsync(out.data(), ws_hk_.data(), plan.kept * H * 2,
+                                       cudaMemcpyDeviceToDevice, st->stream),
+                       "output copy");
+      return HbmTensor(out, {plan.kept, H}, DType::BF16);
+    }
+    HbmBuffer out(device_, std::max<int64_t>(plan.kept * cfg_.labels * 4, 8));
+    if (plan.kept)
+      st->check_cuda(cudaMemcpyAsync(out.data(), ws_logits_.data(), plan.kept * cfg_.labels * 4,
+                                     cudaMemcpyDeviceToDevice, st->stream),
+                     "output copy");
+    return HbmTensor(out, {plan.kept, cfg_.labels}, DType::F32);
+  }();
+  last_plan_ = std::move(plan);
+  return result;
+}
+
+int DecoderModel::launch(const Plan& plan, const Cache& cache) {
+  auto st = device_.state();
+  cudaStream_t s = st->stream;
+  const int H = cfg_.hidden, D = cfg_.head_dim;
+  const int64_t T = plan.rows_padded;
+  const Staged& sg = plan.staged;
+  const HbmBuffer& stage = ws_stage_;
+  int kernels = 0;
+  auto fail = [&](int rc, const char* what) {
+    if (rc != 0) st->fail(std::string(what) + " launch rejected (" + std::to_string(rc) + ")");
+    ++kernels;
+  };
+  auto gemm = [&](const void* a, long lda, const void* w, int M, int N, int K, void* c, long ldc,
+                  int epi, const void* res) {
+    foa::GemmArgs g;
+    g.a = a;
+    g.lda = lda;
+    g.w = w;
+    g.ldw = K;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.c = c;
+    g.ldc = ldc;
+    g.residual = res;
+    g.ldr = ldc;
+    g.epilogue = epi;
+    g.workspace = static_cast<float*>(ws_gemm_.data());
+    g.workspace_bytes = ws_gemm_.size();
+    g.counters = i32(ws_counters_);
+    g.counters_len = static_cast<int>(ws_counters_.size() / 4);
+    g.status = st->status;
+    fail(foa::gemm_bf16(g, s), "gemm");
+  };
+  const int qkv_cols = (qh_l_ + 2 * kvh_l_) * D;
+  __nv_bfloat16* x = bf(ws_x_);
+  __nv_bfloat16* h = bf(ws_h_);
+  const auto& W = weights_;
+  auto w = [&](const std::string& n) -> __nv_bfloat16* { return W.at(n).ptr; };
+  const int64_t count = std::max<int64_t>(plan.requests, plan.rows_padded);
+
+  // Tokens: padded rows read ID 0 (zeroed by the staging), the requests' IDs are gathered.
+  fail(foa::gather_tokens(i32(stage, sg.sources), static_cast<int>(count), i32(stage, sg.tokens), s),
+       "gather tokens");
+  // The embedding table is whole on every chip (the head is vocabulary-parallel).
+  fail(foa::embedding(i32(stage, sg.tokens), w("embed"), H, 0, cfg_.vocab, x, H,
+                      static_cast<int>(T), H, s),
+       "embedding");
+  const bool tp = tp_ > 1;
+  float* partial = tp ? coll_->partial_buffer(static_cast<size_t>(T) * H) : nullptr;
+  foa::PagedAttention attn;
+  attn.q = bf(ws_q_);
+  attn.o = bf(ws_attn_);
+  attn.table = i32(stage, sg.table);
+  attn.segments = reinterpret_cast<const foa::Segment*>(i32(stage, sg.segments));
+  attn.q_heads = qh_l_;
+  attn.kv_heads = kvh_l_;
+  attn.head_dim = D;
+  attn.scale = 1.0f / std::sqrt(static_cast<float>(D));
+  attn.partial_o = static_cast<float*>(ws_part_o_.data());
+  attn.partial_lse = static_cast<float*>(ws_part_lse_.data());
+  attn.partial_capacity = static_cast<size_t>(ws_decode_ * qh_l_ * ws_splits_);
+  attn.max_keys = static_cast<int>(plan.max_keys);
+  attn.status = st->status;
+  foa::RopeTable rope{static_cast<const float*>(inv_freq_.data()), attention_factor_};
+
+  for (int l = 0; l < cfg_.layers; ++l) {
+    const std::string p = "layers." + std::to_string(l) + ".";
+    if (l == 0)
+      fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "in_norm"), h, H, nullptr, 0, static_cast<int>(T),
+                        H, cfg_.eps, s),
+           "rmsnorm");
+    gemm(h, H, w(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
+         nullptr);
+    __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(cache.layers()[l].data());
+    fail(foa::qk_norm_rope_cache(bf(ws_qkv_), qkv_cols, static_cast<int>(T), qh_l_, kvh_l_, D,
+                                 cfg_.qk_norm ? w(p + "q_norm") : nullptr,
+                                 cfg_.qk_norm ? w(p + "k_norm") : nullptr, cfg_.eps,
+                                 i32(stage, sg.positions), rope, bf(ws_q_), layer_cache,
+                                 i32(stage, sg.slots), s),
+         "attention front");
+    attn.cache = layer_cache;
+    if (plan.decode > 0) {
+      attn.num_segments = static_cast<int>(plan.prefill > 0 ? plan.decode : plan.segments_padded);
+      fail(foa::paged_decode(attn, s), "decode attention");
+      if (plan.max_keys > 512) ++kernels;  // the split merge
+    }
+    if (plan.prefill > 0) {
+      attn.num_segments = static_cast<int>(plan.decode + plan.prefill);
+      fail(foa::paged_prefill(attn, i32(stage, sg.work), static_cast<int>(plan.work), s),
+           "prefill attention");
+    }
+    const std::string next_norm =
+        l + 1 < cfg_.layers ? "layers." + std::to_string(l + 1) + ".in_norm" : "final_norm";
+    if (!tp) {
+      gemm(ws_attn_.data(), qh_l_ * D, w(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
+           foa::kEpiBf16, x);
+      fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
+                        H, cfg_.eps, s),
+           "rmsnorm");
+      gemm(h, H, w(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
+           foa::kEpiSwiGLU, nullptr);
+      gemm(ws_act_.data(), inter_l_, w(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
+           foa::kEpiBf16, x);
+      fail(foa::rmsnorm(x, H, nullptr, 0, w(next_norm), h, H, nullptr, 0, static_cast<int>(T), H,
+                        cfg_.eps, s),
+           "rmsnorm");
+    } else {
+      gemm(ws_attn_.data(), qh_l_ * D, w(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
+           foa::kEpiF32, nullptr);
+      coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
+      ++kernels;
+      gemm(h, H, w(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
+           foa::kEpiSwiGLU, nullptr);
+      gemm(ws_act_.data(), inter_l_, w(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
+           foa::kEpiF32, nullptr);
+      coll_->add_norm(partial, x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
+      ++kernels;
+    }
+  }
+
+  const int K = static_cast<int>(std::max<int64_t>(plan.kept_padded, 0));
+  if (K == 0) return kernels;
+  fail(foa::gather_rows(h, H, i32(stage, sg.kept), K, bf(ws_hk_), H, H, s), "gather rows");
+  if (cfg_.output == Output::Hidden) return kernels;
+  if (cfg_.output == Output::Scores) {
+    gemm(ws_hk_.data(), H, w("score"), K, cfg_.labels, H, ws_logits_.data(), cfg_.labels,
+         foa::kEpiF32, nullptr);
+    return kernels;
+  }
+  gemm(ws_hk_.data(), H, w("lm_head"), K, vocab_l_, H, ws_logits_.data(), vocab_l_, foa::kEpiF32,
+       nullptr);
+  const int valid = vocab_end_ - vocab_begin_;
+  if (!tp) {
+    fail(foa::argmax_rows(static_cast<float*>(ws_logits_.data()), vocab_l_, K, vocab_l_, valid, 0,
+                          i32(ws_tokens_), nullptr, s),
+         "argmax");
+  } else {
+    fail(foa::argmax_rows(static_cast<float*>(ws_logits_.data()), vocab_l_, K, vocab_l_, valid,
+                          vocab_begin_, i32(ws_idx_), static_cast<float*>(ws_val_.data()), s),
+         "argmax");
+    coll_->argmax(static_cast<float*>(ws_val_.data()), i32(ws_idx_), K, i32(ws_tokens_), s);
+    ++kernels;
+  }
+  return kernels;
+}
+
+}  // namespace foa::engine

@@ -1,0 +1,167 @@
+// Decoder models on one GPU (one rank of a tensor-parallel group): weights, workspace, and the
+// launch sequence of one call, captured into CUDA graphs for decode steps.
+//
+// The reference composes each decoder from Rust module trees scheduled on its NPU
+// (crates/furiosa-opt-models/src/schedule/decoder/mod.rs:398-510, models/decoder/attention/
+// qwen3/launch.rs:60-70). Here a call is a fixed sequence of sm_100a kernels per layer:
+//   RMSNorm -> packed q/k/v GEMM -> QK-norm + RoPE + paged KV write -> paged attention ->
+//   o_proj GEMM (+ residual, or + fused reduce-scatter/all-reduce + residual + RMSNorm across
+//   ranks) -> RMSNorm -> gate/up GEMM with SwiGLU epilogue -> down GEMM (+ residual / fused
+//   collective) -> next RMSNorm,
+// then the kept rows' vocabulary head with a first-maximum argmax.
+#pragma once
+
+#include <cuda_bf16.h>
+
+#include <functional>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "batch.h"
+#include "runtime.h"
+
+namespace foa::engine {
+
+struct RopeSpec {
+  std::string type = "default";  // default | linear | llama3 | yarn
+  double theta = 10000.0;
+  double factor = 1.0;
+  double low_freq_factor = 1.0, high_freq_factor = 4.0;  // llama3
+  double original_max_positions = 0;                     // llama3 / yarn
+  double beta_fast = 32.0, beta_slow = 1.0;              // yarn
+  double mscale = 1.0, mscale_all_dim = 0.0;             // yarn
+  double attention_factor = 0.0;                         // yarn; 0 derives it
+  bool truncate = true;                                  // yarn
+};
+
+// Inverse frequencies of the rotated pairs (FP64 on the host, uploaded as FP32) and the factor
+// cos/sin are scaled by.
+std::vector<float> rope_inv_freq(const RopeSpec& rope, int head_dim, float* attention_factor);
+
+enum class Output { Tokens = 0, Hidden = 1, Scores = 2 };
+
+struct ModelConfig {
+  std::string architecture, family, size, precision = "bfloat16";
+  int hidden = 0, intermediate = 0, layers = 0, q_heads = 0, kv_heads = 0, head_dim = 128;
+  int vocab = 0;
+  float eps = 1e-6f;
+  bool qk_norm = false, tied = false;
+  RopeSpec rope;
+  int window = 0;   // positions a request reaches at most
+  int rows = 8192;  // rows of one call at most
+  Output output = Output::Tokens;
+  int labels = 0;   // score head rows (sequence classification)
+  // Mixture of experts (0 experts: dense)
+  int experts = 0, top_k = 0, expert_intermediate = 0;
+  bool norm_topk = true;
+};
+
+// Tensor-parallel collectives a model's launches need; implemented over NVLink peer memory.
+class Collectives {
+ public:
+  virtual ~Collectives() = default;
+  virtual int rank() const = 0;
+  virtual int world() const = 0;
+  // Sums every rank's FP32 partial [rows, cols] in rank order, adds the BF16 residual (updated in
+  // place, rounded once) and writes RMSNorm(residual) * weight to `out` on every rank.
+  virtual void add_norm(const float* partial, __nv_bfloat16* residual, const __nv_bfloat16* weight,
+                        float eps, __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) = 0;
+  // The first maximum over ranks of (value, token) candidates [rows]: tokens into `out`.
+  virtual void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
+                      cudaStream_t stream) = 0;
+  // Scratch the add_norm partial must live in (symmetric across ranks), at least rows*cols FP32.
+  virtual float* partial_buffer(size_t floats) = 0;
+};
+
+struct WeightSlot {
+  __nv_bfloat16* ptr = nullptr;
+  std::vector<int64_t> shape;  // this rank's shape
+};
+
+class DecoderModel {
+ public:
+  DecoderModel(const Device& device, ModelConfig cfg, int tp, int rank);
+  ~DecoderModel();
+  const ModelConfig& config() const { return cfg_; }
+  Limits limits() const;
+  int tp() const { return tp_; }
+  int rank() const { return rank_; }
+  const Device& device() const { return device_; }
+
+  // Weight slots by engine name ("embed", "layers.3.qkv", ...), this rank's shard.
+  const std::map<std::string, WeightSlot>& weights() const { return weights_; }
+  // Fills every weight with N(0, std) (norm weights with 1) from `seed`.
+  void init_random(uint64_t seed, float std);
+  size_t weight_bytes() const { return arena_bytes_; }
+
+  // Rank geometry.
+  int q_heads_local() const { return qh_l_; }
+  int kv_heads_local() const { return kvh_l_; }
+  int kv_head_first() const { return kvh_first_; }
+  int q_head_first() const { return qh_first_; }
+  int intermediate_local() const { return inter_l_; }
+  int vocab_begin() const { return vocab_begin_; }
+  int vocab_end() const { return vocab_end_; }
+  int vocab_local() const { return vocab_l_; }
+
+  void set_collectives(std::shared_ptr<Collectives> c) { coll_ = std::move(c); }
+  void set_graphs(bool enabled) { graphs_enabled_ = enabled; }
+
+  // One call: plans, stages and launches; returns the kept rows' output (tokens I32 [kept],
+  // hidden BF16 [kept, hidden] or scores F32 [kept, labels]) once the launches are submitted.
+  HbmTensor forward(const std::vector<Request>& requests, Cache& cache);
+
+  // Timing hooks for benchmarks: the last call's plan, and the kernels launched so far (graph
+  // replays count every kernel node).
+  const Plan& last_plan() const { return last_plan_; }
+  uint64_t kernel_launches() const { return launches_; }
+
+ private:
+  void allocate_weights();
+  void ensure_workspace(int64_t rows, int64_t kept, int64_t decode_splits, int64_t decode_rows);
+  int launch(const Plan& plan, const Cache& cache);  // returns the kernels it launched
+  int64_t graph_bucket(int64_t rows) const;
+
+  Device device_;
+  ModelConfig cfg_;
+  int tp_, rank_;
+  int qh_l_, kvh_l_, qh_first_, kvh_first_, inter_l_, vocab_begin_, vocab_end_, vocab_l_;
+  std::map<std::string, WeightSlot> weights_;
+  HbmBuffer arena_;
+  size_t arena_bytes_ = 0;
+  std::vector<float> inv_freq_host_;
+  float attention_factor_ = 1.f;
+  HbmBuffer inv_freq_;
+
+  // Workspace (device), sized for `ws_rows_` rows and `ws_kept_` kept rows.
+  int64_t ws_rows_ = 0, ws_kept_ = 0, ws_splits_ = 0, ws_decode_ = 0;
+  HbmBuffer ws_x_, ws_h_, ws_qkv_, ws_q_, ws_attn_, ws_act_, ws_hk_, ws_logits_, ws_idx_, ws_val_,
+      ws_tokens_, ws_stage_, ws_part_o_, ws_part_lse_, ws_gemm_, ws_counters_, ws_partial_;
+  size_t stage_capacity_ = 0;
+  std::vector<uint8_t> host_stage_;
+  HostBuffer pinned_stage_[2];
+  cudaEvent_t stage_done_[2] = {nullptr, nullptr};
+  int stage_slot_ = 0;
+
+  std::shared_ptr<Collectives> coll_;
+  bool graphs_enabled_ = true;
+  struct GraphKey {
+    int64_t rows, splits;
+    bool operator<(const GraphKey& o) const {
+      return rows < o.rows || (rows == o.rows && splits < o.splits);
+    }
+  };
+  struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    int kernels = 0;
+    const void* cache = nullptr;
+  };
+  std::map<GraphKey, GraphEntry> graphs_;
+  uint64_t launches_ = 0;
+  void clear_graphs();
+  Plan last_plan_;
+};
+
+}  // namespace foa::engine

@@ -8,6 +8,7 @@
 
 #include <cfloat>
 #include <climits>
+#include <algorithm>
 
 #include "ops.cuh"
 #include "sm100.cuh"
@@ -234,7 +235,80 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
   }
 }
 
+// ------------------------------------------------------------------------------------ init / gather
+// SplitMix64-style mixing of (seed, index) into 64 random bits.
+__device__ __forceinline__ uint64_t mix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+__global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64_t seed) {
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const uint64_t r = mix64(seed * 0x100000001B3ull + (uint64_t)i);
+    // Box-Muller on two 24-bit uniforms in (0, 1].
+    const float u1 = ((float)(r & 0xFFFFFF) + 1.0f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((r >> 24) & 0xFFFFFF) * (1.0f / 16777216.0f);
+    const float z = sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2);
+    dst[i] = __float2bfloat16_rn(z * std);
+  }
+}
+
+__global__ void fill_bf16_kernel(__nv_bfloat16* dst, long n, float v) {
+  const __nv_bfloat16 b = __float2bfloat16_rn(v);
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    dst[i] = b;
+}
+
+__global__ void gather_tokens_kernel(const int32_t* sources, int count, int32_t* out) {
+  const int s = blockIdx.x;
+  if (s >= count) return;
+  const int32_t* rec = sources + 4 * s;
+  const uint64_t addr = (uint64_t)(uint32_t)rec[0] | ((uint64_t)(uint32_t)rec[1] << 32);
+  const int32_t* src = reinterpret_cast<const int32_t*>(addr);
+  const int len = rec[2], first = rec[3];
+  for (int i = threadIdx.x; i < len; i += blockDim.x) out[first + i] = src[i];
+}
+
+__global__ void gather_rows_kernel(const __nv_bfloat16* in, long ldi, const int32_t* rows,
+                                   __nv_bfloat16* out, long ldo, int cols) {
+  const int i = blockIdx.x;
+  const int r = rows[i];
+  for (int v = threadIdx.x; v < cols / 8; v += blockDim.x)
+    reinterpret_cast<uint4*>(out + (long)i * ldo)[v] =
+        reinterpret_cast<const uint4*>(in + (long)r * ldi)[v];
+}
+
 }  // namespace
+
+int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  init_normal_kernel<<<grid, 256, 0, stream>>>(dst, n, std, seed);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int fill_bf16(__nv_bfloat16* dst, long n, float value, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  fill_bf16_kernel<<<grid, 256, 0, stream>>>(dst, n, value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int gather_tokens(const int32_t* sources, int count, int32_t* out, cudaStream_t stream) {
+  if (count <= 0) return 0;
+  gather_tokens_kernel<<<count, 128, 0, stream>>>(sources, count, out);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int gather_rows(const __nv_bfloat16* in, long ldi, const int32_t* rows, int n, __nv_bfloat16* out,
+                long ldo, int cols, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  if (cols % 8 != 0) return -2;
+  gather_rows_kernel<<<n, 128, 0, stream>>>(in, ldi, rows, out, ldo, cols);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
 
 int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, long ldr,
             const __nv_bfloat16* weight, __nv_bfloat16* out, long ldo,

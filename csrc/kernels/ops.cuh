@@ -52,4 +52,19 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slot_mapping,
                        cudaStream_t stream);
 
+// Fills `n` BF16 values with N(0, std) from a counter-based hash of (seed, index): the same
+// values on every device and every run.
+int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream);
+
+// Fills `n` BF16 values with a constant.
+int fill_bf16(__nv_bfloat16* dst, long n, float value, cudaStream_t stream);
+
+// Token gather: `sources` holds `count` records (address low, address high, length, first row) of
+// I32 device arrays; copies each into `out` at its first row.
+int gather_tokens(const int32_t* sources, int count, int32_t* out, cudaStream_t stream);
+
+// out[i, :] = in[rows[i], :] for i < n, BF16 rows of `cols` elements.
+int gather_rows(const __nv_bfloat16* in, long ldi, const int32_t* rows, int n, __nv_bfloat16* out,
+                long ldo, int cols, cudaStream_t stream);
+
 }  // namespace foa

@@ -1,0 +1,599 @@
+// The engine's Python classes: the surface of the `furiosa_opt_engine` wheel (its generated stubs
+// name every class and method: crates/furiosa-opt-engine/python/furiosa_opt_engine/*.pyi).
+//
+// Calls release the GIL around device work. Errors map to Python classes by kind: invalid input
+// to ValueError, a refused feature to NotImplementedError, a device failure to RuntimeError, a
+// file failure to OSError.
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <cstring>
+
+#include "engine/batch.h"
+#include "engine/model.h"
+#include "engine/registry.h"
+#include "engine/runtime.h"
+
+namespace py = pybind11;
+using namespace foa::engine;
+
+namespace {
+
+// ------------------------------------------------------------------------------------ helpers
+struct Range {
+  int64_t start = 0, stop = 0, step = 1;
+};
+
+Range to_range(const py::object& r) {
+  if (!py::isinstance(r, py::module_::import("builtins").attr("range")))
+    throw py::type_error("expected a range");
+  return Range{r.attr("start").cast<int64_t>(), r.attr("stop").cast<int64_t>(),
+               r.attr("step").cast<int64_t>()};
+}
+
+py::object make_range(int64_t a, int64_t b) {
+  return py::module_::import("builtins").attr("range")(a, b);
+}
+
+int process_rank(size_t chips) {
+  // A placement of N chips runs as N processes, one per GPU: this process serves chips[rank].
+  if (chips <= 1) return 0;
+  py::object dist = py::module_::import("furiosa_opt_models_b200.parallel.dist");
+  return dist.attr("rank_for_chips")(chips).cast<int>();
+}
+
+// ------------------------------------------------------------------------------------ Placement
+struct Placement {
+  std::vector<int> chips;
+  int64_t pes_begin = 0, pes_end = 0;
+};
+
+// ------------------------------------------------------------------------------------ tensors
+py::array host_numpy(const std::vector<int64_t>& shape, DType dtype, const uint8_t* data) {
+  std::vector<py::ssize_t> dims(shape.begin(), shape.end());
+  auto np = py::module_::import("numpy");
+  size_t n = 1;
+  for (auto s : shape) n *= static_cast<size_t>(s);
+  auto copy = [&](const char* fmt) {
+    py::array a(py::dtype(fmt), dims);
+    std::memcpy(a.mutable_data(), data, n * dtype_size(dtype));
+    return a;
+  };
+  switch (dtype) {
+    case DType::Bool: return copy("?");
+    case DType::U8: return copy("u1");
+    case DType::I8: return copy("i1");
+    case DType::I16: return copy("i2");
+    case DType::I32: return copy("i4");
+    case DType::I64: return copy("i8");
+    case DType::F16: return copy("f2");
+    case DType::F32: return copy("f4");
+    case DType::F64: return copy("f8");
+    case DType::BF16: {
+      // NumPy has no BF16: observe the values as lossless F32.
+      py::array_t<float> a(dims);
+      auto* out = a.mutable_data();
+      for (size_t i = 0; i < n; ++i) {
+        uint32_t bits = static_cast<uint32_t>(reinterpret_cast<const uint16_t*>(data)[i]) << 16;
+        std::memcpy(out + i, &bits, 4);
+      }
+      return a;
+    }
+    case DType::F8E4M3:
+    case DType::F8E5M2: return copy("u1");
+  }
+  return copy("u1");
+}
+
+}  // namespace
+
+// Decoder objects the binding hands out: the model, its load's descriptive fields.
+struct PyDecoder {
+  std::shared_ptr<DecoderModel> model;
+  std::string size, precision, kv_cache = "bfloat16";
+  int parallel = 1;
+};
+struct PyQwen3ForCausalLM : PyDecoder {};
+struct PyQwen3ForSequenceClassification : PyDecoder {};
+struct PyQwen3Model : PyDecoder {};
+struct PyLlamaForCausalLM : PyDecoder {};
+struct PyMistralForCausalLM : PyDecoder {};
+struct PyQwen3MoeForCausalLM : PyDecoder {};
+
+struct PyCacheSpec {
+  CacheSpec spec;
+  Device device;
+};
+struct PyCache {
+  std::shared_ptr<Cache> cache;
+  Device device;
+};
+
+struct PyRequest {
+  std::vector<std::vector<int64_t>> rows;
+  int64_t cached = 0;
+  std::shared_ptr<HbmTensor> tokens;
+  Keep keep;
+  py::object keep_obj;
+  std::optional<int64_t> adapter;
+  py::object positions = py::none(), mask = py::none();
+  std::vector<std::pair<int64_t, py::object>> overrides;
+};
+
+enum class PyKeep { NONE, LAST, ALL };
+enum class PyOutput { TOKENS, HIDDEN, SCORES };
+
+struct PyKind {
+  KindTag tag = KindTag::Paged;
+  int64_t length = 0;
+};
+struct PyKindPaged : PyKind {};
+struct PyKindState : PyKind {};
+struct PyKindCross : PyKind {};
+
+ModelConfig model_config_from_dict(const py::dict& d) {
+  ModelConfig c;
+  auto get = [&](const char* k, auto def) {
+    using T = decltype(def);
+    return d.contains(k) ? d[k].cast<T>() : def;
+  };
+  c.architecture = get("architecture", std::string("Qwen3ForCausalLM"));
+  c.family = get("family", std::string("qwen3"));
+  c.size = get("size", std::string("custom"));
+  c.precision = get("precision", std::string("bfloat16"));
+  c.hidden = get("hidden", 0);
+  c.intermediate = get("intermediate", 0);
+  c.layers = get("layers", 0);
+  c.q_heads = get("q_heads", 0);
+  c.kv_heads = get("kv_heads", 0);
+  c.head_dim = get("head_dim", 128);
+  c.vocab = get("vocab", 0);
+  c.eps = get("eps", 1e-6f);
+  c.qk_norm = get("qk_norm", false);
+  c.tied = get("tied", false);
+  c.window = get("window", 32768);
+  c.rows = get("rows", 8192);
+  c.labels = get("labels", 0);
+  c.experts = get("experts", 0);
+  c.top_k = get("top_k", 0);
+  c.expert_intermediate = get("expert_intermediate", 0);
+  c.norm_topk = get("norm_topk", true);
+  const std::string out = get("output", std::string("tokens"));
+  c.output = out == "hidden" ? Output::Hidden : out == "scores" ? Output::Scores : Output::Tokens;
+  if (d.contains("rope")) {
+    py::dict r = d["rope"];
+    auto rg = [&](const char* k, auto def) {
+      using T = decltype(def);
+      return r.contains(k) && !r[k].is_none() ? r[k].cast<T>() : def;
+    };
+    c.rope.type = rg("type", std::string("default"));
+    c.rope.theta = rg("theta", 10000.0);
+    c.rope.factor = rg("factor", 1.0);
+    c.rope.low_freq_factor = rg("low_freq_factor", 1.0);
+    c.rope.high_freq_factor = rg("high_freq_factor", 4.0);
+    c.rope.original_max_positions = rg("original_max_positions", 0.0);
+    c.rope.beta_fast = rg("beta_fast", 32.0);
+    c.rope.beta_slow = rg("beta_slow", 1.0);
+    c.rope.mscale = rg("mscale", 1.0);
+    c.rope.mscale_all_dim = rg("mscale_all_dim", 0.0);
+    c.rope.attention_factor = rg("attention_factor", 0.0);
+    c.rope.truncate = rg("truncate", true);
+  }
+  return c;
+}
+
+void bind_checkpoint_and_load(py::module_& m);
+
+void bind_engine(py::module_& m) {
+  // Exception classes by kind.
+  py::register_exception_translator([](std::exception_ptr p) {
+    try {
+      if (p) std::rethrow_exception(p);
+    } catch (const ValueError& e) {
+      PyErr_SetString(PyExc_ValueError, e.what());
+    } catch (const Unsupported& e) {
+      PyErr_SetString(PyExc_NotImplementedError, e.what());
+    } catch (const DeviceError& e) {
+      PyErr_SetString(PyExc_RuntimeError, e.what());
+    } catch (const IoError& e) {
+      PyErr_SetString(PyExc_OSError, e.what());
+    }
+  });
+
+  py::module_ decoder = m.def_submodule("decoder", "Decoder calls: requests, caches and outputs.");
+  py::module_ qwen3 = m.def_submodule("qwen3", "Qwen3 decoders.");
+  py::module_ llama = m.def_submodule("llama", "Llama decoders.");
+  py::module_ mistral = m.def_submodule("mistral", "Mistral decoders.");
+  py::module_ qwen3_moe = m.def_submodule("qwen3_moe", "Qwen3 mixture-of-experts decoders.");
+
+  // ---------------------------------------------------------------- Placement / Device
+  py::class_<Placement>(m, "Placement", "Physical chips, in rank order, and the PEs used on each.")
+      .def(py::init([](const std::vector<int>& chips, const py::object& pes) {
+             Range r = to_range(pes);
+             if (r.step != 1) throw ValueError("pes has a step other than 1");
+             return Placement{chips, r.start, r.stop};
+           }),
+           py::arg("chips"), py::arg("pes"))
+      .def_property_readonly("chips", [](const Placement& p) { return p.chips; })
+      .def_property_readonly("pes", [](const Placement& p) { return make_range(p.pes_begin, p.pes_end); })
+      .def("__eq__", [](const Placement& a, const py::object& o) {
+        if (!py::isinstance<Placement>(o)) return false;
+        const auto& b = o.cast<const Placement&>();
+        return a.chips == b.chips && a.pes_begin == b.pes_begin && a.pes_end == b.pes_end;
+      })
+      .def("__repr__", [](const Placement& p) {
+        std::string s = "Placement(chips=[";
+        for (size_t i = 0; i < p.chips.size(); ++i) s += (i ? ", " : "") + std::to_string(p.chips[i]);
+        return s + "], pes=range(" + std::to_string(p.pes_begin) + ", " + std::to_string(p.pes_end) + "))";
+      });
+
+  py::class_<Device>(m, "Device", "An opened device; memory sizes are bytes per chip.")
+      .def(py::init([](const Placement& p) {
+             const int rank = process_rank(p.chips.size());
+             py::gil_scoped_release nogil;
+             return Device(p.chips, static_cast<int>(p.pes_begin), static_cast<int>(p.pes_end), rank);
+           }),
+           py::arg("placement"))
+      .def_property_readonly("capacity", &Device::capacity)
+      .def_property_readonly("available", &Device::available)
+      .def_property_readonly("chips", &Device::chips)
+      .def_property_readonly("rank", [](const Device& d) { return d.state()->rank; })
+      .def_property_readonly("ordinal", [](const Device& d) { return d.state()->ordinal; })
+      .def_property_readonly("stream", [](const Device& d) { return reinterpret_cast<uint64_t>(d.state()->stream); })
+      .def("synchronize", [](const Device& d) {
+        py::gil_scoped_release nogil;
+        d.synchronize();
+      });
+
+  // ---------------------------------------------------------------- buffers / transfers
+  py::class_<Transfer>(m, "Transfer", "A submitted copy between a HostBuffer and an HbmBuffer.")
+      .def("done", &Transfer::done)
+      .def("wait", [](const Transfer& t) {
+        py::gil_scoped_release nogil;
+        t.wait();
+      });
+
+  py::class_<HostBuffer>(m, "HostBuffer", py::buffer_protocol(),
+                         "Page-locked host memory that copies read and write.")
+      .def(py::init([](const py::object& source) {
+             if (py::isinstance<py::int_>(source)) {
+               const int64_t n = source.cast<int64_t>();
+               if (n < 0) throw py::value_error("negative size");
+               return HostBuffer(static_cast<size_t>(n));
+             }
+             if (!PyObject_CheckBuffer(source.ptr()))
+               throw py::type_error("source is neither an integer nor a C-contiguous buffer");
+             py::buffer_info info = py::buffer(source).request();
+             Py_buffer view;
+             if (PyObject_GetBuffer(source.ptr(), &view, PyBUF_C_CONTIGUOUS) != 0) {
+               PyErr_Clear();
+               throw py::type_error("source is not C-contiguous");
+             }
+             HostBuffer b(view.buf, static_cast<size_t>(view.len));
+             PyBuffer_Release(&view);
+             return b;
+           }),
+           py::arg("source"))
+      .def("__len__", &HostBuffer::size)
+      .def("slice", &HostBuffer::slice, py::arg("offset"), py::arg("size"))
+      .def("to_hbm", &HostBuffer::to_hbm, py::arg("buffer"))
+      .def_buffer([](HostBuffer& b) -> py::buffer_info {
+        // Exporting waits for the copies already submitted on the bytes.
+        if (auto t = b.last()) Transfer(t).wait();
+        return py::buffer_info(b.data(), 1, py::format_descriptor<uint8_t>::format(), 1,
+                               {static_cast<py::ssize_t>(b.size())}, {1});
+      });
+
+  py::class_<HbmBuffer>(m, "HbmBuffer", "Device memory of len bytes on each chip.")
+      .def(py::init([](const Device& d, int64_t size) {
+             if (size < 0) throw ValueError("negative size");
+             return HbmBuffer(d, static_cast<size_t>(size));
+           }),
+           py::arg("device"), py::arg("size"))
+      .def("__len__", &HbmBuffer::size)
+      .def("slice", &HbmBuffer::slice, py::arg("offset"), py::arg("size"))
+      .def("to_host", [](const HbmBuffer& b, const HostBuffer& h) { return copy_to_host(b, h); },
+           py::arg("host"))
+      .def_property_readonly("data_ptr", [](const HbmBuffer& b) { return reinterpret_cast<uint64_t>(b.data()); });
+
+  // ---------------------------------------------------------------- tensors
+  py::class_<HbmTensor, std::shared_ptr<HbmTensor>>(m, "HbmTensor",
+                                                   "Dense row-major elements in an HbmBuffer.")
+      .def(py::init([](const HbmBuffer& b, const std::vector<int64_t>& shape, const std::string& dtype) {
+             return std::make_shared<HbmTensor>(b, shape, dtype_from_name(dtype));
+           }),
+           py::arg("buffer"), py::arg("shape"), py::arg("dtype"))
+      .def_property_readonly("shape", &HbmTensor::shape)
+      .def_property_readonly("dtype", [](const HbmTensor& t) { return std::string(dtype_name(t.dtype())); })
+      .def_property_readonly("buffer", &HbmTensor::buffer)
+      .def_property_readonly("data_ptr", [](const HbmTensor& t) { return reinterpret_cast<uint64_t>(t.buffer().data()); })
+      .def("wait", [](const HbmTensor& t) {
+        py::gil_scoped_release nogil;
+        t.wait();
+      })
+      .def("to_host", [](const HbmTensor& t) {
+        std::vector<uint8_t> bytes;
+        {
+          py::gil_scoped_release nogil;
+          bytes = t.to_host_bytes();
+        }
+        return HostTensor(t.shape(), t.dtype(), bytes.data());
+      })
+      .def("__getitem__", [](const HbmTensor& t, const py::slice& s) {
+        if (t.shape().empty()) throw ValueError("the tensor has no axes");
+        py::ssize_t start, stop, step, len;
+        if (!s.compute(static_cast<py::ssize_t>(t.shape()[0]), &start, &stop, &step, &len))
+          throw py::error_already_set();
+        if (step != 1) throw ValueError("the slice steps by other than one row");
+        return std::make_shared<HbmTensor>(t.rows(start, std::max(start, stop)));
+      });
+
+  py::class_<HostTensor>(m, "HostTensor", "A host tensor, its contents copied on construction.")
+      .def(py::init([](const py::object& values, const py::object& dtype) {
+             py::object np = py::module_::import("numpy");
+             py::object helper = py::module_::import("furiosa_opt_engine._host");
+             py::tuple t = helper.attr("from_values")(values, dtype);
+             std::vector<int64_t> shape = t[0].cast<std::vector<int64_t>>();
+             std::string name = t[1].cast<std::string>();
+             py::bytes raw = t[2];
+             std::string s = raw;
+             return HostTensor(shape, dtype_from_name(name), s.data());
+           }),
+           py::arg("values"), py::kw_only(), py::arg("dtype") = py::none())
+      .def_static("empty", [](const std::vector<int64_t>& shape, const std::string& dtype) {
+        return HostTensor(shape, dtype_from_name(dtype));
+      }, py::arg("shape"), py::kw_only(), py::arg("dtype"))
+      .def_static("from_dlpack", [](const py::object& value) {
+        py::object helper = py::module_::import("furiosa_opt_engine._host");
+        py::tuple t = helper.attr("from_dlpack")(value);
+        std::vector<int64_t> shape = t[0].cast<std::vector<int64_t>>();
+        std::string s = t[2].cast<py::bytes>();
+        return HostTensor(shape, dtype_from_name(t[1].cast<std::string>()), s.data());
+      }, py::arg("value"))
+      .def_property_readonly("shape", &HostTensor::shape)
+      .def_property_readonly("dtype", [](const HostTensor& t) { return std::string(dtype_name(t.dtype())); })
+      .def("write", [](HostTensor& t, const py::bytes& b) {
+        std::string s = b;
+        t.write(s.data(), s.size());
+      }, py::arg("bytes"))
+      .def("numpy", [](const HostTensor& t) { return host_numpy(t.shape(), t.dtype(), t.data()); })
+      .def("raw", [](const HostTensor& t) { return py::bytes(reinterpret_cast<const char*>(t.data()), t.nbytes()); })
+      .def("to_hbm", [](const HostTensor& t, const Device& d) {
+        py::gil_scoped_release nogil;
+        return std::make_shared<HbmTensor>(t.to_hbm(d));
+      }, py::arg("device"));
+
+  // ---------------------------------------------------------------- decoder: cache
+  py::class_<Pool>(decoder, "Pool", "A block format.")
+      .def(py::init([](int64_t block, int64_t bytes) { return Pool{block, bytes}; }), py::arg("block"), py::arg("bytes"))
+      .def_readonly("block", &Pool::block)
+      .def_readonly("bytes", &Pool::bytes)
+      .def("__eq__", [](const Pool& a, const Pool& b) { return a == b; })
+      .def("__repr__", [](const Pool& p) {
+        return "Pool(block=" + std::to_string(p.block) + ", bytes=" + std::to_string(p.bytes) + ")";
+      });
+
+  py::class_<PyKind> kind(decoder, "Kind", "What the blocks of a group hold.");
+  py::class_<PyKindPaged, PyKind>(kind, "Paged").def(py::init([]() { return PyKindPaged{{KindTag::Paged, 0}}; }))
+      .def("__eq__", [](const PyKind& a, const py::object& o) {
+        return py::isinstance<PyKindPaged>(o);
+      });
+  py::class_<PyKindState, PyKind>(kind, "State").def(py::init([]() { return PyKindState{{KindTag::State, 0}}; }))
+      .def("__eq__", [](const PyKind& a, const py::object& o) { return py::isinstance<PyKindState>(o); });
+  py::class_<PyKindCross, PyKind>(kind, "Cross")
+      .def(py::init([](int64_t length) { return PyKindCross{{KindTag::Cross, length}}; }), py::arg("length"))
+      .def_property_readonly("length", [](const PyKindCross& k) { return k.length; })
+      .def("__eq__", [](const PyKind& a, const py::object& o) {
+        return py::isinstance<PyKindCross>(o) && o.cast<const PyKind&>().length == a.length;
+      });
+
+  py::class_<Group>(decoder, "Group", "Layers whose cache has one kind and takes its blocks from one pool.")
+      .def_readonly("pool", &Group::pool)
+      .def_property_readonly("layers", [](const Group& g) { return make_range(g.layers_begin, g.layers_end); })
+      .def_property_readonly("kind", [](const Group& g) -> py::object {
+        switch (g.kind.tag) {
+          case KindTag::Paged: return py::cast(PyKindPaged{{KindTag::Paged, 0}});
+          case KindTag::State: return py::cast(PyKindState{{KindTag::State, 0}});
+          default: return py::cast(PyKindCross{{KindTag::Cross, g.kind.length}});
+        }
+      })
+      .def_property_readonly("window", [](const Group& g) -> py::object {
+        return g.window ? py::cast(*g.window) : py::none();
+      });
+
+  py::class_<PyCacheSpec>(decoder, "CacheSpec", "The cache a loaded decoder's calls read.")
+      .def_property_readonly("pools", [](const PyCacheSpec& s) { return s.spec.pools; })
+      .def_property_readonly("groups", [](const PyCacheSpec& s) { return s.spec.groups; })
+      .def("__eq__", [](const PyCacheSpec& a, const PyCacheSpec& b) { return a.spec == b.spec; });
+
+  py::class_<PyCache>(decoder, "Cache", "The storage of a CacheSpec on the decoder's device.")
+      .def(py::init([](const PyCacheSpec& spec, int64_t blocks) {
+             if (blocks <= 0) throw ValueError("cache blocks must be positive");
+             py::gil_scoped_release nogil;
+             return PyCache{std::make_shared<Cache>(spec.device, spec.spec, blocks), spec.device};
+           }),
+           py::arg("spec"), py::arg("blocks"))
+      .def_property_readonly("blocks", [](const PyCache& c) { return c.cache->blocks(); })
+      .def_property_readonly("spec", [](const PyCache& c) { return PyCacheSpec{c.cache->spec(), c.device}; })
+      .def_property_readonly("layers", [](const PyCache& c) { return c.cache->layers(); });
+
+  // ---------------------------------------------------------------- decoder: requests
+  py::enum_<PyKeep>(decoder, "Keep", "The appended rows of a request that a call returns.")
+      .value("NONE", PyKeep::NONE)
+      .value("LAST", PyKeep::LAST)
+      .value("ALL", PyKeep::ALL);
+  py::enum_<PyOutput>(decoder, "Output", "What a decoder's call returns of each kept row.")
+      .value("TOKENS", PyOutput::TOKENS)
+      .value("HIDDEN", PyOutput::HIDDEN)
+      .value("SCORES", PyOutput::SCORES);
+
+  py::class_<PyRequest>(decoder, "Request", "One sequence's tokens after the cached positions its blocks hold.")
+      .def(py::init([](const std::vector<std::vector<int64_t>>& rows, int64_t cached,
+                       std::shared_ptr<HbmTensor> tokens, const py::object& keep,
+                       const py::object& adapter, const py::object& positions,
+                       const py::object& mask, const py::object& overrides) {
+             if (tokens->dtype() != DType::I32 || tokens->shape().size() != 1)
+               throw ValueError("tokens are not one-dimensional I32 IDs");
+             if (cached < 0) throw ValueError("cached positions are not negative");
+             PyRequest r;
+             r.rows = rows;
+             r.cached = cached;
+             r.tokens = tokens;
+             r.keep_obj = keep;
+             if (py::isinstance<PyKeep>(keep)) {
+               switch (keep.cast<PyKeep>()) {
+                 case PyKeep::NONE: r.keep.kind = KeepKind::None; break;
+                 case PyKeep::LAST: r.keep.kind = KeepKind::Last; break;
+                 case PyKeep::ALL: r.keep.kind = KeepKind::All; break;
+               }
+             } else {
+               Range k = to_range(keep);
+               if (k.step != 1 || k.start < 0 || k.stop < 0)
+                 throw ValueError("keep is a range with a step other than 1 or a negative bound");
+               r.keep = Keep{KeepKind::Range, k.start, k.stop};
+             }
+             if (!adapter.is_none()) r.adapter = adapter.cast<int64_t>();
+             r.positions = positions;
+             r.mask = mask;
+             for (auto item : overrides) {
+               py::tuple t = item.cast<py::tuple>();
+               r.overrides.push_back({t[0].cast<int64_t>(), t[1]});
+             }
+             return r;
+           }),
+           py::arg("rows"), py::arg("cached"), py::arg("tokens"),
+           py::arg("keep") = PyKeep::LAST, py::kw_only(), py::arg("adapter") = py::none(),
+           py::arg("positions") = py::none(), py::arg("mask") = py::none(),
+           py::arg("overrides") = py::list())
+      .def_readonly("rows", &PyRequest::rows)
+      .def_readonly("cached", &PyRequest::cached)
+      .def_readonly("tokens", &PyRequest::tokens)
+      .def_readonly("keep", &PyRequest::keep_obj)
+      .def_readonly("adapter", &PyRequest::adapter)
+      .def_readonly("positions", &PyRequest::positions)
+      .def_readonly("mask", &PyRequest::mask)
+      .def_property_readonly("overrides", [](const PyRequest& r) {
+        py::list l;
+        for (auto& o : r.overrides) l.append(py::make_tuple(o.first, o.second));
+        return l;
+      });
+
+  // ---------------------------------------------------------------- decoders
+  auto forward = [](PyDecoder& d, const std::vector<PyRequest*>& requests, PyCache& cache,
+                    const py::object& adapters) {
+    std::vector<Request> reqs;
+    reqs.reserve(requests.size());
+    for (const PyRequest* pr : requests) {
+      Request r;
+      r.rows = pr->rows;
+      r.cached = pr->cached;
+      r.tokens = pr->tokens->buffer();
+      r.length = pr->tokens->shape()[0];
+      if (pr->tokens->buffer().device() != d.model->device().state())
+        throw ValueError("a tensor lies on another device");
+      r.keep = pr->keep;
+      r.adapter = pr->adapter;
+      r.positions = !pr->positions.is_none();
+      r.mask = !pr->mask.is_none();
+      r.overrides = !pr->overrides.empty();
+      reqs.push_back(std::move(r));
+    }
+    if (!adapters.is_none() && py::len(adapters) > 0) {
+      // No loaded decoder takes adapters: the planner refuses with the reference's message.
+      const Limits lim = d.model->limits();
+      if (lim.adapters == 0) throw Unsupported("adapters are not served");
+    }
+    py::gil_scoped_release nogil;
+    std::lock_guard<std::mutex> g(d.model->device().state()->mu);
+    return std::make_shared<HbmTensor>(d.model->forward(reqs, *cache.cache));
+  };
+
+  py::class_<PyDecoder>(m, "Decoder", "A decoder loaded on a device, whatever its model.")
+      .def_property_readonly("size", [](const PyDecoder& d) { return d.size; })
+      .def_property_readonly("precision", [](const PyDecoder& d) { return d.precision; })
+      .def_property_readonly("parallel", [](const PyDecoder& d) { return d.parallel; })
+      .def_property_readonly("kv_cache", [](const PyDecoder& d) { return d.kv_cache; })
+      .def_property_readonly("cache", [](const PyDecoder& d) {
+        return PyCacheSpec{d.model->limits().cache, d.model->device()};
+      })
+      .def_property_readonly("window", [](const PyDecoder& d) { return d.model->limits().window; })
+      .def_property_readonly("rows", [](const PyDecoder& d) { return d.model->limits().rows; })
+      .def_property_readonly("device", [](const PyDecoder& d) { return d.model->device(); })
+      .def_property_readonly("output", [](const PyDecoder& d) {
+        switch (d.model->config().output) {
+          case Output::Hidden: return PyOutput::HIDDEN;
+          case Output::Scores: return PyOutput::SCORES;
+          default: return PyOutput::TOKENS;
+        }
+      })
+      .def_property_readonly("adapters", [](const PyDecoder&) { return py::none(); })
+      .def("forward", forward, py::arg("requests"), py::arg("cache"), py::arg("adapters") = py::none())
+      .def("set_graphs", [](PyDecoder& d, bool on) { d.model->set_graphs(on); })
+      .def_property_readonly("weight_bytes", [](const PyDecoder& d) { return d.model->weight_bytes(); })
+      .def_property_readonly("kernel_launches", [](const PyDecoder& d) { return d.model->kernel_launches(); })
+      .def_property_readonly("last_staged_bytes", [](const PyDecoder& d) { return d.model->last_plan().staged.bytes; })
+      .def("weight", [](const PyDecoder& d, const std::string& name) {
+        const auto& w = d.model->weights().at(name);
+        return py::make_tuple(reinterpret_cast<uint64_t>(w.ptr), w.shape);
+      })
+      .def("weight_names", [](const PyDecoder& d) {
+        std::vector<std::string> n;
+        for (auto& [k, v] : d.model->weights()) n.push_back(k);
+        return n;
+      })
+      .def_property_readonly("geometry", [](const PyDecoder& d) {
+        py::dict g;
+        g["q_heads"] = d.model->q_heads_local();
+        g["kv_heads"] = d.model->kv_heads_local();
+        g["q_head_first"] = d.model->q_head_first();
+        g["kv_head_first"] = d.model->kv_head_first();
+        g["intermediate"] = d.model->intermediate_local();
+        g["vocab_begin"] = d.model->vocab_begin();
+        g["vocab_end"] = d.model->vocab_end();
+        g["vocab_local"] = d.model->vocab_local();
+        g["tp"] = d.model->tp();
+        g["rank"] = d.model->rank();
+        return g;
+      });
+
+  py::class_<PyQwen3ForCausalLM, PyDecoder>(qwen3, "ForCausalLM", "HF Qwen3ForCausalLM, loaded on a device.");
+  py::class_<PyQwen3ForSequenceClassification, PyDecoder>(qwen3, "ForSequenceClassification",
+                                                         "HF Qwen3ForSequenceClassification, loaded on a device.");
+  py::class_<PyQwen3Model, PyDecoder>(qwen3, "Model", "HF Qwen3Model, loaded on a device.");
+  py::class_<PyLlamaForCausalLM, PyDecoder>(llama, "ForCausalLM", "HF LlamaForCausalLM, loaded on a device.");
+  py::class_<PyMistralForCausalLM, PyDecoder>(mistral, "ForCausalLM", "HF MistralForCausalLM, loaded on a device.");
+  py::class_<PyQwen3MoeForCausalLM, PyDecoder>(qwen3_moe, "ForCausalLM",
+                                               "HF Qwen3MoeForCausalLM, loaded on a device.");
+
+  // Builds a decoder of `config` (a dict of geometry) with N(0, std) weights: synthetic models
+  // of a named architecture for benchmarks and tests.
+  m.def("_synthetic_decoder", [](const Device& device, const py::dict& config, int tp, int rank,
+                                 uint64_t seed, float stdv) -> py::object {
+    ModelConfig cfg = model_config_from_dict(config);
+    std::shared_ptr<DecoderModel> model;
+    {
+      py::gil_scoped_release nogil;
+      model = std::make_shared<DecoderModel>(device, cfg, tp, rank);
+      if (stdv > 0) model->init_random(seed, stdv);
+    }
+    auto fill = [&](PyDecoder& d) {
+      d.model = model;
+      d.size = cfg.size;
+      d.precision = cfg.precision;
+      d.parallel = tp;
+    };
+    if (cfg.family == "llama") { PyLlamaForCausalLM d; fill(d); return py::cast(d); }
+    if (cfg.family == "mistral") { PyMistralForCausalLM d; fill(d); return py::cast(d); }
+    if (cfg.output == Output::Hidden) { PyQwen3Model d; fill(d); return py::cast(d); }
+    if (cfg.output == Output::Scores) { PyQwen3ForSequenceClassification d; fill(d); return py::cast(d); }
+    PyQwen3ForCausalLM d;
+    fill(d);
+    return py::cast(d);
+  }, py::arg("device"), py::arg("config"), py::arg("tp") = 1, py::arg("rank") = 0,
+     py::arg("seed") = 0, py::arg("std") = 0.02f);
+
+  m.def("_layout", [](const std::vector<int64_t>& lens) { return layout(lens); });
+
+  bind_checkpoint_and_load(m);
+}

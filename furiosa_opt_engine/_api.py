@@ -1,3 +1,38 @@
-"""Placeholder surface; the engine classes are added as they land."""
+"""The engine's public classes, re-exported from the native extension."""
 
-__all__: list[str] = []
+import sys as _sys
+
+from . import _native
+
+Placement = _native.Placement
+Device = _native.Device
+HbmBuffer = _native.HbmBuffer
+HostBuffer = _native.HostBuffer
+Transfer = _native.Transfer
+HbmTensor = _native.HbmTensor
+HostTensor = _native.HostTensor
+Decoder = _native.Decoder
+decoder = _native.decoder
+qwen3 = _native.qwen3
+llama = _native.llama
+mistral = _native.mistral
+qwen3_moe = _native.qwen3_moe
+
+for _name in ("decoder", "qwen3", "llama", "mistral", "qwen3_moe"):
+    _sys.modules[f"furiosa_opt_engine.{_name}"] = getattr(_native, _name)
+
+__all__ = [
+    "Decoder",
+    "Device",
+    "HbmBuffer",
+    "HbmTensor",
+    "HostBuffer",
+    "HostTensor",
+    "Placement",
+    "Transfer",
+    "decoder",
+    "llama",
+    "mistral",
+    "qwen3",
+    "qwen3_moe",
+]

@@ -1,0 +1,63 @@
+"""Named model geometries: the architectures the benchmarks and tests instantiate with synthetic
+weights (random-init N(0, 0.02)), matching the published shapes of each checkpoint."""
+
+from __future__ import annotations
+
+import copy
+
+QWEN3_ROPE = {"type": "default", "theta": 1_000_000.0}
+
+CONFIGS: dict[str, dict] = {
+    # The tiny Qwen3-architecture decoder of the CPU oracle configuration.
+    "tiny-qwen3": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="tiny", hidden=256, intermediate=768,
+        layers=2, q_heads=4, kv_heads=2, head_dim=64, vocab=1024, eps=1e-6, qk_norm=True, tied=True,
+        rope=QWEN3_ROPE, window=4096, rows=8192,
+    ),
+    "qwen3-0.6b": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="0.6B", hidden=1024, intermediate=3072,
+        layers=28, q_heads=16, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,
+        tied=True, rope=QWEN3_ROPE, window=40960, rows=8192,
+    ),
+    "qwen3-1.7b": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="1.7B", hidden=2048, intermediate=6144,
+        layers=28, q_heads=16, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,
+        tied=True, rope=QWEN3_ROPE, window=40960, rows=8192,
+    ),
+    "qwen3-4b": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="4B", hidden=2560, intermediate=9728,
+        layers=36, q_heads=32, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,
+        tied=True, rope=QWEN3_ROPE, window=40960, rows=8192,
+    ),
+    "qwen3-8b": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="8B", hidden=4096, intermediate=12288,
+        layers=36, q_heads=32, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,
+        tied=False, rope=QWEN3_ROPE, window=40960, rows=8192,
+    ),
+    "llama-3.1-8b": dict(
+        architecture="LlamaForCausalLM", family="llama", size="8B", hidden=4096, intermediate=14336,
+        layers=32, q_heads=32, kv_heads=8, head_dim=128, vocab=128256, eps=1e-5, qk_norm=False,
+        tied=False, window=131072, rows=8192,
+        rope={"type": "llama3", "theta": 500000.0, "factor": 8.0, "low_freq_factor": 1.0,
+              "high_freq_factor": 4.0, "original_max_positions": 8192},
+    ),
+    "llama-3.3-70b": dict(
+        architecture="LlamaForCausalLM", family="llama", size="70B", hidden=8192, intermediate=28672,
+        layers=80, q_heads=64, kv_heads=8, head_dim=128, vocab=128256, eps=1e-5, qk_norm=False,
+        tied=False, window=131072, rows=8192,
+        rope={"type": "llama3", "theta": 500000.0, "factor": 8.0, "low_freq_factor": 1.0,
+              "high_freq_factor": 4.0, "original_max_positions": 8192},
+    ),
+    "qwen3-30b-a3b": dict(
+        architecture="Qwen3MoeForCausalLM", family="qwen3_moe", size="30B-A3B", hidden=2048,
+        intermediate=6144, layers=48, q_heads=32, kv_heads=4, head_dim=128, vocab=151936, eps=1e-6,
+        qk_norm=True, tied=False, rope=QWEN3_ROPE, window=40960, rows=8192, experts=128, top_k=8,
+        expert_intermediate=768, norm_topk=True,
+    ),
+}
+
+
+def get(name: str, **overrides) -> dict:
+    cfg = copy.deepcopy(CONFIGS[name])
+    cfg.update(overrides)
+    return cfg

@@ -1,0 +1,79 @@
+"""Dense PyTorch forward of the decoder families on the engine's weight layout: the oracle of the
+engine's paged calls (full causal attention over each sequence, FP32 math)."""
+
+from __future__ import annotations
+
+import torch
+
+from . import reference
+
+
+def split_gate_up(gate_up: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Gate and up rows of the engine's gate/up weight (128-row blocks alternating gate, up)."""
+    rows, k = gate_up.shape
+    blocks = gate_up.reshape(rows // 256, 2, 128, k)
+    return blocks[:, 0].reshape(-1, k), blocks[:, 1].reshape(-1, k)
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """The engine's gate/up layout of separate gate [I, K] and up [I, K] weights."""
+    i, k = gate.shape
+    return torch.stack([gate.reshape(i // 128, 128, k), up.reshape(i // 128, 128, k)], 1).reshape(2 * i, k)
+
+
+def inv_freq(cfg: dict) -> torch.Tensor:
+    d = cfg.get("head_dim", 128)
+    rope = cfg.get("rope", {"type": "default", "theta": 10000.0})
+    base = 1.0 / (rope.get("theta", 10000.0) ** (torch.arange(0, d, 2, dtype=torch.float64) / d))
+    kind = rope.get("type", "default")
+    if kind == "linear":
+        base = base / rope["factor"]
+    elif kind == "llama3":
+        import math
+
+        old = rope["original_max_positions"]
+        low_wl, high_wl = old / rope["low_freq_factor"], old / rope["high_freq_factor"]
+        out = base.clone()
+        for j, f in enumerate(base.tolist()):
+            wl = 2 * math.pi / f
+            if wl < high_wl:
+                out[j] = f
+            elif wl > low_wl:
+                out[j] = f / rope["factor"]
+            else:
+                s = (old / wl - rope["low_freq_factor"]) / (rope["high_freq_factor"] - rope["low_freq_factor"])
+                out[j] = (1 - s) * f / rope["factor"] + s * f
+        base = out
+    return base.float()
+
+
+def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor) -> torch.Tensor:
+    """Logits [len(ids), vocab] of one sequence from position 0, FP32."""
+    H, D = cfg["hidden"], cfg.get("head_dim", 128)
+    qh, kvh = cfg["q_heads"], cfg["kv_heads"]
+    eps = cfg["eps"]
+    T = ids.shape[0]
+    x = w["embed"][ids.long()].float()
+    pos = torch.arange(T)
+    freqs = inv_freq(cfg)
+    mask = torch.ones(T, T, dtype=torch.bool).tril()
+    for l in range(cfg["layers"]):
+        p = f"layers.{l}."
+        h = reference.rmsnorm(x, w[p + "in_norm"], eps).bfloat16().float()
+        qkv = (h @ w[p + "qkv"].float().T).bfloat16().float()
+        q, k, v = reference.qk_front(qkv, qh, kvh, D, w.get(p + "q_norm"), w.get(p + "k_norm"), eps, pos, freqs)
+        q, k = q.bfloat16().float(), k.bfloat16().float()
+        g = qh // kvh
+        k = k.repeat_interleave(g, 1)
+        v = v.repeat_interleave(g, 1)
+        s = torch.einsum("qhd,khd->hqk", q, k) * D ** -0.5
+        s = s.masked_fill(~mask[None], float("-inf"))
+        a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, qh * D).bfloat16().float()
+        x = (x + a @ w[p + "o"].float().T).bfloat16().float()
+        h = reference.rmsnorm(x, w[p + "post_norm"], eps).bfloat16().float()
+        gate, up = split_gate_up(w[p + "gate_up"].float())
+        act = reference.swiglu(h @ gate.T, h @ up.T).bfloat16().float()
+        x = (x + act @ w[p + "down"].float().T).bfloat16().float()
+    h = reference.rmsnorm(x, w["final_norm"], eps).bfloat16().float()
+    head = w["lm_head"] if "lm_head" in w else w["embed"]
+    return h @ head[: cfg["vocab"]].float().T
