@@ -20,6 +20,7 @@
 #include <cfloat>
 
 #include "attention.cuh"
+#include "launch.cuh"
 #include "sm100.cuh"
 
 namespace foa {
@@ -197,6 +198,8 @@ __device__ __forceinline__ void load_q(uint32_t (&qa)[D / 16][4], RowPtr row_ptr
 // in turn, each double-buffering its blocks with cp.async.
 template <int D>
 __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention p, int max_splits) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   const int G = p.q_heads / p.kv_heads;
   const int seg_index = blockIdx.x / p.kv_heads, kvh = blockIdx.x % p.kv_heads;
@@ -332,6 +335,8 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
 // Merges the 512-key splits of each (segment, head) by log-sum-exp, in split order.
 template <int D>
 __global__ void decode_merge_kernel(const PagedAttention p, int max_splits) {
+  pdl_wait();
+  pdl_trigger();
   const int seg_index = blockIdx.x, head = blockIdx.y;
   const Segment seg = p.segments[seg_index];
   const int keys = seg.cached + seg.len;
@@ -359,6 +364,8 @@ __global__ void decode_merge_kernel(const PagedAttention p, int max_splits) {
 template <int D>
 __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention p,
                                                             const int32_t* work) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   const int G = p.q_heads / p.kv_heads;
   const int seg_index = work[2 * blockIdx.x], tile = work[2 * blockIdx.x + 1];
@@ -471,9 +478,9 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
     configured[dev & 63] = true;
   }
   dim3 grid(p.num_segments * p.kv_heads, max_splits);
-  paged_decode_kernel<D><<<grid, 128, smem, stream>>>(p, max_splits);
+  launch_pdl(paged_decode_kernel<D>, dim3(grid), dim3(128), smem, stream, p, max_splits);
   if (max_splits > 1)
-    decode_merge_kernel<D><<<dim3(p.num_segments, p.q_heads), D, 0, stream>>>(p, max_splits);
+    launch_pdl(decode_merge_kernel<D>, dim3(p.num_segments, p.q_heads), dim3(D), 0, stream, p, max_splits);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -487,7 +494,7 @@ int prefill_launch(const PagedAttention& p, const int32_t* work, int num_work, c
     cudaFuncSetAttribute(paged_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured[dev & 63] = true;
   }
-  paged_prefill_kernel<D><<<dim3(num_work, p.kv_heads), 128, smem, stream>>>(p, work);
+  launch_pdl(paged_prefill_kernel<D>, dim3(num_work, p.kv_heads), dim3(128), smem, stream, p, work);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

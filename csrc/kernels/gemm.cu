@@ -27,9 +27,11 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 #include "gemm.cuh"
+#include "launch.cuh"
 #include "sm100.cuh"
 #include "tmap.cuh"
 
@@ -53,7 +55,13 @@ struct KParams {
   int* counters;
   int* status;
   int out_rows, out_cols;     // logical output shape
+  unsigned long long* trace;  // milestone timestamps of CTA 0, or null
+  int debug;                  // measurement switches (FOA_GEMM_DEBUG): 1 no stores, 2 no TMEM loads
 };
+
+__device__ __forceinline__ void mark(const KParams& p, int i) {
+  if (p.trace != nullptr && blockIdx.x == 0) p.trace[i] = global_ns();
+}
 
 template <int kMB, int kBN, int kStages, int kAcc>
 struct Cfg {
@@ -94,6 +102,7 @@ template <int kEpi>
 __device__ __forceinline__ void store16(const KParams& p, int row, int col, const float (&v)[16],
                                         bool along_row) {
   // along_row: the 16 values are C[row, col + t]; otherwise C[row + t, col].
+  if (p.debug & 1) return;
   if (kEpi == kEpiF32) {
     float* c = static_cast<float*>(p.c);
     if (along_row) {
@@ -185,6 +194,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
+  pdl_trigger();
+  if (threadIdx.x == 0) mark(p, 0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -210,20 +221,51 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  if (threadIdx.x == 0) mark(p, 1);
 
   if (warp == 0) {
     // ----------------------------------------------------------------- TMA producer
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = true;
+      // The first stages' weight tiles do not depend on earlier kernels: issue them before
+      // waiting for the previous kernel (PDL), then their activation tiles after it.
+      int pre = 0;
+      if (blockIdx.x < p.units) {
+        const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
+        const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+        pre = min(kStages, kb1 - kb0);
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* st = smem + i * C::kStageBytes;
+          mbar_arrive_expect_tx(full + i, C::kStageBytes);
+          if (p.swap)
+            tma_load_2d(st, &tmP, full + i, (kb0 + i) * kBlockK, tp * C::kPRows);
+          else
+            tma_load_2d(st + C::kPBytes, &tmQ, full + i, (kb0 + i) * kBlockK, tq * kBN);
+        }
+        pdl_wait();
+        mark(p, 2);
+        for (int i = 0; i < pre; ++i) {
+          uint8_t* st = smem + i * C::kStageBytes;
+          if (p.swap)
+            tma_load_2d(st + C::kPBytes, &tmQ, full + i, (kb0 + i) * kBlockK, tq * kBN);
+          else
+            tma_load_2d(st, &tmP, full + i, (kb0 + i) * kBlockK, tp * C::kPRows);
+        }
+      } else {
+        pdl_wait();
+      }
       for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
         const int tile = u / p.splits, split = u % p.splits;
         const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
-          const int s = it % kStages;
-          const uint32_t ph = (it / kStages) & 1;
+        for (int kb = kb0 + (u == (int)blockIdx.x ? pre : 0); kb < kb1; ++kb) {
+          const uint32_t i2 = it + (u == (int)blockIdx.x ? pre : 0);
+          const int s = i2 % kStages;
+          const uint32_t ph = (i2 / kStages) & 1;
           if (!mbar_wait(empty + s, ph ^ 1, p.status, kTimeoutSmemEmpty, abort)) {
             ok = false;
             break;
@@ -232,7 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(full + s, C::kStageBytes);
           tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
           tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+          ++it;
         }
+        if (u == (int)blockIdx.x) it += pre;
       }
       if (!ok) {
         // Drain: let every load issued into the ring land before the CTA exits.
@@ -263,6 +307,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          if (it == 0) mark(p, 3);
+          if (false) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint8_t* st = smem + s * C::kStageBytes;
 #pragma unroll
@@ -277,12 +326,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(empty + s);
         }
         if (ok) mma_commit(tfull + b);
+        if (tc == 0) mark(p, 4);
       }
     }
   } else {
     // ----------------------------------------------------------------- epilogue (4 warps)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int lrow = q * 32 + lane;
+    pdl_wait();  // the residual and the output may be earlier kernels' memory
     uint32_t tc = 0;
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tc) {
       const int tile = u / p.splits, split = u % p.splits;
@@ -290,13 +341,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int b = tc % kAcc;
       const uint32_t aph = (tc / kAcc) & 1;
       if (!mbar_wait(tfull + b, aph, p.status, kTimeoutTmemFull, abort)) break;
+      if (tc == 0 && lrow == 0) mark(p, 5);
       tc_fence_after();
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols;
 
       auto tmem16 = [&](int mb, int c0, float (&v)[16]) {
         uint32_t r[16];
-        tmem_ld_32x32b_x16(tbase + mb * kBN + c0, r);
-        tmem_ld_wait();
+        if (p.debug & 2) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) r[t] = 0;
+        } else {
+          tmem_ld_32x32b_x16(tbase + mb * kBN + c0, r);
+          tmem_ld_wait();
+        }
 #pragma unroll
         for (int t = 0; t < 16; ++t) v[t] = __uint_as_float(r[t]);
       };
@@ -389,6 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(tempty + b);
       }
     }
+    if (lrow == 0) mark(p, 6);
   }
 
   if (kRed == kRedCluster) {
@@ -472,6 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
+    if (lane == 0) mark(p, 7);
   }
 }
 
@@ -546,6 +605,12 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   const bool cluster_fits =
       pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn);
   pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
+  // FOA_GEMM_RED=global|cluster forces how splits meet (measurements only).
+  static const char* force = std::getenv("FOA_GEMM_RED");
+  if (force != nullptr && splits > 1) {
+    if (force[0] == 'g') pl.red = 1;
+    if (force[0] == 'c' && cluster_fits) pl.red = 2;
+  }
   if (pl.red == 1) {
     // Global scratch bounds the split count.
     while (splits > 1 && ((size_t)tiles * splits * red_bytes > ws_bytes || tiles > counters_len))
@@ -586,15 +651,22 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, cons
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  int n = 0;
   if (kRed == kRedCluster) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = pl.splits;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = pl.splits;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
   }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
   const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, tp, tq, kp);
   return err == cudaSuccess ? 0 : -5;
 }
@@ -733,6 +805,9 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.ws = a.workspace;
   kp.counters = a.counters;
   kp.status = a.status;
+  kp.trace = a.trace;
+  static const int debug = std::getenv("FOA_GEMM_DEBUG") ? std::atoi(std::getenv("FOA_GEMM_DEBUG")) : 0;
+  kp.debug = debug;
   kp.out_rows = a.M;
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;

@@ -41,6 +41,9 @@ struct GemmArgs {
   int* counters = nullptr;
   int counters_len = 0;
   int* status = nullptr;  // device status word (see sm100.cuh)
+  // Optional: CTA 0 writes %globaltimer at 8 milestones here (kernel entry, setup done, first
+  // loads issued, first stage landed, last MMA issued, accumulator seen, epilogue done, exit).
+  unsigned long long* trace = nullptr;
   int num_sms = 0;        // 0: query the device
 };
 

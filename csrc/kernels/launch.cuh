@@ -1,0 +1,47 @@
+// Kernel launches with programmatic dependent launch (PDL).
+//
+// Every engine kernel calls pdl_trigger() early (its dependents may start launching) and
+// pdl_wait() before it touches memory an earlier kernel of the stream writes. Launched with the
+// programmatic-serialization attribute, a kernel's prologue (barrier setup, TMEM allocation,
+// tensor-map prefetch, and in the GEMMs the first weight tiles) overlaps the tail of the kernel
+// before it; without the attribute both calls are no-ops. FOA_PDL=0 in the environment turns the
+// attribute off.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdlib>
+#include <utility>
+
+namespace foa {
+
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("FOA_PDL");
+    return v == nullptr || v[0] != '0';
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+}  // namespace foa

@@ -11,6 +11,7 @@
 #include <algorithm>
 
 #include "ops.cuh"
+#include "launch.cuh"
 #include "sm100.cuh"
 
 namespace foa {
@@ -29,6 +30,8 @@ __global__ void __launch_bounds__(128) rmsnorm_kernel(
     const __nv_bfloat16* __restrict__ x, long ldx, const __nv_bfloat16* __restrict__ residual,
     long ldr, const __nv_bfloat16* __restrict__ weight, __nv_bfloat16* __restrict__ out, long ldo,
     __nv_bfloat16* residual_out, long ldro, int cols, float eps) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int nvec = cols / 8;
   float h[kVec][8];
@@ -93,6 +96,8 @@ __global__ void embedding_kernel(const int32_t* __restrict__ ids,
                                  const __nv_bfloat16* __restrict__ table, long ldt,
                                  int row_begin, int row_end, __nv_bfloat16* __restrict__ out,
                                  long ldo, int cols) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const int id = ids[row];
   const bool local = id >= row_begin && id < row_end;
@@ -115,6 +120,8 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
 __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, long ld,
                                                      int cols, int valid, int base,
                                                      int32_t* out_index, float* out_value) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   const float* src = logits + (long)row * ld;
   float bv = -INFINITY;
@@ -152,6 +159,8 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
 
 __global__ void argmax_merge_kernel(const float* values, const int32_t* indices, int ranks,
                                     int rows, int32_t* out) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x * blockDim.x + threadIdx.x;
   if (row >= rows) return;
   float bv = -INFINITY;
@@ -171,6 +180,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
     const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, float attn_factor,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
     const int32_t* __restrict__ slots) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int E = kHD / 64;  // elements per lane in each half
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int heads = q_heads + 2 * kv_heads;
@@ -245,6 +256,8 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
 }
 
 __global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64_t seed) {
+  pdl_wait();
+  pdl_trigger();
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const uint64_t r = mix64(seed * 0x100000001B3ull + (uint64_t)i);
     // Box-Muller on two 24-bit uniforms in (0, 1].
@@ -256,12 +269,16 @@ __global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64
 }
 
 __global__ void fill_bf16_kernel(__nv_bfloat16* dst, long n, float v) {
+  pdl_wait();
+  pdl_trigger();
   const __nv_bfloat16 b = __float2bfloat16_rn(v);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     dst[i] = b;
 }
 
 __global__ void gather_tokens_kernel(const int32_t* sources, int count, int32_t* out) {
+  pdl_wait();
+  pdl_trigger();
   const int s = blockIdx.x;
   if (s >= count) return;
   const int32_t* rec = sources + 4 * s;
@@ -273,6 +290,8 @@ __global__ void gather_tokens_kernel(const int32_t* sources, int count, int32_t*
 
 __global__ void gather_rows_kernel(const __nv_bfloat16* in, long ldi, const int32_t* rows,
                                    __nv_bfloat16* out, long ldo, int cols) {
+  pdl_wait();
+  pdl_trigger();
   const int i = blockIdx.x;
   const int r = rows[i];
   for (int v = threadIdx.x; v < cols / 8; v += blockDim.x)
@@ -285,20 +304,20 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* in, long ldi, const int3
 int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream) {
   if (n <= 0) return 0;
   const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
-  init_normal_kernel<<<grid, 256, 0, stream>>>(dst, n, std, seed);
+  launch_pdl(init_normal_kernel, dim3(grid), dim3(256), 0, stream, dst, n, std, seed);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int fill_bf16(__nv_bfloat16* dst, long n, float value, cudaStream_t stream) {
   if (n <= 0) return 0;
   const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
-  fill_bf16_kernel<<<grid, 256, 0, stream>>>(dst, n, value);
+  launch_pdl(fill_bf16_kernel, dim3(grid), dim3(256), 0, stream, dst, n, value);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int gather_tokens(const int32_t* sources, int count, int32_t* out, cudaStream_t stream) {
   if (count <= 0) return 0;
-  gather_tokens_kernel<<<count, 128, 0, stream>>>(sources, count, out);
+  launch_pdl(gather_tokens_kernel, dim3(count), dim3(128), 0, stream, sources, count, out);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -306,7 +325,7 @@ int gather_rows(const __nv_bfloat16* in, long ldi, const int32_t* rows, int n, _
                 long ldo, int cols, cudaStream_t stream) {
   if (n <= 0) return 0;
   if (cols % 8 != 0) return -2;
-  gather_rows_kernel<<<n, 128, 0, stream>>>(in, ldi, rows, out, ldo, cols);
+  launch_pdl(gather_rows_kernel, dim3(n), dim3(128), 0, stream, in, ldi, rows, out, ldo, cols);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -319,7 +338,7 @@ int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, lon
   const int vec = (cols / 8 + 127) / 128;
 #define FOA_RMS(V)                                                                          \
   case V:                                                                                   \
-    rmsnorm_kernel<V><<<rows, 128, 0, stream>>>(x, ldx, residual, ldr, weight, out, ldo,    \
+    launch_pdl(rmsnorm_kernel<V>, dim3(rows), dim3(128), 0, stream, x, ldx, residual, ldr, weight, out, ldo,    \
                                                 residual_out, ldro, cols, eps);             \
     break;
   switch (vec) {
@@ -351,14 +370,14 @@ int embedding(const int32_t* ids, const __nv_bfloat16* table, long ldt, int row_
               cudaStream_t stream) {
   if (rows <= 0) return 0;
   if (cols % 8 != 0) return -2;
-  embedding_kernel<<<rows, 128, 0, stream>>>(ids, table, ldt, row_begin, row_end, out, ldo, cols);
+  launch_pdl(embedding_kernel, dim3(rows), dim3(128), 0, stream, ids, table, ldt, row_begin, row_end, out, ldo, cols);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int argmax_rows(const float* logits, long ld, int rows, int cols, int valid_cols, int index_base,
                 int32_t* out_index, float* out_value, cudaStream_t stream) {
   if (rows <= 0) return 0;
-  argmax_kernel<<<rows, 512, 0, stream>>>(logits, ld, cols, valid_cols, index_base, out_index,
+  launch_pdl(argmax_kernel, dim3(rows), dim3(512), 0, stream, logits, ld, cols, valid_cols, index_base, out_index,
                                           out_value);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
@@ -366,7 +385,7 @@ int argmax_rows(const float* logits, long ld, int rows, int cols, int valid_cols
 int argmax_merge(const float* values, const int32_t* indices, int ranks, int rows,
                  int32_t* out_tokens, cudaStream_t stream) {
   if (rows <= 0) return 0;
-  argmax_merge_kernel<<<(rows + 127) / 128, 128, 0, stream>>>(values, indices, ranks, rows,
+  launch_pdl(argmax_merge_kernel, dim3((rows + 127) / 128), dim3(128), 0, stream, values, indices, ranks, rows,
                                                               out_tokens);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
@@ -381,17 +400,17 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
   const int grid = (int)((tasks + 3) / 4);
   switch (head_dim) {
     case 64:
-      qk_norm_rope_cache_kernel<64><<<grid, 128, 0, stream>>>(
+      launch_pdl(qk_norm_rope_cache_kernel<64>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
           rope.attention_factor, q_out, cache, slots);
       break;
     case 128:
-      qk_norm_rope_cache_kernel<128><<<grid, 128, 0, stream>>>(
+      launch_pdl(qk_norm_rope_cache_kernel<128>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
           rope.attention_factor, q_out, cache, slots);
       break;
     case 256:
-      qk_norm_rope_cache_kernel<256><<<grid, 128, 0, stream>>>(
+      launch_pdl(qk_norm_rope_cache_kernel<256>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
           rope.attention_factor, q_out, cache, slots);
       break;

@@ -32,8 +32,9 @@ void bind_ops(py::module_& m) {
       "gemm",
       [](uint64_t a, long lda, uint64_t w, long ldw, int M, int N, int K, uint64_t c, long ldc,
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
-         uint64_t counters, int counters_len, uint64_t status, uint64_t stream) {
+         uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace) {
         foa::GemmArgs g;
+        g.trace = reinterpret_cast<unsigned long long*>(trace);
         g.a = as_ptr<void>(a);
         g.lda = lda;
         g.w = as_ptr<void>(w);
@@ -60,7 +61,7 @@ void bind_ops(py::module_& m) {
       py::arg("K"), py::arg("c"), py::arg("ldc"), py::arg("res"), py::arg("ldr"),
       py::arg("epilogue"), py::arg("mode"), py::arg("splits"), py::arg("ws"),
       py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
-      py::arg("stream"));
+      py::arg("stream"), py::arg("trace") = 0);
 
   m.def(
       "gemm_scratch",

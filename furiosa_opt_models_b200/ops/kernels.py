@@ -31,6 +31,7 @@ def gemm(
     out: torch.Tensor | None = None,
     mode: int = MODE_AUTO,
     splits: int = 0,
+    trace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
@@ -57,6 +58,7 @@ def gemm(
         out.data_ptr(), out.stride(0), _ptr(residual), 0 if residual is None else residual.stride(0),
         epilogue, mode, splits, s.workspace.data_ptr(), s.workspace.numel() * 4,
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
+        0 if trace is None else trace.data_ptr(),
     )
     return out
 
