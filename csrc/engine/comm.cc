@@ -1,0 +1,160 @@
+#include "comm.h"
+
+#include <cstring>
+
+namespace foa::engine {
+
+namespace {
+size_t align_to(size_t v, size_t a) { return (v + a - 1) / a * a; }
+}  // namespace
+
+PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int64_t rows, int cols,
+                                 int64_t kept)
+    : device_(device), world_(world), rank_(rank), rows_(rows), kept_(kept), cols_(cols) {
+  if (world < 2 || world > foa::kMaxRanks) throw Unsupported("tensor parallelism takes 2 to 8 chips");
+  auto st = device_.state();
+  st->activate();
+  status_ = st->status;
+  size_t off = 0;
+  off_signal_ = off;
+  off = align_to(off + 64 * sizeof(unsigned long long), 4096);
+  off_arrivals_ = off;
+  off = align_to(off + 64, 256);
+  off_epoch_ = off;
+  off = align_to(off + 64, 256);
+  off_partial_ = off;
+  off = align_to(off + 2 * static_cast<size_t>(rows) * cols * sizeof(float), 4096);
+  off_residual_ = off;
+  off = align_to(off + static_cast<size_t>(rows) * cols * 2, 4096);
+  off_hidden_ = off;
+  off = align_to(off + static_cast<size_t>(rows) * cols * 2, 4096);
+  off_gvalue_ = off;
+  off = align_to(off + static_cast<size_t>(world) * kept * 4, 256);
+  off_gindex_ = off;
+  off = align_to(off + static_cast<size_t>(world) * kept * 4, 4096);
+  heap_bytes_ = off;
+  st->check_cuda(cudaMalloc(&heap_, heap_bytes_), "tensor-parallel heap");
+  st->check_cuda(cudaMemset(heap_, 0, heap_bytes_), "tensor-parallel heap");
+  peer_base_.assign(world, nullptr);
+  opened_.assign(world, false);
+  peer_base_[rank] = heap_;
+}
+
+PeerCollectives::~PeerCollectives() {
+  device_.state()->activate();
+  cudaStreamSynchronize(device_.state()->stream);
+  for (int p = 0; p < world_; ++p)
+    if (opened_[p]) cudaIpcCloseMemHandle(peer_base_[p]);
+  if (heap_) cudaFree(heap_);
+}
+
+std::string PeerCollectives::handle() const {
+  cudaIpcMemHandle_t h;
+  device_.state()->activate();
+  if (cudaIpcGetMemHandle(&h, heap_) != cudaSuccess) {
+    cudaGetLastError();
+    throw DeviceError("cannot export the tensor-parallel heap");
+  }
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+void PeerCollectives::connect(const std::vector<std::string>& handles) {
+  if (static_cast<int>(handles.size()) != world_) throw ValueError("one handle per rank");
+  auto st = device_.state();
+  st->activate();
+  for (int p = 0; p < world_; ++p) {
+    if (p == rank_) continue;
+    cudaIpcMemHandle_t h;
+    if (handles[p].size() != sizeof(h)) throw ValueError("malformed peer handle");
+    std::memcpy(&h, handles[p].data(), sizeof(h));
+    void* ptr = nullptr;
+    st->check_cuda(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), "open peer heap");
+    peer_base_[p] = ptr;
+    opened_[p] = true;
+  }
+  for (int p = 0; p < world_; ++p) {
+    char* b = static_cast<char*>(peer_base_[p]);
+    peers_.signal[p] = reinterpret_cast<unsigned long long*>(b + off_signal_);
+    peers_.partial[p] = reinterpret_cast<float*>(b + off_partial_);
+    peers_.residual[p] = reinterpret_cast<__nv_bfloat16*>(b + off_residual_);
+    peers_.hidden[p] = reinterpret_cast<__nv_bfloat16*>(b + off_hidden_);
+    peers_.gather_value[p] = reinterpret_cast<float*>(b + off_gvalue_);
+    peers_.gather_index[p] = reinterpret_cast<int32_t*>(b + off_gindex_);
+  }
+  connected_ = true;
+}
+
+void PeerCollectives::begin_call(cudaStream_t stream) {
+  if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
+  ++epoch_;
+  site_ = 0;
+  half_ = 0;
+  auto* ep = reinterpret_cast<unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
+  if (foa::tp_set_epoch(ep, epoch_, stream) != 0) device_.state()->fail("epoch launch failed");
+}
+
+float* PeerCollectives::partial_buffer(size_t floats) {
+  if (floats > static_cast<size_t>(rows_) * cols_) throw ValueError("call exceeds the tensor-parallel heap");
+  return reinterpret_cast<float*>(static_cast<char*>(heap_) + off_partial_) +
+         static_cast<size_t>(half_) * rows_ * cols_;
+}
+
+__nv_bfloat16* PeerCollectives::residual_buffer() {
+  return reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(heap_) + off_residual_);
+}
+
+__nv_bfloat16* PeerCollectives::hidden_buffer() {
+  return reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(heap_) + off_hidden_);
+}
+
+void PeerCollectives::add_norm(const float* partial, __nv_bfloat16* residual,
+                               const __nv_bfloat16* weight, float eps, __nv_bfloat16* out,
+                               int rows, int cols, cudaStream_t stream) {
+  if (partial != partial_buffer(0) || residual != residual_buffer() || out != hidden_buffer())
+    throw DeviceError("tensor-parallel add_norm takes the heap's own buffers");
+  foa::AddNormArgs a{};
+  a.peers = peers_;
+  for (int p = 0; p < world_; ++p) a.peers.partial[p] += static_cast<size_t>(half_) * rows_ * cols_;
+  a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
+  a.arrivals = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_arrivals_);
+  a.weight = weight;
+  a.eps = eps;
+  a.rows = rows;
+  a.cols = cols;
+  a.rank = rank_;
+  a.world = world_;
+  a.site = site_++;
+  // Few rows: every rank reduces every row (one barrier, local writes); many rows: each rank
+  // reduces a slice and stores it into every rank (less NVLink traffic, two barriers).
+  a.two_shot = rows > 256 ? 1 : 0;
+  a.status = status_;
+  half_ ^= 1;
+  if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
+}
+
+void PeerCollectives::argmax(const float* value, const int32_t* index, int rows, int32_t* out,
+                             cudaStream_t stream) {
+  if (rows > kept_) throw ValueError("call keeps more rows than the tensor-parallel heap holds");
+  foa::ArgmaxArgs a{};
+  a.peers = peers_;
+  a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
+  a.value = value;
+  a.index = index;
+  a.out = out;
+  a.rows = rows;
+  a.rank = rank_;
+  a.world = world_;
+  a.site = site_++;
+  a.status = status_;
+  if (foa::tp_argmax(a, stream) != 0) device_.state()->fail("tensor-parallel argmax launch failed");
+}
+
+void PeerCollectives::barrier(cudaStream_t stream) {
+  auto* ep = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
+  ++epoch_;
+  foa::tp_set_epoch(const_cast<unsigned long long*>(ep), epoch_, stream);
+  if (foa::tp_barrier(peers_, ep, rank_, world_, 0, status_, stream) != 0)
+    device_.state()->fail("tensor-parallel barrier launch failed");
+}
+
+}  // namespace foa::engine

@@ -1,0 +1,57 @@
+// Tensor-parallel collectives of one rank: a symmetric heap in device memory, exported through
+// CUDA IPC and opened by every peer, and the fused collective kernels over it.
+#pragma once
+
+#include <string>
+#include <vector>
+
+#include "kernels/comm.cuh"
+#include "model.h"
+#include "runtime.h"
+
+namespace foa::engine {
+
+class PeerCollectives : public Collectives {
+ public:
+  // A heap for calls of up to `rows` rows of `cols` columns and `kept` returned rows.
+  PeerCollectives(const Device& device, int world, int rank, int64_t rows, int cols, int64_t kept);
+  ~PeerCollectives() override;
+
+  // This rank's heap as an opaque IPC handle; `connect` opens every rank's handle (in rank order).
+  std::string handle() const;
+  void connect(const std::vector<std::string>& handles);
+  bool connected() const { return connected_; }
+
+  int rank() const override { return rank_; }
+  int world() const override { return world_; }
+  void begin_call(cudaStream_t stream) override;
+  void add_norm(const float* partial, __nv_bfloat16* residual, const __nv_bfloat16* weight,
+                float eps, __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) override;
+  void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
+              cudaStream_t stream) override;
+  float* partial_buffer(size_t floats) override;
+  __nv_bfloat16* residual_buffer() override;
+  __nv_bfloat16* hidden_buffer() override;
+  // A device-side barrier of every rank (used before the heap is released).
+  void barrier(cudaStream_t stream);
+
+ private:
+  Device device_;
+  int world_, rank_;
+  int64_t rows_, kept_;
+  int cols_;
+  void* heap_ = nullptr;
+  size_t heap_bytes_ = 0;
+  size_t off_signal_, off_arrivals_, off_epoch_, off_partial_, off_residual_, off_hidden_,
+      off_gvalue_, off_gindex_;
+  std::vector<void*> peer_base_;   // every rank's heap as mapped here (own heap at rank_)
+  std::vector<bool> opened_;
+  foa::PeerBuffers peers_{};
+  bool connected_ = false;
+  unsigned long long epoch_ = 0;
+  int site_ = 0;
+  int half_ = 0;                   // partial buffer of the next add_norm
+  int* status_ = nullptr;
+};
+
+}  // namespace foa::engine

@@ -190,18 +190,81 @@ void DecoderModel::allocate_weights() {
   }
 }
 
+namespace {
+uint32_t name_tag(const std::string& s) {
+  uint32_t h = 2166136261u;  // FNV-1a
+  for (unsigned char c : s) h = (h ^ c) * 16777619u;
+  return h & 0xFFFFFu;
+}
+}  // namespace
+
 void DecoderModel::init_random(uint64_t seed, float stdv) {
   auto st = device_.state();
   st->activate();
-  uint64_t k = 0;
+  const int H = cfg_.hidden, D = cfg_.head_dim;
+  HbmBuffer map_rows, map_tags;
   for (auto& [name, w] : weights_) {
     if (name == "lm_head" && cfg_.tied) continue;
     long n = 1;
     for (auto s : w.shape) n *= s;
-    const bool norm = name.find("norm") != std::string::npos;
-    int rc = norm ? foa::fill_bf16(w.ptr, n, 1.0f, st->stream)
-                  : foa::init_normal_bf16(w.ptr, n, stdv, seed * 1315423911ull + (++k), st->stream);
-    if (rc != 0) st->fail("weight initialisation launch failed");
+    if (name.find("norm") != std::string::npos) {
+      if (foa::fill_bf16(w.ptr, n, 1.0f, st->stream) != 0) st->fail("weight initialisation launch failed");
+      continue;
+    }
+    // The logical row, tag and column window of every shard row, so each tensor-parallel split
+    // of one model holds the same logical weights.
+    const int rows = static_cast<int>(w.shape[0]), cols = static_cast<int>(w.shape[1]);
+    std::vector<int32_t> full(rows);
+    std::vector<uint32_t> tags(rows);
+    long full_cols = cols, col_offset = 0;
+    const auto dot = name.rfind('.');
+    const std::string prefix = dot == std::string::npos ? "" : name.substr(0, dot + 1);
+    const std::string leaf = dot == std::string::npos ? name : name.substr(dot + 1);
+    for (int r = 0; r < rows; ++r) {
+      full[r] = r;
+      tags[r] = name_tag(name);
+    }
+    if (leaf == "lm_head") {
+      for (int r = 0; r < rows; ++r) full[r] = vocab_begin_ + r;
+    } else if (leaf == "qkv") {
+      for (int r = 0; r < rows; ++r) {
+        if (r < qh_l_ * D) {
+          full[r] = qh_first_ * D + r;
+          tags[r] = name_tag(prefix + "q");
+        } else if (r < (qh_l_ + kvh_l_) * D) {
+          full[r] = kvh_first_ * D + (r - qh_l_ * D);
+          tags[r] = name_tag(prefix + "k");
+        } else {
+          full[r] = kvh_first_ * D + (r - (qh_l_ + kvh_l_) * D);
+          tags[r] = name_tag(prefix + "v");
+        }
+      }
+    } else if (leaf == "o") {
+      full_cols = static_cast<long>(cfg_.q_heads) * D;
+      col_offset = static_cast<long>(qh_first_) * D;
+    } else if (leaf == "gate_up") {
+      for (int r = 0; r < rows; ++r) {
+        const int block = r / 128;
+        full[r] = rank_ * inter_l_ + (block / 2) * 128 + r % 128;
+        tags[r] = name_tag(prefix + (block % 2 == 0 ? "gate" : "up"));
+      }
+    } else if (leaf == "down") {
+      full_cols = cfg_.intermediate;
+      col_offset = static_cast<long>(rank_) * inter_l_;
+    }
+    (void)H;
+    if (map_rows.size() < static_cast<size_t>(rows) * 4) {
+      map_rows = HbmBuffer(device_, static_cast<size_t>(rows) * 4);
+      map_tags = HbmBuffer(device_, static_cast<size_t>(rows) * 4);
+    }
+    st->check_cuda(cudaMemcpyAsync(map_rows.data(), full.data(), rows * 4, cudaMemcpyHostToDevice, st->stream), "init map");
+    st->check_cuda(cudaMemcpyAsync(map_tags.data(), tags.data(), rows * 4, cudaMemcpyHostToDevice, st->stream), "init map");
+    if (foa::init_normal_rows(w.ptr, rows, cols, static_cast<const int32_t*>(map_rows.data()),
+                              static_cast<const uint32_t*>(map_tags.data()), full_cols, col_offset,
+                              stdv, seed, st->stream) != 0)
+      st->fail("weight initialisation launch failed");
+    // The host maps must outlive their copies.
+    st->check_cuda(cudaStreamSynchronize(st->stream), "weight initialisation");
   }
   st->check_cuda(cudaStreamSynchronize(st->stream), "weight initialisation");
 }
@@ -300,6 +363,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
                  "stage operands");
   st->check_cuda(cudaEventRecord(stage_done_[slot], st->stream), "staging event");
   plan.max_keys = splits * 512;  // the decode grid covers the bucket's splits
+  if (coll_) coll_->begin_call(st->stream);
 
   if (graphable) {
     const GraphKey key{bucket, splits};
@@ -402,8 +466,10 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     fail(foa::gemm_bf16(g, s), "gemm");
   };
   const int qkv_cols = (qh_l_ + 2 * kvh_l_) * D;
-  __nv_bfloat16* x = bf(ws_x_);
-  __nv_bfloat16* h = bf(ws_h_);
+  // Tensor-parallel ranks keep the residual stream and the normed rows in the symmetric heap,
+  // where the fused collectives write them.
+  __nv_bfloat16* x = coll_ ? coll_->residual_buffer() : bf(ws_x_);
+  __nv_bfloat16* h = coll_ ? coll_->hidden_buffer() : bf(ws_h_);
   const auto& W = weights_;
   auto w = [&](const std::string& n) -> __nv_bfloat16* { return W.at(n).ptr; };
   const int64_t count = std::max<int64_t>(plan.requests, plan.rows_padded);
@@ -416,7 +482,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                       static_cast<int>(T), H, s),
        "embedding");
   const bool tp = tp_ > 1;
-  float* partial = tp ? coll_->partial_buffer(static_cast<size_t>(T) * H) : nullptr;
+  float* partial = nullptr;
   foa::PagedAttention attn;
   attn.q = bf(ws_q_);
   attn.o = bf(ws_attn_);
@@ -475,12 +541,14 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                         cfg_.eps, s),
            "rmsnorm");
     } else {
+      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
       gemm(ws_attn_.data(), qh_l_ * D, w(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
            foa::kEpiF32, nullptr);
       coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
       gemm(h, H, w(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr);
+      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
       gemm(ws_act_.data(), inter_l_, w(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
            foa::kEpiF32, nullptr);
       coll_->add_norm(partial, x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);

@@ -71,8 +71,13 @@ class Collectives {
   // The first maximum over ranks of (value, token) candidates [rows]: tokens into `out`.
   virtual void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
                       cudaStream_t stream) = 0;
-  // Scratch the add_norm partial must live in (symmetric across ranks), at least rows*cols FP32.
+  // Scratch the next add_norm's partial must live in (symmetric across ranks).
   virtual float* partial_buffer(size_t floats) = 0;
+  // The residual stream and the normed rows, in memory every rank can write.
+  virtual __nv_bfloat16* residual_buffer() = 0;
+  virtual __nv_bfloat16* hidden_buffer() = 0;
+  // Marks the start of a call (before its launches or its graph launch, on the call's stream).
+  virtual void begin_call(cudaStream_t stream) = 0;
 };
 
 struct WeightSlot {
@@ -106,7 +111,11 @@ class DecoderModel {
   int vocab_end() const { return vocab_end_; }
   int vocab_local() const { return vocab_l_; }
 
-  void set_collectives(std::shared_ptr<Collectives> c) { coll_ = std::move(c); }
+  void set_collectives(std::shared_ptr<Collectives> c) {
+    coll_ = std::move(c);
+    clear_graphs();
+  }
+  const std::shared_ptr<Collectives>& collectives() const { return coll_; }
   void set_graphs(bool enabled) { graphs_enabled_ = enabled; }
 
   // One call: plans, stages and launches; returns the kept rows' output (tokens I32 [kept],

@@ -1,0 +1,242 @@
+// Tensor-parallel collectives over NVLink peer memory.
+//
+// The reference's all-reduce is a deterministic FP32 recursive doubling over chip DMA, narrowed
+// to BF16 once at the end (crates/furiosa-opt-models/src/ops/collective/mod.rs:22-141); its
+// all-gather joins parts in chip order (gather.rs:17-99). Here every rank reads its peers'
+// FP32 partial sums directly over NVLink (peer pointers opened through CUDA IPC) and adds them in
+// rank order, so every rank computes the same bits; the sum is fused with the residual add (one
+// rounding) and the RMSNorm that follows, and, for large calls, with the all-gather of the normed
+// rows (two-shot: each rank reduces a slice of rows and stores it into every rank's buffers).
+//
+// Ranks meet at device-side barriers: a rank stores a monotonically increasing value into its
+// slot of every peer's signal array (release, system scope) and waits, bounded, until every slot
+// of its own array has reached the value. A wait that gives up records kTimeoutPeer and returns.
+
+#include "comm.cuh"
+#include "launch.cuh"
+#include "sm100.cuh"
+
+namespace foa {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ unsigned long long barrier_value(const unsigned long long* epoch,
+                                                            int site, int phase) {
+  return (*epoch) * 4096ull + (unsigned long long)site * 2ull + (unsigned long long)phase + 1ull;
+}
+
+__device__ void signal_all(const PeerBuffers& pb, int rank, int world, unsigned long long v) {
+  __threadfence_system();
+  for (int p = 0; p < world; ++p) st_release_sys(pb.signal[p] + rank, v);
+}
+
+__device__ bool wait_all(const PeerBuffers& pb, int rank, int world, unsigned long long v,
+                         int* status) {
+  const unsigned long long* s = pb.signal[rank];
+  const uint64_t start = global_ns();
+  for (int p = 0; p < world; ++p) {
+    uint32_t spins = 0;
+    while (ld_acquire_sys(s + p) < v) {
+      if ((++spins & 255u) == 0 && global_ns() - start > kWaitLimitNs) {
+        record_status(status, kTimeoutPeer);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5;
+  if ((threadIdx.x & 31) == 0) red[warp] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) t += red[w];
+  return t;
+}
+
+// One CTA of 256 threads per row; each thread holds kVec vectors of 8 columns.
+template <int kVec>
+__global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  __shared__ int ok_s;
+  const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
+  const int row = a.two_shot ? a.rank * rs + blockIdx.x : blockIdx.x;
+  if (threadIdx.x == 0) {
+    const unsigned long long v = barrier_value(a.epoch, a.site, 0);
+    if (blockIdx.x == 0) signal_all(a.peers, a.rank, a.world, v);
+    ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
+  }
+  __syncthreads();
+  const bool ok = ok_s;
+  const int nvec = a.cols / 8;
+  if (ok && row < a.rows && blockIdx.x < rs) {
+    float h[kVec][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int v = threadIdx.x + i * 256;
+      if (v >= nvec) continue;
+      float acc[8];
+#pragma unroll
+      for (int t = 0; t < 8; ++t) acc[t] = 0.f;
+      for (int p = 0; p < a.world; ++p) {
+        const float4* src = reinterpret_cast<const float4*>(a.peers.partial[p] + (long)row * a.cols + v * 8);
+        const float4 x0 = src[0], x1 = src[1];
+        acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
+        acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+      }
+      const __nv_bfloat16* rp = a.peers.residual[a.rank] + (long)row * a.cols + v * 8;
+      const uint4 rv = *reinterpret_cast<const uint4*>(rp);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      uint32_t packed[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        packed[t] = pack_bf16x2(acc[2 * t] + bf16_lo(rw[t]), acc[2 * t + 1] + bf16_hi(rw[t]));
+        h[i][2 * t] = bf16_lo(packed[t]);
+        h[i][2 * t + 1] = bf16_hi(packed[t]);
+        ss += h[i][2 * t] * h[i][2 * t] + h[i][2 * t + 1] * h[i][2 * t + 1];
+      }
+      const uint4 out = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      if (a.two_shot) {
+        for (int p = 0; p < a.world; ++p)
+          *reinterpret_cast<uint4*>(a.peers.residual[p] + (long)row * a.cols + v * 8) = out;
+      } else {
+        *reinterpret_cast<uint4*>(a.peers.residual[a.rank] + (long)row * a.cols + v * 8) = out;
+      }
+    }
+    const float total = block_sum(ss, red);
+    const float inv = rsqrtf(total / (float)a.cols + a.eps);
+#pragma unroll
+    for (int i = 0; i < kVec; ++i) {
+      const int v = threadIdx.x + i * 256;
+      if (v >= nvec) continue;
+      const uint4 wv = *reinterpret_cast<const uint4*>(a.weight + v * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        o[t] = pack_bf16x2(h[i][2 * t] * inv * bf16_lo(ww[t]), h[i][2 * t + 1] * inv * bf16_hi(ww[t]));
+      const uint4 out = make_uint4(o[0], o[1], o[2], o[3]);
+      if (a.two_shot) {
+        for (int p = 0; p < a.world; ++p)
+          *reinterpret_cast<uint4*>(a.peers.hidden[p] + (long)row * a.cols + v * 8) = out;
+      } else {
+        *reinterpret_cast<uint4*>(a.peers.hidden[a.rank] + (long)row * a.cols + v * 8) = out;
+      }
+    }
+  }
+  if (!a.two_shot) return;
+  // Two-shot: the last CTA of this rank tells every peer its slice has landed and waits until
+  // every peer's slice has landed here, so the kernel ends only with every row in place.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int done = atomicAdd(a.arrivals, 1u);
+    if (done == gridDim.x - 1) {
+      *a.arrivals = 0;
+      const unsigned long long v = barrier_value(a.epoch, a.site, 1);
+      signal_all(a.peers, a.rank, a.world, v);
+      wait_all(a.peers, a.rank, a.world, v, a.status);
+    }
+  }
+}
+
+__global__ void __launch_bounds__(256) tp_argmax_kernel(const ArgmaxArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  // Push this rank's candidates into every rank's gather arrays.
+  for (int i = threadIdx.x; i < a.rows; i += blockDim.x) {
+    const float v = a.value[i];
+    const int32_t x = a.index[i];
+    for (int p = 0; p < a.world; ++p) {
+      a.peers.gather_value[p][(long)a.rank * a.rows + i] = v;
+      a.peers.gather_index[p][(long)a.rank * a.rows + i] = x;
+    }
+  }
+  __syncthreads();
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    const unsigned long long v = barrier_value(a.epoch, a.site, 0);
+    signal_all(a.peers, a.rank, a.world, v);
+    ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const float* gv = a.peers.gather_value[a.rank];
+  const int32_t* gi = a.peers.gather_index[a.rank];
+  for (int i = threadIdx.x; i < a.rows; i += blockDim.x) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int p = 0; p < a.world; ++p) {
+      const float v = gv[(long)p * a.rows + i];
+      const int x = gi[(long)p * a.rows + i];
+      if (v > bv || (v == bv && x < bi)) {
+        bv = v;
+        bi = x;
+      }
+    }
+    a.out[i] = bi == 0x7fffffff ? 0 : bi;
+  }
+}
+
+__global__ void tp_barrier_kernel(PeerBuffers peers, const unsigned long long* epoch, int rank,
+                                  int world, int site, int* status) {
+  pdl_wait();
+  const unsigned long long v = barrier_value(epoch, site, 0);
+  signal_all(peers, rank, world, v);
+  wait_all(peers, rank, world, v, status);
+}
+
+__global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { *p = v; }
+
+}  // namespace
+
+int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream) {
+  set_u64_kernel<<<1, 1, 0, stream>>>(epoch, value);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int tp_add_norm(const AddNormArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return 0;
+  if (a.world < 1 || a.world > kMaxRanks || a.cols % 8 != 0) return -2;
+  const int vec = (a.cols / 8 + 255) / 256;
+  const int grid = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
+  cudaError_t e;
+  switch (vec) {
+    case 1: e = launch_pdl(tp_add_norm_kernel<1>, dim3(grid), dim3(256), 0, stream, a); break;
+    case 2: e = launch_pdl(tp_add_norm_kernel<2>, dim3(grid), dim3(256), 0, stream, a); break;
+    case 3:
+    case 4: e = launch_pdl(tp_add_norm_kernel<4>, dim3(grid), dim3(256), 0, stream, a); break;
+    default: return -2;
+  }
+  return e == cudaSuccess ? 0 : -5;
+}
+
+int tp_argmax(const ArgmaxArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return 0;
+  return launch_pdl(tp_argmax_kernel, dim3(1), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -5;
+}
+
+int tp_barrier(const PeerBuffers& peers, const unsigned long long* epoch, int rank, int world,
+               int site, int* status, cudaStream_t stream) {
+  return launch_pdl(tp_barrier_kernel, dim3(1), dim3(1), 0, stream, peers, epoch, rank, world,
+                    site, status) == cudaSuccess
+             ? 0
+             : -5;
+}
+
+}  // namespace foa

@@ -1,0 +1,58 @@
+// Tensor-parallel collectives over NVLink peer memory, fused with the work around them.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace foa {
+
+constexpr int kMaxRanks = 8;
+
+// Every rank's symmetric buffers, as this rank addresses them (peer pointers through CUDA IPC).
+struct PeerBuffers {
+  float* partial[kMaxRanks];            // FP32 partial sums [rows, cols]
+  __nv_bfloat16* residual[kMaxRanks];   // the residual stream [rows, cols]
+  __nv_bfloat16* hidden[kMaxRanks];     // normed rows [rows, cols]
+  unsigned long long* signal[kMaxRanks];  // barrier slots: slot i is written by rank i
+  float* gather_value[kMaxRanks];       // argmax candidates [ranks][rows]
+  int32_t* gather_index[kMaxRanks];
+};
+
+struct AddNormArgs {
+  PeerBuffers peers;
+  const unsigned long long* epoch;  // this call's epoch (device memory, written per call)
+  unsigned int* arrivals;           // this rank's CTA arrival counter (zero between calls)
+  const __nv_bfloat16* weight;
+  float eps;
+  int rows, cols, rank, world, site;
+  int two_shot;                     // 1: reduce a row slice and push it to every rank
+  int* status;
+};
+
+// residual = bf16(sum over ranks in rank order of partial + residual); hidden = RMSNorm(residual)
+// * weight; every rank ends with the same residual and hidden rows.
+int tp_add_norm(const AddNormArgs& args, cudaStream_t stream);
+
+struct ArgmaxArgs {
+  PeerBuffers peers;
+  const unsigned long long* epoch;
+  const float* value;     // this rank's candidates [rows]
+  const int32_t* index;
+  int32_t* out;           // tokens [rows]
+  int rows, rank, world, site;
+  int* status;
+};
+
+// Exchanges every rank's (value, index) candidates and keeps the first maximum.
+int tp_argmax(const ArgmaxArgs& args, cudaStream_t stream);
+
+// Writes this call's epoch (stream-ordered, outside any captured graph).
+int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream);
+
+// Every rank waits for every other at this site (a device-side barrier, bounded).
+int tp_barrier(const PeerBuffers& peers, const unsigned long long* epoch, int rank, int world,
+               int site, int* status, cudaStream_t stream);
+
+}  // namespace foa

@@ -268,6 +268,22 @@ __global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64
   }
 }
 
+__global__ void init_normal_rows_kernel(__nv_bfloat16* dst, int rows, int cols,
+                                        const int32_t* full_row, const uint32_t* tag,
+                                        long full_cols, long col_offset, float std, uint64_t seed) {
+  pdl_wait();
+  pdl_trigger();
+  const long n = (long)rows * cols;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    const uint64_t logical = (uint64_t)full_row[r] * (uint64_t)full_cols + (uint64_t)(col_offset + c);
+    const uint64_t x = mix64((seed * 0x100000001B3ull) ^ ((uint64_t)tag[r] << 40) ^ logical);
+    const float u1 = ((float)(x & 0xFFFFFF) + 1.0f) * (1.0f / 16777216.0f);
+    const float u2 = (float)((x >> 24) & 0xFFFFFF) * (1.0f / 16777216.0f);
+    dst[i] = __float2bfloat16_rn(sqrtf(-2.0f * logf(u1)) * cospif(2.0f * u2) * std);
+  }
+}
+
 __global__ void fill_bf16_kernel(__nv_bfloat16* dst, long n, float v) {
   pdl_wait();
   pdl_trigger();
@@ -305,6 +321,17 @@ int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaS
   if (n <= 0) return 0;
   const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
   launch_pdl(init_normal_kernel, dim3(grid), dim3(256), 0, stream, dst, n, std, seed);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
+}
+
+int init_normal_rows(__nv_bfloat16* dst, int rows, int cols, const int32_t* full_row,
+                     const uint32_t* tag, long full_cols, long col_offset, float std, uint64_t seed,
+                     cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return 0;
+  const long n = (long)rows * cols;
+  const int grid = (int)std::min<long>((n + 255) / 256, 148L * 16);
+  launch_pdl(init_normal_rows_kernel, dim3(grid), dim3(256), 0, stream, dst, rows, cols, full_row,
+             tag, full_cols, col_offset, std, seed);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 

@@ -56,6 +56,14 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
 // values on every device and every run.
 int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream);
 
+// Fills a [rows, cols] BF16 shard of a larger logical matrix with N(0, std): shard row r is
+// logical row full_row[r] of the matrix tagged tag[r], columns start at col_offset of full_cols.
+// The values depend on (seed, tag, logical index) only, so every tensor-parallel split of one
+// model holds the same logical weights.
+int init_normal_rows(__nv_bfloat16* dst, int rows, int cols, const int32_t* full_row,
+                     const uint32_t* tag, long full_cols, long col_offset, float std, uint64_t seed,
+                     cudaStream_t stream);
+
 // Fills `n` BF16 values with a constant.
 int fill_bf16(__nv_bfloat16* dst, long n, float value, cudaStream_t stream);
 

@@ -116,7 +116,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // ---------------------------------------------------------------------------------------------
-// TMA (non-multicast tensor loads only: this engine never issues a cluster-multicast load)
+// TMA tensor loads: each CTA loads its own tiles from this GPU's memory.
 // ---------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -11,6 +11,7 @@
 #include <cstring>
 
 #include "engine/batch.h"
+#include "engine/comm.h"
 #include "engine/model.h"
 #include "engine/registry.h"
 #include "engine/runtime.h"
@@ -594,6 +595,37 @@ void bind_engine(py::module_& m) {
      py::arg("seed") = 0, py::arg("std") = 0.02f);
 
   m.def("_layout", [](const std::vector<int64_t>& lens) { return layout(lens); });
+
+  // Tensor parallelism: a symmetric heap per rank, connected through CUDA IPC handles that the
+  // ranks exchange over their process group.
+  m.def("_tp_attach", [](PyDecoder& d, int world, int rank) {
+    const auto& cfg = d.model->config();
+    auto coll = std::make_shared<PeerCollectives>(d.model->device(), world, rank, cfg.rows,
+                                                  cfg.hidden, cfg.rows);
+    d.model->set_collectives(coll);
+    return py::bytes(coll->handle());
+  });
+  m.def("_tp_connect", [](PyDecoder& d, const std::vector<py::bytes>& handles) {
+    std::vector<std::string> hs;
+    for (const auto& h : handles) hs.push_back(std::string(h));
+    auto* coll = dynamic_cast<PeerCollectives*>(d.model->collectives().get());
+    if (coll == nullptr) throw ValueError("the decoder has no tensor-parallel heap");
+    py::gil_scoped_release nogil;
+    coll->connect(hs);
+  });
+  m.def("_tp_barrier", [](PyDecoder& d) {
+    auto* coll = dynamic_cast<PeerCollectives*>(d.model->collectives().get());
+    if (coll == nullptr) return;
+    py::gil_scoped_release nogil;
+    coll->barrier(d.model->device().state()->stream);
+    d.model->device().synchronize();
+    d.model->device().state()->check_status();
+  });
+  m.def("_tp_detach", [](PyDecoder& d) {
+    py::gil_scoped_release nogil;
+    d.model->device().synchronize();
+    d.model->set_collectives(nullptr);
+  });
 
   bind_checkpoint_and_load(m);
 }

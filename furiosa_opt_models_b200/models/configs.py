@@ -14,6 +14,12 @@ CONFIGS: dict[str, dict] = {
         layers=2, q_heads=4, kv_heads=2, head_dim=64, vocab=1024, eps=1e-6, qk_norm=True, tied=True,
         rope=QWEN3_ROPE, window=4096, rows=8192,
     ),
+    # A tiny Qwen3 geometry that splits over 2, 4 and 8 chips (tensor-parallel tests).
+    "tiny-qwen3-tp": dict(
+        architecture="Qwen3ForCausalLM", family="qwen3", size="tiny", hidden=256, intermediate=1024,
+        layers=2, q_heads=8, kv_heads=2, head_dim=64, vocab=1024, eps=1e-6, qk_norm=True, tied=True,
+        rope=QWEN3_ROPE, window=4096, rows=8192,
+    ),
     "qwen3-0.6b": dict(
         architecture="Qwen3ForCausalLM", family="qwen3", size="0.6B", hidden=1024, intermediate=3072,
         layers=28, q_heads=16, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,

@@ -1,12 +1,39 @@
-"""Tensor-parallel plumbing of a loaded decoder: peer memory and the fused collectives its
-launches call (attached once per model, on every rank)."""
+"""Tensor-parallel plumbing of a loaded decoder.
+
+Each rank (one process per GPU) allocates a symmetric heap for the fused collectives, exports it
+as a CUDA IPC handle, and opens every peer's handle after an all-gather over the process group.
+From then on the decoder's row-parallel projections end in a fused kernel that reads the peers'
+FP32 partial sums over NVLink, adds them in rank order with the residual and applies the next
+RMSNorm; the vocabulary-parallel head ends in an exchange of (value, token) candidates.
+"""
 
 from __future__ import annotations
 
 
 def attach(model, device) -> None:
-    raise NotImplementedError("tensor parallelism is not attached yet")
+    """Connects `model` (this rank's shard) to its peers; every rank calls it, in the same order."""
+    import torch.distributed as dist
+
+    from furiosa_opt_engine import _native
+
+    world, rank = dist.get_world_size(), dist.get_rank()
+    handle = _native._tp_attach(model, world, rank)
+    handles: list = [None] * world
+    dist.all_gather_object(handles, handle)
+    _native._tp_connect(model, handles)
+    dist.barrier()
+    # A device-side barrier through the heaps proves every peer mapping works before any call.
+    _native._tp_barrier(model)
+    dist.barrier()
 
 
 def detach(model) -> None:
-    pass
+    """Releases the heap once every rank has stopped using it."""
+    import torch.distributed as dist
+
+    from furiosa_opt_engine import _native
+
+    model.device.synchronize()
+    dist.barrier()
+    _native._tp_detach(model)
+    dist.barrier()

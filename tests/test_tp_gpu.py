@@ -1,0 +1,41 @@
+"""Tensor parallelism on 2+ GPUs: the same synthetic decoder (identical logical weights at every
+split) decodes the same greedy tokens at TP=1 and TP=N. Each rank is a process of its own GPU; the
+fused collectives spin only on peers of other GPUs."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WORKER = os.path.join(ROOT, "tests", "workers", "tp_parity.py")
+
+
+def _run(world: int, out: str, model: str, steps: int) -> list:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533", WORKER, out,
+           model, str(steps)]
+    subprocess.run(cmd, check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        return json.load(f)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_matches_single_gpu(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    one = _run(1, str(tmp_path / "tp1.json"), "tiny-qwen3-tp", 12)
+    many = _run(world, str(tmp_path / f"tp{world}.json"), "tiny-qwen3-tp", 12)
+    # Greedy tokens agree (the FP32 partial sums are added in another grouping, so a near-tie may
+    # flip a token late in a sequence; the first tokens must match exactly).
+    assert [t[:4] for t in one] == [t[:4] for t in many]
+    agree = sum(a == b for s1, s2 in zip(one, many) for a, b in zip(s1, s2))
+    total = sum(len(s) for s in one)
+    assert agree >= 0.9 * total, (agree, total)
