@@ -70,10 +70,10 @@ std::vector<std::pair<int64_t, int64_t>> layout(const std::vector<int64_t>& leng
 }
 
 // ------------------------------------------------------------------------------------ planning
-Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const Cache& cache,
-               int64_t adapters_given, const std::vector<bool>& filled, int group,
-               int64_t pad_rows, std::vector<uint8_t>& host) {
-  if (!(cache.spec() == limits.cache)) throw ValueError("cache was allocated for another model");
+Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const CacheSpec& spec,
+               int64_t cache_blocks, int64_t adapters_given, const std::vector<bool>& filled,
+               int group, int64_t pad_rows, std::vector<uint8_t>& host) {
+  if (!(spec == limits.cache)) throw ValueError("cache was allocated for another model");
   std::vector<int64_t> blocks;
   for (const Group& g : limits.cache.groups) {
     if (g.kind.tag != KindTag::Paged) throw Unsupported("a call plans paged cache groups");
@@ -106,7 +106,7 @@ Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const
         throw ValueError("request has fewer blocks than its positions need");
       for (int64_t i = 0; i < used; ++i) {
         const int64_t id = r.rows[g][i];
-        if (id < 0 || id >= cache.blocks()) throw ValueError("block ID is outside the cache");
+        if (id < 0 || id >= cache_blocks) throw ValueError("block ID is outside the cache");
       }
     }
     if (r.keep.kind == KeepKind::Range && (r.keep.from > r.keep.to || r.keep.to > len))

@@ -133,9 +133,10 @@ struct Plan {
 // (grown as needed). `group` is the query heads per key/value head (for the prefill tiles);
 // `pad_decode` pads an all-decode call to `pad_rows` rows (CUDA-graph buckets, 0: no padding).
 // Throws ValueError (invalid input) or Unsupported with the reference's messages.
-Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const Cache& cache,
-               int64_t adapters_given, const std::vector<bool>& adapter_slots_filled, int group,
-               int64_t pad_rows, std::vector<uint8_t>& host);
+Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const CacheSpec& spec,
+               int64_t blocks, int64_t adapters_given,
+               const std::vector<bool>& adapter_slots_filled, int group, int64_t pad_rows,
+               std::vector<uint8_t>& host);
 
 // The call rows of requests of the given lengths: one-row requests first, then the others, each
 // in request order. Returns [start, end) per request.

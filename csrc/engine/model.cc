@@ -345,7 +345,8 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   const int slot = stage_slot_;
   stage_slot_ ^= 1;
   st->check_cuda(cudaEventSynchronize(stage_done_[slot]), "staging wait");
-  Plan plan = plan_call(requests, lim, cache, 0, {}, group, graphable ? bucket : 0, host_stage_);
+  Plan plan = plan_call(requests, lim, cache.spec(), cache.blocks(), 0, {}, group,
+                        graphable ? bucket : 0, host_stage_);
   if (pinned_stage_[slot].size() < plan.staged.bytes)
     pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
   std::memcpy(pinned_stage_[slot].data(), host_stage_.data(), plan.staged.bytes);
@@ -463,6 +464,10 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     g.counters = i32(ws_counters_);
     g.counters_len = static_cast<int>(ws_counters_.size() / 4);
     g.status = st->status;
+    if (batch_invariant_) {
+      g.mode = foa::kModeRows;
+      g.splits = 1;
+    }
     fail(foa::gemm_bf16(g, s), "gemm");
   };
   const int qkv_cols = (qh_l_ + 2 * kvh_l_) * D;

@@ -117,6 +117,13 @@ class DecoderModel {
   }
   const std::shared_ptr<Collectives>& collectives() const { return coll_; }
   void set_graphs(bool enabled) { graphs_enabled_ = enabled; }
+  // Batch-invariant calls: every projection uses one tiling and one K order whatever the call's
+  // row count (no split-K, one operand mapping), and attention tiles each row by its own history.
+  void set_batch_invariant(bool on) {
+    batch_invariant_ = on;
+    clear_graphs();
+  }
+  bool batch_invariant() const { return batch_invariant_; }
 
   // One call: plans, stages and launches; returns the kept rows' output (tokens I32 [kept],
   // hidden BF16 [kept, hidden] or scores F32 [kept, labels]) once the launches are submitted.
@@ -156,6 +163,7 @@ class DecoderModel {
 
   std::shared_ptr<Collectives> coll_;
   bool graphs_enabled_ = true;
+  bool batch_invariant_ = false;
   struct GraphKey {
     int64_t rows, splits;
     bool operator<(const GraphKey& o) const {

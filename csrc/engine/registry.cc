@@ -1,0 +1,558 @@
+#include "registry.h"
+
+#include <cmath>
+#include <cstring>
+#include <map>
+
+namespace foa::engine {
+
+void LoadRefusal::raise() const {
+  const std::string msg = name + ": " + reason;
+  if (unsupported) throw Unsupported(msg);
+  throw ValueError(msg);
+}
+
+namespace {
+
+[[noreturn]] void invalid(const std::string& name, const std::string& reason) {
+  LoadRefusal{false, name, reason}.raise();
+}
+[[noreturn]] void unsupported(const std::string& name, const std::string& reason) {
+  LoadRefusal{true, name, reason}.raise();
+}
+
+const std::vector<std::string> kNames = {
+#include "architectures.inc"
+};
+
+// ------------------------------------------------------------------------------------ config
+int64_t need_int(const Json& c, const char* key) {
+  const Json& v = c[key];
+  if (!v.is_number()) invalid(std::string("config.json:") + key, "missing or not a number");
+  return v.as_int();
+}
+
+double get_num(const Json& c, const char* key, double def) {
+  const Json& v = c[key];
+  return v.is_number() ? v.as_double() : def;
+}
+
+bool get_bool(const Json& c, const char* key, bool def) {
+  const Json& v = c[key];
+  return v.is_bool() ? v.as_bool() : def;
+}
+
+RopeSpec rope_of(const Json& c, double default_theta) {
+  RopeSpec r;
+  r.theta = get_num(c, "rope_theta", default_theta);
+  const Json* s = &c["rope_scaling"];
+  if (s->is_null() && c["rope_parameters"].is_object()) s = &c["rope_parameters"];
+  if (s->is_object()) {
+    std::string type = (*s)["rope_type"].is_string() ? (*s)["rope_type"].as_string()
+                       : (*s)["type"].is_string()    ? (*s)["type"].as_string()
+                                                     : "default";
+    if ((*s)["rope_theta"].is_number()) r.theta = (*s)["rope_theta"].as_double();
+    if (type == "dynamic" || type == "longrope" || type == "mrope")
+      unsupported("rope_scaling", type + " scaling is not served");
+    if (type != "default" && type != "linear" && type != "llama3" && type != "yarn")
+      unsupported("rope_scaling", "unknown rope type " + type);
+    r.type = type;
+    r.factor = get_num(*s, "factor", 1.0);
+    r.low_freq_factor = get_num(*s, "low_freq_factor", 1.0);
+    r.high_freq_factor = get_num(*s, "high_freq_factor", 4.0);
+    r.original_max_positions =
+        get_num(*s, "original_max_position_embeddings", get_num(c, "max_position_embeddings", 0));
+    r.beta_fast = get_num(*s, "beta_fast", 32.0);
+    r.beta_slow = get_num(*s, "beta_slow", 1.0);
+    r.mscale = get_num(*s, "mscale", 1.0);
+    r.mscale_all_dim = get_num(*s, "mscale_all_dim", 0.0);
+    r.attention_factor = get_num(*s, "attention_factor", 0.0);
+    r.truncate = get_bool(*s, "truncate", true);
+  }
+  return r;
+}
+
+struct KnownSize {
+  const char* family;
+  const char* size;
+  int hidden, intermediate, layers, q_heads, kv_heads;
+};
+// Published geometries of the checkpoints each family serves by name.
+const KnownSize kSizes[] = {
+    {"qwen3", "0.6B", 1024, 3072, 28, 16, 8},   {"qwen3", "1.7B", 2048, 6144, 28, 16, 8},
+    {"qwen3", "4B", 2560, 9728, 36, 32, 8},     {"qwen3", "8B", 4096, 12288, 36, 32, 8},
+    {"qwen3", "14B", 5120, 17408, 40, 40, 8},   {"qwen3", "32B", 5120, 25600, 64, 64, 8},
+    {"llama", "1B", 2048, 8192, 16, 32, 8},     {"llama", "3B", 3072, 8192, 28, 24, 8},
+    {"llama", "8B", 4096, 14336, 32, 32, 8},    {"llama", "70B", 8192, 28672, 80, 64, 8},
+    {"mistral", "7B", 4096, 14336, 32, 32, 8},  {"mistral", "12B", 5120, 14336, 40, 32, 8},
+    {"qwen3_moe", "30B-A3B", 2048, 6144, 48, 32, 4}, {"qwen3_moe", "235B-A22B", 4096, 12288, 94, 64, 4},
+};
+
+std::string size_of(const std::string& family, const ModelConfig& m) {
+  for (const auto& k : kSizes)
+    if (family == k.family && m.hidden == k.hidden && m.layers == k.layers &&
+        m.q_heads == k.q_heads && m.kv_heads == k.kv_heads &&
+        (family == "qwen3_moe" || m.intermediate == k.intermediate))
+      return k.size;
+  return "custom";
+}
+
+// The decoder geometry every family shares, from an HF config.
+ModelConfig decoder_config(const Checkpoint& ck, const std::string& family, double theta, float eps_default) {
+  const Json& c = ck.config();
+  ModelConfig m;
+  m.family = family;
+  m.hidden = static_cast<int>(need_int(c, "hidden_size"));
+  m.layers = static_cast<int>(need_int(c, "num_hidden_layers"));
+  m.q_heads = static_cast<int>(need_int(c, "num_attention_heads"));
+  m.kv_heads = c["num_key_value_heads"].is_number() ? static_cast<int>(c["num_key_value_heads"].as_int())
+                                                   : m.q_heads;
+  m.head_dim = c["head_dim"].is_number() ? static_cast<int>(c["head_dim"].as_int()) : m.hidden / m.q_heads;
+  m.vocab = static_cast<int>(need_int(c, "vocab_size"));
+  m.intermediate = c["intermediate_size"].is_number() ? static_cast<int>(c["intermediate_size"].as_int()) : 0;
+  m.eps = static_cast<float>(get_num(c, "rms_norm_eps", eps_default));
+  m.tied = get_bool(c, "tie_word_embeddings", false);
+  m.rope = rope_of(c, theta);
+  const int64_t positions = c["max_position_embeddings"].is_number() ? c["max_position_embeddings"].as_int() : 32768;
+  m.window = static_cast<int>(std::min<int64_t>(positions, 131072));
+  m.rows = 8192;
+  if (m.head_dim != 64 && m.head_dim != 128)
+    unsupported("head_dim", std::to_string(m.head_dim) + ", the attention kernels hold 64 or 128");
+  if (m.q_heads % m.kv_heads != 0 || m.q_heads / m.kv_heads > 16)
+    unsupported("num_key_value_heads", "query heads do not group evenly over at most 16 per key/value head");
+  if (m.hidden % 64 != 0) unsupported("hidden_size", "not a multiple of 64");
+  if (get_bool(c, "attention_bias", false)) unsupported("attention_bias", family + " projects without biases");
+  if (get_bool(c, "mlp_bias", false)) unsupported("mlp_bias", family + " projects without biases");
+  return m;
+}
+
+// ------------------------------------------------------------------------------------ scopes
+ModelConfig qwen3_scope(const Checkpoint& ck, Output output, const std::string& form) {
+  ModelConfig m = decoder_config(ck, "qwen3", 1000000.0, 1e-6f);
+  const Json& c = ck.config();
+  m.qk_norm = true;
+  if (get_bool(c, "use_sliding_window", false))
+    unsupported("use_sliding_window", "Qwen3 attends the whole history");
+  const Json& q = ck.declaration();
+  if (form == "bf16" && !q.is_null() && ck.quantization().empty())
+    unsupported("quantization_config", "the BF16 line reads unquantized checkpoints");
+  if (form == "fp8_block") {
+    if (q.is_null() || !q["weight_block_size"].is_array())
+      invalid("config.json:quantization_config", "not a block-scaled FP8 declaration");
+    m.precision = "float8_e4m3fn";
+  }
+  if (m.intermediate % 128 != 0) unsupported("intermediate_size", "not a multiple of 128");
+  m.output = output;
+  if (output == Output::Scores) m.labels = 256;
+  m.size = size_of("qwen3", m);
+  return m;
+}
+
+ModelConfig llama_scope(const Checkpoint& ck, const std::string& family, const std::string& form) {
+  ModelConfig m = decoder_config(ck, family, family == "mistral" ? 1000000.0 : 500000.0, 1e-5f);
+  const Json& c = ck.config();
+  if (family == "mistral" && c["sliding_window"].is_number())
+    unsupported("sliding_window", "Mistral attends the whole history here");
+  const Json& q = ck.declaration();
+  if (form == "bf16" && !q.is_null() && ck.quantization().empty())
+    unsupported("quantization_config", "the BF16 line reads unquantized checkpoints");
+  if (form == "nvfp4") {
+    const bool nvfp4 = q.is_object() && ((q["quant_algo"].is_string() && q["quant_algo"].as_string() == "NVFP4") ||
+                                         (q["quantization"].is_object() && q["quantization"]["quant_algo"].is_string() &&
+                                          q["quantization"]["quant_algo"].as_string() == "NVFP4"));
+    if (!nvfp4) invalid("config.json:quantization_config", "not an NVFP4 declaration");
+    m.precision = "uint8";
+  }
+  if (form == "fp8_block") {
+    if (q.is_null() || !q["weight_block_size"].is_array())
+      invalid("config.json:quantization_config", "not a block-scaled FP8 declaration");
+    m.precision = "float8_e4m3fn";
+  }
+  if (m.intermediate % 128 != 0) unsupported("intermediate_size", "not a multiple of 128");
+  m.size = size_of(family, m);
+  return m;
+}
+
+ModelConfig qwen3_moe_scope(const Checkpoint& ck) {
+  ModelConfig m = decoder_config(ck, "qwen3_moe", 1000000.0, 1e-6f);
+  const Json& c = ck.config();
+  m.qk_norm = true;
+  m.experts = static_cast<int>(need_int(c, "num_experts"));
+  m.top_k = static_cast<int>(need_int(c, "num_experts_per_tok"));
+  m.expert_intermediate = static_cast<int>(need_int(c, "moe_intermediate_size"));
+  m.norm_topk = get_bool(c, "norm_topk_prob", true);
+  if (c["mlp_only_layers"].is_array() && c["mlp_only_layers"].size() > 0)
+    unsupported("mlp_only_layers", "every layer routes to experts here");
+  if (get_num(c, "decoder_sparse_step", 1) != 1) unsupported("decoder_sparse_step", "every layer routes to experts here");
+  if (!ck.declaration().is_null()) unsupported("quantization_config", "the MoE line reads BF16 checkpoints");
+  m.size = size_of("qwen3_moe", m);
+  m.precision = "bfloat16";
+  return m;
+}
+
+Implementation make(const char* family, const char* cls, const char* form, Output out,
+                    std::function<ModelConfig(const Checkpoint&)> scope) {
+  Implementation i;
+  i.family = family;
+  i.cls = cls;
+  i.form = form;
+  i.output = out;
+  i.scope = std::move(scope);
+  return i;
+}
+
+const std::map<std::string, std::vector<Implementation>>& served() {
+  static const std::map<std::string, std::vector<Implementation>> table = [] {
+    std::map<std::string, std::vector<Implementation>> t;
+    t["Qwen3ForCausalLM"] = {
+        make("qwen3", "qwen3.ForCausalLM", "bf16", Output::Tokens,
+             [](const Checkpoint& c) { return qwen3_scope(c, Output::Tokens, "bf16"); }),
+        make("qwen3", "qwen3.ForCausalLM", "fp8_block", Output::Tokens,
+             [](const Checkpoint& c) { return qwen3_scope(c, Output::Tokens, "fp8_block"); }),
+    };
+    t["Qwen3ForSequenceClassification"] = {
+        make("qwen3", "qwen3.ForSequenceClassification", "bf16", Output::Scores,
+             [](const Checkpoint& c) { return qwen3_scope(c, Output::Scores, "bf16"); })};
+    t["Qwen3Model"] = {make("qwen3", "qwen3.Model", "bf16", Output::Hidden,
+                            [](const Checkpoint& c) { return qwen3_scope(c, Output::Hidden, "bf16"); })};
+    t["LlamaForCausalLM"] = {
+        make("llama", "llama.ForCausalLM", "bf16", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "llama", "bf16"); }),
+        make("llama", "llama.ForCausalLM", "nvfp4", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "llama", "nvfp4"); }),
+        make("llama", "llama.ForCausalLM", "fp8_block", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "llama", "fp8_block"); }),
+    };
+    t["MistralForCausalLM"] = {make("mistral", "mistral.ForCausalLM", "bf16", Output::Tokens,
+                                    [](const Checkpoint& c) { return llama_scope(c, "mistral", "bf16"); })};
+    t["Qwen3MoeForCausalLM"] = {make("qwen3_moe", "qwen3_moe.ForCausalLM", "bf16", Output::Tokens,
+                                     [](const Checkpoint& c) { return qwen3_moe_scope(c); })};
+    return t;
+  }();
+  return table;
+}
+
+}  // namespace
+
+const std::vector<std::string>& architecture_names() { return kNames; }
+
+Listed listed(const std::vector<std::string>& names) {
+  for (const auto& n : names) {
+    for (const auto& k : kNames) {
+      if (k != n) continue;
+      Listed l;
+      l.name = k;
+      auto it = served().find(k);
+      if (it == served().end() || it->second.empty()) unsupported(k, "no model type is implemented");
+      for (const auto& i : it->second) l.implementations.push_back(&i);
+      return l;
+    }
+  }
+  std::string joined;
+  for (size_t i = 0; i < names.size(); ++i) joined += (i ? ", " : "") + names[i];
+  invalid(joined, "unknown architecture");
+}
+
+const Implementation* choose(const Listed& l, const Checkpoint& c, ModelConfig* config) {
+  std::vector<std::pair<const Implementation*, ModelConfig>> ok;
+  std::vector<std::pair<bool, std::string>> refused;
+  for (const Implementation* i : l.implementations) {
+    try {
+      ModelConfig m = i->scope(c);
+      ok.emplace_back(i, m);
+    } catch (const Unsupported& e) {
+      refused.emplace_back(true, e.what());
+    } catch (const ValueError& e) {
+      refused.emplace_back(false, e.what());
+    }
+  }
+  if (ok.size() == 1) {
+    *config = ok[0].second;
+    config->architecture = l.name;
+    return ok[0].first;
+  }
+  if (ok.empty() && refused.size() == 1) {
+    if (refused[0].first) throw Unsupported(refused[0].second);
+    throw ValueError(refused[0].second);
+  }
+  if (ok.empty()) {
+    // Report the refusal of the line that reads the checkpoint's own form first.
+    for (const auto& r : refused)
+      if (r.first) throw Unsupported(r.second);
+    std::string joined;
+    for (size_t i = 0; i < refused.size(); ++i) joined += (i ? "; " : "") + refused[i].second;
+    invalid(l.name, "no implementation serves the checkpoint: " + joined);
+  }
+  std::string sizes;
+  for (size_t i = 0; i < ok.size(); ++i) sizes += (i ? "; " : "") + ok[i].second.size;
+  invalid(l.name, "implementations of sizes " + sizes + " all serve the checkpoint");
+}
+
+Selection select(const LoadOptions& o, const Checkpoint& ck) {
+  std::vector<std::string> names;
+  if (o.architecture) {
+    names.push_back(*o.architecture);
+  } else {
+    for (const auto& a : ck.config()["architectures"].items())
+      if (a.is_string()) names.push_back(a.as_string());
+    if (ck.config()["_class_name"].is_string()) names.push_back(ck.config()["_class_name"].as_string());
+  }
+  if (names.empty()) invalid("config.json:architectures", "the config names no architecture");
+  const Listed l = listed(names);
+  Selection s;
+  s.architecture = l.name;
+  const Checkpoint* read = &ck;
+  Checkpoint quantized;
+  if (o.quantization) {
+    quantized = ck.quantized(*o.quantization == "fp8_per_tensor" ? "tensor" : "channel");
+    read = &quantized;
+  }
+  if (o.encoder && read->part() == Part::Whole)
+    unsupported("encoder", "a decoder holds no media encoder that loads alone");
+  s.implementation = choose(l, *read, &s.config);
+  const ModelConfig& m = s.config;
+  s.chips = o.chips.value_or(1);
+  if (s.chips != 1 && s.chips != 2 && s.chips != 4 && s.chips != 8)
+    unsupported("chips", "a load runs on 1, 2, 4 or 8 chips");
+  if (s.chips > 1) {
+    const int inter = m.experts > 0 ? 128 * s.chips : m.intermediate;
+    const bool split = m.q_heads % s.chips == 0 &&
+                       (m.kv_heads % s.chips == 0 || s.chips % m.kv_heads == 0) &&
+                       inter % s.chips == 0 && (inter / s.chips) % 128 == 0;
+    if (!split)
+      unsupported("chips", "the " + l.name + " " + m.size + " geometry does not split over " +
+                               std::to_string(s.chips) + " chips");
+  }
+  if (o.kv_cache && *o.kv_cache != "bfloat16")
+    unsupported("kv_cache", "every implementation caches keys and values in BF16");
+  if (o.layers) unsupported("layers", "every implementation loads whole");
+  if (o.adapters && s.implementation->adapters == 0)
+    unsupported("adapters", "the " + l.name + " " + m.size + " implementation takes no adapter");
+  if (o.quantization) unsupported("quantization", "load-time FP8 quantization of BF16 checkpoints is not served");
+  if (s.implementation->form == "nvfp4" || s.implementation->form == "fp8_block")
+    unsupported("quantization_config", "the " + s.implementation->form + " line loads through its own path");
+  if (m.experts > 0) unsupported(l.name, "mixture-of-experts loads run through the expert-parallel path");
+  return s;
+}
+
+// ------------------------------------------------------------------------------------ weights
+namespace {
+
+uint16_t f32_to_bf16(float f) {
+  uint32_t b;
+  std::memcpy(&b, &f, 4);
+  if ((b & 0x7fffffffu) > 0x7f800000u) return static_cast<uint16_t>((b >> 16) | 0x40);  // NaN
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return static_cast<uint16_t>(b >> 16);
+}
+
+float f16_to_f32(uint16_t h) {
+  const uint32_t s = (h & 0x8000u) << 16, e = (h >> 10) & 0x1f, m = h & 0x3ff;
+  uint32_t b;
+  if (e == 0) {
+    if (m == 0) {
+      b = s;
+    } else {  // subnormal
+      float f = std::ldexp(static_cast<float>(m), -24);
+      std::memcpy(&b, &f, 4);
+      b |= s;
+    }
+  } else if (e == 31) {
+    b = s | 0x7f800000u | (m << 13);
+  } else {
+    b = s | ((e + 112) << 23) | (m << 13);
+  }
+  float f;
+  std::memcpy(&f, &b, 4);
+  return f;
+}
+
+// Element (r, c) of a 2-D (or 1-D) checkpoint tensor as BF16 bits.
+struct Source {
+  const StoredTensor* t;
+  int64_t rows, cols;
+  Source(const StoredTensor* s) : t(s) {
+    rows = s->shape.size() == 2 ? s->shape[0] : 1;
+    cols = s->shape.empty() ? 1 : s->shape.back();
+  }
+  void row(int64_t r, int64_t c0, int64_t n, uint16_t* out) const {
+    const uint8_t* base = t->data();
+    const int64_t off = r * cols + c0;
+    switch (t->dtype) {
+      case StDType::BF16: std::memcpy(out, base + off * 2, n * 2); break;
+      case StDType::F16:
+        for (int64_t i = 0; i < n; ++i) {
+          uint16_t h;
+          std::memcpy(&h, base + (off + i) * 2, 2);
+          out[i] = f32_to_bf16(f16_to_f32(h));
+        }
+        break;
+      case StDType::F32:
+        for (int64_t i = 0; i < n; ++i) {
+          float f;
+          std::memcpy(&f, base + (off + i) * 4, 4);
+          out[i] = f32_to_bf16(f);
+        }
+        break;
+      default: throw ValueError("a projection of dtype " + std::string(st_dtype_name(t->dtype)) + " does not load as BF16");
+    }
+  }
+};
+
+}  // namespace
+
+void load_weights(DecoderModel& model, const Checkpoint& ck) {
+  const ModelConfig& cfg = model.config();
+  const int H = cfg.hidden, D = cfg.head_dim;
+  const int qh_l = model.q_heads_local(), kvh_l = model.kv_heads_local();
+  const int qh0 = model.q_head_first(), kvh0 = model.kv_head_first();
+  const int inter_l = model.intermediate_local(), rank = model.rank();
+  std::map<std::string, bool> used;
+  for (const auto& n : ck.names()) used[n] = false;
+  std::vector<std::string> missing;
+  auto take = [&](const std::string& name, std::vector<int64_t> shape) -> const StoredTensor* {
+    const StoredTensor* t = ck.get(name);
+    if (!t) {
+      missing.push_back(name);
+      return nullptr;
+    }
+    if (t->shape != shape) {
+      std::string s;
+      for (auto x : t->shape) s += (s.empty() ? "" : ", ") + std::to_string(x);
+      invalid(name, "shape [" + s + "] is not the model's");
+    }
+    used[name] = true;
+    return t;
+  };
+  auto st = model.device().state();
+  std::vector<uint16_t> host;
+  auto upload = [&](const std::string& slot) {
+    const WeightSlot& w = model.weights().at(slot);
+    st->check_cuda(cudaMemcpy(w.ptr, host.data(), host.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+  };
+  auto image = [&](const std::string& slot) {
+    const WeightSlot& w = model.weights().at(slot);
+    size_t n = 1;
+    for (auto s : w.shape) n *= static_cast<size_t>(s);
+    host.assign(n, 0);
+    return w.shape;
+  };
+  // Rows [src0, src0 + n) of `s`, columns [c0, c0 + ncols), into image rows from dst0.
+  auto copy_rows = [&](const Source& s, int64_t src0, int64_t n, int64_t dst0, int64_t c0, int64_t ncols,
+                       int64_t dst_cols) {
+    for (int64_t r = 0; r < n; ++r) s.row(src0 + r, c0, ncols, host.data() + (dst0 + r) * dst_cols);
+  };
+  const std::string pre = "model.";
+  // Embedding (whole on every chip) and head (this chip's vocabulary rows).
+  if (auto* t = take(pre + "embed_tokens.weight", {cfg.vocab, H})) {
+    image("embed");
+    copy_rows(Source(t), 0, cfg.vocab, 0, 0, H, H);
+    upload("embed");
+  }
+  if (!cfg.tied) {
+    if (auto* t = take("lm_head.weight", {cfg.vocab, H})) {
+      image("lm_head");
+      const int64_t n = model.vocab_end() - model.vocab_begin();
+      copy_rows(Source(t), model.vocab_begin(), n, 0, 0, H, H);
+      upload("lm_head");
+    }
+  } else if (ck.get("lm_head.weight")) {
+    used["lm_head.weight"] = true;  // a tied head the checkpoint also stores
+  }
+  if (auto* t = take(pre + "norm.weight", {H})) {
+    image("final_norm");
+    Source(t).row(0, 0, H, host.data());
+    upload("final_norm");
+  }
+  if (cfg.output == Output::Scores) {
+    const StoredTensor* t = ck.get("score.weight");
+    if (!t) {
+      missing.push_back("score.weight");
+    } else {
+      used["score.weight"] = true;
+      image("score");
+      copy_rows(Source(t), 0, t->shape[0], 0, 0, H, H);
+      upload("score");
+    }
+  }
+  for (int l = 0; l < cfg.layers; ++l) {
+    const std::string hf = pre + "layers." + std::to_string(l) + ".";
+    const std::string en = "layers." + std::to_string(l) + ".";
+    if (auto* t = take(hf + "input_layernorm.weight", {H})) {
+      image(en + "in_norm");
+      Source(t).row(0, 0, H, host.data());
+      upload(en + "in_norm");
+    }
+    if (auto* t = take(hf + "post_attention_layernorm.weight", {H})) {
+      image(en + "post_norm");
+      Source(t).row(0, 0, H, host.data());
+      upload(en + "post_norm");
+    }
+    const auto* q = take(hf + "self_attn.q_proj.weight", {static_cast<int64_t>(cfg.q_heads) * D, H});
+    const auto* k = take(hf + "self_attn.k_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
+    const auto* v = take(hf + "self_attn.v_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
+    if (q && k && v) {
+      image(en + "qkv");
+      copy_rows(Source(q), static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D, 0, 0, H, H);
+      copy_rows(Source(k), static_cast<int64_t>(kvh0) * D, static_cast<int64_t>(kvh_l) * D,
+                static_cast<int64_t>(qh_l) * D, 0, H, H);
+      copy_rows(Source(v), static_cast<int64_t>(kvh0) * D, static_cast<int64_t>(kvh_l) * D,
+                static_cast<int64_t>(qh_l + kvh_l) * D, 0, H, H);
+      upload(en + "qkv");
+    }
+    if (cfg.qk_norm) {
+      for (const char* which : {"q_norm", "k_norm"}) {
+        if (auto* t = take(hf + "self_attn." + which + ".weight", {D})) {
+          image(en + which);
+          Source(t).row(0, 0, D, host.data());
+          upload(en + which);
+        }
+      }
+    }
+    if (auto* t = take(hf + "self_attn.o_proj.weight", {H, static_cast<int64_t>(cfg.q_heads) * D})) {
+      image(en + "o");
+      copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D,
+                static_cast<int64_t>(qh_l) * D);
+      upload(en + "o");
+    }
+    if (cfg.experts == 0) {
+      const auto* g = take(hf + "mlp.gate_proj.weight", {cfg.intermediate, H});
+      const auto* u = take(hf + "mlp.up_proj.weight", {cfg.intermediate, H});
+      if (g && u) {
+        // Gate and up rows alternate in 128-row blocks, so one GEMM tile holds both halves of
+        // the SwiGLU it feeds.
+        image(en + "gate_up");
+        const Source sg(g), su(u);
+        for (int64_t j = 0; j < inter_l; ++j) {
+          const int64_t src = static_cast<int64_t>(rank) * inter_l + j;
+          const int64_t block = j / 128, in = j % 128;
+          sg.row(src, 0, H, host.data() + ((block * 256) + in) * H);
+          su.row(src, 0, H, host.data() + ((block * 256) + 128 + in) * H);
+        }
+        upload(en + "gate_up");
+      }
+      if (auto* t = take(hf + "mlp.down_proj.weight", {H, cfg.intermediate})) {
+        image(en + "down");
+        copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(rank) * inter_l, inter_l, inter_l);
+        upload(en + "down");
+      }
+    }
+  }
+  if (!missing.empty()) {
+    std::string s;
+    for (size_t i = 0; i < missing.size() && i < 8; ++i) s += (i ? ", " : "") + missing[i];
+    if (missing.size() > 8) s += ", ... (" + std::to_string(missing.size()) + " in all)";
+    invalid("checkpoint", "missing tensors: " + s);
+  }
+  std::vector<std::string> extra;
+  for (const auto& [n, u] : used)
+    if (!u) extra.push_back(n);
+  if (!extra.empty()) {
+    std::string s;
+    for (size_t i = 0; i < extra.size() && i < 8; ++i) s += (i ? ", " : "") + extra[i];
+    if (extra.size() > 8) s += ", ... (" + std::to_string(extra.size()) + " in all)";
+    invalid("checkpoint", "unexpected tensors: " + s);
+  }
+}
+
+}  // namespace foa::engine

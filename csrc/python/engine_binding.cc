@@ -15,6 +15,7 @@
 #include "engine/model.h"
 #include "engine/registry.h"
 #include "engine/runtime.h"
+#include "python/pytypes.h"
 
 namespace py = pybind11;
 using namespace foa::engine;
@@ -88,19 +89,6 @@ py::array host_numpy(const std::vector<int64_t>& shape, DType dtype, const uint8
 }
 
 }  // namespace
-
-// Decoder objects the binding hands out: the model, its load's descriptive fields.
-struct PyDecoder {
-  std::shared_ptr<DecoderModel> model;
-  std::string size, precision, kv_cache = "bfloat16";
-  int parallel = 1;
-};
-struct PyQwen3ForCausalLM : PyDecoder {};
-struct PyQwen3ForSequenceClassification : PyDecoder {};
-struct PyQwen3Model : PyDecoder {};
-struct PyLlamaForCausalLM : PyDecoder {};
-struct PyMistralForCausalLM : PyDecoder {};
-struct PyQwen3MoeForCausalLM : PyDecoder {};
 
 struct PyCacheSpec {
   CacheSpec spec;
@@ -595,6 +583,79 @@ void bind_engine(py::module_& m) {
      py::arg("seed") = 0, py::arg("std") = 0.02f);
 
   m.def("_layout", [](const std::vector<int64_t>& lens) { return layout(lens); });
+
+  // The batch planner without a device: requests as dicts, the model's limits and the cache's
+  // spec as tuples. Raises the planner's refusals; returns the plan's host arrays.
+  m.def("_plan", [](const py::list& requests, int64_t window, int64_t rows, int64_t adapters_limit,
+                    const py::list& spec_pools, const py::list& spec_groups,
+                    const py::list& cache_pools, const py::list& cache_groups, int64_t blocks,
+                    int64_t adapters_given, const std::vector<bool>& filled, int group) {
+    auto spec_of = [](const py::list& pools, const py::list& groups) {
+      CacheSpec s;
+      for (auto p : pools) {
+        auto t = p.cast<py::tuple>();
+        s.pools.push_back(Pool{t[0].cast<int64_t>(), t[1].cast<int64_t>()});
+      }
+      for (auto g : groups) {
+        auto t = g.cast<py::tuple>();
+        Group gr;
+        gr.pool = t[0].cast<int64_t>();
+        gr.layers_begin = t[1].cast<int64_t>();
+        gr.layers_end = t[2].cast<int64_t>();
+        const std::string kind = t[3].cast<std::string>();
+        gr.kind.tag = kind == "paged" ? KindTag::Paged : kind == "state" ? KindTag::State : KindTag::Cross;
+        gr.kind.length = t[4].cast<int64_t>();
+        if (!t[5].is_none()) gr.window = t[5].cast<int64_t>();
+        s.groups.push_back(gr);
+      }
+      return s;
+    };
+    Limits lim;
+    lim.window = window;
+    lim.rows = rows;
+    lim.adapters = adapters_limit;
+    lim.cache = spec_of(spec_pools, spec_groups);
+    const CacheSpec cache_spec = spec_of(cache_pools, cache_groups);
+    std::vector<Request> reqs;
+    for (auto item : requests) {
+      py::dict d = item.cast<py::dict>();
+      Request r;
+      r.rows = d["rows"].cast<std::vector<std::vector<int64_t>>>();
+      r.cached = d["cached"].cast<int64_t>();
+      r.length = d["length"].cast<int64_t>();
+      py::object keep = d.contains("keep") ? py::object(d["keep"]) : py::str("last");
+      if (py::isinstance<py::str>(keep)) {
+        const std::string k = keep.cast<std::string>();
+        r.keep.kind = k == "none" ? KeepKind::None : k == "all" ? KeepKind::All : KeepKind::Last;
+      } else {
+        auto t = keep.cast<py::tuple>();
+        r.keep = Keep{KeepKind::Range, t[0].cast<int64_t>(), t[1].cast<int64_t>()};
+      }
+      if (d.contains("adapter") && !d["adapter"].is_none()) r.adapter = d["adapter"].cast<int64_t>();
+      r.positions = d.contains("positions") && d["positions"].cast<bool>();
+      r.mask = d.contains("mask") && d["mask"].cast<bool>();
+      r.overrides = d.contains("overrides") && d["overrides"].cast<bool>();
+      reqs.push_back(std::move(r));
+    }
+    std::vector<uint8_t> host;
+    const Plan p = plan_call(reqs, lim, cache_spec, blocks, adapters_given, filled, group, 0, host);
+    auto arr = [&](size_t off, int64_t n) {
+      std::vector<int32_t> v(n);
+      std::memcpy(v.data(), host.data() + off, n * 4);
+      return v;
+    };
+    py::dict out;
+    out["rows"] = p.rows;
+    out["decode"] = p.decode;
+    out["prefill"] = p.prefill;
+    out["kept"] = p.kept_rows;
+    out["positions"] = arr(p.staged.positions, p.rows);
+    out["slots"] = arr(p.staged.slots, p.rows);
+    out["segments"] = arr(p.staged.segments, 5 * (p.decode + p.prefill));
+    out["work"] = arr(p.staged.work, 2 * p.work);
+    out["staged_bytes"] = p.staged.bytes;
+    return out;
+  });
 
   // Tensor parallelism: a symmetric heap per rank, connected through CUDA IPC handles that the
   // ranks exchange over their process group.

@@ -1,4 +1,174 @@
-// Checkpoints and load options (filled in by the checkpoint layer).
+// Checkpoints and load options: the choices of a load, checked against the registry before any
+// weight is read, and the strict load into device memory.
 #include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include "engine/checkpoint.h"
+#include "engine/registry.h"
+#include "python/pytypes.h"
+
 namespace py = pybind11;
-void bind_checkpoint_and_load(py::module_& m) { (void)m; }
+using namespace foa::engine;
+
+namespace {
+
+Json to_json(const py::object& o) {
+  const std::string text = py::module_::import("json").attr("dumps")(o).cast<std::string>();
+  return Json::parse(text);
+}
+
+py::object from_json(const Json& j) {
+  return py::module_::import("json").attr("loads")(j.dump());
+}
+
+struct PyCheckpoint {
+  std::shared_ptr<Checkpoint> ck;
+};
+
+py::object make_decoder(const Selection& s, std::shared_ptr<DecoderModel> model, bool invariant) {
+  auto fill = [&](PyDecoder& d) {
+    d.model = model;
+    d.size = s.config.size;
+    d.precision = s.config.precision;
+    d.parallel = s.chips;
+    d.batch_invariant = invariant;
+  };
+  const std::string& cls = s.implementation->cls;
+  if (cls == "qwen3.ForSequenceClassification") {
+    PyQwen3ForSequenceClassification d;
+    fill(d);
+    return py::cast(d);
+  }
+  if (cls == "qwen3.Model") {
+    PyQwen3Model d;
+    fill(d);
+    return py::cast(d);
+  }
+  if (cls == "llama.ForCausalLM") {
+    PyLlamaForCausalLM d;
+    fill(d);
+    return py::cast(d);
+  }
+  if (cls == "mistral.ForCausalLM") {
+    PyMistralForCausalLM d;
+    fill(d);
+    return py::cast(d);
+  }
+  PyQwen3ForCausalLM d;
+  fill(d);
+  return py::cast(d);
+}
+
+}  // namespace
+
+void bind_checkpoint_and_load(py::module_& m) {
+  py::class_<PyCheckpoint>(m, "Checkpoint",
+                           "The tensors of a checkpoint directory, mapped or read into host memory, "
+                           "and the config of its model.")
+      .def(py::init([](const py::object& path, const py::object& config) {
+             const std::string p = py::str(py::module_::import("os").attr("fspath")(path));
+             std::optional<Json> cfg;
+             if (!config.is_none()) cfg = to_json(config);
+             py::gil_scoped_release nogil;
+             return PyCheckpoint{std::make_shared<Checkpoint>(Checkpoint::open(p, cfg ? &*cfg : nullptr))};
+           }),
+           py::arg("path"), py::arg("config") = py::none())
+      .def("read", [](const PyCheckpoint& c) {
+        py::gil_scoped_release nogil;
+        return PyCheckpoint{std::make_shared<Checkpoint>(c.ck->read())};
+      })
+      .def_property_readonly("config", [](const PyCheckpoint& c) { return from_json(c.ck->config()); })
+      .def("names", [](const PyCheckpoint& c) { return c.ck->names(); })
+      .def_static("declared", [](const py::object& path, const py::object& config) {
+        const std::string p = py::str(py::module_::import("os").attr("fspath")(path));
+        std::optional<Json> cfg;
+        if (!config.is_none()) cfg = to_json(config);
+        return PyCheckpoint{std::make_shared<Checkpoint>(Checkpoint::open(p, cfg ? &*cfg : nullptr, true))};
+      }, py::arg("path"), py::arg("config") = py::none());
+
+  py::class_<LoadOptions>(m, "LoadOptions",
+                          "A load's architecture, chips, KV cache form, layers, batch invariance, "
+                          "quantization and LoRA adapters.")
+      .def(py::init<>())
+      .def("chips", [](const LoadOptions& o, int64_t chips) {
+        if (chips <= 0) throw ValueError("chips: a model loads onto at least one chip");
+        LoadOptions n = o;
+        n.chips = static_cast<int>(chips);
+        return n;
+      }, py::arg("chips"))
+      .def("kv_cache", [](const LoadOptions& o, const std::string& dtype) {
+        dtype_from_name(dtype);
+        LoadOptions n = o;
+        n.kv_cache = dtype;
+        return n;
+      }, py::arg("dtype"))
+      .def("architecture", [](const LoadOptions& o, const std::string& name) {
+        const Listed l = listed({name});
+        LoadOptions n = o;
+        n.architecture = l.name;
+        return n;
+      }, py::arg("name"))
+      .def("layers", [](const LoadOptions& o, const py::object& r) {
+        const int64_t start = r.attr("start").cast<int64_t>(), stop = r.attr("stop").cast<int64_t>(),
+                      step = r.attr("step").cast<int64_t>();
+        if (step != 1 || start < 0 || stop < 0)
+          throw ValueError("layers: a range of step 1 with non-negative bounds");
+        LoadOptions n = o;
+        n.layers = std::make_pair(start, stop);
+        return n;
+      }, py::arg("layers"))
+      .def("batch_invariant", [](const LoadOptions& o) {
+        LoadOptions n = o;
+        n.batch_invariant = true;
+        return n;
+      })
+      .def("quantization", [](const LoadOptions& o, const std::string& name) {
+        if (name != "fp8_per_tensor" && name != "fp8_per_channel")
+          throw ValueError(name + ": a quantization is fp8_per_tensor or fp8_per_channel");
+        LoadOptions n = o;
+        n.quantization = name;
+        return n;
+      }, py::arg("name"))
+      .def("encoder", [](const LoadOptions& o) {
+        LoadOptions n = o;
+        n.encoder = true;
+        return n;
+      })
+      .def("adapters", [](const LoadOptions& o) {
+        LoadOptions n = o;
+        n.adapters = true;
+        return n;
+      })
+      .def("parse", [](const LoadOptions& o, const PyCheckpoint& c) {
+        select(o, *c.ck);
+      }, py::arg("checkpoint"))
+      .def("select", [](const LoadOptions& o, const PyCheckpoint& c) {
+        const Selection s = select(o, *c.ck);
+        py::dict d;
+        d["architecture"] = s.architecture;
+        d["class"] = s.implementation->cls;
+        d["size"] = s.config.size;
+        d["precision"] = s.config.precision;
+        d["chips"] = s.chips;
+        return d;
+      }, py::arg("checkpoint"))
+      .def("load", [](const LoadOptions& o, const PyCheckpoint& c, const Device& device) -> py::object {
+        const Selection s = select(o, *c.ck);
+        if (device.chips() != s.chips)
+          throw ValueError("the device opens " + std::to_string(device.chips()) + " chips, the load " +
+                           std::to_string(s.chips));
+        std::shared_ptr<DecoderModel> model;
+        {
+          py::gil_scoped_release nogil;
+          model = std::make_shared<DecoderModel>(device, s.config, s.chips, device.state()->rank);
+          load_weights(*model, *c.ck);
+          model->set_batch_invariant(o.batch_invariant);
+        }
+        py::object decoder = make_decoder(s, model, o.batch_invariant);
+        if (s.chips > 1)
+          py::module_::import("furiosa_opt_models_b200.parallel.tp").attr("attach")(decoder, device);
+        return decoder;
+      }, py::arg("checkpoint"), py::arg("device"));
+
+  m.def("_architectures", []() { return architecture_names(); });
+}

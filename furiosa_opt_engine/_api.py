@@ -12,6 +12,8 @@ Transfer = _native.Transfer
 HbmTensor = _native.HbmTensor
 HostTensor = _native.HostTensor
 Decoder = _native.Decoder
+Checkpoint = _native.Checkpoint
+LoadOptions = _native.LoadOptions
 decoder = _native.decoder
 qwen3 = _native.qwen3
 llama = _native.llama
@@ -22,12 +24,14 @@ for _name in ("decoder", "qwen3", "llama", "mistral", "qwen3_moe"):
     _sys.modules[f"furiosa_opt_engine.{_name}"] = getattr(_native, _name)
 
 __all__ = [
+    "Checkpoint",
     "Decoder",
     "Device",
     "HbmBuffer",
     "HbmTensor",
     "HostBuffer",
     "HostTensor",
+    "LoadOptions",
     "Placement",
     "Transfer",
     "decoder",

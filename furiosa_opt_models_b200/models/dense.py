@@ -47,8 +47,10 @@ def inv_freq(cfg: dict) -> torch.Tensor:
     return base.float()
 
 
-def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor) -> torch.Tensor:
-    """Logits [len(ids), vocab] of one sequence from position 0, FP32."""
+def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> torch.Tensor:
+    """Logits [len(ids), vocab] of one sequence from position 0, FP32 math; with `round_bf16` every
+    stored activation is rounded to BF16 where the engine's GPU kernels store BF16."""
+    rb = (lambda t: t.bfloat16().float()) if round_bf16 else (lambda t: t)
     H, D = cfg["hidden"], cfg.get("head_dim", 128)
     qh, kvh = cfg["q_heads"], cfg["kv_heads"]
     eps = cfg["eps"]
@@ -59,21 +61,23 @@ def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor) -> torch.T
     mask = torch.ones(T, T, dtype=torch.bool).tril()
     for l in range(cfg["layers"]):
         p = f"layers.{l}."
-        h = reference.rmsnorm(x, w[p + "in_norm"], eps).bfloat16().float()
-        qkv = (h @ w[p + "qkv"].float().T).bfloat16().float()
-        q, k, v = reference.qk_front(qkv, qh, kvh, D, w.get(p + "q_norm"), w.get(p + "k_norm"), eps, pos, freqs)
-        q, k = q.bfloat16().float(), k.bfloat16().float()
+        h = rb(reference.rmsnorm(x, w[p + "in_norm"], eps))
+        qkv = rb(h @ w[p + "qkv"].float().T)
+        q, k, v = reference.qk_front(qkv, qh, kvh, D, w.get(p + "q_norm"), w.get(p + "k_norm"), eps, pos,
+                                     freqs, round_bf16=round_bf16)
+        q, k = rb(q), rb(k)
         g = qh // kvh
         k = k.repeat_interleave(g, 1)
         v = v.repeat_interleave(g, 1)
         s = torch.einsum("qhd,khd->hqk", q, k) * D ** -0.5
         s = s.masked_fill(~mask[None], float("-inf"))
-        a = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, qh * D).bfloat16().float()
-        x = (x + a @ w[p + "o"].float().T).bfloat16().float()
-        h = reference.rmsnorm(x, w[p + "post_norm"], eps).bfloat16().float()
+        a = rb(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, qh * D))
+        x = rb(x + a @ w[p + "o"].float().T)
+        h = rb(reference.rmsnorm(x, w[p + "post_norm"], eps))
         gate, up = split_gate_up(w[p + "gate_up"].float())
-        act = reference.swiglu(h @ gate.T, h @ up.T).bfloat16().float()
-        x = (x + act @ w[p + "down"].float().T).bfloat16().float()
-    h = reference.rmsnorm(x, w["final_norm"], eps).bfloat16().float()
+        g, u = h @ gate.T, h @ up.T
+        act = rb(reference.swiglu(g, u)) if round_bf16 else torch.nn.functional.silu(g) * u
+        x = rb(x + act @ w[p + "down"].float().T)
+    h = rb(reference.rmsnorm(x, w["final_norm"], eps))
     head = w["lm_head"] if "lm_head" in w else w["embed"]
     return h @ head[: cfg["vocab"]].float().T

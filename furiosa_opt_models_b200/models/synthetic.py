@@ -1,0 +1,137 @@
+"""Synthetic Hugging Face checkpoints: a config.json and safetensors files of random-init
+N(0, std) weights under the HF tensor names of a named geometry. Tests and benchmarks load them
+through the public LoadOptions path (there is no network for published checkpoints)."""
+
+from __future__ import annotations
+
+import json
+import os
+
+import torch
+
+from . import configs
+
+
+def hf_config(cfg: dict) -> dict:
+    """The HF config.json of an engine geometry."""
+    out = {
+        "architectures": [cfg["architecture"]],
+        "model_type": {"qwen3": "qwen3", "llama": "llama", "mistral": "mistral", "qwen3_moe": "qwen3_moe"}[cfg["family"]],
+        "hidden_size": cfg["hidden"],
+        "intermediate_size": cfg["intermediate"],
+        "num_hidden_layers": cfg["layers"],
+        "num_attention_heads": cfg["q_heads"],
+        "num_key_value_heads": cfg["kv_heads"],
+        "head_dim": cfg["head_dim"],
+        "vocab_size": cfg["vocab"],
+        "rms_norm_eps": cfg["eps"],
+        "tie_word_embeddings": cfg["tied"],
+        "max_position_embeddings": cfg["window"],
+        "torch_dtype": "bfloat16",
+        "attention_bias": False,
+    }
+    rope = cfg.get("rope", {"type": "default", "theta": 10000.0})
+    out["rope_theta"] = rope["theta"]
+    if rope.get("type", "default") != "default":
+        scaling = {"rope_type": rope["type"], "factor": rope["factor"]}
+        for k in ("low_freq_factor", "high_freq_factor"):
+            if k in rope:
+                scaling[k] = rope[k]
+        if "original_max_positions" in rope:
+            scaling["original_max_position_embeddings"] = rope["original_max_positions"]
+        out["rope_scaling"] = scaling
+    if cfg["family"] == "qwen3":
+        out["use_sliding_window"] = False
+    if cfg["family"] == "qwen3_moe":
+        out.update(num_experts=cfg["experts"], num_experts_per_tok=cfg["top_k"],
+                   moe_intermediate_size=cfg["expert_intermediate"], norm_topk_prob=cfg["norm_topk"],
+                   decoder_sparse_step=1, mlp_only_layers=[])
+    return out
+
+
+def hf_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict[str, torch.Tensor]:
+    """HF-named BF16 weights of a geometry (CPU tensors)."""
+    g = torch.Generator().manual_seed(seed)
+    H, D, I = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
+    qh, kvh, V = cfg["q_heads"], cfg["kv_heads"], cfg["vocab"]
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g) * std).bfloat16()
+
+    def ones(n):
+        return (1.0 + 0.1 * torch.randn(n, generator=g)).bfloat16()
+
+    w = {"model.embed_tokens.weight": rnd(V, H), "model.norm.weight": ones(H)}
+    if not cfg["tied"]:
+        w["lm_head.weight"] = rnd(V, H)
+    for l in range(cfg["layers"]):
+        p = f"model.layers.{l}."
+        w[p + "input_layernorm.weight"] = ones(H)
+        w[p + "post_attention_layernorm.weight"] = ones(H)
+        w[p + "self_attn.q_proj.weight"] = rnd(qh * D, H)
+        w[p + "self_attn.k_proj.weight"] = rnd(kvh * D, H)
+        w[p + "self_attn.v_proj.weight"] = rnd(kvh * D, H)
+        w[p + "self_attn.o_proj.weight"] = rnd(H, qh * D)
+        if cfg.get("qk_norm"):
+            w[p + "self_attn.q_norm.weight"] = ones(D)
+            w[p + "self_attn.k_norm.weight"] = ones(D)
+        if cfg["family"] == "qwen3_moe":
+            E, Ie = cfg["experts"], cfg["expert_intermediate"]
+            w[p + "mlp.gate.weight"] = rnd(E, H)
+            for e in range(E):
+                w[p + f"mlp.experts.{e}.gate_proj.weight"] = rnd(Ie, H)
+                w[p + f"mlp.experts.{e}.up_proj.weight"] = rnd(Ie, H)
+                w[p + f"mlp.experts.{e}.down_proj.weight"] = rnd(H, Ie)
+        else:
+            w[p + "mlp.gate_proj.weight"] = rnd(I, H)
+            w[p + "mlp.up_proj.weight"] = rnd(I, H)
+            w[p + "mlp.down_proj.weight"] = rnd(H, I)
+    return w
+
+
+def write(directory: str, name_or_cfg, seed: int = 0, std: float = 0.02, shards: int = 1) -> dict:
+    """Writes a synthetic checkpoint of `name_or_cfg` into `directory`; returns its weights."""
+    from safetensors.torch import save_file
+
+    cfg = configs.get(name_or_cfg) if isinstance(name_or_cfg, str) else name_or_cfg
+    os.makedirs(directory, exist_ok=True)
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(hf_config(cfg), f)
+    weights = hf_weights(cfg, seed, std)
+    names = sorted(weights)
+    if shards == 1:
+        save_file(weights, os.path.join(directory, "model.safetensors"))
+    else:
+        per = (len(names) + shards - 1) // shards
+        weight_map = {}
+        for s in range(shards):
+            part = names[s * per : (s + 1) * per]
+            fname = f"model-{s + 1:05d}-of-{shards:05d}.safetensors"
+            save_file({n: weights[n] for n in part}, os.path.join(directory, fname))
+            weight_map.update({n: fname for n in part})
+        with open(os.path.join(directory, "model.safetensors.index.json"), "w") as f:
+            json.dump({"metadata": {}, "weight_map": weight_map}, f)
+    return weights
+
+
+def engine_weights(cfg: dict, hf: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    """The engine's (single-chip) weight layout of HF-named weights, for the dense oracle."""
+    from .dense import interleave_gate_up
+
+    out = {"embed": hf["model.embed_tokens.weight"], "final_norm": hf["model.norm.weight"]}
+    if "lm_head.weight" in hf:
+        out["lm_head"] = hf["lm_head.weight"]
+    for l in range(cfg["layers"]):
+        p, e = f"model.layers.{l}.", f"layers.{l}."
+        out[e + "in_norm"] = hf[p + "input_layernorm.weight"]
+        out[e + "post_norm"] = hf[p + "post_attention_layernorm.weight"]
+        out[e + "qkv"] = torch.cat([hf[p + "self_attn.q_proj.weight"], hf[p + "self_attn.k_proj.weight"],
+                                    hf[p + "self_attn.v_proj.weight"]])
+        out[e + "o"] = hf[p + "self_attn.o_proj.weight"]
+        if p + "self_attn.q_norm.weight" in hf:
+            out[e + "q_norm"] = hf[p + "self_attn.q_norm.weight"]
+            out[e + "k_norm"] = hf[p + "self_attn.k_norm.weight"]
+        if p + "mlp.gate_proj.weight" in hf:
+            out[e + "gate_up"] = interleave_gate_up(hf[p + "mlp.gate_proj.weight"], hf[p + "mlp.up_proj.weight"])
+            out[e + "down"] = hf[p + "mlp.down_proj.weight"]
+    return out

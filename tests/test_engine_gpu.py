@@ -78,3 +78,52 @@ def test_refusals_match_reference_messages():
             model.forward(reqs, cache)
     with pytest.raises(NotImplementedError, match="explicit positions are not served"):
         model.forward([dec.Request([[0]], 0, ids, positions=ids)], cache)
+
+
+def test_load_checkpoint_strictly_and_decode(tmp_path):
+    """A synthetic HF checkpoint through Checkpoint -> LoadOptions.load: the loaded decoder's
+    greedy continuation agrees with the dense forward of the checkpoint's own weights."""
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=5, std=0.05, shards=2)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    ck = engine.Checkpoint(str(tmp_path / "m"))
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine.LoadOptions().load(ck, device)
+    assert type(model).__name__ == "ForCausalLM" and model.size == "custom"
+    assert model.cache.pools[0].block == 16
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    gen = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg["vocab"], (21,), generator=gen, dtype=torch.int32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(prompt).to_hbm(device), 21, alloc.take(4))]
+    toks = [serving.prefill(model, cache, seqs, [0]).to_host().numpy()[0]]
+    for _ in range(8):
+        toks.append(serving.decode(model, cache, seqs).to_host().numpy()[0])
+    seq = prompt.clone()
+    for t in toks:
+        logits = dense.forward(w, cfg, seq)[-1]
+        assert logits[int(t)] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+        seq = torch.cat([seq, torch.tensor([int(t)], dtype=torch.int32)])
+
+
+def test_load_refuses_a_missing_tensor(tmp_path):
+    import os
+
+    import furiosa_opt_engine as engine
+    from safetensors.torch import load_file, save_file
+    from furiosa_opt_models_b200.models import synthetic
+
+    synthetic.write(str(tmp_path / "m"), "tiny-qwen3")
+    path = str(tmp_path / "m" / "model.safetensors")
+    w = load_file(path)
+    del w["model.layers.1.mlp.down_proj.weight"]
+    w["model.extra.weight"] = torch.zeros(4, dtype=torch.bfloat16)
+    save_file(w, path)
+    device = engine.Device(engine.Placement([0], range(8)))
+    with pytest.raises(ValueError, match="missing tensors: model.layers.1.mlp.down_proj.weight"):
+        engine.LoadOptions().load(engine.Checkpoint(str(tmp_path / "m")), device)

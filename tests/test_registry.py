@@ -1,0 +1,89 @@
+"""The registry and load options: every name once, lookups and refusals by kind and message, and
+the choices a load makes from a config alone (no weight is read, no device opened)."""
+
+import json
+import os
+
+import pytest
+
+import furiosa_opt_engine as engine
+from furiosa_opt_engine import _native
+from furiosa_opt_models_b200.models import configs, synthetic
+
+
+def test_lists_every_name_once():
+    names = _native._architectures()
+    assert len(names) == 670
+    assert len(set(names)) == 670
+
+
+def _ckpt(tmp_path, config):
+    d = tmp_path / "ck"
+    d.mkdir(exist_ok=True)
+    return engine.Checkpoint(str(d), config)
+
+
+def test_selects_the_first_listed_architecture(tmp_path):
+    unknown = "UnknownForCausalLM"
+    with pytest.raises(ValueError, match="config.json:hidden_size"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, {"architectures": [unknown, "Qwen3ForCausalLM"]}))
+    with pytest.raises(NotImplementedError, match="ApertusForCausalLM: no model type is implemented"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, {"architectures": [unknown, "ApertusForCausalLM", "Qwen3ForCausalLM"]}))
+    with pytest.raises(NotImplementedError, match="FluxPipeline"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, {"architectures": [unknown], "_class_name": "FluxPipeline"}))
+    with pytest.raises(ValueError, match="UnknownForCausalLM, UnknownModel: unknown architecture"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, {"architectures": [unknown, "UnknownModel"]}))
+    with pytest.raises(ValueError, match="the config names no architecture"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, {}))
+
+
+@pytest.mark.parametrize("name,size", [("qwen3-1.7b", "1.7B"), ("qwen3-8b", "8B"), ("llama-3.1-8b", "8B"),
+                                       ("llama-3.3-70b", "70B"), ("tiny-qwen3", "custom")])
+def test_parse_reads_the_config_alone(tmp_path, name, size):
+    cfg = synthetic.hf_config(configs.get(name))
+    sel = engine.LoadOptions().select(_ckpt(tmp_path, cfg))
+    assert sel["size"] == size
+    assert sel["precision"] == "bfloat16"
+
+
+def test_option_refusals(tmp_path):
+    ck = _ckpt(tmp_path, synthetic.hf_config(configs.get("qwen3-1.7b")))
+    with pytest.raises(ValueError, match="chips: a model loads onto at least one chip"):
+        engine.LoadOptions().chips(0)
+    with pytest.raises(ValueError):
+        engine.LoadOptions().kv_cache("nonsense")
+    with pytest.raises(NotImplementedError, match="kv_cache: every implementation caches keys and values in BF16"):
+        engine.LoadOptions().kv_cache("float16").parse(ck)
+    with pytest.raises(NotImplementedError, match="layers: every implementation loads whole"):
+        engine.LoadOptions().layers(range(0, 4)).parse(ck)
+    with pytest.raises(ValueError):
+        engine.LoadOptions().layers(range(0, 4, 2))
+    with pytest.raises(ValueError, match="a quantization is fp8_per_tensor or fp8_per_channel"):
+        engine.LoadOptions().quantization("int4")
+    with pytest.raises(NotImplementedError, match="takes no adapter"):
+        engine.LoadOptions().adapters().parse(ck)
+    with pytest.raises(NotImplementedError, match="chips: a load runs on 1, 2, 4 or 8 chips"):
+        engine.LoadOptions().chips(3).parse(ck)
+    assert engine.LoadOptions().chips(8).select(ck)["chips"] == 8
+    with pytest.raises(ValueError, match="unknown architecture"):
+        engine.LoadOptions().architecture("NoSuchForCausalLM")
+    with pytest.raises(NotImplementedError, match="no model type is implemented"):
+        engine.LoadOptions().architecture("BloomForCausalLM")
+    assert engine.LoadOptions().architecture("Qwen3ForCausalLM").batch_invariant().select(ck)["class"] == "qwen3.ForCausalLM"
+
+
+def test_qwen3_refusals(tmp_path):
+    base = synthetic.hf_config(configs.get("qwen3-1.7b"))
+    with pytest.raises(NotImplementedError, match="use_sliding_window: Qwen3 attends the whole history"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, dict(base, use_sliding_window=True)))
+    with pytest.raises(NotImplementedError, match="attention_bias"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, dict(base, attention_bias=True)))
+    with pytest.raises(NotImplementedError, match="rope_scaling"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, dict(base, rope_scaling={"rope_type": "dynamic", "factor": 2.0})))
+
+
+def test_classes_of_the_family(tmp_path):
+    base = synthetic.hf_config(configs.get("qwen3-0.6b"))
+    for arch, cls in [("Qwen3ForSequenceClassification", "qwen3.ForSequenceClassification"),
+                      ("Qwen3Model", "qwen3.Model")]:
+        assert engine.LoadOptions().select(_ckpt(tmp_path, dict(base, architectures=[arch])))["class"] == cls
