@@ -48,9 +48,9 @@ def parse() -> argparse.Namespace:
 
 def reference_arm(args) -> None:
     reason = (
-        "the reference (furiosa-ai/furiosa-opt-models) targets FuriosaAI RNGD NPUs only: its kernels "
-        "are Rust for the furiosa-opt VISA SDK (cargo-furiosa-opt, nightly-2026-05-01) and it has no "
-        "CUDA/NCCL path, so it neither installs nor runs on a B200"
+        "the reference (furiosa-ai/furiosa-opt-models) does not install here: its root is a uv "
+        "workspace with no build backend and its engine wheel needs maturin, nightly Rust and "
+        "cargo-furiosa-opt to build Rust/VISA kernels for FuriosaAI RNGD NPUs; it has no CUDA path"
     )
     rank = int(os.environ.get("RANK", "0"))
     if rank == 0:
