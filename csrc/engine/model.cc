@@ -351,7 +351,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
     pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
   std::memcpy(pinned_stage_[slot].data(), host_stage_.data(), plan.staged.bytes);
 
-  const int64_t splits_needed = plan.decode > 0 ? (plan.max_keys + 511) / 512 : 1;
+  const int64_t splits_needed = plan.decode > 0 ? (plan.max_keys + 2047) / 2048 : 1;
   const int64_t splits = next_pow2(splits_needed);
   ensure_workspace(plan.rows_padded, std::max<int64_t>(plan.kept_padded, 1), splits,
                    plan.segments_padded);
@@ -363,7 +363,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
                                  cudaMemcpyHostToDevice, st->stream),
                  "stage operands");
   st->check_cuda(cudaEventRecord(stage_done_[slot], st->stream), "staging event");
-  plan.max_keys = splits * 512;  // the decode grid covers the bucket's splits
+  plan.max_keys = splits * 2048;  // the decode grid covers the bucket's splits
   if (coll_) coll_->begin_call(st->stream);
 
   if (graphable) {
@@ -462,7 +462,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     g.workspace = static_cast<float*>(ws_gemm_.data());
     g.workspace_bytes = ws_gemm_.size();
     g.counters = i32(ws_counters_);
-    g.counters_len = static_cast<int>(ws_counters_.size() / 4);
+    g.counters_len = 32768;  // the first half; the second serves the attention merge
     g.status = st->status;
     if (batch_invariant_) {
       g.mode = foa::kModeRows;
@@ -523,7 +523,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     if (plan.decode > 0) {
       attn.num_segments = static_cast<int>(plan.prefill > 0 ? plan.decode : plan.segments_padded);
       fail(foa::paged_decode(attn, s), "decode attention");
-      if (plan.max_keys > 512) ++kernels;  // the split merge
+      if (plan.max_keys > attn.keys_per_split) ++kernels;  // the split merge
     }
     if (plan.prefill > 0) {
       attn.num_segments = static_cast<int>(plan.decode + plan.prefill);

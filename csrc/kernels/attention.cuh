@@ -33,7 +33,7 @@ struct PagedAttention {
   float* partial_lse = nullptr;
   size_t partial_capacity = 0;  // elements of partial_lse (partial_o holds head_dim times more)
   int max_keys = 0;             // longest history of any segment (bounds the split count)
-  int keys_per_split = 512;     // fixed split width: each row's tiling depends on its own length
+  int keys_per_split = 2048;    // fixed split width: each row's tiling depends on its own length
   int* status = nullptr;
 };
 

@@ -167,10 +167,11 @@ void bind_ops(py::module_& m) {
         [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
                     int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
                     uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
-                    int keys_per_split, uint64_t status, uint64_t stream) {
+                    int keys_per_split, uint64_t status, uint64_t stream, uint64_t counters) {
           auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
                              head_dim, scale, partial_o, partial_lse, capacity, max_keys,
                              keys_per_split, status);
+          (void)counters;
           py::gil_scoped_release nogil;
           check(foa::paged_decode(a, as_stream(stream)), "paged_decode");
         });

@@ -118,8 +118,10 @@ def _attn_common(segments: torch.Tensor) -> None:
         raise ValueError("segments are int32 [n, 5]: row_start, len, cached, table_start, nblocks")
 
 
-def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys_per_split=512, out=None):
-    """Flash-decoding of one-row segments over the paged cache. q: [rows, q_heads, d]."""
+def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys_per_split=2048, out=None,
+                 counters=None):
+    """Flash-decoding of one-row segments over the paged cache. q: [rows, q_heads, d]. With
+    `counters` (int32, zero, one per segment and key/value head) the splits merge in the kernel."""
     _attn_common(segments)
     rows, q_heads, d = q.shape
     out = torch.empty_like(q) if out is None else out
@@ -132,7 +134,8 @@ def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys
     native().ops.paged_decode(
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(), n,
         q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5), po.data_ptr(),
-        pl.data_ptr(), need, int(max_keys), keys_per_split, s.status.data_ptr(), _stream())
+        pl.data_ptr(), need, int(max_keys), keys_per_split, s.status.data_ptr(), _stream(),
+        0 if counters is None else counters.data_ptr())
     return out
 
 
