@@ -24,10 +24,13 @@
 // as the reference's contractions round once (ops/pointwise/add.rs:1).
 
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cuda_fp8.h>
 
 #include <algorithm>
 #include <cstdio>
 #include <cstdlib>
+#include <cstring>
 #include <mutex>
 
 #include "gemm.cuh"
@@ -57,18 +60,65 @@ struct KParams {
   int out_rows, out_cols;     // logical output shape
   unsigned long long* trace;  // milestone timestamps of CTA 0, or null
   int debug;                  // measurement switches (FOA_GEMM_DEBUG): 1 no stores, 2 no TMEM loads
+  // Quantized weights (kWF != 0): block scales and the factor the FP32 sums take.
+  const void* wscale;         // FP8: FP32 [ceil(N/128)][ceil(K/128)]; NVFP4: E4M3 [N][K/16]
+  long wscale_ld;             // scale elements per scale row
+  float acc_scale;            // NVFP4 tensor scale (1 otherwise), applied to the reduced sum
 };
+
+// Weight formats a GEMM reads.
+enum : int { kWBf16 = 0, kWFp8Block = 1, kWNvfp4 = 2 };
+
+// Eight E4M3 codes times their block scale, rounded to BF16.
+__device__ __forceinline__ uint4 dequant_fp8x8(uint2 v, float scale) {
+  uint32_t w[4];
+  const uint32_t in[2] = {v.x, v.y};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>(in[i >> 1] >> (16 * (i & 1)));
+    const __half2_raw h = __nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3);
+    const float2 f = __half22float2(__half2(h));
+    w[i] = pack_bf16x2(f.x * scale, f.y * scale);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+// BF16 bits of an E2M1 code: +-{0, 0.5, 1, 1.5, 2, 3, 4, 6}.
+__device__ __forceinline__ uint32_t e2m1_bf16_bits(uint32_t code) {
+  const uint32_t c = code & 7u;
+  const uint32_t mag = c == 0 ? 0u : c == 1 ? 0x3F00u : (((126u + (c >> 1)) << 7) | ((c & 1u) << 6));
+  return mag | ((code & 8u) << 12);
+}
+
+// Eight E2M1 codes (low nibble first) times their E4M3 scale: exact in BF16.
+__device__ __forceinline__ uint4 dequant_e2m1x8(uint32_t v, uint8_t scale_byte) {
+  const __half_raw hs = __nv_cvt_fp8_to_halfraw(scale_byte, __NV_E4M3);
+  const float s = __half2float(__half(hs));
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = __uint_as_float(e2m1_bf16_bits(v >> (8 * i)) << 16) * s;
+    const float hi = __uint_as_float(e2m1_bf16_bits(v >> (8 * i + 4)) << 16) * s;
+    w[i] = pack_bf16x2(lo, hi);
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
 
 __device__ __forceinline__ void mark(const KParams& p, int i) {
   if (p.trace != nullptr && blockIdx.x == 0) p.trace[i] = global_ns();
 }
 
-template <int kMB, int kBN, int kStages, int kAcc>
+template <int kMB, int kBN, int kStages, int kAcc, int kWF = kWBf16>
 struct Cfg {
   static constexpr int kPRows = 128 * kMB;
   static constexpr int kPBytes = kPRows * 128;
   static constexpr int kQBytes = kBN * 128;
   static constexpr int kStageBytes = kPBytes + kQBytes;
+  // Quantized weights land raw in a side ring first (rows of one k-block: 64 FP8 bytes or 32
+  // packed NVFP4 bytes), sized for the larger of the two operand tiles.
+  static constexpr int kWRows = kPRows > kBN ? kPRows : kBN;
+  static constexpr int kRawRow = kWF == kWFp8Block ? 64 : kWF == kWNvfp4 ? 32 : 0;
+  static constexpr int kRawBytes = kWRows * kRawRow;
   static constexpr int kAccCols = kMB * kBN;
   static constexpr int kColsRaw = kAcc * kAccCols;
   static constexpr int kTmemCols = kColsRaw <= 32    ? 32
@@ -76,8 +126,9 @@ struct Cfg {
                                    : kColsRaw <= 128 ? 128
                                    : kColsRaw <= 256 ? 256
                                                      : 512;
-  static constexpr int kBarrierBytes = 256;
-  static constexpr int kSmemBytes = kStages * kStageBytes + kBarrierBytes + 1024;
+  static constexpr int kBarrierBytes = 512;
+  static constexpr int kSmemBytes = kStages * (kStageBytes + kRawBytes) + kBarrierBytes + 1024;
+  static constexpr int kThreadsCta = kWF == kWBf16 ? 192 : 320;
   static_assert(kColsRaw <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 232448, "stages exceed shared memory");
   static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "invalid MMA N");
@@ -176,17 +227,20 @@ __device__ __forceinline__ void store_one(const KParams& p, int row, int col, fl
   static_cast<__nv_bfloat16*>(p.c)[(long)row * p.ldc + col] = __float2bfloat16_rn(v);
 }
 
-template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed, int kWF = kWBf16>
+__global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCta), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP,
-                     const __grid_constant__ CUtensorMap tmQ, const KParams p) {
-  using C = Cfg<kMB, kBN, kStages, kAcc>;
+                     const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmW, const KParams p) {
+  using C = Cfg<kMB, kBN, kStages, kAcc, kWF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * C::kStageBytes);
+  uint8_t* raw = smem + kStages * C::kStageBytes;  // quantized weight ring (kWF != 0)
+  uint64_t* full = reinterpret_cast<uint64_t*>(raw + kStages * C::kRawBytes);
   uint64_t* empty = full + kStages;
-  uint64_t* tfull = empty + kStages;
+  uint64_t* rawfull = empty + kStages;
+  uint64_t* tfull = rawfull + kStages;
   uint64_t* tempty = tfull + kAcc;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kAcc);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -199,8 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(full + s, 1);
+      // A stage is full when its TMA bytes land and, for quantized weights, the four converter
+      // warps have written the weight tile.
+      mbar_init(full + s, kWF == kWBf16 ? 1 : 5);
       mbar_init(empty + s, 1);
+      mbar_init(rawfull + s, 1);
     }
     for (int b = 0; b < kAcc; ++b) {
       mbar_init(tfull + b, 1);
@@ -212,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
+    if (kWF != kWBf16) tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -228,6 +286,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       uint32_t it = 0;
       bool ok = true;
+      // Weight tile of stage s: straight into the stage (BF16), or raw into the side ring for the
+      // converter warps (quantized formats).
+      auto load_w = [&](int s, int kb, int tp, int tq) {
+        uint8_t* st = smem + s * C::kStageBytes;
+        if constexpr (kWF == kWBf16) {
+          if (p.swap)
+            tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
+          else
+            tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+        } else {
+          const int rows = p.swap ? C::kPRows : kBN;
+          mbar_arrive_expect_tx(rawfull + s, rows * C::kRawRow);
+          tma_load_2d(raw + s * C::kRawBytes, &tmW, rawfull + s, kb * C::kRawRow,
+                      p.swap ? tp * C::kPRows : tq * kBN);
+        }
+      };
+      auto load_a = [&](int s, int kb, int tp, int tq) {
+        uint8_t* st = smem + s * C::kStageBytes;
+        if (p.swap)
+          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+        else
+          tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
+      };
+      const uint32_t full_bytes =
+          kWF == kWBf16 ? C::kStageBytes : (p.swap ? C::kQBytes : C::kPBytes);
       // The first stages' weight tiles do not depend on earlier kernels: issue them before
       // waiting for the previous kernel (PDL), then their activation tiles after it.
       int pre = 0;
@@ -238,22 +321,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
         pre = min(kStages, kb1 - kb0);
         for (int i = 0; i < pre; ++i) {
-          uint8_t* st = smem + i * C::kStageBytes;
-          mbar_arrive_expect_tx(full + i, C::kStageBytes);
-          if (p.swap)
-            tma_load_2d(st, &tmP, full + i, (kb0 + i) * kBlockK, tp * C::kPRows);
-          else
-            tma_load_2d(st + C::kPBytes, &tmQ, full + i, (kb0 + i) * kBlockK, tq * kBN);
+          mbar_arrive_expect_tx(full + i, full_bytes);
+          load_w(i, kb0 + i, tp, tq);
         }
         pdl_wait();
         mark(p, 2);
-        for (int i = 0; i < pre; ++i) {
-          uint8_t* st = smem + i * C::kStageBytes;
-          if (p.swap)
-            tma_load_2d(st + C::kPBytes, &tmQ, full + i, (kb0 + i) * kBlockK, tq * kBN);
-          else
-            tma_load_2d(st, &tmP, full + i, (kb0 + i) * kBlockK, tp * C::kPRows);
-        }
+        for (int i = 0; i < pre; ++i) load_a(i, kb0 + i, tp, tq);
       } else {
         pdl_wait();
       }
@@ -270,10 +343,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          uint8_t* st = smem + s * C::kStageBytes;
-          mbar_arrive_expect_tx(full + s, C::kStageBytes);
-          tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
-          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+          mbar_arrive_expect_tx(full + s, full_bytes);
+          load_w(s, kb, tp, tq);
+          load_a(s, kb, tp, tq);
           ++it;
         }
         if (u == (int)blockIdx.x) it += pre;
@@ -308,10 +380,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           if (it == 0) mark(p, 3);
-          if (false) {
-            ok = false;
-            break;
-          }
           tc_fence_after();
           const uint8_t* st = smem + s * C::kStageBytes;
 #pragma unroll
@@ -327,6 +395,58 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (ok) mma_commit(tfull + b);
         if (tc == 0) mark(p, 4);
+      }
+    }
+  } else if (kWF != kWBf16 && warp >= 6) {
+    // ----------------------------------------------------------------- weight converters (4 warps)
+    // Expand each raw weight tile into the BF16 128-byte-swizzled layout the MMA reads: FP8 codes
+    // times their 128x128 block scale (rounded once to BF16), or E2M1 codes times their E4M3
+    // 16-element scale (exact in BF16; the tensor scale multiplies the FP32 sums later).
+    const int ct = threadIdx.x - 192;
+    const int wrows_total = p.swap ? p.Mp : p.Nq;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      const int tile = u / p.splits, split = u % p.splits;
+      const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
+      const int kb0 = split * p.kb_per_split;
+      const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+      const int rows = p.swap ? C::kPRows : kBN;
+      const int wrow0 = p.swap ? tp * C::kPRows : tq * kBN;
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int s = it % kStages;
+        const uint32_t ph = (it / kStages) & 1;
+        int got = 1;
+        if (lane == 0) got = mbar_wait(rawfull + s, ph, p.status, kTimeoutTmaFull, abort);
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) {
+          ok = false;
+          break;
+        }
+        const uint8_t* src = raw + s * C::kRawBytes;
+        uint8_t* dst = smem + s * C::kStageBytes + (p.swap ? 0 : C::kPBytes);
+        for (int id = ct; id < rows * 8; id += 128) {
+          const int r = id >> 3, c = id & 7;
+          const int grow = wrow0 + r;
+          uint4 out = make_uint4(0, 0, 0, 0);
+          if (grow < wrows_total) {
+            if constexpr (kWF == kWFp8Block) {
+              const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+              const float sc =
+                  static_cast<const float*>(p.wscale)[(long)(grow >> 7) * p.wscale_ld + (kb >> 1)];
+              out = dequant_fp8x8(v, sc);
+            } else {
+              const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * 32 + c * 4);
+              const uint8_t sb =
+                  static_cast<const uint8_t*>(p.wscale)[(long)grow * p.wscale_ld + kb * 4 + (c >> 1)];
+              out = dequant_e2m1x8(v, sb);
+            }
+          }
+          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = out;
+        }
+        fence_proxy_async();  // the tile is read by the tensor cores (async proxy)
+        __syncwarp();
+        if (lane == 0) mbar_arrive(full + s);
       }
     }
   } else {
@@ -355,7 +475,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
         }
 #pragma unroll
-        for (int t = 0; t < 16; ++t) v[t] = __uint_as_float(r[t]);
+        for (int t = 0; t < 16; ++t)
+          v[t] = kWF == kWNvfp4 ? __uint_as_float(r[t]) * p.acc_scale : __uint_as_float(r[t]);
       };
       // Partials are stored column-major ([col][row]) so a warp's 32 rows are 128 contiguous bytes.
       const long tile_elems = (long)C::kPRows * kBN;
@@ -455,7 +576,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     cluster_sync();
     // 2. Push this split's partial into the shared memory of the CTA that reduces each row;
     //    DSMEM stores do not stall. Receive layout per CTA: [split][half][col][row of slice].
-    if (warp >= 2 && !*abort) {
+    if (warp >= 2 && warp < 6 && !*abort) {
       const int q = warp & 3;
       const int lrow = q * 32 + lane;
       const int S = p.splits;
@@ -485,14 +606,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
 #pragma unroll
           for (int t = 0; t < 16; ++t)
-            dsmem_st_f32(base + 4u * (uint32_t)((c0 + t) * rs), __uint_as_float(r[t]));
+            dsmem_st_f32(base + 4u * (uint32_t)((c0 + t) * rs),
+                         kWF == kWNvfp4 ? __uint_as_float(r[t]) * p.acc_scale : __uint_as_float(r[t]));
         }
       }
       tc_fence_before();
     }
     // 3. Every partial has landed; each CTA adds its slice in split order.
     cluster_sync();
-    if (warp >= 2) {
+    if (warp >= 2 && warp < 6) {
       const int tid = threadIdx.x - 64;
       const int S = p.splits;
       const int rank = (int)cluster_rank();
@@ -564,11 +686,23 @@ int pick_swap_bn(int m) {
 }
 
 // Shared-memory bytes of the operand ring of a swap-mapping configuration (see launch_swap).
-int swap_ring_bytes(int mb, int kbn) {
+// Pipeline shape of a (tile, weight format): as many stages as fit 220 KiB of shared memory (at
+// most 8), and double-buffered accumulators when two fit in TMEM.
+template <int kMB, int kBN, int kWF>
+struct Shape {
+  static constexpr int kStage = 128 * kMB * 128 + kBN * 128;
+  static constexpr int kRaw = (kMB * 128 > kBN ? kMB * 128 : kBN) * (kWF == 1 ? 64 : kWF == 2 ? 32 : 0);
+  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw);
+  static constexpr int kStages = kFit > 8 ? 8 : kFit;
+  static constexpr int kAcc = kMB * kBN * 2 <= 512 ? 2 : 1;
+};
+
+// Bytes of the operand ring of a swap-mapping configuration (the cluster reduction reuses it).
+int swap_ring_bytes(int mb, int kbn, int wf) {
   const int stage = 128 * mb * 128 + kbn * 128;
-  int stages = 0;
-  if (mb == 1) stages = kbn <= 32 ? 8 : kbn == 64 ? 8 : kbn == 128 ? 6 : 4;
-  else stages = kbn <= 32 ? 6 : kbn == 64 ? 5 : kbn == 128 ? 4 : 3;
+  const int raw = (mb * 128 > kbn ? mb * 128 : kbn) * (wf == 1 ? 64 : wf == 2 ? 32 : 0);
+  int stages = (220 * 1024 - 2048) / (stage + raw);
+  if (stages > 8) stages = 8;
   return stage * stages;
 }
 
@@ -603,7 +737,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   const size_t red_bytes = (size_t)128 * pl.mb * pl.kbn * sizeof(float);
   const size_t recv_bytes = (size_t)(128 * pl.mb + 2 * splits) * pl.kbn * sizeof(float);
   const bool cluster_fits =
-      pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn);
+      pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn, a.w_format);
   pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
   // FOA_GEMM_RED=global|cluster forces how splits meet (measurements only).
   static const char* force = std::getenv("FOA_GEMM_RED");
@@ -634,11 +768,12 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   return pl;
 }
 
-template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed>
-int launch(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, const Plan& pl,
-           cudaStream_t stream) {
-  using C = Cfg<kMB, kBN, kStages, kAcc>;
-  auto kernel = gemm_bf16_kernel<kMB, kBN, kStages, kAcc, kEpi, kRed>;
+template <int kMB, int kBN, int kEpi, int kRed, int kWF>
+int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw, const KParams& kp,
+           const Plan& pl, cudaStream_t stream) {
+  using S = Shape<kMB, kBN, kWF>;
+  using C = Cfg<kMB, kBN, S::kStages, S::kAcc, kWF>;
+  auto kernel = gemm_bf16_kernel<kMB, kBN, S::kStages, S::kAcc, kEpi, kRed, kWF>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -648,7 +783,7 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, cons
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(pl.grid);
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(C::kThreadsCta);
   cfg.dynamicSmemBytes = C::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -667,24 +802,25 @@ int launch(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, cons
   }
   cfg.attrs = attr;
   cfg.numAttrs = n;
-  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, tp, tq, kp);
+  const cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, tp, tq, tw, kp);
   return err == cudaSuccess ? 0 : -5;
 }
 
 // Clusters of `size` CTAs of this configuration that the device holds at once (cached).
-template <int kMB, int kBN, int kStages, int kAcc, int kEpi>
+template <int kMB, int kBN, int kEpi, int kWF>
 int max_active_clusters(int size) {
-  using C = Cfg<kMB, kBN, kStages, kAcc>;
+  using S = Shape<kMB, kBN, kWF>;
+  using C = Cfg<kMB, kBN, S::kStages, S::kAcc, kWF>;
   static int cache[64][9] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   int& slot = cache[dev & 63][size];
   if (slot == 0) {
-    auto kernel = gemm_bf16_kernel<kMB, kBN, kStages, kAcc, kEpi, kRedCluster>;
+    auto kernel = gemm_bf16_kernel<kMB, kBN, S::kStages, S::kAcc, kEpi, kRedCluster, kWF>;
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmemBytes);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(size * 64);
-    cfg.blockDim = dim3(kThreads);
+    cfg.blockDim = dim3(C::kThreadsCta);
     cfg.dynamicSmemBytes = C::kSmemBytes;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -703,66 +839,89 @@ int max_active_clusters(int size) {
   return slot;
 }
 
-template <int kMB, int kBN, int kStages, int kAcc, int kEpi>
-int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp, const Plan& pl,
-               cudaStream_t stream) {
+template <int kMB, int kBN, int kEpi, int kWF>
+int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+               const KParams& kp, const Plan& pl, cudaStream_t stream) {
   switch (pl.red) {
     case kRedNone:
-      return launch<kMB, kBN, kStages, kAcc, kEpi, kRedNone>(tp, tq, kp, pl, stream);
+      return launch<kMB, kBN, kEpi, kRedNone, kWF>(tp, tq, tw, kp, pl, stream);
     case kRedGlobal:
-      return launch<kMB, kBN, kStages, kAcc, kEpi, kRedGlobal>(tp, tq, kp, pl, stream);
+      return launch<kMB, kBN, kEpi, kRedGlobal, kWF>(tp, tq, tw, kp, pl, stream);
     default:
       if constexpr (kMB * kBN * 128 * 4 <= 232448 - 2048)
-        return launch<kMB, kBN, kStages, kAcc, kEpi, kRedCluster>(tp, tq, kp, pl, stream);
+        return launch<kMB, kBN, kEpi, kRedCluster, kWF>(tp, tq, tw, kp, pl, stream);
       return -2;
   }
 }
 
-template <int kMB, int kBN, int kStages, int kAcc>
-int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp,
-                     const Plan& pl, cudaStream_t stream) {
-  if (epi == kEpiBf16) return launch_red<kMB, kBN, kStages, kAcc, kEpiBf16>(tp, tq, kp, pl, stream);
-  if (epi == kEpiF32) return launch_red<kMB, kBN, kStages, kAcc, kEpiF32>(tp, tq, kp, pl, stream);
+template <int kMB, int kBN, int kWF>
+int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+                     const KParams& kp, const Plan& pl, cudaStream_t stream) {
+  if (epi == kEpiBf16) return launch_red<kMB, kBN, kEpiBf16, kWF>(tp, tq, tw, kp, pl, stream);
+  if (epi == kEpiF32) return launch_red<kMB, kBN, kEpiF32, kWF>(tp, tq, tw, kp, pl, stream);
   return -2;
 }
 
-int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const KParams& kp,
-                const Plan& pl, cudaStream_t stream) {
+template <int kWF>
+int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+                const KParams& kp, const Plan& pl, cudaStream_t stream) {
   if (pl.mb == 2) {
     if (epi != kEpiSwiGLU) return -2;
     switch (pl.kbn) {
-      case 16: return launch_red<2, 16, 6, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
-      case 32: return launch_red<2, 32, 6, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
-      case 64: return launch_red<2, 64, 5, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
-      case 128: return launch_red<2, 128, 4, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
-      default: return launch_red<2, 256, 3, 1, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+      case 16: return launch_red<2, 16, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
+      case 32: return launch_red<2, 32, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
+      case 64: return launch_red<2, 64, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
+      case 128: return launch_red<2, 128, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
+      default: return launch_red<2, 256, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
     }
   }
   switch (pl.kbn) {
-    case 16: return launch_plain_epi<1, 16, 8, 2>(epi, tp, tq, kp, pl, stream);
-    case 32: return launch_plain_epi<1, 32, 8, 2>(epi, tp, tq, kp, pl, stream);
-    case 64: return launch_plain_epi<1, 64, 8, 2>(epi, tp, tq, kp, pl, stream);
-    case 128: return launch_plain_epi<1, 128, 6, 2>(epi, tp, tq, kp, pl, stream);
-    default: return launch_plain_epi<1, 256, 4, 2>(epi, tp, tq, kp, pl, stream);
+    case 16: return launch_plain_epi<1, 16, kWF>(epi, tp, tq, tw, kp, pl, stream);
+    case 32: return launch_plain_epi<1, 32, kWF>(epi, tp, tq, tw, kp, pl, stream);
+    case 64: return launch_plain_epi<1, 64, kWF>(epi, tp, tq, tw, kp, pl, stream);
+    case 128: return launch_plain_epi<1, 128, kWF>(epi, tp, tq, tw, kp, pl, stream);
+    default: return launch_plain_epi<1, 256, kWF>(epi, tp, tq, tw, kp, pl, stream);
   }
 }
 
-int cluster_limit_of(int mb, int kbn, int epi, int size) {
+template <int kWF>
+int launch_rows(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+                const KParams& kp, const Plan& pl, cudaStream_t stream) {
+  switch (epi) {
+    case kEpiBf16: return launch_red<1, 256, kEpiBf16, kWF>(tp, tq, tw, kp, pl, stream);
+    case kEpiF32: return launch_red<1, 256, kEpiF32, kWF>(tp, tq, tw, kp, pl, stream);
+    case kEpiSwiGLU: return launch_red<1, 256, kEpiSwiGLU, kWF>(tp, tq, tw, kp, pl, stream);
+  }
+  return -2;
+}
+
+template <int kWF>
+int cluster_limit_wf(int mb, int kbn, int epi, int size) {
   if (mb == 2) {
     switch (kbn) {
-      case 16: return max_active_clusters<2, 16, 6, 2, kEpiSwiGLU>(size);
-      case 32: return max_active_clusters<2, 32, 6, 2, kEpiSwiGLU>(size);
-      case 64: return max_active_clusters<2, 64, 5, 2, kEpiSwiGLU>(size);
-      default: return max_active_clusters<2, 128, 4, 2, kEpiSwiGLU>(size);
+      case 16: return max_active_clusters<2, 16, kEpiSwiGLU, kWF>(size);
+      case 32: return max_active_clusters<2, 32, kEpiSwiGLU, kWF>(size);
+      case 64: return max_active_clusters<2, 64, kEpiSwiGLU, kWF>(size);
+      default: return max_active_clusters<2, 128, kEpiSwiGLU, kWF>(size);
     }
   }
   const bool f32 = epi == kEpiF32;
   switch (kbn) {
-    case 16: return f32 ? max_active_clusters<1, 16, 8, 2, kEpiF32>(size) : max_active_clusters<1, 16, 8, 2, kEpiBf16>(size);
-    case 32: return f32 ? max_active_clusters<1, 32, 8, 2, kEpiF32>(size) : max_active_clusters<1, 32, 8, 2, kEpiBf16>(size);
-    case 64: return f32 ? max_active_clusters<1, 64, 8, 2, kEpiF32>(size) : max_active_clusters<1, 64, 8, 2, kEpiBf16>(size);
-    case 128: return f32 ? max_active_clusters<1, 128, 6, 2, kEpiF32>(size) : max_active_clusters<1, 128, 6, 2, kEpiBf16>(size);
-    default: return f32 ? max_active_clusters<1, 256, 4, 2, kEpiF32>(size) : max_active_clusters<1, 256, 4, 2, kEpiBf16>(size);
+    case 16: return f32 ? max_active_clusters<1, 16, kEpiF32, kWF>(size) : max_active_clusters<1, 16, kEpiBf16, kWF>(size);
+    case 32: return f32 ? max_active_clusters<1, 32, kEpiF32, kWF>(size) : max_active_clusters<1, 32, kEpiBf16, kWF>(size);
+    case 64: return f32 ? max_active_clusters<1, 64, kEpiF32, kWF>(size) : max_active_clusters<1, 64, kEpiBf16, kWF>(size);
+    case 128: return f32 ? max_active_clusters<1, 128, kEpiF32, kWF>(size) : max_active_clusters<1, 128, kEpiBf16, kWF>(size);
+    default: return f32 ? max_active_clusters<1, 256, kEpiF32, kWF>(size) : max_active_clusters<1, 256, kEpiBf16, kWF>(size);
+  }
+}
+
+int g_cluster_wf = 0;  // weight format of the plan being made (read by cluster_limit_of)
+
+int cluster_limit_of(int mb, int kbn, int epi, int size) {
+  switch (g_cluster_wf) {
+    case kWFp8Block: return cluster_limit_wf<kWFp8Block>(mb, kbn, epi, size);
+    case kWNvfp4: return cluster_limit_wf<kWNvfp4>(mb, kbn, epi, size);
+    default: return cluster_limit_wf<kWBf16>(mb, kbn, epi, size);
   }
 }
 
@@ -785,8 +944,11 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.epilogue != kEpiF32 && (a.ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
   if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
   if (a.residual != nullptr && a.epilogue != kEpiBf16) return -2;
+  if (a.w_format != kWBf16 && a.w_scale == nullptr) return -2;
+  if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
 
   const int sms = a.num_sms > 0 ? a.num_sms : device_sms();
+  g_cluster_wf = a.w_format;
   const Plan pl = make_plan(a, sms, a.workspace ? a.workspace_bytes : 0,
                             a.counters ? a.counters_len : 0);
 
@@ -810,28 +972,48 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.debug = debug;
   kp.out_rows = a.M;
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
+  kp.wscale = a.w_scale;
+  kp.wscale_ld = a.w_scale_ld;
+  kp.acc_scale = a.w_format == kWNvfp4 ? a.w_tensor_scale : 1.0f;
   if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
 
-  CUtensorMap tp, tq;
+  CUtensorMap tp, tq, tw;
+  std::memset(&tw, 0, sizeof(tw));
   const int prow_box = 128 * pl.mb;
+  const int wrows_box = pl.swap ? prow_box : pl.kbn;
+  if (a.w_format != kWBf16) {
+    // Raw quantized rows: K bytes (FP8) or K/2 bytes (NVFP4) a row, one k-block per box.
+    const long row_bytes = a.w_format == kWFp8Block ? a.K : a.K / 2;
+    const long ld_bytes = a.w_format == kWFp8Block ? a.ldw : a.ldw / 2;
+    const int box_bytes = a.w_format == kWFp8Block ? 64 : 32;
+    if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, row_bytes, ld_bytes,
+                        wrows_box, box_bytes, CU_TENSOR_MAP_SWIZZLE_NONE))
+      return -4;
+  }
+  const bool quant = a.w_format != kWBf16;
   if (!pl.swap) {
     kp.Mp = a.M;
     kp.Nq = a.N;
     if (!encode_tmap_bf16_kmajor(&tp, a.a, a.M, a.K, a.lda, prow_box)) return -4;
-    if (!encode_tmap_bf16_kmajor(&tq, a.w, a.N, a.K, a.ldw, pl.kbn)) return -4;
+    if (quant) tq = tw;  // unused by the quantized producer
+    else if (!encode_tmap_bf16_kmajor(&tq, a.w, a.N, a.K, a.ldw, pl.kbn)) return -4;
     if (pl.red == 2) return -2;
-    switch (a.epilogue) {
-      case kEpiBf16: return launch_red<1, 256, 4, 2, kEpiBf16>(tp, tq, kp, pl, stream);
-      case kEpiF32: return launch_red<1, 256, 4, 2, kEpiF32>(tp, tq, kp, pl, stream);
-      case kEpiSwiGLU: return launch_red<1, 256, 4, 2, kEpiSwiGLU>(tp, tq, kp, pl, stream);
+    switch (a.w_format) {
+      case kWFp8Block: return launch_rows<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
+      case kWNvfp4: return launch_rows<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
+      default: return launch_rows<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
     }
-    return -2;
   }
   kp.Mp = a.N;
   kp.Nq = a.M;
-  if (!encode_tmap_bf16_kmajor(&tp, a.w, a.N, a.K, a.ldw, prow_box)) return -4;
+  if (quant) tp = tw;
+  else if (!encode_tmap_bf16_kmajor(&tp, a.w, a.N, a.K, a.ldw, prow_box)) return -4;
   if (!encode_tmap_bf16_kmajor(&tq, a.a, a.M, a.K, a.lda, pl.kbn)) return -4;
-  return launch_swap(a.epilogue, tp, tq, kp, pl, stream);
+  switch (a.w_format) {
+    case kWFp8Block: return launch_swap<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
+    case kWNvfp4: return launch_swap<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
+    default: return launch_swap<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
+  }
 }
 
 }  // namespace foa

@@ -45,7 +45,21 @@ struct GemmArgs {
   // loads issued, first stage landed, last MMA issued, accumulator seen, epilogue done, exit).
   unsigned long long* trace = nullptr;
   int num_sms = 0;        // 0: query the device
+  // Quantized weights (W8A16 / W4A16): `w` then holds raw codes and the kernel dequantizes each
+  // k-block into BF16 in shared memory before the MMAs read it.
+  //   kWeightFp8Block: E4M3 codes [N, K] (ldw bytes a row), w_scale FP32 [ceil(N/128), w_scale_ld]
+  //                    with one scale per 128x128 block (K % 64 == 0).
+  //   kWeightNvfp4:    E2M1 codes [N, K/2 bytes] (ldw counts elements, two a byte, lower column in
+  //                    the low nibble), w_scale E4M3 [N, w_scale_ld] one per 16 columns,
+  //                    w_tensor_scale the FP32 factor of the whole tensor ("weight_scale_2")
+  //                    that multiplies the FP32 sums (K % 64 == 0).
+  int w_format = 0;
+  const void* w_scale = nullptr;
+  long w_scale_ld = 0;
+  float w_tensor_scale = 1.0f;
 };
+
+enum GemmWeightFormat : int { kWeightBf16 = 0, kWeightFp8Block = 1, kWeightNvfp4 = 2 };
 
 // Plans and launches one GEMM on `stream`. Returns 0, or a negative code for a rejected argument
 // (no launch happens then): -1 misaligned pointer/stride, -2 bad shape, -3 scratch too small,

@@ -256,8 +256,7 @@ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
 }
 
 __global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64_t seed) {
-  pdl_wait();
-  pdl_trigger();
+  pdl_wait();  // weight producers: no early trigger, since GEMMs load weights before waiting
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const uint64_t r = mix64(seed * 0x100000001B3ull + (uint64_t)i);
     // Box-Muller on two 24-bit uniforms in (0, 1].
@@ -271,8 +270,7 @@ __global__ void init_normal_kernel(__nv_bfloat16* dst, long n, float std, uint64
 __global__ void init_normal_rows_kernel(__nv_bfloat16* dst, int rows, int cols,
                                         const int32_t* full_row, const uint32_t* tag,
                                         long full_cols, long col_offset, float std, uint64_t seed) {
-  pdl_wait();
-  pdl_trigger();
+  pdl_wait();  // weight producers: no early trigger, since GEMMs load weights before waiting
   const long n = (long)rows * cols;
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
     const int r = (int)(i / cols), c = (int)(i % cols);
@@ -285,8 +283,7 @@ __global__ void init_normal_rows_kernel(__nv_bfloat16* dst, int rows, int cols,
 }
 
 __global__ void fill_bf16_kernel(__nv_bfloat16* dst, long n, float v) {
-  pdl_wait();
-  pdl_trigger();
+  pdl_wait();  // weight producers: no early trigger, since GEMMs load weights before waiting
   const __nv_bfloat16 b = __float2bfloat16_rn(v);
   for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
     dst[i] = b;

@@ -1,0 +1,129 @@
+// Quantizers of the FP8 block-scaled and NVFP4 weight formats (the reference's forms:
+// crates/furiosa-opt-models/src/tensor/form/{fp8,nvfp4}.rs; NVFP4 rounding as vLLM's reference
+// quantizer rounds).
+#include <cuda_fp8.h>
+
+#include <algorithm>
+
+#include "launch.cuh"
+#include "quant.cuh"
+#include "sm100.cuh"
+
+namespace foa {
+namespace {
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float m = 0.f;
+  for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = fmaxf(m, red[w]);
+  __syncthreads();
+  return m;
+}
+
+// One CTA of 256 threads per 128x128 block.
+__global__ void __launch_bounds__(256) fp8_block_kernel(const __nv_bfloat16* w, int rows, int cols,
+                                                        uint8_t* codes, float* scales) {
+  pdl_wait();  // no early trigger: a dependent GEMM reads these codes before its own wait
+  __shared__ float red[8];
+  const int br = blockIdx.y, bc = blockIdx.x;
+  const int r0 = br * 128, c0 = bc * 128;
+  float m = 0.f;
+  for (int i = threadIdx.x; i < 128 * 128; i += 256) {
+    const int r = r0 + i / 128, c = c0 + i % 128;
+    if (r < rows && c < cols) m = fmaxf(m, fabsf(__bfloat162float(w[(long)r * cols + c])));
+  }
+  const float amax = block_max(m, red);
+  const float scale = fmaxf(amax, 1e-10f) / 448.f;
+  if (threadIdx.x == 0) scales[(long)br * gridDim.x + bc] = scale;
+  const float inv = 1.f / scale;
+  for (int i = threadIdx.x; i < 128 * 128; i += 256) {
+    const int r = r0 + i / 128, c = c0 + i % 128;
+    if (r < rows && c < cols)
+      codes[(long)r * cols + c] =
+          __nv_cvt_float_to_fp8(__bfloat162float(w[(long)r * cols + c]) * inv, __NV_SATFINITE, __NV_E4M3);
+  }
+}
+
+__global__ void absmax_kernel(const __nv_bfloat16* x, long n, float* out) {
+  pdl_wait();  // no early trigger: a dependent GEMM reads these codes before its own wait
+  float m = 0.f;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
+    m = fmaxf(m, fabsf(__bfloat162float(x[i])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  // Non-negative floats order as their bit patterns.
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int*>(out), __float_as_int(m));
+}
+
+// E2M1 code of |x| (x >= 0) rounded to nearest, ties to the even code.
+__device__ __forceinline__ uint32_t e2m1_magnitude(float m) {
+  return m <= 0.25f ? 0u : m < 0.75f ? 1u : m <= 1.25f ? 2u : m < 1.75f ? 3u
+       : m <= 2.5f ? 4u : m < 3.5f ? 5u : m <= 5.f ? 6u : 7u;
+}
+
+// One thread per 16-element group.
+__global__ void nvfp4_kernel(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes,
+                             uint8_t* scales, const float* amax_p, float* tensor_scale) {
+  pdl_wait();  // no early trigger: a dependent GEMM reads these codes before its own wait
+  const int groups = cols / 16;
+  const long g = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  const float amax = *amax_p;
+  const float global = amax > 0.f ? 448.f * 6.f / amax : 1.f;
+  if (g == 0 && tensor_scale != nullptr) *tensor_scale = 1.f / global;
+  if (g >= (long)rows * groups) return;
+  const long r = g / groups, c0 = (g % groups) * 16;
+  float v[16], m = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    v[i] = __bfloat162float(w[r * cols + c0 + i]);
+    m = fmaxf(m, fabsf(v[i]));
+  }
+  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(m / 6.f * global, __NV_SATFINITE, __NV_E4M3);
+  scales[r * groups + c0 / 16] = s8;
+  const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
+  const float s = __half2float(__half(hr));
+  const float k = s > 0.f ? global / s : 0.f;
+  uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x = v[i] * k;
+    const uint32_t code = e2m1_magnitude(fabsf(x)) | (x < 0.f ? 8u : 0u);
+    packed[i / 8] |= code << (4 * (i % 8));
+  }
+  uint2* dst = reinterpret_cast<uint2*>(codes + r * (cols / 2) + c0 / 2);
+  *dst = make_uint2(packed[0], packed[1]);
+}
+
+}  // namespace
+
+int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, float* scales,
+                       cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return 0;
+  dim3 grid((cols + 127) / 128, (rows + 127) / 128);
+  return launch_pdl(fp8_block_kernel, grid, dim3(256), 0, stream, w, rows, cols, codes, scales) ==
+                 cudaSuccess
+             ? 0
+             : -5;
+}
+
+int absmax_bf16(const __nv_bfloat16* x, long n, float* out, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  const int grid = (int)std::min<long>((n + 255) / 256, 148L * 8);
+  return launch_pdl(absmax_kernel, dim3(grid), dim3(256), 0, stream, x, n, out) == cudaSuccess ? 0 : -5;
+}
+
+int quantize_nvfp4(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, uint8_t* scales,
+                   const float* amax, float* tensor_scale, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return 0;
+  if (cols % 16 != 0) return -2;
+  const long groups = (long)rows * (cols / 16);
+  return launch_pdl(nvfp4_kernel, dim3((unsigned)((groups + 255) / 256)), dim3(256), 0, stream, w,
+                    rows, cols, codes, scales, amax, tensor_scale) == cudaSuccess
+             ? 0
+             : -5;
+}
+
+}  // namespace foa

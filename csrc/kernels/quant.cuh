@@ -1,0 +1,28 @@
+// Weight and activation quantizers of the FP8 and NVFP4 formats.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace foa {
+
+// Block-scaled FP8: W [rows, cols] BF16 -> E4M3 codes [rows, cols] and FP32 scales
+// [ceil(rows/128), ceil(cols/128)] with one scale per 128x128 block:
+// scale = max(amax(block), 1e-10) / 448, code = e4m3_rne(w / scale) saturated to +-448.
+int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, float* scales,
+                       cudaStream_t stream);
+
+// NVFP4 (E2M1 codes, E4M3 scale per 16 elements along cols, FP32 tensor scale):
+// global = 448 * 6 / amax(W) (the tensor's "weight_scale_2" is 1 / global);
+// block scale s = e4m3(amax(block) / 6 * global); code = e2m1_rne(w * global / s).
+// Codes pack two per byte, the lower column in the low nibble. `amax` is a device FP32 holding
+// amax(W) (absmax_bf16 computes it); `tensor_scale`, when not null, receives 1 / global.
+int quantize_nvfp4(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, uint8_t* scales,
+                   const float* amax, float* tensor_scale, cudaStream_t stream);
+
+// amax over n BF16 values into *out (out must start at 0).
+int absmax_bf16(const __nv_bfloat16* x, long n, float* out, cudaStream_t stream);
+
+}  // namespace foa

@@ -10,6 +10,7 @@
 #include "kernels/gemm.cuh"
 #include "kernels/ops.cuh"
 #include "kernels/attention.cuh"
+#include "kernels/quant.cuh"
 
 namespace py = pybind11;
 
@@ -32,8 +33,13 @@ void bind_ops(py::module_& m) {
       "gemm",
       [](uint64_t a, long lda, uint64_t w, long ldw, int M, int N, int K, uint64_t c, long ldc,
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
-         uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace) {
+         uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
+         int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale) {
         foa::GemmArgs g;
+        g.w_format = w_format;
+        g.w_scale = as_ptr<void>(w_scale);
+        g.w_scale_ld = w_scale_ld;
+        g.w_tensor_scale = w_tensor_scale;
         g.trace = reinterpret_cast<unsigned long long*>(trace);
         g.a = as_ptr<void>(a);
         g.lda = lda;
@@ -61,7 +67,41 @@ void bind_ops(py::module_& m) {
       py::arg("K"), py::arg("c"), py::arg("ldc"), py::arg("res"), py::arg("ldr"),
       py::arg("epilogue"), py::arg("mode"), py::arg("splits"), py::arg("ws"),
       py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
-      py::arg("stream"), py::arg("trace") = 0);
+      py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
+      py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f);
+
+  m.def(
+      "quantize_fp8_block",
+      [](uint64_t w, int rows, int cols, uint64_t codes, uint64_t scales, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::quantize_fp8_block(as_ptr<const __nv_bfloat16>(w), rows, cols,
+                                      as_ptr<uint8_t>(codes), as_ptr<float>(scales),
+                                      as_stream(stream)),
+              "quantize_fp8_block");
+      },
+      py::arg("w"), py::arg("rows"), py::arg("cols"), py::arg("codes"), py::arg("scales"),
+      py::arg("stream"));
+  m.def(
+      "absmax",
+      [](uint64_t x, long n, uint64_t out, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::absmax_bf16(as_ptr<const __nv_bfloat16>(x), n, as_ptr<float>(out),
+                               as_stream(stream)),
+              "absmax");
+      },
+      py::arg("x"), py::arg("n"), py::arg("out"), py::arg("stream"));
+  m.def(
+      "quantize_nvfp4",
+      [](uint64_t w, int rows, int cols, uint64_t codes, uint64_t scales, uint64_t amax,
+         uint64_t tensor_scale, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::quantize_nvfp4(as_ptr<const __nv_bfloat16>(w), rows, cols, as_ptr<uint8_t>(codes),
+                                  as_ptr<uint8_t>(scales), as_ptr<const float>(amax),
+                                  as_ptr<float>(tensor_scale), as_stream(stream)),
+              "quantize_nvfp4");
+      },
+      py::arg("w"), py::arg("rows"), py::arg("cols"), py::arg("codes"), py::arg("scales"),
+      py::arg("amax"), py::arg("tensor_scale"), py::arg("stream"));
 
   m.def(
       "gemm_scratch",

@@ -87,3 +87,83 @@ def paged_attention(q: torch.Tensor, cache: torch.Tensor, table, segments, scale
         s = s.masked_fill(~mask[None], float("-inf"))
         out[row_start : row_start + length] = torch.einsum("hlk,khd->lhd", torch.softmax(s, -1), v)
     return out
+
+
+# ------------------------------------------------------------------------------ quantized weights
+# FP8 block contract: E4M3 codes, one FP32 scale per 128 x 128 block, a group's scale its largest
+# magnitude over 448 and never below 1e-10 (crates/furiosa-opt-models/src/tensor/form/fp8.rs:1-12).
+# NVFP4: E2M1 codes, an E4M3 scale per 16 inputs, an FP32 tensor scale multiplying the reduced sum
+# ("Late", crates/furiosa-opt-models/src/tensor/form/nvfp4.rs:1-10).
+
+E4M3_MAX = 448.0
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+def _e4m3(x: torch.Tensor) -> torch.Tensor:
+    """E4M3 bytes of FP32 values, rounded to nearest even and saturated at +-448."""
+    return x.clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def _e4m3_value(b: torch.Tensor) -> torch.Tensor:
+    return b.view(torch.float8_e4m3fn).float()
+
+
+def fp8_block_quantize(w: torch.Tensor):
+    """BF16 [rows, cols] -> (E4M3 codes uint8 [rows, cols], FP32 scales [rows/128, cols/128])."""
+    rows, cols = w.shape
+    br, bc = (rows + 127) // 128, (cols + 127) // 128
+    wf = torch.zeros(br * 128, bc * 128, dtype=torch.float32, device=w.device)
+    wf[:rows, :cols] = w.float()
+    amax = wf.view(br, 128, bc, 128).abs().amax(dim=(1, 3))
+    # Tensor-by-tensor divisions: PyTorch divides by a Python scalar as a product with its
+    # reciprocal on CUDA, which is not the correctly rounded quotient the kernels compute.
+    scales = torch.clamp(amax, min=1e-10) / torch.full_like(amax, E4M3_MAX)
+    inv = (torch.ones_like(scales) / scales).repeat_interleave(128, 0).repeat_interleave(128, 1)[:rows, :cols]
+    return _e4m3(w.float() * inv), scales
+
+
+def fp8_block_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """Each coefficient ``code * block scale``, rounded once to BF16, as FP32."""
+    rows, cols = codes.shape
+    s = scales.repeat_interleave(128, 0).repeat_interleave(128, 1)[:rows, :cols]
+    return (_e4m3_value(codes) * s).bfloat16().float()
+
+
+def _e2m1_code(x: torch.Tensor) -> torch.Tensor:
+    """Nearest E2M1 code of each value, ties to the even code; the sign in bit 3."""
+    vals = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=x.device)
+    d = (x.abs()[..., None] - vals).abs()
+    tie = d == d.amin(-1, keepdim=True)
+    idx = torch.arange(8, device=x.device)
+    # Lowest index among the nearest, preferring an even one when two are equally near.
+    key = torch.where(tie, idx + 16 * (idx % 2), torch.full_like(idx, 1 << 10))
+    code = key.argmin(-1).to(torch.uint8)
+    return code | ((x < 0).to(torch.uint8) << 3)
+
+
+def nvfp4_quantize(w: torch.Tensor):
+    """BF16 [rows, cols] -> (packed codes uint8 [rows, cols/2], E4M3 scales uint8 [rows, cols/16],
+    FP32 tensor scale ``1 / global``), global = 448 * 6 / amax(W)."""
+    rows, cols = w.shape
+    wf = w.float()
+    amax = wf.abs().max()
+    glob = torch.full_like(amax, 448.0 * 6.0) / amax if amax > 0 else torch.ones_like(amax)
+    blocks = wf.view(rows, cols // 16, 16)
+    bmax = blocks.abs().amax(-1)
+    s8 = _e4m3((bmax / torch.full_like(bmax, 6.0)) * glob)
+    s = _e4m3_value(s8)
+    k = torch.where(s > 0, glob / s, torch.zeros_like(s))
+    codes = _e2m1_code(blocks * k[..., None]).view(rows, cols)
+    packed = codes[:, 0::2] | (codes[:, 1::2] << 4)
+    return packed, s8, float(torch.ones_like(glob) / glob)
+
+
+def nvfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """``code * block scale`` (exact in BF16) as FP32 [rows, cols]; the tensor scale is not applied."""
+    rows = packed.shape[0]
+    lo, hi = packed & 15, packed >> 4
+    codes = torch.stack([lo, hi], dim=-1).view(rows, -1).long()
+    vals = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=packed.device)
+    mag = vals[codes & 7]
+    v = torch.where((codes & 8) != 0, -mag, mag)
+    return v * _e4m3_value(scales).repeat_interleave(16, 1)

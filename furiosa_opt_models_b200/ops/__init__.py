@@ -13,6 +13,10 @@ from .kernels import (  # noqa: F401
     MODE_AUTO,
     MODE_ROWS,
     MODE_SWAP,
+    W_BF16,
+    W_FP8_BLOCK,
+    W_NVFP4,
+    QuantizedWeight,
     argmax,
     embedding,
     gemm,
@@ -21,4 +25,6 @@ from .kernels import (  # noqa: F401
     paged_decode,
     paged_prefill,
     prefill_work,
+    quantize_fp8_block,
+    quantize_nvfp4,
 )

@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+from dataclasses import dataclass
+
 import torch
 
 from .native import native, scratch
@@ -23,9 +25,62 @@ def _rowmajor(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be a 2-D tensor with unit column stride")
 
 
+W_BF16, W_FP8_BLOCK, W_NVFP4 = 0, 1, 2
+
+
+@dataclass
+class QuantizedWeight:
+    """A weight [rows, cols] held in a quantized format that the GEMM dequantizes on the fly.
+
+    fp8_block: ``codes`` E4M3 as uint8 [rows, cols], ``scales`` FP32 [ceil(rows/128), ceil(cols/128)]
+    (one per 128x128 block, the checkpoint's ``weight_scale_inv``).
+    nvfp4: ``codes`` uint8 [rows, cols/2] (two E2M1 codes a byte, lower column in the low nibble),
+    ``scales`` E4M3 as uint8 [rows, cols/16], ``tensor_scale`` the FP32 ``weight_scale_2``.
+    """
+
+    format: str
+    codes: torch.Tensor
+    scales: torch.Tensor
+    rows: int
+    cols: int
+    tensor_scale: float = 1.0
+
+    @property
+    def code(self) -> int:
+        return {"fp8_block": W_FP8_BLOCK, "nvfp4": W_NVFP4}[self.format]
+
+
+def quantize_fp8_block(w: torch.Tensor) -> QuantizedWeight:
+    """Block-scaled FP8 of a BF16 weight on the device (scale = max(amax, 1e-10) / 448)."""
+    _rowmajor(w, "w")
+    w = w.contiguous()
+    rows, cols = w.shape
+    codes = torch.empty(rows, cols, dtype=torch.uint8, device=w.device)
+    scales = torch.empty((rows + 127) // 128, (cols + 127) // 128, dtype=torch.float32, device=w.device)
+    native().ops.quantize_fp8_block(w.data_ptr(), rows, cols, codes.data_ptr(), scales.data_ptr(), _stream())
+    return QuantizedWeight("fp8_block", codes, scales, rows, cols)
+
+
+def quantize_nvfp4(w: torch.Tensor) -> QuantizedWeight:
+    """NVFP4 of a BF16 weight on the device (global = 448 * 6 / amax; 16-column E4M3 scales)."""
+    _rowmajor(w, "w")
+    w = w.contiguous()
+    rows, cols = w.shape
+    if cols % 16:
+        raise ValueError("NVFP4 needs columns in multiples of 16")
+    codes = torch.empty(rows, cols // 2, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(rows, cols // 16, dtype=torch.uint8, device=w.device)
+    amax = torch.zeros(2, dtype=torch.float32, device=w.device)
+    ops = native().ops
+    ops.absmax(w.data_ptr(), w.numel(), amax.data_ptr(), _stream())
+    ops.quantize_nvfp4(w.data_ptr(), rows, cols, codes.data_ptr(), scales.data_ptr(), amax.data_ptr(),
+                       amax.data_ptr() + 4, _stream())
+    return QuantizedWeight("nvfp4", codes, scales, rows, cols, float(amax[1].item()))
+
+
 def gemm(
     a: torch.Tensor,
-    w: torch.Tensor,
+    w: torch.Tensor | QuantizedWeight,
     epilogue: int = EPI_BF16,
     residual: torch.Tensor | None = None,
     out: torch.Tensor | None = None,
@@ -36,16 +91,31 @@ def gemm(
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
     EPI_BF16 returns BF16 [M, N] (plus ``residual`` before the one rounding), EPI_F32 FP32 [M, N],
-    EPI_SWIGLU BF16 [M, N/2] for gate/up weights interleaved in 128-row blocks.
+    EPI_SWIGLU BF16 [M, N/2] for gate/up weights interleaved in 128-row blocks. A
+    ``QuantizedWeight`` is dequantized to BF16 tile by tile inside the kernel (W8A16 / W4A16).
     """
     _rowmajor(a, "a")
-    _rowmajor(w, "w")
-    if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16:
-        raise ValueError("gemm takes BF16 operands")
     M, K = a.shape
-    N = w.shape[0]
-    if w.shape[1] != K:
-        raise ValueError("inner dimensions differ")
+    quant = isinstance(w, QuantizedWeight)
+    if quant:
+        _rowmajor(w.codes, "codes")
+        N = w.rows
+        if w.cols != K:
+            raise ValueError("inner dimensions differ")
+        w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (2 if w.format == "nvfp4" else 1)
+        qargs = dict(w_format=w.code, w_scale=w.scales.data_ptr(), w_scale_ld=w.scales.stride(0),
+                     w_tensor_scale=float(w.tensor_scale))
+    else:
+        _rowmajor(w, "w")
+        if w.dtype != torch.bfloat16:
+            raise ValueError("gemm takes BF16 operands")
+        N = w.shape[0]
+        if w.shape[1] != K:
+            raise ValueError("inner dimensions differ")
+        w_ptr, ldw = w.data_ptr(), w.stride(0)
+        qargs = {}
+    if a.dtype != torch.bfloat16:
+        raise ValueError("gemm takes BF16 activations")
     cols = N // 2 if epilogue == EPI_SWIGLU else N
     if out is None:
         dtype = torch.float32 if epilogue == EPI_F32 else torch.bfloat16
@@ -54,11 +124,11 @@ def gemm(
         _rowmajor(residual, "residual")
     s = scratch(a.device)
     native().ops.gemm(
-        a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), M, N, K,
+        a.data_ptr(), a.stride(0), w_ptr, ldw, M, N, K,
         out.data_ptr(), out.stride(0), _ptr(residual), 0 if residual is None else residual.stride(0),
         epilogue, mode, splits, s.workspace.data_ptr(), s.workspace.numel() * 4,
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
-        0 if trace is None else trace.data_ptr(),
+        0 if trace is None else trace.data_ptr(), **qargs,
     )
     return out
 

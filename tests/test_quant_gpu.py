@@ -1,0 +1,110 @@
+"""Quantized weights on the device: the FP8 block and NVFP4 quantizers bit for bit against the
+PyTorch restatement, and the tcgen05 GEMM with on-the-fly dequantization (W8A16 / W4A16) against
+an FP32 product with the dequantized weights."""
+
+import pytest
+import torch
+
+from furiosa_opt_models_b200.models import reference as R
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from furiosa_opt_models_b200 import ops
+
+    return ops
+
+
+def _close(out, ref, tol=2e-2):
+    err = (out.float() - ref).abs().max().item()
+    scale = ref.abs().max().item() + 1e-6
+    assert err <= tol * scale, f"max error {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("rows,cols", [(128, 128), (300, 520), (1024, 2048)])
+def test_fp8_block_quantizer_bitwise(rows, cols):
+    ops = _ops()
+    torch.manual_seed(rows + cols)
+    w = torch.randn(rows, cols, device="cuda", dtype=torch.bfloat16) * 0.03
+    w[:128, :128] = 0  # an all-zero block keeps its floor scale
+    q = ops.quantize_fp8_block(w)
+    torch.cuda.synchronize()
+    codes, scales = R.fp8_block_quantize(w)
+    assert torch.equal(q.scales, scales)
+    assert torch.equal(q.codes, codes)
+
+
+@pytest.mark.parametrize("rows,cols", [(64, 64), (257, 1024), (2048, 4096)])
+def test_nvfp4_quantizer_bitwise(rows, cols):
+    ops = _ops()
+    torch.manual_seed(rows * 3 + cols)
+    w = torch.randn(rows, cols, device="cuda", dtype=torch.bfloat16) * 0.02
+    q = ops.quantize_nvfp4(w)
+    torch.cuda.synchronize()
+    packed, s8, ts = R.nvfp4_quantize(w)
+    assert q.tensor_scale == pytest.approx(ts, rel=0, abs=0)
+    assert torch.equal(q.scales, s8)
+    assert torch.equal(q.codes, packed)
+
+
+def _weights(fmt, N, K, seed):
+    ops = _ops()
+    torch.manual_seed(seed)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    if fmt == "fp8_block":
+        q = ops.quantize_fp8_block(w)
+        deq = R.fp8_block_dequantize(q.codes, q.scales)
+        factor = 1.0
+    else:
+        q = ops.quantize_nvfp4(w)
+        deq = R.nvfp4_dequantize(q.codes, q.scales)
+        factor = q.tensor_scale
+    return q, deq, factor
+
+
+@pytest.mark.parametrize("fmt", ["fp8_block", "nvfp4"])
+@pytest.mark.parametrize(
+    "M,N,K,mode,splits",
+    [
+        (1, 256, 1024, 2, 0),
+        (7, 768, 2048, 2, 0),
+        (64, 2048, 4096, 2, 0),
+        (64, 640, 1024, 2, 1),
+        (200, 1024, 2048, 2, 0),
+        (300, 512, 1024, 1, 0),
+        (1024, 1536, 2048, 1, 0),
+    ],
+)
+def test_quantized_gemm(fmt, M, N, K, mode, splits):
+    ops = _ops()
+    q, deq, factor = _weights(fmt, N, K, M + N)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    out = ops.gemm(a, q, mode=mode, splits=splits)
+    torch.cuda.synchronize()
+    ops.scratch().check()
+    _close(out, (a.float() @ deq.T) * factor)
+
+
+@pytest.mark.parametrize("fmt", ["fp8_block", "nvfp4"])
+@pytest.mark.parametrize("M,mode", [(16, 2), (128, 2), (384, 1)])
+def test_quantized_swiglu(fmt, M, mode):
+    ops = _ops()
+    inter, K = 768, 1024
+    q, deq, factor = _weights(fmt, 2 * inter, K, M)
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    out = ops.gemm(a, q, epilogue=ops.EPI_SWIGLU, mode=mode)
+    torch.cuda.synchronize()
+    full = (a.float() @ deq.T) * factor
+    blocks = full.view(M, -1, 2, 128)
+    ref = R.swiglu(blocks[:, :, 0].reshape(M, inter), blocks[:, :, 1].reshape(M, inter))
+    _close(out, ref)
+
+
+def test_quantized_gemm_f32_epilogue():
+    ops = _ops()
+    q, deq, factor = _weights("nvfp4", 512, 2048, 5)
+    a = torch.randn(32, 2048, device="cuda", dtype=torch.bfloat16)
+    out = ops.gemm(a, q, epilogue=ops.EPI_F32)
+    torch.cuda.synchronize()
+    _close(out, (a.float() @ deq.T) * factor, 1e-3)
