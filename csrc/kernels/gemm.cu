@@ -42,7 +42,6 @@ namespace foa {
 namespace {
 
 constexpr int kBlockK = 64;  // 64 BF16 = 128 bytes: one swizzled row
-constexpr int kThreads = 192;
 
 struct KParams {
   int Mp, Nq;                 // rows of the M-side and N-side operands
@@ -64,10 +63,17 @@ struct KParams {
   const void* wscale;         // FP8: FP32 [ceil(N/128)][ceil(K/128)]; NVFP4: E4M3 [N][K/16]
   long wscale_ld;             // scale elements per scale row
   float acc_scale;            // NVFP4 tensor scale (1 otherwise), applied to the reduced sum
+  // Block-scaled operands (kWF == kWNvfp4A4): scale atoms of the M-side and N-side operands,
+  // [row block of 128][K/64][512 bytes], and the bytes between two row blocks.
+  const uint8_t* sf_p;
+  const uint8_t* sf_q;
+  long sf_stride_p, sf_stride_q;
+  int sf_blocks_q;            // 128-row blocks of the N side's atoms
 };
 
-// Weight formats a GEMM reads.
-enum : int { kWBf16 = 0, kWFp8Block = 1, kWNvfp4 = 2 };
+// Weight formats a GEMM reads: BF16; FP8 block-scaled or NVFP4 codes dequantized to BF16 in
+// shared memory (BF16 activations); NVFP4 codes of both operands on the block-scaled MMA.
+enum : int { kWBf16 = 0, kWFp8Block = 1, kWNvfp4 = 2, kWNvfp4A4 = 3 };
 
 // Eight E4M3 codes times their block scale, rounded to BF16.
 __device__ __forceinline__ uint4 dequant_fp8x8(uint2 v, float scale) {
@@ -119,16 +125,24 @@ struct Cfg {
   static constexpr int kWRows = kPRows > kBN ? kPRows : kBN;
   static constexpr int kRawRow = kWF == kWFp8Block ? 64 : kWF == kWNvfp4 ? 32 : 0;
   static constexpr int kRawBytes = kWRows * kRawRow;
+  // Block-scaled operands: per stage one 2 KiB group of scale atoms (4 MMAs x 512 bytes) for each
+  // 128 rows of either side, copied into TMEM columns after the accumulators. An MMA reads the
+  // scales of its 32-row slices from consecutive columns, four bytes (four K groups) a column.
+  static constexpr int kQGroups = (kBN + 127) / 128;
+  static constexpr int kSfBytes = kWF == kWNvfp4A4 ? (kMB + kQGroups) * 2048 : 0;
+  static constexpr int kSfCols = kWF == kWNvfp4A4 ? 16 * (kMB + kQGroups) : 0;
+  static constexpr int kBoxX = kWF == kWNvfp4A4 ? 128 : 64;  // TMA x extent of a k-block
   static constexpr int kAccCols = kMB * kBN;
-  static constexpr int kColsRaw = kAcc * kAccCols;
+  static constexpr int kSfCol0 = kAcc * kAccCols;
+  static constexpr int kColsRaw = kAcc * kAccCols + kSfCols;
   static constexpr int kTmemCols = kColsRaw <= 32    ? 32
                                    : kColsRaw <= 64  ? 64
                                    : kColsRaw <= 128 ? 128
                                    : kColsRaw <= 256 ? 256
                                                      : 512;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kSmemBytes = kStages * (kStageBytes + kRawBytes) + kBarrierBytes + 1024;
-  static constexpr int kThreadsCta = kWF == kWBf16 ? 192 : 320;
+  static constexpr int kSmemBytes = kStages * (kStageBytes + kRawBytes + kSfBytes) + kBarrierBytes + 1024;
+  static constexpr int kThreadsCta = (kWF == kWFp8Block || kWF == kWNvfp4) ? 320 : 192;
   static_assert(kColsRaw <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 232448, "stages exceed shared memory");
   static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "invalid MMA N");
@@ -236,8 +250,9 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* raw = smem + kStages * C::kStageBytes;  // quantized weight ring (kWF != 0)
-  uint64_t* full = reinterpret_cast<uint64_t*>(raw + kStages * C::kRawBytes);
+  uint8_t* raw = smem + kStages * C::kStageBytes;  // quantized weight ring (kWF 1, 2)
+  uint8_t* sfr = raw + kStages * C::kRawBytes;      // scale-atom ring (kWF 3)
+  uint64_t* full = reinterpret_cast<uint64_t*>(sfr + kStages * C::kSfBytes);
   uint64_t* empty = full + kStages;
   uint64_t* rawfull = empty + kStages;
   uint64_t* tfull = rawfull + kStages;
@@ -255,7 +270,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     for (int s = 0; s < kStages; ++s) {
       // A stage is full when its TMA bytes land and, for quantized weights, the four converter
       // warps have written the weight tile.
-      mbar_init(full + s, kWF == kWBf16 ? 1 : 5);
+      mbar_init(full + s, (kWF == kWBf16 || kWF == kWNvfp4A4) ? 1 : 5);
       mbar_init(empty + s, 1);
       mbar_init(rawfull + s, 1);
     }
@@ -269,7 +284,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
-    if (kWF != kWBf16) tma_prefetch_desc(&tmW);
+    if (kWF == kWFp8Block || kWF == kWNvfp4) tma_prefetch_desc(&tmW);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -288,13 +303,30 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       bool ok = true;
       // Weight tile of stage s: straight into the stage (BF16), or raw into the side ring for the
       // converter warps (quantized formats).
+      // Scale atoms of stage s: the M side's 128-row blocks first, then the N side's block.
+      auto load_sf = [&](int s, int kb, int tp, int tq, bool p_side) {
+        uint8_t* dst = sfr + s * C::kSfBytes;
+        if (p_side) {
+          for (int mb = 0; mb < kMB; ++mb)
+            bulk_load(dst + mb * 2048, p.sf_p + (long)(tp * kMB + mb) * p.sf_stride_p + (long)kb * 2048,
+                      2048, full + s);
+        } else {
+          // A 256-row tile past the last block re-reads that block: its rows have zero codes.
+          for (int g = 0; g < C::kQGroups; ++g)
+            bulk_load(dst + (kMB + g) * 2048,
+                      p.sf_q + (long)min(((tq * kBN) >> 7) + g, p.sf_blocks_q - 1) * p.sf_stride_q +
+                          (long)kb * 2048,
+                      2048, full + s);
+        }
+      };
       auto load_w = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
-        if constexpr (kWF == kWBf16) {
+        if constexpr (kWF == kWBf16 || kWF == kWNvfp4A4) {
           if (p.swap)
-            tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
+            tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
           else
-            tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+            tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * C::kBoxX, tq * kBN);
+          if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap != 0);
         } else {
           const int rows = p.swap ? C::kPRows : kBN;
           mbar_arrive_expect_tx(rawfull + s, rows * C::kRawRow);
@@ -305,12 +337,14 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       auto load_a = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
         if (p.swap)
-          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * kBlockK, tq * kBN);
+          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * C::kBoxX, tq * kBN);
         else
-          tma_load_2d(st, &tmP, full + s, kb * kBlockK, tp * C::kPRows);
+          tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
+        if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap == 0);
       };
-      const uint32_t full_bytes =
-          kWF == kWBf16 ? C::kStageBytes : (p.swap ? C::kQBytes : C::kPBytes);
+      const uint32_t full_bytes = kWF == kWBf16      ? C::kStageBytes
+                                  : kWF == kWNvfp4A4 ? C::kStageBytes + C::kSfBytes
+                                                     : (p.swap ? C::kQBytes : C::kPBytes);
       // The first stages' weight tiles do not depend on earlier kernels: issue them before
       // waiting for the previous kernel (PDL), then their activation tiles after it.
       int pre = 0;
@@ -360,11 +394,16 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   } else if (warp == 1) {
     // ----------------------------------------------------------------- MMA issuer
     if (elect_one()) {
-      constexpr uint32_t idesc = idesc_bf16_f32(128, kBN);
+      constexpr uint32_t idesc =
+          kWF == kWNvfp4A4 ? idesc_nvf4_f32(128, kBN) : idesc_bf16_f32(128, kBN);
+      const uint32_t sfa_t = tmem_base + C::kSfCol0;
+      const uint32_t sfb_t = sfa_t + 16 * kMB;
       uint32_t it = 0, tc = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++tc) {
         const int split = u % p.splits;
+        // A 64-row N tile reads the second half of its 128-row scale atoms when it is odd.
+        const uint32_t sfb_shift = (kBN == 64 && ((u / p.splits) / p.tiles_p) % 2 == 1) ? 2u : 0u;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
         const int b = tc % kAcc;
@@ -382,13 +421,41 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           if (it == 0) mark(p, 3);
           tc_fence_after();
           const uint8_t* st = smem + s * C::kStageBytes;
+          if constexpr (kWF == kWNvfp4A4) {
+            // Scales into TMEM, then four K=64 block-scaled MMAs (32 bytes of each row apiece);
+            // the copies and MMAs of this thread execute in issue order.
+            // TMEM: A scales [mb][kk][4 columns]; B scales [kk][group][4 columns].
+            const uint8_t* sf = sfr + s * C::kSfBytes;
 #pragma unroll
-          for (int kk = 0; kk < kBlockK / 16; ++kk) {
-            const uint64_t bdesc = sdesc_kmajor_sw128(st + C::kPBytes + kk * 32);
+            for (int mb = 0; mb < kMB; ++mb)
 #pragma unroll
-            for (int mb = 0; mb < kMB; ++mb) {
-              const uint64_t adesc = sdesc_kmajor_sw128(st + mb * 16384 + kk * 32);
-              mma_bf16(d0 + mb * kBN, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              for (int kk = 0; kk < 4; ++kk)
+                tmem_cp_sf_atom(sfa_t + mb * 16 + kk * 4, sdesc_sf_atom(sf + mb * 2048 + kk * 512));
+#pragma unroll
+            for (int g = 0; g < C::kQGroups; ++g)
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                tmem_cp_sf_atom(sfb_t + kk * 4 * C::kQGroups + g * 4,
+                                sdesc_sf_atom(sf + (kMB + g) * 2048 + kk * 512));
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bdesc = sdesc_kmajor_sw128(st + C::kPBytes + kk * 32);
+#pragma unroll
+              for (int mb = 0; mb < kMB; ++mb) {
+                const uint64_t adesc = sdesc_kmajor_sw128(st + mb * 16384 + kk * 32);
+                mma_nvf4(d0 + mb * kBN, adesc, bdesc, idesc, sfa_t + mb * 16 + kk * 4,
+                         sfb_t + kk * 4 * C::kQGroups + sfb_shift, (kb > kb0 || kk > 0) ? 1u : 0u);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < kBlockK / 16; ++kk) {
+              const uint64_t bdesc = sdesc_kmajor_sw128(st + C::kPBytes + kk * 32);
+#pragma unroll
+              for (int mb = 0; mb < kMB; ++mb) {
+                const uint64_t adesc = sdesc_kmajor_sw128(st + mb * 16384 + kk * 32);
+                mma_bf16(d0 + mb * kBN, adesc, bdesc, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+              }
             }
           }
           mma_commit(empty + s);
@@ -397,7 +464,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         if (tc == 0) mark(p, 4);
       }
     }
-  } else if (kWF != kWBf16 && warp >= 6) {
+  } else if ((kWF == kWFp8Block || kWF == kWNvfp4) && warp >= 6) {
     // ----------------------------------------------------------------- weight converters (4 warps)
     // Expand each raw weight tile into the BF16 128-byte-swizzled layout the MMA reads: FP8 codes
     // times their 128x128 block scale (rounded once to BF16), or E2M1 codes times their E4M3
@@ -476,7 +543,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         }
 #pragma unroll
         for (int t = 0; t < 16; ++t)
-          v[t] = kWF == kWNvfp4 ? __uint_as_float(r[t]) * p.acc_scale : __uint_as_float(r[t]);
+          v[t] = (kWF == kWNvfp4 || kWF == kWNvfp4A4) ? __uint_as_float(r[t]) * p.acc_scale
+                                                       : __uint_as_float(r[t]);
       };
       // Partials are stored column-major ([col][row]) so a warp's 32 rows are 128 contiguous bytes.
       const long tile_elems = (long)C::kPRows * kBN;
@@ -607,7 +675,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
 #pragma unroll
           for (int t = 0; t < 16; ++t)
             dsmem_st_f32(base + 4u * (uint32_t)((c0 + t) * rs),
-                         kWF == kWNvfp4 ? __uint_as_float(r[t]) * p.acc_scale : __uint_as_float(r[t]));
+                         (kWF == kWNvfp4 || kWF == kWNvfp4A4) ? __uint_as_float(r[t]) * p.acc_scale
+                                                              : __uint_as_float(r[t]));
         }
       }
       tc_fence_before();
@@ -692,16 +761,18 @@ template <int kMB, int kBN, int kWF>
 struct Shape {
   static constexpr int kStage = 128 * kMB * 128 + kBN * 128;
   static constexpr int kRaw = (kMB * 128 > kBN ? kMB * 128 : kBN) * (kWF == 1 ? 64 : kWF == 2 ? 32 : 0);
-  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw);
+  static constexpr int kSfGroups = kWF == 3 ? kMB + (kBN + 127) / 128 : 0;
+  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw + kSfGroups * 2048);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kAcc = kMB * kBN * 2 <= 512 ? 2 : 1;
+  static constexpr int kAcc = kMB * kBN * 2 + 16 * kSfGroups <= 512 ? 2 : 1;
 };
 
 // Bytes of the operand ring of a swap-mapping configuration (the cluster reduction reuses it).
 int swap_ring_bytes(int mb, int kbn, int wf) {
   const int stage = 128 * mb * 128 + kbn * 128;
   const int raw = (mb * 128 > kbn ? mb * 128 : kbn) * (wf == 1 ? 64 : wf == 2 ? 32 : 0);
-  int stages = (220 * 1024 - 2048) / (stage + raw);
+  const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : 0;
+  int stages = (220 * 1024 - 2048) / (stage + raw + sf);
   if (stages > 8) stages = 8;
   return stage * stages;
 }
@@ -714,7 +785,8 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   Plan pl{};
   const bool swap = a.mode == kModeSwap || (a.mode == kModeAuto && a.M <= 256);
   pl.swap = swap;
-  pl.kblocks = (a.K + kBlockK - 1) / kBlockK;
+  const int kelems = a.w_format == kWNvfp4A4 ? 256 : kBlockK;  // K elements of one stage
+  pl.kblocks = (a.K + kelems - 1) / kelems;
   if (!swap) {
     pl.mb = 1;
     pl.kbn = 256;
@@ -723,6 +795,12 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   } else {
     pl.mb = a.epilogue == kEpiSwiGLU ? 2 : 1;
     pl.kbn = pick_swap_bn(a.M);
+    if (a.w_format == kWNvfp4A4) {
+      // Block-scaled N tiles read whole 64-row halves of a scale atom; two M blocks and their
+      // scales leave TMEM room for N <= 128.
+      pl.kbn = std::max(pl.kbn, 64);
+      if (pl.mb == 2) pl.kbn = std::min(pl.kbn, 128);
+    }
     pl.tiles_p = (a.N + 128 * pl.mb - 1) / (128 * pl.mb);
     pl.tiles_q = (a.M + pl.kbn - 1) / pl.kbn;
   }
@@ -884,6 +962,35 @@ int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUt
   }
 }
 
+// Block-scaled NVFP4 configurations: swap N tiles of 64/128/256 (two M blocks: 64/128).
+int launch_swap_nvf4(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+                     const KParams& kp, const Plan& pl, cudaStream_t stream) {
+  constexpr int W = kWNvfp4A4;
+  if (pl.mb == 2) {
+    if (epi != kEpiSwiGLU) return -2;
+    return pl.kbn == 64 ? launch_red<2, 64, kEpiSwiGLU, W>(tp, tq, tw, kp, pl, stream)
+                        : launch_red<2, 128, kEpiSwiGLU, W>(tp, tq, tw, kp, pl, stream);
+  }
+  switch (pl.kbn) {
+    case 64: return launch_plain_epi<1, 64, W>(epi, tp, tq, tw, kp, pl, stream);
+    case 128: return launch_plain_epi<1, 128, W>(epi, tp, tq, tw, kp, pl, stream);
+    default: return launch_plain_epi<1, 256, W>(epi, tp, tq, tw, kp, pl, stream);
+  }
+}
+
+int cluster_limit_nvf4(int mb, int kbn, int epi, int size) {
+  constexpr int W = kWNvfp4A4;
+  if (mb == 2)
+    return kbn == 64 ? max_active_clusters<2, 64, kEpiSwiGLU, W>(size)
+                     : max_active_clusters<2, 128, kEpiSwiGLU, W>(size);
+  const bool f32 = epi == kEpiF32;
+  switch (kbn) {
+    case 64: return f32 ? max_active_clusters<1, 64, kEpiF32, W>(size) : max_active_clusters<1, 64, kEpiBf16, W>(size);
+    case 128: return f32 ? max_active_clusters<1, 128, kEpiF32, W>(size) : max_active_clusters<1, 128, kEpiBf16, W>(size);
+    default: return f32 ? max_active_clusters<1, 256, kEpiF32, W>(size) : max_active_clusters<1, 256, kEpiBf16, W>(size);
+  }
+}
+
 template <int kWF>
 int launch_rows(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
                 const KParams& kp, const Plan& pl, cudaStream_t stream) {
@@ -921,6 +1028,7 @@ int cluster_limit_of(int mb, int kbn, int epi, int size) {
   switch (g_cluster_wf) {
     case kWFp8Block: return cluster_limit_wf<kWFp8Block>(mb, kbn, epi, size);
     case kWNvfp4: return cluster_limit_wf<kWNvfp4>(mb, kbn, epi, size);
+    case kWNvfp4A4: return cluster_limit_nvf4(mb, kbn, epi, size);
     default: return cluster_limit_wf<kWBf16>(mb, kbn, epi, size);
   }
 }
@@ -946,6 +1054,13 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.residual != nullptr && a.epilogue != kEpiBf16) return -2;
   if (a.w_format != kWBf16 && a.w_scale == nullptr) return -2;
   if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
+  const bool nvf4 = a.w_format == kWNvfp4A4;
+  if (nvf4) {
+    // Both operands are packed E2M1 codes (two a byte) with 128-row-blocked scale atoms.
+    if (a.K % 256 != 0 || a.lda % 32 != 0 || a.ldw % 32 != 0 || a.a_scale == nullptr) return -2;
+    if ((reinterpret_cast<uintptr_t>(a.a_scale) & 15) || (reinterpret_cast<uintptr_t>(a.w_scale) & 15))
+      return -1;
+  }
 
   const int sms = a.num_sms > 0 ? a.num_sms : device_sms();
   g_cluster_wf = a.w_format;
@@ -974,14 +1089,24 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;
   kp.wscale_ld = a.w_scale_ld;
-  kp.acc_scale = a.w_format == kWNvfp4 ? a.w_tensor_scale : 1.0f;
+  kp.acc_scale = (a.w_format == kWNvfp4 || nvf4) ? a.w_tensor_scale : 1.0f;
+  if (nvf4) {
+    const long atoms = (long)(a.K / 64) * 512;  // bytes of one 128-row block of scale atoms
+    const uint8_t* sw = static_cast<const uint8_t*>(a.w_scale);
+    const uint8_t* sa = static_cast<const uint8_t*>(a.a_scale);
+    kp.sf_p = pl.swap ? sw : sa;
+    kp.sf_q = pl.swap ? sa : sw;
+    kp.sf_stride_p = kp.sf_stride_q = atoms;
+    kp.sf_blocks_q = ((pl.swap ? a.M : a.N) + 127) / 128;
+  }
   if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
 
   CUtensorMap tp, tq, tw;
   std::memset(&tw, 0, sizeof(tw));
   const int prow_box = 128 * pl.mb;
   const int wrows_box = pl.swap ? prow_box : pl.kbn;
-  if (a.w_format != kWBf16) {
+  const bool converted = a.w_format == kWFp8Block || a.w_format == kWNvfp4;
+  if (converted) {
     // Raw quantized rows: K bytes (FP8) or K/2 bytes (NVFP4) a row, one k-block per box.
     const long row_bytes = a.w_format == kWFp8Block ? a.K : a.K / 2;
     const long ld_bytes = a.w_format == kWFp8Block ? a.ldw : a.ldw / 2;
@@ -990,28 +1115,34 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
                         wrows_box, box_bytes, CU_TENSOR_MAP_SWIZZLE_NONE))
       return -4;
   }
-  const bool quant = a.w_format != kWBf16;
+  // Operand maps: BF16 rows of 64 elements, or packed E2M1 rows of 128 bytes (256 elements).
+  auto operand = [&](CUtensorMap* m, const void* base, long rows, long ld, int box) {
+    return nvf4 ? encode_tmap_u8_kmajor(m, base, rows, a.K / 2, ld / 2, box)
+                : encode_tmap_bf16_kmajor(m, base, rows, a.K, ld, box);
+  };
   if (!pl.swap) {
     kp.Mp = a.M;
     kp.Nq = a.N;
-    if (!encode_tmap_bf16_kmajor(&tp, a.a, a.M, a.K, a.lda, prow_box)) return -4;
-    if (quant) tq = tw;  // unused by the quantized producer
-    else if (!encode_tmap_bf16_kmajor(&tq, a.w, a.N, a.K, a.ldw, pl.kbn)) return -4;
+    if (!operand(&tp, a.a, a.M, a.lda, prow_box)) return -4;
+    if (converted) tq = tw;  // unused by the converting producer
+    else if (!operand(&tq, a.w, a.N, a.ldw, pl.kbn)) return -4;
     if (pl.red == 2) return -2;
     switch (a.w_format) {
       case kWFp8Block: return launch_rows<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
       case kWNvfp4: return launch_rows<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
+      case kWNvfp4A4: return launch_rows<kWNvfp4A4>(a.epilogue, tp, tq, tw, kp, pl, stream);
       default: return launch_rows<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
     }
   }
   kp.Mp = a.N;
   kp.Nq = a.M;
-  if (quant) tp = tw;
-  else if (!encode_tmap_bf16_kmajor(&tp, a.w, a.N, a.K, a.ldw, prow_box)) return -4;
-  if (!encode_tmap_bf16_kmajor(&tq, a.a, a.M, a.K, a.lda, pl.kbn)) return -4;
+  if (converted) tp = tw;
+  else if (!operand(&tp, a.w, a.N, a.ldw, prow_box)) return -4;
+  if (!operand(&tq, a.a, a.M, a.lda, pl.kbn)) return -4;
   switch (a.w_format) {
     case kWFp8Block: return launch_swap<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
     case kWNvfp4: return launch_swap<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
+    case kWNvfp4A4: return launch_swap_nvf4(a.epilogue, tp, tq, tw, kp, pl, stream);
     default: return launch_swap<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
   }
 }

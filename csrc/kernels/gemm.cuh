@@ -53,13 +53,24 @@ struct GemmArgs {
   //                    the low nibble), w_scale E4M3 [N, w_scale_ld] one per 16 columns,
   //                    w_tensor_scale the FP32 factor of the whole tensor ("weight_scale_2")
   //                    that multiplies the FP32 sums (K % 64 == 0).
+  //   kWeightNvfp4A4:  block-scaled NVFP4 on both operands (W4A4): `a` and `w` hold packed E2M1
+  //                    codes (lda/ldw count elements), `a_scale` and `w_scale` their UE4M3 scales
+  //                    as 128-row-blocked atoms [ceil(rows/128)][K/64][512 bytes] (in each atom the
+  //                    scale of row r, group k sits at byte (r % 32) * 16 + (r / 32) * 4 + k), and
+  //                    w_tensor_scale the product of both tensor scales (K % 256 == 0).
   int w_format = 0;
   const void* w_scale = nullptr;
   long w_scale_ld = 0;
   float w_tensor_scale = 1.0f;
+  const void* a_scale = nullptr;
 };
 
-enum GemmWeightFormat : int { kWeightBf16 = 0, kWeightFp8Block = 1, kWeightNvfp4 = 2 };
+enum GemmWeightFormat : int {
+  kWeightBf16 = 0,
+  kWeightFp8Block = 1,
+  kWeightNvfp4 = 2,
+  kWeightNvfp4A4 = 3,
+};
 
 // Plans and launches one GEMM on `stream`. Returns 0, or a negative code for a rejected argument
 // (no launch happens then): -1 misaligned pointer/stride, -2 bad shape, -3 scratch too small,

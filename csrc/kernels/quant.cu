@@ -64,6 +64,34 @@ __device__ __forceinline__ uint32_t e2m1_magnitude(float m) {
        : m <= 2.5f ? 4u : m < 3.5f ? 5u : m <= 5.f ? 6u : 7u;
 }
 
+// The factor a group's values take before E2M1 rounding: 1 / (s * (1 / global)), 0 when the
+// block scale s is 0 (the order of vLLM's reference NVFP4 quantizer).
+__device__ __forceinline__ float code_factor(__nv_fp8_storage_t s8, float global) {
+  const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
+  const float s = __half2float(__half(hr));
+  const float restore = s * (1.f / global);
+  return restore != 0.f ? 1.f / restore : 0.f;
+}
+
+// 16 values -> 8 bytes of E2M1 codes (lower index in the low nibble).
+__device__ __forceinline__ uint2 e2m1_pack16(const float (&v)[16], float k) {
+  uint32_t packed[2] = {0u, 0u};
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float x = v[i] * k;
+    const uint32_t code = e2m1_magnitude(fabsf(x)) | (x < 0.f ? 8u : 0u);
+    packed[i / 8] |= code << (4 * (i % 8));
+  }
+  return make_uint2(packed[0], packed[1]);
+}
+
+// Byte offset of the scale of (row, 16-group g) in 128-row-blocked atoms of a K-column matrix.
+__device__ __forceinline__ long sf_atom_offset(long row, int g, int K) {
+  const long rb = row >> 7;
+  const int rr = (int)(row & 127);
+  return (rb * (K / 64) + g / 4) * 512 + (rr & 31) * 16 + (rr >> 5) * 4 + (g & 3);
+}
+
 // One thread per 16-element group.
 __global__ void nvfp4_kernel(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes,
                              uint8_t* scales, const float* amax_p, float* tensor_scale) {
@@ -83,18 +111,53 @@ __global__ void nvfp4_kernel(const __nv_bfloat16* w, int rows, int cols, uint8_t
   }
   const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(m / 6.f * global, __NV_SATFINITE, __NV_E4M3);
   scales[r * groups + c0 / 16] = s8;
-  const __half_raw hr = __nv_cvt_fp8_to_halfraw(s8, __NV_E4M3);
-  const float s = __half2float(__half(hr));
-  const float k = s > 0.f ? global / s : 0.f;
-  uint32_t packed[2] = {0u, 0u};
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const float x = v[i] * k;
-    const uint32_t code = e2m1_magnitude(fabsf(x)) | (x < 0.f ? 8u : 0u);
-    packed[i / 8] |= code << (4 * (i % 8));
+  const float k = code_factor(s8, global);
+  *reinterpret_cast<uint2*>(codes + r * (cols / 2) + c0 / 2) = e2m1_pack16(v, k);
+}
+
+// Activations under a fixed tensor scale (W4A4 inputs): one thread per 16-group of the padded
+// rows; rows past `rows` get zero codes and zero scales.
+__global__ void nvfp4_act_kernel(const __nv_bfloat16* x, long ldx, int rows, int rows_pad, int K,
+                                 float global, uint8_t* codes, long ldc, uint8_t* sf) {
+  pdl_wait();
+  pdl_trigger();
+  const int groups = K / 16;
+  const long g = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (g >= (long)rows_pad * groups) return;
+  const long r = g / groups;
+  const int gi = (int)(g % groups);
+  if (r >= rows) {
+    sf[sf_atom_offset(r, gi, K)] = 0;
+    return;
   }
-  uint2* dst = reinterpret_cast<uint2*>(codes + r * (cols / 2) + c0 / 2);
-  *dst = make_uint2(packed[0], packed[1]);
+  float v[16], m = 0.f;
+  const uint4* src = reinterpret_cast<const uint4*>(x + r * ldx + gi * 16);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const uint4 q = src[h];
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[h * 8 + 2 * i] = __uint_as_float(w[i] << 16);
+      v[h * 8 + 2 * i + 1] = __uint_as_float(w[i] & 0xFFFF0000u);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) m = fmaxf(m, fabsf(v[i]));
+  const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(m / 6.f * global, __NV_SATFINITE, __NV_E4M3);
+  sf[sf_atom_offset(r, gi, K)] = s8;
+  *reinterpret_cast<uint2*>(codes + r * ldc + gi * 8) = e2m1_pack16(v, code_factor(s8, global));
+}
+
+// Row-major scales [rows][K/16] -> 128-row-blocked atoms (zero for the padded rows).
+__global__ void sf_atoms_kernel(const uint8_t* src, long lds, int rows, int rows_pad, int K, uint8_t* dst) {
+  pdl_wait();  // weight producer: no early trigger
+  const int groups = K / 16;
+  const long g = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (g >= (long)rows_pad * groups) return;
+  const long r = g / groups;
+  const int gi = (int)(g % groups);
+  dst[sf_atom_offset(r, gi, K)] = r < rows ? src[r * lds + gi] : 0;
 }
 
 }  // namespace
@@ -105,6 +168,30 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
   dim3 grid((cols + 127) / 128, (rows + 127) / 128);
   return launch_pdl(fp8_block_kernel, grid, dim3(256), 0, stream, w, rows, cols, codes, scales) ==
                  cudaSuccess
+             ? 0
+             : -5;
+}
+
+int quantize_nvfp4_act(const __nv_bfloat16* x, long ldx, int rows, int K, float global,
+                       uint8_t* codes, long ldc, uint8_t* sf_atoms, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (K % 64 != 0 || ldx % 8 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) || ldc % 8 != 0) return -2;
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const long groups = (long)rows_pad * (K / 16);
+  return launch_pdl(nvfp4_act_kernel, dim3((unsigned)((groups + 255) / 256)), dim3(256), 0, stream, x,
+                    ldx, rows, rows_pad, K, global, codes, ldc, sf_atoms) == cudaSuccess
+             ? 0
+             : -5;
+}
+
+int nvfp4_scale_atoms(const uint8_t* scales, long lds, int rows, int K, uint8_t* sf_atoms,
+                      cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (K % 64 != 0) return -2;
+  const int rows_pad = (rows + 127) / 128 * 128;
+  const long groups = (long)rows_pad * (K / 16);
+  return launch_pdl(sf_atoms_kernel, dim3((unsigned)((groups + 255) / 256)), dim3(256), 0, stream,
+                    scales, lds, rows, rows_pad, K, sf_atoms) == cudaSuccess
              ? 0
              : -5;
 }

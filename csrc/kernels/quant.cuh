@@ -16,11 +16,22 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
 
 // NVFP4 (E2M1 codes, E4M3 scale per 16 elements along cols, FP32 tensor scale):
 // global = 448 * 6 / amax(W) (the tensor's "weight_scale_2" is 1 / global);
-// block scale s = e4m3(amax(block) / 6 * global); code = e2m1_rne(w * global / s).
+// block scale s = e4m3(amax(block) / 6 * global); code = e2m1_rne(w / (s * (1 / global))).
 // Codes pack two per byte, the lower column in the low nibble. `amax` is a device FP32 holding
 // amax(W) (absmax_bf16 computes it); `tensor_scale`, when not null, receives 1 / global.
 int quantize_nvfp4(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, uint8_t* scales,
                    const float* amax, float* tensor_scale, cudaStream_t stream);
+
+// NVFP4 activations under a fixed tensor scale `global` (1 / the checkpoint's input_scale), the
+// W4A4 input form of the block-scaled GEMM: codes [rows, K/2] (row stride ldc bytes) and scales as
+// 128-row-blocked atoms [ceil(rows/128)][K/64][512] (padded rows zero).
+int quantize_nvfp4_act(const __nv_bfloat16* x, long ldx, int rows, int K, float global,
+                       uint8_t* codes, long ldc, uint8_t* sf_atoms, cudaStream_t stream);
+
+// Row-major E4M3 scales [rows][K/16] (row stride lds) -> the 128-row-blocked atoms the
+// block-scaled GEMM reads.
+int nvfp4_scale_atoms(const uint8_t* scales, long lds, int rows, int K, uint8_t* sf_atoms,
+                      cudaStream_t stream);
 
 // amax over n BF16 values into *out (out must start at 0).
 int absmax_bf16(const __nv_bfloat16* x, long n, float* out, cudaStream_t stream);

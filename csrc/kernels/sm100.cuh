@@ -192,6 +192,76 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(const void* smem) {
   return desc;
 }
 
+// Instruction descriptor of a block-scaled kind::mxf4nvf4 MMA: E2M1 A/B (both K-major), FP32
+// accumulate, one UE4M3 scale per 16 elements of K (scale-factor ids 0), shape M x N.
+__host__ __device__ constexpr uint32_t idesc_nvf4_f32(int m, int n) {
+  return (1u << 7)                                 // A format: E2M1
+         | (1u << 10)                              // B format: E2M1
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (0u << 23)                              // scale format: UE4M3
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// Instruction descriptor of a dense kind::f8f6f4 MMA: E4M3 A/B (both K-major), FP32 accumulate.
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int m, int n) {
+  return (1u << 4)                                 // D format: F32
+         | (0u << 7)                               // A format: E4M3
+         | (0u << 10)                              // B format: E4M3
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// Shared-memory descriptor of one scale-factor atom for tcgen05.cp: 32 rows of 16 bytes, no
+// swizzle, eight-row core matrices 128 bytes apart.
+__device__ __forceinline__ uint64_t sdesc_sf_atom(const void* smem) {
+  const uint64_t addr = smem_u32(smem);
+  uint64_t desc = 0;
+  desc |= (addr >> 4) & 0x3FFFull;      // start address
+  desc |= (uint64_t)1 << 16;            // leading byte offset (one 16-byte column: unused)
+  desc |= (uint64_t)(128 >> 4) << 32;   // stride byte offset: one 8-row core matrix
+  desc |= (uint64_t)1 << 46;            // descriptor version of sm_100
+  return desc;                          // layout 0: no swizzle
+}
+
+// Copies one 32 x 128-bit scale atom from shared memory into TMEM columns [taddr, taddr + 4) of
+// all four lane quarters (the layout block-scaled MMAs read their scales in).
+__device__ __forceinline__ void tmem_cp_sf_atom(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(sdesc)
+               : "memory");
+}
+
+// D[tmem] (+)= (A * SFA)[smem] * (B * SFB)[smem]^T for E2M1 operands with UE4M3 scales per 16.
+__device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n}\n"
+      ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem),
+      "r"(sfb_tmem)
+      : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T for E4M3 operands.
+__device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Untiled bulk copy global -> shared (no multicast), completing on `bar` with `bytes`
+// transaction bytes. Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                          uint32_t idesc, uint32_t accumulate) {

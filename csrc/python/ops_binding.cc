@@ -34,8 +34,9 @@ void bind_ops(py::module_& m) {
       [](uint64_t a, long lda, uint64_t w, long ldw, int M, int N, int K, uint64_t c, long ldc,
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
          uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
-         int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale) {
+         int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale) {
         foa::GemmArgs g;
+        g.a_scale = as_ptr<void>(a_scale);
         g.w_format = w_format;
         g.w_scale = as_ptr<void>(w_scale);
         g.w_scale_ld = w_scale_ld;
@@ -68,7 +69,30 @@ void bind_ops(py::module_& m) {
       py::arg("epilogue"), py::arg("mode"), py::arg("splits"), py::arg("ws"),
       py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
       py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
-      py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f);
+      py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0);
+
+  m.def(
+      "quantize_nvfp4_act",
+      [](uint64_t x, long ldx, int rows, int K, float global, uint64_t codes, long ldc,
+         uint64_t sf_atoms, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::quantize_nvfp4_act(as_ptr<const __nv_bfloat16>(x), ldx, rows, K, global,
+                                      as_ptr<uint8_t>(codes), ldc, as_ptr<uint8_t>(sf_atoms),
+                                      as_stream(stream)),
+              "quantize_nvfp4_act");
+      },
+      py::arg("x"), py::arg("ldx"), py::arg("rows"), py::arg("K"), py::arg("global_scale"),
+      py::arg("codes"), py::arg("ldc"), py::arg("sf_atoms"), py::arg("stream"));
+  m.def(
+      "nvfp4_scale_atoms",
+      [](uint64_t scales, long lds, int rows, int K, uint64_t sf_atoms, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::nvfp4_scale_atoms(as_ptr<const uint8_t>(scales), lds, rows, K,
+                                     as_ptr<uint8_t>(sf_atoms), as_stream(stream)),
+              "nvfp4_scale_atoms");
+      },
+      py::arg("scales"), py::arg("lds"), py::arg("rows"), py::arg("K"), py::arg("sf_atoms"),
+      py::arg("stream"));
 
   m.def(
       "quantize_fp8_block",

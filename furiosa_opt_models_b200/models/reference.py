@@ -141,21 +141,51 @@ def _e2m1_code(x: torch.Tensor) -> torch.Tensor:
     return code | ((x < 0).to(torch.uint8) << 3)
 
 
+def _nvfp4_groups(x: torch.Tensor, glob: torch.Tensor):
+    """E2M1 codes [rows, cols] (uint8, sign in bit 3) and E4M3 scale bytes [rows, cols/16] of FP32
+    values under the tensor scale ``glob``: s = e4m3(amax/6 * glob), code = e2m1(x / (s * (1/glob)))."""
+    rows, cols = x.shape
+    blocks = x.view(rows, cols // 16, 16)
+    bmax = blocks.abs().amax(-1)
+    s8 = _e4m3((bmax / torch.full_like(bmax, 6.0)) * glob)
+    restore = _e4m3_value(s8) * (torch.ones_like(glob) / glob)
+    k = torch.where(restore != 0, torch.ones_like(restore) / restore, torch.zeros_like(restore))
+    return _e2m1_code(blocks * k[..., None]).view(rows, cols), s8
+
+
+def _pack_nibbles(codes: torch.Tensor) -> torch.Tensor:
+    return codes[:, 0::2] | (codes[:, 1::2] << 4)
+
+
 def nvfp4_quantize(w: torch.Tensor):
     """BF16 [rows, cols] -> (packed codes uint8 [rows, cols/2], E4M3 scales uint8 [rows, cols/16],
     FP32 tensor scale ``1 / global``), global = 448 * 6 / amax(W)."""
-    rows, cols = w.shape
     wf = w.float()
     amax = wf.abs().max()
     glob = torch.full_like(amax, 448.0 * 6.0) / amax if amax > 0 else torch.ones_like(amax)
-    blocks = wf.view(rows, cols // 16, 16)
-    bmax = blocks.abs().amax(-1)
-    s8 = _e4m3((bmax / torch.full_like(bmax, 6.0)) * glob)
-    s = _e4m3_value(s8)
-    k = torch.where(s > 0, glob / s, torch.zeros_like(s))
-    codes = _e2m1_code(blocks * k[..., None]).view(rows, cols)
-    packed = codes[:, 0::2] | (codes[:, 1::2] << 4)
-    return packed, s8, float(torch.ones_like(glob) / glob)
+    codes, s8 = _nvfp4_groups(wf, glob)
+    return _pack_nibbles(codes), s8, float(torch.ones_like(glob) / glob)
+
+
+def nvfp4_quantize_input(x: torch.Tensor, input_scale: float):
+    """W4A4 inputs: BF16 [rows, cols] under the fixed tensor scale ``global = 1 / input_scale``
+    (FP32) -> (packed codes, E4M3 scales [rows, cols/16])."""
+    glob = torch.ones((), dtype=torch.float32, device=x.device) / torch.tensor(
+        input_scale, dtype=torch.float32, device=x.device)
+    codes, s8 = _nvfp4_groups(x.float(), glob)
+    return _pack_nibbles(codes), s8
+
+
+def nvfp4_scale_atoms(s8: torch.Tensor) -> torch.Tensor:
+    """Row-major scales [rows, K/16] -> 128-row-blocked atoms [ceil(rows/128), K/64, 512] in which
+    the scale of (row r, group k) of a block sits at byte (r % 32) * 16 + (r / 32) * 4 + k."""
+    rows, groups = s8.shape
+    rb = (rows + 127) // 128
+    padded = torch.zeros(rb * 128, groups, dtype=torch.uint8, device=s8.device)
+    padded[:rows] = s8
+    # [rb, r1 (4), r0 (32), kc, k (4)] -> [rb, kc, r0, r1, k]
+    v = padded.view(rb, 4, 32, groups // 4, 4).permute(0, 3, 2, 1, 4)
+    return v.reshape(rb, groups // 4, 512).contiguous()
 
 
 def nvfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:

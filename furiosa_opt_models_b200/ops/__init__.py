@@ -16,6 +16,7 @@ from .kernels import (  # noqa: F401
     W_BF16,
     W_FP8_BLOCK,
     W_NVFP4,
+    W_NVFP4_A4,
     QuantizedWeight,
     argmax,
     embedding,
@@ -27,4 +28,6 @@ from .kernels import (  # noqa: F401
     prefill_work,
     quantize_fp8_block,
     quantize_nvfp4,
+    quantize_nvfp4_input,
+    nvfp4_w4a4,
 )

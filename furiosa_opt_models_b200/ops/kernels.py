@@ -25,7 +25,7 @@ def _rowmajor(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be a 2-D tensor with unit column stride")
 
 
-W_BF16, W_FP8_BLOCK, W_NVFP4 = 0, 1, 2
+W_BF16, W_FP8_BLOCK, W_NVFP4, W_NVFP4_A4 = 0, 1, 2, 3
 
 
 @dataclass
@@ -36,6 +36,9 @@ class QuantizedWeight:
     (one per 128x128 block, the checkpoint's ``weight_scale_inv``).
     nvfp4: ``codes`` uint8 [rows, cols/2] (two E2M1 codes a byte, lower column in the low nibble),
     ``scales`` E4M3 as uint8 [rows, cols/16], ``tensor_scale`` the FP32 ``weight_scale_2``.
+    nvfp4_a4 (W4A4 on the block-scaled MMA): ``codes`` as for nvfp4, ``scales`` the 128-row-blocked
+    scale atoms [ceil(rows/128), cols/64, 512], ``input_scale`` the FP32 tensor scale the inputs
+    quantize under; the sums take ``input_scale * tensor_scale``.
     """
 
     format: str
@@ -44,10 +47,40 @@ class QuantizedWeight:
     rows: int
     cols: int
     tensor_scale: float = 1.0
+    input_scale: float = 1.0
 
     @property
     def code(self) -> int:
-        return {"fp8_block": W_FP8_BLOCK, "nvfp4": W_NVFP4}[self.format]
+        return {"fp8_block": W_FP8_BLOCK, "nvfp4": W_NVFP4, "nvfp4_a4": W_NVFP4_A4}[self.format]
+
+
+def _f32(x: float) -> float:
+    return float(torch.tensor(x, dtype=torch.float32))
+
+
+def nvfp4_w4a4(q: QuantizedWeight, input_scale: float) -> QuantizedWeight:
+    """The W4A4 form of an NVFP4 weight: its scales repacked into 128-row-blocked atoms."""
+    if q.format != "nvfp4":
+        raise ValueError("nvfp4_w4a4 takes an nvfp4 weight")
+    if q.cols % 256:
+        raise ValueError("W4A4 needs inputs in multiples of 256")
+    atoms = torch.empty((q.rows + 127) // 128, q.cols // 64, 512, dtype=torch.uint8, device=q.codes.device)
+    native().ops.nvfp4_scale_atoms(q.scales.data_ptr(), q.scales.stride(0), q.rows, q.cols,
+                                   atoms.data_ptr(), _stream())
+    return QuantizedWeight("nvfp4_a4", q.codes, atoms, q.rows, q.cols, q.tensor_scale, _f32(input_scale))
+
+
+def quantize_nvfp4_input(x: torch.Tensor, input_scale: float):
+    """W4A4 inputs: (packed codes [rows, K/2], scale atoms [ceil(rows/128), K/64, 512]) of BF16 ``x``
+    under ``global = 1 / input_scale`` (FP32)."""
+    _rowmajor(x, "x")
+    rows, K = x.shape
+    codes = torch.empty(rows, K // 2, dtype=torch.uint8, device=x.device)
+    atoms = torch.empty((rows + 127) // 128, K // 64, 512, dtype=torch.uint8, device=x.device)
+    glob = float(torch.tensor(1.0, dtype=torch.float32) / torch.tensor(input_scale, dtype=torch.float32))
+    native().ops.quantize_nvfp4_act(x.data_ptr(), x.stride(0), rows, K, glob, codes.data_ptr(),
+                                    codes.stride(0), atoms.data_ptr(), _stream())
+    return codes, atoms
 
 
 def quantize_fp8_block(w: torch.Tensor) -> QuantizedWeight:
@@ -97,14 +130,20 @@ def gemm(
     _rowmajor(a, "a")
     M, K = a.shape
     quant = isinstance(w, QuantizedWeight)
+    a_ptr, lda = a.data_ptr(), a.stride(0)
     if quant:
         _rowmajor(w.codes, "codes")
         N = w.rows
         if w.cols != K:
             raise ValueError("inner dimensions differ")
-        w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (2 if w.format == "nvfp4" else 1)
+        w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (1 if w.format == "fp8_block" else 2)
         qargs = dict(w_format=w.code, w_scale=w.scales.data_ptr(), w_scale_ld=w.scales.stride(0),
                      w_tensor_scale=float(w.tensor_scale))
+        if w.format == "nvfp4_a4":
+            codes, atoms = quantize_nvfp4_input(a, w.input_scale)
+            keep = (codes, atoms)  # noqa: F841 (alive until the launch is enqueued)
+            a_ptr, lda = codes.data_ptr(), K
+            qargs.update(a_scale=atoms.data_ptr(), w_tensor_scale=_f32(_f32(w.input_scale) * _f32(w.tensor_scale)))
     else:
         _rowmajor(w, "w")
         if w.dtype != torch.bfloat16:
@@ -124,7 +163,7 @@ def gemm(
         _rowmajor(residual, "residual")
     s = scratch(a.device)
     native().ops.gemm(
-        a.data_ptr(), a.stride(0), w_ptr, ldw, M, N, K,
+        a_ptr, lda, w_ptr, ldw, M, N, K,
         out.data_ptr(), out.stride(0), _ptr(residual), 0 if residual is None else residual.stride(0),
         epilogue, mode, splits, s.workspace.data_ptr(), s.workspace.numel() * 4,
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),

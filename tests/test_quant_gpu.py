@@ -108,3 +108,67 @@ def test_quantized_gemm_f32_epilogue():
     out = ops.gemm(a, q, epilogue=ops.EPI_F32)
     torch.cuda.synchronize()
     _close(out, (a.float() @ deq.T) * factor, 1e-3)
+
+
+# ------------------------------------------------------------------ W4A4 on the block-scaled MMA
+
+
+@pytest.mark.parametrize("rows,K", [(1, 256), (77, 512), (300, 1024)])
+def test_nvfp4_input_quantizer_bitwise(rows, K):
+    ops = _ops()
+    torch.manual_seed(rows + K)
+    x = torch.randn(rows, K, device="cuda", dtype=torch.bfloat16)
+    input_scale = float(x.float().abs().max()) / (6 * 448) * 1.3
+    codes, atoms = ops.quantize_nvfp4_input(x, input_scale)
+    torch.cuda.synchronize()
+    ref_codes, ref_s8 = R.nvfp4_quantize_input(x, input_scale)
+    assert torch.equal(codes, ref_codes)
+    assert torch.equal(atoms, R.nvfp4_scale_atoms(ref_s8))
+
+
+def test_nvfp4_scale_atoms():
+    ops = _ops()
+    q = ops.quantize_nvfp4(torch.randn(200, 512, device="cuda", dtype=torch.bfloat16))
+    w4 = ops.nvfp4_w4a4(q, 0.01)
+    torch.cuda.synchronize()
+    assert torch.equal(w4.scales, R.nvfp4_scale_atoms(q.scales))
+
+
+@pytest.mark.parametrize(
+    "M,N,K,mode,epi",
+    [
+        (1, 256, 1024, 2, 0),
+        (48, 512, 2048, 2, 0),
+        (100, 768, 1024, 2, 0),
+        (200, 1024, 2048, 2, 0),
+        (64, 4096, 4096, 2, 1),
+        (512, 768, 1024, 1, 0),
+        (1024, 2048, 4096, 1, 0),
+        (32, 1536, 1024, 2, 2),
+        (160, 1536, 1024, 2, 2),
+        (384, 1536, 1024, 1, 2),
+    ],
+)
+def test_nvfp4_w4a4_gemm(M, N, K, mode, epi):
+    ops = _ops()
+    torch.manual_seed(M + N + K)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    input_scale = float(a.float().abs().max()) / (6 * 448)
+    q = ops.quantize_nvfp4(w)
+    w4 = ops.nvfp4_w4a4(q, input_scale)
+    out = ops.gemm(a, w4, epilogue=epi, mode=mode)
+    torch.cuda.synchronize()
+    ops.scratch().check()
+    ac, as8 = R.nvfp4_quantize_input(a, input_scale)
+    a_deq = R.nvfp4_dequantize(ac, as8)
+    w_deq = R.nvfp4_dequantize(q.codes, q.scales)
+    alpha = float(torch.tensor(w4.input_scale, dtype=torch.float32) * torch.tensor(q.tensor_scale, dtype=torch.float32))
+    full = (a_deq @ w_deq.T) * alpha
+    if epi == 2:
+        blocks = full.view(M, -1, 2, 128)
+        inter = N // 2
+        ref = R.swiglu(blocks[:, :, 0].reshape(M, inter), blocks[:, :, 1].reshape(M, inter))
+    else:
+        ref = full
+    _close(out, ref, 1e-2 if epi != 1 else 1e-4)
