@@ -69,11 +69,16 @@ struct KParams {
   const uint8_t* sf_q;
   long sf_stride_p, sf_stride_q;
   int sf_blocks_q;            // 128-row blocks of the N side's atoms
+  // FP8 W8A8 (kWF == kWFp8A8): activation scales [K/128][ascale_ld] (transposed per k-block).
+  const float* ascale;
+  long ascale_ld;
 };
 
 // Weight formats a GEMM reads: BF16; FP8 block-scaled or NVFP4 codes dequantized to BF16 in
 // shared memory (BF16 activations); NVFP4 codes of both operands on the block-scaled MMA.
-enum : int { kWBf16 = 0, kWFp8Block = 1, kWNvfp4 = 2, kWNvfp4A4 = 3 };
+// FP8 codes of both operands on the FP8 MMA, each 128-input block's sum scaled by the
+// epilogue warps before the blocks add (W8A8).
+enum : int { kWBf16 = 0, kWFp8Block = 1, kWNvfp4 = 2, kWNvfp4A4 = 3, kWFp8A8 = 4 };
 
 // Eight E4M3 codes times their block scale, rounded to BF16.
 __device__ __forceinline__ uint4 dequant_fp8x8(uint2 v, float scale) {
@@ -131,7 +136,9 @@ struct Cfg {
   static constexpr int kQGroups = (kBN + 127) / 128;
   static constexpr int kSfBytes = kWF == kWNvfp4A4 ? (kMB + kQGroups) * 2048 : 0;
   static constexpr int kSfCols = kWF == kWNvfp4A4 ? 16 * (kMB + kQGroups) : 0;
-  static constexpr int kBoxX = kWF == kWNvfp4A4 ? 128 : 64;  // TMA x extent of a k-block
+  static constexpr int kBoxX = (kWF == kWNvfp4A4 || kWF == kWFp8A8) ? 128 : 64;  // TMA x of a k-block
+  // W8A8: the FP32 activation scales of one k-block for the tile's tokens.
+  static constexpr int kAscBytes = kWF == kWFp8A8 ? 4 * (kBN > 128 ? kBN : 128) : 0;
   static constexpr int kAccCols = kMB * kBN;
   static constexpr int kSfCol0 = kAcc * kAccCols;
   static constexpr int kColsRaw = kAcc * kAccCols + kSfCols;
@@ -141,8 +148,10 @@ struct Cfg {
                                    : kColsRaw <= 256 ? 256
                                                      : 512;
   static constexpr int kBarrierBytes = 512;
-  static constexpr int kSmemBytes = kStages * (kStageBytes + kRawBytes + kSfBytes) + kBarrierBytes + 1024;
-  static constexpr int kThreadsCta = (kWF == kWFp8Block || kWF == kWNvfp4) ? 320 : 192;
+  static constexpr int kSmemBytes =
+      kStages * (kStageBytes + kRawBytes + kSfBytes + kAscBytes) + kBarrierBytes + 1024;
+  // Converter warps (kWF 1, 2) or a second stream of scaling warps (kWF 4) take warps 6-9.
+  static constexpr int kThreadsCta = (kWF == kWFp8Block || kWF == kWNvfp4 || kWF == kWFp8A8) ? 320 : 192;
   static_assert(kColsRaw <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 232448, "stages exceed shared memory");
   static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "invalid MMA N");
@@ -252,12 +261,14 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* raw = smem + kStages * C::kStageBytes;  // quantized weight ring (kWF 1, 2)
   uint8_t* sfr = raw + kStages * C::kRawBytes;      // scale-atom ring (kWF 3)
-  uint64_t* full = reinterpret_cast<uint64_t*>(sfr + kStages * C::kSfBytes);
+  uint8_t* asr = sfr + kStages * C::kSfBytes;       // activation-scale ring (kWF 4)
+  uint64_t* full = reinterpret_cast<uint64_t*>(asr + kStages * C::kAscBytes);
   uint64_t* empty = full + kStages;
   uint64_t* rawfull = empty + kStages;
   uint64_t* tfull = rawfull + kStages;
   uint64_t* tempty = tfull + kAcc;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + kAcc);
+  uint64_t* xfer = tempty + kAcc;  // W8A8: odd-block stream's sum ready / taken (two barriers)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(xfer + 2);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -270,14 +281,17 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     for (int s = 0; s < kStages; ++s) {
       // A stage is full when its TMA bytes land and, for quantized weights, the four converter
       // warps have written the weight tile.
-      mbar_init(full + s, (kWF == kWBf16 || kWF == kWNvfp4A4) ? 1 : 5);
-      mbar_init(empty + s, 1);
+      mbar_init(full + s, (kWF == kWFp8Block || kWF == kWNvfp4) ? 5 : 1);
+      // W8A8: a stage is free once its MMAs completed and the eight scaling warps read its scales.
+      mbar_init(empty + s, kWF == kWFp8A8 ? 9 : 1);
       mbar_init(rawfull + s, 1);
     }
     for (int b = 0; b < kAcc; ++b) {
       mbar_init(tfull + b, 1);
-      mbar_init(tempty + b, 128);
+      mbar_init(tempty + b, kWF == kWFp8A8 ? 256 : 128);  // W8A8: both scaling streams
     }
+    mbar_init(xfer, 128);
+    mbar_init(xfer + 1, 128);
     *abort = 0;
     fence_barrier_init();
   }
@@ -321,7 +335,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       };
       auto load_w = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
-        if constexpr (kWF == kWBf16 || kWF == kWNvfp4A4) {
+        if constexpr (kWF == kWBf16 || kWF == kWNvfp4A4 || kWF == kWFp8A8) {
           if (p.swap)
             tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
           else
@@ -341,9 +355,16 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         else
           tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
         if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap == 0);
+        if constexpr (kWF == kWFp8A8) {
+          if (p.swap)
+            bulk_load(asr + s * C::kAscBytes, p.ascale + (long)kb * p.ascale_ld + tq * kBN, kBN * 4, full + s);
+          else
+            bulk_load(asr + s * C::kAscBytes, p.ascale + (long)kb * p.ascale_ld + tp * 128, 512, full + s);
+        }
       };
       const uint32_t full_bytes = kWF == kWBf16      ? C::kStageBytes
                                   : kWF == kWNvfp4A4 ? C::kStageBytes + C::kSfBytes
+                                  : kWF == kWFp8A8   ? C::kStageBytes + (p.swap ? kBN * 4 : 512)
                                                      : (p.swap ? C::kQBytes : C::kPBytes);
       // The first stages' weight tiles do not depend on earlier kernels: issue them before
       // waiting for the previous kernel (PDL), then their activation tiles after it.
@@ -389,6 +410,46 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         const uint32_t first = it > (uint32_t)kStages ? it - kStages : 0;
         for (uint32_t j = first; j < it; ++j)
           mbar_wait(full + (j % kStages), (j / kStages) & 1, p.status, kTimeoutDrain, nullptr);
+      }
+    }
+  } else if (kWF == kWFp8A8 && warp == 1) {
+    // ----------------------------------------------------------------- MMA issuer (W8A8)
+    // One 128-input block at a time into alternating TMEM buffers: the epilogue warps scale each
+    // block's sum before the blocks add.
+    if (elect_one()) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, kBN);
+      uint32_t it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+        const int split = u % p.splits;
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          const int b = it % kAcc;
+          const uint32_t bph = (it / kAcc) & 1;
+          if (!mbar_wait(tempty + b, bph ^ 1, p.status, kTimeoutTmemEmpty, abort) ||
+              !mbar_wait(full + s, ph, p.status, kTimeoutTmaFull, abort)) {
+            ok = false;
+            break;
+          }
+          if (it == 0) mark(p, 3);
+          tc_fence_after();
+          const uint8_t* st = smem + s * C::kStageBytes;
+          const uint32_t d0 = tmem_base + b * C::kAccCols;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = sdesc_kmajor_sw128(st + C::kPBytes + kk * 32);
+#pragma unroll
+            for (int mb = 0; mb < kMB; ++mb)
+              mma_e4m3(d0 + mb * kBN, sdesc_kmajor_sw128(st + mb * 16384 + kk * 32), bdesc, idesc,
+                       kk > 0 ? 1u : 0u);
+          }
+          mma_commit(empty + s);
+          mma_commit(tfull + b);
+        }
+        if (u == (int)blockIdx.x) mark(p, 4);
       }
     }
   } else if (warp == 1) {
@@ -522,12 +583,113 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     const int lrow = q * 32 + lane;
     pdl_wait();  // the residual and the output may be earlier kernels' memory
     uint32_t tc = 0;
+    uint32_t kit = 0;  // W8A8: k-blocks consumed (stage and buffer sequence of the MMA warp)
+    uint32_t xfer_count = 0;  // W8A8: hand-overs between the two scaling streams
     for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tc) {
       const int tile = u / p.splits, split = u % p.splits;
       const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
-      const int b = tc % kAcc;
-      const uint32_t aph = (tc / kAcc) & 1;
-      if (!mbar_wait(tfull + b, aph, p.status, kTimeoutTmemFull, abort)) break;
+      int b = tc % kAcc;
+      if constexpr (kWF == kWFp8A8) {
+        // Each 128-input block's FP32 sum times its combined activation and weight scale, added in
+        // block order in registers by two streams of four warps that split the tile: warps 2-5
+        // take the first half of the columns (or the first M block), warps 6-9 the rest. The odd
+        // stream stores its half of the total into the last block's buffer and hands over; the
+        // even stream then runs the epilogue below over the whole tile.
+        const int stream = warp >= 6 ? 1 : 0;
+        constexpr int kCnt = kMB == 2 ? kBN : kBN / 2;  // values a thread sums
+        const int mb_s = kMB == 2 ? stream : 0;
+        const int c_s = kMB == 2 ? 0 : stream * kCnt;
+        const uint32_t col_s = mb_s * kBN + c_s;        // first TMEM column of this stream
+        const int kb0 = split * p.kb_per_split;
+        const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
+        float acc[kCnt];
+#pragma unroll
+        for (int c = 0; c < kCnt; ++c) acc[c] = 0.f;
+        const float* wsc = static_cast<const float*>(p.wscale);
+        const long wrow = (long)(p.swap ? tp * kMB + mb_s : tq) * p.wscale_ld;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++kit) {
+          const int s = kit % kStages;
+          const uint32_t ph = (kit / kStages) & 1;
+          b = kit % kAcc;
+          const uint32_t bph = (kit / kAcc) & 1;
+          const float sw = __ldg(wsc + wrow + kb);
+          int got = 1;
+          if (lane == 0)
+            got = mbar_wait(tfull + b, bph, p.status, kTimeoutTmemFull, abort) &&
+                  mbar_wait(full + s, ph, p.status, kTimeoutTmaFull, abort);
+          if (!__shfl_sync(0xffffffffu, got, 0)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // TMEM loads go out in batches with one wait each: the round trips bound this loop.
+          const float* asc = reinterpret_cast<const float*>(asr + s * C::kAscBytes);
+          const float srow = p.swap ? 0.f : asc[lrow] * sw;
+          const uint32_t tb = tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols + col_s;
+          constexpr int kBatch = kCnt >= 32 ? 32 : kCnt;
+#pragma unroll
+          for (int c0 = 0; c0 < kCnt; c0 += kBatch) {
+            uint32_t r[kBatch];
+            if constexpr (kBatch == 32)
+              tmem_ld_32x32b_x32(tb + c0, *reinterpret_cast<uint32_t(*)[32]>(r));
+            else
+              tmem_ld_32x32b_x16(tb + c0, *reinterpret_cast<uint32_t(*)[16]>(r));
+            float sc[kBatch];
+            if (p.swap) {
+#pragma unroll
+              for (int t = 0; t < kBatch; t += 4) {
+                const float4 a4 = *reinterpret_cast<const float4*>(asc + c_s + c0 + t);
+                sc[t] = a4.x * sw;
+                sc[t + 1] = a4.y * sw;
+                sc[t + 2] = a4.z * sw;
+                sc[t + 3] = a4.w * sw;
+              }
+            } else {
+#pragma unroll
+              for (int t = 0; t < kBatch; ++t) sc[t] = srow;
+            }
+            tmem_ld_wait();
+#pragma unroll
+            for (int t = 0; t < kBatch; ++t) acc[c0 + t] = fmaf(__uint_as_float(r[t]), sc[t], acc[c0 + t]);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(empty + s);
+          if (kb + 1 < kb1) {
+            tc_fence_before();
+            mbar_arrive(tempty + b);
+          }
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c0 = 0; c0 < kCnt; c0 += 16) {
+          uint32_t r[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) r[t] = __float_as_uint(acc[c0 + t]);
+          tmem_st_32x32b_x16(tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols + col_s + c0, r);
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        const uint32_t xph = xfer_count & 1;
+        ++xfer_count;
+        if (stream == 1) {
+          // Hand over, release the buffer (the even stream releases it too), and wait until the
+          // hand-over was taken so that the two barriers never run a phase ahead.
+          mbar_arrive(xfer);
+          mbar_arrive(tempty + b);
+          int taken = 1;
+          if (lane == 0) taken = mbar_wait(xfer + 1, xph, p.status, kTimeoutTmemFull, abort);
+          if (!__shfl_sync(0xffffffffu, taken, 0)) break;
+          continue;
+        }
+        int ready = 1;
+        if (lane == 0) ready = mbar_wait(xfer, xph, p.status, kTimeoutTmemFull, abort);
+        if (!__shfl_sync(0xffffffffu, ready, 0)) break;
+        mbar_arrive(xfer + 1);
+      } else {
+        const uint32_t aph = (tc / kAcc) & 1;
+        if (!mbar_wait(tfull + b, aph, p.status, kTimeoutTmemFull, abort)) break;
+      }
       if (tc == 0 && lrow == 0) mark(p, 5);
       tc_fence_after();
       const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols;
@@ -649,7 +811,13 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       const int lrow = q * 32 + lane;
       const int S = p.splits;
       const int split = blockIdx.x % S;
-      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16);
+      // One unit per CTA here: its accumulator is buffer 0, or (W8A8) its last k-block's buffer.
+      int bsel = 0;
+      if constexpr (kWF == kWFp8A8) {
+        const int kb0 = split * p.kb_per_split;
+        bsel = (min(kb0 + p.kb_per_split, p.kblocks) - kb0 - 1) % kAcc;
+      }
+      const uint32_t tbase = tmem_base + (uint32_t(q * 32) << 16) + bsel * C::kAccCols;
       const uint32_t red = smem_u32(smem);
       for (int mb = 0; mb < kMB; ++mb) {
         int owner, rl, rs, half;
@@ -762,16 +930,19 @@ struct Shape {
   static constexpr int kStage = 128 * kMB * 128 + kBN * 128;
   static constexpr int kRaw = (kMB * 128 > kBN ? kMB * 128 : kBN) * (kWF == 1 ? 64 : kWF == 2 ? 32 : 0);
   static constexpr int kSfGroups = kWF == 3 ? kMB + (kBN + 127) / 128 : 0;
-  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw + kSfGroups * 2048);
+  static constexpr int kAsc = kWF == 4 ? 4 * (kBN > 128 ? kBN : 128) : 0;
+  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw + kSfGroups * 2048 + kAsc);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
-  static constexpr int kAcc = kMB * kBN * 2 + 16 * kSfGroups <= 512 ? 2 : 1;
+  // W8A8 keeps up to eight per-block partial sums in flight so the MMAs run ahead of the scaling.
+  static constexpr int kAccW8 = 512 / (kMB * kBN) > 8 ? 8 : 512 / (kMB * kBN);
+  static constexpr int kAcc = kWF == 4 ? kAccW8 : kMB * kBN * 2 + 16 * kSfGroups <= 512 ? 2 : 1;
 };
 
 // Bytes of the operand ring of a swap-mapping configuration (the cluster reduction reuses it).
 int swap_ring_bytes(int mb, int kbn, int wf) {
   const int stage = 128 * mb * 128 + kbn * 128;
   const int raw = (mb * 128 > kbn ? mb * 128 : kbn) * (wf == 1 ? 64 : wf == 2 ? 32 : 0);
-  const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : 0;
+  const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : wf == 4 ? 4 * std::max(kbn, 128) : 0;
   int stages = (220 * 1024 - 2048) / (stage + raw + sf);
   if (stages > 8) stages = 8;
   return stage * stages;
@@ -783,15 +954,17 @@ int cluster_limit_of(int mb, int kbn, int epi, int size);
 Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len,
                ClusterLimit cluster_limit = cluster_limit_of) {
   Plan pl{};
-  const bool swap = a.mode == kModeSwap || (a.mode == kModeAuto && a.M <= 256);
+  // W8A8 SwiGLU runs on the swap mapping at every row count (its rows tiles hold 128 columns).
+  const bool swap = a.mode == kModeSwap || (a.mode == kModeAuto && a.M <= 256) ||
+                    (a.w_format == kWFp8A8 && a.epilogue == kEpiSwiGLU);
   pl.swap = swap;
-  const int kelems = a.w_format == kWNvfp4A4 ? 256 : kBlockK;  // K elements of one stage
+  const int kelems = a.w_format == kWNvfp4A4 ? 256 : a.w_format == kWFp8A8 ? 128 : kBlockK;
   pl.kblocks = (a.K + kelems - 1) / kelems;
   if (!swap) {
     pl.mb = 1;
-    pl.kbn = 256;
+    pl.kbn = a.w_format == kWFp8A8 ? 128 : 256;  // W8A8 sums a tile row in registers
     pl.tiles_p = (a.M + 127) / 128;
-    pl.tiles_q = (a.N + 255) / 256;
+    pl.tiles_q = (a.N + pl.kbn - 1) / pl.kbn;
   } else {
     pl.mb = a.epilogue == kEpiSwiGLU ? 2 : 1;
     pl.kbn = pick_swap_bn(a.M);
@@ -801,6 +974,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
       pl.kbn = std::max(pl.kbn, 64);
       if (pl.mb == 2) pl.kbn = std::min(pl.kbn, 128);
     }
+    if (a.w_format == kWFp8A8) pl.kbn = std::max(32, std::min(pl.kbn, pl.mb == 2 ? 64 : 128));
     pl.tiles_p = (a.N + 128 * pl.mb - 1) / (128 * pl.mb);
     pl.tiles_q = (a.M + pl.kbn - 1) / pl.kbn;
   }
@@ -978,6 +1152,40 @@ int launch_swap_nvf4(int epi, const CUtensorMap& tp, const CUtensorMap& tq, cons
   }
 }
 
+// W8A8 configurations: swap N tiles of 32..128 (two M blocks: up to 64), rows 128 x 128.
+int launch_swap_fp8(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+                    const KParams& kp, const Plan& pl, cudaStream_t stream) {
+  constexpr int W = kWFp8A8;
+  if (pl.mb == 2) {
+    if (epi != kEpiSwiGLU) return -2;
+    switch (pl.kbn) {
+      case 32: return launch_red<2, 32, kEpiSwiGLU, W>(tp, tq, tw, kp, pl, stream);
+      default: return launch_red<2, 64, kEpiSwiGLU, W>(tp, tq, tw, kp, pl, stream);
+    }
+  }
+  switch (pl.kbn) {
+    case 32: return launch_plain_epi<1, 32, W>(epi, tp, tq, tw, kp, pl, stream);
+    case 64: return launch_plain_epi<1, 64, W>(epi, tp, tq, tw, kp, pl, stream);
+    default: return launch_plain_epi<1, 128, W>(epi, tp, tq, tw, kp, pl, stream);
+  }
+}
+
+int cluster_limit_fp8(int mb, int kbn, int epi, int size) {
+  constexpr int W = kWFp8A8;
+  if (mb == 2) {
+    switch (kbn) {
+      case 32: return max_active_clusters<2, 32, kEpiSwiGLU, W>(size);
+      default: return max_active_clusters<2, 64, kEpiSwiGLU, W>(size);
+    }
+  }
+  const bool f32 = epi == kEpiF32;
+  switch (kbn) {
+    case 32: return f32 ? max_active_clusters<1, 32, kEpiF32, W>(size) : max_active_clusters<1, 32, kEpiBf16, W>(size);
+    case 64: return f32 ? max_active_clusters<1, 64, kEpiF32, W>(size) : max_active_clusters<1, 64, kEpiBf16, W>(size);
+    default: return f32 ? max_active_clusters<1, 128, kEpiF32, W>(size) : max_active_clusters<1, 128, kEpiBf16, W>(size);
+  }
+}
+
 int cluster_limit_nvf4(int mb, int kbn, int epi, int size) {
   constexpr int W = kWNvfp4A4;
   if (mb == 2)
@@ -1029,6 +1237,7 @@ int cluster_limit_of(int mb, int kbn, int epi, int size) {
     case kWFp8Block: return cluster_limit_wf<kWFp8Block>(mb, kbn, epi, size);
     case kWNvfp4: return cluster_limit_wf<kWNvfp4>(mb, kbn, epi, size);
     case kWNvfp4A4: return cluster_limit_nvf4(mb, kbn, epi, size);
+    case kWFp8A8: return cluster_limit_fp8(mb, kbn, epi, size);
     default: return cluster_limit_wf<kWBf16>(mb, kbn, epi, size);
   }
 }
@@ -1055,6 +1264,12 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.w_format != kWBf16 && a.w_scale == nullptr) return -2;
   if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
   const bool nvf4 = a.w_format == kWNvfp4A4;
+  const bool fp8 = a.w_format == kWFp8A8;
+  if (fp8) {
+    // E4M3 codes of both operands (one a byte), FP32 activation scales [K/128][a_scale_ld].
+    if (a.K % 128 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.a_scale == nullptr) return -2;
+    if (a.a_scale_ld < ((a.M + 127) / 128) * 128 || (reinterpret_cast<uintptr_t>(a.a_scale) & 15)) return -1;
+  }
   if (nvf4) {
     // Both operands are packed E2M1 codes (two a byte) with 128-row-blocked scale atoms.
     if (a.K % 256 != 0 || a.lda % 32 != 0 || a.ldw % 32 != 0 || a.a_scale == nullptr) return -2;
@@ -1099,6 +1314,10 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     kp.sf_stride_p = kp.sf_stride_q = atoms;
     kp.sf_blocks_q = ((pl.swap ? a.M : a.N) + 127) / 128;
   }
+  if (fp8) {
+    kp.ascale = static_cast<const float*>(a.a_scale);
+    kp.ascale_ld = a.a_scale_ld;
+  }
   if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
 
   CUtensorMap tp, tq, tw;
@@ -1117,8 +1336,9 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   }
   // Operand maps: BF16 rows of 64 elements, or packed E2M1 rows of 128 bytes (256 elements).
   auto operand = [&](CUtensorMap* m, const void* base, long rows, long ld, int box) {
-    return nvf4 ? encode_tmap_u8_kmajor(m, base, rows, a.K / 2, ld / 2, box)
-                : encode_tmap_bf16_kmajor(m, base, rows, a.K, ld, box);
+    if (nvf4) return encode_tmap_u8_kmajor(m, base, rows, a.K / 2, ld / 2, box);
+    if (fp8) return encode_tmap_u8_kmajor(m, base, rows, a.K, ld, box);
+    return encode_tmap_bf16_kmajor(m, base, rows, a.K, ld, box);
   };
   if (!pl.swap) {
     kp.Mp = a.M;
@@ -1131,6 +1351,11 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
       case kWFp8Block: return launch_rows<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
       case kWNvfp4: return launch_rows<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
       case kWNvfp4A4: return launch_rows<kWNvfp4A4>(a.epilogue, tp, tq, tw, kp, pl, stream);
+      case kWFp8A8:
+        if (a.epilogue == kEpiSwiGLU) return -2;
+        return a.epilogue == kEpiF32
+                   ? launch_red<1, 128, kEpiF32, kWFp8A8>(tp, tq, tw, kp, pl, stream)
+                   : launch_red<1, 128, kEpiBf16, kWFp8A8>(tp, tq, tw, kp, pl, stream);
       default: return launch_rows<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
     }
   }
@@ -1143,6 +1368,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     case kWFp8Block: return launch_swap<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);
     case kWNvfp4: return launch_swap<kWNvfp4>(a.epilogue, tp, tq, tw, kp, pl, stream);
     case kWNvfp4A4: return launch_swap_nvf4(a.epilogue, tp, tq, tw, kp, pl, stream);
+    case kWFp8A8: return launch_swap_fp8(a.epilogue, tp, tq, tw, kp, pl, stream);
     default: return launch_swap<kWBf16>(a.epilogue, tp, tq, tw, kp, pl, stream);
   }
 }

@@ -62,7 +62,12 @@ struct GemmArgs {
   const void* w_scale = nullptr;
   long w_scale_ld = 0;
   float w_tensor_scale = 1.0f;
+  //   kWeightFp8A8:    block-scaled FP8 on both operands (W8A8): `a` and `w` hold E4M3 codes,
+  //                    w_scale FP32 [ceil(N/128), w_scale_ld] per 128x128 block, a_scale FP32
+  //                    [K/128, a_scale_ld] per (128-input group, row) with a_scale_ld >= M rounded
+  //                    up to 128 (K % 128 == 0).
   const void* a_scale = nullptr;
+  long a_scale_ld = 0;
 };
 
 enum GemmWeightFormat : int {
@@ -70,6 +75,7 @@ enum GemmWeightFormat : int {
   kWeightFp8Block = 1,
   kWeightNvfp4 = 2,
   kWeightNvfp4A4 = 3,
+  kWeightFp8A8 = 4,
 };
 
 // Plans and launches one GEMM on `stream`. Returns 0, or a negative code for a rejected argument

@@ -36,15 +36,42 @@ __global__ void __launch_bounds__(256) fp8_block_kernel(const __nv_bfloat16* w, 
     if (r < rows && c < cols) m = fmaxf(m, fabsf(__bfloat162float(w[(long)r * cols + c])));
   }
   const float amax = block_max(m, red);
-  const float scale = fmaxf(amax, 1e-10f) / 448.f;
+  const float scale = fmaxf(amax, 1e-10f) * (1.f / 448.f);
   if (threadIdx.x == 0) scales[(long)br * gridDim.x + bc] = scale;
-  const float inv = 1.f / scale;
   for (int i = threadIdx.x; i < 128 * 128; i += 256) {
     const int r = r0 + i / 128, c = c0 + i % 128;
     if (r < rows && c < cols)
       codes[(long)r * cols + c] =
-          __nv_cvt_float_to_fp8(__bfloat162float(w[(long)r * cols + c]) * inv, __NV_SATFINITE, __NV_E4M3);
+          __nv_cvt_float_to_fp8(__bfloat162float(w[(long)r * cols + c]) / scale, __NV_SATFINITE, __NV_E4M3);
   }
+}
+
+// FP8 activations per (row, 128-input group), one warp per group: scale = max(amax, 1e-10) *
+// fl(1/448), code = e4m3_sat(x / scale). Scales land transposed, [K/128][rows_pad], so that the
+// scales of one k-block are contiguous over rows.
+__global__ void fp8_act_kernel(const __nv_bfloat16* x, long ldx, int rows, int K, uint8_t* codes,
+                               long ldc, float* scales, int rows_pad) {
+  pdl_wait();
+  pdl_trigger();
+  const int groups = K / 128;
+  const long wid = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (long)rows * groups) return;
+  const long r = wid / groups;
+  const int g = (int)(wid % groups);
+  const uint2 q = *reinterpret_cast<const uint2*>(x + r * ldx + g * 128 + lane * 4);
+  float v[4] = {__uint_as_float(q.x << 16), __uint_as_float(q.x & 0xFFFF0000u),
+                __uint_as_float(q.y << 16), __uint_as_float(q.y & 0xFFFF0000u)};
+  float m = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  const float scale = fmaxf(m, 1e-10f) * (1.f / 448.f);
+  if (lane == 0) scales[(long)g * rows_pad + r] = scale;
+  uint32_t packed = 0;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    packed |= (uint32_t)__nv_cvt_float_to_fp8(v[i] / scale, __NV_SATFINITE, __NV_E4M3) << (8 * i);
+  *reinterpret_cast<uint32_t*>(codes + r * ldc + g * 128 + lane * 4) = packed;
 }
 
 __global__ void absmax_kernel(const __nv_bfloat16* x, long n, float* out) {
@@ -168,6 +195,19 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
   dim3 grid((cols + 127) / 128, (rows + 127) / 128);
   return launch_pdl(fp8_block_kernel, grid, dim3(256), 0, stream, w, rows, cols, codes, scales) ==
                  cudaSuccess
+             ? 0
+             : -5;
+}
+
+int quantize_fp8_act(const __nv_bfloat16* x, long ldx, int rows, int K, uint8_t* codes, long ldc,
+                     float* scales, int rows_pad, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (K % 128 != 0 || ldx % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 7) || ldc % 4 != 0 ||
+      rows_pad < rows)
+    return -2;
+  const long warps = (long)rows * (K / 128);
+  return launch_pdl(fp8_act_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, stream,
+                    x, ldx, rows, K, codes, ldc, scales, rows_pad) == cudaSuccess
              ? 0
              : -5;
 }

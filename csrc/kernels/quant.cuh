@@ -10,7 +10,7 @@ namespace foa {
 
 // Block-scaled FP8: W [rows, cols] BF16 -> E4M3 codes [rows, cols] and FP32 scales
 // [ceil(rows/128), ceil(cols/128)] with one scale per 128x128 block:
-// scale = max(amax(block), 1e-10) / 448, code = e4m3_rne(w / scale) saturated to +-448.
+// scale = max(amax(block), 1e-10) * fl(1/448), code = e4m3_rne(w / scale) saturated to +-448.
 int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, float* scales,
                        cudaStream_t stream);
 
@@ -21,6 +21,12 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
 // amax(W) (absmax_bf16 computes it); `tensor_scale`, when not null, receives 1 / global.
 int quantize_nvfp4(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, uint8_t* scales,
                    const float* amax, float* tensor_scale, cudaStream_t stream);
+
+// FP8 activations per (row, 128-input group), the W8A8 input form of the block-scaled FP8 GEMM:
+// scale = max(amax, 1e-10) * fl(1/448), codes [rows, K] E4M3 (row stride ldc bytes), scales FP32
+// [K/128][rows_pad] (rows_pad >= rows; entries past `rows` are not written).
+int quantize_fp8_act(const __nv_bfloat16* x, long ldx, int rows, int K, uint8_t* codes, long ldc,
+                     float* scales, int rows_pad, cudaStream_t stream);
 
 // NVFP4 activations under a fixed tensor scale `global` (1 / the checkpoint's input_scale), the
 // W4A4 input form of the block-scaled GEMM: codes [rows, K/2] (row stride ldc bytes) and scales as

@@ -34,9 +34,11 @@ void bind_ops(py::module_& m) {
       [](uint64_t a, long lda, uint64_t w, long ldw, int M, int N, int K, uint64_t c, long ldc,
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
          uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
-         int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale) {
+         int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
+         long a_scale_ld) {
         foa::GemmArgs g;
         g.a_scale = as_ptr<void>(a_scale);
+        g.a_scale_ld = a_scale_ld;
         g.w_format = w_format;
         g.w_scale = as_ptr<void>(w_scale);
         g.w_scale_ld = w_scale_ld;
@@ -69,7 +71,21 @@ void bind_ops(py::module_& m) {
       py::arg("epilogue"), py::arg("mode"), py::arg("splits"), py::arg("ws"),
       py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
       py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
-      py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0);
+      py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0,
+      py::arg("a_scale_ld") = 0);
+
+  m.def(
+      "quantize_fp8_act",
+      [](uint64_t x, long ldx, int rows, int K, uint64_t codes, long ldc, uint64_t scales,
+         int rows_pad, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::quantize_fp8_act(as_ptr<const __nv_bfloat16>(x), ldx, rows, K,
+                                    as_ptr<uint8_t>(codes), ldc, as_ptr<float>(scales), rows_pad,
+                                    as_stream(stream)),
+              "quantize_fp8_act");
+      },
+      py::arg("x"), py::arg("ldx"), py::arg("rows"), py::arg("K"), py::arg("codes"), py::arg("ldc"),
+      py::arg("scales"), py::arg("rows_pad"), py::arg("stream"));
 
   m.def(
       "quantize_nvfp4_act",

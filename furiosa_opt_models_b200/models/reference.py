@@ -117,9 +117,35 @@ def fp8_block_quantize(w: torch.Tensor):
     amax = wf.view(br, 128, bc, 128).abs().amax(dim=(1, 3))
     # Tensor-by-tensor divisions: PyTorch divides by a Python scalar as a product with its
     # reciprocal on CUDA, which is not the correctly rounded quotient the kernels compute.
-    scales = torch.clamp(amax, min=1e-10) / torch.full_like(amax, E4M3_MAX)
-    inv = (torch.ones_like(scales) / scales).repeat_interleave(128, 0).repeat_interleave(128, 1)[:rows, :cols]
-    return _e4m3(w.float() * inv), scales
+    scales = torch.clamp(amax, min=1e-10) * torch.full_like(amax, 1.0 / E4M3_MAX)
+    s = scales.repeat_interleave(128, 0).repeat_interleave(128, 1)[:rows, :cols]
+    return _e4m3(w.float() / s), scales
+
+
+def fp8_quantize_input(x: torch.Tensor):
+    """W8A8 inputs per (row, 128-input group): scale = max(amax, 1e-10) * fl(1/448), codes
+    e4m3_sat(x / scale) -> (codes uint8 [rows, K], FP32 scales [rows, K/128])."""
+    rows, K = x.shape
+    xf = x.float().view(rows, K // 128, 128)
+    amax = xf.abs().amax(-1)
+    scales = torch.clamp(amax, min=1e-10) * torch.full_like(amax, 1.0 / E4M3_MAX)
+    return _e4m3(xf / scales[..., None]).view(rows, K), scales
+
+
+def fp8_block_w8a8(a: torch.Tensor, codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """The FP8 block contract of one GEMM: each 128-input block's FP32 sum times its activation
+    scale, then its weight scale, the blocks added in order -> FP32 [rows, out]."""
+    ac, asc = fp8_quantize_input(a)
+    av = _e4m3_value(ac)
+    wv = _e4m3_value(codes)
+    rows, K = ac.shape
+    N = codes.shape[0]
+    out = torch.zeros(rows, N, dtype=torch.float32, device=a.device)
+    wsc = scales.repeat_interleave(128, 0)[:N]  # [N, K/128]
+    for g in range(K // 128):
+        part = av[:, g * 128:(g + 1) * 128] @ wv[:, g * 128:(g + 1) * 128].T
+        out += (part * asc[:, g:g + 1]) * wsc[:, g][None, :]
+    return out
 
 
 def fp8_block_dequantize(codes: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:

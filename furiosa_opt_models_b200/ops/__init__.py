@@ -17,6 +17,7 @@ from .kernels import (  # noqa: F401
     W_FP8_BLOCK,
     W_NVFP4,
     W_NVFP4_A4,
+    W_FP8_W8A16,
     QuantizedWeight,
     argmax,
     embedding,
@@ -29,5 +30,6 @@ from .kernels import (  # noqa: F401
     quantize_fp8_block,
     quantize_nvfp4,
     quantize_nvfp4_input,
+    quantize_fp8_input,
     nvfp4_w4a4,
 )

@@ -25,7 +25,7 @@ def _rowmajor(t: torch.Tensor, name: str) -> None:
         raise ValueError(f"{name} must be a 2-D tensor with unit column stride")
 
 
-W_BF16, W_FP8_BLOCK, W_NVFP4, W_NVFP4_A4 = 0, 1, 2, 3
+W_BF16, W_FP8_W8A16, W_NVFP4, W_NVFP4_A4, W_FP8_BLOCK = 0, 1, 2, 3, 4
 
 
 @dataclass
@@ -33,7 +33,9 @@ class QuantizedWeight:
     """A weight [rows, cols] held in a quantized format that the GEMM dequantizes on the fly.
 
     fp8_block: ``codes`` E4M3 as uint8 [rows, cols], ``scales`` FP32 [ceil(rows/128), ceil(cols/128)]
-    (one per 128x128 block, the checkpoint's ``weight_scale_inv``).
+    (one per 128x128 block, the checkpoint's ``weight_scale_inv``); inputs quantize per 128-input
+    group and each block's sum takes its scales (W8A8). fp8_block_w8a16: the same weights
+    dequantized to BF16 in the kernel, BF16 inputs.
     nvfp4: ``codes`` uint8 [rows, cols/2] (two E2M1 codes a byte, lower column in the low nibble),
     ``scales`` E4M3 as uint8 [rows, cols/16], ``tensor_scale`` the FP32 ``weight_scale_2``.
     nvfp4_a4 (W4A4 on the block-scaled MMA): ``codes`` as for nvfp4, ``scales`` the 128-row-blocked
@@ -51,7 +53,8 @@ class QuantizedWeight:
 
     @property
     def code(self) -> int:
-        return {"fp8_block": W_FP8_BLOCK, "nvfp4": W_NVFP4, "nvfp4_a4": W_NVFP4_A4}[self.format]
+        return {"fp8_block": W_FP8_BLOCK, "fp8_block_w8a16": W_FP8_W8A16, "nvfp4": W_NVFP4,
+                "nvfp4_a4": W_NVFP4_A4}[self.format]
 
 
 def _f32(x: float) -> float:
@@ -83,8 +86,20 @@ def quantize_nvfp4_input(x: torch.Tensor, input_scale: float):
     return codes, atoms
 
 
+def quantize_fp8_input(x: torch.Tensor):
+    """W8A8 inputs: (E4M3 codes uint8 [rows, K], FP32 scales [K/128, rows rounded up to 128])."""
+    _rowmajor(x, "x")
+    rows, K = x.shape
+    pad = (rows + 127) // 128 * 128
+    codes = torch.empty(rows, K, dtype=torch.uint8, device=x.device)
+    scales = torch.empty(K // 128, pad, dtype=torch.float32, device=x.device)
+    native().ops.quantize_fp8_act(x.data_ptr(), x.stride(0), rows, K, codes.data_ptr(), codes.stride(0),
+                                  scales.data_ptr(), pad, _stream())
+    return codes, scales
+
+
 def quantize_fp8_block(w: torch.Tensor) -> QuantizedWeight:
-    """Block-scaled FP8 of a BF16 weight on the device (scale = max(amax, 1e-10) / 448)."""
+    """Block-scaled FP8 of a BF16 weight on the device (scale = max(amax, 1e-10) * fl(1/448))."""
     _rowmajor(w, "w")
     w = w.contiguous()
     rows, cols = w.shape
@@ -125,7 +140,9 @@ def gemm(
 
     EPI_BF16 returns BF16 [M, N] (plus ``residual`` before the one rounding), EPI_F32 FP32 [M, N],
     EPI_SWIGLU BF16 [M, N/2] for gate/up weights interleaved in 128-row blocks. A
-    ``QuantizedWeight`` is dequantized to BF16 tile by tile inside the kernel (W8A16 / W4A16).
+    ``QuantizedWeight`` runs in its format's contract: ``fp8_block`` and ``nvfp4_a4`` quantize the
+    inputs and use the FP8 / block-scaled FP4 tensor cores (W8A8, W4A4); ``fp8_block_w8a16`` and
+    ``nvfp4`` dequantize the weights to BF16 tile by tile inside the kernel (W8A16, W4A16).
     """
     _rowmajor(a, "a")
     M, K = a.shape
@@ -136,7 +153,7 @@ def gemm(
         N = w.rows
         if w.cols != K:
             raise ValueError("inner dimensions differ")
-        w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (1 if w.format == "fp8_block" else 2)
+        w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (1 if w.format.startswith("fp8") else 2)
         qargs = dict(w_format=w.code, w_scale=w.scales.data_ptr(), w_scale_ld=w.scales.stride(0),
                      w_tensor_scale=float(w.tensor_scale))
         if w.format == "nvfp4_a4":
@@ -144,6 +161,11 @@ def gemm(
             keep = (codes, atoms)  # noqa: F841 (alive until the launch is enqueued)
             a_ptr, lda = codes.data_ptr(), K
             qargs.update(a_scale=atoms.data_ptr(), w_tensor_scale=_f32(_f32(w.input_scale) * _f32(w.tensor_scale)))
+        elif w.format == "fp8_block":
+            codes, ascales = quantize_fp8_input(a)
+            keep = (codes, ascales)  # noqa: F841
+            a_ptr, lda = codes.data_ptr(), K
+            qargs.update(a_scale=ascales.data_ptr(), a_scale_ld=ascales.stride(0))
     else:
         _rowmajor(w, "w")
         if w.dtype != torch.bfloat16:

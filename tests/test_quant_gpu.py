@@ -2,6 +2,8 @@
 PyTorch restatement, and the tcgen05 GEMM with on-the-fly dequantization (W8A16 / W4A16) against
 an FP32 product with the dequantized weights."""
 
+import dataclasses
+
 import pytest
 import torch
 
@@ -52,8 +54,8 @@ def _weights(fmt, N, K, seed):
     ops = _ops()
     torch.manual_seed(seed)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
-    if fmt == "fp8_block":
-        q = ops.quantize_fp8_block(w)
+    if fmt == "fp8_block_w8a16":
+        q = dataclasses.replace(ops.quantize_fp8_block(w), format=fmt)
         deq = R.fp8_block_dequantize(q.codes, q.scales)
         factor = 1.0
     else:
@@ -63,7 +65,7 @@ def _weights(fmt, N, K, seed):
     return q, deq, factor
 
 
-@pytest.mark.parametrize("fmt", ["fp8_block", "nvfp4"])
+@pytest.mark.parametrize("fmt", ["fp8_block_w8a16", "nvfp4"])
 @pytest.mark.parametrize(
     "M,N,K,mode,splits",
     [
@@ -86,7 +88,7 @@ def test_quantized_gemm(fmt, M, N, K, mode, splits):
     _close(out, (a.float() @ deq.T) * factor)
 
 
-@pytest.mark.parametrize("fmt", ["fp8_block", "nvfp4"])
+@pytest.mark.parametrize("fmt", ["fp8_block_w8a16", "nvfp4"])
 @pytest.mark.parametrize("M,mode", [(16, 2), (128, 2), (384, 1)])
 def test_quantized_swiglu(fmt, M, mode):
     ops = _ops()
@@ -165,6 +167,57 @@ def test_nvfp4_w4a4_gemm(M, N, K, mode, epi):
     w_deq = R.nvfp4_dequantize(q.codes, q.scales)
     alpha = float(torch.tensor(w4.input_scale, dtype=torch.float32) * torch.tensor(q.tensor_scale, dtype=torch.float32))
     full = (a_deq @ w_deq.T) * alpha
+    if epi == 2:
+        blocks = full.view(M, -1, 2, 128)
+        inter = N // 2
+        ref = R.swiglu(blocks[:, :, 0].reshape(M, inter), blocks[:, :, 1].reshape(M, inter))
+    else:
+        ref = full
+    _close(out, ref, 1e-2 if epi != 1 else 1e-4)
+
+
+# ------------------------------------------------------------------ W8A8 on the FP8 tensor cores
+
+
+@pytest.mark.parametrize("rows,K", [(1, 128), (77, 512), (300, 2048)])
+def test_fp8_input_quantizer_bitwise(rows, K):
+    ops = _ops()
+    torch.manual_seed(rows + K)
+    x = torch.randn(rows, K, device="cuda", dtype=torch.bfloat16)
+    x[0, :128] = 0  # an all-zero group keeps its floor scale
+    codes, scales = ops.quantize_fp8_input(x)
+    torch.cuda.synchronize()
+    ref_codes, ref_scales = R.fp8_quantize_input(x)
+    assert torch.equal(codes, ref_codes)
+    assert torch.equal(scales[:, :rows], ref_scales.T)
+
+
+@pytest.mark.parametrize(
+    "M,N,K,mode,epi,splits",
+    [
+        (1, 256, 1024, 2, 0, 0),
+        (16, 512, 2048, 2, 0, 0),
+        (48, 768, 1024, 2, 0, 1),
+        (100, 1024, 2048, 2, 0, 0),
+        (64, 4096, 4096, 2, 1, 0),
+        (200, 640, 1024, 2, 0, 0),
+        (512, 768, 1024, 1, 0, 0),
+        (1000, 2048, 4096, 1, 0, 0),
+        (32, 1536, 1024, 2, 2, 0),
+        (100, 1536, 2048, 2, 2, 0),
+        (700, 1536, 1024, 0, 2, 0),
+    ],
+)
+def test_fp8_w8a8_gemm(M, N, K, mode, epi, splits):
+    ops = _ops()
+    torch.manual_seed(M + N + K)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    q = ops.quantize_fp8_block(w)
+    out = ops.gemm(a, q, epilogue=epi, mode=mode, splits=splits)
+    torch.cuda.synchronize()
+    ops.scratch().check()
+    full = R.fp8_block_w8a8(a, q.codes, q.scales)
     if epi == 2:
         blocks = full.view(M, -1, 2, 128)
         inter = N // 2
