@@ -6,6 +6,7 @@
 
 #include "kernels/attention.cuh"
 #include "kernels/gemm.cuh"
+#include "kernels/quant.cuh"
 #include "kernels/ops.cuh"
 
 namespace foa::engine {
@@ -19,6 +20,7 @@ int64_t next_pow2(int64_t v) {
   return p;
 }
 __nv_bfloat16* bf(const HbmBuffer& b) { return static_cast<__nv_bfloat16*>(b.data()); }
+uint8_t* u8(const HbmBuffer& b) { return static_cast<uint8_t*>(b.data()); }
 int32_t* i32(const HbmBuffer& b, size_t off = 0) {
   return reinterpret_cast<int32_t*>(static_cast<char*>(b.data()) + off);
 }
@@ -166,20 +168,59 @@ void DecoderModel::allocate_weights() {
       plan.push_back({p + "down", {H, inter_l_}});
     }
   }
-  size_t total = 0;
-  std::vector<size_t> offs;
-  for (auto& e : plan) {
-    offs.push_back(total);
+  const std::string& wf = cfg_.weight_format;
+  const int format = wf == "fp8_block" ? foa::kWeightFp8A8
+                     : wf == "nvfp4"   ? foa::kWeightNvfp4
+                     : wf == "nvfp4_a4" ? foa::kWeightNvfp4A4
+                                        : foa::kWeightBf16;
+  if (format == foa::kWeightBf16 && wf != "bf16") throw ValueError("unknown weight format " + wf);
+  auto projection = [](const std::string& name) {
+    const auto dot = name.rfind('.');
+    const std::string leaf = dot == std::string::npos ? name : name.substr(dot + 1);
+    return leaf == "qkv" || leaf == "o" || leaf == "gate_up" || leaf == "down";
+  };
+  // Byte sizes of a slot: [BF16 or codes, scales].
+  auto sizes = [&](const std::string& name, const std::vector<int64_t>& shape) -> std::pair<size_t, size_t> {
     size_t n = 1;
-    for (auto s : e.second) n *= static_cast<size_t>(s);
-    total = align_up(total + n * 2);
+    for (auto s : shape) n *= static_cast<size_t>(s);
+    if (format == foa::kWeightBf16 || !projection(name)) return {n * 2, 0};
+    const int64_t rows = shape[0], cols = shape[1];
+    const int64_t rb = (rows + 127) / 128;
+    if (format == foa::kWeightFp8A8) {
+      if (cols % 128 != 0) throw Unsupported(name + ": FP8 block inputs come in multiples of 128");
+      return {n, static_cast<size_t>(rb * (cols / 128) * 4)};
+    }
+    if (cols % (format == foa::kWeightNvfp4A4 ? 256 : 64) != 0)
+      throw Unsupported(name + ": NVFP4 inputs here come in multiples of " +
+                        std::to_string(format == foa::kWeightNvfp4A4 ? 256 : 64));
+    if (format == foa::kWeightNvfp4) return {n / 2, static_cast<size_t>(rows * (cols / 16))};
+    return {n / 2, static_cast<size_t>(rb * (cols / 64) * 512)};
+  };
+  size_t total = 0;
+  std::vector<std::pair<size_t, size_t>> offs;
+  for (auto& e : plan) {
+    const auto [a, b] = sizes(e.first, e.second);
+    const size_t o0 = total;
+    total = align_up(total + a);
+    const size_t o1 = total;
+    total = align_up(total + b);
+    offs.push_back({o0, b ? o1 : 0});
   }
   arena_ = HbmBuffer(device_, std::max<size_t>(total, 256));
   arena_bytes_ = total;
   for (size_t i = 0; i < plan.size(); ++i) {
     WeightSlot w;
-    w.ptr = reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(arena_.data()) + offs[i]);
+    char* base = static_cast<char*>(arena_.data());
     w.shape = plan[i].second;
+    if (format != foa::kWeightBf16 && projection(plan[i].first)) {
+      w.format = format;
+      w.codes = reinterpret_cast<uint8_t*>(base + offs[i].first);
+      w.scales = base + offs[i].second;
+      const int64_t cols = w.shape[1];
+      w.scale_ld = format == foa::kWeightFp8A8 ? cols / 128 : format == foa::kWeightNvfp4 ? cols / 16 : cols / 64 * 512;
+    } else {
+      w.ptr = reinterpret_cast<__nv_bfloat16*>(base + offs[i].first);
+    }
     weights_[plan[i].first] = w;
   }
   if (cfg_.tied) {
@@ -198,13 +239,46 @@ uint32_t name_tag(const std::string& s) {
 }
 }  // namespace
 
+void DecoderModel::quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv) {
+  auto st = device_.state();
+  const int rows = static_cast<int>(w.shape[0]), cols = static_cast<int>(w.shape[1]);
+  if (w.format == foa::kWeightFp8A8) {
+    if (foa::quantize_fp8_block(src, rows, cols, w.codes, static_cast<float*>(w.scales), st->stream) != 0)
+      st->fail("weight quantization launch failed");
+    return;
+  }
+  // NVFP4: one tensor scale from a fixed magnitude bound (8 standard deviations), the same on
+  // every tensor-parallel shard of the weight; synthetic inputs quantize under a bound of 8.
+  const float bound[2] = {8.f * stdv, 0.f};
+  HbmBuffer amax(device_, 16);
+  st->check_cuda(cudaMemcpyAsync(amax.data(), bound, 8, cudaMemcpyHostToDevice, st->stream), "amax");
+  HbmBuffer rowmajor;
+  uint8_t* sc = static_cast<uint8_t*>(w.scales);
+  if (w.format == foa::kWeightNvfp4A4) {
+    rowmajor = HbmBuffer(device_, static_cast<size_t>(rows) * (cols / 16));
+    sc = static_cast<uint8_t*>(rowmajor.data());
+  }
+  float* amax_p = static_cast<float*>(amax.data());
+  if (foa::quantize_nvfp4(src, rows, cols, w.codes, sc, amax_p, amax_p + 1, st->stream) != 0)
+    st->fail("weight quantization launch failed");
+  if (w.format == foa::kWeightNvfp4A4 &&
+      foa::nvfp4_scale_atoms(sc, cols / 16, rows, cols, static_cast<uint8_t*>(w.scales), st->stream) != 0)
+    st->fail("weight quantization launch failed");
+  float ts = 1.f;
+  st->check_cuda(cudaMemcpyAsync(&ts, amax_p + 1, 4, cudaMemcpyDeviceToHost, st->stream), "tensor scale");
+  st->check_cuda(cudaStreamSynchronize(st->stream), "weight quantization");
+  w.tensor_scale = ts;
+  w.input_scale = 8.f / (6.f * 448.f);
+}
+
 void DecoderModel::init_random(uint64_t seed, float stdv) {
   auto st = device_.state();
   st->activate();
   const int H = cfg_.hidden, D = cfg_.head_dim;
-  HbmBuffer map_rows, map_tags;
+  HbmBuffer map_rows, map_tags, init_tmp;
   for (auto& [name, w] : weights_) {
     if (name == "lm_head" && cfg_.tied) continue;
+    if (w.format != foa::kWeightBf16 && w.codes == nullptr) continue;
     long n = 1;
     for (auto s : w.shape) n *= s;
     if (name.find("norm") != std::string::npos) {
@@ -259,10 +333,16 @@ void DecoderModel::init_random(uint64_t seed, float stdv) {
     }
     st->check_cuda(cudaMemcpyAsync(map_rows.data(), full.data(), rows * 4, cudaMemcpyHostToDevice, st->stream), "init map");
     st->check_cuda(cudaMemcpyAsync(map_tags.data(), tags.data(), rows * 4, cudaMemcpyHostToDevice, st->stream), "init map");
-    if (foa::init_normal_rows(w.ptr, rows, cols, static_cast<const int32_t*>(map_rows.data()),
+    __nv_bfloat16* dst = w.ptr;
+    if (w.format != foa::kWeightBf16) {
+      if (init_tmp.size() < static_cast<size_t>(rows) * cols * 2) init_tmp = HbmBuffer(device_, static_cast<size_t>(rows) * cols * 2);
+      dst = static_cast<__nv_bfloat16*>(init_tmp.data());
+    }
+    if (foa::init_normal_rows(dst, rows, cols, static_cast<const int32_t*>(map_rows.data()),
                               static_cast<const uint32_t*>(map_tags.data()), full_cols, col_offset,
                               stdv, seed, st->stream) != 0)
       st->fail("weight initialisation launch failed");
+    if (w.format != foa::kWeightBf16) quantize_slot(w, dst, stdv);
     // The host maps must outlive their copies.
     st->check_cuda(cudaStreamSynchronize(st->stream), "weight initialisation");
   }
@@ -280,6 +360,13 @@ void DecoderModel::ensure_workspace(int64_t rows, int64_t kept, int64_t splits, 
     ws_q_ = HbmBuffer(device_, R * qh_l_ * D * 2);
     ws_attn_ = HbmBuffer(device_, R * qh_l_ * D * 2);
     ws_act_ = HbmBuffer(device_, std::max<int64_t>(R * inter_l_ * 2, 256));
+    if (cfg_.weight_format != "bf16") {
+      // Quantized inputs of the widest projection input: FP8 codes (1 byte) or NVFP4 codes (half),
+      // FP8 scales [K/128][R] or NVFP4 atoms [R/128][K/64][512] (R a multiple of 128).
+      const int64_t kmax = std::max<int64_t>({H, static_cast<int64_t>(qh_l_) * D, inter_l_});
+      ws_qa_ = HbmBuffer(device_, R * kmax);
+      ws_qs_ = HbmBuffer(device_, std::max<int64_t>(kmax / 128 * R * 4, R * kmax / 16));
+    }
     ws_rows_ = R;
     changed = true;
   }
@@ -444,13 +531,37 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     if (rc != 0) st->fail(std::string(what) + " launch rejected (" + std::to_string(rc) + ")");
     ++kernels;
   };
-  auto gemm = [&](const void* a, long lda, const void* w, int M, int N, int K, void* c, long ldc,
+  auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
                   int epi, const void* res) {
     foa::GemmArgs g;
     g.a = a;
     g.lda = lda;
-    g.w = w;
+    g.w = w.format == foa::kWeightBf16 ? static_cast<const void*>(w.ptr) : w.codes;
     g.ldw = K;
+    g.w_format = w.format;
+    g.w_scale = w.scales;
+    g.w_scale_ld = w.scale_ld;
+    if (w.format == foa::kWeightNvfp4) g.w_tensor_scale = w.tensor_scale;
+    if (w.format == foa::kWeightFp8A8) {
+      // Inputs quantized per (row, 128-input group) ahead of the FP8 MMA.
+      const int pad = (M + 127) / 128 * 128;
+      fail(foa::quantize_fp8_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, u8(ws_qa_), K,
+                                 static_cast<float*>(ws_qs_.data()), pad, s),
+           "input quantization");
+      g.a = ws_qa_.data();
+      g.lda = K;
+      g.a_scale = ws_qs_.data();
+      g.a_scale_ld = pad;
+    } else if (w.format == foa::kWeightNvfp4A4) {
+      // Inputs quantized under the projection's input scale ahead of the block-scaled MMA.
+      fail(foa::quantize_nvfp4_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, 1.f / w.input_scale,
+                                   u8(ws_qa_), K / 2, u8(ws_qs_), s),
+           "input quantization");
+      g.a = ws_qa_.data();
+      g.lda = K;
+      g.a_scale = ws_qs_.data();
+      g.w_tensor_scale = w.input_scale * w.tensor_scale;
+    }
     g.M = M;
     g.N = N;
     g.K = K;
@@ -465,7 +576,8 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     g.counters_len = 32768;  // the first half; the second serves the attention merge
     g.status = st->status;
     if (batch_invariant_) {
-      g.mode = foa::kModeRows;
+      // W8A8 SwiGLU tiles only on the swap mapping; its sums do not depend on the tile shape.
+      g.mode = (w.format == foa::kWeightFp8A8 && epi == foa::kEpiSwiGLU) ? foa::kModeSwap : foa::kModeRows;
       g.splits = 1;
     }
     fail(foa::gemm_bf16(g, s), "gemm");
@@ -477,6 +589,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   __nv_bfloat16* h = coll_ ? coll_->hidden_buffer() : bf(ws_h_);
   const auto& W = weights_;
   auto w = [&](const std::string& n) -> __nv_bfloat16* { return W.at(n).ptr; };
+  auto ws = [&](const std::string& n) -> const WeightSlot& { return W.at(n); };
   const int64_t count = std::max<int64_t>(plan.requests, plan.rows_padded);
 
   // Tokens: padded rows read ID 0 (zeroed by the staging), the requests' IDs are gathered.
@@ -510,7 +623,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "in_norm"), h, H, nullptr, 0, static_cast<int>(T),
                         H, cfg_.eps, s),
            "rmsnorm");
-    gemm(h, H, w(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
+    gemm(h, H, ws(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
          nullptr);
     __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(cache.layers()[l].data());
     fail(foa::qk_norm_rope_cache(bf(ws_qkv_), qkv_cols, static_cast<int>(T), qh_l_, kvh_l_, D,
@@ -533,28 +646,28 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     const std::string next_norm =
         l + 1 < cfg_.layers ? "layers." + std::to_string(l + 1) + ".in_norm" : "final_norm";
     if (!tp) {
-      gemm(ws_attn_.data(), qh_l_ * D, w(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
+      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
            foa::kEpiBf16, x);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
                         H, cfg_.eps, s),
            "rmsnorm");
-      gemm(h, H, w(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
+      gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr);
-      gemm(ws_act_.data(), inter_l_, w(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
+      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
            foa::kEpiBf16, x);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(next_norm), h, H, nullptr, 0, static_cast<int>(T), H,
                         cfg_.eps, s),
            "rmsnorm");
     } else {
       partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
-      gemm(ws_attn_.data(), qh_l_ * D, w(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
+      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
            foa::kEpiF32, nullptr);
       coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
-      gemm(h, H, w(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
+      gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr);
       partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
-      gemm(ws_act_.data(), inter_l_, w(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
+      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
            foa::kEpiF32, nullptr);
       coll_->add_norm(partial, x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
@@ -566,11 +679,11 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   fail(foa::gather_rows(h, H, i32(stage, sg.kept), K, bf(ws_hk_), H, H, s), "gather rows");
   if (cfg_.output == Output::Hidden) return kernels;
   if (cfg_.output == Output::Scores) {
-    gemm(ws_hk_.data(), H, w("score"), K, cfg_.labels, H, ws_logits_.data(), cfg_.labels,
+    gemm(ws_hk_.data(), H, ws("score"), K, cfg_.labels, H, ws_logits_.data(), cfg_.labels,
          foa::kEpiF32, nullptr);
     return kernels;
   }
-  gemm(ws_hk_.data(), H, w("lm_head"), K, vocab_l_, H, ws_logits_.data(), vocab_l_, foa::kEpiF32,
+  gemm(ws_hk_.data(), H, ws("lm_head"), K, vocab_l_, H, ws_logits_.data(), vocab_l_, foa::kEpiF32,
        nullptr);
   const int valid = vocab_end_ - vocab_begin_;
   if (!tp) {

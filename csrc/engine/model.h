@@ -44,6 +44,11 @@ enum class Output { Tokens = 0, Hidden = 1, Scores = 2 };
 
 struct ModelConfig {
   std::string architecture, family, size, precision = "bfloat16";
+  // Weight format of the q/k/v, o, gate/up and down projections: "bf16"; "fp8_block" (E4M3 with an
+  // FP32 scale per 128x128 block, W8A8); "nvfp4" (E2M1 with E4M3 scales per 16 and an FP32 tensor
+  // scale, BF16 inputs: W4A16); "nvfp4_a4" (the same weights, NVFP4 inputs under input_scale:
+  // W4A4 on the block-scaled MMA).
+  std::string weight_format = "bf16";
   int hidden = 0, intermediate = 0, layers = 0, q_heads = 0, kv_heads = 0, head_dim = 128;
   int vocab = 0;
   float eps = 1e-6f;
@@ -81,8 +86,16 @@ class Collectives {
 };
 
 struct WeightSlot {
-  __nv_bfloat16* ptr = nullptr;
-  std::vector<int64_t> shape;  // this rank's shape
+  __nv_bfloat16* ptr = nullptr;  // BF16 weights (null for a quantized projection)
+  std::vector<int64_t> shape;    // this rank's logical shape
+  // A quantized projection (foa::GemmWeightFormat != 0): codes and block scales.
+  int format = 0;
+  uint8_t* codes = nullptr;      // E4M3 [rows, cols] or packed E2M1 [rows, cols/2]
+  void* scales = nullptr;        // FP8: FP32 [ceil(rows/128), scale_ld]; W4A16: E4M3 [rows, cols/16];
+                                 // W4A4: 128-row-blocked atoms [ceil(rows/128), cols/64, 512]
+  long scale_ld = 0;
+  float tensor_scale = 1.f;      // NVFP4 weight_scale_2
+  float input_scale = 1.f;       // W4A4 input_scale
 };
 
 class DecoderModel {
@@ -97,6 +110,8 @@ class DecoderModel {
 
   // Weight slots by engine name ("embed", "layers.3.qkv", ...), this rank's shard.
   const std::map<std::string, WeightSlot>& weights() const { return weights_; }
+  // A slot to fill (checkpoint loading sets the scales of quantized projections).
+  WeightSlot& weight_slot(const std::string& name) { return weights_.at(name); }
   // Fills every weight with N(0, std) (norm weights with 1) from `seed`.
   void init_random(uint64_t seed, float std);
   size_t weight_bytes() const { return arena_bytes_; }
@@ -136,6 +151,8 @@ class DecoderModel {
 
  private:
   void allocate_weights();
+  // Quantizes BF16 weights `src` into the slot's format (synthetic initialisation).
+  void quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv);
   void ensure_workspace(int64_t rows, int64_t kept, int64_t decode_splits, int64_t decode_rows);
   int launch(const Plan& plan, const Cache& cache);  // returns the kernels it launched
   int64_t graph_bucket(int64_t rows) const;
@@ -155,6 +172,8 @@ class DecoderModel {
   int64_t ws_rows_ = 0, ws_kept_ = 0, ws_splits_ = 0, ws_decode_ = 0;
   HbmBuffer ws_x_, ws_h_, ws_qkv_, ws_q_, ws_attn_, ws_act_, ws_hk_, ws_logits_, ws_idx_, ws_val_,
       ws_tokens_, ws_stage_, ws_part_o_, ws_part_lse_, ws_gemm_, ws_counters_, ws_partial_;
+  // Quantized inputs of W8A8 / W4A4 projections: codes and scales of the widest input.
+  HbmBuffer ws_qa_, ws_qs_;
   size_t stage_capacity_ = 0;
   std::vector<uint8_t> host_stage_;
   HostBuffer pinned_stage_[2];

@@ -1,5 +1,8 @@
 #include "registry.h"
 
+#include "kernels/gemm.cuh"
+#include "kernels/quant.cuh"
+
 #include <cmath>
 #include <cstring>
 #include <map>
@@ -329,8 +332,14 @@ Selection select(const LoadOptions& o, const Checkpoint& ck) {
   if (o.adapters && s.implementation->adapters == 0)
     unsupported("adapters", "the " + l.name + " " + m.size + " implementation takes no adapter");
   if (o.quantization) unsupported("quantization", "load-time FP8 quantization of BF16 checkpoints is not served");
-  if (s.implementation->form == "nvfp4" || s.implementation->form == "fp8_block")
-    unsupported("quantization_config", "the " + s.implementation->form + " line loads through its own path");
+  if (s.implementation->form == "fp8_block") s.config.weight_format = "fp8_block";
+  if (s.implementation->form == "nvfp4") {
+    // ModelOpt NVFP4 checkpoints with calibrated input scales run W4A4 on the block-scaled MMA;
+    // without them (or with FOA_NVFP4_W4A16=1) the inputs stay BF16 (W4A16).
+    const char* a16 = std::getenv("FOA_NVFP4_W4A16");
+    const bool inputs = ck.get("model.layers.0.self_attn.q_proj.input_scale") != nullptr;
+    s.config.weight_format = (inputs && !(a16 && a16[0] == '1')) ? "nvfp4_a4" : "nvfp4";
+  }
   if (m.experts > 0) unsupported(l.name, "mixture-of-experts loads run through the expert-parallel path");
   return s;
 }
@@ -442,6 +451,119 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
                        int64_t dst_cols) {
     for (int64_t r = 0; r < n; ++r) s.row(src0 + r, c0, ncols, host.data() + (dst0 + r) * dst_cols);
   };
+  // ---- quantized projections: codes and scales sliced and stacked like the BF16 rows.
+  // One part of a fused projection: rows [r0, r0 + n) and columns [c0, c0 + nc) of the
+  // checkpoint's q/k/v, gate/up, o or down, placed at image rows `dst` (a list of 128-row blocks
+  // or a contiguous range).
+  struct Part {
+    std::string base;          // "model.layers.3.self_attn.q_proj"
+    int64_t rows, cols;        // the checkpoint's logical shape
+    int64_t r0, n;             // source rows
+    std::vector<int64_t> dst;  // destination row of each source row block of 128 (or one entry)
+    bool blocked;              // dst holds one entry per 128 source rows
+  };
+  auto f32_of = [&](const StoredTensor* t, int64_t i) -> float {
+    float f = 0.f;
+    if (t->dtype == StDType::F32) std::memcpy(&f, t->data() + i * 4, 4);
+    else if (t->dtype == StDType::BF16) {
+      uint16_t h;
+      std::memcpy(&h, t->data() + i * 2, 2);
+      const uint32_t b = static_cast<uint32_t>(h) << 16;
+      std::memcpy(&f, &b, 4);
+    } else {
+      invalid(t->file, "a scale of dtype " + std::string(st_dtype_name(t->dtype)) + " does not load");
+    }
+    return f;
+  };
+  auto scalar = [&](const std::string& name) -> float {
+    const StoredTensor* t = ck.get(name);
+    if (!t) {
+      missing.push_back(name);
+      return 1.f;
+    }
+    if (t->numel() != 1) invalid(name, "a tensor scale holds one value");
+    used[name] = true;
+    return f32_of(t, 0);
+  };
+  auto load_quantized = [&](const std::string& slot, const std::vector<Part>& parts, int64_t c0, int64_t nc) {
+    WeightSlot& w = model.weight_slot(slot);
+    const int64_t R = w.shape[0], C = w.shape[1];
+    const bool fp8 = w.format == foa::kWeightFp8A8;
+    const int64_t code_bytes = fp8 ? C : C / 2;
+    std::vector<uint8_t> codes(static_cast<size_t>(R * code_bytes), 0);
+    // FP8: FP32 block scales [R/128][C/128]; NVFP4: E4M3 [R][C/16] (atoms built on the device).
+    std::vector<float> fscales;
+    std::vector<uint8_t> bscales;
+    if (fp8) fscales.assign(static_cast<size_t>((R + 127) / 128 * (C / 128)), 0.f);
+    else bscales.assign(static_cast<size_t>(R * (C / 16)), 0);
+    float tensor_scale = 0.f, input_scale = 0.f;
+    for (const Part& p : parts) {
+      const int64_t src_code_bytes = fp8 ? p.cols : p.cols / 2;
+      const StoredTensor* wt = take(p.base + ".weight", {p.rows, src_code_bytes});
+      if (wt && wt->dtype != (fp8 ? StDType::F8_E4M3 : StDType::U8))
+        invalid(p.base + ".weight", std::string("codes of dtype ") + st_dtype_name(wt->dtype) + " are not " + (fp8 ? "F8_E4M3" : "U8"));
+      auto dst_row = [&](int64_t i) {  // image row of source row r0 + i
+        return p.blocked ? p.dst[i / 128] + i % 128 : p.dst[0] + i;
+      };
+      const int64_t cb0 = fp8 ? c0 : c0 / 2, cbn = fp8 ? nc : nc / 2;
+      if (wt)
+        for (int64_t i = 0; i < p.n; ++i)
+          std::memcpy(codes.data() + dst_row(i) * code_bytes, wt->data() + (p.r0 + i) * src_code_bytes + cb0, cbn);
+      if (fp8) {
+        const StoredTensor* sc = ck.get(p.base + ".weight_scale_inv");
+        std::string sname = p.base + ".weight_scale_inv";
+        if (!sc) {
+          sc = ck.get(p.base + ".weight_scale");
+          sname = p.base + ".weight_scale";
+        }
+        const int64_t srows = (p.rows + 127) / 128, scols = (p.cols + 127) / 128;
+        if (!sc) {
+          missing.push_back(p.base + ".weight_scale_inv");
+          continue;
+        }
+        if (sc->shape != std::vector<int64_t>{srows, scols}) invalid(sname, "not one scale per 128x128 block");
+        if (p.r0 % 128 != 0 || p.n % 128 != 0 || c0 % 128 != 0 || nc % 128 != 0)
+          unsupported(sname, "a shard boundary falls inside a 128x128 scale block");
+        used[sname] = true;
+        for (int64_t i = 0; i < p.n; i += 128)
+          for (int64_t j = 0; j < nc / 128; ++j)
+            fscales[static_cast<size_t>((dst_row(i) / 128) * (C / 128) + j)] =
+                f32_of(sc, (p.r0 + i) / 128 * scols + c0 / 128 + j);
+      } else {
+        const StoredTensor* sc = take(p.base + ".weight_scale", {p.rows, p.cols / 16});
+        if (sc && sc->dtype != StDType::F8_E4M3) invalid(p.base + ".weight_scale", "block scales are F8_E4M3");
+        if (sc)
+          for (int64_t i = 0; i < p.n; ++i)
+            std::memcpy(bscales.data() + dst_row(i) * (C / 16), sc->data() + (p.r0 + i) * (p.cols / 16) + c0 / 16, nc / 16);
+        const float ts = scalar(p.base + ".weight_scale_2");
+        const bool has_in = ck.get(p.base + ".input_scale") != nullptr;
+        const float is = has_in ? scalar(p.base + ".input_scale") : 1.f;
+        if (tensor_scale != 0.f && (ts != tensor_scale || (has_in && is != input_scale)))
+          unsupported(p.base, "fused projections with different tensor scales");
+        tensor_scale = ts;
+        input_scale = is;
+      }
+    }
+    st->check_cuda(cudaMemcpy(w.codes, codes.data(), codes.size(), cudaMemcpyHostToDevice), "weight upload");
+    if (fp8) {
+      st->check_cuda(cudaMemcpy(w.scales, fscales.data(), fscales.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+      return;
+    }
+    w.tensor_scale = tensor_scale;
+    w.input_scale = input_scale;
+    if (w.format == foa::kWeightNvfp4) {
+      st->check_cuda(cudaMemcpy(w.scales, bscales.data(), bscales.size(), cudaMemcpyHostToDevice), "weight upload");
+      return;
+    }
+    HbmBuffer tmp(model.device(), bscales.size());
+    st->check_cuda(cudaMemcpy(tmp.data(), bscales.data(), bscales.size(), cudaMemcpyHostToDevice), "weight upload");
+    if (foa::nvfp4_scale_atoms(static_cast<const uint8_t*>(tmp.data()), C / 16, static_cast<int>(R),
+                               static_cast<int>(C), static_cast<uint8_t*>(w.scales), st->stream) != 0)
+      st->fail("scale repack launch failed");
+    st->check_cuda(cudaStreamSynchronize(st->stream), "scale repack");
+  };
+  const bool quantized = cfg.weight_format != "bf16";
+
   const std::string pre = "model.";
   // Embedding (whole on every chip) and head (this chip's vocabulary rows).
   if (auto* t = take(pre + "embed_tokens.weight", {cfg.vocab, H})) {
@@ -488,9 +610,18 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       Source(t).row(0, 0, H, host.data());
       upload(en + "post_norm");
     }
-    const auto* q = take(hf + "self_attn.q_proj.weight", {static_cast<int64_t>(cfg.q_heads) * D, H});
-    const auto* k = take(hf + "self_attn.k_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
-    const auto* v = take(hf + "self_attn.v_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
+    if (quantized) {
+      const int64_t qr = static_cast<int64_t>(cfg.q_heads) * D, kr = static_cast<int64_t>(cfg.kv_heads) * D;
+      const int64_t ql = static_cast<int64_t>(qh_l) * D, kl = static_cast<int64_t>(kvh_l) * D;
+      load_quantized(en + "qkv",
+                     {Part{hf + "self_attn.q_proj", qr, H, static_cast<int64_t>(qh0) * D, ql, {0}, false},
+                      Part{hf + "self_attn.k_proj", kr, H, static_cast<int64_t>(kvh0) * D, kl, {ql}, false},
+                      Part{hf + "self_attn.v_proj", kr, H, static_cast<int64_t>(kvh0) * D, kl, {ql + kl}, false}},
+                     0, H);
+    }
+    const auto* q = quantized ? nullptr : take(hf + "self_attn.q_proj.weight", {static_cast<int64_t>(cfg.q_heads) * D, H});
+    const auto* k = quantized ? nullptr : take(hf + "self_attn.k_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
+    const auto* v = quantized ? nullptr : take(hf + "self_attn.v_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
     if (q && k && v) {
       image(en + "qkv");
       copy_rows(Source(q), static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D, 0, 0, H, H);
@@ -509,13 +640,32 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
         }
       }
     }
-    if (auto* t = take(hf + "self_attn.o_proj.weight", {H, static_cast<int64_t>(cfg.q_heads) * D})) {
+    if (quantized) {
+      load_quantized(en + "o",
+                     {Part{hf + "self_attn.o_proj", H, static_cast<int64_t>(cfg.q_heads) * D, 0, H, {0}, false}},
+                     static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D);
+    } else if (auto* t = take(hf + "self_attn.o_proj.weight", {H, static_cast<int64_t>(cfg.q_heads) * D})) {
       image(en + "o");
       copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D,
                 static_cast<int64_t>(qh_l) * D);
       upload(en + "o");
     }
-    if (cfg.experts == 0) {
+    if (cfg.experts == 0 && quantized) {
+      // Gate and up rows alternate in 128-row blocks (see the BF16 path below).
+      std::vector<int64_t> gate_dst, up_dst;
+      for (int64_t b = 0; b < inter_l / 128; ++b) {
+        gate_dst.push_back(b * 256);
+        up_dst.push_back(b * 256 + 128);
+      }
+      const int64_t r0 = static_cast<int64_t>(rank) * inter_l;
+      load_quantized(en + "gate_up",
+                     {Part{hf + "mlp.gate_proj", cfg.intermediate, H, r0, inter_l, gate_dst, true},
+                      Part{hf + "mlp.up_proj", cfg.intermediate, H, r0, inter_l, up_dst, true}},
+                     0, H);
+      load_quantized(en + "down", {Part{hf + "mlp.down_proj", H, cfg.intermediate, 0, H, {0}, false}},
+                     static_cast<int64_t>(rank) * inter_l, inter_l);
+    }
+    if (cfg.experts == 0 && !quantized) {
       const auto* g = take(hf + "mlp.gate_proj.weight", {cfg.intermediate, H});
       const auto* u = take(hf + "mlp.up_proj.weight", {cfg.intermediate, H});
       if (g && u) {

@@ -6,6 +6,8 @@
 // file failure to OSError.
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
+
+#include "kernels/gemm.cuh"
 #include <pybind11/stl.h>
 
 #include <cstring>
@@ -131,6 +133,7 @@ ModelConfig model_config_from_dict(const py::dict& d) {
   c.family = get("family", std::string("qwen3"));
   c.size = get("size", std::string("custom"));
   c.precision = get("precision", std::string("bfloat16"));
+  c.weight_format = get("weight_format", std::string("bf16"));
   c.hidden = get("hidden", 0);
   c.intermediate = get("intermediate", 0);
   c.layers = get("layers", 0);
@@ -525,6 +528,19 @@ void bind_engine(py::module_& m) {
       .def("weight", [](const PyDecoder& d, const std::string& name) {
         const auto& w = d.model->weights().at(name);
         return py::make_tuple(reinterpret_cast<uint64_t>(w.ptr), w.shape);
+      })
+      .def("quantized_weight", [](const PyDecoder& d, const std::string& name) -> py::object {
+        const auto& w = d.model->weights().at(name);
+        if (w.format == 0) return py::none();
+        py::dict q;
+        q["format"] = w.format == foa::kWeightFp8A8 ? "fp8_block" : w.format == foa::kWeightNvfp4 ? "nvfp4" : "nvfp4_a4";
+        q["codes"] = reinterpret_cast<uint64_t>(w.codes);
+        q["scales"] = reinterpret_cast<uint64_t>(w.scales);
+        q["scale_ld"] = w.scale_ld;
+        q["tensor_scale"] = w.tensor_scale;
+        q["input_scale"] = w.input_scale;
+        q["shape"] = w.shape;
+        return q;
       })
       .def("weight_names", [](const PyDecoder& d) {
         std::vector<std::string> n;

@@ -63,6 +63,14 @@ CONFIGS: dict[str, dict] = {
 }
 
 
+# Quantized serving configurations: the same geometries with block-scaled FP8 (W8A8) or NVFP4
+# (W4A4 on the block-scaled MMA) projections.
+CONFIGS["llama-3.1-8b-fp8"] = dict(CONFIGS["llama-3.1-8b"], precision="float8_e4m3fn", weight_format="fp8_block")
+CONFIGS["llama-3.3-70b-nvfp4"] = dict(CONFIGS["llama-3.3-70b"], precision="uint8", weight_format="nvfp4_a4")
+CONFIGS["llama-3.1-8b-nvfp4"] = dict(CONFIGS["llama-3.1-8b"], precision="uint8", weight_format="nvfp4_a4")
+CONFIGS["qwen3-8b-fp8"] = dict(CONFIGS["qwen3-8b"], precision="float8_e4m3fn", weight_format="fp8_block")
+
+
 def get(name: str, **overrides) -> dict:
     cfg = copy.deepcopy(CONFIGS[name])
     cfg.update(overrides)

@@ -47,7 +47,21 @@ def inv_freq(cfg: dict) -> torch.Tensor:
     return base.float()
 
 
-def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> torch.Tensor:
+def linear(x: torch.Tensor, w) -> torch.Tensor:
+    """``x @ w.T`` in FP32 for a BF16 weight, or under a quantized weight's contract."""
+    if isinstance(w, torch.Tensor):
+        return x @ w.float().T
+    return reference.quantized_linear(x, w)
+
+
+def _gate_up(x: torch.Tensor, w) -> tuple[torch.Tensor, torch.Tensor]:
+    full = linear(x, w)
+    T = full.shape[0]
+    blocks = full.view(T, -1, 2, 128)
+    return blocks[:, :, 0].reshape(T, -1), blocks[:, :, 1].reshape(T, -1)
+
+
+def forward(w: dict, cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> torch.Tensor:
     """Logits [len(ids), vocab] of one sequence from position 0, FP32 math; with `round_bf16` every
     stored activation is rounded to BF16 where the engine's GPU kernels store BF16."""
     rb = (lambda t: t.bfloat16().float()) if round_bf16 else (lambda t: t)
@@ -62,7 +76,7 @@ def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor, round_bf16
     for l in range(cfg["layers"]):
         p = f"layers.{l}."
         h = rb(reference.rmsnorm(x, w[p + "in_norm"], eps))
-        qkv = rb(h @ w[p + "qkv"].float().T)
+        qkv = rb(linear(h, w[p + "qkv"]))
         q, k, v = reference.qk_front(qkv, qh, kvh, D, w.get(p + "q_norm"), w.get(p + "k_norm"), eps, pos,
                                      freqs, round_bf16=round_bf16)
         q, k = rb(q), rb(k)
@@ -72,12 +86,11 @@ def forward(w: dict[str, torch.Tensor], cfg: dict, ids: torch.Tensor, round_bf16
         s = torch.einsum("qhd,khd->hqk", q, k) * D ** -0.5
         s = s.masked_fill(~mask[None], float("-inf"))
         a = rb(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, qh * D))
-        x = rb(x + a @ w[p + "o"].float().T)
+        x = rb(x + linear(a, w[p + "o"]))
         h = rb(reference.rmsnorm(x, w[p + "post_norm"], eps))
-        gate, up = split_gate_up(w[p + "gate_up"].float())
-        g, u = h @ gate.T, h @ up.T
+        g, u = _gate_up(h, w[p + "gate_up"])
         act = rb(reference.swiglu(g, u)) if round_bf16 else torch.nn.functional.silu(g) * u
-        x = rb(x + act @ w[p + "down"].float().T)
+        x = rb(x + linear(act, w[p + "down"]))
     h = rb(reference.rmsnorm(x, w["final_norm"], eps))
     head = w["lm_head"] if "lm_head" in w else w["embed"]
     return h @ head[: cfg["vocab"]].float().T

@@ -223,3 +223,29 @@ def nvfp4_dequantize(packed: torch.Tensor, scales: torch.Tensor) -> torch.Tensor
     mag = vals[codes & 7]
     v = torch.where((codes & 8) != 0, -mag, mag)
     return v * _e4m3_value(scales).repeat_interleave(16, 1)
+
+
+def nvfp4_scales_from_atoms(atoms: torch.Tensor, rows: int) -> torch.Tensor:
+    """The inverse of ``nvfp4_scale_atoms``: row-major scales [rows, K/16]."""
+    rb, kc, _ = atoms.shape
+    v = atoms.view(rb, kc, 32, 4, 4).permute(0, 3, 2, 1, 4)  # [rb, r1, r0, kc, k]
+    return v.reshape(rb * 128, kc * 4)[:rows].contiguous()
+
+
+def quantized_linear(x: torch.Tensor, w) -> torch.Tensor:
+    """``x @ W.T`` (FP32) under the contract of a quantized weight ``w`` (a ``QuantizedWeight``
+    with codes and scales on any device): W8A8 for fp8_block, W4A4 for nvfp4_a4, W4A16 for nvfp4
+    (``x`` is rounded to BF16 first, as the engine stores its inputs)."""
+    dev = x.device
+    codes, scales = w.codes.to(dev), w.scales.to(dev)
+    xb = x.bfloat16()
+    if w.format == "fp8_block":
+        return fp8_block_w8a8(xb, codes, scales)
+    if w.format == "fp8_block_w8a16":
+        return xb.float() @ fp8_block_dequantize(codes, scales).T
+    if w.format == "nvfp4":
+        return (xb.float() @ nvfp4_dequantize(codes, scales).T) * w.tensor_scale
+    s8 = nvfp4_scales_from_atoms(scales, w.rows)
+    ac, as8 = nvfp4_quantize_input(xb, w.input_scale)
+    alpha = float(torch.tensor(w.input_scale, dtype=torch.float32) * torch.tensor(w.tensor_scale, dtype=torch.float32))
+    return (nvfp4_dequantize(ac, as8) @ nvfp4_dequantize(codes, s8).T) * alpha

@@ -20,10 +20,29 @@ def tensor(ptr: int, shape, dtype: torch.dtype, device: int | None = None) -> to
     return t.view(torch.bfloat16) if dtype == torch.bfloat16 else t
 
 
-def weights(model) -> dict[str, torch.Tensor]:
-    """Every weight of a loaded decoder, as torch views of its device memory."""
+def weights(model) -> dict:
+    """Every weight of a loaded decoder, as torch views of its device memory: BF16 tensors, or
+    ``QuantizedWeight`` views (codes and scales) for quantized projections."""
+    from furiosa_opt_models_b200.ops.kernels import QuantizedWeight
+
     out = {}
+    dev = model.device.ordinal
     for name in model.weight_names():
-        ptr, shape = model.weight(name)
-        out[name] = tensor(ptr, shape, torch.bfloat16, model.device.ordinal)
+        q = model.quantized_weight(name)
+        if q is None:
+            ptr, shape = model.weight(name)
+            out[name] = tensor(ptr, shape, torch.bfloat16, dev)
+            continue
+        rows, cols = q["shape"]
+        fmt = q["format"]
+        if fmt == "fp8_block":
+            codes = tensor(q["codes"], (rows, cols), torch.uint8, dev)
+            scales = tensor(q["scales"], ((rows + 127) // 128, cols // 128), torch.float32, dev)
+        elif fmt == "nvfp4":
+            codes = tensor(q["codes"], (rows, cols // 2), torch.uint8, dev)
+            scales = tensor(q["scales"], (rows, cols // 16), torch.uint8, dev)
+        else:
+            codes = tensor(q["codes"], (rows, cols // 2), torch.uint8, dev)
+            scales = tensor(q["scales"], ((rows + 127) // 128, cols // 64, 512), torch.uint8, dev)
+        out[name] = QuantizedWeight(fmt, codes, scales, rows, cols, q["tensor_scale"], q["input_scale"])
     return out

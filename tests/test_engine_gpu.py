@@ -18,9 +18,17 @@ def _build(name="tiny-qwen3", **over):
 
 
 def _weights(model):
+    import dataclasses
+
     from furiosa_opt_models_b200.utils import devmem
 
-    return {k: v.float().cpu() for k, v in devmem.weights(model).items()}
+    out = {}
+    for k, v in devmem.weights(model).items():
+        if isinstance(v, torch.Tensor):
+            out[k] = v.float().cpu()
+        else:
+            out[k] = dataclasses.replace(v, codes=v.codes.cpu(), scales=v.scales.cpu())
+    return out
 
 
 @pytest.mark.parametrize("graphs", [True, False])
@@ -127,3 +135,42 @@ def test_load_refuses_a_missing_tensor(tmp_path):
     device = engine.Device(engine.Placement([0], range(8)))
     with pytest.raises(ValueError, match="missing tensors: model.layers.1.mlp.down_proj.weight"):
         engine.LoadOptions().load(engine.Checkpoint(str(tmp_path / "m")), device)
+
+
+@pytest.mark.parametrize("fmt", ["fp8_block", "nvfp4_a4", "nvfp4"])
+def test_quantized_decoder_matches_dense_contract(fmt):
+    """Quantized projections (W8A8, W4A4, W4A16) through the engine against the dense forward
+    that applies the same contracts (input quantization included) in FP32."""
+    engine, cfg, device, model = _build(weight_format=fmt)
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import dense
+
+    w = _weights(model)
+    assert not isinstance(w["layers.0.qkv"], torch.Tensor)
+    lengths = [5, 19, 40]
+    gen = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen, dtype=torch.int32) for n in lengths]
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(p).to_hbm(device), len(p), alloc.take(4))
+            for p in prompts]
+    steps = 4
+    out = serving.prefill(model, cache, seqs, list(range(len(seqs))))
+    tokens = [[t] for t in out.to_host().numpy().tolist()]
+    for _ in range(steps):
+        out = serving.decode(model, cache, seqs)
+        for i, t in enumerate(out.to_host().numpy().tolist()):
+            tokens[i].append(t)
+    device.synchronize()
+    for i, p in enumerate(prompts):
+        seq = p.clone()
+        for step in range(steps + 1):
+            logits = dense.forward(w, cfg, seq)[-1]
+            top = torch.topk(logits, 2).values
+            pick = tokens[i][step]
+            # Input quantization turns a rounding difference upstream into a whole code step (a
+            # third of a value for E2M1), so the engine's token may trail the dense maximum.
+            tol = 0.15 if fmt == "nvfp4_a4" else 5e-2
+            assert logits[pick] >= top[0] - tol * max(1.0, abs(top[0].item())), (fmt, i, step)
+            seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
