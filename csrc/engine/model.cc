@@ -188,7 +188,7 @@ void DecoderModel::allocate_weights() {
     const int64_t rb = (rows + 127) / 128;
     if (format == foa::kWeightFp8A8) {
       if (cols % 128 != 0) throw Unsupported(name + ": FP8 block inputs come in multiples of 128");
-      return {n, static_cast<size_t>(rb * (cols / 128) * 4)};
+      return {n, static_cast<size_t>(rb * (cols / 128) * 16)};  // each scale four times
     }
     if (cols % (format == foa::kWeightNvfp4A4 ? 256 : 64) != 0)
       throw Unsupported(name + ": NVFP4 inputs here come in multiples of " +
@@ -243,8 +243,12 @@ void DecoderModel::quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float 
   auto st = device_.state();
   const int rows = static_cast<int>(w.shape[0]), cols = static_cast<int>(w.shape[1]);
   if (w.format == foa::kWeightFp8A8) {
-    if (foa::quantize_fp8_block(src, rows, cols, w.codes, static_cast<float*>(w.scales), st->stream) != 0)
+    const long n = static_cast<long>((rows + 127) / 128) * (cols / 128);
+    HbmBuffer plain(device_, n * 4);
+    if (foa::quantize_fp8_block(src, rows, cols, w.codes, static_cast<float*>(plain.data()), st->stream) != 0 ||
+        foa::fp8_scales_pad4(static_cast<const float*>(plain.data()), n, static_cast<float*>(w.scales), st->stream) != 0)
       st->fail("weight quantization launch failed");
+    st->check_cuda(cudaStreamSynchronize(st->stream), "weight quantization");
     return;
   }
   // NVFP4: one tensor scale from a fixed magnitude bound (8 standard deviations), the same on

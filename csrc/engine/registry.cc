@@ -546,7 +546,11 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
     }
     st->check_cuda(cudaMemcpy(w.codes, codes.data(), codes.size(), cudaMemcpyHostToDevice), "weight upload");
     if (fp8) {
-      st->check_cuda(cudaMemcpy(w.scales, fscales.data(), fscales.size() * 4, cudaMemcpyHostToDevice), "weight upload");
+      // The W8A8 GEMM stages each block scale as a 16-byte entry (the value four times).
+      std::vector<float> padded(fscales.size() * 4);
+      for (size_t i = 0; i < fscales.size(); ++i)
+        for (int j = 0; j < 4; ++j) padded[i * 4 + j] = fscales[i];
+      st->check_cuda(cudaMemcpy(w.scales, padded.data(), padded.size() * 4, cudaMemcpyHostToDevice), "weight upload");
       return;
     }
     w.tensor_scale = tensor_scale;

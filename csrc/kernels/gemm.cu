@@ -137,8 +137,10 @@ struct Cfg {
   static constexpr int kSfBytes = kWF == kWNvfp4A4 ? (kMB + kQGroups) * 2048 : 0;
   static constexpr int kSfCols = kWF == kWNvfp4A4 ? 16 * (kMB + kQGroups) : 0;
   static constexpr int kBoxX = (kWF == kWNvfp4A4 || kWF == kWFp8A8) ? 128 : 64;  // TMA x of a k-block
-  // W8A8: the FP32 activation scales of one k-block for the tile's tokens.
-  static constexpr int kAscBytes = kWF == kWFp8A8 ? 4 * (kBN > 128 ? kBN : 128) : 0;
+  // W8A8: the FP32 activation scales of one k-block for the tile's tokens, then the weight scale
+  // of each M block (16 bytes apiece, as stored).
+  static constexpr int kAscOnly = 4 * (kBN > 128 ? kBN : 128);
+  static constexpr int kAscBytes = kWF == kWFp8A8 ? kAscOnly + 16 * kMB : 0;
   static constexpr int kAccCols = kMB * kBN;
   static constexpr int kSfCol0 = kAcc * kAccCols;
   static constexpr int kColsRaw = kAcc * kAccCols + kSfCols;
@@ -360,11 +362,16 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
             bulk_load(asr + s * C::kAscBytes, p.ascale + (long)kb * p.ascale_ld + tq * kBN, kBN * 4, full + s);
           else
             bulk_load(asr + s * C::kAscBytes, p.ascale + (long)kb * p.ascale_ld + tp * 128, 512, full + s);
+          // Weight scales [row block][K/128][4 copies]: one 16-byte entry per M block.
+          const float* wsc = static_cast<const float*>(p.wscale);
+          for (int mb = 0; mb < (p.swap ? kMB : 1); ++mb)
+            bulk_load(asr + s * C::kAscBytes + C::kAscOnly + 16 * mb,
+                      wsc + ((long)(p.swap ? tp * kMB + mb : tq) * p.wscale_ld + kb) * 4, 16, full + s);
         }
       };
       const uint32_t full_bytes = kWF == kWBf16      ? C::kStageBytes
                                   : kWF == kWNvfp4A4 ? C::kStageBytes + C::kSfBytes
-                                  : kWF == kWFp8A8   ? C::kStageBytes + (p.swap ? kBN * 4 : 512)
+                                  : kWF == kWFp8A8   ? C::kStageBytes + (p.swap ? kBN * 4 + 16 * kMB : 512 + 16)
                                                      : (p.swap ? C::kQBytes : C::kPBytes);
       // The first stages' weight tiles do not depend on earlier kernels: issue them before
       // waiting for the previous kernel (PDL), then their activation tiles after it.
@@ -605,15 +612,12 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         float acc[kCnt];
 #pragma unroll
         for (int c = 0; c < kCnt; ++c) acc[c] = 0.f;
-        const float* wsc = static_cast<const float*>(p.wscale);
-        const long wrow = (long)(p.swap ? tp * kMB + mb_s : tq) * p.wscale_ld;
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++kit) {
           const int s = kit % kStages;
           const uint32_t ph = (kit / kStages) & 1;
           b = kit % kAcc;
           const uint32_t bph = (kit / kAcc) & 1;
-          const float sw = __ldg(wsc + wrow + kb);
           int got = 1;
           if (lane == 0)
             got = mbar_wait(tfull + b, bph, p.status, kTimeoutTmemFull, abort) &&
@@ -625,6 +629,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           tc_fence_after();
           // TMEM loads go out in batches with one wait each: the round trips bound this loop.
           const float* asc = reinterpret_cast<const float*>(asr + s * C::kAscBytes);
+          const float sw = *reinterpret_cast<const float*>(asr + s * C::kAscBytes + C::kAscOnly +
+                                                           16 * (p.swap ? mb_s : 0));
           const float srow = p.swap ? 0.f : asc[lrow] * sw;
           const uint32_t tb = tmem_base + (uint32_t(q * 32) << 16) + b * C::kAccCols + col_s;
           constexpr int kBatch = kCnt >= 32 ? 32 : kCnt;
@@ -930,7 +936,7 @@ struct Shape {
   static constexpr int kStage = 128 * kMB * 128 + kBN * 128;
   static constexpr int kRaw = (kMB * 128 > kBN ? kMB * 128 : kBN) * (kWF == 1 ? 64 : kWF == 2 ? 32 : 0);
   static constexpr int kSfGroups = kWF == 3 ? kMB + (kBN + 127) / 128 : 0;
-  static constexpr int kAsc = kWF == 4 ? 4 * (kBN > 128 ? kBN : 128) : 0;
+  static constexpr int kAsc = kWF == 4 ? 4 * (kBN > 128 ? kBN : 128) + 16 * kMB : 0;
   static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw + kSfGroups * 2048 + kAsc);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   // W8A8 keeps up to eight per-block partial sums in flight so the MMAs run ahead of the scaling.
@@ -942,7 +948,7 @@ struct Shape {
 int swap_ring_bytes(int mb, int kbn, int wf) {
   const int stage = 128 * mb * 128 + kbn * 128;
   const int raw = (mb * 128 > kbn ? mb * 128 : kbn) * (wf == 1 ? 64 : wf == 2 ? 32 : 0);
-  const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : wf == 4 ? 4 * std::max(kbn, 128) : 0;
+  const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : wf == 4 ? 4 * std::max(kbn, 128) + 16 * mb : 0;
   int stages = (220 * 1024 - 2048) / (stage + raw + sf);
   if (stages > 8) stages = 8;
   return stage * stages;
@@ -1268,7 +1274,9 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (fp8) {
     // E4M3 codes of both operands (one a byte), FP32 activation scales [K/128][a_scale_ld].
     if (a.K % 128 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.a_scale == nullptr) return -2;
-    if (a.a_scale_ld < ((a.M + 127) / 128) * 128 || (reinterpret_cast<uintptr_t>(a.a_scale) & 15)) return -1;
+    if (a.a_scale_ld < ((a.M + 127) / 128) * 128 || (reinterpret_cast<uintptr_t>(a.a_scale) & 15) ||
+        (reinterpret_cast<uintptr_t>(a.w_scale) & 15))
+      return -1;
   }
   if (nvf4) {
     // Both operands are packed E2M1 codes (two a byte) with 128-row-blocked scale atoms.

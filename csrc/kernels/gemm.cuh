@@ -63,7 +63,8 @@ struct GemmArgs {
   long w_scale_ld = 0;
   float w_tensor_scale = 1.0f;
   //   kWeightFp8A8:    block-scaled FP8 on both operands (W8A8): `a` and `w` hold E4M3 codes,
-  //                    w_scale FP32 [ceil(N/128), w_scale_ld] per 128x128 block, a_scale FP32
+  //                    w_scale FP32 [ceil(N/128), w_scale_ld, 4] per 128x128 block (each scale four
+  //                    times, one 16-byte entry; see fp8_scales_pad4), a_scale FP32
   //                    [K/128, a_scale_ld] per (128-input group, row) with a_scale_ld >= M rounded
   //                    up to 128 (K % 128 == 0).
   const void* a_scale = nullptr;

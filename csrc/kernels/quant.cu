@@ -199,6 +199,23 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
              : -5;
 }
 
+__global__ void pad4_kernel(const float* src, long n, float4* dst) {
+  pdl_wait();  // weight producer: no early trigger
+  const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float v = src[i];
+    dst[i] = make_float4(v, v, v, v);
+  }
+}
+
+int fp8_scales_pad4(const float* scales, long n, float* padded, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  return launch_pdl(pad4_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, stream, scales, n,
+                    reinterpret_cast<float4*>(padded)) == cudaSuccess
+             ? 0
+             : -5;
+}
+
 int quantize_fp8_act(const __nv_bfloat16* x, long ldx, int rows, int K, uint8_t* codes, long ldc,
                      float* scales, int rows_pad, cudaStream_t stream) {
   if (rows <= 0) return 0;

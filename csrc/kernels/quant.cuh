@@ -22,6 +22,10 @@ int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* code
 int quantize_nvfp4(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, uint8_t* scales,
                    const float* amax, float* tensor_scale, cudaStream_t stream);
 
+// The W8A8 GEMM's weight-scale layout: each of n FP32 block scales four times (16 bytes apiece), so
+// that the GEMM stages one block's scale with a 16-byte bulk copy.
+int fp8_scales_pad4(const float* scales, long n, float* padded, cudaStream_t stream);
+
 // FP8 activations per (row, 128-input group), the W8A8 input form of the block-scaled FP8 GEMM:
 // scale = max(amax, 1e-10) * fl(1/448), codes [rows, K] E4M3 (row stride ldc bytes), scales FP32
 // [K/128][rows_pad] (rows_pad >= rows; entries past `rows` are not written).

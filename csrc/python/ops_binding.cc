@@ -75,6 +75,14 @@ void bind_ops(py::module_& m) {
       py::arg("a_scale_ld") = 0);
 
   m.def(
+      "fp8_scales_pad4",
+      [](uint64_t scales, long n, uint64_t padded, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::fp8_scales_pad4(as_ptr<const float>(scales), n, as_ptr<float>(padded), as_stream(stream)),
+              "fp8_scales_pad4");
+      },
+      py::arg("scales"), py::arg("n"), py::arg("padded"), py::arg("stream"));
+  m.def(
       "quantize_fp8_act",
       [](uint64_t x, long ldx, int rows, int K, uint64_t codes, long ldc, uint64_t scales,
          int rows_pad, uint64_t stream) {

@@ -50,6 +50,15 @@ class QuantizedWeight:
     cols: int
     tensor_scale: float = 1.0
     input_scale: float = 1.0
+    # fp8_block on the W8A8 GEMM: the scales with each value four times (16-byte entries).
+    gemm_scales: torch.Tensor | None = None
+
+    def fp8_gemm_scales(self) -> torch.Tensor:
+        if self.gemm_scales is None:
+            s = self.scales.contiguous()
+            self.gemm_scales = torch.empty(*s.shape, 4, dtype=torch.float32, device=s.device)
+            native().ops.fp8_scales_pad4(s.data_ptr(), s.numel(), self.gemm_scales.data_ptr(), _stream())
+        return self.gemm_scales
 
     @property
     def code(self) -> int:
@@ -165,7 +174,9 @@ def gemm(
             codes, ascales = quantize_fp8_input(a)
             keep = (codes, ascales)  # noqa: F841
             a_ptr, lda = codes.data_ptr(), K
-            qargs.update(a_scale=ascales.data_ptr(), a_scale_ld=ascales.stride(0))
+            padded = w.fp8_gemm_scales()
+            qargs.update(a_scale=ascales.data_ptr(), a_scale_ld=ascales.stride(0),
+                         w_scale=padded.data_ptr(), w_scale_ld=padded.shape[1])
     else:
         _rowmajor(w, "w")
         if w.dtype != torch.bfloat16:

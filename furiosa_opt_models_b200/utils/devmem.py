@@ -35,14 +35,17 @@ def weights(model) -> dict:
             continue
         rows, cols = q["shape"]
         fmt = q["format"]
+        padded = None
         if fmt == "fp8_block":
             codes = tensor(q["codes"], (rows, cols), torch.uint8, dev)
-            scales = tensor(q["scales"], ((rows + 127) // 128, cols // 128), torch.float32, dev)
+            padded = tensor(q["scales"], ((rows + 127) // 128, cols // 128, 4), torch.float32, dev)
+            scales = padded[..., 0]
         elif fmt == "nvfp4":
             codes = tensor(q["codes"], (rows, cols // 2), torch.uint8, dev)
             scales = tensor(q["scales"], (rows, cols // 16), torch.uint8, dev)
         else:
             codes = tensor(q["codes"], (rows, cols // 2), torch.uint8, dev)
             scales = tensor(q["scales"], ((rows + 127) // 128, cols // 64, 512), torch.uint8, dev)
-        out[name] = QuantizedWeight(fmt, codes, scales, rows, cols, q["tensor_scale"], q["input_scale"])
+        out[name] = QuantizedWeight(fmt, codes, scales, rows, cols, q["tensor_scale"], q["input_scale"],
+                                    gemm_scales=padded if fmt == "fp8_block" else None)
     return out
