@@ -72,6 +72,12 @@ struct KParams {
   // FP8 W8A8 (kWF == kWFp8A8): activation scales [K/128][ascale_ld] (transposed per k-block).
   const float* ascale;
   long ascale_ld;
+  // Grouped (mixture-of-experts) swap GEMM: the N-side token tiles and the group (expert) whose
+  // weights each tile multiplies come from the device; weights of group g start at row
+  // g * group_rows.
+  const int* group_tiles;  // number of token tiles (device), or null
+  const int* tile_group;   // group of each token tile (device)
+  long group_rows;
 };
 
 // Weight formats a GEMM reads: BF16; FP8 block-scaled or NVFP4 codes dequantized to BF16 in
@@ -278,6 +284,12 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   const int lane = threadIdx.x % 32;
   pdl_trigger();
   if (threadIdx.x == 0) mark(p, 0);
+  // A grouped launch learns its token tiles from the routing kernel before it.
+  int units = p.units;
+  if (p.group_tiles != nullptr) {
+    pdl_wait();
+    units = p.tiles_p * min(*reinterpret_cast<const volatile int*>(p.group_tiles), p.tiles_q) * p.splits;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
@@ -338,10 +350,12 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       auto load_w = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
         if constexpr (kWF == kWBf16 || kWF == kWNvfp4A4 || kWF == kWFp8A8) {
-          if (p.swap)
-            tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
-          else
+          if (p.swap) {
+            const long g0 = p.tile_group != nullptr ? (long)p.tile_group[tq] * p.group_rows : 0;
+            tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, (int)(g0 + tp * C::kPRows));
+          } else {
             tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * C::kBoxX, tq * kBN);
+          }
           if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap != 0);
         } else {
           const int rows = p.swap ? C::kPRows : kBN;
@@ -376,7 +390,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       // The first stages' weight tiles do not depend on earlier kernels: issue them before
       // waiting for the previous kernel (PDL), then their activation tiles after it.
       int pre = 0;
-      if (blockIdx.x < p.units) {
+      if (blockIdx.x < units) {
         const int split = blockIdx.x % p.splits, tile = blockIdx.x / p.splits;
         const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
         const int kb0 = split * p.kb_per_split;
@@ -392,7 +406,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       } else {
         pdl_wait();
       }
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int tile = u / p.splits, split = u % p.splits;
         const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
         const int kb0 = split * p.kb_per_split;
@@ -427,7 +441,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       constexpr uint32_t idesc = idesc_e4m3_f32(128, kBN);
       uint32_t it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int split = u % p.splits;
         const int kb0 = split * p.kb_per_split;
         const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
@@ -468,7 +482,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       const uint32_t sfb_t = sfa_t + 16 * kMB;
       uint32_t it = 0, tc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x, ++tc) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++tc) {
         const int split = u % p.splits;
         // A 64-row N tile reads the second half of its 128-row scale atoms when it is odd.
         const uint32_t sfb_shift = (kBN == 64 && ((u / p.splits) / p.tiles_p) % 2 == 1) ? 2u : 0u;
@@ -541,7 +555,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     const int wrows_total = p.swap ? p.Mp : p.Nq;
     uint32_t it = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < p.units && ok; u += gridDim.x) {
+    for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
       const int tile = u / p.splits, split = u % p.splits;
       const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
       const int kb0 = split * p.kb_per_split;
@@ -592,7 +606,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     uint32_t tc = 0;
     uint32_t kit = 0;  // W8A8: k-blocks consumed (stage and buffer sequence of the MMA warp)
     uint32_t xfer_count = 0;  // W8A8: hand-overs between the two scaling streams
-    for (int u = blockIdx.x; u < p.units; u += gridDim.x, ++tc) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++tc) {
       const int tile = u / p.splits, split = u % p.splits;
       const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
       int b = tc % kAcc;
@@ -962,7 +976,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   Plan pl{};
   // W8A8 SwiGLU runs on the swap mapping at every row count (its rows tiles hold 128 columns).
   const bool swap = a.mode == kModeSwap || (a.mode == kModeAuto && a.M <= 256) ||
-                    (a.w_format == kWFp8A8 && a.epilogue == kEpiSwiGLU);
+                    (a.w_format == kWFp8A8 && a.epilogue == kEpiSwiGLU) || a.group_tiles != nullptr;
   pl.swap = swap;
   const int kelems = a.w_format == kWNvfp4A4 ? 256 : a.w_format == kWFp8A8 ? 128 : kBlockK;
   pl.kblocks = (a.K + kelems - 1) / kelems;
@@ -981,11 +995,15 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
       if (pl.mb == 2) pl.kbn = std::min(pl.kbn, 128);
     }
     if (a.w_format == kWFp8A8) pl.kbn = std::max(32, std::min(pl.kbn, pl.mb == 2 ? 64 : 128));
+    if (a.group_tiles != nullptr) {
+      pl.kbn = a.group_tile;
+      pl.tiles_q = (a.M + pl.kbn - 1) / pl.kbn;
+    }
     pl.tiles_p = (a.N + 128 * pl.mb - 1) / (128 * pl.mb);
     pl.tiles_q = (a.M + pl.kbn - 1) / pl.kbn;
   }
   const int tiles = pl.tiles_p * pl.tiles_q;
-  int splits = a.splits;
+  int splits = a.group_tiles != nullptr ? 1 : a.splits;
   if (splits <= 0) {
     splits = 1;
     if (tiles * 2 <= num_sms) splits = std::min(8, num_sms / tiles);
@@ -1271,6 +1289,14 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
   const bool nvf4 = a.w_format == kWNvfp4A4;
   const bool fp8 = a.w_format == kWFp8A8;
+  const bool grouped = a.group_tiles != nullptr;
+  if (grouped) {
+    const int t = a.group_tile;
+    if (a.w_format != kWBf16 || a.tile_group == nullptr || a.groups <= 0 || a.N % 128 != 0 ||
+        !(t == 16 || t == 32 || t == 64 || t == 128 || t == 256) || a.residual != nullptr)
+      return -2;
+    if (a.epilogue == kEpiSwiGLU && t > 128) return -2;
+  }
   if (fp8) {
     // E4M3 codes of both operands (one a byte), FP32 activation scales [K/128][a_scale_ld].
     if (a.K % 128 != 0 || a.lda % 16 != 0 || a.ldw % 16 != 0 || a.a_scale == nullptr) return -2;
@@ -1312,6 +1338,11 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;
   kp.wscale_ld = a.w_scale_ld;
+  if (grouped) {
+    kp.group_tiles = a.group_tiles;
+    kp.tile_group = a.tile_group;
+    kp.group_rows = a.N;
+  }
   kp.acc_scale = (a.w_format == kWNvfp4 || nvf4) ? a.w_tensor_scale : 1.0f;
   if (nvf4) {
     const long atoms = (long)(a.K / 64) * 512;  // bytes of one 128-row block of scale atoms
@@ -1370,7 +1401,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.Mp = a.N;
   kp.Nq = a.M;
   if (converted) tp = tw;
-  else if (!operand(&tp, a.w, a.N, a.ldw, prow_box)) return -4;
+  else if (!operand(&tp, a.w, (long)a.N * (grouped ? a.groups : 1), a.ldw, prow_box)) return -4;
   if (!operand(&tq, a.a, a.M, a.lda, pl.kbn)) return -4;
   switch (a.w_format) {
     case kWFp8Block: return launch_swap<kWFp8Block>(a.epilogue, tp, tq, tw, kp, pl, stream);

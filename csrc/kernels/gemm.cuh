@@ -69,6 +69,14 @@ struct GemmArgs {
   //                    up to 128 (K % 128 == 0).
   const void* a_scale = nullptr;
   long a_scale_ld = 0;
+  // Grouped GEMM (mixture-of-experts experts, BF16 weights, swap mapping, no split-K): `w` holds
+  // `groups` weight matrices [N, K] one after another; `a` holds M token rows sorted by group with
+  // each group's rows padded to `group_tile` (16, 32, 64, 128 or 256); `group_tiles` (device) is the
+  // number of token tiles in use and `tile_group` (device) the group of each tile.
+  const int* group_tiles = nullptr;
+  const int* tile_group = nullptr;
+  int group_tile = 0;
+  int groups = 0;
 };
 
 enum GemmWeightFormat : int {

@@ -11,6 +11,7 @@
 #include "kernels/ops.cuh"
 #include "kernels/attention.cuh"
 #include "kernels/quant.cuh"
+#include "kernels/moe.cuh"
 
 namespace py = pybind11;
 
@@ -35,8 +36,12 @@ void bind_ops(py::module_& m) {
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
          uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
          int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
-         long a_scale_ld) {
+         long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups) {
         foa::GemmArgs g;
+        g.group_tiles = as_ptr<const int>(group_tiles);
+        g.tile_group = as_ptr<const int>(tile_group);
+        g.group_tile = group_tile;
+        g.groups = groups;
         g.a_scale = as_ptr<void>(a_scale);
         g.a_scale_ld = a_scale_ld;
         g.w_format = w_format;
@@ -72,7 +77,57 @@ void bind_ops(py::module_& m) {
       py::arg("ws_bytes"), py::arg("counters"), py::arg("counters_len"), py::arg("status"),
       py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
       py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0,
-      py::arg("a_scale_ld") = 0);
+      py::arg("a_scale_ld") = 0, py::arg("group_tiles") = 0, py::arg("tile_group") = 0,
+      py::arg("group_tile") = 0, py::arg("groups") = 0);
+
+  m.def(
+      "moe_route",
+      [](uint64_t logits, long ld, int rows, int experts, int k, bool normalize, uint64_t ids,
+         uint64_t weights, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::moe_route(as_ptr<const __nv_bfloat16>(logits), ld, rows, experts, k, normalize,
+                             as_ptr<int32_t>(ids), as_ptr<float>(weights), as_stream(stream)),
+              "moe_route");
+      },
+      py::arg("logits"), py::arg("ld"), py::arg("rows"), py::arg("experts"), py::arg("k"),
+      py::arg("normalize"), py::arg("ids"), py::arg("weights"), py::arg("stream"));
+  m.def(
+      "moe_align",
+      [](uint64_t ids, int rows, int k, int experts, int first, int count, int tile, int capacity,
+         uint64_t pos, uint64_t src, uint64_t tile_expert, uint64_t tiles, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::moe_align(as_ptr<const int32_t>(ids), rows, k, experts, first, count, tile, capacity,
+                             as_ptr<int32_t>(pos), as_ptr<int32_t>(src), as_ptr<int32_t>(tile_expert),
+                             as_ptr<int32_t>(tiles), as_stream(stream)),
+              "moe_align");
+      },
+      py::arg("ids"), py::arg("rows"), py::arg("k"), py::arg("experts"), py::arg("first"),
+      py::arg("count"), py::arg("tile"), py::arg("capacity"), py::arg("pos"), py::arg("src"),
+      py::arg("tile_expert"), py::arg("tiles"), py::arg("stream"));
+  m.def(
+      "moe_gather",
+      [](uint64_t x, long ldx, uint64_t src, uint64_t tiles, int tile, int capacity, int cols,
+         uint64_t out, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::moe_gather(as_ptr<const __nv_bfloat16>(x), ldx, as_ptr<const int32_t>(src),
+                              as_ptr<const int32_t>(tiles), tile, capacity, cols,
+                              as_ptr<__nv_bfloat16>(out), as_stream(stream)),
+              "moe_gather");
+      },
+      py::arg("x"), py::arg("ldx"), py::arg("src"), py::arg("tiles"), py::arg("tile"),
+      py::arg("capacity"), py::arg("cols"), py::arg("out"), py::arg("stream"));
+  m.def(
+      "moe_combine",
+      [](uint64_t y, long ldy, uint64_t pos, uint64_t weights, int rows, int k, int cols,
+         uint64_t residual, long ldr, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::moe_combine(as_ptr<const __nv_bfloat16>(y), ldy, as_ptr<const int32_t>(pos),
+                               as_ptr<const float>(weights), rows, k, cols,
+                               as_ptr<__nv_bfloat16>(residual), ldr, as_stream(stream)),
+              "moe_combine");
+      },
+      py::arg("y"), py::arg("ldy"), py::arg("pos"), py::arg("weights"), py::arg("rows"),
+      py::arg("k"), py::arg("cols"), py::arg("residual"), py::arg("ldr"), py::arg("stream"));
 
   m.def(
       "fp8_scales_pad4",

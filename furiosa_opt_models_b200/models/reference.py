@@ -249,3 +249,48 @@ def quantized_linear(x: torch.Tensor, w) -> torch.Tensor:
     ac, as8 = nvfp4_quantize_input(xb, w.input_scale)
     alpha = float(torch.tensor(w.input_scale, dtype=torch.float32) * torch.tensor(w.tensor_scale, dtype=torch.float32))
     return (nvfp4_dequantize(ac, as8) @ nvfp4_dequantize(codes, s8).T) * alpha
+
+
+# ------------------------------------------------------------------------------ mixture of experts
+# Routing and combine contract: crates/furiosa-opt-models/src/modules/feedforward/moe.rs:1-7
+# (top-k of BF16 logits, best first, equal logits in ascending expert order; FP32 softmax; the
+# weighted sum in FP32 in choice order, rounded once).
+
+
+def moe_route(logits: torch.Tensor, k: int, normalize: bool = True):
+    """(ids [rows, k] int64, weights [rows, k] FP32) of BF16 logits [rows, E]."""
+    lf = logits.float()
+    probs = torch.softmax(lf, dim=-1)
+    rows, E = lf.shape
+    # Stable descending sort keeps equal logits in ascending expert order.
+    order = torch.sort(lf, dim=-1, descending=True, stable=True).indices[:, :k]
+    w = torch.gather(probs, 1, order)
+    if normalize:
+        total = torch.zeros(rows, dtype=torch.float32, device=lf.device)
+        for j in range(k):
+            total = total + w[:, j]
+        w = w / total[:, None]
+    return order, w
+
+
+def moe_forward(h: torch.Tensor, router: torch.Tensor, gate_up: torch.Tensor, down: torch.Tensor, k: int,
+                normalize: bool = True):
+    """The MoE block of BF16 rows h [T, H] -> BF16 [T, H]: router [E, H], gate_up [E, 2I, H] (128-row
+    blocks alternating gate/up), down [E, H, I]. Router logits, expert rows and the output round to
+    BF16 once each."""
+    logits = (h.float() @ router.float().T).bfloat16()
+    ids, w = moe_route(logits, k, normalize)
+    T, H = h.shape
+    acc = torch.zeros(T, H, dtype=torch.float32, device=h.device)
+    for j in range(k):
+        rows = torch.zeros(T, H, dtype=torch.float32, device=h.device)
+        for e in ids[:, j].unique().tolist():
+            sel = ids[:, j] == e
+            gu = h[sel].float() @ gate_up[e].float().T
+            blocks = gu.view(gu.shape[0], -1, 2, 128)
+            g = blocks[:, :, 0].reshape(gu.shape[0], -1)
+            u = blocks[:, :, 1].reshape(gu.shape[0], -1)
+            act = swiglu(g, u).bfloat16().float()
+            rows[sel] = (act @ down[e].float().T).bfloat16().float()
+        acc = acc + w[:, j:j + 1] * rows
+    return acc.bfloat16()

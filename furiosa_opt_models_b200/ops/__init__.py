@@ -32,4 +32,10 @@ from .kernels import (  # noqa: F401
     quantize_nvfp4_input,
     quantize_fp8_input,
     nvfp4_w4a4,
+    moe_route,
+    moe_align,
+    moe_capacity,
+    moe_gather,
+    moe_combine,
+    grouped_gemm,
 )

@@ -301,3 +301,72 @@ def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=Non
         segments.shape[0], q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5),
         work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream())
     return out
+
+
+# ------------------------------------------------------------------------------ mixture of experts
+
+
+def moe_route(logits: torch.Tensor, k: int, normalize: bool = True):
+    """Top-k routing of BF16 logits [rows, experts]: (ids int32 [rows, k], weights FP32 [rows, k])."""
+    _rowmajor(logits, "logits")
+    rows, experts = logits.shape
+    ids = torch.empty(rows, k, dtype=torch.int32, device=logits.device)
+    w = torch.empty(rows, k, dtype=torch.float32, device=logits.device)
+    native().ops.moe_route(logits.data_ptr(), logits.stride(0), rows, experts, k, bool(normalize),
+                           ids.data_ptr(), w.data_ptr(), _stream())
+    return ids, w
+
+
+def moe_capacity(rows: int, k: int, count: int, tile: int) -> int:
+    return (rows * k + count * (tile - 1) + tile - 1) // tile * tile
+
+
+def moe_align(ids: torch.Tensor, experts: int, tile: int, first: int = 0, count: int | None = None):
+    """Groups selections by expert: (pos [rows, k], src [capacity], tile_expert [capacity/tile],
+    tiles [1]) for the experts [first, first + count)."""
+    rows, k = ids.shape
+    count = experts - first if count is None else count
+    cap = moe_capacity(rows, k, count, tile)
+    dev = ids.device
+    pos = torch.empty(rows, k, dtype=torch.int32, device=dev)
+    src = torch.empty(cap, dtype=torch.int32, device=dev)
+    tile_expert = torch.zeros(cap // tile, dtype=torch.int32, device=dev)
+    tiles = torch.zeros(1, dtype=torch.int32, device=dev)
+    native().ops.moe_align(ids.data_ptr(), rows, k, experts, first, count, tile, cap, pos.data_ptr(),
+                           src.data_ptr(), tile_expert.data_ptr(), tiles.data_ptr(), _stream())
+    return pos, src, tile_expert, tiles
+
+
+def grouped_gemm(a: torch.Tensor, w: torch.Tensor, tiles: torch.Tensor, tile_expert: torch.Tensor, tile: int,
+                 epilogue: int = EPI_BF16) -> torch.Tensor:
+    """Per-expert ``epilogue(a[rows of e] @ w[e].T)``: a [capacity, K] BF16 sorted by expert (each
+    expert's rows padded to ``tile``), w [E, N, K] BF16; rows past the tiles in use are not written."""
+    _rowmajor(a, "a")
+    E, N, K = w.shape
+    M = a.shape[0]
+    cols = N // 2 if epilogue == EPI_SWIGLU else N
+    out = torch.zeros(M, cols, dtype=torch.float32 if epilogue == EPI_F32 else torch.bfloat16, device=a.device)
+    s = scratch(a.device)
+    native().ops.gemm(
+        a.data_ptr(), a.stride(0), w.data_ptr(), K, M, N, K, out.data_ptr(), out.stride(0), 0, 0,
+        epilogue, MODE_SWAP, 1, s.workspace.data_ptr(), s.workspace.numel() * 4, s.counters.data_ptr(),
+        s.counters.numel(), s.status.data_ptr(), _stream(), 0,
+        group_tiles=tiles.data_ptr(), tile_group=tile_expert.data_ptr(), group_tile=tile, groups=E,
+    )
+    return out
+
+
+def moe_gather(x: torch.Tensor, src: torch.Tensor, tiles: torch.Tensor, tile: int) -> torch.Tensor:
+    cap = src.shape[0]
+    out = torch.zeros(cap, x.shape[1], dtype=x.dtype, device=x.device)
+    native().ops.moe_gather(x.data_ptr(), x.stride(0), src.data_ptr(), tiles.data_ptr(), tile, cap,
+                            x.shape[1], out.data_ptr(), _stream())
+    return out
+
+
+def moe_combine(y: torch.Tensor, pos: torch.Tensor, weights: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """residual += bf16(sum_j w_j * y[pos_j]) in choice order (in place); returns residual."""
+    rows, k = pos.shape
+    native().ops.moe_combine(y.data_ptr(), y.stride(0), pos.data_ptr(), weights.data_ptr(), rows, k,
+                             residual.shape[1], residual.data_ptr(), residual.stride(0), _stream())
+    return residual
