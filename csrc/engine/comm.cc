@@ -9,8 +9,8 @@ size_t align_to(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace
 
 PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int64_t rows, int cols,
-                                 int64_t kept)
-    : device_(device), world_(world), rank_(rank), rows_(rows), kept_(kept), cols_(cols) {
+                                 int64_t kept, int64_t moe_rows)
+    : device_(device), world_(world), rank_(rank), rows_(rows), kept_(kept), moe_rows_(moe_rows), cols_(cols) {
   if (world < 2 || world > foa::kMaxRanks) throw Unsupported("tensor parallelism takes 2 to 8 chips");
   auto st = device_.state();
   st->activate();
@@ -32,6 +32,8 @@ PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int6
   off = align_to(off + static_cast<size_t>(world) * kept * 4, 256);
   off_gindex_ = off;
   off = align_to(off + static_cast<size_t>(world) * kept * 4, 4096);
+  off_moe_ = off;
+  off = align_to(off + 2 * static_cast<size_t>(moe_rows) * cols * 2, 4096);
   heap_bytes_ = off;
   st->check_cuda(cudaMalloc(&heap_, heap_bytes_), "tensor-parallel heap");
   st->check_cuda(cudaMemset(heap_, 0, heap_bytes_), "tensor-parallel heap");
@@ -105,6 +107,39 @@ __nv_bfloat16* PeerCollectives::residual_buffer() {
 
 __nv_bfloat16* PeerCollectives::hidden_buffer() {
   return reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(heap_) + off_hidden_);
+}
+
+__nv_bfloat16* PeerCollectives::moe_rows(int which, size_t rows) {
+  if (rows > static_cast<size_t>(moe_rows_)) throw ValueError("call exceeds the expert-parallel heap");
+  return reinterpret_cast<__nv_bfloat16*>(static_cast<char*>(heap_) + off_moe_) +
+         static_cast<size_t>(which & 1) * moe_rows_ * cols_;
+}
+
+void PeerCollectives::moe_combine_norm(int which, const int32_t* pos_all, const int32_t* ids,
+                                       const float* weights, int experts_local,
+                                       const __nv_bfloat16* norm, float eps, int rows, int k, int cols,
+                                       cudaStream_t stream) {
+  foa::MoeCombineArgs a{};
+  a.peers = peers_;
+  for (int p = 0; p < world_; ++p)
+    a.y[p] = reinterpret_cast<const __nv_bfloat16*>(static_cast<char*>(peer_base_[p]) + off_moe_) +
+             static_cast<size_t>(which & 1) * moe_rows_ * cols_;
+  a.ldy = cols;
+  a.pos = pos_all;
+  a.ids = ids;
+  a.weights = weights;
+  a.experts_local = experts_local;
+  a.norm = norm;
+  a.eps = eps;
+  a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
+  a.rows = rows;
+  a.k = k;
+  a.cols = cols;
+  a.rank = rank_;
+  a.world = world_;
+  a.site = site_++;
+  a.status = status_;
+  if (foa::tp_moe_combine_norm(a, stream) != 0) device_.state()->fail("expert-parallel combine launch failed");
 }
 
 void PeerCollectives::add_norm(const float* partial, __nv_bfloat16* residual,

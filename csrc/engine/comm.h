@@ -13,8 +13,10 @@ namespace foa::engine {
 
 class PeerCollectives : public Collectives {
  public:
-  // A heap for calls of up to `rows` rows of `cols` columns and `kept` returned rows.
-  PeerCollectives(const Device& device, int world, int rank, int64_t rows, int cols, int64_t kept);
+  // A heap for calls of up to `rows` rows of `cols` columns and `kept` returned rows, and (mixture
+  // of experts) two buffers of `moe_rows` expert rows.
+  PeerCollectives(const Device& device, int world, int rank, int64_t rows, int cols, int64_t kept,
+                  int64_t moe_rows = 0);
   ~PeerCollectives() override;
 
   // This rank's heap as an opaque IPC handle; `connect` opens every rank's handle (in rank order).
@@ -32,18 +34,22 @@ class PeerCollectives : public Collectives {
   float* partial_buffer(size_t floats) override;
   __nv_bfloat16* residual_buffer() override;
   __nv_bfloat16* hidden_buffer() override;
+  __nv_bfloat16* moe_rows(int which, size_t rows) override;
+  void moe_combine_norm(int which, const int32_t* pos_all, const int32_t* ids, const float* weights,
+                        int experts_local, const __nv_bfloat16* norm, float eps, int rows, int k,
+                        int cols, cudaStream_t stream) override;
   // A device-side barrier of every rank (used before the heap is released).
   void barrier(cudaStream_t stream);
 
  private:
   Device device_;
   int world_, rank_;
-  int64_t rows_, kept_;
+  int64_t rows_, kept_, moe_rows_;
   int cols_;
   void* heap_ = nullptr;
   size_t heap_bytes_ = 0;
   size_t off_signal_, off_arrivals_, off_epoch_, off_partial_, off_residual_, off_hidden_,
-      off_gvalue_, off_gindex_;
+      off_gvalue_, off_gindex_, off_moe_;
   std::vector<void*> peer_base_;   // every rank's heap as mapped here (own heap at rank_)
   std::vector<bool> opened_;
   foa::PeerBuffers peers_{};

@@ -7,6 +7,7 @@
 #include "kernels/attention.cuh"
 #include "kernels/gemm.cuh"
 #include "kernels/quant.cuh"
+#include "kernels/moe.cuh"
 #include "kernels/ops.cuh"
 
 namespace foa::engine {
@@ -99,6 +100,14 @@ DecoderModel::DecoderModel(const Device& device, ModelConfig cfg, int tp, int ra
   if (inter % tp_ != 0 || (inter / tp_) % 128 != 0)
     throw Unsupported("the intermediate width does not split into 128-row blocks over the chips");
   inter_l_ = inter / tp_;
+  if (cfg_.experts > 0) {
+    // Experts split evenly over the ranks (expert parallelism = tensor parallelism here).
+    if (cfg_.experts % tp_ != 0) throw Unsupported("the experts do not split evenly over the chips");
+    if (cfg_.expert_intermediate % 128 != 0) throw Unsupported("the expert width is not a multiple of 128");
+    if (cfg_.top_k <= 0 || cfg_.top_k > 32 || cfg_.experts > 512) throw Unsupported("the routing is outside 32 of 512 experts");
+    experts_l_ = cfg_.experts / tp_;
+    expert_first_ = rank_ * experts_l_;
+  }
   vocab_l_ = (cfg_.vocab + tp_ - 1) / tp_;
   vocab_l_ = (vocab_l_ + 7) / 8 * 8;
   vocab_begin_ = rank_ * vocab_l_;
@@ -119,6 +128,17 @@ DecoderModel::~DecoderModel() {
   clear_graphs();
   for (auto& e : stage_done_)
     if (e) cudaEventDestroy(e);
+}
+
+int DecoderModel::moe_tile(int64_t rows) const {
+  // Token tiles near the rows an expert receives on average (16 to 128).
+  const int64_t per = rows * std::max(cfg_.top_k, 1) / std::max(cfg_.experts, 1);
+  return per <= 16 ? 16 : per <= 32 ? 32 : per <= 64 ? 64 : 128;
+}
+
+int64_t DecoderModel::moe_capacity(int64_t rows) const {
+  // Every selection plus a partial tile per local expert, for the largest tile.
+  return (rows * cfg_.top_k + static_cast<int64_t>(experts_l_) * 127 + 127) / 128 * 128;
 }
 
 void DecoderModel::clear_graphs() {
@@ -166,6 +186,12 @@ void DecoderModel::allocate_weights() {
     if (cfg_.experts == 0) {
       plan.push_back({p + "gate_up", {2 * inter_l_, H}});
       plan.push_back({p + "down", {H, inter_l_}});
+    } else {
+      // Router (every expert, on every rank) and this rank's experts, one after another.
+      const int64_t I = cfg_.expert_intermediate;
+      plan.push_back({p + "router", {cfg_.experts, H}});
+      plan.push_back({p + "experts_gate_up", {static_cast<int64_t>(experts_l_) * 2 * I, H}});
+      plan.push_back({p + "experts_down", {static_cast<int64_t>(experts_l_) * H, I}});
     }
   }
   const std::string& wf = cfg_.weight_format;
@@ -329,6 +355,19 @@ void DecoderModel::init_random(uint64_t seed, float stdv) {
     } else if (leaf == "down") {
       full_cols = cfg_.intermediate;
       col_offset = static_cast<long>(rank_) * inter_l_;
+    } else if (leaf == "experts_gate_up") {
+      const int I = cfg_.expert_intermediate;
+      for (int r = 0; r < rows; ++r) {
+        const int e = expert_first_ + r / (2 * I), rr = r % (2 * I), block = rr / 128;
+        full[r] = (block / 2) * 128 + rr % 128;
+        tags[r] = name_tag(prefix + "experts." + std::to_string(e) + (block % 2 == 0 ? ".gate" : ".up"));
+      }
+    } else if (leaf == "experts_down") {
+      for (int r = 0; r < rows; ++r) {
+        const int e = expert_first_ + r / H;
+        full[r] = r % H;
+        tags[r] = name_tag(prefix + "experts." + std::to_string(e) + ".down");
+      }
     }
     (void)H;
     if (map_rows.size() < static_cast<size_t>(rows) * 4) {
@@ -372,6 +411,23 @@ void DecoderModel::ensure_workspace(int64_t rows, int64_t kept, int64_t splits, 
       ws_qs_ = HbmBuffer(device_, std::max<int64_t>(kmax / 128 * R * 4, R * kmax / 16));
     }
     ws_rows_ = R;
+    changed = true;
+  }
+  if (cfg_.experts > 0 && rows > ws_moe_rows_) {
+    const int64_t R = std::max<int64_t>(256, next_pow2(rows));
+    const int64_t E = cfg_.experts, K = cfg_.top_k, I = cfg_.expert_intermediate;
+    const int64_t cap = moe_capacity(R);
+    ws_logits_e_ = HbmBuffer(device_, R * E * 2);
+    ws_ids_ = HbmBuffer(device_, R * K * 4);
+    ws_rw_ = HbmBuffer(device_, R * K * 4);
+    ws_pos_ = HbmBuffer(device_, static_cast<int64_t>(tp_) * R * K * 4);
+    ws_src_ = HbmBuffer(device_, cap * 4);
+    ws_tile_e_ = HbmBuffer(device_, (cap / 16 + 1) * 4);
+    ws_tiles_ = HbmBuffer(device_, 256);
+    ws_xs_ = HbmBuffer(device_, cap * H * 2);
+    ws_eact_ = HbmBuffer(device_, cap * I * 2);
+    ws_y_ = HbmBuffer(device_, cap * H * 2);
+    ws_moe_rows_ = R;
     changed = true;
   }
   if (kept > ws_kept_) {
@@ -649,12 +705,71 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     }
     const std::string next_norm =
         l + 1 < cfg_.layers ? "layers." + std::to_string(l + 1) + ".in_norm" : "final_norm";
+    // Attention output projection, then the post-attention RMSNorm (fused with the cross-rank
+    // sum under tensor parallelism).
     if (!tp) {
       gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
            foa::kEpiBf16, x);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
                         H, cfg_.eps, s),
            "rmsnorm");
+    } else {
+      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
+      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
+           foa::kEpiF32, nullptr);
+      coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
+      ++kernels;
+    }
+    if (cfg_.experts > 0) {
+      // Mixture of experts (rows replicated on every rank; this rank's experts only): router,
+      // routing, grouping by expert, grouped gate/up + SwiGLU and down GEMMs, then the combine
+      // in choice order fused with the next RMSNorm (over NVLink under expert parallelism).
+      const int E = cfg_.experts, Kc = cfg_.top_k, I = cfg_.expert_intermediate;
+      const int tile = moe_tile(T);
+      const int64_t cap = moe_capacity(T);
+      gemm(h, H, ws(p + "router"), static_cast<int>(T), E, H, ws_logits_e_.data(), E, foa::kEpiBf16, nullptr);
+      fail(foa::moe_route(bf(ws_logits_e_), E, static_cast<int>(T), E, Kc, cfg_.norm_topk, i32(ws_ids_),
+                          static_cast<float*>(ws_rw_.data()), s),
+           "moe route");
+      fail(foa::moe_align_ranks(i32(ws_ids_), static_cast<int>(T), Kc, E, 0, experts_l_, tp_, rank_, tile,
+                                static_cast<int>(cap), i32(ws_pos_), i32(ws_src_), i32(ws_tile_e_),
+                                i32(ws_tiles_), s),
+           "moe align");
+      fail(foa::moe_gather(h, H, i32(ws_src_), i32(ws_tiles_), tile, static_cast<int>(cap), H, bf(ws_xs_), s),
+           "moe gather");
+      __nv_bfloat16* y = tp ? coll_->moe_rows(l & 1, static_cast<size_t>(cap)) : bf(ws_y_);
+      auto grouped = [&](const void* a, const WeightSlot& wt, int N, int Kd, void* c, int ldc, int epi) {
+        foa::GemmArgs g;
+        g.a = a;
+        g.lda = Kd;
+        g.w = wt.ptr;
+        g.ldw = Kd;
+        g.M = static_cast<int>(cap);
+        g.N = N;
+        g.K = Kd;
+        g.c = c;
+        g.ldc = ldc;
+        g.epilogue = epi;
+        g.mode = foa::kModeSwap;
+        g.status = st->status;
+        g.group_tiles = i32(ws_tiles_);
+        g.tile_group = i32(ws_tile_e_);
+        g.group_tile = tile;
+        g.groups = experts_l_;
+        fail(foa::gemm_bf16(g, s), "grouped gemm");
+      };
+      grouped(ws_xs_.data(), W.at(p + "experts_gate_up"), 2 * I, H, ws_eact_.data(), I, foa::kEpiSwiGLU);
+      grouped(ws_eact_.data(), W.at(p + "experts_down"), H, I, y, H, foa::kEpiBf16);
+      if (!tp) {
+        fail(foa::moe_combine_norm(y, H, i32(ws_pos_), static_cast<float*>(ws_rw_.data()), static_cast<int>(T),
+                                   Kc, H, x, H, w(next_norm), cfg_.eps, h, H, s),
+             "moe combine");
+      } else {
+        coll_->moe_combine_norm(l & 1, i32(ws_pos_), i32(ws_ids_), static_cast<float*>(ws_rw_.data()),
+                                experts_l_, w(next_norm), cfg_.eps, static_cast<int>(T), Kc, H, s);
+        ++kernels;
+      }
+    } else if (!tp) {
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr);
       gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
@@ -663,11 +778,6 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                         cfg_.eps, s),
            "rmsnorm");
     } else {
-      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
-      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
-           foa::kEpiF32, nullptr);
-      coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
-      ++kernels;
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr);
       partial = coll_->partial_buffer(static_cast<size_t>(T) * H);

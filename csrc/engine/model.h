@@ -83,6 +83,13 @@ class Collectives {
   virtual __nv_bfloat16* hidden_buffer() = 0;
   // Marks the start of a call (before its launches or its graph launch, on the call's stream).
   virtual void begin_call(cudaStream_t stream) = 0;
+  // Expert parallelism: this rank's expert-row buffer `which` (0 or 1, alternating by layer) of
+  // the symmetric heap, and the combine that reads every rank's rows after a barrier, adds the
+  // weighted sum to the residual and writes the next RMSNorm's rows (moe_combine_norm contract).
+  virtual __nv_bfloat16* moe_rows(int which, size_t rows) = 0;
+  virtual void moe_combine_norm(int which, const int32_t* pos_all, const int32_t* ids,
+                                const float* weights, int experts_local, const __nv_bfloat16* norm,
+                                float eps, int rows, int k, int cols, cudaStream_t stream) = 0;
 };
 
 struct WeightSlot {
@@ -122,6 +129,11 @@ class DecoderModel {
   int kv_head_first() const { return kvh_first_; }
   int q_head_first() const { return qh_first_; }
   int intermediate_local() const { return inter_l_; }
+  int experts_local() const { return experts_l_; }
+  int expert_first() const { return expert_first_; }
+  // Expert rows of a call of `rows` rows (the grouped GEMM's sorted buffer, padded per expert).
+  int64_t moe_capacity(int64_t rows) const;
+  int moe_tile(int64_t rows) const;
   int vocab_begin() const { return vocab_begin_; }
   int vocab_end() const { return vocab_end_; }
   int vocab_local() const { return vocab_l_; }
@@ -161,6 +173,7 @@ class DecoderModel {
   ModelConfig cfg_;
   int tp_, rank_;
   int qh_l_, kvh_l_, qh_first_, kvh_first_, inter_l_, vocab_begin_, vocab_end_, vocab_l_;
+  int experts_l_ = 0, expert_first_ = 0;
   std::map<std::string, WeightSlot> weights_;
   HbmBuffer arena_;
   size_t arena_bytes_ = 0;
@@ -174,6 +187,9 @@ class DecoderModel {
       ws_tokens_, ws_stage_, ws_part_o_, ws_part_lse_, ws_gemm_, ws_counters_, ws_partial_;
   // Quantized inputs of W8A8 / W4A4 projections: codes and scales of the widest input.
   HbmBuffer ws_qa_, ws_qs_;
+  // Mixture of experts: router logits, routing, grouping and the sorted expert rows.
+  HbmBuffer ws_logits_e_, ws_ids_, ws_rw_, ws_pos_, ws_src_, ws_tile_e_, ws_tiles_, ws_xs_, ws_eact_, ws_y_;
+  int64_t ws_moe_rows_ = 0;
   size_t stage_capacity_ = 0;
   std::vector<uint8_t> host_stage_;
   HostBuffer pinned_stage_[2];

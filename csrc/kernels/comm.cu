@@ -155,6 +155,74 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
   }
 }
 
+template <int kVec>
+__global__ void __launch_bounds__(256) tp_moe_combine_kernel(const MoeCombineArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  __shared__ int ok_s;
+  if (threadIdx.x == 0) {
+    const unsigned long long v = barrier_value(a.epoch, a.site, 0);
+    if (blockIdx.x == 0) signal_all(a.peers, a.rank, a.world, v);
+    ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
+  }
+  __syncthreads();
+  if (!ok_s) return;
+  const int r = blockIdx.x;
+  const long n = (long)a.rows * a.k;
+  float xs[kVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c >= a.cols) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < a.k; ++j) {
+      const long sel = (long)r * a.k + j;
+      const int owner = a.ids[sel] / a.experts_local;
+      if (owner < 0 || owner >= a.world) continue;
+      const int p = a.pos[owner * n + sel];
+      if (p < 0) continue;
+      const float w = a.weights[sel];
+      const uint4 q = *reinterpret_cast<const uint4*>(a.y[owner] + (long)p * a.ldy + c);
+      const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        acc[2 * t] = __fadd_rn(acc[2 * t], __fmul_rn(w, bf16_lo(v[t])));
+        acc[2 * t + 1] = __fadd_rn(acc[2 * t + 1], __fmul_rn(w, bf16_hi(v[t])));
+      }
+    }
+    __nv_bfloat16* xr = a.peers.residual[a.rank] + (long)r * a.cols + c;
+    const uint4 q = *reinterpret_cast<const uint4*>(xr);
+    const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float m0 = __bfloat162float(__float2bfloat16_rn(acc[2 * t]));
+      const float m1 = __bfloat162float(__float2bfloat16_rn(acc[2 * t + 1]));
+      o[t] = pack_bf16x2(bf16_lo(v[t]) + m0, bf16_hi(v[t]) + m1);
+      xs[i][2 * t] = bf16_lo(o[t]);
+      xs[i][2 * t + 1] = bf16_hi(o[t]);
+      ss += xs[i][2 * t] * xs[i][2 * t] + xs[i][2 * t + 1] * xs[i][2 * t + 1];
+    }
+    *reinterpret_cast<uint4*>(xr) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  const float total = block_sum(ss, red);
+  const float inv = rsqrtf(total / (float)a.cols + a.eps);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c >= a.cols) continue;
+    const uint4 wv = *reinterpret_cast<const uint4*>(a.norm + c);
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      o[t] = pack_bf16x2(xs[i][2 * t] * inv * bf16_lo(ww[t]), xs[i][2 * t + 1] * inv * bf16_hi(ww[t]));
+    *reinterpret_cast<uint4*>(a.peers.hidden[a.rank] + (long)r * a.cols + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 __global__ void __launch_bounds__(256) tp_argmax_kernel(const ArgmaxArgs a) {
   pdl_wait();
   pdl_trigger();
@@ -204,6 +272,14 @@ __global__ void tp_barrier_kernel(PeerBuffers peers, const unsigned long long* e
 __global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { *p = v; }
 
 }  // namespace
+
+int tp_moe_combine_norm(const MoeCombineArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0) return 0;
+  if (a.cols % 8 != 0 || a.cols > 8 * 256 * 4 || a.world < 1 || a.world > kMaxRanks) return -2;
+  const int vec = (a.cols / 8 + 255) / 256;
+  auto kernel = vec <= 1 ? tp_moe_combine_kernel<1> : vec <= 2 ? tp_moe_combine_kernel<2> : tp_moe_combine_kernel<4>;
+  return launch_pdl(kernel, dim3(a.rows), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -5;
+}
 
 int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream) {
   set_u64_kernel<<<1, 1, 0, stream>>>(epoch, value);

@@ -48,6 +48,27 @@ struct ArgmaxArgs {
 // Exchanges every rank's (value, index) candidates and keeps the first maximum.
 int tp_argmax(const ArgmaxArgs& args, cudaStream_t stream);
 
+struct MoeCombineArgs {
+  PeerBuffers peers;                       // residual, hidden and signal slots
+  const __nv_bfloat16* y[kMaxRanks];       // every rank's expert rows [capacity, cols] (BF16)
+  long ldy;
+  const int32_t* pos;                      // [world][rows * k]: a selection's row on its expert's rank
+  const int32_t* ids;                      // [rows, k] experts, best first
+  const float* weights;                    // [rows, k]
+  int experts_local;                       // experts per rank (rank of expert e: e / experts_local)
+  const __nv_bfloat16* norm;
+  float eps;
+  const unsigned long long* epoch;
+  int rows, k, cols, rank, world, site;
+  int* status;
+};
+
+// Expert-parallel combine over NVLink: after a barrier (every rank's expert rows in place), each
+// rank reads every selection's BF16 row from the rank that computed it and forms
+// residual = bf16(residual + bf16(sum_j w_j * y_j)) in choice order, then hidden = RMSNorm(residual)
+// * norm; every rank ends with the same rows.
+int tp_moe_combine_norm(const MoeCombineArgs& args, cudaStream_t stream);
+
 // Writes this call's epoch (stream-ordered, outside any captured graph).
 int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream);
 

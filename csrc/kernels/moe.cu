@@ -74,12 +74,18 @@ __global__ void route_kernel(const __nv_bfloat16* logits, long ld, int rows, int
 constexpr int kAlignThreads = 512;
 constexpr int kAlignWarps = kAlignThreads / 32;
 
+// CTA c groups the experts [first + c * count, first + (c + 1) * count) and writes its positions
+// to pos + c * rows * k; only CTA `local` writes the sorted rows' sources and tiles.
 __global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids, int rows, int k,
-                                                             int first, int count, int tile,
-                                                             int capacity, int32_t* pos, int32_t* src,
-                                                             int32_t* tile_expert, int32_t* tiles) {
+                                                             int first0, int count, int tile,
+                                                             int capacity, int local, int32_t* pos_all,
+                                                             int32_t* src, int32_t* tile_expert,
+                                                             int32_t* tiles) {
   pdl_wait();
   pdl_trigger();
+  const int first = first0 + (int)blockIdx.x * count;
+  const bool mine = (int)blockIdx.x == local;
+  int32_t* pos = pos_all + (long)blockIdx.x * rows * k;
   __shared__ int cnt[kMaxExperts], off[kMaxExperts], running[kMaxExperts], add[kMaxExperts];
   __shared__ int wcount[kAlignWarps][kMaxExperts];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -90,7 +96,8 @@ __global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids
     add[e] = 0;
     for (int w = 0; w < kAlignWarps; ++w) wcount[w][e] = 0;
   }
-  for (int p = tid; p < capacity; p += kAlignThreads) src[p] = -1;
+  if (mine)
+    for (int p = tid; p < capacity; p += kAlignThreads) src[p] = -1;
   __syncthreads();
   for (int i = tid; i < n; i += kAlignThreads) {
     const int e = ids[i] - first;
@@ -103,10 +110,10 @@ __global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids
       off[e] = o;
       o += (cnt[e] + tile - 1) / tile * tile;
     }
-    *tiles = o / tile;
+    if (mine) *tiles = o / tile;
   }
   __syncthreads();
-  for (int e = tid; e < count; e += kAlignThreads) {
+  for (int e = tid; e < count && mine; e += kAlignThreads) {
     const int t0 = off[e] / tile, nt = (cnt[e] + tile - 1) / tile;
     for (int t = 0; t < nt; ++t) tile_expert[t0 + t] = e;
   }
@@ -129,7 +136,7 @@ __global__ void __launch_bounds__(kAlignThreads) align_kernel(const int32_t* ids
       for (int w = 0; w < warp; ++w) before += wcount[w][e];
       const int p = off[e] + running[e] + before + before_lane;
       pos[i] = p;
-      src[p] = i / k;
+      if (mine) src[p] = i / k;
     } else if (i < n) {
       pos[i] = -1;
     }
@@ -194,7 +201,91 @@ __global__ void combine_kernel(const __nv_bfloat16* y, long ldy, const int32_t* 
   }
 }
 
+// One CTA of 256 threads per row: x = bf16(x + bf16(sum_j w_j * y_j)), then RMSNorm(x) * weight.
+template <int kVec>
+__global__ void __launch_bounds__(256) combine_norm_kernel(const __nv_bfloat16* y, long ldy, const int32_t* pos,
+                                                          const float* weights, int k, int cols,
+                                                          __nv_bfloat16* residual, long ldr,
+                                                          const __nv_bfloat16* norm, float eps,
+                                                          __nv_bfloat16* out, long ldo) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[8];
+  const int r = blockIdx.x;
+  float xs[kVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c >= cols) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int j = 0; j < k; ++j) {
+      const int p = pos[(long)r * k + j];
+      if (p < 0) continue;
+      const float w = weights[(long)r * k + j];
+      const uint4 q = *reinterpret_cast<const uint4*>(y + (long)p * ldy + c);
+      const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        acc[2 * t] = __fadd_rn(acc[2 * t], __fmul_rn(w, __uint_as_float(v[t] << 16)));
+        acc[2 * t + 1] = __fadd_rn(acc[2 * t + 1], __fmul_rn(w, __uint_as_float(v[t] & 0xFFFF0000u)));
+      }
+    }
+    __nv_bfloat16* xr = residual + (long)r * ldr + c;
+    const uint4 q = *reinterpret_cast<const uint4*>(xr);
+    const uint32_t v[4] = {q.x, q.y, q.z, q.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const float m0 = __bfloat162float(__float2bfloat16_rn(acc[2 * t]));
+      const float m1 = __bfloat162float(__float2bfloat16_rn(acc[2 * t + 1]));
+      const __nv_bfloat162 b = __floats2bfloat162_rn(__uint_as_float(v[t] << 16) + m0,
+                                                     __uint_as_float(v[t] & 0xFFFF0000u) + m1);
+      o[t] = *reinterpret_cast<const uint32_t*>(&b);
+      xs[i][2 * t] = __low2float(b);
+      xs[i][2 * t + 1] = __high2float(b);
+      ss += xs[i][2 * t] * xs[i][2 * t] + xs[i][2 * t + 1] * xs[i][2 * t + 1];
+    }
+    *reinterpret_cast<uint4*>(xr) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float total = 0.f;
+  for (int w = 0; w < 8; ++w) total += red[w];
+  const float inv = rsqrtf(total / (float)cols + eps);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int c = (threadIdx.x + i * 256) * 8;
+    if (c >= cols) continue;
+    const uint4 wq = *reinterpret_cast<const uint4*>(norm + c);
+    const uint32_t wv[4] = {wq.x, wq.y, wq.z, wq.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      const __nv_bfloat162 b = __floats2bfloat162_rn(xs[i][2 * t] * inv * __uint_as_float(wv[t] << 16),
+                                                     xs[i][2 * t + 1] * inv * __uint_as_float(wv[t] & 0xFFFF0000u));
+      o[t] = *reinterpret_cast<const uint32_t*>(&b);
+    }
+    *reinterpret_cast<uint4*>(out + (long)r * ldo + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 }  // namespace
+
+int moe_combine_norm(const __nv_bfloat16* y, long ldy, const int32_t* pos, const float* weights, int rows,
+                     int k, int cols, __nv_bfloat16* residual, long ldr, const __nv_bfloat16* norm, float eps,
+                     __nv_bfloat16* out, long ldo, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (cols % 8 != 0 || ldy % 8 != 0 || ldr % 8 != 0 || ldo % 8 != 0 || cols > 8 * 256 * 4) return -2;
+  const int vec = (cols / 8 + 255) / 256;
+  auto kernel = vec <= 1 ? combine_norm_kernel<1> : vec <= 2 ? combine_norm_kernel<2> : combine_norm_kernel<4>;
+  return launch_pdl(kernel, dim3(rows), dim3(256), 0, stream, y, ldy, pos, weights, k, cols, residual, ldr,
+                    norm, eps, out, ldo) == cudaSuccess
+             ? 0
+             : -5;
+}
 
 int moe_route(const __nv_bfloat16* logits, long ld, int rows, int experts, int k, bool normalize,
               int32_t* ids, float* weights, cudaStream_t stream) {
@@ -210,11 +301,20 @@ int moe_route(const __nv_bfloat16* logits, long ld, int rows, int experts, int k
 int moe_align(const int32_t* ids, int rows, int k, int experts, int first, int count, int tile,
               int capacity, int32_t* pos, int32_t* src, int32_t* tile_expert, int32_t* tiles,
               cudaStream_t stream) {
-  if (count <= 0 || count > kMaxExperts || first < 0 || first + count > experts || tile <= 0) return -2;
+  return moe_align_ranks(ids, rows, k, experts, first, count, 1, 0, tile, capacity, pos, src,
+                         tile_expert, tiles, stream);
+}
+
+int moe_align_ranks(const int32_t* ids, int rows, int k, int experts, int first, int count, int ranks,
+                    int local, int tile, int capacity, int32_t* pos, int32_t* src, int32_t* tile_expert,
+                    int32_t* tiles, cudaStream_t stream) {
+  if (count <= 0 || count > kMaxExperts || first < 0 || first + ranks * count > experts || tile <= 0 ||
+      ranks <= 0 || local < 0 || local >= ranks)
+    return -2;
   const long need = ((long)rows * k + (long)count * (tile - 1) + tile - 1) / tile * tile;
   if (capacity < need) return -3;
-  return launch_pdl(align_kernel, dim3(1), dim3(kAlignThreads), 0, stream, ids, rows, k, first, count,
-                    tile, capacity, pos, src, tile_expert, tiles) == cudaSuccess
+  return launch_pdl(align_kernel, dim3(ranks), dim3(kAlignThreads), 0, stream, ids, rows, k, first, count,
+                    tile, capacity, local, pos, src, tile_expert, tiles) == cudaSuccess
              ? 0
              : -5;
 }

@@ -32,6 +32,13 @@ int moe_align(const int32_t* ids, int rows, int k, int experts, int first, int c
               int capacity, int32_t* pos, int32_t* src, int32_t* tile_expert, int32_t* tiles,
               cudaStream_t stream);
 
+// Every expert-parallel rank's grouping at once: rank c (one CTA each) groups the experts
+// [first + c * count, first + (c + 1) * count) into pos + c * rows * k; `src`, `tile_expert` and
+// `tiles` are the grouping of rank `local`.
+int moe_align_ranks(const int32_t* ids, int rows, int k, int experts, int first, int count, int ranks,
+                    int local, int tile, int capacity, int32_t* pos, int32_t* src, int32_t* tile_expert,
+                    int32_t* tiles, cudaStream_t stream);
+
 // out[p] = x[src[p]] for the sorted rows in use (zeros for padding), BF16 rows of `cols`.
 int moe_gather(const __nv_bfloat16* x, long ldx, const int32_t* src, const int32_t* tiles, int tile,
                int capacity, int cols, __nv_bfloat16* out, cudaStream_t stream);
@@ -40,5 +47,11 @@ int moe_gather(const __nv_bfloat16* x, long ldx, const int32_t* src, const int32
 // where y holds BF16 expert rows [capacity, cols]. Selections with pos < 0 contribute nothing.
 int moe_combine(const __nv_bfloat16* y, long ldy, const int32_t* pos, const float* weights, int rows,
                 int k, int cols, __nv_bfloat16* residual, long ldr, cudaStream_t stream);
+
+// The combine followed by the next RMSNorm: residual = bf16(residual + bf16(sum_j w_j * y_j)),
+// out = bf16(RMSNorm(residual) * norm). cols <= 8192.
+int moe_combine_norm(const __nv_bfloat16* y, long ldy, const int32_t* pos, const float* weights, int rows,
+                     int k, int cols, __nv_bfloat16* residual, long ldr, const __nv_bfloat16* norm, float eps,
+                     __nv_bfloat16* out, long ldo, cudaStream_t stream);
 
 }  // namespace foa

@@ -678,7 +678,8 @@ void bind_engine(py::module_& m) {
   m.def("_tp_attach", [](PyDecoder& d, int world, int rank) {
     const auto& cfg = d.model->config();
     auto coll = std::make_shared<PeerCollectives>(d.model->device(), world, rank, cfg.rows,
-                                                  cfg.hidden, cfg.rows);
+                                                  cfg.hidden, cfg.rows,
+                                                  cfg.experts > 0 ? d.model->moe_capacity(cfg.rows) : 0);
     d.model->set_collectives(coll);
     return py::bytes(coll->handle());
   });

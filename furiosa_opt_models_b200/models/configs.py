@@ -20,6 +20,13 @@ CONFIGS: dict[str, dict] = {
         layers=2, q_heads=8, kv_heads=2, head_dim=64, vocab=1024, eps=1e-6, qk_norm=True, tied=True,
         rope=QWEN3_ROPE, window=4096, rows=8192,
     ),
+    # A tiny Qwen3-MoE geometry (16 experts, top-4) for the expert tests; splits over 2/4/8 chips.
+    "tiny-qwen3-moe": dict(
+        architecture="Qwen3MoeForCausalLM", family="qwen3_moe", size="tiny", hidden=256, intermediate=768,
+        layers=2, q_heads=8, kv_heads=2, head_dim=64, vocab=1024, eps=1e-6, qk_norm=True, tied=False,
+        rope=QWEN3_ROPE, window=4096, rows=8192, experts=16, top_k=4, expert_intermediate=256,
+        norm_topk=True,
+    ),
     "qwen3-0.6b": dict(
         architecture="Qwen3ForCausalLM", family="qwen3", size="0.6B", hidden=1024, intermediate=3072,
         layers=28, q_heads=16, kv_heads=8, head_dim=128, vocab=151936, eps=1e-6, qk_norm=True,

@@ -88,6 +88,14 @@ def forward(w: dict, cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> t
         a = rb(torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(T, qh * D))
         x = rb(x + linear(a, w[p + "o"]))
         h = rb(reference.rmsnorm(x, w[p + "post_norm"], eps))
+        if cfg.get("experts", 0):
+            E, I = cfg["experts"], cfg["expert_intermediate"]
+            moe = reference.moe_forward(h.bfloat16(), w[p + "router"].bfloat16(),
+                                        w[p + "experts_gate_up"].bfloat16().view(E, 2 * I, H),
+                                        w[p + "experts_down"].bfloat16().view(E, H, I), cfg["top_k"],
+                                        cfg.get("norm_topk", True))
+            x = rb(x + moe.float())
+            continue
         g, u = _gate_up(h, w[p + "gate_up"])
         act = rb(reference.swiglu(g, u)) if round_bf16 else torch.nn.functional.silu(g) * u
         x = rb(x + linear(act, w[p + "down"]))

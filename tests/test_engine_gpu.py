@@ -174,3 +174,40 @@ def test_quantized_decoder_matches_dense_contract(fmt):
             tol = 0.15 if fmt == "nvfp4_a4" else 5e-2
             assert logits[pick] >= top[0] - tol * max(1.0, abs(top[0].item())), (fmt, i, step)
             seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_moe_decoder_matches_dense(graphs):
+    """A tiny Qwen3-MoE decoder (16 experts, top-4) through the engine's routing, grouped expert
+    GEMMs and choice-order combine against the dense forward of the same weights."""
+    engine, cfg, device, model = _build("tiny-qwen3-moe")
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import dense
+
+    model.set_graphs(graphs)
+    w = _weights(model)
+    lengths = [9, 30, 64]
+    gen = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen, dtype=torch.int32) for n in lengths]
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(p).to_hbm(device), len(p), alloc.take(6))
+            for p in prompts]
+    steps = 6
+    out = serving.prefill(model, cache, seqs, list(range(len(seqs))))
+    tokens = [[t] for t in out.to_host().numpy().tolist()]
+    for _ in range(steps):
+        out = serving.decode(model, cache, seqs)
+        for i, t in enumerate(out.to_host().numpy().tolist()):
+            tokens[i].append(t)
+    device.synchronize()
+    for i, p in enumerate(prompts):
+        seq = p.clone()
+        for step in range(steps + 1):
+            logits = dense.forward(w, cfg, seq)[-1]
+            top = torch.topk(logits, 2).values
+            pick = tokens[i][step]
+            # A router logit one BF16 step apart can reorder or swap a selected expert.
+            assert logits[pick] >= top[0] - 5e-2 * max(1.0, abs(top[0].item())), (i, step)
+            seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
