@@ -340,7 +340,9 @@ Selection select(const LoadOptions& o, const Checkpoint& ck) {
     const bool inputs = ck.get("model.layers.0.self_attn.q_proj.input_scale") != nullptr;
     s.config.weight_format = (inputs && !(a16 && a16[0] == '1')) ? "nvfp4_a4" : "nvfp4";
   }
-  if (m.experts > 0) unsupported(l.name, "mixture-of-experts loads run through the expert-parallel path");
+  if (m.experts > 0 && m.experts % s.chips != 0)
+    unsupported("chips", "the " + std::to_string(m.experts) + " experts do not split over " +
+                             std::to_string(s.chips) + " chips");
   return s;
 }
 
@@ -653,6 +655,51 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D,
                 static_cast<int64_t>(qh_l) * D);
       upload(en + "o");
+    }
+    if (cfg.experts > 0) {
+      // Router (every expert) and this rank's experts, gate/up interleaved in 128-row blocks.
+      const int E = cfg.experts, El = model.experts_local(), e0 = model.expert_first();
+      const int64_t I = cfg.expert_intermediate;
+      if (auto* t = take(hf + "mlp.gate.weight", {E, H})) {
+        image(en + "router");
+        copy_rows(Source(t), 0, E, 0, 0, H, H);
+        upload(en + "router");
+      }
+      image(en + "experts_gate_up");
+      bool complete = true;
+      for (int x = 0; x < El; ++x) {
+        const std::string ep = hf + "mlp.experts." + std::to_string(e0 + x) + ".";
+        const auto* g = take(ep + "gate_proj.weight", {I, H});
+        const auto* u = take(ep + "up_proj.weight", {I, H});
+        if (!g || !u) {
+          complete = false;
+          continue;
+        }
+        const Source sg(g), su(u);
+        for (int64_t j = 0; j < I; ++j) {
+          const int64_t block = j / 128, in = j % 128, base = static_cast<int64_t>(x) * 2 * I;
+          sg.row(j, 0, H, host.data() + (base + block * 256 + in) * H);
+          su.row(j, 0, H, host.data() + (base + block * 256 + 128 + in) * H);
+        }
+      }
+      if (complete) upload(en + "experts_gate_up");
+      image(en + "experts_down");
+      complete = true;
+      for (int x = 0; x < El; ++x) {
+        const std::string ep = hf + "mlp.experts." + std::to_string(e0 + x) + ".";
+        if (auto* t = take(ep + "down_proj.weight", {H, I}))
+          copy_rows(Source(t), 0, H, static_cast<int64_t>(x) * H, 0, I, I);
+        else
+          complete = false;
+      }
+      if (complete) upload(en + "experts_down");
+      // Other ranks' experts are theirs to load.
+      for (int x = 0; x < E; ++x) {
+        if (x >= e0 && x < e0 + El) continue;
+        const std::string ep = hf + "mlp.experts." + std::to_string(x) + ".";
+        for (const char* n : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+          if (used.count(ep + n)) used[ep + n] = true;
+      }
     }
     if (cfg.experts == 0 && quantized) {
       // Gate and up rows alternate in 128-row blocks (see the BF16 path below).

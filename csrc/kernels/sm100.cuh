@@ -252,7 +252,7 @@ __device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
-// Untiled bulk copy global -> shared (no multicast), completing on `bar` with `bytes`
+// Untiled bulk copy global -> this CTA's shared memory, completing on `bar` with `bytes`
 // transaction bytes. Both addresses 16-byte aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile(

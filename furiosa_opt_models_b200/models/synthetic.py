@@ -134,4 +134,11 @@ def engine_weights(cfg: dict, hf: dict[str, torch.Tensor]) -> dict[str, torch.Te
         if p + "mlp.gate_proj.weight" in hf:
             out[e + "gate_up"] = interleave_gate_up(hf[p + "mlp.gate_proj.weight"], hf[p + "mlp.up_proj.weight"])
             out[e + "down"] = hf[p + "mlp.down_proj.weight"]
+        if p + "mlp.gate.weight" in hf:
+            E = cfg["experts"]
+            out[e + "router"] = hf[p + "mlp.gate.weight"]
+            out[e + "experts_gate_up"] = torch.cat([
+                interleave_gate_up(hf[p + f"mlp.experts.{x}.gate_proj.weight"], hf[p + f"mlp.experts.{x}.up_proj.weight"])
+                for x in range(E)])
+            out[e + "experts_down"] = torch.cat([hf[p + f"mlp.experts.{x}.down_proj.weight"] for x in range(E)])
     return out

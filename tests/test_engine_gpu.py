@@ -88,7 +88,8 @@ def test_refusals_match_reference_messages():
         model.forward([dec.Request([[0]], 0, ids, positions=ids)], cache)
 
 
-def test_load_checkpoint_strictly_and_decode(tmp_path):
+@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-qwen3-moe"])
+def test_load_checkpoint_strictly_and_decode(tmp_path, name):
     """A synthetic HF checkpoint through Checkpoint -> LoadOptions.load: the loaded decoder's
     greedy continuation agrees with the dense forward of the checkpoint's own weights."""
     import furiosa_opt_engine as engine
@@ -96,7 +97,7 @@ def test_load_checkpoint_strictly_and_decode(tmp_path):
     from furiosa_opt_models_b200 import serving
     from furiosa_opt_models_b200.models import configs, dense, synthetic
 
-    cfg = configs.get("tiny-qwen3")
+    cfg = configs.get(name)
     hf = synthetic.write(str(tmp_path / "m"), cfg, seed=5, std=0.05, shards=2)
     w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
     ck = engine.Checkpoint(str(tmp_path / "m"))
@@ -115,7 +116,8 @@ def test_load_checkpoint_strictly_and_decode(tmp_path):
     seq = prompt.clone()
     for t in toks:
         logits = dense.forward(w, cfg, seq)[-1]
-        assert logits[int(t)] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+        tol = 5e-2 if cfg.get("experts") else 1e-2
+        assert logits[int(t)] >= logits.max() - tol * max(1.0, abs(logits.max().item()))
         seq = torch.cat([seq, torch.tensor([int(t)], dtype=torch.int32)])
 
 

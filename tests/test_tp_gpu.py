@@ -39,3 +39,18 @@ def test_tp_matches_single_gpu(world, tmp_path):
     agree = sum(a == b for s1, s2 in zip(one, many) for a, b in zip(s1, s2))
     total = sum(len(s) for s in one)
     assert agree >= 0.9 * total, (agree, total)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_expert_parallel_matches_single_gpu(world, tmp_path):
+    """Qwen3-MoE with experts sharded over `world` ranks (the combine reads peers' expert rows over
+    NVLink) against one GPU holding every expert."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    one = _run(1, str(tmp_path / "ep1.json"), "tiny-qwen3-moe", 12)
+    many = _run(world, str(tmp_path / f"ep{world}.json"), "tiny-qwen3-moe", 12)
+    assert [t[:4] for t in one] == [t[:4] for t in many]
+    agree = sum(a == b for s1, s2 in zip(one, many) for a, b in zip(s1, s2))
+    total = sum(len(s) for s in one)
+    assert agree >= 0.9 * total, (agree, total)
