@@ -1,0 +1,48 @@
+"""What the plugin serves, checked where vLLM parses its configuration and each request (the
+reference's refusals: integrations/furiosa-opt-vllm/furiosa_opt_vllm/admission.py). A refusal
+names the option and why, and vLLM reports it before any device work."""
+
+from __future__ import annotations
+
+
+class Refused(ValueError):
+    """An option or request the plugin does not serve."""
+
+    def __init__(self, option: str, reason: str):
+        super().__init__(f"{option}: {reason}")
+        self.option = option
+        self.reason = reason
+
+    def __reduce__(self):
+        return (Refused, (self.option, self.reason))
+
+
+CHIPS = (1, 2, 4, 8)
+
+
+def options(pipeline: int, tensor: int, speculative: bool, lora: bool, kv_cache_dtype: str,
+            prefill_context: int = 1, decode_context: int = 1) -> None:
+    """Engine-level options: parallelism, speculation, adapters, cache precision."""
+    if pipeline != 1:
+        raise Refused("pipeline_parallel_size", "pipeline parallelism is not served; use tensor parallelism")
+    if tensor not in CHIPS:
+        raise Refused("tensor_parallel_size", f"{tensor} GPUs; a replica runs on 1, 2, 4 or 8")
+    if prefill_context != 1 or decode_context != 1:
+        raise Refused("context_parallel_size", "context parallelism is not served")
+    if speculative:
+        raise Refused("speculative_config", "speculative decoding is not served")
+    if lora:
+        raise Refused("enable_lora", "adapters are not served through this plugin")
+    if kv_cache_dtype not in ("auto", "bfloat16"):
+        raise Refused("kv_cache_dtype", "the engine caches keys and values in BF16")
+
+
+def sampling(temperature: float, top_k: int, top_p: float, n: int, logprobs, prompt_logprobs,
+             min_tokens: int = 0) -> None:
+    """Request-level: the engine's head returns each row's first maximum (greedy decoding)."""
+    if temperature > 0:
+        raise Refused("temperature", "the engine decodes greedily; use temperature=0")
+    if logprobs is not None or prompt_logprobs is not None:
+        raise Refused("logprobs", "the engine returns tokens, not log-probabilities")
+    if n != 1:
+        raise Refused("n", "one sequence per request")

@@ -1,0 +1,47 @@
+"""vLLM platform for B200 through the engine: vLLM's CUDA platform, with the plugin's worker,
+16-token KV pages, no torch.compile or vLLM CUDA graphs (the engine captures its own), synchronous
+scheduling, and the plugin's refusals (the reference's platform:
+integrations/furiosa-opt-vllm/furiosa_opt_vllm/platform.py)."""
+
+from __future__ import annotations
+
+from vllm.platforms.cuda import NvmlCudaPlatform
+
+from . import admission
+
+
+class B200Platform(NvmlCudaPlatform):
+    @classmethod
+    def check_and_update_config(cls, vllm_config) -> None:
+        pc = vllm_config.parallel_config
+        cc = vllm_config.cache_config
+        admission.options(
+            pipeline=pc.pipeline_parallel_size,
+            tensor=pc.tensor_parallel_size,
+            speculative=vllm_config.speculative_config is not None,
+            lora=vllm_config.lora_config is not None,
+            kv_cache_dtype=str(cc.cache_dtype),
+            prefill_context=getattr(pc, "prefill_context_parallel_size", 1),
+            decode_context=getattr(pc, "decode_context_parallel_size", 1),
+        )
+        super().check_and_update_config(vllm_config)
+        pc.worker_cls = "furiosa_opt_vllm.worker.Worker"
+        cc.block_size = 16
+        vllm_config.scheduler_config.async_scheduling = False
+        mc = vllm_config.model_config
+        if mc is not None:
+            mc.enforce_eager = True
+        try:
+            from vllm.config import CompilationMode, CUDAGraphMode
+
+            vllm_config.compilation_config.mode = CompilationMode.NONE
+            vllm_config.compilation_config.cudagraph_mode = CUDAGraphMode.NONE
+        except Exception:
+            pass
+
+    @classmethod
+    def validate_request(cls, processed_inputs, params) -> None:
+        if getattr(params, "temperature", None) is None:
+            raise admission.Refused("pooling", "the engine serves generation")
+        admission.sampling(params.temperature, params.top_k, params.top_p, params.n, params.logprobs,
+                           params.prompt_logprobs)

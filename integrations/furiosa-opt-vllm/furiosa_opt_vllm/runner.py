@@ -1,0 +1,82 @@
+"""The model runner: turns each scheduled step into one engine call.
+
+vLLM's scheduler decides which requests run, how many tokens each feeds and which KV blocks they
+hold; this runner keeps each request's known tokens and block table, stages the step's tokens in
+one host-to-device copy, calls the engine (`Decoder.forward`) and returns the sampled tokens in
+vLLM's order (the reference's runner: integrations/furiosa-opt-vllm/furiosa_opt_vllm/runner.py).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+from .paging import BlockTable, first_group
+from .request import State
+
+
+class Runner:
+    def __init__(self, model, device, cache):
+        import furiosa_opt_engine as engine
+        from furiosa_opt_engine import decoder as dec
+
+        self.engine, self.dec = engine, dec
+        self.model, self.device, self.cache = model, device, cache
+        self.states: dict[str, State] = {}
+
+    # -------------------------------------------------------------------- scheduler bookkeeping
+    def update(self, so) -> None:
+        for rid in so.finished_req_ids:
+            self.states.pop(rid, None)
+        for nr in so.scheduled_new_reqs:
+            prompt = list(nr.prefill_token_ids if getattr(nr, "prefill_token_ids", None) else nr.prompt_token_ids)
+            self.states[nr.req_id] = State(prompt, len(prompt), nr.num_computed_tokens,
+                                           BlockTable(first_group(nr.block_ids)))
+        cr = so.scheduled_cached_reqs
+        resumed = getattr(cr, "resumed_req_ids", set()) or set()
+        all_tokens = getattr(cr, "all_token_ids", {}) or {}
+        for i, rid in enumerate(cr.req_ids):
+            st = self.states[rid]
+            nb = cr.new_block_ids[i]
+            if rid in resumed:
+                st.table.replace(first_group(nb))
+                if rid in all_tokens:
+                    st.tokens = list(all_tokens[rid])
+            elif nb is not None:
+                st.table.append(first_group(nb))
+            st.computed = cr.num_computed_tokens[i]
+
+    # -------------------------------------------------------------------- one call
+    def step(self, so) -> tuple[list[str], list[list[int]]]:
+        """Runs the scheduled rows; returns (request IDs in order, sampled tokens per request)."""
+        self.update(so)
+        order = list(so.num_scheduled_tokens.keys())
+        if not order:
+            return [], []
+        counts = [int(so.num_scheduled_tokens[r]) for r in order]
+        flat = np.empty(sum(counts), dtype=np.int32)
+        keeps, at = [], 0
+        for rid, n in zip(order, counts):
+            st = self.states[rid]
+            flat[at : at + n] = st.scheduled(n)
+            keeps.append(st.samples_after(n))
+            at += n
+        tokens = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device)
+        reqs, at = [], 0
+        for rid, n, keep in zip(order, counts, keeps):
+            st = self.states[rid]
+            reqs.append(self.dec.Request([st.table.blocks], st.computed, tokens[at : at + n],
+                                         self.dec.Keep.LAST if keep else self.dec.Keep.NONE))
+            at += n
+        out = self.model.forward(reqs, self.cache)
+        picked = out.to_host().numpy().tolist() if any(keeps) else []
+        sampled, k = [], 0
+        for rid, n, keep in zip(order, counts, keeps):
+            st = self.states[rid]
+            st.computed += n
+            if keep:
+                st.tokens.append(int(picked[k]))
+                sampled.append([int(picked[k])])
+                k += 1
+            else:
+                sampled.append([])
+        return order, sampled

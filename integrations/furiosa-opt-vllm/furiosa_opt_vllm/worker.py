@@ -1,0 +1,106 @@
+"""The vLLM worker of one GPU: vLLM's executor calls it as it calls its own GPU worker, and it
+answers through the engine. It loads the checkpoint with the engine (every chip of a replica is
+one worker process, joined in vLLM's process group), reports the engine's KV layout so vLLM's
+cache manager hands out the engine's blocks, allocates the cache once vLLM sized it, and runs
+every scheduled step as one engine call (the reference's worker:
+integrations/furiosa-opt-vllm/furiosa_opt_vllm/worker.py)."""
+
+from __future__ import annotations
+
+import torch
+from vllm.v1.outputs import ModelRunnerOutput
+from vllm.v1.worker.worker_base import WorkerBase
+
+from . import cache as kv
+from . import load
+from .runner import Runner
+
+
+class Worker(WorkerBase):
+    def __init__(self, vllm_config, local_rank: int, rank: int, distributed_init_method: str,
+                 is_driver_worker: bool = False, **kwargs):
+        super().__init__(vllm_config=vllm_config, local_rank=local_rank, rank=rank,
+                         distributed_init_method=distributed_init_method, is_driver_worker=is_driver_worker)
+        self.model = self.device = self.cache = self.runner = None
+        self.pending: ModelRunnerOutput | None = None
+
+    # ------------------------------------------------------------------------ life cycle
+    def init_device(self) -> None:
+        from vllm.distributed import ensure_model_parallel_initialized, init_distributed_environment
+
+        torch.cuda.set_device(self.local_rank)
+        pc = self.parallel_config
+        init_distributed_environment(pc.world_size, self.rank, self.distributed_init_method, self.local_rank,
+                                     backend="nccl")
+        ensure_model_parallel_initialized(pc.tensor_parallel_size, pc.pipeline_parallel_size)
+
+    def load_model(self, *args, **kwargs) -> None:
+        self.model, self.device = load.load(self.model_config.model, self.rank,
+                                            self.parallel_config.tensor_parallel_size)
+
+    def determine_available_memory(self) -> int:
+        free, total = torch.cuda.mem_get_info()
+        budget = int(total * self.cache_config.gpu_memory_utilization) - (total - free)
+        # The engine addresses each layer's cache with 32-bit byte offsets.
+        layers = len(self.model.cache.groups[0].layers)
+        return max(min(budget, layers * ((1 << 31) - (1 << 20))), 0)
+
+    def get_kv_cache_spec(self):
+        return kv.spec(self.model, self.model_config)
+
+    def initialize_from_config(self, kv_cache_config) -> None:
+        from furiosa_opt_engine import decoder as dec
+
+        self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
+        self.runner = Runner(self.model, self.device, self.cache)
+
+    def compile_or_warm_up_model(self):
+        from vllm.v1.worker.worker_base import CompilationTimes
+
+        return CompilationTimes(0.0, 0.0)
+
+    def get_supported_tasks(self):
+        return ("generate",)
+
+    def check_health(self) -> None:
+        pass
+
+    def update_max_model_len(self, max_model_len: int) -> None:
+        self.model_config.max_model_len = max_model_len
+
+    def reset_mm_cache(self) -> None:
+        pass
+
+    def reset_encoder_cache(self) -> None:
+        pass
+
+    def get_kv_connector_handshake_metadata(self):
+        return None
+
+    def take_draft_token_ids(self):
+        return None
+
+    def shutdown(self) -> None:
+        if self.model is not None and self.parallel_config.tensor_parallel_size > 1:
+            from furiosa_opt_models_b200.parallel import tp
+
+            tp.detach(self.model)
+        self.model = self.runner = self.cache = None
+
+    # ------------------------------------------------------------------------ steps
+    def execute_model(self, scheduler_output):
+        if scheduler_output.total_num_scheduled_tokens == 0:
+            self.runner.update(scheduler_output)
+            self.pending = ModelRunnerOutput(req_ids=[], req_id_to_index={})
+            return None
+        ids, sampled = self.runner.step(scheduler_output)
+        self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
+                                         sampled_token_ids=sampled)
+        return None
+
+    def sample_tokens(self, grammar_output=None):
+        out, self.pending = self.pending, None
+        return out
+
+    def execute_dummy_batch(self) -> None:
+        pass

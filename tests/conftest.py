@@ -27,3 +27,13 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+# The framework plugins live beside the engine, each a package of its own directory.
+import os as _os
+import sys as _sys
+
+_ROOT = _os.path.dirname(_os.path.dirname(_os.path.abspath(__file__)))
+for _plugin in ("furiosa-opt-vllm", "furiosa-opt-sglang"):
+    _path = _os.path.join(_ROOT, "integrations", _plugin)
+    if _os.path.isdir(_path) and _path not in _sys.path:
+        _sys.path.insert(0, _path)

@@ -1,0 +1,81 @@
+"""The plugin's host contracts without a GPU: batch framing and planning, block tables, request
+state, refusals."""
+
+import pickle
+
+import pytest
+
+from furiosa_opt_vllm import admission, batch, paging
+from furiosa_opt_vllm.request import State
+
+
+def test_call_groups_chunks_and_keeps_last_rows():
+    rows = (batch.Row("a", 5, False), batch.Row("a", 6, True), batch.Row("b", 0, False))
+    call = batch.Call[str].plan(rows, every=False)
+    assert call.requests == (batch.Request("a", 5, (0, 1), True), batch.Request("b", 0, (2,), False))
+    assert call.kept == (1,)
+    assert batch.Call[int].plan((batch.Row(0, 4, False), batch.Row(1, 0, True)), every=True).kept == (0, 1)
+
+
+def test_batch_copies_tokens_and_derives_history():
+    tokens = [1, 2, 3]
+    parsed = batch.Batch.parse(tokens, [2, 1], [7, 1])
+    tokens[0] = 9
+    assert parsed.tokens == ((1, 2), (3,))
+    assert parsed.cached == (5, 0)
+
+
+@pytest.mark.parametrize(("tokens", "lengths", "totals"), [([1], [2], [2]), ([1, 1], [0, 2], [1, 2]), ([1], [1], [0])])
+def test_batch_refuses_bad_framing(tokens, lengths, totals):
+    with pytest.raises(batch.Framing) as e:
+        batch.Batch.parse(tokens, lengths, totals)
+    restored = pickle.loads(pickle.dumps(e.value))
+    assert (restored.tokens, restored.scheduled) == (e.value.tokens, e.value.scheduled)
+
+
+def test_block_tables_grow_and_resume():
+    t = paging.BlockTable([3, 4])
+    t.append([9])
+    assert t.blocks == [3, 4, 9] and t.covers(48) and not t.covers(49)
+    t.replace([1])
+    assert t.blocks == [1]
+    assert paging.first_group(([5, 6],)) == [5, 6]
+    with pytest.raises(ValueError):
+        paging.first_group(([1], [2]))
+
+
+def test_request_state_schedules_and_samples():
+    s = State([1, 2, 3, 4], 4, 0, paging.BlockTable([0]))
+    assert s.scheduled(3) == [1, 2, 3] and not s.samples_after(3)
+    s.computed = 3
+    assert s.scheduled(1) == [4] and s.samples_after(1)
+    with pytest.raises(ValueError):
+        s.scheduled(2)
+
+
+@pytest.mark.parametrize(("kwargs", "option"), [
+    (dict(pipeline=2, tensor=1, speculative=False, lora=False, kv_cache_dtype="auto"), "pipeline_parallel_size"),
+    (dict(pipeline=1, tensor=3, speculative=False, lora=False, kv_cache_dtype="auto"), "tensor_parallel_size"),
+    (dict(pipeline=1, tensor=1, speculative=True, lora=False, kv_cache_dtype="auto"), "speculative_config"),
+    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto"), "enable_lora"),
+    (dict(pipeline=1, tensor=1, speculative=False, lora=False, kv_cache_dtype="fp8"), "kv_cache_dtype"),
+])
+def test_refusals_name_the_option(kwargs, option):
+    with pytest.raises(admission.Refused) as e:
+        admission.options(**kwargs)
+    assert e.value.option == option
+    admission.options(pipeline=1, tensor=8, speculative=False, lora=False, kv_cache_dtype="auto")
+
+
+def test_sampling_refusals():
+    admission.sampling(0.0, -1, 1.0, 1, None, None)
+    with pytest.raises(admission.Refused):
+        admission.sampling(0.7, -1, 1.0, 1, None, None)
+    with pytest.raises(admission.Refused):
+        admission.sampling(0.0, -1, 1.0, 1, 5, None)
+
+
+def test_entry_point_names_the_platform():
+    import furiosa_opt_vllm
+
+    assert furiosa_opt_vllm.register() == "furiosa_opt_vllm.platform.B200Platform"

@@ -1,0 +1,43 @@
+"""vLLM through the plugin: vLLM's own LLM (scheduler, sampling parameters, request handling) on a
+synthetic Qwen3 checkpoint, every forward pass in the engine; the greedy continuations agree with
+the dense forward of the checkpoint's weights, and a sampled request is refused."""
+
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+WORKER = os.path.join(ROOT, "tests", "workers", "vllm_generate.py")
+
+
+def test_vllm_generates_through_the_engine(tmp_path):
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=11, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    gen = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (5, 17, 40)]
+    out = str(tmp_path / "out.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable, WORKER, str(tmp_path / "m"), out,
+                    json.dumps(prompts)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        tokens = json.load(f)
+    assert [len(t) for t in tokens] == [8, 8, 8]
+    for p, toks in zip(prompts, tokens):
+        seq = torch.tensor(p, dtype=torch.int32)
+        for t in toks:
+            logits = dense.forward(w, cfg, seq)[-1]
+            assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+            seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+    with open(out + ".refused") as f:
+        assert json.load(f) is True
