@@ -233,12 +233,14 @@ def main() -> None:
             "higher_is_better": True,
             "scaling": "strong",
             "vs_baseline": None,
-            "dtype": "bf16",
+            "dtype": {"fp8_block": "fp8 (W8A8, 128x128 block scales)", "nvfp4_a4": "nvfp4 (W4A4)",
+                      "nvfp4": "nvfp4 weights, bf16 inputs (W4A16)"}.get(cfg.get("weight_format", "bf16"), "bf16"),
             "data": "synthetic: uniform-random prompt token IDs; random-init N(0,0.02) weights",
             "p50_ttft_ms": round(ttft, 3),
             "p50_tpot_ms": round(tpot, 4),
             "config": {
-                "model": f"{args.model} (shape of the named checkpoint, BF16)",
+                "model": f"{args.model} (shape of the named checkpoint, "
+                         f"{cfg.get('weight_format', 'bf16')} projections, BF16 KV cache)",
                 "global_batch": args.concurrency,
                 "seq_len": total,
                 "input_len": args.input_len,
@@ -264,7 +266,8 @@ def run_e2e(args, engine, serving, model, cache, device, prompts_host, nblocks, 
     import numpy as np
     from furiosa_opt_engine import decoder as dec
 
-    pinned = [engine.HostBuffer(p.numpy()) for p in prompts_host]
+    # A host buffer holds every chip's bytes (a rank copies its own slice): the inputs replicated.
+    pinned = [engine.HostBuffer(np.tile(p.numpy(), world)) for p in prompts_host]
     h2d = d2h = calls = 0
 
     def wave():
@@ -286,7 +289,7 @@ def run_e2e(args, engine, serving, model, cache, device, prompts_host, nblocks, 
             calls += 1
             last[call] = host
         for _ in range(args.output_len - 1):
-            step_in = engine.HostBuffer(last)
+            step_in = engine.HostBuffer(np.tile(last, world))
             buf = engine.HbmBuffer(device, args.concurrency * 4)
             step_in.to_hbm(buf)
             h2d += args.concurrency * 4

@@ -159,9 +159,11 @@ void PeerCollectives::add_norm(const float* partial, __nv_bfloat16* residual,
   a.rank = rank_;
   a.world = world_;
   a.site = site_++;
-  // Few rows: every rank reduces every row (one barrier, local writes); many rows: each rank
-  // reduces a slice and stores it into every rank (less NVLink traffic, two barriers).
-  a.two_shot = rows > 256 ? 1 : 0;
+  // Little data: every rank reduces every row (one barrier; reads (world - 1) partials over
+  // NVLink). More: each rank reduces a slice and stores it into every rank (a second barrier, but
+  // 1/world of the reads), which wins once the one-shot reads outgrow a barrier's latency.
+  const size_t one_shot_bytes = static_cast<size_t>(rows) * cols * 4 * (world_ - 1);
+  a.two_shot = (rows >= world_ && one_shot_bytes > (size_t{1} << 20)) ? 1 : 0;
   a.status = status_;
   half_ ^= 1;
   if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
