@@ -36,7 +36,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline"])
     p.add_argument("--model", default="qwen3-1.7b")
     p.add_argument("--concurrency", type=int, default=64)
     p.add_argument("--input-len", type=int, default=1024)
@@ -111,6 +111,68 @@ class ClockSampler:
         }
 
 
+def baseline_arm(args, torch, dist, world, rank, local) -> None:
+    """The same waves on stock PyTorch (cuBLAS matmuls, fused SDPA attention over a contiguous KV
+    cache, NCCL all-reduce), eager: the library baseline the engine is compared with."""
+    from furiosa_opt_models_b200.models import configs
+    from furiosa_opt_models_b200.models.baseline import Baseline
+
+    cfg = configs.get(args.model)
+    if cfg.get("experts") or cfg.get("weight_format", "bf16") != "bf16":
+        if rank == 0:
+            print(json.dumps({"impl": "baseline", "unavailable": "the PyTorch baseline covers dense BF16 decoders"}))
+        return
+    model = Baseline(cfg, tp=world, rank=rank)
+    B, L = args.concurrency, args.input_len + args.output_len
+    model.allocate(B, L)
+    gen = torch.Generator().manual_seed(1234)
+    prompts = torch.randint(0, cfg["vocab"], (B, args.input_len), generator=gen, dtype=torch.int64).cuda()
+    chunk = max(1, 8192 // args.input_len)
+
+    def wave():
+        toks = []
+        for b0 in range(0, B, chunk):  # prefill in chunks of about 8192 rows, as the engine's calls
+            toks.append(model.forward(prompts[b0:b0 + chunk], 0, b0))
+        last = torch.cat(toks)[:, None]
+        for step in range(args.output_len - 1):
+            last = model.forward(last, args.input_len + step)[:, None]
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    for _ in range(args.warmup):
+        wave()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local)
+    with sampler:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            wave()
+        t1.record()
+        torch.cuda.synchronize()
+    barrier()
+    ms = torch.tensor([t0.elapsed_time(t1) / args.steps], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = ms.item()
+    if rank == 0:
+        print(json.dumps({
+            "impl": "baseline", "metric": METRIC,
+            "value": round(B * args.output_len / (ms / 1e3), 1), "unit": "output tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 3),
+            "higher_is_better": True, "scaling": "strong", "dtype": "bf16",
+            "data": "synthetic: uniform-random prompt token IDs; random-init N(0,0.02) weights",
+            "config": {"model": f"{args.model} (shape of the named checkpoint)", "global_batch": B,
+                       "seq_len": L, "parallelism": f"tp{world}",
+                       "stack": "PyTorch eager: cuBLAS matmul, fused SDPA over a contiguous KV cache, NCCL all-reduce"},
+            "clocks": sampler.summary(),
+        }), flush=True)
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
@@ -131,6 +193,11 @@ def main() -> None:
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local))
+    if args.impl == "baseline":
+        baseline_arm(args, torch, dist, world, rank, local)
+        if world > 1:
+            dist.destroy_process_group()
+        return
 
     import furiosa_opt_engine as engine
     from furiosa_opt_models_b200 import serving
