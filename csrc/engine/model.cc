@@ -195,7 +195,9 @@ void DecoderModel::allocate_weights() {
     }
   }
   const std::string& wf = cfg_.weight_format;
+  const bool per_row = wf == "fp8_channel" || wf == "fp8_tensor";
   const int format = wf == "fp8_block" ? foa::kWeightFp8A8
+                     : per_row          ? foa::kWeightFp8Block
                      : wf == "nvfp4"   ? foa::kWeightNvfp4
                      : wf == "nvfp4_a4" ? foa::kWeightNvfp4A4
                                         : foa::kWeightBf16;
@@ -212,6 +214,10 @@ void DecoderModel::allocate_weights() {
     if (format == foa::kWeightBf16 || !projection(name)) return {n * 2, 0};
     const int64_t rows = shape[0], cols = shape[1];
     const int64_t rb = (rows + 127) / 128;
+    if (per_row) {
+      if (cols % 64 != 0) throw Unsupported(name + ": FP8 inputs here come in multiples of 64");
+      return {n, static_cast<size_t>(rows * 4)};
+    }
     if (format == foa::kWeightFp8A8) {
       if (cols % 128 != 0) throw Unsupported(name + ": FP8 block inputs come in multiples of 128");
       return {n, static_cast<size_t>(rb * (cols / 128) * 16)};  // each scale four times
@@ -244,6 +250,10 @@ void DecoderModel::allocate_weights() {
       w.scales = base + offs[i].second;
       const int64_t cols = w.shape[1];
       w.scale_ld = format == foa::kWeightFp8A8 ? cols / 128 : format == foa::kWeightNvfp4 ? cols / 16 : cols / 64 * 512;
+      if (per_row) {
+        w.scale_rows = 1;
+        w.scale_ld = 1;
+      }
     } else {
       w.ptr = reinterpret_cast<__nv_bfloat16*>(base + offs[i].first);
     }
@@ -265,9 +275,19 @@ uint32_t name_tag(const std::string& s) {
 }
 }  // namespace
 
-void DecoderModel::quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv) {
+void DecoderModel::quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv, float amax) {
   auto st = device_.state();
   const int rows = static_cast<int>(w.shape[0]), cols = static_cast<int>(w.shape[1]);
+  if (w.format == foa::kWeightFp8Block && w.scale_rows == 1) {
+    // Per channel: each row's magnitude; per tensor: a magnitude bound the whole tensor shares
+    // (the checkpoint's fused amax at load, 8 standard deviations for synthetic weights).
+    float bound = -1.f;
+    if (cfg_.weight_format == "fp8_tensor") bound = amax >= 0.f ? amax : 8.f * stdv;
+    if (foa::quantize_fp8_rows(src, rows, cols, bound, w.codes, static_cast<float*>(w.scales), st->stream) != 0)
+      st->fail("weight quantization launch failed");
+    st->check_cuda(cudaStreamSynchronize(st->stream), "weight quantization");
+    return;
+  }
   if (w.format == foa::kWeightFp8A8) {
     const long n = static_cast<long>((rows + 127) / 128) * (cols / 128);
     HbmBuffer plain(device_, n * 4);
@@ -280,15 +300,15 @@ void DecoderModel::quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float 
   // NVFP4: one tensor scale from a fixed magnitude bound (8 standard deviations), the same on
   // every tensor-parallel shard of the weight; synthetic inputs quantize under a bound of 8.
   const float bound[2] = {8.f * stdv, 0.f};
-  HbmBuffer amax(device_, 16);
-  st->check_cuda(cudaMemcpyAsync(amax.data(), bound, 8, cudaMemcpyHostToDevice, st->stream), "amax");
+  HbmBuffer amax_buf(device_, 16);
+  st->check_cuda(cudaMemcpyAsync(amax_buf.data(), bound, 8, cudaMemcpyHostToDevice, st->stream), "amax");
   HbmBuffer rowmajor;
   uint8_t* sc = static_cast<uint8_t*>(w.scales);
   if (w.format == foa::kWeightNvfp4A4) {
     rowmajor = HbmBuffer(device_, static_cast<size_t>(rows) * (cols / 16));
     sc = static_cast<uint8_t*>(rowmajor.data());
   }
-  float* amax_p = static_cast<float*>(amax.data());
+  float* amax_p = static_cast<float*>(amax_buf.data());
   if (foa::quantize_nvfp4(src, rows, cols, w.codes, sc, amax_p, amax_p + 1, st->stream) != 0)
     st->fail("weight quantization launch failed");
   if (w.format == foa::kWeightNvfp4A4 &&
@@ -601,6 +621,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     g.w_format = w.format;
     g.w_scale = w.scales;
     g.w_scale_ld = w.scale_ld;
+    g.w_scale_rows = w.scale_rows;
     if (w.format == foa::kWeightNvfp4) g.w_tensor_scale = w.tensor_scale;
     if (w.format == foa::kWeightFp8A8) {
       // Inputs quantized per (row, 128-input group) ahead of the FP8 MMA.

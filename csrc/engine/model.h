@@ -47,7 +47,8 @@ struct ModelConfig {
   // Weight format of the q/k/v, o, gate/up and down projections: "bf16"; "fp8_block" (E4M3 with an
   // FP32 scale per 128x128 block, W8A8); "nvfp4" (E2M1 with E4M3 scales per 16 and an FP32 tensor
   // scale, BF16 inputs: W4A16); "nvfp4_a4" (the same weights, NVFP4 inputs under input_scale:
-  // W4A4 on the block-scaled MMA).
+  // W4A4 on the block-scaled MMA); "fp8_channel" / "fp8_tensor" (BF16 weights quantized at load
+  // to E4M3 with one FP32 scale per output row, or per tensor, restored to BF16 in the GEMM: W8A16).
   std::string weight_format = "bf16";
   int hidden = 0, intermediate = 0, layers = 0, q_heads = 0, kv_heads = 0, head_dim = 128;
   int vocab = 0;
@@ -101,6 +102,7 @@ struct WeightSlot {
   void* scales = nullptr;        // FP8: FP32 [ceil(rows/128), scale_ld]; W4A16: E4M3 [rows, cols/16];
                                  // W4A4: 128-row-blocked atoms [ceil(rows/128), cols/64, 512]
   long scale_ld = 0;
+  int scale_rows = 128;          // FP8 W8A16: rows one scale covers (128: block scales, 1: per row)
   float tensor_scale = 1.f;      // NVFP4 weight_scale_2
   float input_scale = 1.f;       // W4A4 input_scale
 };
@@ -163,8 +165,12 @@ class DecoderModel {
 
  private:
   void allocate_weights();
-  // Quantizes BF16 weights `src` into the slot's format (synthetic initialisation).
-  void quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv);
+  // Quantizes BF16 weights `src` into the slot's format (synthetic initialisation; `amax`, when
+  // >= 0, is the tensor-wide magnitude a per-tensor scale covers).
+ public:
+  void quantize_slot(WeightSlot& w, const __nv_bfloat16* src, float stdv, float amax = -1.f);
+
+ private:
   void ensure_workspace(int64_t rows, int64_t kept, int64_t decode_splits, int64_t decode_rows);
   int launch(const Plan& plan, const Cache& cache);  // returns the kernels it launched
   int64_t graph_bucket(int64_t rows) const;

@@ -331,7 +331,11 @@ Selection select(const LoadOptions& o, const Checkpoint& ck) {
   if (o.layers) unsupported("layers", "every implementation loads whole");
   if (o.adapters && s.implementation->adapters == 0)
     unsupported("adapters", "the " + l.name + " " + m.size + " implementation takes no adapter");
-  if (o.quantization) unsupported("quantization", "load-time FP8 quantization of BF16 checkpoints is not served");
+  if (o.quantization) {
+    if (s.implementation->form != "bf16" || m.experts > 0)
+      unsupported("quantization", "load-time FP8 quantization reads dense BF16 checkpoints");
+    s.config.weight_format = *o.quantization == "fp8_per_tensor" ? "fp8_tensor" : "fp8_channel";
+  }
   if (s.implementation->form == "fp8_block") s.config.weight_format = "fp8_block";
   if (s.implementation->form == "nvfp4") {
     // ModelOpt NVFP4 checkpoints with calibrated input scales run W4A4 on the block-scaled MMA;
@@ -437,10 +441,40 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
   };
   auto st = model.device().state();
   std::vector<uint16_t> host;
+  // A BF16 image into its slot; a slot quantized at load takes it through the device quantizer
+  // (`amax`: the fused tensor's magnitude a per-tensor scale covers).
+  float fused_amax = -1.f;
   auto upload = [&](const std::string& slot) {
-    const WeightSlot& w = model.weights().at(slot);
-    st->check_cuda(cudaMemcpy(w.ptr, host.data(), host.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+    WeightSlot& w = model.weight_slot(slot);
+    if (w.format == foa::kWeightBf16) {
+      st->check_cuda(cudaMemcpy(w.ptr, host.data(), host.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+      return;
+    }
+    HbmBuffer tmp(model.device(), host.size() * 2);
+    st->check_cuda(cudaMemcpy(tmp.data(), host.data(), host.size() * 2, cudaMemcpyHostToDevice), "weight upload");
+    model.quantize_slot(w, static_cast<const __nv_bfloat16*>(tmp.data()), 0.f, fused_amax);
   };
+  // The largest magnitude over whole checkpoint tensors (every rank's shard of them).
+  auto amax_of = [&](std::initializer_list<const StoredTensor*> parts) {
+    float m = 0.f;
+    std::vector<uint16_t> row;
+    for (const StoredTensor* t : parts) {
+      if (!t) continue;
+      const Source src(t);
+      row.resize(static_cast<size_t>(src.cols));
+      for (int64_t r = 0; r < src.rows; ++r) {
+        src.row(r, 0, src.cols, row.data());
+        for (uint16_t b : row) {
+          const uint32_t bits = static_cast<uint32_t>(b & 0x7fff) << 16;
+          float f;
+          std::memcpy(&f, &bits, 4);
+          m = std::max(m, f);
+        }
+      }
+    }
+    return m;
+  };
+  const bool per_tensor = cfg.weight_format == "fp8_tensor";
   auto image = [&](const std::string& slot) {
     const WeightSlot& w = model.weights().at(slot);
     size_t n = 1;
@@ -568,7 +602,9 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       st->fail("scale repack launch failed");
     st->check_cuda(cudaStreamSynchronize(st->stream), "scale repack");
   };
-  const bool quantized = cfg.weight_format != "bf16";
+  // Checkpoints that hold their own codes and scales (load-time FP8 reads BF16 and quantizes).
+  const bool quantized = cfg.weight_format == "fp8_block" || cfg.weight_format == "nvfp4" ||
+                         cfg.weight_format == "nvfp4_a4";
 
   const std::string pre = "model.";
   // Embedding (whole on every chip) and head (this chip's vocabulary rows).
@@ -629,6 +665,7 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
     const auto* k = quantized ? nullptr : take(hf + "self_attn.k_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
     const auto* v = quantized ? nullptr : take(hf + "self_attn.v_proj.weight", {static_cast<int64_t>(cfg.kv_heads) * D, H});
     if (q && k && v) {
+      fused_amax = per_tensor ? amax_of({q, k, v}) : -1.f;
       image(en + "qkv");
       copy_rows(Source(q), static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D, 0, 0, H, H);
       copy_rows(Source(k), static_cast<int64_t>(kvh0) * D, static_cast<int64_t>(kvh_l) * D,
@@ -651,6 +688,7 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
                      {Part{hf + "self_attn.o_proj", H, static_cast<int64_t>(cfg.q_heads) * D, 0, H, {0}, false}},
                      static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D);
     } else if (auto* t = take(hf + "self_attn.o_proj.weight", {H, static_cast<int64_t>(cfg.q_heads) * D})) {
+      fused_amax = per_tensor ? amax_of({t}) : -1.f;
       image(en + "o");
       copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(qh0) * D, static_cast<int64_t>(qh_l) * D,
                 static_cast<int64_t>(qh_l) * D);
@@ -722,6 +760,7 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       if (g && u) {
         // Gate and up rows alternate in 128-row blocks, so one GEMM tile holds both halves of
         // the SwiGLU it feeds.
+        fused_amax = per_tensor ? amax_of({g, u}) : -1.f;
         image(en + "gate_up");
         const Source sg(g), su(u);
         for (int64_t j = 0; j < inter_l; ++j) {
@@ -733,6 +772,7 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
         upload(en + "gate_up");
       }
       if (auto* t = take(hf + "mlp.down_proj.weight", {H, cfg.intermediate})) {
+        fused_amax = per_tensor ? amax_of({t}) : -1.f;
         image(en + "down");
         copy_rows(Source(t), 0, H, 0, static_cast<int64_t>(rank) * inter_l, inter_l, inter_l);
         upload(en + "down");

@@ -62,6 +62,8 @@ struct KParams {
   // Quantized weights (kWF != 0): block scales and the factor the FP32 sums take.
   const void* wscale;         // FP8: FP32 [ceil(N/128)][ceil(K/128)]; NVFP4: E4M3 [N][K/16]
   long wscale_ld;             // scale elements per scale row
+  int wscale_row_shift;       // FP8 converter: scale row = weight row >> shift (7: 128-row blocks, 0: rows)
+  int wscale_k_shift;         // FP8 converter: scale column = k-block >> shift (1: 128 columns, 31: one)
   float acc_scale;            // NVFP4 tensor scale (1 otherwise), applied to the reduced sum
   // Block-scaled operands (kWF == kWNvfp4A4): scale atoms of the M-side and N-side operands,
   // [row block of 128][K/64][512 bytes], and the bytes between two row blocks.
@@ -581,8 +583,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           if (grow < wrows_total) {
             if constexpr (kWF == kWFp8Block) {
               const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-              const float sc =
-                  static_cast<const float*>(p.wscale)[(long)(grow >> 7) * p.wscale_ld + (kb >> 1)];
+              const float sc = static_cast<const float*>(
+                  p.wscale)[(long)(grow >> p.wscale_row_shift) * p.wscale_ld + (kb >> p.wscale_k_shift)];
               out = dequant_fp8x8(v, sc);
             } else {
               const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * 32 + c * 4);
@@ -1338,6 +1340,8 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;
   kp.wscale_ld = a.w_scale_ld;
+  kp.wscale_row_shift = a.w_scale_rows == 1 ? 0 : 7;
+  kp.wscale_k_shift = a.w_scale_rows == 1 ? 31 : 1;
   if (grouped) {
     kp.group_tiles = a.group_tiles;
     kp.tile_group = a.tile_group;

@@ -61,6 +61,9 @@ struct GemmArgs {
   int w_format = 0;
   const void* w_scale = nullptr;
   long w_scale_ld = 0;
+  // kWeightFp8Block only: 128 (one scale per 128x128 block) or 1 (one scale per weight row, as
+  // FP8 quantized at load per channel or per tensor; w_scale FP32 [N], w_scale_ld unused).
+  int w_scale_rows = 128;
   float w_tensor_scale = 1.0f;
   //   kWeightFp8A8:    block-scaled FP8 on both operands (W8A8): `a` and `w` hold E4M3 codes,
   //                    w_scale FP32 [ceil(N/128), w_scale_ld, 4] per 128x128 block (each scale four

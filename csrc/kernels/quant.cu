@@ -216,6 +216,39 @@ int fp8_scales_pad4(const float* scales, long n, float* padded, cudaStream_t str
              : -5;
 }
 
+// One warp per row: scale = amax / 448 (the row's, or `tensor_amax` when >= 0), code =
+// e4m3_sat(w * (1 / scale)); a zero scale gives zero codes.
+__global__ void fp8_rows_kernel(const __nv_bfloat16* w, int rows, int cols, float tensor_amax, uint8_t* codes,
+                                float* scales) {
+  pdl_wait();  // weight producer: no early trigger
+  const int r = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const __nv_bfloat16* src = w + (long)r * cols;
+  float m = 0.f;
+  if (tensor_amax >= 0.f) {
+    m = tensor_amax;
+  } else {
+    for (int c = lane; c < cols; c += 32) m = fmaxf(m, fabsf(__bfloat162float(src[c])));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  }
+  const float scale = m / 448.f;
+  const float rcp = scale == 0.f ? 0.f : 1.f / scale;
+  if (lane == 0) scales[r] = scale;
+  for (int c = lane; c < cols; c += 32)
+    codes[(long)r * cols + c] = __nv_cvt_float_to_fp8(__bfloat162float(src[c]) * rcp, __NV_SATFINITE, __NV_E4M3);
+}
+
+int quantize_fp8_rows(const __nv_bfloat16* w, int rows, int cols, float tensor_amax, uint8_t* codes,
+                      float* scales, cudaStream_t stream) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return launch_pdl(fp8_rows_kernel, dim3((unsigned)((rows * 32L + 255) / 256)), dim3(256), 0, stream, w, rows,
+                    cols, tensor_amax, codes, scales) == cudaSuccess
+             ? 0
+             : -5;
+}
+
 int quantize_fp8_act(const __nv_bfloat16* x, long ldx, int rows, int K, uint8_t* codes, long ldc,
                      float* scales, int rows_pad, cudaStream_t stream) {
   if (rows <= 0) return 0;

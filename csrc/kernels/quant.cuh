@@ -14,6 +14,13 @@ namespace foa {
 int quantize_fp8_block(const __nv_bfloat16* w, int rows, int cols, uint8_t* codes, float* scales,
                        cudaStream_t stream);
 
+// FP8 at load (the reference's per-channel / per-tensor granularity): E4M3 codes [rows, cols] and
+// one FP32 scale per row, scale = amax / 448 over the row, or `tensor_amax` / 448 for every row
+// when tensor_amax >= 0 (a tensor scale covering the weights fused with it); code =
+// e4m3_sat(w * (1 / scale)), zero codes for a zero scale.
+int quantize_fp8_rows(const __nv_bfloat16* w, int rows, int cols, float tensor_amax, uint8_t* codes,
+                      float* scales, cudaStream_t stream);
+
 // NVFP4 (E2M1 codes, E4M3 scale per 16 elements along cols, FP32 tensor scale):
 // global = 448 * 6 / amax(W) (the tensor's "weight_scale_2" is 1 / global);
 // block scale s = e4m3(amax(block) / 6 * global); code = e2m1_rne(w / (s * (1 / global))).

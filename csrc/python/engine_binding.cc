@@ -533,7 +533,10 @@ void bind_engine(py::module_& m) {
         const auto& w = d.model->weights().at(name);
         if (w.format == 0) return py::none();
         py::dict q;
-        q["format"] = w.format == foa::kWeightFp8A8 ? "fp8_block" : w.format == foa::kWeightNvfp4 ? "nvfp4" : "nvfp4_a4";
+        q["format"] = w.format == foa::kWeightFp8A8     ? "fp8_block"
+                      : w.format == foa::kWeightFp8Block ? "fp8_rows"
+                      : w.format == foa::kWeightNvfp4    ? "nvfp4"
+                                                         : "nvfp4_a4";
         q["codes"] = reinterpret_cast<uint64_t>(w.codes);
         q["scales"] = reinterpret_cast<uint64_t>(w.scales);
         q["scale_ld"] = w.scale_ld;

@@ -36,8 +36,10 @@ void bind_ops(py::module_& m) {
          uint64_t res, long ldr, int epilogue, int mode, int splits, uint64_t ws, size_t ws_bytes,
          uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
          int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
-         long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups) {
+         long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups,
+         int w_scale_rows) {
         foa::GemmArgs g;
+        g.w_scale_rows = w_scale_rows;
         g.group_tiles = as_ptr<const int>(group_tiles);
         g.tile_group = as_ptr<const int>(tile_group);
         g.group_tile = group_tile;
@@ -78,7 +80,18 @@ void bind_ops(py::module_& m) {
       py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
       py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0,
       py::arg("a_scale_ld") = 0, py::arg("group_tiles") = 0, py::arg("tile_group") = 0,
-      py::arg("group_tile") = 0, py::arg("groups") = 0);
+      py::arg("group_tile") = 0, py::arg("groups") = 0, py::arg("w_scale_rows") = 128);
+
+  m.def(
+      "quantize_fp8_rows",
+      [](uint64_t w, int rows, int cols, float tensor_amax, uint64_t codes, uint64_t scales, uint64_t stream) {
+        py::gil_scoped_release nogil;
+        check(foa::quantize_fp8_rows(as_ptr<const __nv_bfloat16>(w), rows, cols, tensor_amax,
+                                     as_ptr<uint8_t>(codes), as_ptr<float>(scales), as_stream(stream)),
+              "quantize_fp8_rows");
+      },
+      py::arg("w"), py::arg("rows"), py::arg("cols"), py::arg("tensor_amax"), py::arg("codes"),
+      py::arg("scales"), py::arg("stream"));
 
   m.def(
       "moe_route",

@@ -243,6 +243,8 @@ def quantized_linear(x: torch.Tensor, w) -> torch.Tensor:
         return fp8_block_w8a8(xb, codes, scales)
     if w.format == "fp8_block_w8a16":
         return xb.float() @ fp8_block_dequantize(codes, scales).T
+    if w.format == "fp8_rows":
+        return xb.float() @ (_e4m3_value(codes) * scales[:, None]).bfloat16().float().T
     if w.format == "nvfp4":
         return (xb.float() @ nvfp4_dequantize(codes, scales).T) * w.tensor_scale
     s8 = nvfp4_scales_from_atoms(scales, w.rows)
@@ -294,3 +296,14 @@ def moe_forward(h: torch.Tensor, router: torch.Tensor, gate_up: torch.Tensor, do
             rows[sel] = (act @ down[e].float().T).bfloat16().float()
         acc = acc + w[:, j:j + 1] * rows
     return acc.bfloat16()
+
+
+def fp8_rows_quantize(w: torch.Tensor, tensor_amax: float | None = None):
+    """Load-time FP8 (crates/furiosa-opt-models/src/tensor/form/fp8.rs:195-220): scale =
+    amax / 448 per row (or the tensor's), code = e4m3_sat(w * (1 / scale)), zero codes for a zero
+    scale -> (codes uint8 [rows, cols], FP32 scales [rows])."""
+    wf = w.float()
+    amax = wf.abs().amax(-1) if tensor_amax is None else torch.full((w.shape[0],), float(tensor_amax), device=w.device)
+    scales = amax / torch.full_like(amax, E4M3_MAX)
+    rcp = torch.where(scales == 0, torch.zeros_like(scales), torch.ones_like(scales) / scales)
+    return _e4m3(wf * rcp[:, None]), scales

@@ -28,6 +28,7 @@ from .kernels import (  # noqa: F401
     paged_prefill,
     prefill_work,
     quantize_fp8_block,
+    quantize_fp8_rows,
     quantize_nvfp4,
     quantize_nvfp4_input,
     quantize_fp8_input,

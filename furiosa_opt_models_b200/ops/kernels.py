@@ -36,6 +36,8 @@ class QuantizedWeight:
     (one per 128x128 block, the checkpoint's ``weight_scale_inv``); inputs quantize per 128-input
     group and each block's sum takes its scales (W8A8). fp8_block_w8a16: the same weights
     dequantized to BF16 in the kernel, BF16 inputs.
+    fp8_rows: E4M3 ``codes`` [rows, cols] with one FP32 scale per row ``scales`` [rows] (FP8
+    quantized at load per channel or per tensor), restored to BF16 in the kernel (W8A16).
     nvfp4: ``codes`` uint8 [rows, cols/2] (two E2M1 codes a byte, lower column in the low nibble),
     ``scales`` E4M3 as uint8 [rows, cols/16], ``tensor_scale`` the FP32 ``weight_scale_2``.
     nvfp4_a4 (W4A4 on the block-scaled MMA): ``codes`` as for nvfp4, ``scales`` the 128-row-blocked
@@ -62,8 +64,8 @@ class QuantizedWeight:
 
     @property
     def code(self) -> int:
-        return {"fp8_block": W_FP8_BLOCK, "fp8_block_w8a16": W_FP8_W8A16, "nvfp4": W_NVFP4,
-                "nvfp4_a4": W_NVFP4_A4}[self.format]
+        return {"fp8_block": W_FP8_BLOCK, "fp8_block_w8a16": W_FP8_W8A16, "fp8_rows": W_FP8_W8A16,
+                "nvfp4": W_NVFP4, "nvfp4_a4": W_NVFP4_A4}[self.format]
 
 
 def _f32(x: float) -> float:
@@ -105,6 +107,19 @@ def quantize_fp8_input(x: torch.Tensor):
     native().ops.quantize_fp8_act(x.data_ptr(), x.stride(0), rows, K, codes.data_ptr(), codes.stride(0),
                                   scales.data_ptr(), pad, _stream())
     return codes, scales
+
+
+def quantize_fp8_rows(w: torch.Tensor, tensor_amax: float | None = None) -> QuantizedWeight:
+    """FP8 of a BF16 weight with one scale per row (amax / 448), or per tensor with
+    ``tensor_amax``; codes are ``w * (1 / scale)`` saturated."""
+    _rowmajor(w, "w")
+    w = w.contiguous()
+    rows, cols = w.shape
+    codes = torch.empty(rows, cols, dtype=torch.uint8, device=w.device)
+    scales = torch.empty(rows, dtype=torch.float32, device=w.device)
+    native().ops.quantize_fp8_rows(w.data_ptr(), rows, cols, -1.0 if tensor_amax is None else float(tensor_amax),
+                                   codes.data_ptr(), scales.data_ptr(), _stream())
+    return QuantizedWeight("fp8_rows", codes, scales, rows, cols)
 
 
 def quantize_fp8_block(w: torch.Tensor) -> QuantizedWeight:
@@ -164,7 +179,7 @@ def gemm(
             raise ValueError("inner dimensions differ")
         w_ptr, ldw = w.codes.data_ptr(), w.codes.stride(0) * (1 if w.format.startswith("fp8") else 2)
         qargs = dict(w_format=w.code, w_scale=w.scales.data_ptr(), w_scale_ld=w.scales.stride(0),
-                     w_tensor_scale=float(w.tensor_scale))
+                     w_tensor_scale=float(w.tensor_scale), w_scale_rows=1 if w.format == "fp8_rows" else 128)
         if w.format == "nvfp4_a4":
             codes, atoms = quantize_nvfp4_input(a, w.input_scale)
             keep = (codes, atoms)  # noqa: F841 (alive until the launch is enqueued)

@@ -40,6 +40,9 @@ def weights(model) -> dict:
             codes = tensor(q["codes"], (rows, cols), torch.uint8, dev)
             padded = tensor(q["scales"], ((rows + 127) // 128, cols // 128, 4), torch.float32, dev)
             scales = padded[..., 0]
+        elif fmt == "fp8_rows":
+            codes = tensor(q["codes"], (rows, cols), torch.uint8, dev)
+            scales = tensor(q["scales"], (rows,), torch.float32, dev)
         elif fmt == "nvfp4":
             codes = tensor(q["codes"], (rows, cols // 2), torch.uint8, dev)
             scales = tensor(q["scales"], (rows, cols // 16), torch.uint8, dev)

@@ -213,3 +213,36 @@ def test_moe_decoder_matches_dense(graphs):
             # A router logit one BF16 step apart can reorder or swap a selected expert.
             assert logits[pick] >= top[0] - 5e-2 * max(1.0, abs(top[0].item())), (i, step)
             seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
+
+
+@pytest.mark.parametrize("granularity", ["fp8_per_channel", "fp8_per_tensor"])
+def test_load_time_fp8_quantization(tmp_path, granularity):
+    """A BF16 checkpoint quantized to FP8 at load (LoadOptions.quantization): greedy decoding
+    agrees with the dense forward of the loaded codes and scales (restored to BF16, W8A16)."""
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    synthetic.write(str(tmp_path / "m"), cfg, seed=8, std=0.05)
+    ck = engine.Checkpoint(str(tmp_path / "m"))
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine.LoadOptions().quantization(granularity).load(ck, device)
+    w = _weights(model)
+    assert w["layers.0.qkv"].format == "fp8_rows"
+    if granularity == "fp8_per_tensor":
+        assert w["layers.0.qkv"].scales.unique().numel() == 1
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    gen = torch.Generator().manual_seed(2)
+    prompt = torch.randint(0, cfg["vocab"], (19,), generator=gen, dtype=torch.int32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(prompt).to_hbm(device), 19, alloc.take(4))]
+    toks = [serving.prefill(model, cache, seqs, [0]).to_host().numpy()[0]]
+    for _ in range(6):
+        toks.append(serving.decode(model, cache, seqs).to_host().numpy()[0])
+    seq = prompt.clone()
+    for t in toks:
+        logits = dense.forward(w, cfg, seq)[-1]
+        assert logits[int(t)] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+        seq = torch.cat([seq, torch.tensor([int(t)], dtype=torch.int32)])

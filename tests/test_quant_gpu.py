@@ -225,3 +225,23 @@ def test_fp8_w8a8_gemm(M, N, K, mode, epi, splits):
     else:
         ref = full
     _close(out, ref, 1e-2 if epi != 1 else 1e-4)
+
+
+# ------------------------------------------------------------------ FP8 quantized at load (W8A16)
+
+
+@pytest.mark.parametrize("tensor_amax", [None, 0.4])
+def test_fp8_rows_quantizer_and_gemm(tensor_amax):
+    ops = _ops()
+    torch.manual_seed(12)
+    w = torch.randn(640, 1024, device="cuda", dtype=torch.bfloat16) * 0.05
+    w[3] = 0  # a zero row keeps zero codes
+    q = ops.quantize_fp8_rows(w, tensor_amax)
+    torch.cuda.synchronize()
+    codes, scales = R.fp8_rows_quantize(w, tensor_amax)
+    assert torch.equal(q.codes, codes) and torch.equal(q.scales, scales)
+    a = torch.randn(48, 1024, device="cuda", dtype=torch.bfloat16)
+    for mode in (1, 2):
+        out = ops.gemm(a, q, mode=mode)
+        torch.cuda.synchronize()
+        _close(out, R.quantized_linear(a.float(), q))
