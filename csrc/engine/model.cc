@@ -9,6 +9,7 @@
 #include "kernels/quant.cuh"
 #include "kernels/moe.cuh"
 #include "kernels/ops.cuh"
+#include "lora.h"
 
 namespace foa::engine {
 
@@ -160,7 +161,7 @@ Limits DecoderModel::limits() const {
   g.layers_begin = 0;
   g.layers_end = cfg_.layers;
   l.cache.groups.push_back(g);
-  l.adapters = 0;
+  l.adapters = adapter_slots_;
   return l;
 }
 
@@ -450,6 +451,10 @@ void DecoderModel::ensure_workspace(int64_t rows, int64_t kept, int64_t splits, 
     ws_moe_rows_ = R;
     changed = true;
   }
+  if (adapter_slots_ > 0 && (changed || !ws_lora_z_.valid())) {
+    const int64_t R = std::max<int64_t>(256, next_pow2(std::max(rows, ws_rows_)));
+    ws_lora_z_ = HbmBuffer(device_, R * 2 * 128 * 2);
+  }
   if (kept > ws_kept_) {
     const int64_t K = std::max<int64_t>(64, next_pow2(kept));
     ws_hk_ = HbmBuffer(device_, K * H * 2);
@@ -486,13 +491,21 @@ int64_t DecoderModel::graph_bucket(int64_t rows) const {
   return 0;
 }
 
-HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cache) {
+HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cache,
+                                const std::vector<std::shared_ptr<const LoraAdapter>>& adapters) {
   auto st = device_.state();
   st->check();
   st->activate();
   const Limits lim = limits();
-  // Decode-only calls whose every request keeps its last row run as CUDA graphs of padded size.
-  bool graphable = graphs_enabled_;
+  std::vector<bool> filled;
+  for (const auto& a : adapters) {
+    if (a && a->owner() != this) throw ValueError("the adapter belongs to another model");
+    filled.push_back(a != nullptr);
+  }
+  call_adapters_ = adapters;
+  // Decode-only calls whose every request keeps its last row run as CUDA graphs of padded size
+  // (calls with adapters run eagerly: their factors differ call to call).
+  bool graphable = graphs_enabled_ && adapters.empty();
   int64_t rows = 0;
   for (const auto& r : requests) {
     rows += r.length;
@@ -512,7 +525,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   const int slot = stage_slot_;
   stage_slot_ ^= 1;
   st->check_cuda(cudaEventSynchronize(stage_done_[slot]), "staging wait");
-  Plan plan = plan_call(requests, lim, cache.spec(), cache.blocks(), 0, {}, group,
+  Plan plan = plan_call(requests, lim, cache.spec(), cache.blocks(), static_cast<int64_t>(adapters.size()), filled, group,
                         graphable ? bucket : 0, host_stage_);
   if (pinned_stage_[slot].size() < plan.staged.bytes)
     pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
@@ -612,8 +625,55 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     ++kernels;
   };
   auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
-                  int epi, const void* res) {
+                  int epi, const void* res, int lora_layer = -1, int lora_module = 0) {
     foa::GemmArgs g;
+    // LoRA slots: Z_s = X A_s^T (its rows zeroed outside slot s), added as extra K segments
+    // Z_s B_s^T into the projection's FP32 sums.
+    int nseg = 0;
+    if (lora_layer >= 0) {
+      int kpad = 0;
+      for (const auto& ad : call_adapters_)
+        if (ad) kpad = std::max(kpad, ad->factor(lora_layer, lora_module).kpad);
+      if (kpad > 0) {
+        __nv_bfloat16* z = bf(ws_lora_z_);
+        const int ldz = 2 * 128;
+        for (size_t slot = 0; slot < call_adapters_.size(); ++slot) {
+          const auto& ad = call_adapters_[slot];
+          if (!ad) continue;
+          const LoraFactor& f = ad->factor(lora_layer, lora_module);
+          if (f.kpad == 0) continue;
+          foa::GemmArgs sh;
+          sh.a = a;
+          sh.lda = lda;
+          sh.w = f.a.data();
+          sh.ldw = K;
+          sh.M = M;
+          sh.N = f.kpad;
+          sh.K = K;
+          sh.c = z + slot * 128;
+          sh.ldc = ldz;
+          sh.status = st->status;
+          sh.workspace = static_cast<float*>(ws_gemm_.data());
+          sh.workspace_bytes = ws_gemm_.size();
+          sh.counters = i32(ws_counters_);
+          sh.counters_len = 32768;
+          if (batch_invariant_) {
+            sh.mode = foa::kModeRows;
+            sh.splits = 1;
+          }
+          fail(foa::gemm_bf16(sh, s), "lora shrink");
+          fail(foa::lora_mask(z + slot * 128, ldz, M, f.kpad, static_cast<int>(slot),
+                              i32(stage, plan.staged.adapters), s),
+               "lora mask");
+          g.seg[nseg].a = z + slot * 128;
+          g.seg[nseg].lda = ldz;
+          g.seg[nseg].w = f.b.data();
+          g.seg[nseg].ldw = f.kpad;
+          g.seg[nseg].K = f.kpad;
+          ++nseg;
+        }
+      }
+    }
     g.a = a;
     g.lda = lda;
     g.w = w.format == foa::kWeightBf16 ? static_cast<const void*>(w.ptr) : w.codes;
@@ -705,7 +765,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                         H, cfg_.eps, s),
            "rmsnorm");
     gemm(h, H, ws(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
-         nullptr);
+         nullptr, l, LoraAdapter::kQkv);
     __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(cache.layers()[l].data());
     fail(foa::qk_norm_rope_cache(bf(ws_qkv_), qkv_cols, static_cast<int>(T), qh_l_, kvh_l_, D,
                                  cfg_.qk_norm ? w(p + "q_norm") : nullptr,
@@ -730,14 +790,14 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     // sum under tensor parallelism).
     if (!tp) {
       gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
-           foa::kEpiBf16, x);
+           foa::kEpiBf16, x, l, LoraAdapter::kO);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
                         H, cfg_.eps, s),
            "rmsnorm");
     } else {
       partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
       gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
-           foa::kEpiF32, nullptr);
+           foa::kEpiF32, nullptr, l, LoraAdapter::kO);
       coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
     }
@@ -792,18 +852,18 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       }
     } else if (!tp) {
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
-           foa::kEpiSwiGLU, nullptr);
+           foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
       gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
-           foa::kEpiBf16, x);
+           foa::kEpiBf16, x, l, LoraAdapter::kDown);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(next_norm), h, H, nullptr, 0, static_cast<int>(T), H,
                         cfg_.eps, s),
            "rmsnorm");
     } else {
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
-           foa::kEpiSwiGLU, nullptr);
+           foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
       partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
       gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
-           foa::kEpiF32, nullptr);
+           foa::kEpiF32, nullptr, l, LoraAdapter::kDown);
       coll_->add_norm(partial, x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
     }

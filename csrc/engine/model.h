@@ -107,6 +107,8 @@ struct WeightSlot {
   float input_scale = 1.f;       // W4A4 input_scale
 };
 
+class LoraAdapter;
+
 class DecoderModel {
  public:
   DecoderModel(const Device& device, ModelConfig cfg, int tp, int rank);
@@ -156,7 +158,13 @@ class DecoderModel {
 
   // One call: plans, stages and launches; returns the kept rows' output (tokens I32 [kept],
   // hidden BF16 [kept, hidden] or scores F32 [kept, labels]) once the launches are submitted.
-  HbmTensor forward(const std::vector<Request>& requests, Cache& cache);
+  HbmTensor forward(const std::vector<Request>& requests, Cache& cache,
+                    const std::vector<std::shared_ptr<const LoraAdapter>>& adapters = {});
+  // LoRA slots a call may hold (0: the decoder runs no adapter).
+  void set_adapter_slots(int slots) {
+    adapter_slots_ = slots;
+    clear_graphs();
+  }
 
   // Timing hooks for benchmarks: the last call's plan, and the kernels launched so far (graph
   // replays count every kernel node).
@@ -173,6 +181,9 @@ class DecoderModel {
  private:
   void ensure_workspace(int64_t rows, int64_t kept, int64_t decode_splits, int64_t decode_rows);
   int launch(const Plan& plan, const Cache& cache);  // returns the kernels it launched
+  int adapter_slots_ = 0;
+  std::vector<std::shared_ptr<const LoraAdapter>> call_adapters_;  // the current call's slots
+  HbmBuffer ws_lora_z_;
   int64_t graph_bucket(int64_t rows) const;
 
   Device device_;

@@ -201,6 +201,8 @@ Implementation make(const char* family, const char* cls, const char* form, Outpu
   i.form = form;
   i.output = out;
   i.scope = std::move(scope);
+  // Dense BF16 decoders take LoRA adapters (two slots a call).
+  i.adapters = (std::string(form) == "bf16" && std::string(family) != "qwen3_moe" && out != Output::Scores) ? 2 : 0;
   return i;
 }
 

@@ -77,6 +77,9 @@ struct KParams {
   // Grouped (mixture-of-experts) swap GEMM: the N-side token tiles and the group (expert) whose
   // weights each tile multiplies come from the device; weights of group g start at row
   // g * group_rows.
+  // Extra K segments (BF16): k-blocks [seg_kb[0], seg_kb[1]) read aux p1/q1 and [seg_kb[1],
+  // kblocks) read aux p2/q2, each from its own column 0. seg_kb[0] == kblocks: one segment.
+  int seg_kb[2];
   const int* group_tiles;  // number of token tiles (device), or null
   const int* tile_group;   // group of each token tile (device)
   long group_rows;
@@ -260,11 +263,20 @@ __device__ __forceinline__ void store_one(const KParams& p, int row, int col, fl
   static_cast<__nv_bfloat16*>(p.c)[(long)row * p.ldc + col] = __float2bfloat16_rn(v);
 }
 
+// Tensor maps beyond the two operands: the raw quantized weights a converter reads, and the
+// operand pairs of up to two extra K segments (BF16 only: LoRA updates [X | Z1 | Z2] x
+// [W | B1 | B2]^T, one rounding for the whole sum).
+struct AuxMaps {
+  CUtensorMap w;
+  CUtensorMap p1, q1, p2, q2;
+};
+
 template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed, int kWF = kWBf16>
 __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCta), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmP,
                      const __grid_constant__ CUtensorMap tmQ,
-                     const __grid_constant__ CUtensorMap tmW, const KParams p) {
+                     const __grid_constant__ AuxMaps aux, const KParams p) {
+  const CUtensorMap& tmW = aux.w;
   using C = Cfg<kMB, kBN, kStages, kAcc, kWF>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -315,6 +327,10 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     tma_prefetch_desc(&tmP);
     tma_prefetch_desc(&tmQ);
     if (kWF == kWFp8Block || kWF == kWNvfp4) tma_prefetch_desc(&tmW);
+    if (kWF == kWBf16 && p.seg_kb[0] < p.kblocks) {
+      tma_prefetch_desc(&aux.p1);
+      tma_prefetch_desc(&aux.q1);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::kTmemCols);
@@ -349,14 +365,34 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
                       2048, full + s);
         }
       };
+      // The K segment of k-block kb: its maps and its first column.
+      auto seg_maps = [&](int kb, const CUtensorMap*& mp, const CUtensorMap*& mq, int& x) {
+        mp = &tmP;
+        mq = &tmQ;
+        x = kb * C::kBoxX;
+        if constexpr (kWF == kWBf16) {
+          if (kb >= p.seg_kb[1]) {
+            mp = &aux.p2;
+            mq = &aux.q2;
+            x = (kb - p.seg_kb[1]) * C::kBoxX;
+          } else if (kb >= p.seg_kb[0]) {
+            mp = &aux.p1;
+            mq = &aux.q1;
+            x = (kb - p.seg_kb[0]) * C::kBoxX;
+          }
+        }
+      };
       auto load_w = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
         if constexpr (kWF == kWBf16 || kWF == kWNvfp4A4 || kWF == kWFp8A8) {
+          const CUtensorMap *mp, *mq;
+          int x;
+          seg_maps(kb, mp, mq, x);
           if (p.swap) {
             const long g0 = p.tile_group != nullptr ? (long)p.tile_group[tq] * p.group_rows : 0;
-            tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, (int)(g0 + tp * C::kPRows));
+            tma_load_2d(st, mp, full + s, x, (int)(g0 + tp * C::kPRows));
           } else {
-            tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * C::kBoxX, tq * kBN);
+            tma_load_2d(st + C::kPBytes, mq, full + s, x, tq * kBN);
           }
           if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap != 0);
         } else {
@@ -368,10 +404,13 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       };
       auto load_a = [&](int s, int kb, int tp, int tq) {
         uint8_t* st = smem + s * C::kStageBytes;
+        const CUtensorMap *mp, *mq;
+        int x;
+        seg_maps(kb, mp, mq, x);
         if (p.swap)
-          tma_load_2d(st + C::kPBytes, &tmQ, full + s, kb * C::kBoxX, tq * kBN);
+          tma_load_2d(st + C::kPBytes, mq, full + s, x, tq * kBN);
         else
-          tma_load_2d(st, &tmP, full + s, kb * C::kBoxX, tp * C::kPRows);
+          tma_load_2d(st, mp, full + s, x, tp * C::kPRows);
         if constexpr (kWF == kWNvfp4A4) load_sf(s, kb, tp, tq, p.swap == 0);
         if constexpr (kWF == kWFp8A8) {
           if (p.swap)
@@ -981,7 +1020,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
                     (a.w_format == kWFp8A8 && a.epilogue == kEpiSwiGLU) || a.group_tiles != nullptr;
   pl.swap = swap;
   const int kelems = a.w_format == kWNvfp4A4 ? 256 : a.w_format == kWFp8A8 ? 128 : kBlockK;
-  pl.kblocks = (a.K + kelems - 1) / kelems;
+  pl.kblocks = (a.K + kelems - 1) / kelems + a.seg[0].K / kBlockK + a.seg[1].K / kBlockK;
   if (!swap) {
     pl.mb = 1;
     pl.kbn = a.w_format == kWFp8A8 ? 128 : 256;  // W8A8 sums a tile row in registers
@@ -1047,7 +1086,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
 }
 
 template <int kMB, int kBN, int kEpi, int kRed, int kWF>
-int launch(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw, const KParams& kp,
+int launch(const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw, const KParams& kp,
            const Plan& pl, cudaStream_t stream) {
   using S = Shape<kMB, kBN, kWF>;
   using C = Cfg<kMB, kBN, S::kStages, S::kAcc, kWF>;
@@ -1118,7 +1157,7 @@ int max_active_clusters(int size) {
 }
 
 template <int kMB, int kBN, int kEpi, int kWF>
-int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                const KParams& kp, const Plan& pl, cudaStream_t stream) {
   switch (pl.red) {
     case kRedNone:
@@ -1133,7 +1172,7 @@ int launch_red(const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& 
 }
 
 template <int kMB, int kBN, int kWF>
-int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                      const KParams& kp, const Plan& pl, cudaStream_t stream) {
   if (epi == kEpiBf16) return launch_red<kMB, kBN, kEpiBf16, kWF>(tp, tq, tw, kp, pl, stream);
   if (epi == kEpiF32) return launch_red<kMB, kBN, kEpiF32, kWF>(tp, tq, tw, kp, pl, stream);
@@ -1141,7 +1180,7 @@ int launch_plain_epi(int epi, const CUtensorMap& tp, const CUtensorMap& tq, cons
 }
 
 template <int kWF>
-int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                 const KParams& kp, const Plan& pl, cudaStream_t stream) {
   if (pl.mb == 2) {
     if (epi != kEpiSwiGLU) return -2;
@@ -1163,7 +1202,7 @@ int launch_swap(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUt
 }
 
 // Block-scaled NVFP4 configurations: swap N tiles of 64/128/256 (two M blocks: 64/128).
-int launch_swap_nvf4(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_swap_nvf4(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                      const KParams& kp, const Plan& pl, cudaStream_t stream) {
   constexpr int W = kWNvfp4A4;
   if (pl.mb == 2) {
@@ -1179,7 +1218,7 @@ int launch_swap_nvf4(int epi, const CUtensorMap& tp, const CUtensorMap& tq, cons
 }
 
 // W8A8 configurations: swap N tiles of 32..128 (two M blocks: up to 64), rows 128 x 128.
-int launch_swap_fp8(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_swap_fp8(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                     const KParams& kp, const Plan& pl, cudaStream_t stream) {
   constexpr int W = kWFp8A8;
   if (pl.mb == 2) {
@@ -1226,7 +1265,7 @@ int cluster_limit_nvf4(int mb, int kbn, int epi, int size) {
 }
 
 template <int kWF>
-int launch_rows(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const CUtensorMap& tw,
+int launch_rows(int epi, const CUtensorMap& tp, const CUtensorMap& tq, const AuxMaps& tw,
                 const KParams& kp, const Plan& pl, cudaStream_t stream) {
   switch (epi) {
     case kEpiBf16: return launch_red<1, 256, kEpiBf16, kWF>(tp, tq, tw, kp, pl, stream);
@@ -1292,6 +1331,14 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   const bool nvf4 = a.w_format == kWNvfp4A4;
   const bool fp8 = a.w_format == kWFp8A8;
   const bool grouped = a.group_tiles != nullptr;
+  const int nseg = (a.seg[0].K > 0) + (a.seg[1].K > 0);
+  if (nseg > 0) {
+    if (a.w_format != kWBf16 || grouped || (a.seg[0].K <= 0 && a.seg[1].K > 0)) return -2;
+    for (int i = 0; i < nseg; ++i)
+      if (a.seg[i].K % kBlockK != 0 || a.seg[i].lda % 8 != 0 || a.seg[i].ldw % 8 != 0 ||
+          (reinterpret_cast<uintptr_t>(a.seg[i].a) & 15) || (reinterpret_cast<uintptr_t>(a.seg[i].w) & 15))
+        return -1;
+  }
   if (grouped) {
     const int t = a.group_tile;
     if (a.w_format != kWBf16 || a.tile_group == nullptr || a.groups <= 0 || a.N % 128 != 0 ||
@@ -1340,6 +1387,11 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;
   kp.wscale_ld = a.w_scale_ld;
+  {
+    const int main_kb = pl.kblocks - a.seg[0].K / kBlockK - a.seg[1].K / kBlockK;
+    kp.seg_kb[0] = nseg > 0 ? main_kb : pl.kblocks;
+    kp.seg_kb[1] = nseg > 1 ? main_kb + a.seg[0].K / kBlockK : pl.kblocks;
+  }
   kp.wscale_row_shift = a.w_scale_rows == 1 ? 0 : 7;
   kp.wscale_k_shift = a.w_scale_rows == 1 ? 31 : 1;
   if (grouped) {
@@ -1363,7 +1415,8 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   }
   if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
 
-  CUtensorMap tp, tq, tw;
+  CUtensorMap tp, tq;
+  AuxMaps tw;
   std::memset(&tw, 0, sizeof(tw));
   const int prow_box = 128 * pl.mb;
   const int wrows_box = pl.swap ? prow_box : pl.kbn;
@@ -1373,7 +1426,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     const long row_bytes = a.w_format == kWFp8Block ? a.K : a.K / 2;
     const long ld_bytes = a.w_format == kWFp8Block ? a.ldw : a.ldw / 2;
     const int box_bytes = a.w_format == kWFp8Block ? 64 : 32;
-    if (!encode_tmap_2d(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, row_bytes, ld_bytes,
+    if (!encode_tmap_2d(&tw.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, row_bytes, ld_bytes,
                         wrows_box, box_bytes, CU_TENSOR_MAP_SWIZZLE_NONE))
       return -4;
   }
@@ -1383,11 +1436,22 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     if (fp8) return encode_tmap_u8_kmajor(m, base, rows, a.K, ld, box);
     return encode_tmap_bf16_kmajor(m, base, rows, a.K, ld, box);
   };
+  // Extra K segments: P is the weight side in the swap mapping, the activation side otherwise.
+  for (int i = 0; i < nseg; ++i) {
+    CUtensorMap* mp = i == 0 ? &tw.p1 : &tw.p2;
+    CUtensorMap* mq = i == 0 ? &tw.q1 : &tw.q2;
+    const GemmSegment& sg = a.seg[i];
+    const bool ok = pl.swap ? (encode_tmap_bf16_kmajor(mp, sg.w, a.N, sg.K, sg.ldw, prow_box) &&
+                               encode_tmap_bf16_kmajor(mq, sg.a, a.M, sg.K, sg.lda, pl.kbn))
+                            : (encode_tmap_bf16_kmajor(mp, sg.a, a.M, sg.K, sg.lda, prow_box) &&
+                               encode_tmap_bf16_kmajor(mq, sg.w, a.N, sg.K, sg.ldw, pl.kbn));
+    if (!ok) return -4;
+  }
   if (!pl.swap) {
     kp.Mp = a.M;
     kp.Nq = a.N;
     if (!operand(&tp, a.a, a.M, a.lda, prow_box)) return -4;
-    if (converted) tq = tw;  // unused by the converting producer
+    if (converted) tq = tw.w;  // unused by the converting producer
     else if (!operand(&tq, a.w, a.N, a.ldw, pl.kbn)) return -4;
     if (pl.red == 2) return -2;
     switch (a.w_format) {
@@ -1404,7 +1468,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   }
   kp.Mp = a.N;
   kp.Nq = a.M;
-  if (converted) tp = tw;
+  if (converted) tp = tw.w;
   else if (!operand(&tp, a.w, (long)a.N * (grouped ? a.groups : 1), a.ldw, prow_box)) return -4;
   if (!operand(&tq, a.a, a.M, a.lda, pl.kbn)) return -4;
   switch (a.w_format) {

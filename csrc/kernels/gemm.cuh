@@ -21,6 +21,16 @@ enum GemmMode : int {
   kModeSwap = 2,   // weights on M, activations on N (few rows: decode)
 };
 
+// An extra K segment of a BF16 GEMM: activations [M, K] (row stride lda) times weights [N, K]
+// (row stride ldw), added into the same FP32 sums before the epilogue (K a multiple of 64).
+struct GemmSegment {
+  const void* a = nullptr;
+  long lda = 0;
+  const void* w = nullptr;
+  long ldw = 0;
+  int K = 0;
+};
+
 struct GemmArgs {
   const void* a = nullptr;  // activations [M, K] BF16, row stride lda elements
   long lda = 0;
@@ -80,6 +90,8 @@ struct GemmArgs {
   const int* tile_group = nullptr;
   int group_tile = 0;
   int groups = 0;
+  // Up to two extra K segments (BF16 weights, not grouped): C = epilogue(A.W^T + A1.W1^T + A2.W2^T).
+  GemmSegment seg[2];
 };
 
 enum GemmWeightFormat : int {

@@ -289,6 +289,15 @@ __global__ void fill_bf16_kernel(__nv_bfloat16* dst, long n, float v) {
     dst[i] = b;
 }
 
+// Zeroes the `cols` columns of z rows whose slot is not `slot` (LoRA: a row runs one adapter).
+__global__ void lora_mask_kernel(__nv_bfloat16* z, long ldz, int rows, int cols, int slot, const int32_t* row_slot) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  if (r >= rows || row_slot[r] == slot) return;
+  for (int c = threadIdx.x; c < cols; c += blockDim.x) z[(long)r * ldz + c] = __float2bfloat16_rn(0.f);
+}
+
 __global__ void gather_tokens_kernel(const int32_t* sources, int count, int32_t* out) {
   pdl_wait();
   pdl_trigger();
@@ -313,6 +322,15 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* in, long ldi, const int3
 }
 
 }  // namespace
+
+int lora_mask(__nv_bfloat16* z, long ldz, int rows, int cols, int slot, const int32_t* row_slot,
+              cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  return launch_pdl(lora_mask_kernel, dim3(rows), dim3(128), 0, stream, z, ldz, rows, cols, slot, row_slot) ==
+                 cudaSuccess
+             ? 0
+             : -5;
+}
 
 int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream) {
   if (n <= 0) return 0;

@@ -52,6 +52,10 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slot_mapping,
                        cudaStream_t stream);
 
+// LoRA: zeroes z[r, 0:cols) (row stride ldz) of every row r whose row_slot[r] is not `slot`.
+int lora_mask(__nv_bfloat16* z, long ldz, int rows, int cols, int slot, const int32_t* row_slot,
+              cudaStream_t stream);
+
 // Fills `n` BF16 values with N(0, std) from a counter-based hash of (seed, index): the same
 // values on every device and every run.
 int init_normal_bf16(__nv_bfloat16* dst, long n, float std, uint64_t seed, cudaStream_t stream);

@@ -420,6 +420,25 @@ void bind_engine(py::module_& m) {
       .value("HIDDEN", PyOutput::HIDDEN)
       .value("SCORES", PyOutput::SCORES);
 
+  py::class_<PyAdapterSpec>(decoder, "AdapterSpec",
+                            "The LoRA adapters a loaded decoder's calls run their requests with: RANK, "
+                            "the rank every update holds, and SLOTS, the adapters one call runs with.")
+      .def_property_readonly_static("RANK", [](py::object) { return LoraAdapter::kRank; })
+      .def_property_readonly_static("SLOTS", [](py::object) { return LoraAdapter::kSlots; });
+  py::class_<PyAdapter>(decoder, "Adapter",
+                        "A PEFT LoRA checkpoint loaded onto a decoder's device: each adapted module's "
+                        "lora_A and lora_B, the scale folded in.")
+      .def(py::init([](const PyAdapterSpec& spec, const py::object& checkpoint) {
+             auto ck = py::module_::import("furiosa_opt_engine._native").attr("_checkpoint_ptr")(checkpoint);
+             const Checkpoint* c = reinterpret_cast<const Checkpoint*>(ck.cast<uintptr_t>());
+             std::shared_ptr<const LoraAdapter> a;
+             {
+               py::gil_scoped_release nogil;
+               a = std::make_shared<LoraAdapter>(*spec.model, *c);
+             }
+             return PyAdapter{a, spec.model};
+           }),
+           py::arg("spec"), py::arg("checkpoint"));
   py::class_<PyRequest>(decoder, "Request", "One sequence's tokens after the cached positions its blocks hold.")
       .def(py::init([](const std::vector<std::vector<int64_t>>& rows, int64_t cached,
                        std::shared_ptr<HbmTensor> tokens, const py::object& keep,
@@ -491,14 +510,25 @@ void bind_engine(py::module_& m) {
       r.overrides = !pr->overrides.empty();
       reqs.push_back(std::move(r));
     }
+    std::vector<std::shared_ptr<const LoraAdapter>> slots;
     if (!adapters.is_none() && py::len(adapters) > 0) {
-      // No loaded decoder takes adapters: the planner refuses with the reference's message.
       const Limits lim = d.model->limits();
       if (lim.adapters == 0) throw Unsupported("adapters are not served");
+      if (static_cast<int64_t>(py::len(adapters)) > lim.adapters)
+        throw ValueError("call holds more adapters than compiled");
+      for (auto a : adapters) {
+        if (a.is_none()) {
+          slots.push_back(nullptr);
+          continue;
+        }
+        const PyAdapter& pa = a.cast<const PyAdapter&>();
+        if (pa.model != d.model) throw ValueError("the adapter belongs to another model");
+        slots.push_back(pa.adapter);
+      }
     }
     py::gil_scoped_release nogil;
     std::lock_guard<std::mutex> g(d.model->device().state()->mu);
-    return std::make_shared<HbmTensor>(d.model->forward(reqs, *cache.cache));
+    return std::make_shared<HbmTensor>(d.model->forward(reqs, *cache.cache, slots));
   };
 
   py::class_<PyDecoder>(m, "Decoder", "A decoder loaded on a device, whatever its model.")
@@ -519,7 +549,10 @@ void bind_engine(py::module_& m) {
           default: return PyOutput::TOKENS;
         }
       })
-      .def_property_readonly("adapters", [](const PyDecoder&) { return py::none(); })
+      .def_property_readonly("adapters", [](const PyDecoder& d) -> py::object {
+        if (d.model->limits().adapters == 0) return py::none();
+        return py::cast(PyAdapterSpec{d.model});
+      })
       .def("forward", forward, py::arg("requests"), py::arg("cache"), py::arg("adapters") = py::none())
       .def("set_graphs", [](PyDecoder& d, bool on) { d.model->set_graphs(on); })
       .def_property_readonly("weight_bytes", [](const PyDecoder& d) { return d.model->weight_bytes(); })
@@ -577,13 +610,14 @@ void bind_engine(py::module_& m) {
   // Builds a decoder of `config` (a dict of geometry) with N(0, std) weights: synthetic models
   // of a named architecture for benchmarks and tests.
   m.def("_synthetic_decoder", [](const Device& device, const py::dict& config, int tp, int rank,
-                                 uint64_t seed, float stdv) -> py::object {
+                                 uint64_t seed, float stdv, int adapters) -> py::object {
     ModelConfig cfg = model_config_from_dict(config);
     std::shared_ptr<DecoderModel> model;
     {
       py::gil_scoped_release nogil;
       model = std::make_shared<DecoderModel>(device, cfg, tp, rank);
       if (stdv > 0) model->init_random(seed, stdv);
+      model->set_adapter_slots(adapters);
     }
     auto fill = [&](PyDecoder& d) {
       d.model = model;
@@ -599,7 +633,7 @@ void bind_engine(py::module_& m) {
     fill(d);
     return py::cast(d);
   }, py::arg("device"), py::arg("config"), py::arg("tp") = 1, py::arg("rank") = 0,
-     py::arg("seed") = 0, py::arg("std") = 0.02f);
+     py::arg("seed") = 0, py::arg("std") = 0.02f, py::arg("adapters") = 0);
 
   m.def("_layout", [](const std::vector<int64_t>& lens) { return layout(lens); });
 

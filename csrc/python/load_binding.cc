@@ -1,6 +1,8 @@
 // Checkpoints and load options: the choices of a load, checked against the registry before any
 // weight is read, and the strict load into device memory.
 #include <pybind11/pybind11.h>
+
+#include "engine/lora.h"
 #include <pybind11/stl.h>
 
 #include "engine/checkpoint.h"
@@ -163,6 +165,7 @@ void bind_checkpoint_and_load(py::module_& m) {
           model = std::make_shared<DecoderModel>(device, s.config, s.chips, device.state()->rank);
           load_weights(*model, *c.ck);
           model->set_batch_invariant(o.batch_invariant);
+          if (o.adapters) model->set_adapter_slots(LoraAdapter::kSlots);
         }
         py::object decoder = make_decoder(s, model, o.batch_invariant);
         if (s.chips > 1)
@@ -171,4 +174,6 @@ void bind_checkpoint_and_load(py::module_& m) {
       }, py::arg("checkpoint"), py::arg("device"));
 
   m.def("_architectures", []() { return architecture_names(); });
+  // The native checkpoint behind a Checkpoint object (for the engine's own classes).
+  m.def("_checkpoint_ptr", [](const PyCheckpoint& c) { return reinterpret_cast<uintptr_t>(c.ck.get()); });
 }

@@ -2,10 +2,13 @@
 // its strides, every launch as a CUDA stream handle. The engine's own model code calls the same
 // launchers from C++; this surface exists so tests and tools can drive one kernel at a time.
 #include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
 
 #include <cstdint>
 #include <stdexcept>
 #include <string>
+#include <tuple>
+#include <vector>
 
 #include "kernels/gemm.cuh"
 #include "kernels/ops.cuh"
@@ -37,9 +40,18 @@ void bind_ops(py::module_& m) {
          uint64_t counters, int counters_len, uint64_t status, uint64_t stream, uint64_t trace,
          int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
          long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups,
-         int w_scale_rows) {
+         int w_scale_rows, const std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>& segments) {
         foa::GemmArgs g;
         g.w_scale_rows = w_scale_rows;
+        if (segments.size() > 2) throw std::runtime_error("gemm: at most two extra K segments");
+        for (size_t i = 0; i < segments.size(); ++i) {
+          const auto& [sa, slda, sw, sldw, sk] = segments[i];
+          g.seg[i].a = as_ptr<void>(sa);
+          g.seg[i].lda = slda;
+          g.seg[i].w = as_ptr<void>(sw);
+          g.seg[i].ldw = sldw;
+          g.seg[i].K = sk;
+        }
         g.group_tiles = as_ptr<const int>(group_tiles);
         g.tile_group = as_ptr<const int>(tile_group);
         g.group_tile = group_tile;
@@ -80,7 +92,8 @@ void bind_ops(py::module_& m) {
       py::arg("stream"), py::arg("trace") = 0, py::arg("w_format") = 0, py::arg("w_scale") = 0,
       py::arg("w_scale_ld") = 0, py::arg("w_tensor_scale") = 1.0f, py::arg("a_scale") = 0,
       py::arg("a_scale_ld") = 0, py::arg("group_tiles") = 0, py::arg("tile_group") = 0,
-      py::arg("group_tile") = 0, py::arg("groups") = 0, py::arg("w_scale_rows") = 128);
+      py::arg("group_tile") = 0, py::arg("groups") = 0, py::arg("w_scale_rows") = 128,
+      py::arg("segments") = std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>{});
 
   m.def(
       "quantize_fp8_rows",

@@ -4,6 +4,7 @@
 #include <memory>
 #include <string>
 
+#include "engine/lora.h"
 #include "engine/model.h"
 
 // A loaded decoder: the model, and its load's descriptive fields.
@@ -19,3 +20,12 @@ struct PyQwen3Model : PyDecoder {};
 struct PyLlamaForCausalLM : PyDecoder {};
 struct PyMistralForCausalLM : PyDecoder {};
 struct PyQwen3MoeForCausalLM : PyDecoder {};
+
+// The LoRA adapters a decoder's calls run with, and one loaded adapter.
+struct PyAdapterSpec {
+  std::shared_ptr<foa::engine::DecoderModel> model;
+};
+struct PyAdapter {
+  std::shared_ptr<const foa::engine::LoraAdapter> adapter;
+  std::shared_ptr<foa::engine::DecoderModel> model;  // keeps the decoder alive
+};

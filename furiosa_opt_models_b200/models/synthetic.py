@@ -142,3 +142,62 @@ def engine_weights(cfg: dict, hf: dict[str, torch.Tensor]) -> dict[str, torch.Te
                 for x in range(E)])
             out[e + "experts_down"] = torch.cat([hf[p + f"mlp.experts.{x}.down_proj.weight"] for x in range(E)])
     return out
+
+
+LORA_MODULES = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+
+
+def write_lora(directory: str, cfg: dict, r: int = 8, alpha: float = 16.0, seed: int = 0, std: float = 0.05,
+               modules=LORA_MODULES) -> dict[str, torch.Tensor]:
+    """A synthetic PEFT LoRA checkpoint for a geometry (adapter_config.json and
+    adapter_model.safetensors); returns {"<layer>.<module>": (A [r, in], B [out, r])}."""
+    from safetensors.torch import save_file
+
+    os.makedirs(directory, exist_ok=True)
+    g = torch.Generator().manual_seed(seed)
+    H, D, I = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
+    shapes = {"q_proj": (H, cfg["q_heads"] * D), "k_proj": (H, cfg["kv_heads"] * D),
+              "v_proj": (H, cfg["kv_heads"] * D), "o_proj": (cfg["q_heads"] * D, H),
+              "gate_proj": (H, I), "up_proj": (H, I), "down_proj": (I, H)}
+    tensors, out = {}, {}
+    for l in range(cfg["layers"]):
+        for m in modules:
+            fin, fout = shapes[m]
+            a = (torch.randn(r, fin, generator=g) * std).bfloat16()
+            b = (torch.randn(fout, r, generator=g) * std).bfloat16()
+            path = ("self_attn." if m in ("q_proj", "k_proj", "v_proj", "o_proj") else "mlp.") + m
+            tensors[f"base_model.model.model.layers.{l}.{path}.lora_A.weight"] = a
+            tensors[f"base_model.model.model.layers.{l}.{path}.lora_B.weight"] = b
+            out[f"{l}.{m}"] = (a, b)
+    save_file(tensors, os.path.join(directory, "adapter_model.safetensors"))
+    config = {"r": r, "lora_alpha": alpha, "target_modules": list(modules), "bias": "none",
+              "peft_type": "LORA", "use_dora": False, "use_rslora": False}
+    with open(os.path.join(directory, "adapter_config.json"), "w") as f:
+        json.dump(config, f)
+    return out
+
+
+def merge_lora(weights: dict, cfg: dict, lora: dict, r: int, alpha: float) -> dict:
+    """Engine-layout FP32 weights with a LoRA update merged (W + alpha / r * B A), for the dense
+    oracle."""
+    from .dense import interleave_gate_up, split_gate_up
+
+    scale = alpha / r
+    out = dict(weights)
+    H, D = cfg["hidden"], cfg["head_dim"]
+    qr, kvr = cfg["q_heads"] * D, cfg["kv_heads"] * D
+    for l in range(cfg["layers"]):
+        def delta(m):
+            a, b = lora[f"{l}.{m}"]
+            return (b.float() * scale).bfloat16().float() @ a.float()
+        p = f"layers.{l}."
+        qkv = out[p + "qkv"].float().clone()
+        qkv[:qr] += delta("q_proj")
+        qkv[qr:qr + kvr] += delta("k_proj")
+        qkv[qr + kvr:] += delta("v_proj")
+        out[p + "qkv"] = qkv
+        out[p + "o"] = out[p + "o"].float() + delta("o_proj")
+        gate, up = split_gate_up(out[p + "gate_up"].float())
+        out[p + "gate_up"] = interleave_gate_up(gate + delta("gate_proj"), up + delta("up_proj"))
+        out[p + "down"] = out[p + "down"].float() + delta("down_proj")
+    return out

@@ -159,6 +159,7 @@ def gemm(
     mode: int = MODE_AUTO,
     splits: int = 0,
     trace: torch.Tensor | None = None,
+    segments: list | None = None,
 ) -> torch.Tensor:
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
@@ -167,6 +168,8 @@ def gemm(
     ``QuantizedWeight`` runs in its format's contract: ``fp8_block`` and ``nvfp4_a4`` quantize the
     inputs and use the FP8 / block-scaled FP4 tensor cores (W8A8, W4A4); ``fp8_block_w8a16`` and
     ``nvfp4`` dequantize the weights to BF16 tile by tile inside the kernel (W8A16, W4A16).
+    ``segments`` [(a1 [M, k1], w1 [N, k1]), ...] (at most two, k a multiple of 64) add
+    ``a1 @ w1.T`` and so on into the same FP32 sums before the epilogue (LoRA updates).
     """
     _rowmajor(a, "a")
     M, K = a.shape
@@ -216,6 +219,7 @@ def gemm(
         epilogue, mode, splits, s.workspace.data_ptr(), s.workspace.numel() * 4,
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
         0 if trace is None else trace.data_ptr(), **qargs,
+        segments=[(sa.data_ptr(), sa.stride(0), sw.data_ptr(), sw.stride(0), sa.shape[1]) for sa, sw in (segments or [])],
     )
     return out
 

@@ -246,3 +246,46 @@ def test_load_time_fp8_quantization(tmp_path, granularity):
         logits = dense.forward(w, cfg, seq)[-1]
         assert logits[int(t)] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
         seq = torch.cat([seq, torch.tensor([int(t)], dtype=torch.int32)])
+
+
+def test_lora_adapters_in_two_slots(tmp_path):
+    """Two PEFT LoRA adapters in the two slots of one call, and a request with none: each
+    request's greedy tokens agree with the dense forward of its merged weights."""
+    import json as _json
+
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine._native._synthetic_decoder(device, cfg, seed=7, std=0.05, adapters=2)
+    spec = model.adapters
+    assert spec is not None and spec.RANK == 32 and spec.SLOTS == 2
+    base = _weights(model)
+    adapters, merged = [], []
+    for i, (r, alpha) in enumerate([(8, 16.0), (16, 8.0)]):
+        d = tmp_path / f"lora{i}"
+        lora = synthetic.write_lora(str(d), cfg, r=r, alpha=alpha, seed=i + 1)
+        with open(d / "adapter_config.json") as f:
+            ck = engine.Checkpoint(str(d), config=_json.load(f))
+        adapters.append(dec.Adapter(spec, ck))
+        merged.append(synthetic.merge_lora(base, cfg, lora, r, alpha))
+    gen = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen, dtype=torch.int32) for n in (9, 21, 14)]
+    slots = [0, 1, None]
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(p).to_hbm(device), len(p), alloc.take(4)) for p in prompts]
+    reqs = [dec.Request([s.blocks], 0, s.prompt, dec.Keep.LAST, adapter=slot) for s, slot in zip(seqs, slots)]
+    out = model.forward(reqs, cache, adapters).to_host().numpy().tolist()
+    device.synchronize()
+    for p, t, slot in zip(prompts, out, slots):
+        w = base if slot is None else merged[slot]
+        logits = dense.forward(w, cfg, p)[-1]
+        assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item())), slot
+    # A request naming an empty slot is refused.
+    with pytest.raises(ValueError):
+        model.forward([dec.Request([seqs[0].blocks], 0, seqs[0].prompt, dec.Keep.LAST, adapter=1)], cache,
+                      [adapters[0], None])

@@ -109,3 +109,28 @@ def test_gemm_cluster_splits(M, N, K, splits):
     again = ops.gemm(a, w, mode=ops.MODE_SWAP, splits=splits, residual=res)
     torch.cuda.synchronize()
     assert torch.equal(out, again)
+
+
+@pytest.mark.parametrize("M,mode,epi", [(16, 2, 0), (64, 2, 1), (200, 1, 0), (48, 2, 2), (300, 1, 2)])
+def test_gemm_extra_k_segments(M, mode, epi):
+    """Extra K segments (the LoRA form [X | Z1 | Z2] x [W | B1 | B2]^T) in every epilogue."""
+    ops = _ops()
+    torch.manual_seed(M)
+    N, K = 768, 1024
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    z1 = torch.randn(M, 128, device="cuda", dtype=torch.bfloat16)
+    b1 = torch.randn(N, 128, device="cuda", dtype=torch.bfloat16) * 0.05
+    z2 = torch.randn(M, 64, device="cuda", dtype=torch.bfloat16)
+    b2 = torch.randn(N, 64, device="cuda", dtype=torch.bfloat16) * 0.05
+    out = ops.gemm(a, w, epilogue=epi, mode=mode, segments=[(z1, b1), (z2, b2)])
+    torch.cuda.synchronize()
+    full = _ref(a, w) + _ref(z1, b1) + _ref(z2, b2)
+    if epi == 2:
+        blocks = full.view(M, -1, 2, 128)
+        from furiosa_opt_models_b200.models import reference as R
+
+        ref = R.swiglu(blocks[:, :, 0].reshape(M, N // 2), blocks[:, :, 1].reshape(M, N // 2))
+    else:
+        ref = full
+    _close(out, ref, 2e-2 if epi != 1 else 1e-3)

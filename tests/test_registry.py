@@ -19,7 +19,7 @@ def test_lists_every_name_once():
 
 def _ckpt(tmp_path, config):
     d = tmp_path / "ck"
-    d.mkdir(exist_ok=True)
+    d.mkdir(parents=True, exist_ok=True)
     return engine.Checkpoint(str(d), config)
 
 
@@ -60,8 +60,10 @@ def test_option_refusals(tmp_path):
         engine.LoadOptions().layers(range(0, 4, 2))
     with pytest.raises(ValueError, match="a quantization is fp8_per_tensor or fp8_per_channel"):
         engine.LoadOptions().quantization("int4")
+    engine.LoadOptions().adapters().parse(ck)  # dense BF16 decoders take LoRA adapters
+    moe = _ckpt(tmp_path / "moe", synthetic.hf_config(configs.get("tiny-qwen3-moe")))
     with pytest.raises(NotImplementedError, match="takes no adapter"):
-        engine.LoadOptions().adapters().parse(ck)
+        engine.LoadOptions().adapters().parse(moe)
     with pytest.raises(NotImplementedError, match="chips: a load runs on 1, 2, 4 or 8 chips"):
         engine.LoadOptions().chips(3).parse(ck)
     assert engine.LoadOptions().chips(8).select(ck)["chips"] == 8
