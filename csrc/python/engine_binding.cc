@@ -720,6 +720,38 @@ void bind_engine(py::module_& m) {
     d.model->set_collectives(coll);
     return py::bytes(coll->handle());
   });
+  // Device time of the fused tensor-parallel add+norm on `rows` rows (every rank calls it in
+  // lockstep): milliseconds per call over `iters` calls on the decoder's stream.
+  m.def("_tp_bench_add_norm", [](PyDecoder& d, int rows, int iters) {
+    auto coll = d.model->collectives();
+    if (!coll) throw ValueError("the decoder has no tensor-parallel heap");
+    const auto& cfg = d.model->config();
+    auto st = d.model->device().state();
+    py::gil_scoped_release nogil;
+    st->activate();
+    cudaStream_t s = st->stream;
+    const auto* w = d.model->weights().at("final_norm").ptr;
+    auto once = [&]() {
+      float* partial = coll->partial_buffer(static_cast<size_t>(rows) * cfg.hidden);
+      coll->add_norm(partial, coll->residual_buffer(), w, cfg.eps, coll->hidden_buffer(), rows, cfg.hidden, s);
+    };
+    coll->begin_call(s);
+    for (int i = 0; i < 3; ++i) once();
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    coll->begin_call(s);
+    cudaEventRecord(a, s);
+    for (int i = 0; i < iters; ++i) once();
+    cudaEventRecord(b, s);
+    cudaEventSynchronize(b);
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    st->check_status();
+    return static_cast<double>(ms) / iters;
+  });
   m.def("_tp_connect", [](PyDecoder& d, const std::vector<py::bytes>& handles) {
     std::vector<std::string> hs;
     for (const auto& h : handles) hs.push_back(std::string(h));

@@ -5,6 +5,7 @@ sequence: `--warmup` launches, then `--iters` timed ones, each after an L2 flush
     python -m furiosa_opt_models_b200.utils.kernel_bench decode-attn --rows 64 --keys 2048
     python -m furiosa_opt_models_b200.utils.kernel_bench prefill-attn --rows 8192 --seqs 8
     python -m furiosa_opt_models_b200.utils.kernel_bench moe --tokens 64
+    torchrun --nproc-per-node 2 -m furiosa_opt_models_b200.utils.kernel_bench add-norm --rows 64
 
 Prints one JSON line: the mean device time per launch and the algorithmic bytes and FLOPs.
 """
@@ -112,6 +113,43 @@ def moe(args) -> dict:
     return dict(kernel="moe_block", tokens=T, tile=tile, us=round(us, 2), expert_weight_gbs=round(wbytes / us / 1e3, 1))
 
 
+def add_norm(args) -> dict:
+    """The fused tensor-parallel add+norm (rank-ordered FP32 sum over NVLink + residual +
+    RMSNorm), device-timed on every rank, the maximum reported."""
+    import datetime
+    import os
+
+    import torch.distributed as dist
+
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import _native
+    from furiosa_opt_models_b200.models import configs
+    from furiosa_opt_models_b200.parallel import tp
+
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    cfg = configs.get(args.model)
+    device = engine.Device(engine.Placement(list(range(world)), range(8)))
+    model = _native._synthetic_decoder(device, cfg, tp=world, rank=rank, seed=0, std=0.02)
+    tp.attach(model, device)
+    ms = _native._tp_bench_add_norm(model, args.rows, args.iters)
+    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    us = t.item() * 1000.0
+    H = cfg["hidden"]
+    one_shot = args.rows * H * 4 * (world - 1) <= (1 << 20) or args.rows < world
+    nvlink = (args.rows * H * 4 * (world - 1) if one_shot
+              else args.rows * H * 4 * (world - 1) / world + 2 * args.rows * H * 2 * (world - 1) / world)
+    tp.detach(model)
+    dist.destroy_process_group()
+    return dict(kernel="tp_add_norm", world=world, rows=args.rows, hidden=H, mode="one-shot" if one_shot else "two-shot",
+                us=round(us, 2), nvlink_bytes_per_rank=int(nvlink),
+                nvlink_gbs=round(nvlink / us / 1e3, 1), roofline_fraction_of_770=round(nvlink / us / 1e3 / 770, 3),
+                _rank=rank)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = p.add_subparsers(dest="what", required=True)
@@ -133,12 +171,17 @@ def main() -> None:
     f.add_argument("--kv-heads", type=int, default=8)
     m = sub.add_parser("moe")
     m.add_argument("--tokens", type=int, default=64)
-    for s in (g, d, f, m):
+    a = sub.add_parser("add-norm")
+    a.add_argument("--rows", type=int, default=64)
+    a.add_argument("--model", default="qwen3-1.7b")
+    for s in (g, d, f, m, a):
         s.add_argument("--warmup", type=int, default=3)
         s.add_argument("--iters", type=int, default=10)
     args = p.parse_args()
-    out = {"gemm": gemm, "decode-attn": decode_attn, "prefill-attn": prefill_attn, "moe": moe}[args.what](args)
-    print(json.dumps(out), flush=True)
+    out = {"gemm": gemm, "decode-attn": decode_attn, "prefill-attn": prefill_attn, "moe": moe,
+           "add-norm": add_norm}[args.what](args)
+    if out.pop("_rank", 0) == 0:
+        print(json.dumps(out), flush=True)
 
 
 if __name__ == "__main__":
