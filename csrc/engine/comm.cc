@@ -1,5 +1,6 @@
 #include "comm.h"
 
+#include <cstdlib>
 #include <cstring>
 
 namespace foa::engine {
@@ -20,10 +21,16 @@ PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int6
   off = align_to(off + 64 * sizeof(unsigned long long), 4096);
   off_arrivals_ = off;
   off = align_to(off + 64, 256);
+  off_seq_ = off;
+  off = align_to(off + 64, 256);
   off_epoch_ = off;
   off = align_to(off + 64, 256);
-  off_partial_ = off;
-  off = align_to(off + 2 * static_cast<size_t>(rows) * cols * sizeof(float), 4096);
+  // Receive region: [2 buffers][world source slots][slot rows][cols] FP32. One-shot calls use
+  // `rows` slot rows of every slot, reduce-scatter calls ceil(rows / world).
+  slot_rows_ = (rows + world - 1) / world;
+  off_recv_ = off;
+  const size_t recv_floats = 2 * static_cast<size_t>(world) * slot_rows_ * cols;
+  off = align_to(off + recv_floats * sizeof(float), 4096);
   off_residual_ = off;
   off = align_to(off + static_cast<size_t>(rows) * cols * 2, 4096);
   off_hidden_ = off;
@@ -37,6 +44,13 @@ PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int6
   heap_bytes_ = off;
   st->check_cuda(cudaMalloc(&heap_, heap_bytes_), "tensor-parallel heap");
   st->check_cuda(cudaMemset(heap_, 0, heap_bytes_), "tensor-parallel heap");
+  // Every receive slot starts unwritten; peers write into it only after `connect`.
+  if (foa::tp_clear_recv(reinterpret_cast<float*>(static_cast<char*>(heap_) + off_recv_), recv_floats,
+                         st->stream) != 0)
+    st->fail("receive region launch failed");
+  st->check_cuda(cudaStreamSynchronize(st->stream), "tensor-parallel heap");
+  const char* lim = std::getenv("FOA_TP_ONESHOT_BYTES");
+  one_shot_limit_ = lim ? static_cast<size_t>(std::strtoull(lim, nullptr, 10)) : (size_t{1} << 20);
   peer_base_.assign(world, nullptr);
   opened_.assign(world, false);
   peer_base_[rank] = heap_;
@@ -77,7 +91,7 @@ void PeerCollectives::connect(const std::vector<std::string>& handles) {
   for (int p = 0; p < world_; ++p) {
     char* b = static_cast<char*>(peer_base_[p]);
     peers_.signal[p] = reinterpret_cast<unsigned long long*>(b + off_signal_);
-    peers_.partial[p] = reinterpret_cast<float*>(b + off_partial_);
+    peers_.recv[p] = reinterpret_cast<float*>(b + off_recv_);
     peers_.residual[p] = reinterpret_cast<__nv_bfloat16*>(b + off_residual_);
     peers_.hidden[p] = reinterpret_cast<__nv_bfloat16*>(b + off_hidden_);
     peers_.gather_value[p] = reinterpret_cast<float*>(b + off_gvalue_);
@@ -90,15 +104,30 @@ void PeerCollectives::begin_call(cudaStream_t stream) {
   if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
   ++epoch_;
   site_ = 0;
-  half_ = 0;
   auto* ep = reinterpret_cast<unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
   if (foa::tp_set_epoch(ep, epoch_, stream) != 0) device_.state()->fail("epoch launch failed");
 }
 
-float* PeerCollectives::partial_buffer(size_t floats) {
-  if (floats > static_cast<size_t>(rows_) * cols_) throw ValueError("call exceeds the tensor-parallel heap");
-  return reinterpret_cast<float*>(static_cast<char*>(heap_) + off_partial_) +
-         static_cast<size_t>(half_) * rows_ * cols_;
+bool PeerCollectives::two_shot(int rows) const {
+  // Little data: every rank receives every row (one NVLink hop, no barrier). More: each row goes
+  // to the rank that reduces its slice, which stores the results into every rank (1/world of the
+  // traffic, plus a closing barrier).
+  const size_t one_shot_bytes = static_cast<size_t>(rows) * cols_ * 4 * (world_ - 1);
+  return one_shot_bytes > one_shot_limit_ || rows > slot_rows_;
+}
+
+foa::GemmPeerOut PeerCollectives::reduce_target(int rows, int cols) {
+  if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
+  if (cols != cols_ || rows > rows_) throw ValueError("call exceeds the tensor-parallel heap");
+  foa::GemmPeerOut t;
+  for (int p = 0; p < world_; ++p) t.dst[p] = peers_.recv[p];
+  t.world = world_;
+  t.rank = rank_;
+  t.owner_rows = two_shot(rows) ? (rows + world_ - 1) / world_ : 0;
+  t.slot_stride = static_cast<long>(slot_rows_) * cols_;
+  t.buf_stride = t.slot_stride * world_;
+  t.seq = reinterpret_cast<const unsigned int*>(static_cast<char*>(heap_) + off_seq_);
+  return t;
 }
 
 __nv_bfloat16* PeerCollectives::residual_buffer() {
@@ -142,16 +171,19 @@ void PeerCollectives::moe_combine_norm(int which, const int32_t* pos_all, const 
   if (foa::tp_moe_combine_norm(a, stream) != 0) device_.state()->fail("expert-parallel combine launch failed");
 }
 
-void PeerCollectives::add_norm(const float* partial, __nv_bfloat16* residual,
-                               const __nv_bfloat16* weight, float eps, __nv_bfloat16* out,
-                               int rows, int cols, cudaStream_t stream) {
-  if (partial != partial_buffer(0) || residual != residual_buffer() || out != hidden_buffer())
+void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+                               __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) {
+  if (residual != residual_buffer() || out != hidden_buffer())
     throw DeviceError("tensor-parallel add_norm takes the heap's own buffers");
+  if (cols != cols_ || rows > rows_) throw ValueError("call exceeds the tensor-parallel heap");
   foa::AddNormArgs a{};
   a.peers = peers_;
-  for (int p = 0; p < world_; ++p) a.peers.partial[p] += static_cast<size_t>(half_) * rows_ * cols_;
   a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
   a.arrivals = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_arrivals_);
+  a.seq = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_seq_);
+  a.recv = peers_.recv[rank_];
+  a.slot_stride = static_cast<long>(slot_rows_) * cols_;
+  a.buf_stride = a.slot_stride * world_;
   a.weight = weight;
   a.eps = eps;
   a.rows = rows;
@@ -159,13 +191,9 @@ void PeerCollectives::add_norm(const float* partial, __nv_bfloat16* residual,
   a.rank = rank_;
   a.world = world_;
   a.site = site_++;
-  // Little data: every rank reduces every row (one barrier; reads (world - 1) partials over
-  // NVLink). More: each rank reduces a slice and stores it into every rank (a second barrier, but
-  // 1/world of the reads), which wins once the one-shot reads outgrow a barrier's latency.
-  const size_t one_shot_bytes = static_cast<size_t>(rows) * cols * 4 * (world_ - 1);
-  a.two_shot = (rows >= world_ && one_shot_bytes > (size_t{1} << 20)) ? 1 : 0;
+  a.two_shot = two_shot(rows) ? 1 : 0;
   a.status = status_;
-  half_ ^= 1;
+  a.trace = trace_;
   if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
 }
 

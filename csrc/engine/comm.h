@@ -27,11 +27,11 @@ class PeerCollectives : public Collectives {
   int rank() const override { return rank_; }
   int world() const override { return world_; }
   void begin_call(cudaStream_t stream) override;
-  void add_norm(const float* partial, __nv_bfloat16* residual, const __nv_bfloat16* weight,
-                float eps, __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) override;
+  foa::GemmPeerOut reduce_target(int rows, int cols) override;
+  void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+                __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) override;
   void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
               cudaStream_t stream) override;
-  float* partial_buffer(size_t floats) override;
   __nv_bfloat16* residual_buffer() override;
   __nv_bfloat16* hidden_buffer() override;
   __nv_bfloat16* moe_rows(int which, size_t rows) override;
@@ -40,6 +40,8 @@ class PeerCollectives : public Collectives {
                         int cols, cudaStream_t stream) override;
   // A device-side barrier of every rank (used before the heap is released).
   void barrier(cudaStream_t stream);
+  // Measurement: the add_norm kernels write milestone timestamps here (null: none).
+  void set_trace(unsigned long long* trace) { trace_ = trace; }
 
  private:
   Device device_;
@@ -48,16 +50,21 @@ class PeerCollectives : public Collectives {
   int cols_;
   void* heap_ = nullptr;
   size_t heap_bytes_ = 0;
-  size_t off_signal_, off_arrivals_, off_epoch_, off_partial_, off_residual_, off_hidden_,
+  // Reduce-scatter (two-shot) rather than one-shot for a call of `rows` rows.
+  bool two_shot(int rows) const;
+
+  size_t off_signal_, off_arrivals_, off_seq_, off_epoch_, off_recv_, off_residual_, off_hidden_,
       off_gvalue_, off_gindex_, off_moe_;
+  int64_t slot_rows_ = 0;          // rows of one source slot of the receive region
+  size_t one_shot_limit_ = 0;      // bytes a one-shot call may push to its peers
   std::vector<void*> peer_base_;   // every rank's heap as mapped here (own heap at rank_)
   std::vector<bool> opened_;
   foa::PeerBuffers peers_{};
   bool connected_ = false;
   unsigned long long epoch_ = 0;
   int site_ = 0;
-  int half_ = 0;                   // partial buffer of the next add_norm
   int* status_ = nullptr;
+  unsigned long long* trace_ = nullptr;
 };
 
 }  // namespace foa::engine

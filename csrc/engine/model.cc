@@ -625,8 +625,10 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     ++kernels;
   };
   auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
-                  int epi, const void* res, int lora_layer = -1, int lora_module = 0) {
+                  int epi, const void* res, int lora_layer = -1, int lora_module = 0,
+                  const foa::GemmPeerOut* peer = nullptr) {
     foa::GemmArgs g;
+    if (peer != nullptr) g.peer = *peer;
     // LoRA slots: Z_s = X A_s^T (its rows zeroed outside slot s), added as extra K segments
     // Z_s B_s^T into the projection's FP32 sums.
     int nseg = 0;
@@ -741,7 +743,6 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                       static_cast<int>(T), H, s),
        "embedding");
   const bool tp = tp_ > 1;
-  float* partial = nullptr;
   foa::PagedAttention attn;
   attn.q = bf(ws_q_);
   attn.o = bf(ws_attn_);
@@ -795,10 +796,10 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                         H, cfg_.eps, s),
            "rmsnorm");
     } else {
-      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
-      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, partial, H,
-           foa::kEpiF32, nullptr, l, LoraAdapter::kO);
-      coll_->add_norm(partial, x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
+      const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
+      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, nullptr, H,
+           foa::kEpiF32, nullptr, l, LoraAdapter::kO, &target);
+      coll_->add_norm(x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
     }
     if (cfg_.experts > 0) {
@@ -861,10 +862,10 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     } else {
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
-      partial = coll_->partial_buffer(static_cast<size_t>(T) * H);
-      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, partial, H,
-           foa::kEpiF32, nullptr, l, LoraAdapter::kDown);
-      coll_->add_norm(partial, x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
+      const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
+      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, nullptr, H,
+           foa::kEpiF32, nullptr, l, LoraAdapter::kDown, &target);
+      coll_->add_norm(x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
       ++kernels;
     }
   }

@@ -20,6 +20,7 @@
 #include <vector>
 
 #include "batch.h"
+#include "kernels/gemm.cuh"
 #include "runtime.h"
 
 namespace foa::engine {
@@ -70,15 +71,17 @@ class Collectives {
   virtual ~Collectives() = default;
   virtual int rank() const = 0;
   virtual int world() const = 0;
-  // Sums every rank's FP32 partial [rows, cols] in rank order, adds the BF16 residual (updated in
-  // place, rounded once) and writes RMSNorm(residual) * weight to `out` on every rank.
-  virtual void add_norm(const float* partial, __nv_bfloat16* residual, const __nv_bfloat16* weight,
-                        float eps, __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) = 0;
+  // Where a row-parallel GEMM of `rows` x `cols` FP32 partials stores them (over NVLink, into the
+  // ranks that reduce them) ahead of the add_norm of the same shape.
+  virtual foa::GemmPeerOut reduce_target(int rows, int cols) = 0;
+  // Sums every rank's FP32 partial [rows, cols] (pushed by the GEMM given reduce_target) in rank
+  // order, adds the BF16 residual (updated in place, rounded once) and writes
+  // RMSNorm(residual) * weight to `out` on every rank.
+  virtual void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+                        __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) = 0;
   // The first maximum over ranks of (value, token) candidates [rows]: tokens into `out`.
   virtual void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
                       cudaStream_t stream) = 0;
-  // Scratch the next add_norm's partial must live in (symmetric across ranks).
-  virtual float* partial_buffer(size_t floats) = 0;
   // The residual stream and the normed rows, in memory every rank can write.
   virtual __nv_bfloat16* residual_buffer() = 0;
   virtual __nv_bfloat16* hidden_buffer() = 0;

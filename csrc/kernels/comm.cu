@@ -2,15 +2,19 @@
 //
 // The reference's all-reduce is a deterministic FP32 recursive doubling over chip DMA, narrowed
 // to BF16 once at the end (crates/furiosa-opt-models/src/ops/collective/mod.rs:22-141); its
-// all-gather joins parts in chip order (gather.rs:17-99). Here every rank reads its peers'
-// FP32 partial sums directly over NVLink (peer pointers opened through CUDA IPC) and adds them in
-// rank order, so every rank computes the same bits; the sum is fused with the residual add (one
-// rounding) and the RMSNorm that follows, and, for large calls, with the all-gather of the normed
-// rows (two-shot: each rank reduces a slice of rows and stores it into every rank's buffers).
+// all-gather joins parts in chip order (gather.rs:17-99). Here the row-parallel GEMM's epilogue
+// stores its FP32 partial tiles straight into the reducing ranks' receive buffers over NVLink as
+// the tiles finish (GemmPeerOut), and the reducer adds the landed partials in rank order, so every
+// rank computes the same bits; the sum is fused with the residual add (one rounding) and the
+// RMSNorm that follows. Small calls push every row to every rank (one-shot: one NVLink hop, no
+// barrier); large calls push each row to the rank that owns its slice (reduce-scatter), and the
+// owner stores the normed rows into every rank (all-gather) before a closing barrier.
 //
-// Ranks meet at device-side barriers: a rank stores a monotonically increasing value into its
-// slot of every peer's signal array (release, system scope) and waits, bounded, until every slot
-// of its own array has reached the value. A wait that gives up records kTimeoutPeer and returns.
+// Arrival is detected without flags: a receive slot holds -0.0 until its value lands (a GEMM
+// never sends -0.0), and the reducer writes -0.0 back after reading. Ranks meet at device-side
+// barriers elsewhere: a rank stores a monotonically increasing value into its slot of every
+// peer's signal array (release, system scope) and waits, bounded, until every slot of its own
+// array has reached the value. A wait that gives up records kTimeoutPeer and returns.
 
 #include "comm.cuh"
 #include "launch.cuh"
@@ -66,24 +70,40 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-// One CTA of 256 threads per row; each thread holds kVec vectors of 8 columns.
+constexpr uint32_t kUnwritten = 0x80000000u;  // -0.0: a receive slot whose value has not landed
+
+__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
+  float4 v;
+  asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ bool unwritten(const float4& v) {
+  return (__float_as_uint(v.x) == kUnwritten) | (__float_as_uint(v.y) == kUnwritten) |
+         (__float_as_uint(v.z) == kUnwritten) | (__float_as_uint(v.w) == kUnwritten);
+}
+
+// One CTA of 256 threads per row; each thread holds kVec vectors of 8 columns. The partials were
+// pushed here by the GEMMs of every rank; each thread polls its 8 values of every source slot,
+// adds them in rank order and marks the slot unwritten again.
 template <int kVec>
 __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
   pdl_wait();
   pdl_trigger();
   __shared__ float red[8];
-  __shared__ int ok_s;
   const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
-  const int row = a.two_shot ? a.rank * rs + blockIdx.x : blockIdx.x;
-  if (threadIdx.x == 0) {
-    const unsigned long long v = barrier_value(a.epoch, a.site, 0);
-    if (blockIdx.x == 0) signal_all(a.peers, a.rank, a.world, v);
-    ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
-  }
-  __syncthreads();
-  const bool ok = ok_s;
+  const int slot_row = blockIdx.x;
+  const int row = a.two_shot ? a.rank * rs + slot_row : slot_row;
+  float* recv = a.recv + (long)(__ldcg(a.seq) & 1u) * a.buf_stride + (long)slot_row * a.cols;
   const int nvec = a.cols / 8;
-  if (ok && row < a.rows && blockIdx.x < rs) {
+  const bool tracer = a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
+  if (tracer) a.trace[0] = global_ns();
+  if (row < a.rows) {
+    const uint64_t start = global_ns();
+    bool late = false;
     float h[kVec][8];
     float ss = 0.f;
 #pragma unroll
@@ -94,10 +114,23 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
 #pragma unroll
       for (int t = 0; t < 8; ++t) acc[t] = 0.f;
       for (int p = 0; p < a.world; ++p) {
-        const float4* src = reinterpret_cast<const float4*>(a.peers.partial[p] + (long)row * a.cols + v * 8);
-        const float4 x0 = src[0], x1 = src[1];
+        float* src = recv + (long)p * a.slot_stride + v * 8;
+        float4 x0, x1;
+        uint32_t spins = 0;
+        for (;;) {
+          x0 = ld_volatile_f4(src);
+          x1 = ld_volatile_f4(src + 4);
+          if (!(unwritten(x0) || unwritten(x1)) || late) break;
+          if ((++spins & 63u) == 0 && global_ns() - start > kWaitLimitNs) {
+            record_status(a.status, kTimeoutPeer);
+            late = true;
+          }
+        }
         acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
         acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
+        const float m = __uint_as_float(kUnwritten);
+        reinterpret_cast<float4*>(src)[0] = make_float4(m, m, m, m);
+        reinterpret_cast<float4*>(src)[1] = make_float4(m, m, m, m);
       }
       const __nv_bfloat16* rp = a.peers.residual[a.rank] + (long)row * a.cols + v * 8;
       const uint4 rv = *reinterpret_cast<const uint4*>(rp);
@@ -119,6 +152,7 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
       }
     }
     const float total = block_sum(ss, red);
+    if (tracer) a.trace[1] = global_ns();
     const float inv = rsqrtf(total / (float)a.cols + a.eps);
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
@@ -139,20 +173,32 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
       }
     }
   }
-  if (!a.two_shot) return;
-  // Two-shot: the last CTA of this rank tells every peer its slice has landed and waits until
-  // every peer's slice has landed here, so the kernel ends only with every row in place.
+  // The last CTA to finish advances the receive sequence (every CTA has read it) and, two-shot,
+  // tells every peer its slice has landed and waits until every peer's slice has landed here, so
+  // the kernel ends only with every row in place.
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    if (a.two_shot)
+      __threadfence_system();
+    else
+      __threadfence();
     const unsigned int done = atomicAdd(a.arrivals, 1u);
     if (done == gridDim.x - 1) {
       *a.arrivals = 0;
-      const unsigned long long v = barrier_value(a.epoch, a.site, 1);
-      signal_all(a.peers, a.rank, a.world, v);
-      wait_all(a.peers, a.rank, a.world, v, a.status);
+      *a.seq += 1u;
+      if (a.two_shot) {
+        const unsigned long long v = barrier_value(a.epoch, a.site, 1);
+        signal_all(a.peers, a.rank, a.world, v);
+        wait_all(a.peers, a.rank, a.world, v, a.status);
+      }
     }
+    if (tracer) a.trace[2] = global_ns();
   }
+}
+
+__global__ void fill_u32_kernel(uint32_t* p, size_t n, uint32_t v) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    p[i] = v;
 }
 
 template <int kVec>
@@ -300,6 +346,12 @@ int tp_add_norm(const AddNormArgs& a, cudaStream_t stream) {
     default: return -2;
   }
   return e == cudaSuccess ? 0 : -5;
+}
+
+int tp_clear_recv(float* recv, size_t floats, cudaStream_t stream) {
+  if (floats == 0) return 0;
+  fill_u32_kernel<<<296, 256, 0, stream>>>(reinterpret_cast<uint32_t*>(recv), floats, kUnwritten);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int tp_argmax(const ArgmaxArgs& a, cudaStream_t stream) {

@@ -58,6 +58,7 @@ struct KParams {
   int* status;
   int out_rows, out_cols;     // logical output shape
   unsigned long long* trace;  // milestone timestamps of CTA 0, or null
+  unsigned long long* cta_trace;  // per-CTA timestamps (8 a CTA; see GemmArgs), or null
   int debug;                  // measurement switches (FOA_GEMM_DEBUG): 1 no stores, 2 no TMEM loads
   // Quantized weights (kWF != 0): block scales and the factor the FP32 sums take.
   const void* wscale;         // FP8: FP32 [ceil(N/128)][ceil(K/128)]; NVFP4: E4M3 [N][K/16]
@@ -83,6 +84,7 @@ struct KParams {
   const int* group_tiles;  // number of token tiles (device), or null
   const int* tile_group;   // group of each token tile (device)
   long group_rows;
+  GemmPeerOut peer;        // tensor-parallel reduction target (peer.world > 0), kEpiF32 only
 };
 
 // Weight formats a GEMM reads: BF16; FP8 block-scaled or NVFP4 codes dequantized to BF16 in
@@ -128,6 +130,8 @@ __device__ __forceinline__ uint4 dequant_e2m1x8(uint32_t v, uint8_t scale_byte) 
 
 __device__ __forceinline__ void mark(const KParams& p, int i) {
   if (p.trace != nullptr && blockIdx.x == 0) p.trace[i] = global_ns();
+  // Milestones 0, 5, 6 of every CTA (its end is written after the last barrier).
+  if (p.cta_trace != nullptr && (i == 0 || i == 5 || i == 6)) p.cta_trace[8 * blockIdx.x + (i == 0 ? 0 : i - 4)] = global_ns();
 }
 
 template <int kMB, int kBN, int kStages, int kAcc, int kWF = kWBf16>
@@ -185,11 +189,113 @@ __device__ __forceinline__ float silu_bf16_times(float g_acc, float u_acc) {
 
 // Stores 16 consecutive output values of one output row (rows mapping) or one output column
 // (swap mapping), applying the residual add and the output type of the epilogue.
+// Tensor-parallel reduction target: where this rank's partial of output row `row` goes on rank q
+// (`poff` is the buffer and source-slot offset, see peer_offset).
+__device__ __forceinline__ float* peer_dst(const KParams& p, long poff, int q, int row) {
+  return p.peer.dst[q] + poff + (long)row * p.ldc;
+}
+
+// -0.0 marks an unwritten receive slot: a -0.0 partial is sent as +0.0 (the sum is unchanged).
+__device__ __forceinline__ float peer_value(float v) {
+  return __float_as_uint(v) == 0x80000000u ? 0.f : v;
+}
+
+__device__ __forceinline__ void peer_store_one(const KParams& p, long poff, int row, int col, float v) {
+  v = peer_value(v);
+  if (p.peer.owner_rows > 0) {
+    const int q = row / p.peer.owner_rows;
+    peer_dst(p, poff, q, row - q * p.peer.owner_rows)[col] = v;
+    return;
+  }
+  for (int q = 0; q < p.peer.world; ++q) peer_dst(p, poff, q, row)[col] = v;
+}
+
+// Buffer and source-slot offset of this launch's peer stores (read after the grid dependency
+// wait: the reducer of the previous call advanced `seq`).
+__device__ __forceinline__ long peer_offset(const KParams& p) {
+  if (p.peer.world == 0) return 0;
+  return (long)(__ldcg(p.peer.seq) & 1u) * p.peer.buf_stride + (long)p.peer.rank * p.peer.slot_stride;
+}
+
 template <int kEpi>
 __device__ __forceinline__ void store16(const KParams& p, int row, int col, const float (&v)[16],
-                                        bool along_row) {
+                                        bool along_row, long poff = 0) {
   // along_row: the 16 values are C[row, col + t]; otherwise C[row + t, col].
   if (p.debug & 1) return;
+  if (kEpi == kEpiF32 && p.peer.world > 0) {
+    if (along_row) {
+      // Rows mapping: lane L holds row `row` (consecutive lanes, consecutive rows). Four lanes
+      // transpose their 4 x 4 float4 blocks so that each store instruction writes 64 contiguous
+      // bytes of a row per lane group instead of 16 bytes a lane (peer stores travel as NVLink
+      // packets of what one instruction covers). Every lane takes part in the shuffles.
+      const int k = threadIdx.x & 3;
+      float4 t4[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        t4[j] = make_float4(peer_value(v[4 * j]), peer_value(v[4 * j + 1]), peer_value(v[4 * j + 2]),
+                            peer_value(v[4 * j + 3]));
+      // Butterfly transpose of the lanes' 4 x 4 float4 blocks: exchange across lane bit 0, then
+      // across lane bit 1 (selects on the lane bits only, so the blocks stay in registers).
+      auto xchg = [](float4 x, int m) {
+        return make_float4(__shfl_xor_sync(0xffffffffu, x.x, m), __shfl_xor_sync(0xffffffffu, x.y, m),
+                           __shfl_xor_sync(0xffffffffu, x.z, m), __shfl_xor_sync(0xffffffffu, x.w, m));
+      };
+      {
+        const bool odd = k & 1;
+        const float4 r0 = xchg(odd ? t4[0] : t4[1], 1);
+        const float4 r1 = xchg(odd ? t4[2] : t4[3], 1);
+        if (odd) {
+          t4[0] = r0;
+          t4[2] = r1;
+        } else {
+          t4[1] = r0;
+          t4[3] = r1;
+        }
+      }
+      {
+        const bool hi = k & 2;
+        const float4 r0 = xchg(hi ? t4[0] : t4[2], 2);
+        const float4 r1 = xchg(hi ? t4[1] : t4[3], 2);
+        if (hi) {
+          t4[0] = r0;
+          t4[1] = r1;
+        } else {
+          t4[2] = r0;
+          t4[3] = r1;
+        }
+      }
+      // t4[i]: columns col + 4k .. + 3 of row (row - k + i).
+      const int c = col + 4 * k;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int ri = row - k + i;
+        if (ri >= p.out_rows || c >= p.out_cols) continue;
+        int q0 = 0, q1 = p.peer.world, r = ri;
+        if (p.peer.owner_rows > 0) {
+          q0 = ri / p.peer.owner_rows;
+          q1 = q0 + 1;
+          r = ri - q0 * p.peer.owner_rows;
+        }
+        const float w[4] = {t4[i].x, t4[i].y, t4[i].z, t4[i].w};
+        for (int q = q0; q < q1; ++q) {
+          float* dst = peer_dst(p, poff, q, r) + c;
+          if (c + 4 <= p.out_cols) {
+            *reinterpret_cast<float4*>(dst) = t4[i];
+          } else {
+#pragma unroll
+            for (int t = 0; t < 4; ++t)
+              if (c + t < p.out_cols) dst[t] = w[t];
+          }
+        }
+      }
+    } else {
+      if (col >= p.out_cols) return;
+#pragma unroll
+      for (int t = 0; t < 16; ++t)
+        if (row + t < p.out_rows) peer_store_one(p, poff, row + t, col, v[t]);
+    }
+    return;
+  }
   if (kEpi == kEpiF32) {
     float* c = static_cast<float*>(p.c);
     if (along_row) {
@@ -253,14 +359,91 @@ __device__ __forceinline__ void store16(const KParams& p, int row, int col, cons
 enum : int { kRedNone = 0, kRedGlobal = 1, kRedCluster = 2 };
 
 template <int kEpi>
-__device__ __forceinline__ void store_one(const KParams& p, int row, int col, float v) {
+__device__ __forceinline__ void store_one(const KParams& p, int row, int col, float v, long poff = 0) {
   if (row >= p.out_rows || col >= p.out_cols) return;
+  if (kEpi == kEpiF32 && p.peer.world > 0) {
+    peer_store_one(p, poff, row, col, v);
+    return;
+  }
   if (kEpi == kEpiF32) {
     static_cast<float*>(p.c)[(long)row * p.ldc + col] = v;
     return;
   }
   if (p.res != nullptr) v += __bfloat162float(p.res[(long)row * p.ldr + col]);
   static_cast<__nv_bfloat16*>(p.c)[(long)row * p.ldc + col] = __float2bfloat16_rn(v);
+}
+
+// Stores 8 consecutive output values C[row, col .. col + 7] (col a multiple of 8), applying the
+// residual add and the output type of the epilogue; the cluster split-K reduction's store.
+template <int kEpi>
+__device__ __forceinline__ void store8(const KParams& p, int row, int col, const float (&v)[8], long poff) {
+  if (row >= p.out_rows || col >= p.out_cols) return;
+  const bool whole = col + 8 <= p.out_cols;
+  if (kEpi == kEpiF32 && p.peer.world > 0) {
+    if (!whole) {
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (col + t < p.out_cols) peer_store_one(p, poff, row, col + t, v[t]);
+      return;
+    }
+    const float4 lo = make_float4(peer_value(v[0]), peer_value(v[1]), peer_value(v[2]), peer_value(v[3]));
+    const float4 hi = make_float4(peer_value(v[4]), peer_value(v[5]), peer_value(v[6]), peer_value(v[7]));
+    int q0 = 0, q1 = p.peer.world, r = row;
+    if (p.peer.owner_rows > 0) {
+      q0 = row / p.peer.owner_rows;
+      q1 = q0 + 1;
+      r = row - q0 * p.peer.owner_rows;
+    }
+    for (int q = q0; q < q1; ++q) {
+      float4* dst = reinterpret_cast<float4*>(peer_dst(p, poff, q, r) + col);
+      dst[0] = lo;
+      dst[1] = hi;
+    }
+    return;
+  }
+  if (kEpi == kEpiF32) {
+    float* dst = static_cast<float*>(p.c) + (long)row * p.ldc + col;
+    if (whole) {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(v[0], v[1], v[2], v[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(v[4], v[5], v[6], v[7]);
+    } else {
+#pragma unroll
+      for (int t = 0; t < 8; ++t)
+        if (col + t < p.out_cols) dst[t] = v[t];
+    }
+    return;
+  }
+  float w[8];
+#pragma unroll
+  for (int t = 0; t < 8; ++t) w[t] = v[t];
+  __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.c) + (long)row * p.ldc + col;
+  if (whole) {
+    if (p.res != nullptr) {
+      const uint4 rv = *reinterpret_cast<const uint4*>(p.res + (long)row * p.ldr + col);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        w[2 * t] += bf16_lo(rw[t]);
+        w[2 * t + 1] += bf16_hi(rw[t]);
+      }
+    }
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pack_bf16x2(w[0], w[1]), pack_bf16x2(w[2], w[3]),
+                                                pack_bf16x2(w[4], w[5]), pack_bf16x2(w[6], w[7]));
+  } else {
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      if (col + t >= p.out_cols) continue;
+      float x = w[t];
+      if (p.res != nullptr) x += __bfloat162float(p.res[(long)row * p.ldr + col + t]);
+      dst[t] = __float2bfloat16_rn(x);
+    }
+  }
+}
+
+// Rows of the tile one CTA of a split-K cluster reduces: an equal share rounded up to 8, so each
+// thread of the reduction adds and stores 8 consecutive outputs at a time.
+__device__ __forceinline__ int slice_rows(int rows, int splits) {
+  return (((rows + splits - 1) / splits) + 7) & ~7;
 }
 
 // Tensor maps beyond the two operands: the raw quantized weights a converter reads, and the
@@ -644,6 +827,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int lrow = q * 32 + lane;
     pdl_wait();  // the residual and the output may be earlier kernels' memory
+    const long poff = kEpi == kEpiF32 ? peer_offset(p) : 0;
     uint32_t tc = 0;
     uint32_t kit = 0;  // W8A8: k-blocks consumed (stage and buffer sequence of the MMA warp)
     uint32_t xfer_count = 0;  // W8A8: hand-overs between the two scaling streams
@@ -847,9 +1031,9 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
             get16(mb, c0, v);
             const int j = tq * kBN + c0;
             if (!p.swap)
-              store16<kEpi>(p, i, j, v, true);
+              store16<kEpi>(p, i, j, v, true, poff);
             else
-              store16<kEpi>(p, j, i, v, false);
+              store16<kEpi>(p, j, i, v, false, poff);
           }
         }
       }
@@ -865,6 +1049,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     // 1. Every CTA of the cluster has drained its MMAs (its epilogue saw the accumulator
     //    complete), so every operand ring is idle and may receive partials.
     cluster_sync();
+    if (p.cta_trace != nullptr && threadIdx.x == 64) p.cta_trace[8 * blockIdx.x + 3] = global_ns();
     // 2. Push this split's partial into the shared memory of the CTA that reduces each row;
     //    DSMEM stores do not stall. Receive layout per CTA: [split][half][col][row of slice].
     if (warp >= 2 && warp < 6 && !*abort) {
@@ -883,12 +1068,12 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       for (int mb = 0; mb < kMB; ++mb) {
         int owner, rl, rs, half;
         if (kEpi == kEpiSwiGLU) {
-          rs = (128 + S - 1) / S;
+          rs = slice_rows(128, S);
           owner = lrow / rs;
           rl = lrow % rs;
           half = mb;
         } else {
-          rs = (C::kPRows + S - 1) / S;
+          rs = slice_rows(C::kPRows, S);
           const int r = mb * 128 + lrow;
           owner = r / rs;
           rl = r % rs;
@@ -910,8 +1095,10 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       }
       tc_fence_before();
     }
+    if (p.cta_trace != nullptr && threadIdx.x == 64) p.cta_trace[8 * blockIdx.x + 4] = global_ns();
     // 3. Every partial has landed; each CTA adds its slice in split order.
     cluster_sync();
+    if (p.cta_trace != nullptr && threadIdx.x == 64) p.cta_trace[8 * blockIdx.x + 5] = global_ns();
     if (warp >= 2 && warp < 6) {
       const int tid = threadIdx.x - 64;
       const int S = p.splits;
@@ -919,31 +1106,47 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       const int tile = blockIdx.x / S;
       const int tp = tile % p.tiles_p, tq = tile / p.tiles_p;
       const float* red = reinterpret_cast<const float*>(smem);
-      if (kEpi == kEpiSwiGLU) {
-        const int rs = (128 + S - 1) / S;
-        for (int e = tid; e < rs * kBN; e += 128) {
-          const int rl = e % rs, c = e / rs;
-          const int f = rank * rs + rl;
-          if (f >= 128) continue;
-          float g = 0.f, u = 0.f;
-          for (int s = 0; s < S; ++s) {
-            g += red[((s * 2 + 0) * kBN + c) * rs + rl];
-            u += red[((s * 2 + 1) * kBN + c) * rs + rl];
+      // Each thread adds 8 consecutive rows of the slice (output features) of one column (token)
+      // over the splits in split order; consecutive threads take consecutive groups of 8.
+      const int rows_here = kEpi == kEpiSwiGLU ? 128 : C::kPRows;
+      const int rs = slice_rows(rows_here, S);
+      const int r0 = rank * rs;
+      const int groups = max(0, min(rs, rows_here - r0)) / 8;
+      const long poff = kEpi == kEpiF32 ? peer_offset(p) : 0;
+      for (int e = tid; e < groups * kBN; e += 128) {
+        const int g = e % groups, c = e / groups;
+        if (kEpi == kEpiSwiGLU) {
+          float gs[8], us[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) gs[t] = us[t] = 0.f;
+          for (int sp = 0; sp < S; ++sp) {
+            const float4* gq = reinterpret_cast<const float4*>(red + ((sp * 2 + 0) * kBN + c) * rs + g * 8);
+            const float4* uq = reinterpret_cast<const float4*>(red + ((sp * 2 + 1) * kBN + c) * rs + g * 8);
+            const float4 g0 = gq[0], g1 = gq[1], u0 = uq[0], u1 = uq[1];
+            gs[0] += g0.x; gs[1] += g0.y; gs[2] += g0.z; gs[3] += g0.w;
+            gs[4] += g1.x; gs[5] += g1.y; gs[6] += g1.z; gs[7] += g1.w;
+            us[0] += u0.x; us[1] += u0.y; us[2] += u0.z; us[3] += u0.w;
+            us[4] += u1.x; us[5] += u1.y; us[6] += u1.z; us[7] += u1.w;
           }
-          store_one<kEpiBf16>(p, tq * kBN + c, tp * 128 + f, silu_bf16_times(g, u));
-        }
-      } else {
-        const int rs = (C::kPRows + S - 1) / S;
-        for (int e = tid; e < rs * kBN; e += 128) {
-          const int rl = e % rs, c = e / rs;
-          const int r = rank * rs + rl;
-          if (r >= C::kPRows) continue;
-          float v = 0.f;
-          for (int s = 0; s < S; ++s) v += red[(s * kBN + c) * rs + rl];
-          store_one<kEpi>(p, tq * kBN + c, tp * C::kPRows + r, v);
+          float o[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) o[t] = silu_bf16_times(gs[t], us[t]);
+          store8<kEpiBf16>(p, tq * kBN + c, tp * 128 + r0 + g * 8, o, 0);
+        } else {
+          float v[8];
+#pragma unroll
+          for (int t = 0; t < 8; ++t) v[t] = 0.f;
+          for (int sp = 0; sp < S; ++sp) {
+            const float4* q4 = reinterpret_cast<const float4*>(red + (sp * kBN + c) * rs + g * 8);
+            const float4 x0 = q4[0], x1 = q4[1];
+            v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
+            v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
+          }
+          store8<kEpi>(p, tq * kBN + c, tp * C::kPRows + r0 + g * 8, v, poff);
         }
       }
     }
+    if (p.cta_trace != nullptr && threadIdx.x == 64) p.cta_trace[8 * blockIdx.x + 6] = global_ns();
   } else {
     __syncthreads();
   }
@@ -951,6 +1154,10 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     tc_fence_after();
     tmem_dealloc(tmem_base, C::kTmemCols);
     if (lane == 0) mark(p, 7);
+  }
+  if (p.cta_trace != nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0) p.cta_trace[8 * blockIdx.x + 7] = global_ns();
   }
 }
 
@@ -1052,7 +1259,7 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   }
   splits = std::max(1, std::min(splits, pl.kblocks));
   const size_t red_bytes = (size_t)128 * pl.mb * pl.kbn * sizeof(float);
-  const size_t recv_bytes = (size_t)(128 * pl.mb + 2 * splits) * pl.kbn * sizeof(float);
+  const size_t recv_bytes = (size_t)(128 * pl.mb + 8 * 2 * splits) * pl.kbn * sizeof(float);
   const bool cluster_fits =
       pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn, a.w_format);
   pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
@@ -1324,7 +1531,18 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15)) return -1;
   if (a.epilogue == kEpiSwiGLU && (a.N % 256 != 0 || a.residual != nullptr)) return -2;
   if (a.epilogue != kEpiF32 && (a.ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
-  if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
+  const GemmPeerOut& po = a.peer;
+  if (po.world > 0) {
+    // Peer stores replace `c`: every destination, stride and buffer offset 16-byte aligned.
+    if (a.epilogue != kEpiF32 || po.world > 8 || po.rank < 0 || po.rank >= po.world ||
+        po.seq == nullptr || po.owner_rows < 0 || a.ldc % 4 != 0 || po.slot_stride % 4 != 0 ||
+        po.buf_stride % 4 != 0)
+      return -2;
+    for (int q = 0; q < po.world; ++q)
+      if (po.dst[q] == nullptr || (reinterpret_cast<uintptr_t>(po.dst[q]) & 15)) return -1;
+  } else if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) {
+    return -1;
+  }
   if (a.residual != nullptr && a.epilogue != kEpiBf16) return -2;
   if (a.w_format != kWBf16 && a.w_scale == nullptr) return -2;
   if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
@@ -1381,6 +1599,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.counters = a.counters;
   kp.status = a.status;
   kp.trace = a.trace;
+  kp.cta_trace = a.cta_trace;
   static const int debug = std::getenv("FOA_GEMM_DEBUG") ? std::atoi(std::getenv("FOA_GEMM_DEBUG")) : 0;
   kp.debug = debug;
   kp.out_rows = a.M;
@@ -1399,6 +1618,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     kp.tile_group = a.tile_group;
     kp.group_rows = a.N;
   }
+  kp.peer = a.peer;
   kp.acc_scale = (a.w_format == kWNvfp4 || nvf4) ? a.w_tensor_scale : 1.0f;
   if (nvf4) {
     const long atoms = (long)(a.K / 64) * 512;  // bytes of one 128-row block of scale atoms

@@ -6,8 +6,6 @@
 // file failure to OSError.
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
-
-#include "kernels/gemm.cuh"
 #include <pybind11/stl.h>
 
 #include <cstring>
@@ -17,6 +15,7 @@
 #include "engine/model.h"
 #include "engine/registry.h"
 #include "engine/runtime.h"
+#include "kernels/gemm.cuh"
 #include "python/pytypes.h"
 
 namespace py = pybind11;
@@ -720,37 +719,133 @@ void bind_engine(py::module_& m) {
     d.model->set_collectives(coll);
     return py::bytes(coll->handle());
   });
-  // Device time of the fused tensor-parallel add+norm on `rows` rows (every rank calls it in
-  // lockstep): milliseconds per call over `iters` calls on the decoder's stream.
-  m.def("_tp_bench_add_norm", [](PyDecoder& d, int rows, int iters) {
+  // Device time of layer 0's attention output projection on `rows` rows of `a` (BF16
+  // [rows, q_heads_local * head_dim], a device address), in milliseconds per call over `iters`
+  // calls on the decoder's stream (every rank calls it in lockstep):
+  //   "fused": the GEMM pushing its FP32 partials to the reducing ranks over NVLink, then the
+  //            tensor-parallel add+norm that sums them (the decoder's path);
+  //   "local": the same GEMM writing its FP32 output to this rank's memory only.
+  m.def("_tp_bench_o_proj", [](PyDecoder& d, int rows, uintptr_t a, int iters) {
     auto coll = d.model->collectives();
     if (!coll) throw ValueError("the decoder has no tensor-parallel heap");
     const auto& cfg = d.model->config();
+    const WeightSlot& wo = d.model->weights().at("layers.0.o");
+    if (wo.format != foa::kWeightBf16 || wo.shape.size() != 2) throw Unsupported("the benchmark takes BF16 weights");
+    const int H = cfg.hidden, K = static_cast<int>(wo.shape[1]);
     auto st = d.model->device().state();
     py::gil_scoped_release nogil;
     st->activate();
     cudaStream_t s = st->stream;
-    const auto* w = d.model->weights().at("final_norm").ptr;
-    auto once = [&]() {
-      float* partial = coll->partial_buffer(static_cast<size_t>(rows) * cfg.hidden);
-      coll->add_norm(partial, coll->residual_buffer(), w, cfg.eps, coll->hidden_buffer(), rows, cfg.hidden, s);
+    HbmBuffer out(d.model->device(), static_cast<size_t>(rows) * H * 4);
+    HbmBuffer ws(d.model->device(), size_t{64} << 20);
+    HbmBuffer counters(d.model->device(), 32768 * 4);
+    unsigned long long* trace_gemm_ = nullptr;
+    st->check_cuda(cudaMemsetAsync(counters.data(), 0, 32768 * 4, s), "counters");
+    auto gemm = [&](const foa::GemmPeerOut* peer) {
+      foa::GemmArgs g;
+      g.a = reinterpret_cast<const void*>(a);
+      g.lda = K;
+      g.w = wo.ptr;
+      g.ldw = K;
+      g.M = rows;
+      g.N = H;
+      g.K = K;
+      g.c = peer ? nullptr : out.data();
+      g.ldc = H;
+      g.epilogue = foa::kEpiF32;
+      g.workspace = static_cast<float*>(ws.data());
+      g.workspace_bytes = ws.size();
+      g.counters = static_cast<int*>(counters.data());
+      g.counters_len = 32768;
+      g.status = st->status;
+      if (peer) g.peer = *peer;
+      g.trace = trace_gemm_;
+      if (foa::gemm_bf16(g, s) != 0) st->fail("benchmark gemm launch failed");
     };
-    coll->begin_call(s);
-    for (int i = 0; i < 3; ++i) once();
-    cudaEvent_t a, b;
-    cudaEventCreate(&a);
-    cudaEventCreate(&b);
-    coll->begin_call(s);
-    cudaEventRecord(a, s);
-    for (int i = 0; i < iters; ++i) once();
-    cudaEventRecord(b, s);
-    cudaEventSynchronize(b);
-    float ms = 0.f;
-    cudaEventElapsedTime(&ms, a, b);
-    cudaEventDestroy(a);
-    cudaEventDestroy(b);
-    st->check_status();
-    return static_cast<double>(ms) / iters;
+    auto fused = [&]() {
+      const foa::GemmPeerOut t = coll->reduce_target(rows, H);
+      gemm(&t);
+      coll->add_norm(coll->residual_buffer(), d.model->weights().at("final_norm").ptr, cfg.eps,
+                     coll->hidden_buffer(), rows, H, s);
+    };
+    auto timed = [&](const std::function<void()>& fn) {
+      coll->begin_call(s);
+      for (int i = 0; i < 3; ++i) fn();
+      cudaEvent_t e0, e1;
+      cudaEventCreate(&e0);
+      cudaEventCreate(&e1);
+      coll->begin_call(s);
+      cudaEventRecord(e0, s);
+      for (int i = 0; i < iters; ++i) fn();
+      cudaEventRecord(e1, s);
+      cudaEventSynchronize(e1);
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, e0, e1);
+      cudaEventDestroy(e0);
+      cudaEventDestroy(e1);
+      st->check_status();
+      return static_cast<double>(ms) / iters;
+    };
+    std::map<std::string, double> r;
+    r["fused"] = timed(fused);
+    r["local"] = timed([&]() { gemm(nullptr); });
+    {
+      // The fused pair again with an event between the two kernels: the GEMM's share (with its
+      // peer stores) and the reducer's share (waits for peers included).
+      std::vector<cudaEvent_t> ev(3 * iters);
+      for (auto& e : ev) cudaEventCreate(&e);
+      coll->begin_call(s);
+      for (int i = 0; i < iters; ++i) {
+        const foa::GemmPeerOut t = coll->reduce_target(rows, H);
+        cudaEventRecord(ev[3 * i], s);
+        gemm(&t);
+        cudaEventRecord(ev[3 * i + 1], s);
+        coll->add_norm(coll->residual_buffer(), d.model->weights().at("final_norm").ptr, cfg.eps,
+                       coll->hidden_buffer(), rows, H, s);
+        cudaEventRecord(ev[3 * i + 2], s);
+      }
+      cudaEventSynchronize(ev.back());
+      double g = 0, n = 0;
+      for (int i = 0; i < iters; ++i) {
+        float a0 = 0.f, a1 = 0.f;
+        cudaEventElapsedTime(&a0, ev[3 * i], ev[3 * i + 1]);
+        cudaEventElapsedTime(&a1, ev[3 * i + 1], ev[3 * i + 2]);
+        g += a0;
+        n += a1;
+      }
+      for (auto& e : ev) cudaEventDestroy(e);
+      st->check_status();
+      r["split_gemm"] = g / iters;
+      r["split_norm"] = n / iters;
+    }
+    {
+      // Milestones of one launch (global timer, relative to the GEMM's entry, microseconds): the
+      // local GEMM, then the fused pair (GEMM marks 0-7, then the reducer's entry, landed, exit).
+      auto* pc = dynamic_cast<PeerCollectives*>(coll.get());
+      HbmBuffer tr(d.model->device(), 16 * 8);
+      std::vector<unsigned long long> h(16);
+      auto read = [&](const char* key, int n) {
+        st->check_cuda(cudaMemcpyAsync(h.data(), tr.data(), 16 * 8, cudaMemcpyDeviceToHost, s), "trace");
+        st->check_cuda(cudaStreamSynchronize(s), "trace");
+        for (int i = 0; i < n; ++i)
+          r[std::string(key) + std::to_string(i)] = h[i] ? (static_cast<double>(h[i]) - static_cast<double>(h[0])) / 1000.0 : -1.0;
+      };
+      coll->begin_call(s);
+      st->check_cuda(cudaMemsetAsync(tr.data(), 0, 16 * 8, s), "trace");
+      trace_gemm_ = static_cast<unsigned long long*>(tr.data());
+      gemm(nullptr);
+      trace_gemm_ = nullptr;
+      read("trace_local_", 8);
+      st->check_cuda(cudaMemsetAsync(tr.data(), 0, 16 * 8, s), "trace");
+      if (pc) pc->set_trace(static_cast<unsigned long long*>(tr.data()) + 8);
+      trace_gemm_ = static_cast<unsigned long long*>(tr.data());
+      fused();
+      trace_gemm_ = nullptr;
+      if (pc) pc->set_trace(nullptr);
+      read("trace_fused_", 11);
+    }
+    r["two_shot"] = coll->reduce_target(rows, H).owner_rows > 0 ? 1.0 : 0.0;
+    return r;
   });
   m.def("_tp_connect", [](PyDecoder& d, const std::vector<py::bytes>& handles) {
     std::vector<std::string> hs;

@@ -160,6 +160,7 @@ def gemm(
     splits: int = 0,
     trace: torch.Tensor | None = None,
     segments: list | None = None,
+    cta_trace: torch.Tensor | None = None,
 ) -> torch.Tensor:
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
@@ -170,6 +171,7 @@ def gemm(
     ``nvfp4`` dequantize the weights to BF16 tile by tile inside the kernel (W8A16, W4A16).
     ``segments`` [(a1 [M, k1], w1 [N, k1]), ...] (at most two, k a multiple of 64) add
     ``a1 @ w1.T`` and so on into the same FP32 sums before the epilogue (LoRA updates).
+    ``trace`` (int64 [8]) and ``cta_trace`` (int64 [4 x CTAs]) receive global-timer milestones.
     """
     _rowmajor(a, "a")
     M, K = a.shape
@@ -220,6 +222,7 @@ def gemm(
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
         0 if trace is None else trace.data_ptr(), **qargs,
         segments=[(sa.data_ptr(), sa.stride(0), sw.data_ptr(), sw.stride(0), sa.shape[1]) for sa, sw in (segments or [])],
+        cta_trace=0 if cta_trace is None else cta_trace.data_ptr(),
     )
     return out
 

@@ -5,7 +5,7 @@ sequence: `--warmup` launches, then `--iters` timed ones, each after an L2 flush
     python -m furiosa_opt_models_b200.utils.kernel_bench decode-attn --rows 64 --keys 2048
     python -m furiosa_opt_models_b200.utils.kernel_bench prefill-attn --rows 8192 --seqs 8
     python -m furiosa_opt_models_b200.utils.kernel_bench moe --tokens 64
-    torchrun --nproc-per-node 2 -m furiosa_opt_models_b200.utils.kernel_bench add-norm --rows 64
+    torchrun --nproc-per-node 2 -m furiosa_opt_models_b200.utils.kernel_bench tp-o-proj --rows 64
 
 Prints one JSON line: the mean device time per launch and the algorithmic bytes and FLOPs.
 """
@@ -36,25 +36,81 @@ def _time(fn, warmup: int, iters: int) -> float:
 
 
 def gemm(args) -> dict:
+    """One GEMM shape. `--rotate R`: R distinct weight copies (together larger than L2) launched
+    back to back without a flush, as a decoder's consecutive projections run; the per-launch time is
+    the loop's. `--cta-trace`: per-CTA global-timer milestones of one launch in that loop."""
     from furiosa_opt_models_b200 import ops
 
     M, N, K = args.M, args.N, args.K
     a = torch.randn(M, K, device="cuda").bfloat16()
-    w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
     fmt = args.format
-    if fmt == "fp8":
-        w = ops.quantize_fp8_block(w)
-        wbytes = N * K * (1 + 1 / 4096)
-    elif fmt == "nvfp4a4":
-        w = ops.nvfp4_w4a4(ops.quantize_nvfp4(w), float(a.float().abs().max()) / 2688)
-        wbytes = N * K * (0.5 + 1 / 16)
-    else:
-        wbytes = N * K * 2
+    copies = max(1, args.rotate)
+    ws = []
+    for _ in range(copies):
+        w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
+        if fmt == "fp8":
+            w = ops.quantize_fp8_block(w)
+        elif fmt == "nvfp4a4":
+            w = ops.nvfp4_w4a4(ops.quantize_nvfp4(w), float(a.float().abs().max()) / 2688)
+        ws.append(w)
+    wbytes = N * K * ({"fp8": 1 + 1 / 4096, "nvfp4a4": 0.5 + 1 / 16}.get(fmt, 2))
     epi = {"bf16": ops.EPI_BF16, "f32": ops.EPI_F32, "swiglu": ops.EPI_SWIGLU}[args.epilogue]
-    us = _time(lambda: ops.gemm(a, w, epilogue=epi), args.warmup, args.iters)
+    out = {}
+    if copies == 1:
+        us = _time(lambda: ops.gemm(a, ws[0], epilogue=epi, splits=args.splits), args.warmup, args.iters)
+    else:
+        # Two traced launches in the middle of the loop: launch `mid` and the one after it.
+        tr = torch.zeros(2, 8 * 1024, dtype=torch.int64, device="cuda")
+        mid = copies // 2
+
+        def loop(trace=False):
+            for i, w in enumerate(ws):
+                if args.impl == "cublas":
+                    torch.matmul(a, w.t())  # the library reference point (BF16 only)
+                    continue
+                t = tr[i - mid] if trace and i in (mid, mid + 1) else None
+                ops.gemm(a, w, epilogue=epi, splits=args.splits, cta_trace=t)
+
+        for _ in range(args.warmup):
+            loop()
+        torch.cuda.synchronize()
+        run = loop
+        if args.graph:
+            # Captured once and replayed, as a decoder's calls run: no host work between launches.
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                loop()
+                torch.cuda.synchronize()
+                with torch.cuda.graph(g, stream=s):
+                    loop(trace=args.cta_trace)
+            torch.cuda.current_stream().wait_stream(s)
+            run = g.replay
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.iters):
+            run()
+        e1.record()
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) * 1000.0 / (args.iters * copies)
+        if args.cta_trace and args.impl != "cublas":
+            if not args.graph:
+                loop(trace=True)
+                torch.cuda.synchronize()
+            both = tr.view(2, -1, 8).cpu().double()
+            t0 = both[0][both[0][:, 0] > 0][:, 0].min()
+            for j, name in ((0, "cta_us"), (1, "next_cta_us")):
+                t = both[j][both[j][:, 0] > 0]
+                rel = (t - t0) / 1000.0
+                q = lambda col: [round(float(x), 2) for x in torch.quantile(rel[:, col], torch.tensor([0.0, 0.5, 1.0], dtype=torch.float64))]
+                names = ["entry", "accumulator", "epilogue", "cluster_sync1", "pushed", "cluster_sync2", "reduced", "exit"]
+                out[name] = {"ctas": int(t.shape[0])}
+                out[name].update({n: q(c) for c, n in enumerate(names) if (t[:, c] > 0).all()})
     flops = 2 * M * N * K
-    return dict(kernel="gemm", format=fmt, M=M, N=N, K=K, us=round(us, 2), tflops=round(flops / us / 1e6, 1),
-                weight_gbs=round(wbytes / us / 1e3, 1))
+    out.update(kernel="gemm", format=fmt, M=M, N=N, K=K, rotate=copies, us=round(us, 2),
+               tflops=round(flops / us / 1e6, 1), weight_gbs=round(wbytes / us / 1e3, 1))
+    return out
 
 
 def decode_attn(args) -> dict:
@@ -113,9 +169,10 @@ def moe(args) -> dict:
     return dict(kernel="moe_block", tokens=T, tile=tile, us=round(us, 2), expert_weight_gbs=round(wbytes / us / 1e3, 1))
 
 
-def add_norm(args) -> dict:
-    """The fused tensor-parallel add+norm (rank-ordered FP32 sum over NVLink + residual +
-    RMSNorm), device-timed on every rank, the maximum reported."""
+def tp_o_proj(args) -> dict:
+    """Layer 0's attention output projection under tensor parallelism, device-timed on every rank
+    (the maximum reported): the GEMM pushing FP32 partials over NVLink fused with the rank-ordered
+    all-reduce + residual + RMSNorm ("fused"), and the same GEMM writing locally ("local")."""
     import datetime
     import os
 
@@ -130,24 +187,51 @@ def add_norm(args) -> dict:
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
-    cfg = configs.get(args.model)
+    # Layer 0 alone, BF16 weights: the projection's geometry is the model's.
+    cfg = configs.get(args.model, layers=1, weight_format="bf16")
     device = engine.Device(engine.Placement(list(range(world)), range(8)))
     model = _native._synthetic_decoder(device, cfg, tp=world, rank=rank, seed=0, std=0.02)
     tp.attach(model, device)
-    ms = _native._tp_bench_add_norm(model, args.rows, args.iters)
-    t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    H, D = cfg["hidden"], cfg.get("head_dim", 128)
+    K = cfg["q_heads"] // world * D
+    a = torch.randn(args.rows, K, device="cuda").bfloat16()
+    r = _native._tp_bench_o_proj(model, args.rows, a.data_ptr(), args.iters)
+    t = torch.tensor([r["fused"], r["local"], r["split_gemm"], r["split_norm"]], dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    us = t.item() * 1000.0
-    H = cfg["hidden"]
-    one_shot = args.rows * H * 4 * (world - 1) <= (1 << 20) or args.rows < world
-    nvlink = (args.rows * H * 4 * (world - 1) if one_shot
-              else args.rows * H * 4 * (world - 1) / world + 2 * args.rows * H * 2 * (world - 1) / world)
+    fused_us, local_us = t[0].item() * 1000.0, t[1].item() * 1000.0
+    split = {"gemm_us": round(t[2].item() * 1000.0, 2), "reduce_norm_us": round(t[3].item() * 1000.0, 2)}
     tp.detach(model)
     dist.destroy_process_group()
-    return dict(kernel="tp_add_norm", world=world, rows=args.rows, hidden=H, mode="one-shot" if one_shot else "two-shot",
-                us=round(us, 2), nvlink_bytes_per_rank=int(nvlink),
-                nvlink_gbs=round(nvlink / us / 1e3, 1), roofline_fraction_of_770=round(nvlink / us / 1e3 / 770, 3),
-                _rank=rank)
+    one_shot = r["two_shot"] == 0
+    # Bytes each rank must move across NVLink: FP32 partials out (every row to every peer, or each
+    # row to its owner), plus (two-shot) the BF16 residual and normed rows of its slice to every peer.
+    nvlink = (args.rows * H * 4 * (world - 1) if one_shot
+              else args.rows * H * 4 * (world - 1) / world + 2 * args.rows * H * 2 * (world - 1) / world)
+    peaks = _peaks()
+    roof = {"nvlink_us": nvlink / 770e3,
+            "weights_us": H * K * 2 / (peaks["hbm_gbs"] * 1e3),
+            "compute_us": 2 * args.rows * H * K / (peaks["bf16_tflops"] * 1e6)}
+    bound = max(roof.values())
+    return dict(kernel="tp_o_proj_add_norm", world=world, rows=args.rows, hidden=H, K=K,
+                mode="one-shot" if one_shot else "two-shot", fused_us=round(fused_us, 2),
+                local_gemm_us=round(local_us, 2), collective_us=round(fused_us - local_us, 2),
+                events_between_kernels=split,
+                trace_local_us=[round(r[f"trace_local_{i}"], 2) for i in range(8)],
+                trace_fused_us=[round(r[f"trace_fused_{i}"], 2) for i in range(11)],
+                nvlink_bytes_per_rank=int(nvlink), roofline_us={k: round(v, 2) for k, v in roof.items()},
+                roofline_fraction=round(bound / fused_us, 3), _rank=rank)
+
+
+def _peaks() -> dict:
+    import os
+
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"])}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 
 
 def main() -> None:
@@ -159,6 +243,11 @@ def main() -> None:
     g.add_argument("--K", type=int, default=4096)
     g.add_argument("--format", default="bf16", choices=["bf16", "fp8", "nvfp4a4"])
     g.add_argument("--epilogue", default="bf16", choices=["bf16", "f32", "swiglu"])
+    g.add_argument("--splits", type=int, default=0)
+    g.add_argument("--rotate", type=int, default=1)
+    g.add_argument("--cta-trace", action="store_true")
+    g.add_argument("--graph", action="store_true")
+    g.add_argument("--impl", default="engine", choices=["engine", "cublas"])
     d = sub.add_parser("decode-attn")
     d.add_argument("--rows", type=int, default=64)
     d.add_argument("--keys", type=int, default=2048)
@@ -171,7 +260,7 @@ def main() -> None:
     f.add_argument("--kv-heads", type=int, default=8)
     m = sub.add_parser("moe")
     m.add_argument("--tokens", type=int, default=64)
-    a = sub.add_parser("add-norm")
+    a = sub.add_parser("tp-o-proj")
     a.add_argument("--rows", type=int, default=64)
     a.add_argument("--model", default="qwen3-1.7b")
     for s in (g, d, f, m, a):
@@ -179,7 +268,7 @@ def main() -> None:
         s.add_argument("--iters", type=int, default=10)
     args = p.parse_args()
     out = {"gemm": gemm, "decode-attn": decode_attn, "prefill-attn": prefill_attn, "moe": moe,
-           "add-norm": add_norm}[args.what](args)
+           "tp-o-proj": tp_o_proj}[args.what](args)
     if out.pop("_rank", 0) == 0:
         print(json.dumps(out), flush=True)
 

@@ -16,8 +16,8 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 WORKER = os.path.join(ROOT, "tests", "workers", "tp_parity.py")
 
 
-def _run(world: int, out: str, model: str, steps: int) -> list:
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+def _run(world: int, out: str, model: str, steps: int, **extra_env) -> list:
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1", **extra_env)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29533", WORKER, out,
            model, str(steps)]
@@ -28,11 +28,15 @@ def _run(world: int, out: str, model: str, steps: int) -> list:
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 @pytest.mark.parametrize("world", [2, 4, 8])
-def test_tp_matches_single_gpu(world, tmp_path):
+@pytest.mark.parametrize("mode", ["one-shot", "two-shot"])
+def test_tp_matches_single_gpu(world, mode, tmp_path):
+    """`two-shot` forces every all-reduce through the reduce-scatter path (each GEMM pushes a row
+    only to the rank that owns its slice; owners store the normed rows into every rank)."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     one = _run(1, str(tmp_path / "tp1.json"), "tiny-qwen3-tp", 12)
-    many = _run(world, str(tmp_path / f"tp{world}.json"), "tiny-qwen3-tp", 12)
+    env = {"FOA_TP_ONESHOT_BYTES": "0"} if mode == "two-shot" else {}
+    many = _run(world, str(tmp_path / f"tp{world}.json"), "tiny-qwen3-tp", 12, **env)
     # Greedy tokens agree (the FP32 partial sums are added in another grouping, so a near-tie may
     # flip a token late in a sequence; the first tokens must match exactly).
     assert [t[:4] for t in one] == [t[:4] for t in many]
