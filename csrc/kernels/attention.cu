@@ -21,6 +21,7 @@
 //   kernel is bound by its MMAs.
 
 #include <cfloat>
+#include <cstdlib>
 
 #include "attention.cuh"
 #include "launch.cuh"
@@ -197,10 +198,20 @@ __device__ __forceinline__ void load_q(uint32_t (&qa)[D / 16][4], RowPtr row_ptr
 }
 
 // ------------------------------------------------------------------------------------ decode
-// One CTA per (segment, key/value head, 2048-key split); four warps take the split's 16-key blocks
-// in turn, each double-buffering its blocks with cp.async.
-template <int D>
-__global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention p, int max_splits) {
+// One CTA per (segment, key/value head, 2048-key split); kWarps warps take the split's 16-key
+// blocks in turn, each keeping kStages blocks in a cp.async ring. Small CTAs (2 warps, 32 KiB)
+// let 6 of them share an SM, so a decode batch's CTAs fit the GPU in one wave.
+// CTAs of a decode configuration an SM holds: by shared memory, and at most 12 warps (the
+// registers of 168 a thread).
+constexpr int decode_ctas_per_sm(int d, int warps, int stages) {
+  const int by_smem = (220 * 1024) / (warps * stages * 2 * 16 * d * 2);
+  const int by_regs = 12 / warps;
+  return by_smem < by_regs ? by_smem : by_regs;
+}
+
+template <int D, int kWarps, int kStages>
+__global__ void __launch_bounds__(32 * kWarps, decode_ctas_per_sm(D, kWarps, kStages))
+    paged_decode_kernel(const PagedAttention p, int max_splits) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
@@ -225,7 +236,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
   Flash<D> f;
   f.init();
   constexpr int kTile = 16 * D * 2;  // bytes of one 16-key K (or V) block
-  const uint32_t wbase = smem_u32(smem) + warp * 4 * kTile;  // [stage][K, V]
+  const uint32_t wbase = smem_u32(smem) + warp * kStages * 2 * kTile;  // [stage][K, V]
   const long page = 2L * p.kv_heads * 16 * D;
   const int b_first = k0 / 16, b_last = (k1 - 1) / 16;
 
@@ -244,15 +255,23 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
     cp_async_commit();
   };
 
+  // kStages - 1 blocks in flight ahead of the one being folded (empty groups past the end keep
+  // the group count uniform).
   int b = b_first + warp;
-  if (b <= b_last) issue(b, 0);
-  for (int stage = 0; b <= b_last; b += 4, stage ^= 1) {
-    if (b + 4 <= b_last) {
-      issue(b + 4, stage ^ 1);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
+#pragma unroll
+  for (int i = 0; i < kStages - 1; ++i) {
+    if (b + i * kWarps <= b_last)
+      issue(b + i * kWarps, i);
+    else
+      cp_async_commit();
+  }
+  for (int stage = 0; b <= b_last; b += kWarps, stage = stage + 1 == kStages ? 0 : stage + 1) {
+    const int ahead = b + (kStages - 1) * kWarps;
+    if (ahead <= b_last)
+      issue(ahead, stage == 0 ? kStages - 1 : stage - 1);
+    else
+      cp_async_commit();
+    cp_async_wait<kStages - 1>();
     __syncwarp();
     const uint32_t kt = wbase + stage * 2 * kTile, vt = kt + kTile;
     float s[2][4];
@@ -269,13 +288,13 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
     __syncwarp();
   }
 
-  // Merge the four warps: row statistics, then the rescaled outputs, through shared memory.
+  // Merge the warps: row statistics, then the rescaled outputs, through shared memory.
   f.l[0] = warp_sum4(f.l[0]);
   f.l[1] = warp_sum4(f.l[1]);
   __syncthreads();  // every warp is done with its K/V buffers
-  float* sm_m = reinterpret_cast<float*>(smem);  // [4][16]
-  float* sm_l = sm_m + 64;                       // [4][16]
-  float* sm_o = sm_l + 64;                       // [16][D]
+  float* sm_m = reinterpret_cast<float*>(smem);  // [kWarps][16]
+  float* sm_l = sm_m + 16 * kWarps;              // [kWarps][16]
+  float* sm_o = sm_l + 16 * kWarps;              // [16][D]
   const int g = lane >> 2, t = lane & 3;
   if (t == 0) {
     sm_m[warp * 16 + g] = f.m[0];
@@ -283,16 +302,16 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
     sm_l[warp * 16 + g] = f.l[0];
     sm_l[warp * 16 + g + 8] = f.l[1];
   }
-  for (int i = threadIdx.x; i < 16 * D; i += 128) sm_o[i] = 0.f;
+  for (int i = threadIdx.x; i < 16 * D; i += 32 * kWarps) sm_o[i] = 0.f;
   __syncthreads();
   float M[2], L[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int r = g + 8 * h;
     float mm = -INFINITY;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm_m[w * 16 + r]);
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, sm_m[w * 16 + r]);
     float ll = 0.f;
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kWarps; ++w) {
       const float mw = sm_m[w * 16 + r];
       ll += mw == -INFINITY ? 0.f : sm_l[w * 16 + r] * exp2f(mw - mm);
     }
@@ -301,7 +320,7 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
   }
   const float w0 = f.m[0] == -INFINITY ? 0.f : exp2f(f.m[0] - M[0]);
   const float w1 = f.m[1] == -INFINITY ? 0.f : exp2f(f.m[1] - M[1]);
-  for (int w = 0; w < 4; ++w) {
+  for (int w = 0; w < kWarps; ++w) {
     if (warp == w) {
 #pragma unroll
       for (int j = 0; j < D / 8; ++j) {
@@ -315,11 +334,11 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const PagedAttention 
     __syncthreads();
   }
   // Rows 0..G-1 hold the group's heads.
-  for (int i = threadIdx.x; i < G * D; i += 128) {
+  for (int i = threadIdx.x; i < G * D; i += 32 * kWarps) {
     const int r = i / D, c = i % D;
     float mm = -INFINITY, ll = 0.f;
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, sm_m[w * 16 + r]);
-    for (int w = 0; w < 4; ++w) {
+    for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, sm_m[w * 16 + r]);
+    for (int w = 0; w < kWarps; ++w) {
       const float mw = sm_m[w * 16 + r];
       ll += mw == -INFINITY ? 0.f : sm_l[w * 16 + r] * exp2f(mw - mm);
     }
@@ -465,6 +484,10 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention
   }
 }
 
+// Warps of a decode CTA and blocks each keeps in its cp.async ring (see paged_decode_kernel).
+constexpr int kDecodeWarps = 2;
+constexpr int kDecodeStages = 2;
+
 template <int D>
 int decode_launch(const PagedAttention& p, cudaStream_t stream) {
   const int max_splits = (p.max_keys + p.keys_per_split - 1) / p.keys_per_split;
@@ -472,16 +495,32 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
     const size_t need = (size_t)p.num_segments * p.q_heads * max_splits;
     if (p.partial_o == nullptr || p.partial_lse == nullptr || need > p.partial_capacity) return -3;
   }
-  const int smem = 4 * 4 * 16 * D * 2;
+  static const int warps = [] {
+    const char* v = std::getenv("FOA_DECODE_WARPS");  // measurement override: 2, 3 or 4
+    const int w = v ? std::atoi(v) : kDecodeWarps;
+    return w >= 2 && w <= 4 ? w : kDecodeWarps;
+  }();
+  static const int stages = [] {
+    const char* v = std::getenv("FOA_DECODE_STAGES");  // measurement override: 2 or 3
+    const int n = v ? std::atoi(v) : kDecodeStages;
+    return n == 2 || n == 3 ? n : kDecodeStages;
+  }();
+  const int smem = warps * stages * 2 * 16 * D * 2;
+  auto kernel = stages == 2 ? (warps == 2 ? paged_decode_kernel<D, 2, 2>
+                               : warps == 3 ? paged_decode_kernel<D, 3, 2>
+                                            : paged_decode_kernel<D, 4, 2>)
+                            : (warps == 2 ? paged_decode_kernel<D, 2, 3>
+                               : warps == 3 ? paged_decode_kernel<D, 3, 3>
+                                            : paged_decode_kernel<D, 4, 3>);
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
-    cudaFuncSetAttribute(paged_decode_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured[dev & 63] = true;
   }
-  dim3 grid(p.num_segments * p.kv_heads, max_splits);
-  launch_pdl(paged_decode_kernel<D>, dim3(grid), dim3(128), smem, stream, p, max_splits);
+  dim3 grid(p.num_segments * p.kv_heads, max_splits);  // one kernel per process: the env is fixed
+  launch_pdl(kernel, dim3(grid), dim3(32 * warps), smem, stream, p, max_splits);
   if (max_splits > 1)
     launch_pdl(decode_merge_kernel<D>, dim3(p.num_segments, p.q_heads), dim3(D), 0, stream, p, max_splits);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
