@@ -89,9 +89,12 @@ __device__ __forceinline__ bool unwritten(const float4& v) {
 // One CTA of 256 threads per row; each thread holds kVec vectors of 8 columns. The partials were
 // pushed here by the GEMMs of every rank; each thread polls its 8 values of every source slot,
 // adds them in rank order and marks the slot unwritten again.
+// It follows the GEMM that pushes the partials. That GEMM lets this kernel launch only after the
+// kernels before it completed (so the previous reducer's sequence advance and every earlier read of
+// the residual and normed rows are done); the partials themselves are polled for, so this kernel
+// does not wait for the GEMM to finish.
 template <int kVec>
 __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
-  pdl_wait();
   pdl_trigger();
   __shared__ float red[8];
   const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
@@ -121,6 +124,7 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
           x0 = ld_volatile_f4(src);
           x1 = ld_volatile_f4(src + 4);
           if (!(unwritten(x0) || unwritten(x1)) || late) break;
+          __nanosleep(100);  // polled while the pushing GEMM runs: leave it the issue slots
           if ((++spins & 63u) == 0 && global_ns() - start > kWaitLimitNs) {
             record_status(a.status, kTimeoutPeer);
             late = true;

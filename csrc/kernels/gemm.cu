@@ -479,7 +479,10 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  pdl_trigger();
+  // A GEMM with a tensor-parallel reduction target lets its reducer launch only once the kernels
+  // before it have completed (the trigger follows the producer's grid-dependency wait): the
+  // reducer then skips its own wait and polls for the partials while this GEMM still runs.
+  if (p.peer.world == 0) pdl_trigger();
   if (threadIdx.x == 0) mark(p, 0);
   // A grouped launch learns its token tiles from the routing kernel before it.
   int units = p.units;
@@ -625,10 +628,12 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           load_w(i, kb0 + i, tp, tq);
         }
         pdl_wait();
+        if (p.peer.world > 0) pdl_trigger();
         mark(p, 2);
         for (int i = 0; i < pre; ++i) load_a(i, kb0 + i, tp, tq);
       } else {
         pdl_wait();
+        if (p.peer.world > 0) pdl_trigger();
       }
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int tile = u / p.splits, split = u % p.splits;
@@ -1259,7 +1264,9 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   }
   splits = std::max(1, std::min(splits, pl.kblocks));
   const size_t red_bytes = (size_t)128 * pl.mb * pl.kbn * sizeof(float);
-  const size_t recv_bytes = (size_t)(128 * pl.mb + 8 * 2 * splits) * pl.kbn * sizeof(float);
+  // The cluster reduction receives every split's slice rows (slice_rows on the device).
+  const int slice = ((128 + splits - 1) / splits + 7) & ~7;
+  const size_t recv_bytes = (size_t)splits * slice * pl.mb * pl.kbn * sizeof(float);
   const bool cluster_fits =
       pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn, a.w_format);
   pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
