@@ -1,5 +1,7 @@
 #include "batch.h"
 
+#include "kernels/attention.cuh"
+
 #include <algorithm>
 #include <cstring>
 #include <unordered_set>
@@ -172,7 +174,7 @@ Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const
   }
   int64_t work = 0;
   for (size_t i : order)
-    if (requests[i].length != 1) work += ceil_div(requests[i].length * group, 64);
+    if (requests[i].length != 1) work += ceil_div(requests[i].length * group, foa::kPrefillTile);
   plan.work = work;
   int64_t table_len = 1;  // one entry for padded segments
   for (const auto& r : requests) table_len += ceil_div(r.cached + r.length, blocks[0]);
@@ -246,7 +248,7 @@ Plan plan_call(const std::vector<Request>& requests, const Limits& limits, const
   int64_t w = 0;
   for (int64_t k = plan.decode; k < plan.decode + plan.prefill; ++k) {
     const int64_t len = segments[5 * k + 1];
-    for (int64_t tile = 0; tile < ceil_div(len * group, 64); ++tile) {
+    for (int64_t tile = 0; tile < ceil_div(len * group, foa::kPrefillTile); ++tile) {
       work_arr[2 * w] = static_cast<int32_t>(k);
       work_arr[2 * w + 1] = static_cast<int32_t>(tile);
       ++w;

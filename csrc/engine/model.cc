@@ -757,6 +757,8 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   attn.partial_capacity = static_cast<size_t>(ws_decode_ * qh_l_ * ws_splits_);
   attn.max_keys = static_cast<int>(plan.max_keys);
   attn.status = st->status;
+  attn.rows = static_cast<int>(T);
+  attn.cache_blocks = cache.blocks();
   foa::RopeTable rope{static_cast<const float*>(inv_freq_.data()), attention_factor_};
 
   for (int l = 0; l < cfg_.layers; ++l) {

@@ -380,9 +380,10 @@ __global__ void decode_merge_kernel(const PagedAttention p, int max_splits) {
 }
 
 // ------------------------------------------------------------------------------------ prefill
-// One CTA per (work item = segment and 64-row query tile, key/value head). Rows of the tile are
-// (token, head) pairs of the group; 64-key tiles of K and V are double-buffered in shared memory
-// and shared by the four warps.
+// The mma.sync path, for geometries the tensor-core kernel (attention_tc.cu) does not take: two
+// CTAs per (work item = segment and 128-row query tile, key/value head), 64 rows each. Rows of the
+// tile are (token, head) pairs of the group; 64-key tiles of K and V are double-buffered in shared
+// memory and shared by the four warps.
 template <int D>
 __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention p,
                                                             const int32_t* work) {
@@ -390,11 +391,13 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention
   pdl_trigger();
   extern __shared__ __align__(128) uint8_t smem[];
   const int G = p.q_heads / p.kv_heads;
-  const int seg_index = work[2 * blockIdx.x], tile = work[2 * blockIdx.x + 1];
+  // Two CTAs per 128-row work item, 64 rows each.
+  const int seg_index = work[2 * (blockIdx.x >> 1)], tile = work[2 * (blockIdx.x >> 1) + 1];
   const int kvh = blockIdx.y;
   const Segment seg = p.segments[seg_index];
   const int total = seg.len * G;
-  const int m0 = tile * 64;
+  const int m0 = tile * kPrefillTile + (blockIdx.x & 1) * 64;
+  if (m0 >= total) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const float scale = p.scale * kLog2e;
@@ -536,7 +539,7 @@ int prefill_launch(const PagedAttention& p, const int32_t* work, int num_work, c
     cudaFuncSetAttribute(paged_prefill_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     configured[dev & 63] = true;
   }
-  launch_pdl(paged_prefill_kernel<D>, dim3(num_work, p.kv_heads), dim3(128), smem, stream, p, work);
+  launch_pdl(paged_prefill_kernel<D>, dim3(2 * num_work, p.kv_heads), dim3(128), smem, stream, p, work);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
@@ -556,6 +559,9 @@ int paged_decode(const PagedAttention& p, cudaStream_t stream) {
 int paged_prefill(const PagedAttention& p, const int32_t* work, int num_work, cudaStream_t stream) {
   if (num_work <= 0) return 0;
   if (p.kv_heads <= 0 || p.q_heads % p.kv_heads != 0) return -2;
+  // FOA_PREFILL_MMA_SYNC=1 keeps the mma.sync kernel (measurements only).
+  static const bool legacy = std::getenv("FOA_PREFILL_MMA_SYNC") != nullptr;
+  if (!legacy && prefill_tc_supported(p)) return paged_prefill_tc(p, work, num_work, stream);
   switch (p.head_dim) {
     case 64: return prefill_launch<64>(p, work, num_work, stream);
     case 128: return prefill_launch<128>(p, work, num_work, stream);

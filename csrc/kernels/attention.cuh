@@ -35,18 +35,27 @@ struct PagedAttention {
   int max_keys = 0;             // longest history of any segment (bounds the split count)
   int keys_per_split = 2048;    // fixed split width: each row's tiling depends on its own length
   int* status = nullptr;
+  // Prefill on the tensor cores (TMA tensor maps): rows of q and o, and pages in the layer's cache.
+  int rows = 0;
+  long cache_blocks = 0;
 };
 
 // Decode: every segment appends one row (len == 1) and attends its whole history.
 int paged_decode(const PagedAttention& args, cudaStream_t stream);
 
 // Prefill / chunks: segments of any length attend their history plus their own rows causally.
-// `work` lists (segment, query tile) pairs, `num_work` of them; a tile is 64 (token, head) rows
-// of one key/value head.
+// `work` lists (segment, query tile) pairs, `num_work` of them; a tile is 128 (token, head) rows
+// of one key/value head. Runs on the tcgen05 tensor cores when `prefill_tc_supported` (head_dim
+// 64 or 128, a GQA group dividing 128, `rows` and `cache_blocks` set), else on mma.sync.
 int paged_prefill(const PagedAttention& args, const int32_t* work, int num_work,
                   cudaStream_t stream);
+bool prefill_tc_supported(const PagedAttention& args);
+int paged_prefill_tc(const PagedAttention& args, const int32_t* work, int num_work,
+                     cudaStream_t stream);
 
-// Query tiles of a segment of `len` rows with `group` query heads per key/value head.
-inline int prefill_tiles(int len, int group) { return (len * group + 63) / 64; }
+// Rows of a prefill query tile, and the query tiles of a segment of `len` rows with `group`
+// query heads per key/value head.
+constexpr int kPrefillTile = 128;
+inline int prefill_tiles(int len, int group) { return (len * group + kPrefillTile - 1) / kPrefillTile; }
 
 }  // namespace foa

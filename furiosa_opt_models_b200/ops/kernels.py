@@ -303,17 +303,22 @@ def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys
     return out
 
 
+PREFILL_TILE = 128  # (token, head) rows of a prefill query tile
+
+
 def prefill_work(segments_cpu, group: int) -> torch.Tensor:
     """(segment, query tile) pairs of the prefill kernel, as int32 [n, 2]."""
     work = []
     for i, (_, length, _, _, _) in enumerate(segments_cpu.tolist()):
-        for tile in range((length * group + 63) // 64):
+        for tile in range((length * group + PREFILL_TILE - 1) // PREFILL_TILE):
             work.append((i, tile))
     return torch.tensor(work, dtype=torch.int32).reshape(-1, 2)
 
 
-def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=None):
-    """Causal attention of segments' rows over their history and themselves."""
+def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=None, tensor_cores=True):
+    """Causal attention of segments' rows over their history and themselves (128-row query tiles
+    of ``prefill_work``). ``cache`` is the layer's pages [blocks, 2, kv_heads, 16, d];
+    ``tensor_cores=False`` runs the mma.sync kernel."""
     _attn_common(segments)
     rows, q_heads, d = q.shape
     out = torch.empty_like(q) if out is None else out
@@ -321,7 +326,8 @@ def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=Non
     native().ops.paged_prefill(
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(),
         segments.shape[0], q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5),
-        work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream())
+        work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream(),
+        rows=rows if tensor_cores else 0, cache_blocks=cache.shape[0] if tensor_cores else 0)
     return out
 
 

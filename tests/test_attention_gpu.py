@@ -37,17 +37,38 @@ def test_paged_decode(q_heads, kv_heads, d):
     assert err < 2e-2, err
 
 
-@pytest.mark.parametrize("q_heads,kv_heads,d", [(16, 8, 128), (32, 8, 128), (8, 8, 64)])
-def test_paged_prefill(q_heads, kv_heads, d):
+@pytest.mark.parametrize("tensor_cores", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("q_heads,kv_heads,d", [(16, 8, 128), (32, 8, 128), (8, 8, 64), (64, 8, 128),
+                                                (16, 16, 128), (32, 4, 64)])
+def test_paged_prefill(q_heads, kv_heads, d, tensor_cores):
     from furiosa_opt_models_b200 import ops
     from furiosa_opt_models_b200.models import reference
 
-    lengths = [7, 16, 33, 64, 130, 1]
-    cached = [0, 0, 20, 100, 0, 40]
+    # Chunks with and without history, lengths around the 128-row and 128-key tile edges.
+    lengths = [7, 16, 33, 64, 130, 1, 200, 65]
+    cached = [0, 0, 20, 100, 0, 40, 300, 127]
     q, cache, table, segs = _setup(lengths, cached, q_heads, kv_heads, d)
     ref = reference.paged_attention(q, cache, table, segs)
     work = ops.prefill_work(segs, q_heads // kv_heads)
-    out = ops.paged_prefill(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), kv_heads, work.cuda())
+    out = ops.paged_prefill(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), kv_heads, work.cuda(),
+                            tensor_cores=tensor_cores)
     torch.cuda.synchronize()
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 2e-2, err
+
+
+def test_paged_prefill_long_prompts():
+    """Prompts of 1024 and 2047 tokens (16 and 32 K/V tiles): the running maximum, the lazy
+    rescale and the two-stage ring over many tiles, on the tensor cores."""
+    from furiosa_opt_models_b200 import ops
+    from furiosa_opt_models_b200.models import reference
+
+    q, cache, table, segs = _setup([1024, 2047, 300], [0, 0, 1500], 16, 8, 128, blocks=512, seed=1)
+    # Scores large enough that later keys raise the maximum by more than 2^8.
+    q = q * 4
+    ref = reference.paged_attention(q, cache, table, segs)
+    work = ops.prefill_work(segs, 2)
+    out = ops.paged_prefill(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), 8, work.cuda())
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 3e-2, err

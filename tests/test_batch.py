@@ -99,7 +99,9 @@ def test_refuses_unheld_adapters():
 
 
 def test_prefill_work_tiles():
-    # A segment of 33 rows with 2 query heads per key/value head spans ceil(66 / 64) tiles.
-    p = plan([req([1, 2, 3], 0, 33), req([9], 4, 1)], rows=64, group=2)
+    # Query tiles hold 128 (token, head) rows: 33 rows x 2 heads fit one tile, 65 x 2 need two.
+    p = plan([req([1, 2, 3], 0, 33), req([9], 4, 1)], rows=128, group=2)
     assert p["decode"] == 1 and p["prefill"] == 1
+    assert p["work"] == [1, 0]
+    p = plan([req([1, 2, 3, 4, 5], 0, 65), req([9], 4, 1)], rows=128, group=2, window=128)
     assert p["work"] == [1, 0, 1, 1]
