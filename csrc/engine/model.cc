@@ -97,6 +97,12 @@ DecoderModel::DecoderModel(const Device& device, ModelConfig cfg, int tp, int ra
     kvh_l_ = 1;
     kvh_first_ = rank_ * cfg_.kv_heads / tp_;
   }
+  // Decode attention splits every history into fixed chunks of keys. With few key/value heads on
+  // a chip (tensor parallelism) the chunks shrink, so that a decode batch still gives the GPU
+  // enough CTAs: 2048 keys at 8 or more heads, down to 256 keys at one. The width depends on the
+  // geometry only: a row's result does not depend on the batch it is in.
+  keys_per_split_ = 2048;
+  while (keys_per_split_ > 256 && keys_per_split_ * 8 > 2048 * kvh_l_) keys_per_split_ /= 2;
   const int inter = cfg_.experts > 0 ? 0 : cfg_.intermediate;
   if (inter % tp_ != 0 || (inter / tp_) % 128 != 0)
     throw Unsupported("the intermediate width does not split into 128-row blocks over the chips");
@@ -531,7 +537,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
     pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
   std::memcpy(pinned_stage_[slot].data(), host_stage_.data(), plan.staged.bytes);
 
-  const int64_t splits_needed = plan.decode > 0 ? (plan.max_keys + 2047) / 2048 : 1;
+  const int64_t splits_needed = plan.decode > 0 ? (plan.max_keys + keys_per_split_ - 1) / keys_per_split_ : 1;
   const int64_t splits = next_pow2(splits_needed);
   ensure_workspace(plan.rows_padded, std::max<int64_t>(plan.kept_padded, 1), splits,
                    plan.segments_padded);
@@ -543,7 +549,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
                                  cudaMemcpyHostToDevice, st->stream),
                  "stage operands");
   st->check_cuda(cudaEventRecord(stage_done_[slot], st->stream), "staging event");
-  plan.max_keys = splits * 2048;  // the decode grid covers the bucket's splits
+  plan.max_keys = splits * keys_per_split_;  // the decode grid covers the bucket's splits
   if (coll_) coll_->begin_call(st->stream);
 
   if (graphable) {
@@ -756,6 +762,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   attn.partial_lse = static_cast<float*>(ws_part_lse_.data());
   attn.partial_capacity = static_cast<size_t>(ws_decode_ * qh_l_ * ws_splits_);
   attn.max_keys = static_cast<int>(plan.max_keys);
+  attn.keys_per_split = keys_per_split_;
   attn.status = st->status;
   attn.rows = static_cast<int>(T);
   attn.cache_blocks = cache.blocks();
