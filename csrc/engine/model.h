@@ -203,7 +203,8 @@ class DecoderModel {
 
   // Workspace (device), sized for `ws_rows_` rows and `ws_kept_` kept rows.
   int64_t ws_rows_ = 0, ws_kept_ = 0, ws_splits_ = 0, ws_decode_ = 0;
-  int keys_per_split_ = 2048;  // decode attention's key chunk (see the constructor)
+  int keys_per_split_ = 2048;  // decode attention's key chunk and warps a CTA (see the constructor)
+  int decode_warps_ = 2;
   HbmBuffer ws_x_, ws_h_, ws_qkv_, ws_q_, ws_attn_, ws_act_, ws_hk_, ws_logits_, ws_idx_, ws_val_,
       ws_tokens_, ws_stage_, ws_part_o_, ws_part_lse_, ws_gemm_, ws_counters_, ws_partial_;
   // Quantized inputs of W8A8 / W4A4 projections: codes and scales of the widest input.

@@ -498,11 +498,14 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
     const size_t need = (size_t)p.num_segments * p.q_heads * max_splits;
     if (p.partial_o == nullptr || p.partial_lse == nullptr || need > p.partial_capacity) return -3;
   }
-  static const int warps = [] {
+  static const int env_warps = [] {
     const char* v = std::getenv("FOA_DECODE_WARPS");  // measurement override: 2, 3 or 4
-    const int w = v ? std::atoi(v) : kDecodeWarps;
-    return w >= 2 && w <= 4 ? w : kDecodeWarps;
+    const int w = v ? std::atoi(v) : 0;
+    return w >= 2 && w <= 4 ? w : 0;
   }();
+  const int warps = env_warps        ? env_warps
+                    : p.decode_warps >= 2 && p.decode_warps <= 4 ? p.decode_warps
+                                                                 : kDecodeWarps;
   static const int stages = [] {
     const char* v = std::getenv("FOA_DECODE_STAGES");  // measurement override: 2 or 3
     const int n = v ? std::atoi(v) : kDecodeStages;
@@ -515,14 +518,14 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
                             : (warps == 2 ? paged_decode_kernel<D, 2, 3>
                                : warps == 3 ? paged_decode_kernel<D, 3, 3>
                                             : paged_decode_kernel<D, 4, 3>);
-  static bool configured[64] = {false};
+  static bool configured[3][2][64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (!configured[dev & 63]) {
+  if (!configured[warps - 2][stages - 2][dev & 63]) {
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    configured[dev & 63] = true;
+    configured[warps - 2][stages - 2][dev & 63] = true;
   }
-  dim3 grid(p.num_segments * p.kv_heads, max_splits);  // one kernel per process: the env is fixed
+  dim3 grid(p.num_segments * p.kv_heads, max_splits);
   launch_pdl(kernel, dim3(grid), dim3(32 * warps), smem, stream, p, max_splits);
   if (max_splits > 1)
     launch_pdl(decode_merge_kernel<D>, dim3(p.num_segments, p.q_heads), dim3(D), 0, stream, p, max_splits);

@@ -38,6 +38,8 @@ struct PagedAttention {
   // Prefill on the tensor cores (TMA tensor maps): rows of q and o, and pages in the layer's cache.
   int rows = 0;
   long cache_blocks = 0;
+  // Decode: warps a CTA (2, 3 or 4; 0 takes the default of 2).
+  int decode_warps = 0;
 };
 
 // Decode: every segment appends one row (len == 1) and attends its whole history.

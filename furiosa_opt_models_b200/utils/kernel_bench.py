@@ -122,9 +122,11 @@ def decode_attn(args) -> dict:
     table = torch.arange(rows * nb, dtype=torch.int32, device="cuda")
     seg = torch.tensor([[r, 1, keys - 1, r * nb, nb] for r in range(rows)], dtype=torch.int32, device="cuda")
     q = torch.randn(rows, qh, d, device="cuda").bfloat16()
-    us = _time(lambda: ops.paged_decode(q, cache, table, seg, kvh, keys), args.warmup, args.iters)
+    us = _time(lambda: ops.paged_decode(q, cache, table, seg, kvh, keys, keys_per_split=args.split),
+               args.warmup, args.iters)
     kv_bytes = rows * keys * kvh * d * 2 * 2
-    return dict(kernel="paged_decode", rows=rows, keys=keys, us=round(us, 2), kv_gbs=round(kv_bytes / us / 1e3, 1))
+    return dict(kernel="paged_decode", rows=rows, keys=keys, kv_heads=kvh, split=args.split, us=round(us, 2),
+                kv_gbs=round(kv_bytes / us / 1e3, 1))
 
 
 def prefill_attn(args) -> dict:
@@ -253,6 +255,7 @@ def main() -> None:
     d.add_argument("--keys", type=int, default=2048)
     d.add_argument("--q-heads", type=int, default=16)
     d.add_argument("--kv-heads", type=int, default=8)
+    d.add_argument("--split", type=int, default=2048, help="keys per split")
     f = sub.add_parser("prefill-attn")
     f.add_argument("--rows", type=int, default=8192)
     f.add_argument("--seqs", type=int, default=8)
