@@ -1,0 +1,72 @@
+// Media encoders: a call turns images (merged patches with their positions) or audio frames into
+// rows of the language model's width, which a framework places at the media's placeholder tokens.
+//
+// Reference: crates/furiosa-opt-engine/src/vision_language/mod.rs (Image :19-41, Audio :44-60,
+// Encoder :79-94, launches :98-118) and gemma4_unified.rs (vision :42-84, audio :86-103);
+// crates/furiosa-opt-models/src/models/vision_language/gemma4_unified.rs (the embedders).
+#pragma once
+
+#include <array>
+#include <cstdint>
+#include <string>
+#include <vector>
+
+#include "checkpoint.h"
+#include "runtime.h"
+
+namespace foa::engine {
+
+// Widths of a Gemma-4 unified media encoder, from its config.
+struct EncoderConfig {
+  int text = 0;       // text_config.hidden_size: the rows' width
+  int embed = 0;      // vision_config.mm_embed_dim
+  int patch = 0;      // 3 x (patch_size x pooling_kernel_size)^2 features of a merged patch
+  int positions = 0;  // vision_config.mm_posemb_size: positions of each coordinate
+  int samples = 0;    // audio_config.audio_embed_dim: samples of an audio frame
+  float vision_eps = 1e-6f, audio_eps = 1e-6f;  // the unit RMS norms' epsilons
+  float ln_eps = 1e-5f;                          // the patch path's LayerNorms (torch's default)
+  std::string size;                               // "12B" for the published widths, else "custom"
+};
+
+// The config's widths; refuses another model type, a quantized checkpoint, or widths the kernels
+// do not take (each a multiple of 64 for the projections' K).
+EncoderConfig encoder_config(const Checkpoint& ck);
+
+struct ImageInput {
+  HbmBuffer patches;                           // [n, patch] BF16
+  std::vector<std::array<int32_t, 2>> positions;  // (x, y) of each of the n patches
+};
+
+struct AudioInput {
+  HbmBuffer frames;  // [n, samples] BF16
+  int64_t count = 0;
+};
+
+class MediaEncoder {
+ public:
+  // Rows a launch takes at most (the reference compiles launches of 512 and 2304 rows).
+  static constexpr int64_t kLaunchRows = 2304;
+
+  MediaEncoder(const Device& device, EncoderConfig cfg);
+  // Strict load of `model.vision_embedder.*`, `model.embed_vision.*` and `model.embed_audio.*`
+  // (the language model's tensors are ignored).
+  void load(const Checkpoint& ck);
+  const EncoderConfig& config() const { return cfg_; }
+  const Device& device() const { return device_; }
+
+  // Each image's rows ([patches, text] BF16), in order, returned at submission.
+  std::vector<HbmTensor> vision(const std::vector<ImageInput>& images);
+  // Each clip's rows ([frames, text] BF16), in order, returned at submission.
+  std::vector<HbmTensor> audio(const std::vector<AudioInput>& clips);
+
+ private:
+  Device device_;
+  EncoderConfig cfg_;
+  HbmBuffer ln1_w_, ln1_b_, dense_w_, dense_b_, ln2_w_, ln2_b_, table_, pn_w_, pn_b_, vision_proj_,
+      audio_proj_;
+  // Consecutive items packed into launches of at most kLaunchRows rows; an item larger than a
+  // launch is refused.
+  static std::vector<std::vector<size_t>> launches(const std::vector<int64_t>& rows);
+};
+
+}  // namespace foa::engine

@@ -1,5 +1,7 @@
 #include "registry.h"
 
+#include "encoder.h"
+
 #include "kernels/gemm.cuh"
 #include "kernels/quant.cuh"
 
@@ -232,6 +234,16 @@ const std::map<std::string, std::vector<Implementation>>& served() {
                                     [](const Checkpoint& c) { return llama_scope(c, "mistral", "bf16"); })};
     t["Qwen3MoeForCausalLM"] = {make("qwen3_moe", "qwen3_moe.ForCausalLM", "bf16", Output::Tokens,
                                      [](const Checkpoint& c) { return qwen3_moe_scope(c); })};
+    // Gemma 4 unified's media embedders, loaded alone (registry.rs:571): an Encoder.
+    t["Gemma4UnifiedForConditionalGeneration"] = {
+        make("gemma4_unified", "Encoder", "bf16", Output::Hidden, [](const Checkpoint& c) {
+          const EncoderConfig e = encoder_config(c);
+          ModelConfig m;
+          m.family = "gemma4_unified";
+          m.size = e.size;
+          m.hidden = e.text;
+          return m;
+        })};
     return t;
   }();
   return table;
@@ -312,9 +324,18 @@ Selection select(const LoadOptions& o, const Checkpoint& ck) {
     quantized = ck.quantized(*o.quantization == "fp8_per_tensor" ? "tensor" : "channel");
     read = &quantized;
   }
-  if (o.encoder && read->part() == Part::Whole)
-    unsupported("encoder", "a decoder holds no media encoder that loads alone");
   s.implementation = choose(l, *read, &s.config);
+  // A media encoder loads alone, and a decoder holds none that does (the reference's
+  // `Listed::reads(Part)`: vision_language/gemma4_unified.rs:25-33 and the decoders').
+  const bool encoder = s.implementation->family == "gemma4_unified";
+  if (encoder && !o.encoder) unsupported("encoder", "a media encoder loads alone, so choose the encoder");
+  if (!encoder && o.encoder) unsupported("encoder", "a decoder holds no media encoder that loads alone");
+  if (encoder) {
+    s.chips = o.chips.value_or(1);
+    if (s.chips != 1) unsupported("chips", "a media encoder runs on one chip");
+    if (o.adapters) unsupported("adapters", "a media encoder takes no adapters");
+    return s;
+  }
   const ModelConfig& m = s.config;
   s.chips = o.chips.value_or(1);
   if (s.chips != 1 && s.chips != 2 && s.chips != 4 && s.chips != 8)
@@ -417,6 +438,57 @@ struct Source {
 };
 
 }  // namespace
+
+std::vector<uint16_t> tensor_bf16(const StoredTensor& t) {
+  const int64_t n = t.numel();
+  std::vector<uint16_t> out(static_cast<size_t>(n));
+  const uint8_t* base = t.data();
+  switch (t.dtype) {
+    case StDType::BF16: std::memcpy(out.data(), base, n * 2); break;
+    case StDType::F16:
+      for (int64_t i = 0; i < n; ++i) {
+        uint16_t h;
+        std::memcpy(&h, base + i * 2, 2);
+        out[i] = f32_to_bf16(f16_to_f32(h));
+      }
+      break;
+    case StDType::F32:
+      for (int64_t i = 0; i < n; ++i) {
+        float f;
+        std::memcpy(&f, base + i * 4, 4);
+        out[i] = f32_to_bf16(f);
+      }
+      break;
+    default: throw ValueError("a tensor of dtype " + std::string(st_dtype_name(t.dtype)) + " does not load as BF16");
+  }
+  return out;
+}
+
+std::vector<float> tensor_f32(const StoredTensor& t) {
+  const int64_t n = t.numel();
+  std::vector<float> out(static_cast<size_t>(n));
+  const uint8_t* base = t.data();
+  for (int64_t i = 0; i < n; ++i) {
+    switch (t.dtype) {
+      case StDType::BF16: {
+        uint16_t h;
+        std::memcpy(&h, base + i * 2, 2);
+        const uint32_t b = static_cast<uint32_t>(h) << 16;
+        std::memcpy(&out[i], &b, 4);
+        break;
+      }
+      case StDType::F16: {
+        uint16_t h;
+        std::memcpy(&h, base + i * 2, 2);
+        out[i] = f16_to_f32(h);
+        break;
+      }
+      case StDType::F32: std::memcpy(&out[i], base + i * 4, 4); break;
+      default: throw ValueError("a tensor of dtype " + std::string(st_dtype_name(t.dtype)) + " does not load as FP32");
+    }
+  }
+  return out;
+}
 
 void load_weights(DecoderModel& model, const Checkpoint& ck) {
   const ModelConfig& cfg = model.config();

@@ -27,6 +27,10 @@ struct LoadRefusal {
   [[noreturn]] void raise() const;
 };
 
+// A checkpoint tensor's values (BF16, F16 or F32 in the file) as BF16 bits, or as FP32.
+std::vector<uint16_t> tensor_bf16(const StoredTensor& t);
+std::vector<float> tensor_f32(const StoredTensor& t);
+
 struct Implementation {
   std::string family;      // qwen3 | llama | mistral | qwen3_moe
   std::string cls;         // Python class path, e.g. "qwen3.ForCausalLM"

@@ -1,0 +1,117 @@
+// Media encoders: `Encoder` (what a load of a media encoder alone returns) and the media it takes,
+// `vision_language.Image` and `vision_language.Audio`.
+//
+// Reference: crates/furiosa-opt-python/src/vision_language.rs (Image :29-69, Audio :71-104) and
+// model/mod.rs:357-417 (Encoder.vision / Encoder.audio).
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include <array>
+
+#include "engine/encoder.h"
+#include "python/pytypes.h"
+
+namespace py = pybind11;
+using namespace foa::engine;
+
+namespace {
+
+struct PyImage {
+  std::shared_ptr<HbmTensor> pixels;
+  std::vector<std::array<int32_t, 2>> positions;
+};
+
+struct PyAudio {
+  std::shared_ptr<HbmTensor> frames;
+};
+
+// Refuses `t` unless it holds `count` two-dimensional BF16 rows.
+void bf16_rows(const HbmTensor& t, int64_t count, const char* what) {
+  if (t.dtype() != DType::BF16 || t.shape().size() != 2 || t.shape()[0] != count)
+    throw ValueError(std::string(what) + " are not two-dimensional BF16 rows, one for each " +
+                     (std::string(what) == "pixels" ? "position" : "frame"));
+}
+
+// The tensor's storage, refused unless it lies on the encoder's device.
+HbmBuffer on(const HbmTensor& t, const MediaEncoder& e) {
+  if (t.buffer().valid() && t.buffer().device() != e.device().state())
+    throw ValueError("a tensor lies on another device than the encoder's");
+  return t.buffer();
+}
+
+}  // namespace
+
+void bind_encoder(py::module_& m) {
+  py::module_ vl = m.def_submodule("vision_language", "The media a vision-language model's encoder takes.");
+  py::class_<PyImage>(vl, "Image",
+                      "An image or a video's frames: `pixels`, merged patches as BF16 rows [n, features], "
+                      "and the (x, y) position of each patch in its frame.")
+      .def(py::init([](std::shared_ptr<HbmTensor> pixels, const std::vector<std::array<int32_t, 2>>& positions) {
+             bf16_rows(*pixels, static_cast<int64_t>(positions.size()), "pixels");
+             return PyImage{std::move(pixels), positions};
+           }),
+           py::arg("pixels"), py::arg("positions"),
+           "`pixels` lie on the model's device; `positions` name the valid patches only.\n\n"
+           "Raises:\n    ValueError: `pixels` are not two-dimensional BF16 rows, one for each position.")
+      .def_property_readonly("pixels", [](const PyImage& i) { return i.pixels; })
+      .def_property_readonly("positions", [](const PyImage& i) { return i.positions; });
+  py::class_<PyAudio>(vl, "Audio", "Audio: `frames`, BF16 rows [n, samples] of samples each.")
+      .def(py::init([](std::shared_ptr<HbmTensor> frames) {
+             const int64_t n = frames->shape().empty() ? 0 : frames->shape()[0];
+             bf16_rows(*frames, n, "frames");
+             return PyAudio{std::move(frames)};
+           }),
+           py::arg("frames"),
+           "`frames` lie on the model's device.\n\n"
+           "Raises:\n    ValueError: `frames` are not two-dimensional BF16 rows.")
+      .def_property_readonly("frames", [](const PyAudio& a) { return a.frames; });
+
+  py::class_<PyEncoder>(m, "Encoder",
+                        "A media encoder loaded on a device, whatever its model: its calls turn images, video "
+                        "frames and audio into rows of its language model's width.")
+      .def("vision",
+           [](const PyEncoder& e, const std::vector<PyImage>& images) {
+             std::vector<ImageInput> in;
+             for (const auto& im : images) in.push_back(ImageInput{on(*im.pixels, *e.encoder), im.positions});
+             std::vector<HbmTensor> rows;
+             {
+               py::gil_scoped_release nogil;
+               rows = e.encoder->vision(in);
+             }
+             std::vector<std::shared_ptr<HbmTensor>> out;
+             for (auto& r : rows) out.push_back(std::make_shared<HbmTensor>(std::move(r)));
+             return out;
+           },
+           py::arg("images"),
+           "The rows of each of `images`, `[patches, width]` BF16 in order, returned once the device "
+           "accepted the call; reading them waits for it.\n\n"
+           "Raises:\n    ValueError: A patch is not of the model's features, a position is outside those the\n"
+           "        model places, or a tensor lies on another device.\n"
+           "    NotImplementedError: An image holds more patches than a call takes.\n"
+           "    RuntimeError: The device refuses the call.")
+      .def("audio",
+           [](const PyEncoder& e, const std::vector<PyAudio>& clips) {
+             std::vector<AudioInput> in;
+             for (const auto& c : clips)
+               in.push_back(AudioInput{on(*c.frames, *e.encoder), c.frames->shape().empty() ? 0 : c.frames->shape()[0]});
+             std::vector<HbmTensor> rows;
+             {
+               py::gil_scoped_release nogil;
+               rows = e.encoder->audio(in);
+             }
+             std::vector<std::shared_ptr<HbmTensor>> out;
+             for (auto& r : rows) out.push_back(std::make_shared<HbmTensor>(std::move(r)));
+             return out;
+           },
+           py::arg("clips"),
+           "The rows of each of `clips`, `[frames, width]` BF16 in order, returned once the device "
+           "accepted the call; reading them waits for it.\n\n"
+           "Raises:\n    ValueError: A frame is not of the model's samples, or a tensor lies on another device.\n"
+           "    NotImplementedError: A clip holds more frames than a call takes.\n"
+           "    RuntimeError: The device refuses the call.")
+      .def_property_readonly("size", [](const PyEncoder& e) { return e.encoder->config().size; })
+      .def_property_readonly("width", [](const PyEncoder& e) { return e.encoder->config().text; })
+      .def_property_readonly("patch_features", [](const PyEncoder& e) { return e.encoder->config().patch; })
+      .def_property_readonly("samples", [](const PyEncoder& e) { return e.encoder->config().samples; })
+      .def_property_readonly("positions", [](const PyEncoder& e) { return e.encoder->config().positions; });
+}

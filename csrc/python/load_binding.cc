@@ -6,6 +6,7 @@
 #include <pybind11/stl.h>
 
 #include "engine/checkpoint.h"
+#include "engine/encoder.h"
 #include "engine/registry.h"
 #include "python/pytypes.h"
 
@@ -159,6 +160,15 @@ void bind_checkpoint_and_load(py::module_& m) {
         if (device.chips() != s.chips)
           throw ValueError("the device opens " + std::to_string(device.chips()) + " chips, the load " +
                            std::to_string(s.chips));
+        if (s.implementation->family == "gemma4_unified") {
+          PyEncoder e;
+          {
+            py::gil_scoped_release nogil;
+            e.encoder = std::make_shared<MediaEncoder>(device, encoder_config(*c.ck));
+            e.encoder->load(*c.ck);
+          }
+          return py::cast(std::move(e));
+        }
         std::shared_ptr<DecoderModel> model;
         {
           py::gil_scoped_release nogil;

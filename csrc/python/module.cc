@@ -6,10 +6,12 @@ namespace py = pybind11;
 
 void bind_ops(py::module_& m);
 void bind_engine(py::module_& m);
+void bind_encoder(py::module_& m);
 
 PYBIND11_MODULE(_native, m) {
   m.doc() = "Native engine of furiosa_opt_engine for NVIDIA Blackwell (sm_100a).";
   py::module_ ops = m.def_submodule("ops", "Raw kernel launchers (device addresses and streams).");
   bind_ops(ops);
   bind_engine(m);
+  bind_encoder(m);
 }

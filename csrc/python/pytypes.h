@@ -4,6 +4,7 @@
 #include <memory>
 #include <string>
 
+#include "engine/encoder.h"
 #include "engine/lora.h"
 #include "engine/model.h"
 
@@ -20,6 +21,10 @@ struct PyQwen3Model : PyDecoder {};
 struct PyLlamaForCausalLM : PyDecoder {};
 struct PyMistralForCausalLM : PyDecoder {};
 struct PyQwen3MoeForCausalLM : PyDecoder {};
+// A media encoder (a load of a vision-language model's encoder alone).
+struct PyEncoder {
+  std::shared_ptr<foa::engine::MediaEncoder> encoder;
+};
 
 // The LoRA adapters a decoder's calls run with, and one loaded adapter.
 struct PyAdapterSpec {

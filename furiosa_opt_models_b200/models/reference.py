@@ -307,3 +307,43 @@ def fp8_rows_quantize(w: torch.Tensor, tensor_amax: float | None = None):
     scales = amax / torch.full_like(amax, E4M3_MAX)
     rcp = torch.where(scales == 0, torch.zeros_like(scales), torch.ones_like(scales) / scales)
     return _e4m3(wf * rcp[:, None]), scales
+
+
+# ------------------------------------------------------------------------------ media encoders
+# Gemma-4 unified embedders (crates/furiosa-opt-models/src/models/vision_language/gemma4_unified.rs):
+# every step rounded to BF16 as the BF16 forward rounds it.
+
+
+def _bf(x: torch.Tensor) -> torch.Tensor:
+    return x.bfloat16().float()
+
+
+def _layernorm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    mean = x.mean(-1, keepdim=True)
+    var = ((x - mean) ** 2).mean(-1, keepdim=True)
+    return _bf((x - mean) * torch.rsqrt(var + eps) * w.float() + b.float())
+
+
+def _unit_rms(x: torch.Tensor, eps: float) -> torch.Tensor:
+    return _bf(x * torch.rsqrt((x * x).mean(-1, keepdim=True) + eps))
+
+
+def gemma4_vision(w: dict, patches: torch.Tensor, positions, eps: float = 1e-6) -> torch.Tensor:
+    """Rows [n, text] of merged patches [n, features] at (x, y) positions, in FP32 (BF16 values)."""
+    e = "model.vision_embedder."
+    x = _layernorm(patches.float(), w[e + "patch_ln1.weight"], w[e + "patch_ln1.bias"])
+    v = _bf(x @ w[e + "patch_dense.weight"].float().T + w[e + "patch_dense.bias"].float())
+    a = _layernorm(v, w[e + "patch_ln2.weight"], w[e + "patch_ln2.bias"])
+    table = w[e + "pos_embedding"].float()
+    xy = torch.tensor(positions, dtype=torch.long)
+    pos = _bf(table[xy[:, 0], 0] + table[xy[:, 1], 1])
+    s = _bf(a + pos)
+    n = _layernorm(s, w[e + "pos_norm.weight"], w[e + "pos_norm.bias"])
+    u = _unit_rms(n, eps)
+    return _bf(u @ w["model.embed_vision.embedding_projection.weight"].float().T)
+
+
+def gemma4_audio(w: dict, frames: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Rows [n, text] of audio frames [n, samples], in FP32 (BF16 values)."""
+    u = _unit_rms(frames.float(), eps)
+    return _bf(u @ w["model.embed_audio.embedding_projection.weight"].float().T)

@@ -201,3 +201,47 @@ def merge_lora(weights: dict, cfg: dict, lora: dict, r: int, alpha: float) -> di
         out[p + "gate_up"] = interleave_gate_up(gate + delta("gate_proj"), up + delta("up_proj"))
         out[p + "down"] = out[p + "down"].float() + delta("down_proj")
     return out
+
+
+def gemma4_unified_config(text: int = 256, embed: int = 192, positions: int = 40, samples: int = 640,
+                          patch_size: int = 16, pooling: int = 3, eps: float = 1e-6) -> dict:
+    """A Gemma-4 unified config.json of the given media-encoder widths (the published model:
+    text 3840, embed 3840, positions 1120, samples 640)."""
+    return {
+        "architectures": ["Gemma4UnifiedForConditionalGeneration"],
+        "model_type": "gemma4_unified",
+        "text_config": {"hidden_size": text},
+        "vision_config": {"mm_embed_dim": embed, "mm_posemb_size": positions, "patch_size": patch_size,
+                          "pooling_kernel_size": pooling, "rms_norm_eps": eps},
+        "audio_config": {"audio_embed_dim": samples, "rms_norm_eps": eps},
+    }
+
+
+def write_gemma4_encoder(directory: str, config: dict, seed: int = 0, std: float = 0.05) -> dict:
+    """A synthetic Gemma-4 unified checkpoint: the media embedders under `model.` (and one language
+    model tensor, which a load of the encoder alone ignores); returns the embedders' tensors."""
+    from safetensors.torch import save_file
+
+    os.makedirs(directory, exist_ok=True)
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(config, f)
+    v = config["vision_config"]
+    E, T, S, N = v["mm_embed_dim"], config["text_config"]["hidden_size"], config["audio_config"]["audio_embed_dim"], v["mm_posemb_size"]
+    P = 3 * (v["patch_size"] * v["pooling_kernel_size"]) ** 2
+    g = torch.Generator().manual_seed(seed)
+
+    def rnd(*shape, scale=std, mean=0.0):
+        return (torch.randn(*shape, generator=g) * scale + mean).bfloat16()
+
+    e = "model.vision_embedder."
+    w = {
+        e + "patch_ln1.weight": rnd(P, scale=0.1, mean=1.0), e + "patch_ln1.bias": rnd(P, scale=0.1),
+        e + "patch_dense.weight": rnd(E, P), e + "patch_dense.bias": rnd(E, scale=0.1),
+        e + "patch_ln2.weight": rnd(E, scale=0.1, mean=1.0), e + "patch_ln2.bias": rnd(E, scale=0.1),
+        e + "pos_embedding": rnd(N, 2, E, scale=0.5),
+        e + "pos_norm.weight": rnd(E, scale=0.1, mean=1.0), e + "pos_norm.bias": rnd(E, scale=0.1),
+        "model.embed_vision.embedding_projection.weight": rnd(T, E),
+        "model.embed_audio.embedding_projection.weight": rnd(T, S),
+    }
+    save_file({**w, "model.language_model.embed_tokens.weight": rnd(8, T)}, os.path.join(directory, "model.safetensors"))
+    return w

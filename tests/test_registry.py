@@ -89,3 +89,34 @@ def test_classes_of_the_family(tmp_path):
     for arch, cls in [("Qwen3ForSequenceClassification", "qwen3.ForSequenceClassification"),
                       ("Qwen3Model", "qwen3.Model")]:
         assert engine.LoadOptions().select(_ckpt(tmp_path, dict(base, architectures=[arch])))["class"] == cls
+
+
+def test_media_encoder_loads_alone(tmp_path):
+    """Gemma 4 unified's media embedders are an Encoder a load of the encoder alone returns; the
+    reference refuses the other combinations (vision_language/gemma4_unified.rs:25-33, the
+    decoders' `reads(Part)`, models/vision_language/gemma4_unified.rs:127-164)."""
+    ck = _ckpt(tmp_path, synthetic.gemma4_unified_config(3840, 3840, 1120, 640))
+    sel = engine.LoadOptions().encoder().select(ck)
+    assert sel["architecture"] == "Gemma4UnifiedForConditionalGeneration"
+    assert sel["size"] == "12B"
+    assert _native.LoadOptions().encoder().select(
+        _ckpt(tmp_path / "small", synthetic.gemma4_unified_config()))["size"] == "custom"
+    with pytest.raises(NotImplementedError, match="^encoder: a media encoder loads alone, so choose the encoder$"):
+        engine.LoadOptions().parse(ck)
+    with pytest.raises(NotImplementedError, match="^quantization: the media encoder's projections stay BF16$"):
+        engine.LoadOptions().encoder().quantization("fp8_per_tensor").parse(ck)
+    with pytest.raises(NotImplementedError, match="^chips: a media encoder runs on one chip$"):
+        engine.LoadOptions().encoder().chips(2).parse(ck)
+    qwen = _ckpt(tmp_path / "qwen", synthetic.hf_config(configs.get("qwen3-1.7b")))
+    with pytest.raises(NotImplementedError, match="^encoder: a decoder holds no media encoder that loads alone$"):
+        engine.LoadOptions().encoder().parse(qwen)
+
+
+def test_media_encoder_refuses_odd_widths(tmp_path):
+    odd = synthetic.gemma4_unified_config(text=250)
+    with pytest.raises(NotImplementedError, match="hidden_size 250 is not a multiple of 64"):
+        engine.LoadOptions().encoder().parse(_ckpt(tmp_path, odd))
+    broken = synthetic.gemma4_unified_config()
+    del broken["vision_config"]["mm_embed_dim"]
+    with pytest.raises(ValueError, match="vision_config.mm_embed_dim"):
+        engine.LoadOptions().encoder().parse(_ckpt(tmp_path / "b", broken))
