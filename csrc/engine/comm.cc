@@ -198,6 +198,15 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   a.status = status_;
   a.trace = trace_;
   if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
+  inject_peer(stream);
+}
+
+void PeerCollectives::inject_peer(cudaStream_t stream) {
+  // Host-side drill of a peer that never answers: the status word the kernel's bounded wait
+  // would write, read when the call's result is.
+  static const int kPeerTimeout = 5;
+  if (device_.state()->injected("peer"))
+    cudaMemcpyAsync(status_, &kPeerTimeout, sizeof(int), cudaMemcpyHostToDevice, stream);
 }
 
 void PeerCollectives::argmax(const float* value, const int32_t* index, int rows, int32_t* out,

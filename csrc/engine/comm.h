@@ -42,6 +42,8 @@ class PeerCollectives : public Collectives {
   void barrier(cudaStream_t stream);
   // Measurement: the add_norm kernels write milestone timestamps here (null: none).
   void set_trace(unsigned long long* trace) { trace_ = trace; }
+  // Fault drill (DeviceState::injected "peer"): the next collective reports a silent peer.
+  void inject_peer(cudaStream_t stream);
 
  private:
   Device device_;

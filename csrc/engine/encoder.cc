@@ -6,6 +6,7 @@
 #include "kernels/gemm.cuh"
 #include "kernels/media.cuh"
 #include "registry.h"
+#include "trace.h"
 
 namespace foa::engine {
 
@@ -174,6 +175,7 @@ void rows_of(const HbmBuffer& b, int64_t count, int width, const std::string& wh
 }  // namespace
 
 std::vector<HbmTensor> MediaEncoder::vision(const std::vector<ImageInput>& images) {
+  TraceScope span("encoder.vision", "call");
   for (const auto& im : images) {
     rows_of(im.patches, static_cast<int64_t>(im.positions.size()), cfg_.patch, "");
     for (const auto& xy : im.positions) {
@@ -241,6 +243,7 @@ std::vector<HbmTensor> MediaEncoder::vision(const std::vector<ImageInput>& image
 }
 
 std::vector<HbmTensor> MediaEncoder::audio(const std::vector<AudioInput>& clips) {
+  TraceScope span("encoder.audio", "call");
   std::vector<int64_t> counts;
   for (const auto& c : clips) {
     rows_of(c.frames, c.count, cfg_.samples, "");

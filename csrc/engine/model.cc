@@ -1,5 +1,7 @@
 #include "model.h"
 
+#include "trace.h"
+
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -503,6 +505,9 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   auto st = device_.state();
   st->check();
   st->activate();
+  TraceScope call_span("forward", "call");
+  const TraceLevel tracing = trace_level();
+  cudaEvent_t device_begin = tracing >= TraceLevel::Info ? Tracer::get().record(st->ordinal, st->stream) : nullptr;
   const Limits lim = limits();
   std::vector<bool> filled;
   for (const auto& a : adapters) {
@@ -512,7 +517,8 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   call_adapters_ = adapters;
   // Decode-only calls whose every request keeps its last row run as CUDA graphs of padded size
   // (calls with adapters run eagerly: their factors differ call to call).
-  bool graphable = graphs_enabled_ && adapters.empty();
+  // (Per-kernel tracing runs eagerly: its events sit between the launches.)
+  bool graphable = graphs_enabled_ && adapters.empty() && tracing < TraceLevel::Trace;
   int64_t rows = 0;
   for (const auto& r : requests) {
     rows += r.length;
@@ -532,8 +538,11 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   const int slot = stage_slot_;
   stage_slot_ ^= 1;
   st->check_cuda(cudaEventSynchronize(stage_done_[slot]), "staging wait");
+  TraceScope plan_span("plan", "host", TraceLevel::Debug);
   Plan plan = plan_call(requests, lim, cache.spec(), cache.blocks(), static_cast<int64_t>(adapters.size()), filled, group,
                         graphable ? bucket : 0, host_stage_);
+  plan_span.end();
+  TraceScope launch_span("stage and launch", "host", TraceLevel::Debug);
   if (pinned_stage_[slot].size() < plan.staged.bytes)
     pinned_stage_[slot] = HostBuffer(std::max<size_t>(plan.staged.bytes * 2, 1 << 16));
   std::memcpy(pinned_stage_[slot].data(), host_stage_.data(), plan.staged.bytes);
@@ -589,6 +598,7 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
     launches_ += launch(plan, cache);
   }
 
+  launch_span.end();
   // The kept rows' output in its own buffer, so later calls do not overwrite it.
   const int H = cfg_.hidden;
   HbmTensor result = [&]() {
@@ -615,6 +625,12 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
                      "output copy");
     return HbmTensor(out, {plan.kept, cfg_.labels}, DType::F32);
   }();
+  if (device_begin != nullptr) {
+    cudaEvent_t device_end = Tracer::get().record(st->ordinal, st->stream);
+    Tracer::get().device_span("forward.device", "GPU", st->ordinal, device_begin, device_end);
+    call_span.args("{\"rows\": " + std::to_string(plan.rows) + ", \"decode\": " + std::to_string(plan.decode) +
+                   ", \"prefill\": " + std::to_string(plan.prefill) + "}");
+  }
   last_plan_ = std::move(plan);
   return result;
 }
@@ -627,9 +643,18 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   const Staged& sg = plan.staged;
   const HbmBuffer& stage = ws_stage_;
   int kernels = 0;
+  // Per-kernel device spans (trace level): an event after every launch.
+  const bool per_kernel = trace_level() >= TraceLevel::Trace;
+  cudaEvent_t prev = per_kernel ? Tracer::get().record(st->ordinal, s) : nullptr;
   auto fail = [&](int rc, const char* what) {
+    if (rc == 0 && st->injected("launch")) rc = -5;
     if (rc != 0) st->fail(std::string(what) + " launch rejected (" + std::to_string(rc) + ")");
     ++kernels;
+    if (per_kernel) {
+      cudaEvent_t now = Tracer::get().record(st->ordinal, s);
+      Tracer::get().device_span(what, "GPU", st->ordinal, prev, now);
+      prev = now;
+    }
   };
   auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
                   int epi, const void* res, int lora_layer = -1, int lora_module = 0,

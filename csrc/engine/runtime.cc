@@ -1,5 +1,7 @@
 #include "runtime.h"
 
+#include <cstdlib>
+
 #include <algorithm>
 #include <cstring>
 
@@ -105,10 +107,28 @@ void DeviceState::check_status() {
   check_cuda(cudaMemcpyAsync(&code, status, sizeof(int), cudaMemcpyDeviceToHost, stream),
              "status read");
   check_cuda(cudaStreamSynchronize(stream), "status wait");
-  if (code != 0) {
-    cudaMemsetAsync(status, 0, sizeof(int), stream);
-    fail("a kernel gave up a bounded wait (status " + std::to_string(code) + ")");
-  }
+  raise_status(code);
+}
+
+void DeviceState::raise_status(int code) {
+  if (code == 0) return;
+  static const char* what[] = {"",
+                               "a TMA stage never landed",
+                               "a pipeline stage was never released",
+                               "an accumulator was never completed",
+                               "an accumulator was never released",
+                               "a peer rank never raised its flag",
+                               "copies in flight did not land while aborting"};
+  const std::string reason = code > 0 && code < 7 ? what[code] : "unknown";
+  cudaMemsetAsync(status, 0, sizeof(int), stream);
+  fail("a kernel gave up a bounded wait: " + reason + " (status " + std::to_string(code) + ")");
+}
+
+bool DeviceState::injected(const char* kind) {
+  if (fault_countdown < 0 || fault_kind != kind) return false;
+  if (fault_countdown-- > 0) return false;
+  fault_kind.clear();
+  return true;
 }
 
 void DeviceState::activate() const { cudaSetDevice(ordinal); }
@@ -137,6 +157,13 @@ Device::Device(std::vector<int> chips, int pes_begin, int pes_end, int rank) {
   state_->check_cuda(cudaStreamCreateWithFlags(&state_->stream, cudaStreamNonBlocking), "stream");
   state_->check_cuda(cudaMalloc(&state_->status, 64), "status word");
   state_->check_cuda(cudaMemset(state_->status, 0, 64), "status word");
+  if (const char* f = std::getenv("FOA_FAULT")) {
+    // <kind>:<countdown>, e.g. "launch:10": the eleventh kernel launch fails.
+    const std::string spec(f);
+    const size_t colon = spec.find(':');
+    state_->fault_kind = spec.substr(0, colon);
+    state_->fault_countdown = colon == std::string::npos ? 0 : std::atoll(spec.c_str() + colon + 1);
+  }
 }
 
 size_t Device::capacity() const {
@@ -248,6 +275,7 @@ std::shared_ptr<TransferState> submit_copy(const std::shared_ptr<DeviceState>& d
   auto t = std::make_shared<TransferState>();
   t->device = dev;
   dev->check_cuda(cudaEventCreateWithFlags(&t->done, cudaEventDisableTiming), "transfer event");
+  if (dev->injected("copy")) dev->fail("transfer failed (injected fault)");
   if (bytes) dev->check_cuda(cudaMemcpyAsync(dst, src, bytes, kind, dev->stream), "transfer");
   dev->check_cuda(cudaEventRecord(t->done, dev->stream), "transfer event");
   return t;
@@ -330,19 +358,30 @@ void HbmTensor::wait() const {
   auto dev = buffer_.device();
   dev->check();
   dev->activate();
+  // The kernels' status word travels with the same synchronisation: a bounded wait that gave up
+  // raises here, when the result is read.
+  int code = 0;
+  dev->check_cuda(cudaMemcpyAsync(&code, dev->status, sizeof(int), cudaMemcpyDeviceToHost, dev->stream),
+                  "status read");
   dev->check_cuda(cudaStreamSynchronize(dev->stream), "wait");
+  dev->raise_status(code);
 }
 
 std::vector<uint8_t> HbmTensor::to_host_bytes() const {
   auto dev = buffer_.device();
   dev->check();
   dev->activate();
+  if (dev->injected("copy")) dev->fail("copy to host failed (injected fault)");
   std::vector<uint8_t> out(nbytes());
+  int code = 0;
   if (!out.empty())
     dev->check_cuda(cudaMemcpyAsync(out.data(), buffer_.data(), out.size(), cudaMemcpyDeviceToHost,
                                     dev->stream),
                     "copy to host");
+  dev->check_cuda(cudaMemcpyAsync(&code, dev->status, sizeof(int), cudaMemcpyDeviceToHost, dev->stream),
+                  "status read");
   dev->check_cuda(cudaStreamSynchronize(dev->stream), "copy to host");
+  dev->raise_status(code);
   return out;
 }
 
@@ -383,6 +422,7 @@ HbmTensor HostTensor::to_hbm(const Device& device) const {
   HbmBuffer buf(device, std::max<size_t>(bytes_.size(), 8));
   auto dev = device.state();
   dev->activate();
+  if (dev->injected("copy")) dev->fail("copy to device failed (injected fault)");
   if (!bytes_.empty())
     dev->check_cuda(cudaMemcpyAsync(buf.data(), bytes_.data(), bytes_.size(), cudaMemcpyHostToDevice,
                                     dev->stream),

@@ -68,7 +68,17 @@ struct DeviceState {
   void fail(const std::string& what);              // poisons and raises DeviceError
   void check_cuda(cudaError_t err, const char* what);
   void check_status();                             // reads the kernel status word (synchronises)
+  // Raises (and poisons) when `code`, a status word read after the work that wrote it, is set.
+  void raise_status(int code);
   void activate() const;                           // cudaSetDevice(ordinal)
+
+  // Host-side fault injection (failure drills and tests; no GPU fault is made): after `countdown`
+  // more events of `fault_kind` the next one fails as the real failure would. Kinds: "launch" (the
+  // driver rejects a kernel launch), "copy" (a host-device copy fails), "peer" (a peer never
+  // answers a collective: its bounded wait gives up). FOA_FAULT=<kind>:<countdown> sets it at open.
+  std::string fault_kind;
+  int64_t fault_countdown = -1;
+  bool injected(const char* kind);
 };
 
 class Device {

@@ -43,20 +43,34 @@ __device__ void signal_all(const PeerBuffers& pb, int rank, int world, unsigned 
   for (int p = 0; p < world; ++p) st_release_sys(pb.signal[p] + rank, v);
 }
 
+// Waits until `*flag` reaches `v` (acquire, system scope); gives up after `limit_ns`, recording
+// kTimeoutPeer.
+__device__ bool wait_flag(const unsigned long long* flag, unsigned long long v, uint64_t start,
+                          uint64_t limit_ns, int* status) {
+  uint32_t spins = 0;
+  while (ld_acquire_sys(flag) < v) {
+    if ((++spins & 255u) == 0 && global_ns() - start > limit_ns) {
+      record_status(status, kTimeoutPeer);
+      return false;
+    }
+  }
+  return true;
+}
+
 __device__ bool wait_all(const PeerBuffers& pb, int rank, int world, unsigned long long v,
                          int* status) {
   const unsigned long long* s = pb.signal[rank];
   const uint64_t start = global_ns();
-  for (int p = 0; p < world; ++p) {
-    uint32_t spins = 0;
-    while (ld_acquire_sys(s + p) < v) {
-      if ((++spins & 255u) == 0 && global_ns() - start > kWaitLimitNs) {
-        record_status(status, kTimeoutPeer);
-        return false;
-      }
-    }
-  }
+  for (int p = 0; p < world; ++p)
+    if (!wait_flag(s + p, v, start, kWaitLimitNs, status)) return false;
   return true;
+}
+
+// The peers' bounded wait on one flag, with its own limit: a test makes it run out (a flag nothing
+// sets) and reads the status the kernel leaves, the context still usable.
+__global__ void wait_probe_kernel(const unsigned long long* flag, unsigned long long v, uint64_t limit_ns,
+                                  int* status) {
+  wait_flag(flag, v, global_ns(), limit_ns, status);
 }
 
 __device__ __forceinline__ float block_sum(float v, float* red) {
@@ -329,6 +343,13 @@ int tp_moe_combine_norm(const MoeCombineArgs& a, cudaStream_t stream) {
   const int vec = (a.cols / 8 + 255) / 256;
   auto kernel = vec <= 1 ? tp_moe_combine_kernel<1> : vec <= 2 ? tp_moe_combine_kernel<2> : tp_moe_combine_kernel<4>;
   return launch_pdl(kernel, dim3(a.rows), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -5;
+}
+
+int wait_probe(const unsigned long long* flag, unsigned long long value, uint64_t limit_ns, int* status,
+               cudaStream_t stream) {
+  if (limit_ns > kWaitLimitNs) return -2;
+  wait_probe_kernel<<<1, 1, 0, stream>>>(flag, value, limit_ns, status);
+  return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream) {

@@ -87,6 +87,11 @@ struct MoeCombineArgs {
 // * norm; every rank ends with the same rows.
 int tp_moe_combine_norm(const MoeCombineArgs& args, cudaStream_t stream);
 
+// One thread waits, bounded by `limit_ns` (at most the kernels' 2 s), until `*flag` reaches
+// `value`, recording the peer-timeout status when it gives up: the wait every peer flag uses.
+int wait_probe(const unsigned long long* flag, unsigned long long value, uint64_t limit_ns, int* status,
+               cudaStream_t stream);
+
 // Writes this call's epoch (stream-ordered, outside any captured graph).
 int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream_t stream);
 

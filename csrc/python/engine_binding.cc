@@ -15,6 +15,7 @@
 #include "engine/model.h"
 #include "engine/registry.h"
 #include "engine/runtime.h"
+#include "engine/trace.h"
 #include "kernels/gemm.cuh"
 #include "python/pytypes.h"
 
@@ -847,6 +848,38 @@ void bind_engine(py::module_& m) {
     r["two_shot"] = coll->reduce_target(rows, H).owner_rows > 0 ? 1.0 : 0.0;
     return r;
   });
+  m.def("_device_status", [](const Device& d) {
+    return py::make_tuple(reinterpret_cast<uint64_t>(d.state()->status), reinterpret_cast<uint64_t>(d.state()->stream));
+  }, py::arg("device"), "The device's kernel status word and stream (device addresses), for drills.");
+  // Host-side fault drills (see DeviceState::injected): no GPU fault is made.
+  m.def("_fault_inject", [](const Device& d, const std::string& kind, int64_t after) {
+    if (kind != "launch" && kind != "copy" && kind != "peer" && kind != "")
+      throw ValueError(kind + ": a fault is launch, copy or peer");
+    d.state()->fault_kind = kind;
+    d.state()->fault_countdown = kind.empty() ? -1 : after;
+  }, py::arg("device"), py::arg("kind"), py::arg("after") = 0,
+     "After `after` more events of `kind` the next one fails as the real failure would.");
+  // Tracing (FURIOSA_OPT_PROFILE / FOA_PROFILE = info | debug | trace; see trace.h).
+  m.def("_trace_level", []() {
+    static const char* names[] = {"off", "info", "debug", "trace"};
+    return std::string(names[static_cast<int>(trace_level())]);
+  });
+  m.def("_trace_set_level", [](const std::string& name) {
+    if (name != "off" && parse_trace_level(name) == TraceLevel::Off)
+      throw ValueError(name + ": a trace level is off, info, debug or trace");
+    set_trace_level(parse_trace_level(name));
+  }, py::arg("level"));
+  m.def("_trace_now_ns", []() { return trace_now_ns(); });
+  m.def("_trace_span", [](const std::string& name, const std::string& cat, uint64_t t0, uint64_t t1) {
+    Tracer::get().host_span(name, cat, t0, t1);
+  }, py::arg("name"), py::arg("cat"), py::arg("t0_ns"), py::arg("t1_ns"),
+     "Adds a host span (the clock of _trace_now_ns) to the trace, for a framework's own phases.");
+  m.def("_trace_flush", [](const std::string& path) {
+    py::gil_scoped_release nogil;
+    return Tracer::get().flush(path);
+  }, py::arg("path") = std::string(),
+     "Writes the spans so far as Chrome trace JSON (default: FURIOSA_OPT_OUT_DIR/trace-<pid>.json) "
+     "and clears them; returns the path, or '' when there was nothing to write.");
   m.def("_tp_connect", [](PyDecoder& d, const std::vector<py::bytes>& handles) {
     std::vector<std::string> hs;
     for (const auto& h : handles) hs.push_back(std::string(h));

@@ -10,6 +10,7 @@
 #include <tuple>
 #include <vector>
 
+#include "kernels/comm.cuh"
 #include "kernels/gemm.cuh"
 #include "kernels/ops.cuh"
 #include "kernels/attention.cuh"
@@ -347,6 +348,15 @@ void bind_ops(py::module_& m) {
           py::gil_scoped_release nogil;
           check(foa::paged_decode(a, as_stream(stream)), "paged_decode");
         });
+  m.def("wait_probe",
+        [](uint64_t flag, unsigned long long value, uint64_t limit_ns, uint64_t status, uint64_t stream) {
+          check(foa::wait_probe(as_ptr<const unsigned long long>(flag), value, limit_ns, as_ptr<int>(status),
+                                as_stream(stream)),
+                "wait_probe");
+        },
+        py::arg("flag"), py::arg("value"), py::arg("limit_ns"), py::arg("status"), py::arg("stream"),
+        "A bounded wait on a device flag (the peers' wait) with its own limit; the status word gets "
+        "the peer-timeout code when it gives up.");
   m.def("paged_prefill",
         [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
                     int num_segments, int q_heads, int kv_heads, int head_dim, float scale,

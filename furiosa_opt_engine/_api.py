@@ -25,6 +25,12 @@ vision_language = _native.vision_language
 for _name in ("decoder", "qwen3", "llama", "mistral", "qwen3_moe", "vision_language"):
     _sys.modules[f"furiosa_opt_engine.{_name}"] = getattr(_native, _name)
 
+if _native._trace_level() != "off":
+    # FURIOSA_OPT_PROFILE=info|debug|trace: the spans are written as a Chrome trace at exit.
+    import atexit as _atexit
+
+    _atexit.register(_native._trace_flush)
+
 __all__ = [
     "Checkpoint",
     "Decoder",

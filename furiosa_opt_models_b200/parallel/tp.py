@@ -10,6 +10,19 @@ RMSNorm; the vocabulary-parallel head ends in an exchange of (value, token) cand
 from __future__ import annotations
 
 
+def exchange_handles(handle: bytes) -> list:
+    """Every rank's heap handle, in rank order. A rank that has died or never joins ends the
+    exchange with the process group's error (its timeout bounds the wait), before any kernel of
+    this rank waits on that peer."""
+    import torch.distributed as dist
+
+    handles: list = [None] * dist.get_world_size()
+    dist.all_gather_object(handles, handle)
+    if any(h is None for h in handles):
+        raise RuntimeError("a rank gave no tensor-parallel heap handle")
+    return handles
+
+
 def attach(model, device) -> None:
     """Connects `model` (this rank's shard) to its peers; every rank calls it, in the same order."""
     import torch.distributed as dist
@@ -18,8 +31,7 @@ def attach(model, device) -> None:
 
     world, rank = dist.get_world_size(), dist.get_rank()
     handle = _native._tp_attach(model, world, rank)
-    handles: list = [None] * world
-    dist.all_gather_object(handles, handle)
+    handles = exchange_handles(handle)
     _native._tp_connect(model, handles)
     dist.barrier()
     # A device-side barrier through the heaps proves every peer mapping works before any call.
