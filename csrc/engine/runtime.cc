@@ -78,6 +78,20 @@ void DeviceState::release(void* ptr, size_t rounded) {
   pooled_bytes += rounded;
 }
 
+size_t DeviceState::trim() {
+  activate();
+  cudaStreamSynchronize(stream);
+  std::lock_guard<std::mutex> g(pool_mu);
+  size_t freed = 0;
+  for (auto& [sz, v] : pool) {
+    for (void* q : v) cudaFree(q);
+    freed += sz * v.size();
+  }
+  pool.clear();
+  pooled_bytes = 0;
+  return freed;
+}
+
 DeviceState::~DeviceState() {
   if (ordinal >= 0) {
     cudaSetDevice(ordinal);

@@ -62,6 +62,9 @@ struct DeviceState {
   size_t pooled_bytes = 0;
   void* allocate(size_t bytes, size_t* rounded);
   void release(void* ptr, size_t rounded);
+  // Returns every cached free block to the driver (after the stream's work): memory a dropped
+  // model or cache held becomes the GPU's again (sleep mode). Returns the bytes freed.
+  size_t trim();
   ~DeviceState();
 
   void check() const;                              // raises when poisoned

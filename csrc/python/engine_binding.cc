@@ -848,6 +848,10 @@ void bind_engine(py::module_& m) {
     r["two_shot"] = coll->reduce_target(rows, H).owner_rows > 0 ? 1.0 : 0.0;
     return r;
   });
+  m.def("_device_trim", [](const Device& d) {
+    py::gil_scoped_release nogil;
+    return d.state()->trim();
+  }, py::arg("device"), "Returns the device's cached free memory to the driver; the bytes freed.");
   m.def("_device_status", [](const Device& d) {
     return py::make_tuple(reinterpret_cast<uint64_t>(d.state()->status), reinterpret_cast<uint64_t>(d.state()->stream));
   }, py::arg("device"), "The device's kernel status word and stream (device addresses), for drills.");

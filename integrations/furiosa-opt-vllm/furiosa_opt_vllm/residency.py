@@ -1,0 +1,132 @@
+"""vLLM's sleep mode and weight reloads on the engine: device memory is freed by dropping what
+holds it (the loaded decoder, the KV cache) and returning the engine's cached blocks to the
+driver; waking loads or allocates it again (the reference's behaviour:
+integrations/furiosa-opt-vllm/furiosa_opt_vllm/residency.py).
+
+- Sleep mode needs `enable_sleep_mode`, under which a load keeps a host copy of the checkpoint's
+  tensors (`Checkpoint.read()`). Level 1 keeps that copy and waking loads from it; level 2 and
+  `discard` drop it, and waking reads the checkpoint's files again.
+- A released KV cache keeps its block count, from which waking allocates it at once (its contents
+  are gone: vLLM sleeps between requests).
+- Waking restores one tag after another, each awake once restored, so a retry after a failure
+  restores only what still sleeps. Releasing goes the other way (cache first).
+- `reload` loads the awake weights again from the checkpoint's files, into the device memory the
+  served ones free first; files that cannot be read keep the served weights.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+from .admission import Refused
+
+TAGS = ("weights", "kv_cache")
+
+
+@dataclass
+class Weights:
+    copy: object  # the host copy waking loads from, or None (read the files again)
+
+
+@dataclass
+class Storage:
+    blocks: int
+
+
+def _require(worker) -> None:
+    if not worker.model_config.enable_sleep_mode:
+        raise Refused("enable_sleep_mode",
+                      "sleeps only with enable_sleep_mode, whose loads keep the weights' copy for level 1")
+    if worker.model is None and "weights" not in worker.asleep:
+        raise RuntimeError("load_model must precede sleep mode")
+
+
+def _drop_model(worker) -> None:
+    """Releases the served weights (every rank in step: a tensor-parallel heap detaches)."""
+    model = worker.model
+    if model is None:
+        return
+    model.device.synchronize()
+    if worker.parallel_config.tensor_parallel_size > 1:
+        from furiosa_opt_models_b200.parallel import tp
+
+        tp.detach(model)
+    worker.model = None
+    if worker.runner is not None:
+        worker.runner.model = None
+    del model
+
+
+def _trim(worker) -> None:
+    from furiosa_opt_engine import _native
+
+    _native._device_trim(worker.device)
+
+
+def sleep(worker, level: int) -> None:
+    """Release the weights and the KV cache; level 1 keeps the weights' host copy."""
+    release(worker, TAGS, keep_copy=level == 1)
+
+
+def release(worker, tags, keep_copy: bool = False) -> None:
+    """Release the memory of the awake `tags`; released weights keep the host copy if asked."""
+    _require(worker)
+    for tag in reversed(TAGS):
+        if tag not in tags or tag in worker.asleep:
+            continue
+        if tag == "kv_cache":
+            if worker.cache is None:
+                raise RuntimeError("initialize_kv_cache must precede sleep mode")
+            worker.asleep[tag] = Storage(worker.cache.blocks)
+            worker.cache = None
+            if worker.runner is not None:
+                worker.runner.cache = None
+        else:
+            worker.asleep[tag] = Weights(worker.copy if keep_copy else None)
+            if not keep_copy:
+                worker.copy = None
+            _drop_model(worker)
+    _trim(worker)
+
+
+def wake_up(worker, tags) -> None:
+    """Restore the memory of `tags`, or of every tag."""
+    from furiosa_opt_engine import decoder as dec
+
+    from . import load
+
+    for tag in TAGS:
+        if tags is not None and tag not in tags:
+            continue
+        state = worker.asleep.get(tag)
+        if state is None:
+            continue
+        if isinstance(state, Weights):
+            copy = state.copy if state.copy is not None else load.host_copy(worker.model_config.model)
+            worker.model = load.load_from(copy, worker.device, worker.parallel_config.tensor_parallel_size)
+            worker.copy = copy
+            if worker.runner is not None:
+                worker.runner.model = worker.model
+        else:
+            worker.cache = dec.Cache(worker.model.cache, state.blocks)
+            if worker.runner is not None:
+                worker.runner.cache = worker.cache
+        del worker.asleep[tag]
+
+
+def reload(worker) -> None:
+    """Load the awake weights again from the checkpoint's files."""
+    from . import load
+
+    if "weights" in worker.asleep:
+        raise RuntimeError("reload_weights requires awake weights; wake them up first")
+    # The files are read before the served weights leave the device.
+    source = load.host_copy(worker.model_config.model) if worker.model_config.enable_sleep_mode else \
+        load.checkpoint(worker.model_config.model)
+    _drop_model(worker)
+    _trim(worker)
+    worker.model = load.load_from(source, worker.device, worker.parallel_config.tensor_parallel_size)
+    if worker.model_config.enable_sleep_mode:
+        worker.copy = source
+    if worker.runner is not None:
+        worker.runner.model = worker.model

@@ -11,6 +11,7 @@ import torch
 from vllm.v1.outputs import ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
+from . import admission, residency
 from . import cache as kv
 from . import load
 from .runner import Runner
@@ -22,6 +23,8 @@ class Worker(WorkerBase):
         super().__init__(vllm_config=vllm_config, local_rank=local_rank, rank=rank,
                          distributed_init_method=distributed_init_method, is_driver_worker=is_driver_worker)
         self.model = self.device = self.cache = self.runner = None
+        self.copy = None  # sleep mode: the host copy of the checkpoint the weights loaded from
+        self.asleep: dict = {}
         self.pending: ModelRunnerOutput | None = None
 
     # ------------------------------------------------------------------------ life cycle
@@ -35,8 +38,30 @@ class Worker(WorkerBase):
         ensure_model_parallel_initialized(pc.tensor_parallel_size, pc.pipeline_parallel_size)
 
     def load_model(self, *args, **kwargs) -> None:
-        self.model, self.device = load.load(self.model_config.model, self.rank,
-                                            self.parallel_config.tensor_parallel_size)
+        self.model, self.device, self.copy = load.load(self.model_config.model, self.rank,
+                                                       self.parallel_config.tensor_parallel_size,
+                                                       keep_copy=bool(self.model_config.enable_sleep_mode))
+
+    # ------------------------------------------------------------------------ sleep mode
+    def sleep(self, level: int = 1) -> None:
+        residency.sleep(self, level)
+
+    def wake_up(self, tags: list[str] | None = None) -> None:
+        residency.wake_up(self, tags)
+
+    def discard(self, tags: tuple[str, ...]) -> None:
+        residency.release(self, tags)
+
+    def reload_weights(self, weights_iterator: object = None, weights_path: str | None = None,
+                       is_checkpoint_format: bool = True) -> None:
+        """Load the weights again from the served checkpoint's files; the engine loads no other
+        source."""
+        for name, value, default in (("weights_iterator", weights_iterator, None),
+                                     ("weights_path", weights_path, None),
+                                     ("is_checkpoint_format", is_checkpoint_format, True)):
+            if value != default:
+                raise admission.Refused(name, "the engine reloads the served checkpoint's own files")
+        residency.reload(self)
 
     def determine_available_memory(self) -> int:
         free, total = torch.cuda.mem_get_info()

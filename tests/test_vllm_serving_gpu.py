@@ -41,3 +41,25 @@ def test_vllm_generates_through_the_engine(tmp_path):
             seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
     with open(out + ".refused") as f:
         assert json.load(f) is True
+
+
+def test_vllm_sleep_mode_frees_and_restores(tmp_path):
+    """vLLM's sleep mode through the plugin: level 1 keeps the host copy, level 2 reads the files,
+    reload_weights loads them again; the continuations are the same each time, and sleeping
+    returns the weights' and cache's device memory."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    synthetic.write(str(tmp_path / "m"), cfg, seed=12, std=0.05)
+    gen = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (6, 21)]
+    out = str(tmp_path / "sleep.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable, os.path.join(ROOT, "tests", "workers", "vllm_sleep.py"),
+                    str(tmp_path / "m"), out, json.dumps(prompts)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        r = json.load(f)
+    assert r["before"] == r["level1"] == r["level2"] == r["reloaded"]
+    assert r["freed_level1"] > 0
