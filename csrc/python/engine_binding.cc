@@ -9,6 +9,7 @@
 #include <pybind11/stl.h>
 
 #include <cstring>
+#include <optional>
 
 #include "engine/batch.h"
 #include "engine/comm.h"
@@ -221,12 +222,14 @@ void bind_engine(py::module_& m) {
       });
 
   py::class_<Device>(m, "Device", "An opened device; memory sizes are bytes per chip.")
-      .def(py::init([](const Placement& p) {
-             const int rank = process_rank(p.chips.size());
+      .def(py::init([](const Placement& p, std::optional<int> rank) {
+             // The process's rank among the placement's chips: given (a framework that runs several
+             // replicas in one process group), else the process group's rank.
+             const int r = rank ? *rank : process_rank(p.chips.size());
              py::gil_scoped_release nogil;
-             return Device(p.chips, static_cast<int>(p.pes_begin), static_cast<int>(p.pes_end), rank);
+             return Device(p.chips, static_cast<int>(p.pes_begin), static_cast<int>(p.pes_end), r);
            }),
-           py::arg("placement"))
+           py::arg("placement"), py::arg("rank") = py::none())
       .def_property_readonly("capacity", &Device::capacity)
       .def_property_readonly("available", &Device::available)
       .def_property_readonly("chips", &Device::chips)

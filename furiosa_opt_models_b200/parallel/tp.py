@@ -9,6 +9,15 @@ RMSNorm; the vocabulary-parallel head ends in an exchange of (value, token) cand
 
 from __future__ import annotations
 
+# The process group a placement's ranks form (None: the default group). A framework that runs
+# several replicas in one group (data parallelism) names each replica's tensor-parallel group.
+_group = None
+
+
+def set_group(group) -> None:
+    global _group
+    _group = group
+
 
 def exchange_handles(handle: bytes) -> list:
     """Every rank's heap handle, in rank order. A rank that has died or never joins ends the
@@ -16,8 +25,8 @@ def exchange_handles(handle: bytes) -> list:
     this rank waits on that peer."""
     import torch.distributed as dist
 
-    handles: list = [None] * dist.get_world_size()
-    dist.all_gather_object(handles, handle)
+    handles: list = [None] * dist.get_world_size(_group)
+    dist.all_gather_object(handles, handle, group=_group)
     if any(h is None for h in handles):
         raise RuntimeError("a rank gave no tensor-parallel heap handle")
     return handles
@@ -29,14 +38,14 @@ def attach(model, device) -> None:
 
     from furiosa_opt_engine import _native
 
-    world, rank = dist.get_world_size(), dist.get_rank()
+    world, rank = dist.get_world_size(_group), dist.get_rank(_group)
     handle = _native._tp_attach(model, world, rank)
     handles = exchange_handles(handle)
     _native._tp_connect(model, handles)
-    dist.barrier()
+    dist.barrier(group=_group)
     # A device-side barrier through the heaps proves every peer mapping works before any call.
     _native._tp_barrier(model)
-    dist.barrier()
+    dist.barrier(group=_group)
 
 
 def detach(model) -> None:
@@ -46,6 +55,6 @@ def detach(model) -> None:
     from furiosa_opt_engine import _native
 
     model.device.synchronize()
-    dist.barrier()
+    dist.barrier(group=_group)
     _native._tp_detach(model)
-    dist.barrier()
+    dist.barrier(group=_group)

@@ -24,10 +24,36 @@ def load_from(ck, device, world: int):
     return opts.load(ck, device)
 
 
-def load(model_path: str, rank: int, world: int, keep_copy: bool = False):
-    """(decoder, device, host copy or None): a load under sleep mode keeps the host copy it loaded."""
+def replica_chips(local_rank: int, tp_rank: int, tp: int, dp_rank: int = 0, visible: str | None = None) -> list:
+    """GPU ordinals of this worker's replica (`tp` chips, one per worker). FURIOSA_VISIBLE_CHIPS
+    (comma-separated ordinals) lists every replica's chips in turn: replica i takes chips
+    i*tp .. (i+1)*tp (the reference's data parallelism); without it the replica is the `tp`
+    consecutive GPUs whose tp_rank-th is this worker's local GPU."""
+    if visible:
+        chips = [int(c) for c in visible.split(",") if c.strip()]
+        mine = chips[dp_rank * tp : (dp_rank + 1) * tp]
+        if len(mine) != tp:
+            raise ValueError(f"FURIOSA_VISIBLE_CHIPS lists {len(chips)} chips; replica {dp_rank} of "
+                             f"{tp} chips needs {(dp_rank + 1) * tp}")
+        return mine
+    first = local_rank - tp_rank
+    if first < 0:
+        raise ValueError(f"local rank {local_rank} cannot hold tensor-parallel rank {tp_rank}")
+    return list(range(first, first + tp))
+
+
+def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips: list | None = None,
+         group=None):
+    """(decoder, device, host copy or None): this worker's chip of its replica (`chips`, its
+    tensor-parallel `rank` of `world`, joined in `group`); a load under sleep mode keeps the host
+    copy it loaded."""
     import furiosa_opt_engine as engine
 
-    device = engine.Device(engine.Placement(list(range(world)), range(8)))
+    chips = chips if chips is not None else list(range(world))
+    device = engine.Device(engine.Placement(chips, range(8)), rank=rank if world > 1 else 0)
+    if world > 1:
+        from furiosa_opt_models_b200.parallel import tp
+
+        tp.set_group(group)
     ck = host_copy(model_path) if keep_copy else checkpoint(model_path)
     return load_from(ck, device, world), device, (ck if keep_copy else None)

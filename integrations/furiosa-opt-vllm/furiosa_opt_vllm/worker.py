@@ -38,9 +38,18 @@ class Worker(WorkerBase):
         ensure_model_parallel_initialized(pc.tensor_parallel_size, pc.pipeline_parallel_size)
 
     def load_model(self, *args, **kwargs) -> None:
-        self.model, self.device, self.copy = load.load(self.model_config.model, self.rank,
-                                                       self.parallel_config.tensor_parallel_size,
-                                                       keep_copy=bool(self.model_config.enable_sleep_mode))
+        import os
+
+        from vllm.distributed import get_tensor_model_parallel_rank, get_tp_group
+
+        pc = self.parallel_config
+        tp_size = pc.tensor_parallel_size
+        tp_rank = get_tensor_model_parallel_rank() if tp_size > 1 else 0
+        chips = load.replica_chips(self.local_rank, tp_rank, tp_size, getattr(pc, "data_parallel_rank", 0) or 0,
+                                   os.environ.get("FURIOSA_VISIBLE_CHIPS"))
+        self.model, self.device, self.copy = load.load(
+            self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
+            chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None)
 
     # ------------------------------------------------------------------------ sleep mode
     def sleep(self, level: int = 1) -> None:

@@ -79,3 +79,17 @@ def test_entry_point_names_the_platform():
     import furiosa_opt_vllm
 
     assert furiosa_opt_vllm.register() == "furiosa_opt_vllm.platform.B200Platform"
+
+
+def test_replica_chips():
+    from furiosa_opt_vllm import load
+
+    # Consecutive GPUs of the replica whose tp_rank-th is this worker's.
+    assert load.replica_chips(local_rank=5, tp_rank=1, tp=2) == [4, 5]
+    assert load.replica_chips(local_rank=0, tp_rank=0, tp=1) == [0]
+    # FURIOSA_VISIBLE_CHIPS lists every replica's chips in turn.
+    assert load.replica_chips(0, 0, 2, dp_rank=1, visible="7,6,5,4") == [5, 4]
+    with pytest.raises(ValueError, match="replica 2 of 2 chips needs 6"):
+        load.replica_chips(0, 0, 2, dp_rank=2, visible="0,1,2,3")
+    with pytest.raises(ValueError, match="cannot hold tensor-parallel rank 3"):
+        load.replica_chips(local_rank=1, tp_rank=3, tp=4)
