@@ -20,8 +20,14 @@ class Refused(ValueError):
 CHIPS = (1, 2, 4, 8)
 
 
+# The engine's adapter slots a call holds and the rank every update holds (decoder.AdapterSpec).
+LORA_SLOTS = 2
+LORA_RANK = 32
+
+
 def options(pipeline: int, tensor: int, speculative: bool, lora: bool, kv_cache_dtype: str,
-            prefill_context: int = 1, decode_context: int = 1) -> None:
+            prefill_context: int = 1, decode_context: int = 1, max_loras: int = 1,
+            max_lora_rank: int = 16) -> None:
     """Engine-level options: parallelism, speculation, adapters, cache precision."""
     if pipeline != 1:
         raise Refused("pipeline_parallel_size", "pipeline parallelism is not served; use tensor parallelism")
@@ -32,7 +38,12 @@ def options(pipeline: int, tensor: int, speculative: bool, lora: bool, kv_cache_
     if speculative:
         raise Refused("speculative_config", "speculative decoding is not served")
     if lora:
-        raise Refused("enable_lora", "adapters are not served through this plugin")
+        if max_loras > LORA_SLOTS:
+            raise Refused("max_loras", f"{max_loras} adapters a step; an engine call holds {LORA_SLOTS}")
+        if max_lora_rank > LORA_RANK:
+            raise Refused("max_lora_rank", f"rank {max_lora_rank}; the engine serves ranks up to {LORA_RANK}")
+        if tensor != 1:
+            raise Refused("enable_lora", "adapters are served on one GPU a replica")
     if kv_cache_dtype not in ("auto", "bfloat16"):
         raise Refused("kv_cache_dtype", "the engine caches keys and values in BF16")
 

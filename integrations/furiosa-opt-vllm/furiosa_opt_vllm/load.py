@@ -15,12 +15,14 @@ def host_copy(model_path: str):
     return checkpoint(model_path).read()
 
 
-def load_from(ck, device, world: int):
+def load_from(ck, device, world: int, adapters: bool = False):
     import furiosa_opt_engine as engine
 
     opts = engine.LoadOptions()
     if world > 1:
         opts = opts.chips(world)
+    if adapters:
+        opts = opts.adapters()
     return opts.load(ck, device)
 
 
@@ -43,7 +45,7 @@ def replica_chips(local_rank: int, tp_rank: int, tp: int, dp_rank: int = 0, visi
 
 
 def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips: list | None = None,
-         group=None):
+         group=None, adapters: bool = False):
     """(decoder, device, host copy or None): this worker's chip of its replica (`chips`, its
     tensor-parallel `rank` of `world`, joined in `group`); a load under sleep mode keeps the host
     copy it loaded."""
@@ -56,4 +58,4 @@ def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips:
 
         tp.set_group(group)
     ck = host_copy(model_path) if keep_copy else checkpoint(model_path)
-    return load_from(ck, device, world), device, (ck if keep_copy else None)
+    return load_from(ck, device, world, adapters), device, (ck if keep_copy else None)

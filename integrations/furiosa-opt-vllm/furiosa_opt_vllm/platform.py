@@ -20,6 +20,8 @@ class B200Platform(NvmlCudaPlatform):
             tensor=pc.tensor_parallel_size,
             speculative=vllm_config.speculative_config is not None,
             lora=vllm_config.lora_config is not None,
+            max_loras=getattr(vllm_config.lora_config, "max_loras", 1) or 1,
+            max_lora_rank=getattr(vllm_config.lora_config, "max_lora_rank", 16) or 16,
             kv_cache_dtype=str(cc.cache_dtype),
             prefill_context=getattr(pc, "prefill_context_parallel_size", 1),
             decode_context=getattr(pc, "decode_context_parallel_size", 1),

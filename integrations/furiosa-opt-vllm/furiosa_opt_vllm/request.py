@@ -15,6 +15,7 @@ class State:
     computed: int
     table: BlockTable
     max_tokens: int | None = None
+    lora: object = None  # vLLM's LoRARequest of the sequence, or None
 
     def scheduled(self, n: int) -> list[int]:
         """The `n` tokens this step feeds (after the history)."""

@@ -103,10 +103,8 @@ def wake_up(worker, tags) -> None:
             continue
         if isinstance(state, Weights):
             copy = state.copy if state.copy is not None else load.host_copy(worker.model_config.model)
-            worker.model = load.load_from(copy, worker.device, worker.parallel_config.tensor_parallel_size)
+            _load(worker, copy)
             worker.copy = copy
-            if worker.runner is not None:
-                worker.runner.model = worker.model
         else:
             worker.cache = dec.Cache(worker.model.cache, state.blocks)
             if worker.runner is not None:
@@ -125,8 +123,21 @@ def reload(worker) -> None:
         load.checkpoint(worker.model_config.model)
     _drop_model(worker)
     _trim(worker)
-    worker.model = load.load_from(source, worker.device, worker.parallel_config.tensor_parallel_size)
+    _load(worker, source)
     if worker.model_config.enable_sleep_mode:
         worker.copy = source
+
+
+def _load(worker, source) -> None:
+    """Serve the weights of `source`; LoRA adapters loaded for the previous weights are read again
+    when a request names them (pins do not survive)."""
+    from . import load, lora
+
+    lora_config = getattr(worker, "lora_config", None)
+    worker.model = load.load_from(source, worker.device, worker.parallel_config.tensor_parallel_size,
+                                  adapters=lora_config is not None)
+    if lora_config is not None:
+        worker.adapters = lora.Adapters(lora_config.max_loras, lora_config.max_cpu_loras, worker.model.adapters)
     if worker.runner is not None:
         worker.runner.model = worker.model
+        worker.runner.adapters = getattr(worker, "adapters", None)

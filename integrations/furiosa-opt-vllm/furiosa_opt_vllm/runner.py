@@ -15,12 +15,13 @@ from .request import State
 
 
 class Runner:
-    def __init__(self, model, device, cache):
+    def __init__(self, model, device, cache, adapters=None):
         import furiosa_opt_engine as engine
         from furiosa_opt_engine import decoder as dec
 
         self.engine, self.dec = engine, dec
         self.model, self.device, self.cache = model, device, cache
+        self.adapters = adapters  # lora.Adapters when vLLM serves LoRA, else None
         self.states: dict[str, State] = {}
 
     # -------------------------------------------------------------------- scheduler bookkeeping
@@ -30,7 +31,8 @@ class Runner:
         for nr in so.scheduled_new_reqs:
             prompt = list(nr.prefill_token_ids if getattr(nr, "prefill_token_ids", None) else nr.prompt_token_ids)
             self.states[nr.req_id] = State(prompt, len(prompt), nr.num_computed_tokens,
-                                           BlockTable(first_group(nr.block_ids)))
+                                           BlockTable(first_group(nr.block_ids)),
+                                           lora=getattr(nr, "lora_request", None))
         cr = so.scheduled_cached_reqs
         resumed = getattr(cr, "resumed_req_ids", set()) or set()
         all_tokens = getattr(cr, "all_token_ids", {}) or {}
@@ -61,13 +63,22 @@ class Runner:
             keeps.append(st.samples_after(n))
             at += n
         tokens = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device)
+        # Adapters: each sequence naming a LoRA runs with its slot of this call's list.
+        slots, adapters = {}, None
+        if self.adapters is not None:
+            named = {rid: self.states[rid].lora for rid in order
+                     if self.states[rid].lora is not None and self.states[rid].lora.lora_int_id}
+            if named:
+                slots = self.adapters.activate(named)
+                adapters = list(self.adapters.slots)
         reqs, at = [], 0
         for rid, n, keep in zip(order, counts, keeps):
             st = self.states[rid]
             reqs.append(self.dec.Request([st.table.blocks], st.computed, tokens[at : at + n],
-                                         self.dec.Keep.LAST if keep else self.dec.Keep.NONE))
+                                         self.dec.Keep.LAST if keep else self.dec.Keep.NONE,
+                                         adapter=slots.get(rid)))
             at += n
-        out = self.model.forward(reqs, self.cache)
+        out = self.model.forward(reqs, self.cache, adapters)
         picked = out.to_host().numpy().tolist() if any(keeps) else []
         sampled, k = [], 0
         for rid, n, keep in zip(order, counts, keeps):

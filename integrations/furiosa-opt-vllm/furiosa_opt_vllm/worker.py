@@ -11,7 +11,7 @@ import torch
 from vllm.v1.outputs import ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
-from . import admission, residency
+from . import admission, lora, residency
 from . import cache as kv
 from . import load
 from .runner import Runner
@@ -24,6 +24,7 @@ class Worker(WorkerBase):
                          distributed_init_method=distributed_init_method, is_driver_worker=is_driver_worker)
         self.model = self.device = self.cache = self.runner = None
         self.copy = None  # sleep mode: the host copy of the checkpoint the weights loaded from
+        self.adapters = None  # lora.Adapters when vLLM serves LoRA
         self.asleep: dict = {}
         self.pending: ModelRunnerOutput | None = None
 
@@ -49,7 +50,11 @@ class Worker(WorkerBase):
                                    os.environ.get("FURIOSA_VISIBLE_CHIPS"))
         self.model, self.device, self.copy = load.load(
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
-            chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None)
+            chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
+            adapters=self.lora_config is not None)
+        if self.lora_config is not None:
+            self.adapters = lora.Adapters(self.lora_config.max_loras, self.lora_config.max_cpu_loras,
+                                          self.model.adapters)
 
     # ------------------------------------------------------------------------ sleep mode
     def sleep(self, level: int = 1) -> None:
@@ -86,7 +91,20 @@ class Worker(WorkerBase):
         from furiosa_opt_engine import decoder as dec
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
-        self.runner = Runner(self.model, self.device, self.cache)
+        self.runner = Runner(self.model, self.device, self.cache, self.adapters)
+
+    # ------------------------------------------------------------------------ LoRA
+    def add_lora(self, lora_request) -> bool:
+        return self.adapters.add(lora_request)
+
+    def remove_lora(self, lora_id: int) -> bool:
+        return self.adapters.remove(lora_id)
+
+    def pin_lora(self, lora_id: int) -> bool:
+        return self.adapters.pin(lora_id)
+
+    def list_loras(self) -> set[int]:
+        return self.adapters.ids() if self.adapters is not None else set()
 
     def compile_or_warm_up_model(self):
         from vllm.v1.worker.worker_base import CompilationTimes

@@ -57,7 +57,9 @@ def test_request_state_schedules_and_samples():
     (dict(pipeline=2, tensor=1, speculative=False, lora=False, kv_cache_dtype="auto"), "pipeline_parallel_size"),
     (dict(pipeline=1, tensor=3, speculative=False, lora=False, kv_cache_dtype="auto"), "tensor_parallel_size"),
     (dict(pipeline=1, tensor=1, speculative=True, lora=False, kv_cache_dtype="auto"), "speculative_config"),
-    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto"), "enable_lora"),
+    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto", max_loras=3), "max_loras"),
+    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto", max_lora_rank=64), "max_lora_rank"),
+    (dict(pipeline=1, tensor=2, speculative=False, lora=True, kv_cache_dtype="auto"), "enable_lora"),
     (dict(pipeline=1, tensor=1, speculative=False, lora=False, kv_cache_dtype="fp8"), "kv_cache_dtype"),
 ])
 def test_refusals_name_the_option(kwargs, option):
@@ -93,3 +95,39 @@ def test_replica_chips():
         load.replica_chips(0, 0, 2, dp_rank=2, visible="0,1,2,3")
     with pytest.raises(ValueError, match="cannot hold tensor-parallel rank 3"):
         load.replica_chips(local_rank=1, tp_rank=3, tp=4)
+
+
+def test_lora_slots_follow_lru_and_pins():
+    from types import SimpleNamespace
+
+    from furiosa_opt_vllm import lora
+
+    reads = []
+
+    def read(req):
+        reads.append(req.lora_int_id)
+        return f"adapter{req.lora_int_id}"
+
+    def req(i, inplace=False):
+        return SimpleNamespace(lora_int_id=i, lora_name=f"l{i}", load_inplace=inplace)
+
+    a = lora.Adapters(max_loras=2, max_cpu_loras=3, spec=None, read=read)
+    assert a.activate({"r1": req(1), "r2": req(2)}) == {"r1": 0, "r2": 1}
+    assert a.slots == ["adapter1", "adapter2"]
+    # A third adapter takes the least recently used slot not in the step.
+    assert a.activate({"r3": req(3)}) == {"r3": 0}
+    assert a.ids() == {1, 2, 3} and reads == [1, 2, 3]
+    # A fourth loaded adapter unloads the least recently used one (1).
+    a.add(req(4))
+    assert a.ids() == {2, 3, 4}
+    # Pinned adapters keep their slots; a step needing more slots than unpinned ones is refused.
+    a.pin(3)
+    a.pin(4)
+    with pytest.raises(RuntimeError, match="hold every slot"):
+        a.activate({"r5": req(5)})
+    assert a.remove(4) and not a.remove(4)
+    # Loading in place reads the checkpoint again.
+    a.add(req(3, inplace=True))
+    assert reads[-1] == 3
+    with pytest.raises(RuntimeError, match="above --max-loras"):
+        a.activate({"x": req(7), "y": req(8), "z": req(9)})

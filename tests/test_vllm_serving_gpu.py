@@ -63,3 +63,35 @@ def test_vllm_sleep_mode_frees_and_restores(tmp_path):
         r = json.load(f)
     assert r["before"] == r["level1"] == r["level2"] == r["reloaded"]
     assert r["freed_level1"] > 0
+
+
+def test_vllm_lora_adapters(tmp_path):
+    """Two PEFT LoRA adapters and none, in one vLLM batch: each continuation agrees with the dense
+    forward of its merged weights."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=13, std=0.05)
+    base = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    paths, merged = [], []
+    for i, (r, alpha) in enumerate([(8, 16.0), (16, 8.0)]):
+        d = str(tmp_path / f"lora{i}")
+        lora = synthetic.write_lora(d, cfg, r=r, alpha=alpha, seed=i + 1)
+        paths.append(d)
+        merged.append(synthetic.merge_lora(base, cfg, lora, r, alpha))
+    prompt = torch.randint(0, cfg["vocab"], (11,), generator=torch.Generator().manual_seed(6)).tolist()
+    out = str(tmp_path / "lora.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable, os.path.join(ROOT, "tests", "workers", "vllm_lora.py"),
+                    str(tmp_path / "m"), out, json.dumps(prompt), json.dumps(paths)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        tokens = json.load(f)
+    for toks, w in zip(tokens, merged + [base]):
+        seq = torch.tensor(prompt, dtype=torch.int32)
+        for t in toks:
+            logits = dense.forward(w, cfg, seq)[-1]
+            assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+            seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+    assert tokens[0] != tokens[2] or tokens[1] != tokens[2]
