@@ -877,10 +877,14 @@ void bind_engine(py::module_& m) {
     set_trace_level(parse_trace_level(name));
   }, py::arg("level"));
   m.def("_trace_now_ns", []() { return trace_now_ns(); });
-  m.def("_trace_span", [](const std::string& name, const std::string& cat, uint64_t t0, uint64_t t1) {
-    Tracer::get().host_span(name, cat, t0, t1);
-  }, py::arg("name"), py::arg("cat"), py::arg("t0_ns"), py::arg("t1_ns"),
-     "Adds a host span (the clock of _trace_now_ns) to the trace, for a framework's own phases.");
+  m.def("_trace_span", [](const std::string& name, const std::string& cat, uint64_t t0, uint64_t t1,
+                          const std::string& args) {
+    if (!args.empty() && (args.front() != '{' || args.back() != '}'))
+      throw ValueError("_trace_span: args is a JSON object");
+    Tracer::get().host_span(name, cat, t0, t1, args);
+  }, py::arg("name"), py::arg("cat"), py::arg("t0_ns"), py::arg("t1_ns"), py::arg("args") = std::string(),
+     "Adds a host span (the clock of _trace_now_ns) to the trace, for a framework's own phases; "
+     "`args` is a JSON object written as the span's args.");
   m.def("_trace_flush", [](const std::string& path) {
     py::gil_scoped_release nogil;
     return Tracer::get().flush(path);
