@@ -19,24 +19,30 @@ class Refused(ValueError):
 
 CHIPS = (1, 2, 4, 8)
 
+# Speculative methods served: drafts the target verifies greedily (furiosa_opt_vllm.speculation).
+SPECULATIVE_METHODS = ("ngram",)
+
 
 # The engine's adapter slots a call holds and the rank every update holds (decoder.AdapterSpec).
 LORA_SLOTS = 2
 LORA_RANK = 32
 
 
-def options(pipeline: int, tensor: int, speculative: bool, lora: bool, kv_cache_dtype: str,
+def options(pipeline: int, tensor: int, speculative: str | None, lora: bool, kv_cache_dtype: str,
             prefill_context: int = 1, decode_context: int = 1, max_loras: int = 1,
             max_lora_rank: int = 16) -> None:
-    """Engine-level options: parallelism, speculation, adapters, cache precision."""
+    """Engine-level options: parallelism, speculation (`speculative` is the speculative config's
+    method, or None), adapters, cache precision."""
     if pipeline != 1:
         raise Refused("pipeline_parallel_size", "pipeline parallelism is not served; use tensor parallelism")
     if tensor not in CHIPS:
         raise Refused("tensor_parallel_size", f"{tensor} GPUs; a replica runs on 1, 2, 4 or 8")
     if prefill_context != 1 or decode_context != 1:
         raise Refused("context_parallel_size", "context parallelism is not served")
-    if speculative:
-        raise Refused("speculative_config", "speculative decoding is not served")
+    if speculative is not None and speculative not in SPECULATIVE_METHODS:
+        raise Refused("speculative_config",
+                      f"method {speculative}: drafts come from n-gram prompt lookup (method 'ngram'); "
+                      "draft models are not served")
     if lora:
         if max_loras > LORA_SLOTS:
             raise Refused("max_loras", f"{max_loras} adapters a step; an engine call holds {LORA_SLOTS}")

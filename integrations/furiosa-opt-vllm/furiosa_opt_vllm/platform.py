@@ -18,7 +18,8 @@ class B200Platform(NvmlCudaPlatform):
         admission.options(
             pipeline=pc.pipeline_parallel_size,
             tensor=pc.tensor_parallel_size,
-            speculative=vllm_config.speculative_config is not None,
+            speculative=(None if vllm_config.speculative_config is None
+                         else str(vllm_config.speculative_config.method)),
             lora=vllm_config.lora_config is not None,
             max_loras=getattr(vllm_config.lora_config, "max_loras", 1) or 1,
             max_lora_rank=getattr(vllm_config.lora_config, "max_lora_rank", 16) or 16,

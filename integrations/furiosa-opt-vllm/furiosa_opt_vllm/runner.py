@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import numpy as np
 
+from . import speculation
 from .paging import BlockTable, first_group
 from .request import State
 
@@ -55,12 +56,20 @@ class Runner:
         if not order:
             return [], []
         counts = [int(so.num_scheduled_tokens[r]) for r in order]
+        spec = getattr(so, "scheduled_spec_decode_tokens", None) or {}
+        drafts = [list(spec.get(r, ())) for r in order]
         flat = np.empty(sum(counts), dtype=np.int32)
         keeps, at = [], 0
-        for rid, n in zip(order, counts):
+        for rid, n, d in zip(order, counts, drafts):
             st = self.states[rid]
-            flat[at : at + n] = st.scheduled(n)
-            keeps.append(st.samples_after(n))
+            known = n - len(d)
+            if d and not st.samples_after(known):
+                raise ValueError(f"{rid}: drafts scheduled before the newest token was fed")
+            flat[at : at + known] = st.scheduled(known)
+            flat[at + known : at + n] = d
+            # Rows the call returns: every row of a request with drafts (the target's token after
+            # each fed token), else the last row when it samples.
+            keeps.append(n if d else int(st.samples_after(known)))
             at += n
         tokens = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device)
         # Adapters: each sequence naming a LoRA runs with its slot of this call's list.
@@ -72,22 +81,26 @@ class Runner:
                 slots = self.adapters.activate(named)
                 adapters = list(self.adapters.slots)
         reqs, at = [], 0
-        for rid, n, keep in zip(order, counts, keeps):
+        for rid, n, keep, d in zip(order, counts, keeps, drafts):
             st = self.states[rid]
-            reqs.append(self.dec.Request([st.table.blocks], st.computed, tokens[at : at + n],
-                                         self.dec.Keep.LAST if keep else self.dec.Keep.NONE,
+            mode = self.dec.Keep.ALL if d else (self.dec.Keep.LAST if keep else self.dec.Keep.NONE)
+            reqs.append(self.dec.Request([st.table.blocks], st.computed, tokens[at : at + n], mode,
                                          adapter=slots.get(rid)))
             at += n
         out = self.model.forward(reqs, self.cache, adapters)
         picked = out.to_host().numpy().tolist() if any(keeps) else []
         sampled, k = [], 0
-        for rid, n, keep in zip(order, counts, keeps):
+        for rid, n, keep, d in zip(order, counts, keeps, drafts):
             st = self.states[rid]
             st.computed += n
-            if keep:
-                st.tokens.append(int(picked[k]))
-                sampled.append([int(picked[k])])
-                k += 1
+            rows = [int(t) for t in picked[k : k + keep]]
+            k += keep
+            if d:
+                # Every fed row came back; the targets start at the newest known token's row.
+                got = speculation.accept(d, rows[n - len(d) - 1 :])
+                st.computed -= len(d) - (len(got) - 1)
             else:
-                sampled.append([])
+                got = rows
+            st.tokens.extend(got)
+            sampled.append(got)
         return order, sampled

@@ -11,7 +11,7 @@ import torch
 from vllm.v1.outputs import ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
-from . import admission, lora, residency
+from . import admission, lora, residency, speculation
 from . import cache as kv
 from . import load
 from .runner import Runner
@@ -27,6 +27,8 @@ class Worker(WorkerBase):
         self.adapters = None  # lora.Adapters when vLLM serves LoRA
         self.asleep: dict = {}
         self.pending: ModelRunnerOutput | None = None
+        self.proposer = None  # speculation.Proposer when vLLM speculates
+        self.drafts = None  # the drafts proposed after the last step, for take_draft_token_ids
 
     # ------------------------------------------------------------------------ life cycle
     def init_device(self) -> None:
@@ -52,6 +54,8 @@ class Worker(WorkerBase):
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
             chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
             adapters=self.lora_config is not None)
+        if self.vllm_config.speculative_config is not None:
+            self.proposer = speculation.Proposer(self.vllm_config)
         if self.lora_config is not None:
             self.adapters = lora.Adapters(self.lora_config.max_loras, self.lora_config.max_cpu_loras,
                                           self.model.adapters)
@@ -130,7 +134,8 @@ class Worker(WorkerBase):
         return None
 
     def take_draft_token_ids(self):
-        return None
+        drafts, self.drafts = self.drafts, None
+        return drafts
 
     def shutdown(self) -> None:
         if self.model is not None and self.parallel_config.tensor_parallel_size > 1:
@@ -148,6 +153,11 @@ class Worker(WorkerBase):
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
                                          sampled_token_ids=sampled)
+        if self.proposer is not None:
+            from vllm.v1.outputs import DraftTokenIds
+
+            histories = [self.runner.states[r].tokens for r in ids]
+            self.drafts = DraftTokenIds(ids, self.proposer.propose(sampled, histories))
         return None
 
     def sample_tokens(self, grammar_output=None):

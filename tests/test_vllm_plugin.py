@@ -54,19 +54,19 @@ def test_request_state_schedules_and_samples():
 
 
 @pytest.mark.parametrize(("kwargs", "option"), [
-    (dict(pipeline=2, tensor=1, speculative=False, lora=False, kv_cache_dtype="auto"), "pipeline_parallel_size"),
-    (dict(pipeline=1, tensor=3, speculative=False, lora=False, kv_cache_dtype="auto"), "tensor_parallel_size"),
-    (dict(pipeline=1, tensor=1, speculative=True, lora=False, kv_cache_dtype="auto"), "speculative_config"),
-    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto", max_loras=3), "max_loras"),
-    (dict(pipeline=1, tensor=1, speculative=False, lora=True, kv_cache_dtype="auto", max_lora_rank=64), "max_lora_rank"),
-    (dict(pipeline=1, tensor=2, speculative=False, lora=True, kv_cache_dtype="auto"), "enable_lora"),
-    (dict(pipeline=1, tensor=1, speculative=False, lora=False, kv_cache_dtype="fp8"), "kv_cache_dtype"),
+    (dict(pipeline=2, tensor=1, speculative=None, lora=False, kv_cache_dtype="auto"), "pipeline_parallel_size"),
+    (dict(pipeline=1, tensor=3, speculative=None, lora=False, kv_cache_dtype="auto"), "tensor_parallel_size"),
+    (dict(pipeline=1, tensor=1, speculative="eagle", lora=False, kv_cache_dtype="auto"), "speculative_config"),
+    (dict(pipeline=1, tensor=1, speculative=None, lora=True, kv_cache_dtype="auto", max_loras=3), "max_loras"),
+    (dict(pipeline=1, tensor=1, speculative=None, lora=True, kv_cache_dtype="auto", max_lora_rank=64), "max_lora_rank"),
+    (dict(pipeline=1, tensor=2, speculative=None, lora=True, kv_cache_dtype="auto"), "enable_lora"),
+    (dict(pipeline=1, tensor=1, speculative=None, lora=False, kv_cache_dtype="fp8"), "kv_cache_dtype"),
 ])
 def test_refusals_name_the_option(kwargs, option):
     with pytest.raises(admission.Refused) as e:
         admission.options(**kwargs)
     assert e.value.option == option
-    admission.options(pipeline=1, tensor=8, speculative=False, lora=False, kv_cache_dtype="auto")
+    admission.options(pipeline=1, tensor=8, speculative=None, lora=False, kv_cache_dtype="auto")
 
 
 def test_sampling_refusals():

@@ -95,3 +95,36 @@ def test_vllm_lora_adapters(tmp_path):
             assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
             seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
     assert tokens[0] != tokens[2] or tokens[1] != tokens[2]
+
+
+def test_vllm_ngram_speculation_is_exact(tmp_path):
+    """n-gram speculative decoding through the plugin: drafts verified greedily by the engine give
+    the same continuations as the dense forward of the checkpoint, and vLLM proposed drafts."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=13, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    gen = torch.Generator().manual_seed(6)
+    # Repeating prompts, so prompt lookup finds n-grams to draft from.
+    prompts = [[int(x) for x in torch.randint(0, cfg["vocab"], (4,), generator=gen)] * 6,
+               torch.randint(0, cfg["vocab"], (19,), generator=gen).tolist()]
+    out = str(tmp_path / "spec.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable,
+                    os.path.join(ROOT, "tests", "workers", "vllm_speculate.py"), str(tmp_path / "m"), out,
+                    json.dumps(prompts)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        got = json.load(f)
+    assert [len(t) for t in got["tokens"]] == [24, 24]
+    for p, toks in zip(prompts, got["tokens"]):
+        seq = torch.tensor(p, dtype=torch.int32)
+        for t in toks:
+            logits = dense.forward(w, cfg, seq)[-1]
+            assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+            seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+    drafts = got["counters"].get("vllm:spec_decode_num_draft_tokens")
+    if drafts is not None:
+        assert drafts > 0
