@@ -180,7 +180,8 @@ void DecoderModel::allocate_weights() {
   // The embedding is whole on every chip, padded to the chips' head shards; the head is the
   // chip's vocabulary shard (a view into the embedding when they are tied).
   plan.push_back({"embed", {static_cast<int64_t>(vocab_l_) * tp_, H}});
-  if (!cfg_.tied) plan.push_back({"lm_head", {vocab_l_, H}});
+  // Only a decoder that returns tokens reads a vocabulary head.
+  if (!cfg_.tied && cfg_.output == Output::Tokens) plan.push_back({"lm_head", {vocab_l_, H}});
   plan.push_back({"final_norm", {H}});
   if (cfg_.output == Output::Scores) plan.push_back({"score", {cfg_.labels, H}});
   for (int l = 0; l < cfg_.layers; ++l) {
@@ -269,7 +270,7 @@ void DecoderModel::allocate_weights() {
     }
     weights_[plan[i].first] = w;
   }
-  if (cfg_.tied) {
+  if (cfg_.tied && cfg_.output == Output::Tokens) {
     WeightSlot head = weights_["embed"];
     head.ptr += static_cast<size_t>(vocab_begin_) * H;
     head.shape = {vocab_l_, H};

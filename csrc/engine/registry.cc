@@ -680,14 +680,19 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
   const bool quantized = cfg.weight_format == "fp8_block" || cfg.weight_format == "nvfp4" ||
                          cfg.weight_format == "nvfp4_a4";
 
-  const std::string pre = "model.";
+  // Names under "model." (a causal or classifier checkpoint); a base model saved on its own
+  // (sentence-embedding checkpoints) names its tensors from the root.
+  const std::string pre = (cfg.output == Output::Hidden && ck.get("model.embed_tokens.weight") == nullptr &&
+                           ck.get("embed_tokens.weight") != nullptr)
+                              ? ""
+                              : "model.";
   // Embedding (whole on every chip) and head (this chip's vocabulary rows).
   if (auto* t = take(pre + "embed_tokens.weight", {cfg.vocab, H})) {
     image("embed");
     copy_rows(Source(t), 0, cfg.vocab, 0, 0, H, H);
     upload("embed");
   }
-  if (!cfg.tied) {
+  if (!cfg.tied && cfg.output == Output::Tokens) {
     if (auto* t = take("lm_head.weight", {cfg.vocab, H})) {
       image("lm_head");
       const int64_t n = model.vocab_end() - model.vocab_begin();
@@ -695,7 +700,9 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       upload("lm_head");
     }
   } else if (ck.get("lm_head.weight")) {
-    used["lm_head.weight"] = true;  // a tied head the checkpoint also stores
+    // A tied head the checkpoint also stores, or the head of a causal checkpoint loaded as its
+    // base model: read by no call.
+    used["lm_head.weight"] = true;
   }
   if (auto* t = take(pre + "norm.weight", {H})) {
     image("final_norm");

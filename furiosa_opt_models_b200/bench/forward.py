@@ -107,7 +107,7 @@ def main(argv=None) -> int:
     device = engine.Device(engine.Placement([0], range(8)))
     model = _native._synthetic_decoder(device, cfg, tp=1, rank=0, seed=0, std=0.02)
     spec = model.cache
-    window = spec.groups[0].window
+    window = model.window  # positions a sequence reaches at most
     block = spec.pools[spec.groups[0].pool].block
     lengths, widths = workloads(inv, args.tier)
     if args.max_input is not None:

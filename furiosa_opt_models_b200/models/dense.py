@@ -61,9 +61,10 @@ def _gate_up(x: torch.Tensor, w) -> tuple[torch.Tensor, torch.Tensor]:
     return blocks[:, :, 0].reshape(T, -1), blocks[:, :, 1].reshape(T, -1)
 
 
-def forward(w: dict, cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> torch.Tensor:
+def forward(w: dict, cfg: dict, ids: torch.Tensor, round_bf16: bool = True, head: bool = True) -> torch.Tensor:
     """Logits [len(ids), vocab] of one sequence from position 0, FP32 math; with `round_bf16` every
-    stored activation is rounded to BF16 where the engine's GPU kernels store BF16."""
+    stored activation is rounded to BF16 where the engine's GPU kernels store BF16. Without `head`,
+    the final-normed hidden rows [len(ids), hidden] (a base model's output)."""
     rb = (lambda t: t.bfloat16().float()) if round_bf16 else (lambda t: t)
     H, D = cfg["hidden"], cfg.get("head_dim", 128)
     qh, kvh = cfg["q_heads"], cfg["kv_heads"]
@@ -100,5 +101,7 @@ def forward(w: dict, cfg: dict, ids: torch.Tensor, round_bf16: bool = True) -> t
         act = rb(reference.swiglu(g, u)) if round_bf16 else torch.nn.functional.silu(g) * u
         x = rb(x + linear(act, w[p + "down"]))
     h = rb(reference.rmsnorm(x, w["final_norm"], eps))
-    head = w["lm_head"] if "lm_head" in w else w["embed"]
-    return h @ head[: cfg["vocab"]].float().T
+    if not head:
+        return h
+    out = w["lm_head"] if "lm_head" in w else w["embed"]
+    return h @ out[: cfg["vocab"]].float().T
