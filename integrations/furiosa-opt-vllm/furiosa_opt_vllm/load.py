@@ -15,10 +15,21 @@ def host_copy(model_path: str):
     return checkpoint(model_path).read()
 
 
-def load_from(ck, device, world: int, adapters: bool = False):
+def architectures(model_path: str) -> list[str]:
+    """The classes the checkpoint's config.json declares."""
+    import json
+    import os
+
+    with open(os.path.join(model_path, "config.json")) as f:
+        return list(json.load(f).get("architectures") or [])
+
+
+def load_from(ck, device, world: int, adapters: bool = False, architecture: str | None = None):
     import furiosa_opt_engine as engine
 
     opts = engine.LoadOptions()
+    if architecture is not None:
+        opts = opts.architecture(architecture)
     if world > 1:
         opts = opts.chips(world)
     if adapters:
@@ -45,10 +56,11 @@ def replica_chips(local_rank: int, tp_rank: int, tp: int, dp_rank: int = 0, visi
 
 
 def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips: list | None = None,
-         group=None, adapters: bool = False):
+         group=None, adapters: bool = False, architecture: str | None = None):
     """(decoder, device, host copy or None): this worker's chip of its replica (`chips`, its
     tensor-parallel `rank` of `world`, joined in `group`); a load under sleep mode keeps the host
-    copy it loaded."""
+    copy it loaded. `architecture` overrides the config's class (a causal checkpoint pooled as its
+    base model)."""
     import furiosa_opt_engine as engine
 
     chips = chips if chips is not None else list(range(world))
@@ -58,4 +70,4 @@ def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips:
 
         tp.set_group(group)
     ck = host_copy(model_path) if keep_copy else checkpoint(model_path)
-    return load_from(ck, device, world, adapters), device, (ck if keep_copy else None)
+    return load_from(ck, device, world, adapters, architecture), device, (ck if keep_copy else None)

@@ -45,6 +45,11 @@ class B200Platform(NvmlCudaPlatform):
     @classmethod
     def validate_request(cls, processed_inputs, params) -> None:
         if getattr(params, "temperature", None) is None:
-            raise admission.Refused("pooling", "the engine serves generation")
+            from . import pooling
+
+            task = getattr(params, "task", None)
+            if task is not None and task not in pooling.TASKS:
+                raise admission.Refused("task", f"{task}: pooling serves {', '.join(pooling.TASKS)}")
+            return
         admission.sampling(params.temperature, params.top_k, params.top_p, params.n, params.logprobs,
                            params.prompt_logprobs)

@@ -16,6 +16,7 @@ class State:
     table: BlockTable
     max_tokens: int | None = None
     lora: object = None  # vLLM's LoRARequest of the sequence, or None
+    pool: object = None  # pooling.Pool of a pooling request, or None
 
     def scheduled(self, n: int) -> list[int]:
         """The `n` tokens this step feeds (after the history)."""

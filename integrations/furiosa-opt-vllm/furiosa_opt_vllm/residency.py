@@ -135,7 +135,7 @@ def _load(worker, source) -> None:
 
     lora_config = getattr(worker, "lora_config", None)
     worker.model = load.load_from(source, worker.device, worker.parallel_config.tensor_parallel_size,
-                                  adapters=lora_config is not None)
+                                  adapters=lora_config is not None, architecture=getattr(worker, "architecture", None))
     if lora_config is not None:
         worker.adapters = lora.Adapters(lora_config.max_loras, lora_config.max_cpu_loras, worker.model.adapters)
     if worker.runner is not None:

@@ -11,7 +11,7 @@ import torch
 from vllm.v1.outputs import ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
-from . import admission, lora, residency, speculation
+from . import admission, lora, pooling, residency, speculation
 from . import cache as kv
 from . import load
 from .runner import Runner
@@ -28,6 +28,7 @@ class Worker(WorkerBase):
         self.asleep: dict = {}
         self.pending: ModelRunnerOutput | None = None
         self.proposer = None  # speculation.Proposer when vLLM speculates
+        self.pooling = getattr(self.model_config, "runner_type", "generate") == "pooling"
         self.drafts = None  # the drafts proposed after the last step, for take_draft_token_ids
 
     # ------------------------------------------------------------------------ life cycle
@@ -50,10 +51,19 @@ class Worker(WorkerBase):
         tp_rank = get_tensor_model_parallel_rank() if tp_size > 1 else 0
         chips = load.replica_chips(self.local_rank, tp_rank, tp_size, getattr(pc, "data_parallel_rank", 0) or 0,
                                    os.environ.get("FURIOSA_VISIBLE_CHIPS"))
+        architecture = None
+        if self.pooling:
+            declared = load.architectures(self.model_config.model)
+            architecture = next((pooling.base_architecture(a) for a in declared
+                                 if pooling.base_architecture(a) is not None), None)
+            if architecture is None:
+                raise admission.Refused("runner", f"pooling serves Qwen3 causal and classifier checkpoints, "
+                                                  f"not {', '.join(declared)}")
+        self.architecture = architecture
         self.model, self.device, self.copy = load.load(
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
             chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
-            adapters=self.lora_config is not None)
+            adapters=self.lora_config is not None, architecture=architecture)
         if self.vllm_config.speculative_config is not None:
             self.proposer = speculation.Proposer(self.vllm_config)
         if self.lora_config is not None:
@@ -95,7 +105,7 @@ class Worker(WorkerBase):
         from furiosa_opt_engine import decoder as dec
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
-        self.runner = Runner(self.model, self.device, self.cache, self.adapters)
+        self.runner = Runner(self.model, self.device, self.cache, self.adapters, self.pooling_config())
 
     # ------------------------------------------------------------------------ LoRA
     def add_lora(self, lora_request) -> bool:
@@ -116,7 +126,20 @@ class Worker(WorkerBase):
         return CompilationTimes(0.0, 0.0)
 
     def get_supported_tasks(self):
-        return ("generate",)
+        if not self.pooling:
+            return ("generate",)
+        return ("classify",) if self.model.output.name == "SCORES" else ("embed",)
+
+    def pooling_config(self) -> dict | None:
+        """The runner's pooling settings: the task the model serves, vLLM's pooling type and, for
+        a classifier, its labels."""
+        if not self.pooling:
+            return None
+        pc = self.model_config.pooler_config
+        method = getattr(pc, "seq_pooling_type", None) or getattr(pc, "pooling_type", None) or "LAST"
+        task = self.get_supported_tasks()[0]
+        labels = int(getattr(self.model_config.hf_config, "num_labels", 0) or 0) if task == "classify" else 0
+        return {"task": task, "method": str(getattr(method, "value", method)), "labels": labels}
 
     def check_health(self) -> None:
         pass
@@ -152,7 +175,8 @@ class Worker(WorkerBase):
             return None
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
-                                         sampled_token_ids=sampled)
+                                         sampled_token_ids=sampled,
+                                         pooler_output=list(self.runner.pooled) if self.pooling else None)
         if self.proposer is not None:
             from vllm.v1.outputs import DraftTokenIds
 

@@ -31,7 +31,7 @@ def worker(monkeypatch):
 
     trims = []
     monkeypatch.setattr(_native, "_device_trim", lambda device: trims.append(device))
-    monkeypatch.setattr(load, "load_from", lambda ck, device, world, adapters=False: FakeModel(ck))
+    monkeypatch.setattr(load, "load_from", lambda ck, device, world, adapters=False, architecture=None: FakeModel(ck))
     monkeypatch.setattr(load, "host_copy", lambda path: f"copy of {path}")
     monkeypatch.setattr(load, "checkpoint", lambda path: f"files of {path}")
     monkeypatch.setattr(dec, "Cache", FakeCache)

@@ -128,3 +128,45 @@ def test_vllm_ngram_speculation_is_exact(tmp_path):
     drafts = got["counters"].get("vllm:spec_decode_num_draft_tokens")
     if drafts is not None:
         assert drafts > 0
+
+
+@pytest.mark.parametrize("mode", ["embed", "classify"])
+def test_vllm_pooling_through_the_engine(tmp_path, mode):
+    """vLLM's pooling runner through the plugin: `embed` on a causal checkpoint served as its base
+    model (the normalized final hidden row of each prompt), `classify` on a sequence classifier
+    (softmax of its label scores), against the dense forward."""
+    pytest.importorskip("vllm")
+    from safetensors.torch import save_file
+
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    d = tmp_path / "m"
+    hf = synthetic.write(str(d), cfg, seed=14, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    score = None
+    if mode == "classify":
+        score = (torch.randn(3, cfg["hidden"], generator=torch.Generator().manual_seed(8)) * 0.05).bfloat16()
+        save_file(dict(hf, **{"score.weight": score}), str(d / "model.safetensors"))
+        conf = json.load(open(d / "config.json"))
+        conf.update(architectures=["Qwen3ForSequenceClassification"], id2label={"0": "a", "1": "b", "2": "c"},
+                    label2id={"a": 0, "b": 1, "c": 2})
+        json.dump(conf, open(d / "config.json", "w"))
+    gen = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (7, 30)]
+    out = str(tmp_path / "pool.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable, os.path.join(ROOT, "tests", "workers", "vllm_pool.py"),
+                    mode, str(d), out, json.dumps(prompts)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        got = json.load(f)
+    for p, g in zip(prompts, got):
+        h = dense.forward(w, cfg, torch.tensor(p), head=False)[-1]
+        if mode == "embed":
+            want = torch.nn.functional.normalize(h, dim=-1)
+        else:
+            want = torch.softmax(h @ score.float().T, -1)
+        g = torch.tensor(g)
+        assert g.shape == want.shape
+        assert torch.allclose(g, want, atol=2e-2), (g, want)
