@@ -1,0 +1,60 @@
+"""The plugin's section of vLLM's `additional_config`: the options under its `furiosa` key
+(the reference's integrations/furiosa-opt-vllm/furiosa_opt_vllm/additional.py: the same key and
+the same strict parsing, with this engine's options).
+
+- `cuda_graphs` (default true): decode calls replay CUDA graphs the engine captured per call
+  shape; false runs every call eagerly (for profiling).
+- `draft_placement` (the reference's chips for a draft model): draft models are not served, so
+  setting it is refused.
+"""
+
+from __future__ import annotations
+
+from typing import Annotated, ClassVar
+
+from pydantic import BaseModel, ConfigDict, Field, ValidationError, field_validator
+
+from .admission import Refused
+
+Index = Annotated[int, Field(strict=True, ge=0)]
+
+
+class Placement(BaseModel):
+    """GPU ordinals in rank order, and the half-open range `pes` the reference splits a chip by
+    (one range on a GPU)."""
+
+    model_config: ClassVar[ConfigDict] = ConfigDict(frozen=True, extra="forbid")
+
+    chips: tuple[Index, ...]
+    pes: tuple[Index, Index] = (0, 8)
+
+    @field_validator("chips")
+    @classmethod
+    def distinct(cls, chips: tuple[int, ...]) -> tuple[int, ...]:
+        if not chips or len(set(chips)) < len(chips):
+            raise ValueError("one or more distinct chips")
+        return chips
+
+
+class Section(BaseModel):
+    """The plugin's options, each at its default unless `additional_config["furiosa"]` sets it."""
+
+    model_config: ClassVar[ConfigDict] = ConfigDict(frozen=True, extra="forbid")
+
+    cuda_graphs: Annotated[bool, Field(strict=True)] = True
+    draft_placement: Placement | None = None
+
+    @classmethod
+    def parse(cls, config) -> Section:
+        """The section of `config`'s `additional_config` (defaults without a `furiosa` key); a
+        malformed section or an option the engine does not serve is refused with its path."""
+        raw = getattr(config, "additional_config", None) or {}
+        try:
+            section = cls.model_validate(raw.get("furiosa", {}) if isinstance(raw, dict) else {})
+        except ValidationError as e:
+            d = e.errors()[0]
+            path = ".".join(map(str, ("additional_config", "furiosa", *d["loc"])))
+            raise Refused(path, d["msg"]) from None
+        if section.draft_placement is not None:
+            raise Refused("additional_config.furiosa.draft_placement", "draft models are not served")
+        return section

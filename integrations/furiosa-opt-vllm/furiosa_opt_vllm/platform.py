@@ -27,6 +27,9 @@ class B200Platform(NvmlCudaPlatform):
             prefill_context=getattr(pc, "prefill_context_parallel_size", 1),
             decode_context=getattr(pc, "decode_context_parallel_size", 1),
         )
+        from .additional import Section
+
+        Section.parse(vllm_config)
         super().check_and_update_config(vllm_config)
         pc.worker_cls = "furiosa_opt_vllm.worker.Worker"
         cc.block_size = 16

@@ -64,6 +64,10 @@ class Worker(WorkerBase):
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
             chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
             adapters=self.lora_config is not None, architecture=architecture)
+        from .additional import Section
+
+        if not Section.parse(self.vllm_config).cuda_graphs:
+            self.model.set_graphs(False)
         if self.vllm_config.speculative_config is not None:
             self.proposer = speculation.Proposer(self.vllm_config)
         if self.lora_config is not None:

@@ -131,3 +131,24 @@ def test_lora_slots_follow_lru_and_pins():
     assert reads[-1] == 3
     with pytest.raises(RuntimeError, match="above --max-loras"):
         a.activate({"x": req(7), "y": req(8), "z": req(9)})
+
+
+def test_additional_config_section():
+    from types import SimpleNamespace
+
+    from furiosa_opt_vllm.additional import Section
+
+    assert Section.parse(SimpleNamespace(additional_config={})).cuda_graphs is True
+    assert Section.parse(SimpleNamespace(additional_config={"other": 1})).cuda_graphs is True
+    assert Section.parse(SimpleNamespace(additional_config={"furiosa": {"cuda_graphs": False}})).cuda_graphs is False
+    with pytest.raises(admission.Refused) as e:
+        Section.parse(SimpleNamespace(additional_config={"furiosa": {"unknown": 1}}))
+    assert e.value.option == "additional_config.furiosa.unknown"
+    with pytest.raises(admission.Refused) as e:
+        Section.parse(SimpleNamespace(additional_config={"furiosa": {"cuda_graphs": "yes"}}))
+    assert e.value.option == "additional_config.furiosa.cuda_graphs"
+    with pytest.raises(admission.Refused, match="draft models are not served"):
+        Section.parse(SimpleNamespace(additional_config={"furiosa": {"draft_placement": {"chips": [1]}}}))
+    with pytest.raises(admission.Refused) as e:
+        Section.parse(SimpleNamespace(additional_config={"furiosa": {"draft_placement": {"chips": [1, 1]}}}))
+    assert e.value.option.startswith("additional_config.furiosa.draft_placement")
