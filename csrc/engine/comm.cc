@@ -234,4 +234,32 @@ void PeerCollectives::barrier(cudaStream_t stream) {
     device_.state()->fail("tensor-parallel barrier launch failed");
 }
 
+void PeerCollectives::gather_rows(const __nv_bfloat16* src, int rows, int cols, bool exchange,
+                                  __nv_bfloat16* dst, cudaStream_t stream) {
+  if (!connected_) throw ValueError("gather_rows: the collectives are not connected");
+  if (rows <= 0 || cols <= 0 || cols % 8 != 0)
+    throw ValueError("gather_rows: rows and columns positive, columns a multiple of 8");
+  if (exchange && rows % world_ != 0)
+    throw ValueError("gather_rows: an exchange splits its rows evenly over the ranks");
+  const int64_t elems = static_cast<int64_t>(rows) * cols * world_;
+  if (elems > rows_ * cols_)
+    throw ValueError("gather_rows: " + std::to_string(elems) + " gathered values pass the landing buffer of " +
+                     std::to_string(rows_ * cols_));
+  barrier(stream);
+  foa::RowsArgs a{};
+  a.peers = peers_;
+  a.src = src;
+  a.rows = rows;
+  a.cols = cols;
+  a.rank = rank_;
+  a.world = world_;
+  a.exchange = exchange ? 1 : 0;
+  if (foa::tp_push_rows(a, stream) != 0) device_.state()->fail("tensor-parallel row push launch failed");
+  barrier(stream);
+  device_.state()->check_cuda(cudaMemcpyAsync(dst, peers_.hidden[rank_], static_cast<size_t>(elems) * 2,
+                                              cudaMemcpyDeviceToDevice, stream),
+                              "gathered rows copy");
+  barrier(stream);
+}
+
 }  // namespace foa::engine

@@ -40,6 +40,13 @@ class PeerCollectives : public Collectives {
                         int cols, cudaStream_t stream) override;
   // A device-side barrier of every rank (used before the heap is released).
   void barrier(cudaStream_t stream);
+  // The reference's AllGather (exchange false: `dst` [rows * world, cols], the parts in rank
+  // order) or Exchange (true: `dst` [rows / world, cols * world], rank t holding rows t * rows /
+  // world .. of every rank's columns) of BF16 rows, between calls; every rank calls it in the same
+  // order with the same shape. The parts land in the heap's hidden buffers between two barriers,
+  // after one that keeps a rank from writing into a peer still in its call.
+  void gather_rows(const __nv_bfloat16* src, int rows, int cols, bool exchange, __nv_bfloat16* dst,
+                   cudaStream_t stream);
   // Measurement: the add_norm kernels write milestone timestamps here (null: none).
   void set_trace(unsigned long long* trace) { trace_ = trace; }
   // Fault drill (DeviceState::injected "peer"): the next collective reports a silent peer.

@@ -16,6 +16,8 @@
 // peer's signal array (release, system scope) and waits, bounded, until every slot of its own
 // array has reached the value. A wait that gives up records kTimeoutPeer and returns.
 
+#include <algorithm>
+
 #include "comm.cuh"
 #include "launch.cuh"
 #include "sm100.cuh"
@@ -335,6 +337,30 @@ __global__ void tp_barrier_kernel(PeerBuffers peers, const unsigned long long* e
 
 __global__ void set_u64_kernel(unsigned long long* p, unsigned long long v) { *p = v; }
 
+__global__ void __launch_bounds__(256) tp_push_rows_kernel(const RowsArgs a) {
+  pdl_wait();
+  const int vec = a.cols / 8;  // 16-byte vectors a row
+  const long total = (long)a.rows * vec;
+  const int part = a.exchange ? a.rows / a.world : a.rows;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int r = static_cast<int>(i / vec);
+    const int c = static_cast<int>(i % vec) * 8;
+    const uint4 v = *reinterpret_cast<const uint4*>(a.src + (long)r * a.cols + c);
+    if (a.exchange) {
+      // Row r goes to rank r / part, at its row r % part, in the column block of this rank.
+      const int t = r / part;
+      __nv_bfloat16* dst = a.peers.hidden[t] + (long)(r % part) * a.world * a.cols + (long)a.rank * a.cols + c;
+      *reinterpret_cast<uint4*>(dst) = v;
+    } else {
+      for (int p = 0; p < a.world; ++p) {
+        __nv_bfloat16* dst = a.peers.hidden[p] + ((long)a.rank * a.rows + r) * a.cols + c;
+        *reinterpret_cast<uint4*>(dst) = v;
+      }
+    }
+  }
+  __threadfence_system();
+}
+
 }  // namespace
 
 int tp_moe_combine_norm(const MoeCombineArgs& a, cudaStream_t stream) {
@@ -382,6 +408,16 @@ int tp_clear_recv(float* recv, size_t floats, cudaStream_t stream) {
 int tp_argmax(const ArgmaxArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return 0;
   return launch_pdl(tp_argmax_kernel, dim3(1), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -5;
+}
+
+int tp_push_rows(const RowsArgs& a, cudaStream_t stream) {
+  if (a.rows <= 0 || a.cols <= 0 || a.cols % 8 != 0 || a.world < 1 || a.world > kMaxRanks ||
+      (a.exchange && a.rows % a.world != 0) ||
+      reinterpret_cast<uintptr_t>(a.src) % 16 != 0)
+    return -2;
+  const long vecs = (long)a.rows * (a.cols / 8);
+  const int blocks = static_cast<int>(std::min<long>((vecs + 255) / 256, 148 * 4));
+  return launch_pdl(tp_push_rows_kernel, dim3(blocks), dim3(256), 0, stream, a) == cudaSuccess ? 0 : -5;
 }
 
 int tp_barrier(const PeerBuffers& peers, const unsigned long long* epoch, int rank, int world,

@@ -63,6 +63,20 @@ struct ArgmaxArgs {
   int* status;
 };
 
+// Row collectives between calls (reference: ops/collective/gather.rs:17-99 `AllGather`, parts
+// joined in chip order, rows stacked [N*S, W] on every chip; ops/collective/mod.rs:313-344
+// `Exchange`, chip t receives rows t*S.. of every chip's columns, [S, N*C]). This rank stores its
+// BF16 part straight into every receiver's landing buffer (peers.hidden) over NVLink, 16 bytes a
+// store, and fences them system-wide before it ends; a barrier then tells the receivers.
+struct RowsArgs {
+  PeerBuffers peers;
+  const __nv_bfloat16* src;  // this rank's part [rows, cols]
+  int rows, cols;            // cols a multiple of 8; for an exchange rows a multiple of world
+  int rank, world;
+  int exchange;              // 0: all-gather, 1: exchange
+};
+int tp_push_rows(const RowsArgs& args, cudaStream_t stream);
+
 // Exchanges every rank's (value, index) candidates and keeps the first maximum.
 int tp_argmax(const ArgmaxArgs& args, cudaStream_t stream);
 

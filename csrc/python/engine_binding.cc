@@ -907,6 +907,30 @@ void bind_engine(py::module_& m) {
     d.model->device().synchronize();
     d.model->device().state()->check_status();
   });
+  // The reference's AllGather / Exchange of BF16 rows over the decoder's peer heap (between calls,
+  // every rank in the same order): [rows, cols] -> [rows * world, cols] or [rows / world, cols * world].
+  auto gather = [](PyDecoder& d, const HbmTensor& x, bool exchange) {
+    auto* coll = dynamic_cast<PeerCollectives*>(d.model->collectives().get());
+    if (coll == nullptr) throw ValueError("the decoder has no tensor-parallel collectives attached");
+    if (x.dtype() != DType::BF16 || x.shape().size() != 2) throw ValueError("a two-dimensional BF16 tensor");
+    const int rows = static_cast<int>(x.shape()[0]), cols = static_cast<int>(x.shape()[1]);
+    const int world = coll->world();
+    const std::vector<int64_t> shape = exchange ? std::vector<int64_t>{rows / world, static_cast<int64_t>(cols) * world}
+                                                : std::vector<int64_t>{static_cast<int64_t>(rows) * world, cols};
+    HbmBuffer out(d.model->device(), static_cast<size_t>(rows) * cols * world * 2);
+    {
+      py::gil_scoped_release nogil;
+      auto st = d.model->device().state();
+      st->activate();
+      coll->gather_rows(static_cast<const __nv_bfloat16*>(x.buffer().data()), rows, cols, exchange,
+                        static_cast<__nv_bfloat16*>(out.data()), st->stream);
+    }
+    return HbmTensor(out, shape, DType::BF16);
+  };
+  m.def("_tp_all_gather", [gather](PyDecoder& d, const HbmTensor& x) { return gather(d, x, false); },
+        py::arg("decoder"), py::arg("rows"));
+  m.def("_tp_exchange", [gather](PyDecoder& d, const HbmTensor& x) { return gather(d, x, true); },
+        py::arg("decoder"), py::arg("rows"));
   m.def("_tp_detach", [](PyDecoder& d) {
     py::gil_scoped_release nogil;
     d.model->device().synchronize();

@@ -63,3 +63,21 @@ def test_expert_parallel_matches_single_gpu(world, tmp_path):
     # The expert-parallel path is deterministic: a second run gives the same tokens.
     again = _run(world, str(tmp_path / f"ep{world}b.json"), "tiny-qwen3-moe", 12)
     assert again == many
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_row_all_gather_and_exchange(world, tmp_path):
+    """The reference's AllGather (parts in rank order) and Exchange (rank t takes rows t*S.. of
+    every rank's columns) of BF16 rows over the peer heap, between decoder calls, on every rank."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    out = str(tmp_path / "rows")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1")
+    subprocess.run(["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                    f"--nproc-per-node={world}", "--master-addr=127.0.0.1", "--master-port=29534",
+                    os.path.join(ROOT, "tests", "workers", "tp_rows.py"), out], check=True, env=env, cwd=ROOT)
+    for r in range(world):
+        with open(f"{out}.{r}") as f:
+            results = json.load(f)
+        assert results and all(results.values()), (r, results)
