@@ -63,3 +63,34 @@ def sampling(temperature: float, top_k: int, top_p: float, n: int, logprobs, pro
         raise Refused("logprobs", "the engine returns tokens, not log-probabilities")
     if n != 1:
         raise Refused("n", "one sequence per request")
+
+
+# Sampling parameters that change the distribution a token is drawn from, at their neutral values:
+# the engine's head returns each row's first maximum of the unmodified logits, so a request that
+# sets any of them is refused rather than answered with tokens that ignore it (the reference's
+# greedy predicate: integrations/furiosa-opt-vllm/furiosa_opt_vllm/generation/__init__.py:125-142).
+NEUTRAL = (
+    ("repetition_penalty", 1.0),
+    ("frequency_penalty", 0.0),
+    ("presence_penalty", 0.0),
+    ("min_tokens", 0),
+    ("logit_bias", None),
+    ("allowed_token_ids", None),
+    ("bad_words", None),
+    ("structured_outputs", None),
+    ("logprob_token_ids", None),
+    ("thinking_token_budget", None),
+    ("extra_args", None),
+)
+
+
+def unmodified(params) -> None:
+    """Refuses a request whose parameters change the greedy token (penalties, biases, masks,
+    grammars); empty lists and dicts count as unset."""
+    for name, neutral in NEUTRAL:
+        value = getattr(params, name, neutral)
+        if neutral is None:
+            if value:  # None, [] and {} leave the distribution alone
+                raise Refused(name, "the engine returns each row's greedy token of the unmodified logits")
+        elif value != neutral:
+            raise Refused(name, "the engine returns each row's greedy token of the unmodified logits")

@@ -56,3 +56,4 @@ class B200Platform(NvmlCudaPlatform):
             return
         admission.sampling(params.temperature, params.top_k, params.top_p, params.n, params.logprobs,
                            params.prompt_logprobs)
+        admission.unmodified(params)

@@ -152,3 +152,16 @@ def test_additional_config_section():
     with pytest.raises(admission.Refused) as e:
         Section.parse(SimpleNamespace(additional_config={"furiosa": {"draft_placement": {"chips": [1, 1]}}}))
     assert e.value.option.startswith("additional_config.furiosa.draft_placement")
+
+
+def test_parameters_that_change_the_greedy_token_are_refused():
+    from types import SimpleNamespace
+
+    admission.unmodified(SimpleNamespace(repetition_penalty=1.0, min_tokens=0, logit_bias={}, bad_words=[],
+                                         structured_outputs=None))
+    for name, value in [("repetition_penalty", 1.1), ("frequency_penalty", 0.5), ("presence_penalty", -0.2),
+                        ("min_tokens", 3), ("logit_bias", {5: 2.0}), ("allowed_token_ids", [1, 2]),
+                        ("bad_words", ["x"]), ("structured_outputs", object()), ("extra_args", {"k": 1})]:
+        with pytest.raises(admission.Refused) as e:
+            admission.unmodified(SimpleNamespace(**{name: value}))
+        assert e.value.option == name
