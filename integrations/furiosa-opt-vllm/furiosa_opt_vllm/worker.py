@@ -132,7 +132,10 @@ class Worker(WorkerBase):
     def get_supported_tasks(self):
         if not self.pooling:
             return ("generate",)
-        return ("classify",) if self.model.output.name == "SCORES" else ("embed",)
+        if self.model is not None:
+            return ("classify",) if self.model.output.name == "SCORES" else ("embed",)
+        declared = load.architectures(self.model_config.model)
+        return ("classify",) if any(a.endswith("ForSequenceClassification") for a in declared) else ("embed",)
 
     def pooling_config(self) -> dict | None:
         """The runner's pooling settings: the task the model serves, vLLM's pooling type and, for
