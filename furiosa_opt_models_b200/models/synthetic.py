@@ -245,3 +245,15 @@ def write_gemma4_encoder(directory: str, config: dict, seed: int = 0, std: float
     }
     save_file({**w, "model.language_model.embed_tokens.weight": rnd(8, T)}, os.path.join(directory, "model.safetensors"))
     return w
+
+
+def write_tokenizer(directory: str, vocab: int) -> None:
+    """A word-level tokenizer of `vocab` tokens named t0, t1, ... (whitespace-separated), saved
+    beside a synthetic checkpoint for frameworks that open a tokenizer even when prompts come as
+    token IDs."""
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    tok = Tokenizer(models.WordLevel(vocab={f"t{i}": i for i in range(vocab)}, unk_token="t0"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="t0", pad_token="t1", eos_token="t2").save_pretrained(directory)

@@ -143,6 +143,7 @@ def test_vllm_pooling_through_the_engine(tmp_path, mode):
     cfg = configs.get("tiny-qwen3")
     d = tmp_path / "m"
     hf = synthetic.write(str(d), cfg, seed=14, std=0.05)
+    synthetic.write_tokenizer(str(d), cfg["vocab"])  # vLLM's pooling front end opens one
     w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
     score = None
     if mode == "classify":
