@@ -10,6 +10,8 @@
 #include <climits>
 #include <algorithm>
 
+#include <cooperative_groups.h>
+
 #include "ops.cuh"
 #include "launch.cuh"
 #include "sm100.cuh"
@@ -117,25 +119,37 @@ __device__ __forceinline__ void better(float& bv, int& bi, float v, int i) {
   }
 }
 
+// One row's argmax split over a cluster of kArgmaxCtas CTAs: CTA c scans its slice of the row
+// (slices start on 4-float boundaries), the CTAs' (value, index) pairs meet in CTA 0's shared
+// memory through the cluster, and CTA 0 keeps the first maximum. A one-CTA scan of a 152K-entry
+// vocabulary row is bound by one SM's load rate; the split reads the row on eight SMs.
+constexpr int kArgmaxCtas = 8;
+
 __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ logits, long ld,
                                                      int cols, int valid, int base,
                                                      int32_t* out_index, float* out_value) {
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x;
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int part = static_cast<int>(cluster.block_rank());
+  const int row = blockIdx.y;
   const float* src = logits + (long)row * ld;
   float bv = -INFINITY;
   int bi = INT_MAX;
   const int n = min(cols, valid);
-  const int n4 = (ld % 4 == 0) ? n / 4 : 0;
-  for (int v = threadIdx.x; v < n4; v += blockDim.x) {
-    const float4 x = __ldg(reinterpret_cast<const float4*>(src) + v);
-    better(bv, bi, x.x, 4 * v);
-    better(bv, bi, x.y, 4 * v + 1);
-    better(bv, bi, x.z, 4 * v + 2);
-    better(bv, bi, x.w, 4 * v + 3);
+  const int per = ((n + kArgmaxCtas - 1) / kArgmaxCtas + 3) & ~3;
+  const int lo = min(n, part * per), hi = min(n, lo + per);
+  const bool vec = ld % 4 == 0;
+  const int hi4 = vec ? lo + ((hi - lo) & ~3) : lo;
+  for (int i = lo + 4 * threadIdx.x; i < hi4; i += 4 * blockDim.x) {
+    const float4 x = __ldg(reinterpret_cast<const float4*>(src + i));
+    better(bv, bi, x.x, i);
+    better(bv, bi, x.y, i + 1);
+    better(bv, bi, x.z, i + 2);
+    better(bv, bi, x.w, i + 3);
   }
-  for (int i = 4 * n4 + threadIdx.x; i < n; i += blockDim.x) better(bv, bi, src[i], i);
+  for (int i = hi4 + threadIdx.x; i < hi; i += blockDim.x) better(bv, bi, src[i], i);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
@@ -144,6 +158,8 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
   }
   __shared__ float sv[16];
   __shared__ int si[16];
+  __shared__ float cta_v;
+  __shared__ int cta_i;
   if ((threadIdx.x & 31) == 0) {
     sv[threadIdx.x >> 5] = bv;
     si[threadIdx.x >> 5] = bi;
@@ -151,10 +167,18 @@ __global__ void __launch_bounds__(512) argmax_kernel(const float* __restrict__ l
   __syncthreads();
   if (threadIdx.x == 0) {
     for (int w = 1; w < (int)(blockDim.x >> 5); ++w) better(bv, bi, sv[w], si[w]);
+    cta_v = bv;
+    cta_i = bi;
+  }
+  cluster.sync();  // every CTA's pair is in its shared memory
+  if (part == 0 && threadIdx.x == 0) {
+    for (int c = 1; c < kArgmaxCtas; ++c)
+      better(bv, bi, *cluster.map_shared_rank(&cta_v, c), *cluster.map_shared_rank(&cta_i, c));
     if (bi == INT_MAX) bi = 0;
     out_index[row] = bi + base;
     if (out_value != nullptr) out_value[row] = bv;
   }
+  cluster.sync();  // no CTA leaves while CTA 0 still reads its shared memory
 }
 
 __global__ void argmax_merge_kernel(const float* values, const int32_t* indices, int ranks,
@@ -419,8 +443,9 @@ int embedding(const int32_t* ids, const __nv_bfloat16* table, long ldt, int row_
 int argmax_rows(const float* logits, long ld, int rows, int cols, int valid_cols, int index_base,
                 int32_t* out_index, float* out_value, cudaStream_t stream) {
   if (rows <= 0) return 0;
-  launch_pdl(argmax_kernel, dim3(rows), dim3(512), 0, stream, logits, ld, cols, valid_cols, index_base, out_index,
-                                          out_value);
+  if (rows > 65535) return -2;
+  launch_pdl_cluster(argmax_kernel, dim3(kArgmaxCtas, rows), dim3(512), kArgmaxCtas, 0, stream, logits, ld, cols,
+                     valid_cols, index_base, out_index, out_value);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
