@@ -1,0 +1,77 @@
+"""SGLang's memory saver on the engine (`release_memory_occupation` / `resume_memory_occupation`
+with the tags `weights`, `kv_cache` and `cuda_graph`; the reference's
+integrations/furiosa-opt-sglang/furiosa_opt_sglang/residency.py).
+
+Device memory is released by dropping what holds it (the loaded decoder, the KV cache) and
+returning the engine's cached device blocks to the driver; resuming loads or allocates it again.
+
+- Only `--enable-memory-saver` releases memory, as with SGLang's own allocator.
+- With `--enable-weights-cpu-backup` the load keeps a host copy of the checkpoint's tensors
+  (`Checkpoint.read()`) and resuming loads from it; without it resuming reads the files again.
+- A released cache keeps its block count and comes back empty (SGLang flushes its radix cache
+  before it releases the KV cache).
+- Releasing goes cache first, then weights; resuming weights first, then the cache, one tag after
+  another, so a retry after a failure resumes only what is still released.
+"""
+
+from __future__ import annotations
+
+from .platform import Refused
+
+TAGS = ("weights", "kv_cache")
+# SGLang's tag for its own CUDA graphs: the engine's graphs belong to the decoder and go and come
+# back with the weights, so the tag is accepted and does nothing of its own.
+GRAPHS = "cuda_graph"
+
+
+class Served:
+    """The engine objects one SGLang scheduler serves on its device.
+
+    `load(source, device)` loads a decoder from a checkpoint or its host copy, `checkpoint(path)`
+    opens the files and `host_copy(path)` reads them into host memory; `cache(spec, blocks)`
+    allocates a KV cache; `trim(device)` returns the engine's cached device blocks to the driver.
+    """
+
+    def __init__(self, path, device, blocks: int, *, load, checkpoint, host_copy, cache, trim,
+                 memory_saver: bool = False, cpu_backup: bool = False):
+        self.path, self.device, self.blocks = path, device, blocks
+        self._load, self._checkpoint, self._host_copy = load, checkpoint, host_copy
+        self._cache, self._trim = cache, trim
+        self.memory_saver, self.cpu_backup = memory_saver, cpu_backup
+        self.copy = host_copy(path) if cpu_backup else None
+        self.model = load(self.copy if self.copy is not None else checkpoint(path), device)
+        self.kv = cache(self.model.cache, blocks)
+        self.released: set[str] = set()
+
+    def _tags(self, tags) -> list[str]:
+        tags = list(TAGS) if tags is None else list(tags)
+        for t in tags:
+            if t not in TAGS and t != GRAPHS:
+                raise Refused("tags", f"{t}: the memory saver releases {', '.join(TAGS)} (and {GRAPHS})")
+        return tags
+
+    def release(self, tags=None) -> None:
+        if not self.memory_saver:
+            raise Refused("enable_memory_saver", "memory is released only under the memory saver")
+        tags = self._tags(tags)
+        if "kv_cache" in tags and "kv_cache" not in self.released:
+            self.device.synchronize()
+            self.kv = None
+            self.released.add("kv_cache")
+        if "weights" in tags and "weights" not in self.released:
+            self.device.synchronize()
+            self.model = None
+            self.released.add("weights")
+        self._trim(self.device)
+
+    def resume(self, tags=None) -> None:
+        tags = self._tags(tags)
+        if "weights" in tags and "weights" in self.released:
+            source = self.copy if self.copy is not None else self._checkpoint(self.path)
+            self.model = self._load(source, self.device)
+            self.released.discard("weights")
+        if "kv_cache" in tags and "kv_cache" in self.released:
+            if self.model is None:
+                raise RuntimeError("the KV cache resumes after the weights it follows")
+            self.kv = self._cache(self.model.cache, self.blocks)
+            self.released.discard("kv_cache")
