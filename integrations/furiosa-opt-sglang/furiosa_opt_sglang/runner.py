@@ -34,3 +34,21 @@ class Runner:
 
     def decode(self, req_rows, seq_lens, tokens, req_to_token) -> list[int]:
         return self.forward(batch.decode_parts(req_rows, seq_lens), tokens, req_to_token)
+
+    def embed(self, req_rows, seq_lens, prefix_lens, new_lens, tokens, req_to_token, normalize=True):
+        """An extend batch of an embedding model (a decoder whose calls return hidden rows, loaded
+        as its base model): each request's last row, L2-normalized unless `normalize` is False,
+        as an FP32 tensor [requests, hidden] (SGLang's LAST pooling of a causal embedder; the
+        reference pools hidden rows the same way:
+        integrations/furiosa-opt-sglang/furiosa_opt_sglang/embedding.py)."""
+        import torch
+
+        if self.model.output != self.dec.Output.HIDDEN:
+            raise ValueError("embedding needs a decoder that returns hidden rows (its base model)")
+        parts = batch.parts(req_rows, seq_lens, prefix_lens, new_lens)
+        flat = np.ascontiguousarray(np.asarray(tokens, dtype=np.int32))
+        dev = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device)
+        reqs = [self.dec.Request([batch.request_blocks(req_to_token, p)], p.cached, dev[p.start : p.start + p.count],
+                                 self.dec.Keep.LAST) for p in parts]
+        rows = torch.from_numpy(np.asarray(self.model.forward(reqs, self.cache).to_host().numpy(), dtype=np.float32))
+        return torch.nn.functional.normalize(rows, p=2, dim=-1) if normalize else rows

@@ -46,3 +46,57 @@ def test_entry_points():
 
     assert furiosa_opt_sglang.activate() == "furiosa_opt_sglang.platform.Platform"
     furiosa_opt_sglang.register()
+
+
+def test_runner_embeds_the_last_rows():
+    """An embedding batch keeps each request's last row and L2-normalizes it (a fake engine whose
+    hidden row is a function of the token)."""
+    from types import SimpleNamespace
+
+    import numpy as np
+    import torch
+
+    from furiosa_opt_sglang.runner import Runner
+
+    class T:
+        def __init__(self, a):
+            self.a = np.asarray(a)
+
+        def __getitem__(self, s):
+            return T(self.a[s])
+
+        def to_hbm(self, device):
+            return self
+
+        def to_host(self):
+            return self
+
+        def numpy(self):
+            return self.a
+
+    keep = SimpleNamespace(LAST="last", NONE="none")
+    out = SimpleNamespace(HIDDEN="hidden", TOKENS="tokens")
+    seen = []
+
+    class Model:
+        output = "hidden"
+
+        def forward(self, reqs, cache):
+            seen.extend((r.cached, r.tokens.a.tolist(), r.keep) for r in reqs)
+            return T(np.array([[float(r.tokens.a[-1]), 1.0, -2.0] for r in reqs], dtype=np.float32))
+
+    r = Runner.__new__(Runner)
+    r.engine = SimpleNamespace(HostTensor=SimpleNamespace(from_dlpack=T))
+    r.dec = SimpleNamespace(Keep=keep, Output=out, Request=lambda rows, cached, tokens, keep: SimpleNamespace(
+        rows=rows, cached=cached, tokens=tokens, keep=keep))
+    r.model, r.device, r.cache = Model(), None, None
+    table = [list(range(0, 64)), list(range(64, 128))]
+    got = r.embed([0, 1], [3, 2], [0, 0], [3, 2], [4, 5, 6, 7, 8], table)
+    want = torch.nn.functional.normalize(torch.tensor([[6.0, 1.0, -2.0], [8.0, 1.0, -2.0]]), dim=-1)
+    assert torch.allclose(got, want)
+    assert seen == [(0, [4, 5, 6], "last"), (0, [7, 8], "last")]
+    raw = r.embed([0], [3], [0], [3], [4, 5, 6], table, normalize=False)
+    assert torch.allclose(raw, torch.tensor([[6.0, 1.0, -2.0]]))
+    Model.output = "tokens"
+    with pytest.raises(ValueError, match="hidden rows"):
+        r.embed([0], [3], [0], [3], [4, 5, 6], table)
