@@ -257,3 +257,60 @@ def write_tokenizer(directory: str, vocab: int) -> None:
     tok = Tokenizer(models.WordLevel(vocab={f"t{i}": i for i in range(vocab)}, unk_token="t0"))
     tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
     PreTrainedTokenizerFast(tokenizer_object=tok, unk_token="t0", pad_token="t1", eos_token="t2").save_pretrained(directory)
+
+
+def hf_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
+    """The HF names and shapes `hf_weights` writes for a geometry, without allocating them."""
+    H, D, I = cfg["hidden"], cfg["head_dim"], cfg["intermediate"]
+    qh, kvh, V = cfg["q_heads"], cfg["kv_heads"], cfg["vocab"]
+    out = {"model.embed_tokens.weight": (V, H), "model.norm.weight": (H,)}
+    if not cfg["tied"]:
+        out["lm_head.weight"] = (V, H)
+    for l in range(cfg["layers"]):
+        p = f"model.layers.{l}."
+        out[p + "input_layernorm.weight"] = (H,)
+        out[p + "post_attention_layernorm.weight"] = (H,)
+        out[p + "self_attn.q_proj.weight"] = (qh * D, H)
+        out[p + "self_attn.k_proj.weight"] = (kvh * D, H)
+        out[p + "self_attn.v_proj.weight"] = (kvh * D, H)
+        out[p + "self_attn.o_proj.weight"] = (H, qh * D)
+        if cfg.get("qk_norm"):
+            out[p + "self_attn.q_norm.weight"] = (D,)
+            out[p + "self_attn.k_norm.weight"] = (D,)
+        if cfg["family"] == "qwen3_moe":
+            E, Ie = cfg["experts"], cfg["expert_intermediate"]
+            out[p + "mlp.gate.weight"] = (E, H)
+            for e in range(E):
+                out[p + f"mlp.experts.{e}.gate_proj.weight"] = (Ie, H)
+                out[p + f"mlp.experts.{e}.up_proj.weight"] = (Ie, H)
+                out[p + f"mlp.experts.{e}.down_proj.weight"] = (H, Ie)
+        else:
+            out[p + "mlp.gate_proj.weight"] = (I, H)
+            out[p + "mlp.up_proj.weight"] = (I, H)
+            out[p + "mlp.down_proj.weight"] = (H, I)
+    return out
+
+
+def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
+    """A checkpoint of the geometry's full size that holds only headers: config.json and a
+    safetensors file whose header declares every BF16 tensor (offsets as if the data followed)
+    but stores no data, for `Checkpoint.declared` (loading checks of models too large to write)."""
+    import struct
+
+    cfg = configs.get(name_or_cfg) if isinstance(name_or_cfg, str) else name_or_cfg
+    os.makedirs(directory, exist_ok=True)
+    with open(os.path.join(directory, "config.json"), "w") as f:
+        json.dump(hf_config(cfg), f)
+    shapes = hf_shapes(cfg)
+    header, at = {}, 0
+    for name in sorted(shapes):
+        n = 2
+        for d in shapes[name]:
+            n *= d
+        header[name] = {"dtype": "BF16", "shape": list(shapes[name]), "data_offsets": [at, at + n]}
+        at += n
+    raw = json.dumps(header).encode()
+    raw += b" " * (-len(raw) % 8)
+    with open(os.path.join(directory, "model.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(raw)) + raw)
+    return shapes

@@ -1,0 +1,32 @@
+"""Checkpoints too large to write, checked from headers alone (the reference's weightless
+checkpoint tests, tests/common/mod.rs and qwen3_moe.rs:41): a header-only safetensors file
+declares every tensor of the full-size geometry, `Checkpoint.declared` maps the names without
+data, and the registry selects the class, size and chip split from it."""
+
+import pytest
+
+import furiosa_opt_engine as engine
+from furiosa_opt_models_b200.models import configs, synthetic
+
+
+@pytest.mark.parametrize("name", ["tiny-qwen3", "tiny-qwen3-moe"])
+def test_shapes_match_the_written_weights(name):
+    cfg = configs.get(name)
+    assert synthetic.hf_shapes(cfg) == {k: tuple(v.shape) for k, v in synthetic.hf_weights(cfg).items()}
+
+
+@pytest.mark.parametrize(("name", "cls", "size"), [
+    ("qwen3-30b-a3b", "qwen3_moe.ForCausalLM", "30B-A3B"),
+    ("llama-3.3-70b", "llama.ForCausalLM", "70B"),
+    ("llama-3.1-8b", "llama.ForCausalLM", "8B"),
+    ("qwen3-8b", "qwen3.ForCausalLM", "8B"),
+    ("qwen3-1.7b", "qwen3.ForCausalLM", "1.7B"),
+])
+def test_full_size_checkpoints_select_from_headers(tmp_path, name, cls, size):
+    shapes = synthetic.write_declared(str(tmp_path), name)
+    ck = engine.Checkpoint.declared(str(tmp_path))
+    assert sorted(ck.names()) == sorted(shapes)
+    engine.LoadOptions().parse(ck)
+    for chips in (1, 2, 4, 8):
+        sel = engine.LoadOptions().chips(chips).select(ck)
+        assert (sel["class"], sel["size"], sel["chips"]) == (cls, size, chips)
