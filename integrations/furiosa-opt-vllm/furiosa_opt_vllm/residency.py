@@ -141,3 +141,10 @@ def _load(worker, source) -> None:
     if worker.runner is not None:
         worker.runner.model = worker.model
         worker.runner.adapters = getattr(worker, "adapters", None)
+
+
+def check_health(worker) -> None:
+    """Raises when the worker's engine device failed (its poison makes every later call raise, a
+    synchronization included); a worker that has not opened its device yet is healthy."""
+    if getattr(worker, "device", None) is not None:
+        worker.device.synchronize()

@@ -149,7 +149,10 @@ class Worker(WorkerBase):
         return {"task": task, "method": str(getattr(method, "value", method)), "labels": labels}
 
     def check_health(self) -> None:
-        pass
+        """Raises when the engine's device failed: a failed launch, copy or bounded device wait
+        poisons the device, and every later call (this synchronization included) raises with the
+        first failure, so vLLM reports the engine unhealthy instead of scheduling more steps."""
+        residency.check_health(self)
 
     def update_max_model_len(self, max_model_len: int) -> None:
         self.model_config.max_model_len = max_model_len

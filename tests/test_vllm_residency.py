@@ -83,3 +83,21 @@ def test_refusals(worker):
     worker.cache = None
     with pytest.raises(RuntimeError, match="initialize_kv_cache must precede sleep mode"):
         residency.sleep(worker, 1)
+
+
+def test_health_check_raises_on_a_failed_device():
+    from types import SimpleNamespace
+
+    w = SimpleNamespace(device=None)
+    residency.check_health(w)  # before load: nothing to check
+    calls = []
+    w.device = SimpleNamespace(synchronize=lambda: calls.append(1))
+    residency.check_health(w)
+    assert calls == [1]
+
+    def failed():
+        raise RuntimeError("the device failed earlier: launch failed")
+
+    w.device = SimpleNamespace(synchronize=failed)
+    with pytest.raises(RuntimeError, match="failed earlier"):
+        residency.check_health(w)
