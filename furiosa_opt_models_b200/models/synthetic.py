@@ -293,21 +293,47 @@ def hf_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
 
 def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
     """A checkpoint of the geometry's full size that holds only headers: config.json and a
-    safetensors file whose header declares every BF16 tensor (offsets as if the data followed)
-    but stores no data, for `Checkpoint.declared` (loading checks of models too large to write)."""
+    safetensors file whose header declares every tensor (offsets as if the data followed) but
+    stores no data, for `Checkpoint.declared` (loading checks of models too large to write).
+    Returns the declared shapes."""
     import struct
 
     cfg = configs.get(name_or_cfg) if isinstance(name_or_cfg, str) else name_or_cfg
     os.makedirs(directory, exist_ok=True)
+    fmt = cfg.get("weight_format", "bf16")
+    conf = hf_config(cfg)
+    # Quantized geometries declare the published checkpoints' formats: FP8 E4M3 projections with
+    # an FP32 scale per 128x128 block, or ModelOpt NVFP4 (packed E2M1 codes, an E4M3 scale per 16
+    # inputs, FP32 tensor and input scales). Norms, embedding and head stay BF16.
+    if fmt == "fp8_block":
+        conf["quantization_config"] = {"quant_method": "fp8", "activation_scheme": "dynamic",
+                                       "weight_block_size": [128, 128]}
+    elif fmt in ("nvfp4", "nvfp4_a4"):
+        conf["quantization_config"] = {"quant_method": "modelopt", "quant_algo": "NVFP4", "group_size": 16}
     with open(os.path.join(directory, "config.json"), "w") as f:
-        json.dump(hf_config(cfg), f)
-    shapes = hf_shapes(cfg)
+        json.dump(conf, f)
+    shapes = dict(hf_shapes(cfg))
+    dtypes = {name: "BF16" for name in shapes}
+    size = {"BF16": 2, "F32": 4, "F8_E4M3": 1, "U8": 1}
+    if fmt != "bf16":
+        for name in [n for n in shapes if n.endswith("_proj.weight")]:
+            R, C = shapes[name]
+            base = name[: -len(".weight")]
+            if fmt == "fp8_block":
+                dtypes[name] = "F8_E4M3"
+                shapes[base + ".weight_scale_inv"] = (-(-R // 128), -(-C // 128))
+                dtypes[base + ".weight_scale_inv"] = "F32"
+            else:
+                shapes[name], dtypes[name] = (R, C // 2), "U8"
+                shapes[base + ".weight_scale"], dtypes[base + ".weight_scale"] = (R, C // 16), "F8_E4M3"
+                for s in ("weight_scale_2", "input_scale"):
+                    shapes[f"{base}.{s}"], dtypes[f"{base}.{s}"] = (), "F32"
     header, at = {}, 0
     for name in sorted(shapes):
-        n = 2
+        n = size[dtypes[name]]
         for d in shapes[name]:
             n *= d
-        header[name] = {"dtype": "BF16", "shape": list(shapes[name]), "data_offsets": [at, at + n]}
+        header[name] = {"dtype": dtypes[name], "shape": list(shapes[name]), "data_offsets": [at, at + n]}
         at += n
     raw = json.dumps(header).encode()
     raw += b" " * (-len(raw) % 8)

@@ -30,3 +30,19 @@ def test_full_size_checkpoints_select_from_headers(tmp_path, name, cls, size):
     for chips in (1, 2, 4, 8):
         sel = engine.LoadOptions().chips(chips).select(ck)
         assert (sel["class"], sel["size"], sel["chips"]) == (cls, size, chips)
+
+
+@pytest.mark.parametrize(("name", "size", "precision"), [
+    ("llama-3.1-8b-fp8", "8B", "float8_e4m3fn"),
+    ("qwen3-8b-fp8", "8B", "float8_e4m3fn"),
+    ("llama-3.3-70b-nvfp4", "70B", "uint8"),
+])
+def test_quantized_full_size_checkpoints_select_their_format(tmp_path, name, size, precision):
+    """The BASELINE-shaped quantized checkpoints (block-FP8 8B, NVFP4 70B), declared in their
+    published formats, select the quantized line at every chip count."""
+    shapes = synthetic.write_declared(str(tmp_path), name)
+    ck = engine.Checkpoint.declared(str(tmp_path))
+    assert sorted(ck.names()) == sorted(shapes)
+    for chips in (1, 8):
+        sel = engine.LoadOptions().chips(chips).select(ck)
+        assert (sel["size"], sel["precision"], sel["chips"]) == (size, precision, chips)
