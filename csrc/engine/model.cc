@@ -657,6 +657,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       prev = now;
     }
   };
+  const char* gemm_name = "gemm";  // the projection's name in per-kernel traces
   auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
                   int epi, const void* res, int lora_layer = -1, int lora_module = 0,
                   const foa::GemmPeerOut* peer = nullptr) {
@@ -756,7 +757,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       g.mode = (w.format == foa::kWeightFp8A8 && epi == foa::kEpiSwiGLU) ? foa::kModeSwap : foa::kModeRows;
       g.splits = 1;
     }
-    fail(foa::gemm_bf16(g, s), "gemm");
+    fail(foa::gemm_bf16(g, s), gemm_name);
   };
   const int qkv_cols = (qh_l_ + 2 * kvh_l_) * D;
   // Tensor-parallel ranks keep the residual stream and the normed rows in the symmetric heap,
@@ -802,6 +803,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "in_norm"), h, H, nullptr, 0, static_cast<int>(T),
                         H, cfg_.eps, s),
            "rmsnorm");
+    gemm_name = "gemm qkv";
     gemm(h, H, ws(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
          nullptr, l, LoraAdapter::kQkv);
     __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(cache.layers()[l].data());
@@ -827,6 +829,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     // Attention output projection, then the post-attention RMSNorm (fused with the cross-rank
     // sum under tensor parallelism).
     if (!tp) {
+      gemm_name = "gemm o";
       gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
            foa::kEpiBf16, x, l, LoraAdapter::kO);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
@@ -834,10 +837,11 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
            "rmsnorm");
     } else {
       const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
+      gemm_name = "gemm o (peer push)";
       gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, nullptr, H,
            foa::kEpiF32, nullptr, l, LoraAdapter::kO, &target);
       coll_->add_norm(x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
-      ++kernels;
+      fail(0, "tp add_norm");
     }
     if (cfg_.experts > 0) {
       // Mixture of experts (rows replicated on every rank; this rank's experts only): router,
@@ -846,6 +850,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       const int E = cfg_.experts, Kc = cfg_.top_k, I = cfg_.expert_intermediate;
       const int tile = moe_tile(T);
       const int64_t cap = moe_capacity(T);
+      gemm_name = "gemm router";
       gemm(h, H, ws(p + "router"), static_cast<int>(T), E, H, ws_logits_e_.data(), E, foa::kEpiBf16, nullptr);
       fail(foa::moe_route(bf(ws_logits_e_), E, static_cast<int>(T), E, Kc, cfg_.norm_topk, i32(ws_ids_),
                           static_cast<float*>(ws_rw_.data()), s),
@@ -886,24 +891,28 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       } else {
         coll_->moe_combine_norm(l & 1, i32(ws_pos_), i32(ws_ids_), static_cast<float*>(ws_rw_.data()),
                                 experts_l_, w(next_norm), cfg_.eps, static_cast<int>(T), Kc, H, s);
-        ++kernels;
+        fail(0, "tp moe combine");
       }
     } else if (!tp) {
+      gemm_name = "gemm gate_up";
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
+      gemm_name = "gemm down";
       gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
            foa::kEpiBf16, x, l, LoraAdapter::kDown);
       fail(foa::rmsnorm(x, H, nullptr, 0, w(next_norm), h, H, nullptr, 0, static_cast<int>(T), H,
                         cfg_.eps, s),
            "rmsnorm");
     } else {
+      gemm_name = "gemm gate_up";
       gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
            foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
       const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
+      gemm_name = "gemm down (peer push)";
       gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, nullptr, H,
            foa::kEpiF32, nullptr, l, LoraAdapter::kDown, &target);
       coll_->add_norm(x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
-      ++kernels;
+      fail(0, "tp add_norm");
     }
   }
 
@@ -912,10 +921,12 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
   fail(foa::gather_rows(h, H, i32(stage, sg.kept), K, bf(ws_hk_), H, H, s), "gather rows");
   if (cfg_.output == Output::Hidden) return kernels;
   if (cfg_.output == Output::Scores) {
+    gemm_name = "gemm score";
     gemm(ws_hk_.data(), H, ws("score"), K, cfg_.labels, H, ws_logits_.data(), cfg_.labels,
          foa::kEpiF32, nullptr);
     return kernels;
   }
+  gemm_name = "gemm lm_head";
   gemm(ws_hk_.data(), H, ws("lm_head"), K, vocab_l_, H, ws_logits_.data(), vocab_l_, foa::kEpiF32,
        nullptr);
   const int valid = vocab_end_ - vocab_begin_;
@@ -928,7 +939,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                           vocab_begin_, i32(ws_idx_), static_cast<float*>(ws_val_.data()), s),
          "argmax");
     coll_->argmax(static_cast<float*>(ws_val_.data()), i32(ws_idx_), K, i32(ws_tokens_), s);
-    ++kernels;
+    fail(0, "tp argmax");
   }
   return kernels;
 }

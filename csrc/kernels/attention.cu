@@ -225,6 +225,18 @@ __global__ void __launch_bounds__(32 * kWarps, decode_ctas_per_sm(D, kWarps, kSt
   const Segment seg = p.segments[seg_index];
   const int keys = seg.cached + seg.len;
   const int nsplit = (keys + p.keys_per_split - 1) / p.keys_per_split;
+  if (nsplit > max_splits) {
+    // A history longer than the launch's max_keys has more splits than its partial slots: the
+    // row's heads are written as zeros and the status word (when given) records the bad argument.
+    if (split == 0) {
+      const int row = seg.row_start + seg.len - 1;
+      const int G = p.q_heads / p.kv_heads;
+      for (int i = threadIdx.x; i < G * D; i += blockDim.x)
+        p.o[((long)row * p.q_heads + kvh * G + i / D) * D + i % D] = __float2bfloat16_rn(0.f);
+      if (threadIdx.x == 0) record_status(p.status, kBadArgument);
+    }
+    return;
+  }
   if (split >= nsplit) return;
   const int k0 = split * p.keys_per_split;
   const int k1 = min(keys, k0 + p.keys_per_split);
@@ -367,7 +379,7 @@ __global__ void decode_merge_kernel(const PagedAttention p, int max_splits) {
   const Segment seg = p.segments[seg_index];
   const int keys = seg.cached + seg.len;
   const int nsplit = (keys + p.keys_per_split - 1) / p.keys_per_split;
-  if (nsplit == 1) return;
+  if (nsplit == 1 || nsplit > max_splits) return;  // one split: written in place; too many: zeros
   const long base = ((long)seg_index * p.q_heads + head) * max_splits;
   float mx = -INFINITY;
   for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, p.partial_lse[base + s]);
@@ -502,19 +514,8 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
     const size_t need = (size_t)p.num_segments * p.q_heads * max_splits;
     if (p.partial_o == nullptr || p.partial_lse == nullptr || need > p.partial_capacity) return -3;
   }
-  static const int env_warps = [] {
-    const char* v = std::getenv("FOA_DECODE_WARPS");  // measurement override: 2, 3 or 4
-    const int w = v ? std::atoi(v) : 0;
-    return w >= 2 && w <= 4 ? w : 0;
-  }();
-  const int warps = env_warps        ? env_warps
-                    : p.decode_warps >= 2 && p.decode_warps <= 4 ? p.decode_warps
-                                                                 : kDecodeWarps;
-  static const int stages = [] {
-    const char* v = std::getenv("FOA_DECODE_STAGES");  // measurement override: 2 or 3
-    const int n = v ? std::atoi(v) : kDecodeStages;
-    return n == 2 || n == 3 ? n : kDecodeStages;
-  }();
+  const int warps = p.decode_warps >= 2 && p.decode_warps <= 4 ? p.decode_warps : kDecodeWarps;
+  const int stages = p.decode_stages == 2 || p.decode_stages == 3 ? p.decode_stages : kDecodeStages;
   const int smem = warps * stages * 2 * 16 * D * 2;
   auto kernel = stages == 2 ? (warps == 2 ? paged_decode_kernel<D, 2, 2>
                                : warps == 3 ? paged_decode_kernel<D, 3, 2>
@@ -566,9 +567,7 @@ int paged_decode(const PagedAttention& p, cudaStream_t stream) {
 int paged_prefill(const PagedAttention& p, const int32_t* work, int num_work, cudaStream_t stream) {
   if (num_work <= 0) return 0;
   if (p.kv_heads <= 0 || p.q_heads % p.kv_heads != 0) return -2;
-  // FOA_PREFILL_MMA_SYNC=1 keeps the mma.sync kernel (measurements only).
-  static const bool legacy = std::getenv("FOA_PREFILL_MMA_SYNC") != nullptr;
-  if (!legacy && prefill_tc_supported(p)) return paged_prefill_tc(p, work, num_work, stream);
+  if (prefill_tc_supported(p)) return paged_prefill_tc(p, work, num_work, stream);
   switch (p.head_dim) {
     case 64: return prefill_launch<64>(p, work, num_work, stream);
     case 128: return prefill_launch<128>(p, work, num_work, stream);

@@ -38,11 +38,15 @@ struct PagedAttention {
   // Prefill on the tensor cores (TMA tensor maps): rows of q and o, and pages in the layer's cache.
   int rows = 0;
   long cache_blocks = 0;
-  // Decode: warps a CTA (2, 3 or 4; 0 takes the default of 2).
+  // Decode: warps a CTA (2, 3 or 4; 0 takes the default of 2) and 16-key blocks each warp keeps
+  // in flight (2 or 3; 0 takes the default of 2).
   int decode_warps = 0;
+  int decode_stages = 0;
 };
 
-// Decode: every segment appends one row (len == 1) and attends its whole history.
+// Decode: every segment appends one row (len == 1) and attends its whole history. A segment whose
+// history (cached + 1) exceeds `max_keys` gets zeros in its output rows and records kBadArgument
+// in `status`: `max_keys` sizes the split scratch, so it must bound every segment.
 int paged_decode(const PagedAttention& args, cudaStream_t stream);
 
 // Prefill / chunks: segments of any length attend their history plus their own rows causally.

@@ -59,7 +59,7 @@ struct KParams {
   int out_rows, out_cols;     // logical output shape
   unsigned long long* trace;  // milestone timestamps of CTA 0, or null
   unsigned long long* cta_trace;  // per-CTA timestamps (8 a CTA; see GemmArgs), or null
-  int debug;                  // measurement switches (FOA_GEMM_DEBUG): 1 no stores, 2 no TMEM loads
+  int debug;                  // measurement switches (GemmArgs::debug): 1 no stores, 2 no TMEM loads
   // Quantized weights (kWF != 0): block scales and the factor the FP32 sums take.
   const void* wscale;         // FP8: FP32 [ceil(N/128)][ceil(K/128)]; NVFP4: E4M3 [N][K/16]
   long wscale_ld;             // scale elements per scale row
@@ -1270,12 +1270,9 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   const bool cluster_fits =
       pl.swap && splits <= 8 && (int)recv_bytes <= swap_ring_bytes(pl.mb, pl.kbn, a.w_format);
   pl.red = splits == 1 ? 0 : cluster_fits ? 2 : 1;
-  // FOA_GEMM_RED=global|cluster forces how splits meet (measurements only).
-  static const char* force = std::getenv("FOA_GEMM_RED");
-  if (force != nullptr && splits > 1) {
-    if (force[0] == 'g') pl.red = 1;
-    if (force[0] == 'c' && cluster_fits) pl.red = 2;
-  }
+  // A measurement may ask how the splits meet (1 global scratch, 2 cluster).
+  if (a.reduction == 1 && splits > 1) pl.red = 1;
+  if (a.reduction == 2 && splits > 1 && cluster_fits) pl.red = 2;
   if (pl.red == 1) {
     // Global scratch bounds the split count.
     while (splits > 1 && ((size_t)tiles * splits * red_bytes > ws_bytes || tiles > counters_len))
@@ -1607,8 +1604,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.status = a.status;
   kp.trace = a.trace;
   kp.cta_trace = a.cta_trace;
-  static const int debug = std::getenv("FOA_GEMM_DEBUG") ? std::atoi(std::getenv("FOA_GEMM_DEBUG")) : 0;
-  kp.debug = debug;
+  kp.debug = a.debug;
   kp.out_rows = a.M;
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;

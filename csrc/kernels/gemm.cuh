@@ -117,6 +117,10 @@ struct GemmArgs {
   GemmSegment seg[2];
   // Optional tensor-parallel reduction target (kEpiF32 only); see GemmPeerOut.
   GemmPeerOut peer;
+  // Measurement only (kernel_bench): how split-K partials meet (0 the plan's choice, 1 global
+  // scratch, 2 cluster shared memory) and work left out (bit 0 no output stores, bit 1 no TMEM loads).
+  int reduction = 0;
+  int debug = 0;
 };
 
 enum GemmWeightFormat : int {

@@ -1,14 +1,6 @@
-// foa_paged_decode_noalloc: paged decode attention that allocates no memory.
-//
-// This entry point has no counterpart in the reference (furiosa-ai/furiosa-opt-models); it is an
-// addition of this framework.
-//
-// Who needs it: code that cannot call cudaMalloc at the moment it runs attention. Examples are a
-// host runtime that must not allocate after start-up (a fixed device-memory budget, or a custom
-// allocator that owns every byte), code running inside another framework's memory pool that
-// forbids foreign allocations, and plug-ins loaded through a plain C interface that has no way to
-// hand back a scratch buffer. Such callers own the inputs and outputs and pass them in, but cannot
-// provide the working memory the kernel needs for long histories.
+// foa_paged_decode_noalloc: paged decode attention that allocates no memory. The interface, its
+// return codes and the size limit are declared in noalloc.h; this file has no counterpart in the
+// reference (furiosa-ai/furiosa-opt-models).
 //
 // What it does: the same flash-decoding kernels as `paged_decode` (attention.cu) on one-row
 // segments over the paged KV cache. When a history is longer than one split (`keys_per_split`
@@ -16,10 +8,6 @@
 // this file, `g_noalloc_scratch`, instead of caller- or engine-allocated buffers. The array is a
 // file-scope `__device__` variable: it is part of the loaded library, every GPU that loads the
 // library holds one copy of it until the process exits, and nothing allocates it at run time.
-//
-// Size limit: kNoAllocScratchBytes (16 MiB). A call needs
-//   segments * q_heads * splits * (head_dim + 1) * 4 bytes,  splits = ceil(max_keys / keys_per_split),
-// and is rejected (FOA_NOALLOC_TOO_LARGE, nothing launched) when that exceeds the limit.
 //
 // Set-up: the first call on each device, with that device current, looks up the device address of
 // the scratch array with cudaGetSymbolAddress and keeps it for later calls on that device. Make
@@ -36,10 +24,11 @@
 #include <mutex>
 
 #include "attention.cuh"
+#include "noalloc.h"
 
 namespace {
 
-constexpr size_t kNoAllocScratchBytes = 16u << 20;
+constexpr size_t kNoAllocScratchBytes = FOA_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
 
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
@@ -55,18 +44,7 @@ void report(char* error, int error_len, const char* msg) {
 
 }  // namespace
 
-// Return codes.
-#define FOA_NOALLOC_OK 0
-#define FOA_NOALLOC_BAD_ARGUMENT (-2)
-#define FOA_NOALLOC_TOO_LARGE (-3)
-#define FOA_NOALLOC_SETUP_FAILED (-4)
-#define FOA_NOALLOC_LAUNCH_FAILED (-5)
-
-// Decode attention of `num_segments` one-row segments (int32 [num_segments][5]: row_start, len=1,
-// cached, table_start, nblocks) over one layer's paged cache (block b: K[kv_heads][16][head_dim]
-// then V, BF16), block IDs in `table`. `q` and `o` are BF16 [rows][q_heads][head_dim]. `max_keys`
-// bounds every segment's history (cached + 1). Runs on `stream` (a cudaStream_t; null is the
-// legacy default stream). Returns FOA_NOALLOC_OK, or a negative code and a message in `error`.
+// Declared in noalloc.h (return codes and the size limit there too).
 extern "C" __attribute__((visibility("default"))) int foa_paged_decode_noalloc(
     const void* q, void* o, const void* cache, const int32_t* table, const int32_t* segments,
     int num_segments, int q_heads, int kv_heads, int head_dim, float scale, int max_keys,

@@ -42,8 +42,9 @@ void bind_ops(py::module_& m) {
          int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
          long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups,
          int w_scale_rows, const std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>& segments,
-         uint64_t cta_trace) {
+         uint64_t cta_trace, int reduction) {
         foa::GemmArgs g;
+        g.reduction = reduction;
         g.cta_trace = reinterpret_cast<unsigned long long*>(cta_trace);
         g.w_scale_rows = w_scale_rows;
         if (segments.size() > 2) throw std::runtime_error("gemm: at most two extra K segments");
@@ -97,7 +98,7 @@ void bind_ops(py::module_& m) {
       py::arg("a_scale_ld") = 0, py::arg("group_tiles") = 0, py::arg("tile_group") = 0,
       py::arg("group_tile") = 0, py::arg("groups") = 0, py::arg("w_scale_rows") = 128,
       py::arg("segments") = std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>{},
-      py::arg("cta_trace") = 0);
+      py::arg("cta_trace") = 0, py::arg("reduction") = 0);
 
   m.def(
       "quantize_fp8_rows",
@@ -340,14 +341,22 @@ void bind_ops(py::module_& m) {
         [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
                     int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
                     uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
-                    int keys_per_split, uint64_t status, uint64_t stream, uint64_t counters) {
+                    int keys_per_split, uint64_t status, uint64_t stream, uint64_t counters, int warps,
+                    int stages) {
           auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
                              head_dim, scale, partial_o, partial_lse, capacity, max_keys,
                              keys_per_split, status);
+          a.decode_warps = warps;
+          a.decode_stages = stages;
           (void)counters;
           py::gil_scoped_release nogil;
           check(foa::paged_decode(a, as_stream(stream)), "paged_decode");
-        });
+        },
+        py::arg("q"), py::arg("o"), py::arg("cache"), py::arg("table"), py::arg("segments"),
+        py::arg("num_segments"), py::arg("q_heads"), py::arg("kv_heads"), py::arg("head_dim"),
+        py::arg("scale"), py::arg("partial_o"), py::arg("partial_lse"), py::arg("capacity"),
+        py::arg("max_keys"), py::arg("keys_per_split"), py::arg("status"), py::arg("stream"),
+        py::arg("counters") = 0, py::arg("warps") = 0, py::arg("stages") = 0);
   m.def("wait_probe",
         [](uint64_t flag, unsigned long long value, uint64_t limit_ns, uint64_t status, uint64_t stream) {
           check(foa::wait_probe(as_ptr<const unsigned long long>(flag), value, limit_ns, as_ptr<int>(status),

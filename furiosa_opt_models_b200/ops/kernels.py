@@ -161,6 +161,7 @@ def gemm(
     trace: torch.Tensor | None = None,
     segments: list | None = None,
     cta_trace: torch.Tensor | None = None,
+    reduction: int = 0,
 ) -> torch.Tensor:
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
@@ -172,6 +173,7 @@ def gemm(
     ``segments`` [(a1 [M, k1], w1 [N, k1]), ...] (at most two, k a multiple of 64) add
     ``a1 @ w1.T`` and so on into the same FP32 sums before the epilogue (LoRA updates).
     ``trace`` (int64 [8]) and ``cta_trace`` (int64 [4 x CTAs]) receive global-timer milestones.
+    ``reduction`` (measurements) makes split-K partials meet in global scratch (1) or the cluster (2).
     """
     _rowmajor(a, "a")
     M, K = a.shape
@@ -222,7 +224,7 @@ def gemm(
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
         0 if trace is None else trace.data_ptr(), **qargs,
         segments=[(sa.data_ptr(), sa.stride(0), sw.data_ptr(), sw.stride(0), sa.shape[1]) for sa, sw in (segments or [])],
-        cta_trace=0 if cta_trace is None else cta_trace.data_ptr(),
+        cta_trace=0 if cta_trace is None else cta_trace.data_ptr(), reduction=reduction,
     )
     return out
 
@@ -283,9 +285,11 @@ def _attn_common(segments: torch.Tensor) -> None:
 
 
 def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys_per_split=2048, out=None,
-                 counters=None):
+                 counters=None, warps=0, stages=0):
     """Flash-decoding of one-row segments over the paged cache. q: [rows, q_heads, d]. With
-    `counters` (int32, zero, one per segment and key/value head) the splits merge in the kernel."""
+    `counters` (int32, zero, one per segment and key/value head) the splits merge in the kernel.
+    `warps` (2-4) and `stages` (2-3) pick the CTA shape (0: the engine's defaults); measurements
+    compare them."""
     _attn_common(segments)
     rows, q_heads, d = q.shape
     out = torch.empty_like(q) if out is None else out
@@ -299,7 +303,7 @@ def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(), n,
         q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5), po.data_ptr(),
         pl.data_ptr(), need, int(max_keys), keys_per_split, s.status.data_ptr(), _stream(),
-        0 if counters is None else counters.data_ptr())
+        0 if counters is None else counters.data_ptr(), warps, stages)
     return out
 
 

@@ -57,7 +57,8 @@ def gemm(args) -> dict:
     epi = {"bf16": ops.EPI_BF16, "f32": ops.EPI_F32, "swiglu": ops.EPI_SWIGLU}[args.epilogue]
     out = {}
     if copies == 1:
-        us = _time(lambda: ops.gemm(a, ws[0], epilogue=epi, splits=args.splits), args.warmup, args.iters)
+        us = _time(lambda: ops.gemm(a, ws[0], epilogue=epi, splits=args.splits, reduction=args.reduction),
+                   args.warmup, args.iters)
     else:
         # Two traced launches in the middle of the loop: launch `mid` and the one after it.
         tr = torch.zeros(2, 8 * 1024, dtype=torch.int64, device="cuda")
@@ -69,7 +70,7 @@ def gemm(args) -> dict:
                     torch.matmul(a, w.t())  # the library reference point (BF16 only)
                     continue
                 t = tr[i - mid] if trace and i in (mid, mid + 1) else None
-                ops.gemm(a, w, epilogue=epi, splits=args.splits, cta_trace=t)
+                ops.gemm(a, w, epilogue=epi, splits=args.splits, cta_trace=t, reduction=args.reduction)
 
         for _ in range(args.warmup):
             loop()
@@ -122,7 +123,8 @@ def decode_attn(args) -> dict:
     table = torch.arange(rows * nb, dtype=torch.int32, device="cuda")
     seg = torch.tensor([[r, 1, keys - 1, r * nb, nb] for r in range(rows)], dtype=torch.int32, device="cuda")
     q = torch.randn(rows, qh, d, device="cuda").bfloat16()
-    us = _time(lambda: ops.paged_decode(q, cache, table, seg, kvh, keys, keys_per_split=args.split),
+    us = _time(lambda: ops.paged_decode(q, cache, table, seg, kvh, keys, keys_per_split=args.split,
+                                        warps=args.warps, stages=args.stages),
                args.warmup, args.iters)
     kv_bytes = rows * keys * kvh * d * 2 * 2
     return dict(kernel="paged_decode", rows=rows, keys=keys, kv_heads=kvh, split=args.split, us=round(us, 2),
@@ -140,7 +142,8 @@ def prefill_attn(args) -> dict:
     seg = seg_cpu.cuda()
     work = ops.prefill_work(seg_cpu, qh // kvh).cuda()
     q = torch.randn(seqs * per, qh, d, device="cuda").bfloat16()
-    us = _time(lambda: ops.paged_prefill(q, cache, table, seg, kvh, work), args.warmup, args.iters)
+    us = _time(lambda: ops.paged_prefill(q, cache, table, seg, kvh, work, tensor_cores=not args.mma_sync),
+               args.warmup, args.iters)
     flops = seqs * 2 * 2 * qh * d * per * per / 2  # causal: QK and PV over half the square
     return dict(kernel="paged_prefill", rows=seqs * per, seqs=seqs, us=round(us, 2), tflops=round(flops / us / 1e6, 1))
 
@@ -250,17 +253,22 @@ def main() -> None:
     g.add_argument("--cta-trace", action="store_true")
     g.add_argument("--graph", action="store_true")
     g.add_argument("--impl", default="engine", choices=["engine", "cublas"])
+    g.add_argument("--reduction", type=int, default=0, choices=[0, 1, 2],
+                   help="split-K partials meet by the plan's choice (0), global scratch (1) or the cluster (2)")
     d = sub.add_parser("decode-attn")
     d.add_argument("--rows", type=int, default=64)
     d.add_argument("--keys", type=int, default=2048)
     d.add_argument("--q-heads", type=int, default=16)
     d.add_argument("--kv-heads", type=int, default=8)
     d.add_argument("--split", type=int, default=2048, help="keys per split")
+    d.add_argument("--warps", type=int, default=0, help="warps a CTA (2-4; 0 the engine's default)")
+    d.add_argument("--stages", type=int, default=0, help="16-key blocks in flight a warp (2-3; 0 default)")
     f = sub.add_parser("prefill-attn")
     f.add_argument("--rows", type=int, default=8192)
     f.add_argument("--seqs", type=int, default=8)
     f.add_argument("--q-heads", type=int, default=16)
     f.add_argument("--kv-heads", type=int, default=8)
+    f.add_argument("--mma-sync", action="store_true", help="the mma.sync kernel instead of tcgen05")
     m = sub.add_parser("moe")
     m.add_argument("--tokens", type=int, default=64)
     a = sub.add_parser("tp-o-proj")

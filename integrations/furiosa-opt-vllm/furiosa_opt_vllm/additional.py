@@ -31,13 +31,18 @@ class Placement(BaseModel):
     @field_validator("chips")
     @classmethod
     def distinct(cls, chips: tuple[int, ...]) -> tuple[int, ...]:
-        if not chips or len(set(chips)) < len(chips):
-            raise ValueError("one or more distinct chips")
+        seen: set[int] = set()
+        for ordinal in chips:
+            if ordinal in seen:
+                raise ValueError(f"GPU {ordinal} is listed twice")
+            seen.add(ordinal)
+        if not seen:
+            raise ValueError("a placement lists at least one GPU")
         return chips
 
 
 class Section(BaseModel):
-    """The plugin's options, each at its default unless `additional_config["furiosa"]` sets it."""
+    """Options read from `additional_config["furiosa"]`; an option left out keeps its default."""
 
     model_config: ClassVar[ConfigDict] = ConfigDict(frozen=True, extra="forbid")
 

@@ -1,91 +1,75 @@
-"""A scheduled step as the engine sees it: which rows each request contributes, where its history
-starts, and which rows come back (the reference's batch planning,
-integrations/furiosa-opt-vllm/furiosa_opt_vllm/batch.py).
+"""Engine calls of one scheduled step.
 
-Pure host logic, independent of vLLM's classes, so the contract is tested without a framework.
+vLLM schedules rows per request; the engine takes at most `decoder.rows` rows a call and reads each
+request's tokens from one device tensor. This module cuts a step into calls of at most that many
+rows, and each request's rows into runs: rows whose tokens the host holds, and the one row whose
+token is still on the device, the previous step's uncollected output (with async scheduling vLLM
+schedules step n+1 before it has read step n's tokens). Only a request's last run returns rows.
+Slicing follows the reference plugin's step loop over `decoder.rows`
+(integrations/furiosa-opt-vllm/furiosa_opt_vllm/generation/sequence.py there).
+
+Pure host logic, tested without vLLM or a GPU.
 """
 
 from __future__ import annotations
 
 import dataclasses
-from typing import Generic, TypeVar
 
-K = TypeVar("K")
+KEEP_NONE, KEEP_LAST, KEEP_ALL = 0, 1, 2
 
 
 class Framing(ValueError):
-    """The framework's token counts do not frame its tokens."""
-
-    def __init__(self, tokens: int, scheduled: int):
-        super().__init__(f"{tokens} tokens for {scheduled} scheduled")
-        self.tokens = tokens
-        self.scheduled = scheduled
-
-    def __reduce__(self):
-        return (Framing, (self.tokens, self.scheduled))
+    """A request's scheduled rows do not fit what the runner knows about it."""
 
 
 @dataclasses.dataclass(frozen=True)
-class Row:
-    """One scheduled row: its request, the position it writes, whether it is kept."""
+class Scheduled:
+    """One request's rows in a step."""
 
-    key: object
-    position: int
-    kept: bool
-
-
-@dataclasses.dataclass(frozen=True)
-class Request(Generic[K]):
-    """A request's rows in one call: its history length, its row indices, whether it is kept."""
-
-    key: K
-    cached: int
-    rows: tuple[int, ...]
-    kept: bool
+    cached: int  # positions already in the cache
+    rows: int  # rows scheduled this step
+    known: int  # leading rows whose token the host holds; the rest (at most one) is on the device
+    keep: int  # KEEP_NONE, KEEP_LAST (the step's last row) or KEEP_ALL
 
 
 @dataclasses.dataclass(frozen=True)
-class Call(Generic[K]):
-    requests: tuple[Request[K], ...]
-    kept: tuple[int, ...]
+class Run:
+    """Consecutive rows of one request inside one engine call."""
 
-    @classmethod
-    def plan(cls, rows: tuple[Row, ...], every: bool) -> "Call[K]":
-        """Groups consecutive rows of one request (a chunk) in order; keeps the last row of each
-        kept request, or every row (pooling) with ``every``."""
-        reqs: list[Request] = []
-        kept: list[int] = []
-        for i, row in enumerate(rows):
-            if reqs and reqs[-1].key == row.key and reqs[-1].rows[-1] == i - 1:
-                last = reqs[-1]
-                reqs[-1] = Request(last.key, last.cached, last.rows + (i,), last.kept or row.kept)
-            else:
-                reqs.append(Request(row.key, row.position, (i,), row.kept))
-            if every or row.kept:
-                kept.append(i)
-        return cls(tuple(reqs), tuple(kept))
+    seq: int  # the request's index in the step
+    cached: int  # positions in the cache before the run
+    offset: int  # the run's first row among the request's scheduled rows
+    rows: int
+    keep: int  # KEEP_* for this run (KEEP_LAST only on the request's final run)
+    device: bool  # the run is the one row read from the previous step's device output
 
 
-@dataclasses.dataclass(frozen=True)
-class Batch:
-    """Tokens of each scheduled request (copied, so the framework may reuse its buffers) and the
-    history each starts after."""
+def plan(step: list[Scheduled], rows: int) -> list[list[Run]]:
+    """Calls of at most `rows` rows covering every scheduled row in step order."""
+    if rows <= 0:
+        raise ValueError("a call takes at least one row")
+    calls: list[list[Run]] = [[]]
+    free = rows
+    for seq, s in enumerate(step):
+        if s.rows <= 0 or not 0 <= s.known <= s.rows or s.rows - s.known > 1:
+            raise Framing(f"request {seq}: {s.rows} rows with {s.known} known (at most one on the device)")
+        pieces = [(0, s.known, False)] if s.known else []
+        if s.known < s.rows:
+            pieces.append((s.known, 1, True))
+        for offset, n, device in pieces:
+            while n:
+                if free == 0:
+                    calls.append([])
+                    free = rows
+                take = min(n, free)
+                last = offset + take == s.rows
+                keep = s.keep if s.keep == KEEP_ALL else (KEEP_LAST if last and s.keep == KEEP_LAST else KEEP_NONE)
+                calls[-1].append(Run(seq, s.cached + offset, offset, take, keep, device))
+                offset += take
+                n -= take
+                free -= take
+    return [c for c in calls if c]
 
-    tokens: tuple[tuple[int, ...], ...]
-    cached: tuple[int, ...]
 
-    @classmethod
-    def parse(cls, tokens, lengths, totals) -> "Batch":
-        """``tokens`` concatenated per request, ``lengths`` scheduled per request, ``totals`` the
-        positions each request reaches after the step."""
-        if len(lengths) != len(totals):
-            raise Framing(len(tokens), sum(lengths))
-        if any(n <= 0 for n in lengths) or any(t < n for n, t in zip(lengths, totals)):
-            raise Framing(len(tokens), sum(max(n, 0) for n in lengths))
-        if sum(lengths) != len(tokens):
-            raise Framing(len(tokens), sum(lengths))
-        out, at = [], 0
-        for n in lengths:
-            out.append(tuple(int(t) for t in tokens[at : at + n]))
-            at += n
-        return cls(tuple(out), tuple(t - n for n, t in zip(lengths, totals)))
+def kept_rows(run: Run) -> int:
+    return run.rows if run.keep == KEEP_ALL else (1 if run.keep == KEEP_LAST else 0)

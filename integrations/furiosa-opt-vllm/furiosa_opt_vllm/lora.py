@@ -1,112 +1,144 @@
-"""vLLM's LoRA adapters as engine adapters (the reference's behaviour:
-integrations/furiosa-opt-vllm/furiosa_opt_vllm/lora.py).
+"""vLLM LoRA requests served as engine adapters.
 
-- Loaded adapters, by LoRA ID: the worker's `add_lora`, or a step whose request names an adapter,
-  reads the adapter's PEFT checkpoint onto the device (again when the request loads in place).
-  Up to `max_cpu_loras` (else `max_loras`) stay loaded, least recently used out first.
-- Slots: the adapters list every engine call takes, `max_loras` of them (at most the engine's
-  SLOTS). Each engine request names its sequence's slot.
-- A pinned adapter stays loaded and in its slot until removed. Making room never evicts a pinned
-  adapter or one the step runs; when only such adapters could make room the call is refused before
-  anything changes.
+The engine takes a fixed list of adapter slots with every call (``decoder.adapters`` of them) and
+each engine request names the slot of its adapter. vLLM names adapters by LoRA ID and may ask for
+more of them than fit on the device. This module keeps:
+
+- a table of loaded adapters (LoRA ID -> engine adapter, the clock tick of its last use and its
+  pin), at most ``max_cpu_loras`` (else ``max_loras``) entries;
+- a lease per engine slot (the LoRA ID that holds it), ``max_loras`` slots.
+
+Whenever an adapter has to come in, the entry (or lease) with the oldest tick that is neither
+pinned nor needed by the current step goes out. Every decision is made before anything changes,
+so a refused step leaves the table as it was. Behaviour follows the reference plugin's LoRA
+support (integrations/furiosa-opt-vllm/furiosa_opt_vllm/lora.py there): LRU unloading, pins that
+keep their slot, and refusal when only pinned or running adapters could make room.
 """
 
 from __future__ import annotations
 
+import dataclasses
+import itertools
 import json
-from collections import OrderedDict
 from pathlib import Path
 
 
+@dataclasses.dataclass
+class _Entry:
+    adapter: object
+    tick: int
+    pinned: bool = False
+
+
 class Adapters:
+    """LoRA adapters of one worker: loaded entries and the engine's slot leases."""
+
     def __init__(self, max_loras: int, max_cpu_loras: int | None, spec, read=None):
         self.max_loras = max_loras
         self.capacity = max_cpu_loras or max_loras
         self.spec = spec
-        self._read_fn = read  # (lora_request) -> engine adapter; tests give their own
-        self.loaded: OrderedDict[int, object] = OrderedDict()  # LoRA ID -> adapter, LRU first
-        self.held: OrderedDict[int, int] = OrderedDict()  # LoRA ID -> slot, LRU first
-        self.pins: set[int] = set()
-        self.slots: list = [None] * max_loras
+        self._reader = read  # lora_request -> engine adapter (tests pass their own)
+        self._entries: dict[int, _Entry] = {}
+        self._lease: list[int | None] = [None] * max_loras  # LoRA ID holding each slot
+        self._clock = itertools.count(1)
 
-    # ---------------------------------------------------------------- worker API
-    def add(self, request, keep: frozenset = frozenset()) -> bool:
+    # ------------------------------------------------------------------ what the engine call takes
+    @property
+    def slots(self) -> list:
+        """The engine adapter in each slot (None for a free slot), in slot order."""
+        return [None if lid is None else self._entries[lid].adapter for lid in self._lease]
+
+    def slot_of(self, lid: int) -> int | None:
+        return self._lease.index(lid) if lid in self._lease else None
+
+    # ------------------------------------------------------------------ the worker's LoRA calls
+    def add(self, request, step: frozenset = frozenset()) -> bool:
+        """Loads `request`'s adapter (again when it asks to load in place) and gives it a slot."""
         lid = request.lora_int_id
-        unload, displace = self._room(lid, keep)
-        if lid not in self.loaded or getattr(request, "load_inplace", False):
-            adapter = self._read(request)
+        protected = step | {lid}
+        unload = None
+        if lid not in self._entries and len(self._entries) >= self.capacity:
+            unload = self._oldest(self._entries, protected)
+            if unload is None:
+                raise RuntimeError(f"LoRA adapter {lid} cannot load: the {self.capacity} loaded adapters are "
+                                   "pinned or used by this step (raise --max-cpu-loras)")
+        slot = self._plan_slot(lid, protected, freed=unload)
+        if lid not in self._entries or getattr(request, "load_inplace", False):
+            adapter = self._read(request)  # may raise: nothing has changed yet
             if unload is not None:
                 self.remove(unload)
-            self.loaded[lid] = adapter
-        self.loaded.move_to_end(lid)
-        self._hold(lid, displace)
+            if lid in self._entries:
+                self._entries[lid].adapter = adapter
+            else:
+                self._entries[lid] = _Entry(adapter, 0)
+        self._take(lid, slot)
         return True
 
     def remove(self, lid: int) -> bool:
-        self.pins.discard(lid)
-        slot = self.held.pop(lid, None)
+        slot = self.slot_of(lid)
         if slot is not None:
-            self.slots[slot] = None
-        return self.loaded.pop(lid, None) is not None
+            self._lease[slot] = None
+        return self._entries.pop(lid, None) is not None
 
     def pin(self, lid: int) -> bool:
-        if lid not in self.loaded:
+        if lid not in self._entries:
             raise ValueError(f"LoRA adapter {lid} is not loaded")
-        _, displace = self._room(lid, frozenset())
-        self._hold(lid, displace)
-        self.pins.add(lid)
+        self._take(lid, self._plan_slot(lid, frozenset({lid})))
+        self._entries[lid].pinned = True
         return True
 
     def ids(self) -> set[int]:
-        return set(self.loaded)
+        return set(self._entries)
 
-    # ---------------------------------------------------------------- a step
+    # ------------------------------------------------------------------ a step
     def activate(self, named: dict) -> dict:
-        """The slot of each request ID in `named` (request ID -> LoRA request), once every adapter
-        of the step is loaded and holds a slot."""
-        adapters = {r.lora_int_id: r for r in named.values()}
-        if len(adapters) > self.max_loras:
-            raise RuntimeError(f"a step runs {len(adapters)} adapters, above --max-loras")
-        step = frozenset(adapters)
-        for r in adapters.values():
+        """Loads and seats every adapter a step names (request ID -> LoRA request); returns each
+        request ID's slot."""
+        wanted = {r.lora_int_id: r for r in named.values()}
+        if len(wanted) > self.max_loras:
+            raise RuntimeError(f"a step runs {len(wanted)} adapters, above --max-loras ({self.max_loras})")
+        step = frozenset(wanted)
+        for r in wanted.values():
             self.add(r, step)
-        return {rid: self.held[r.lora_int_id] for rid, r in named.items()}
+        return {rid: self.slot_of(r.lora_int_id) for rid, r in named.items()}
 
-    # ---------------------------------------------------------------- room
-    def _room(self, lid: int, keep: frozenset):
-        kept = self.pins | set(keep) | {lid}
-        unload = None
-        if lid not in self.loaded and len(self.loaded) >= self.capacity:
-            unload = next((o for o in self.loaded if o not in kept), None)
-            if unload is None:
-                raise RuntimeError(f"LoRA adapter {lid}: the {self.capacity} loaded adapters are pinned or in use; "
-                                   "raise --max-cpu-loras")
-        holders = [o for o in self.held if o != unload]
-        displace = None
-        if lid not in self.held and len(holders) >= self.max_loras:
-            displace = next((o for o in holders if o not in kept), None)
-            if displace is None:
-                raise RuntimeError(f"LoRA adapter {lid}: pinned or running adapters hold every slot; raise --max-loras")
-        return unload, displace
+    # ------------------------------------------------------------------ bookkeeping
+    def _oldest(self, ids, protected) -> int | None:
+        """The least recently used of `ids` that is neither pinned nor protected."""
+        free = [i for i in ids if i not in protected and not self._entries[i].pinned]
+        return min(free, key=lambda i: self._entries[i].tick) if free else None
 
-    def _hold(self, lid: int, displace) -> None:
-        if displace is not None:
-            self.slots[self.held.pop(displace)] = None
-        slot = self.held.pop(lid, None)
-        if slot is None:
-            slot = min(set(range(self.max_loras)) - set(self.held.values()))
-        self.held[lid] = slot
-        self.slots[slot] = self.loaded[lid]
+    def _plan_slot(self, lid: int, protected, freed: int | None = None) -> int:
+        """The slot `lid` will hold: its own, else the lowest free one (or the one `freed` gives
+        up), else the lease of the least recently used unprotected holder."""
+        own = self.slot_of(lid)
+        if own is not None:
+            return own
+        for s, holder in enumerate(self._lease):
+            if holder is None or holder == freed:
+                return s
+        victim = self._oldest([h for h in self._lease if h is not None], protected)
+        if victim is None:
+            raise RuntimeError(f"LoRA adapter {lid} gets no slot: pinned or running adapters hold every "
+                               "slot (raise --max-loras)")
+        return self._lease.index(victim)
+
+    def _take(self, lid: int, slot: int) -> None:
+        own = self.slot_of(lid)
+        if own is not None and own != slot:
+            self._lease[own] = None
+        self._lease[slot] = lid
+        self._entries[lid].tick = next(self._clock)
 
     def _read(self, request):
-        if self._read_fn is not None:
-            return self._read_fn(request)
+        if self._reader is not None:
+            return self._reader(request)
         import furiosa_opt_engine as engine
 
         if getattr(request, "tensorizer_config_dict", None) is not None:
-            raise ValueError(f"LoRA adapter {request.lora_name}: reads no tensorizer checkpoint")
+            raise ValueError(f"LoRA adapter {request.lora_name}: tensorizer checkpoints are not read, only PEFT")
         path = Path(request.lora_path)
         if not (path / "adapter_model.safetensors").is_file():
-            raise ValueError(f"LoRA adapter {request.lora_name}: reads adapter_model.safetensors")
+            raise ValueError(f"LoRA adapter {request.lora_name}: no adapter_model.safetensors in {path}")
         config = json.loads((path / "adapter_config.json").read_text())
         return engine.decoder.Adapter(self.spec, engine.Checkpoint(str(path), config))

@@ -1,6 +1,6 @@
 """vLLM platform for B200 through the engine: vLLM's CUDA platform, with the plugin's worker,
-16-token KV pages, no torch.compile or vLLM CUDA graphs (the engine captures its own), synchronous
-scheduling, and the plugin's refusals (the reference's platform:
+16-token KV pages, no torch.compile or vLLM CUDA graphs (the engine captures its own), async
+scheduling without speculation, and the plugin's refusals (the reference's platform:
 integrations/furiosa-opt-vllm/furiosa_opt_vllm/platform.py)."""
 
 from __future__ import annotations
@@ -33,7 +33,11 @@ class B200Platform(NvmlCudaPlatform):
         super().check_and_update_config(vllm_config)
         pc.worker_cls = "furiosa_opt_vllm.worker.Worker"
         cc.block_size = 16
-        vllm_config.scheduler_config.async_scheduling = False
+        # Async scheduling (vLLM issues step n+1 before it reads step n's tokens; the worker keeps
+        # greedy tokens on the device meanwhile) as vLLM decided it, except with speculation: the
+        # n-gram proposer reads every step's tokens on the host before the next step.
+        if vllm_config.speculative_config is not None:
+            vllm_config.scheduler_config.async_scheduling = False
         mc = vllm_config.model_config
         if mc is not None:
             mc.enforce_eager = True

@@ -17,6 +17,8 @@ class State:
     max_tokens: int | None = None
     lora: object = None  # vLLM's LoRARequest of the sequence, or None
     pool: object = None  # pooling.Pool of a pooling request, or None
+    # The newest sampled token while it is still on the device: (engine output, row), or None.
+    tail: tuple | None = None
 
     def scheduled(self, n: int) -> list[int]:
         """The `n` tokens this step feeds (after the history)."""

@@ -1,17 +1,21 @@
-"""vLLM's sleep mode and weight reloads on the engine: device memory is freed by dropping what
-holds it (the loaded decoder, the KV cache) and returning the engine's cached blocks to the
-driver; waking loads or allocates it again (the reference's behaviour:
-integrations/furiosa-opt-vllm/furiosa_opt_vllm/residency.py).
+"""Sleep mode and weight reloads for vLLM on the engine.
 
-- Sleep mode needs `enable_sleep_mode`, under which a load keeps a host copy of the checkpoint's
-  tensors (`Checkpoint.read()`). Level 1 keeps that copy and waking loads from it; level 2 and
-  `discard` drop it, and waking reads the checkpoint's files again.
-- A released KV cache keeps its block count, from which waking allocates it at once (its contents
-  are gone: vLLM sleeps between requests).
-- Waking restores one tag after another, each awake once restored, so a retry after a failure
-  restores only what still sleeps. Releasing goes the other way (cache first).
-- `reload` loads the awake weights again from the checkpoint's files, into the device memory the
-  served ones free first; files that cannot be read keep the served weights.
+Device memory goes back to the driver when its owners are dropped: the loaded decoder (weights)
+and the KV cache, after which the engine hands its cached device blocks back (`_device_trim`).
+Waking rebuilds them. vLLM's sleep API (`sleep`, `wake_up` with tags, `reload_weights`) is served
+as the reference plugin serves it (integrations/furiosa-opt-vllm/furiosa_opt_vllm/residency.py
+there), with this engine's objects:
+
+- Only a load made under `enable_sleep_mode` can sleep: such a load keeps the checkpoint's tensors
+  in host memory (`Checkpoint.read()`). Sleeping at level 1 keeps that host copy for the wake-up;
+  level 2, or `discard`, lets it go, and the wake-up opens the checkpoint files instead.
+- The KV cache remembers how many blocks it had, so waking allocates it again in one step. What it
+  held is lost, which is fine: vLLM sleeps only with no request in flight.
+- Tags wake in a fixed order and each counts as awake as soon as it is restored; after a failure a
+  second `wake_up` restores only the tags still asleep. Release runs in the opposite order, the cache
+  before the weights.
+- `reload` frees the served weights' device memory first, then loads the checkpoint files again;
+  when the files cannot be read the served weights stay in place.
 """
 
 from __future__ import annotations

@@ -10,9 +10,40 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import pooling, speculation
+from . import batch, pooling, speculation
 from .paging import BlockTable, first_group
 from .request import State
+
+
+class Pending:
+    """A step's sampled tokens, still on the device until `collect()` reads them (once)."""
+
+    def __init__(self, runner: "Runner", order, drafts, kept):
+        self.runner, self.order, self.drafts, self.kept = runner, order, drafts, kept
+
+    def collect(self) -> tuple[list[str], list[list[int]]]:
+        host: dict[int, list[int]] = {}  # one device-to-host read per engine call
+        sampled = []
+        for rid, d, runs in zip(self.order, self.drafts, self.kept):
+            rows = []
+            for out, first, n in runs:
+                key = id(out)
+                if key not in host:
+                    host[key] = out.to_host().numpy().tolist()
+                rows += [int(t) for t in host[key][first : first + n]]
+            st = self.runner.states.get(rid)
+            if d:
+                # Every fed row came back; the targets start at the newest known token's row.
+                fed = len(rows) - len(d)
+                got = speculation.accept(d, rows[fed - 1 :])
+                if st is not None:
+                    st.computed -= len(d) - (len(got) - 1)
+            else:
+                got = rows
+            if st is not None:
+                st.tokens.extend(got)
+            sampled.append(got)
+        return self.order, sampled
 
 
 class Runner:
@@ -52,38 +83,44 @@ class Runner:
                 st.table.replace(first_group(nb))
                 if rid in all_tokens:
                     st.tokens = list(all_tokens[rid])
+                    st.tail = None
             elif nb is not None:
                 st.table.append(first_group(nb))
             st.computed = cr.num_computed_tokens[i]
 
-    # -------------------------------------------------------------------- one call
-    def step(self, so) -> tuple[list[str], list[list[int]]]:
-        """Runs the scheduled rows; returns (request IDs in order, sampled tokens per request).
-        For a pooling model the tokens are empty and `pooled` holds each request's output."""
+    # -------------------------------------------------------------------- one step
+    def step(self, so, collect: bool = True):
+        """Runs the scheduled rows in calls of at most `decoder.rows` rows.
+
+        With `collect` it returns (request IDs in order, sampled tokens per request). Without it
+        (async scheduling, greedy, no drafts) it returns a `Pending` whose `collect()` reads the
+        tokens later: each sampling request's token stays on the device, and the next step, which
+        vLLM schedules before collecting this one, reads its input token from there. For a pooling
+        model the tokens are empty and `pooled` holds each request's output."""
         if self.pooling_config is not None:
             return self.pool_step(so)
         self.update(so)
         order = list(so.num_scheduled_tokens.keys())
         if not order:
-            return [], []
+            return ([], []) if collect else Pending(self, [], [], [])
         counts = [int(so.num_scheduled_tokens[r]) for r in order]
         spec = getattr(so, "scheduled_spec_decode_tokens", None) or {}
         drafts = [list(spec.get(r, ())) for r in order]
-        flat = np.empty(sum(counts), dtype=np.int32)
-        keeps, at = [], 0
+        step, hosts = [], []
         for rid, n, d in zip(order, counts, drafts):
             st = self.states[rid]
-            known = n - len(d)
-            if d and not st.samples_after(known):
+            fed = n - len(d)  # rows of tokens the request has (known, or in flight on the device)
+            on_device = max(0, st.computed + fed - len(st.tokens))
+            if on_device and (st.tail is None or d or on_device > 1):
+                raise ValueError(f"{rid}: {fed} rows scheduled after {st.computed} of {len(st.tokens)} known tokens")
+            samples = st.computed + fed == len(st.tokens) + on_device
+            if d and not samples:
                 raise ValueError(f"{rid}: drafts scheduled before the newest token was fed")
-            flat[at : at + known] = st.scheduled(known)
-            flat[at + known : at + n] = d
-            # Rows the call returns: every row of a request with drafts (the target's token after
-            # each fed token), else the last row when it samples.
-            keeps.append(n if d else int(st.samples_after(known)))
-            at += n
-        tokens = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device)
-        # Adapters: each sequence naming a LoRA runs with its slot of this call's list.
+            hosts.append(st.scheduled(fed - on_device) + d)
+            keep = batch.KEEP_ALL if d else (batch.KEEP_LAST if samples else batch.KEEP_NONE)
+            # The device row is the request's last fed row; drafts (host tokens) never follow it.
+            step.append(batch.Scheduled(st.computed, n, n - on_device, keep))
+        # Adapters: each sequence naming a LoRA runs with its slot of this step's list.
         slots, adapters = {}, None
         if self.adapters is not None:
             named = {rid: self.states[rid].lora for rid in order
@@ -91,30 +128,41 @@ class Runner:
             if named:
                 slots = self.adapters.activate(named)
                 adapters = list(self.adapters.slots)
-        reqs, at = [], 0
-        for rid, n, keep, d in zip(order, counts, keeps, drafts):
-            st = self.states[rid]
-            mode = self.dec.Keep.ALL if d else (self.dec.Keep.LAST if keep else self.dec.Keep.NONE)
-            reqs.append(self.dec.Request([st.table.blocks], st.computed, tokens[at : at + n], mode,
-                                         adapter=slots.get(rid)))
-            at += n
-        out = self.model.forward(reqs, self.cache, adapters)
-        picked = out.to_host().numpy().tolist() if any(keeps) else []
-        sampled, k = [], 0
-        for rid, n, keep, d in zip(order, counts, keeps, drafts):
+        kept: list[list] = [[] for _ in order]  # (output, first row, rows) of each request's kept runs
+        for call in batch.plan(step, int(self.model.rows)):
+            host_rows = [r for r in call if not r.device]
+            flat = np.empty(max(sum(r.rows for r in host_rows), 1), dtype=np.int32)
+            at = 0
+            for r in host_rows:
+                flat[at : at + r.rows] = hosts[r.seq][r.offset : r.offset + r.rows]
+                at += r.rows
+            tokens = self.engine.HostTensor.from_dlpack(flat).to_hbm(self.device) if host_rows else None
+            reqs, at = [], 0
+            for r in call:
+                st = self.states[order[r.seq]]
+                if r.device:
+                    src, row = st.tail
+                    toks = src[row : row + 1]
+                else:
+                    toks = tokens[at : at + r.rows]
+                    at += r.rows
+                mode = (self.dec.Keep.ALL if r.keep == batch.KEEP_ALL else
+                        self.dec.Keep.LAST if r.keep == batch.KEEP_LAST else self.dec.Keep.NONE)
+                reqs.append(self.dec.Request([st.table.blocks], r.cached, toks, mode, adapter=slots.get(order[r.seq])))
+            out = self.model.forward(reqs, self.cache, adapters)
+            k = 0
+            for r in call:
+                n = batch.kept_rows(r)
+                if n:
+                    kept[r.seq].append((out, k, n))
+                k += n
+        for i, (rid, n, d) in enumerate(zip(order, counts, drafts)):
             st = self.states[rid]
             st.computed += n
-            rows = [int(t) for t in picked[k : k + keep]]
-            k += keep
-            if d:
-                # Every fed row came back; the targets start at the newest known token's row.
-                got = speculation.accept(d, rows[n - len(d) - 1 :])
-                st.computed -= len(d) - (len(got) - 1)
-            else:
-                got = rows
-            st.tokens.extend(got)
-            sampled.append(got)
-        return order, sampled
+            # The newest sampled token stays on the device until collected; the next step reads it.
+            st.tail = (kept[i][-1][0], kept[i][-1][1] + kept[i][-1][2] - 1) if kept[i] and not d else None
+        pending = Pending(self, order, drafts, kept)
+        return pending.collect() if collect else pending
 
     def pool_step(self, so) -> tuple[list[str], list[list[int]]]:
         """A step of a pooling model: prompt chunks whose kept rows (hidden values or label

@@ -8,13 +8,26 @@ integrations/furiosa-opt-vllm/furiosa_opt_vllm/worker.py)."""
 from __future__ import annotations
 
 import torch
-from vllm.v1.outputs import ModelRunnerOutput
+from vllm.v1.outputs import AsyncModelRunnerOutput, ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
 from . import admission, lora, pooling, residency, speculation
 from . import cache as kv
 from . import load
 from .runner import Runner
+
+
+class Collected(AsyncModelRunnerOutput):
+    """A greedy step's output whose tokens are still on the device: `get_output` reads them (vLLM
+    calls it after issuing the next step, so the device works while the host schedules)."""
+
+    def __init__(self, pending):
+        self.pending = pending
+
+    def get_output(self) -> ModelRunnerOutput:
+        ids, sampled = self.pending.collect()
+        return ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
+                                 sampled_token_ids=sampled)
 
 
 class Worker(WorkerBase):
@@ -183,6 +196,10 @@ class Worker(WorkerBase):
             self.runner.update(scheduler_output)
             self.pending = ModelRunnerOutput(req_ids=[], req_id_to_index={})
             return None
+        if self.asynchronous():
+            # The tokens stay on the device; vLLM collects them after it has issued the next step.
+            self.pending = Collected(self.runner.step(scheduler_output, collect=False))
+            return None
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
                                          sampled_token_ids=sampled,
@@ -193,6 +210,11 @@ class Worker(WorkerBase):
             histories = [self.runner.states[r].tokens for r in ids]
             self.drafts = DraftTokenIds(ids, self.proposer.propose(sampled, histories))
         return None
+
+    def asynchronous(self) -> bool:
+        """Greedy steps under vLLM's async scheduling: no pooling, no drafts to propose."""
+        sc = getattr(self.vllm_config, "scheduler_config", None)
+        return bool(getattr(sc, "async_scheduling", False)) and not self.pooling and self.proposer is None
 
     def sample_tokens(self, grammar_output=None):
         out, self.pending = self.pending, None

@@ -72,3 +72,24 @@ def test_paged_prefill_long_prompts():
     torch.cuda.synchronize()
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 3e-2, err
+
+
+def test_paged_decode_history_beyond_max_keys():
+    """A segment longer than the launch's max_keys has more splits than the scratch was laid out
+    for: its row is zeros and the status word records a bad argument; the other rows are exact."""
+    from furiosa_opt_models_b200 import ops
+    from furiosa_opt_models_b200.models import reference
+
+    cached = [5, 300, 1500]  # max_keys 1024 below: the last row does not fit
+    q, cache, table, segs = _setup([1] * 3, cached, 16, 8, 128)
+    ref = reference.paged_attention(q, cache, table, segs)
+    s = ops.scratch(torch.device("cuda", 0))
+    s.status.zero_()
+    for split in (512, 1024):  # two splits a row, and one split, each overflowed by the long row
+        out = ops.paged_decode(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), 8, max_keys=1024,
+                               keys_per_split=split)
+        torch.cuda.synchronize()
+        assert int(s.status[0].item()) == 7  # kBadArgument
+        s.status.zero_()
+        assert torch.count_nonzero(out[2]).item() == 0
+        assert (out[:2].float().cpu() - ref[:2]).abs().max().item() < 2e-2

@@ -1,7 +1,5 @@
-"""The plugin's host contracts without a GPU: batch framing and planning, block tables, request
-state, refusals."""
-
-import pickle
+"""The plugin's host contracts without a GPU: step planning, block tables, request state, the
+runner's async collection on a host fake of the engine, refusals."""
 
 import pytest
 
@@ -9,28 +7,127 @@ from furiosa_opt_vllm import admission, batch, paging
 from furiosa_opt_vllm.request import State
 
 
-def test_call_groups_chunks_and_keeps_last_rows():
-    rows = (batch.Row("a", 5, False), batch.Row("a", 6, True), batch.Row("b", 0, False))
-    call = batch.Call[str].plan(rows, every=False)
-    assert call.requests == (batch.Request("a", 5, (0, 1), True), batch.Request("b", 0, (2,), False))
-    assert call.kept == (1,)
-    assert batch.Call[int].plan((batch.Row(0, 4, False), batch.Row(1, 0, True)), every=True).kept == (0, 1)
+def test_step_plan_slices_calls_to_the_decoder_rows():
+    S = batch.Scheduled
+    step = [S(0, 5, 5, batch.KEEP_LAST), S(10, 1, 0, batch.KEEP_LAST), S(3, 4, 4, batch.KEEP_NONE)]
+    calls = batch.plan(step, rows=4)
+    assert [[(r.seq, r.cached, r.offset, r.rows, r.keep, r.device) for r in c] for c in calls] == [
+        [(0, 0, 0, 4, batch.KEEP_NONE, False)],
+        [(0, 4, 4, 1, batch.KEEP_LAST, False), (1, 10, 0, 1, batch.KEEP_LAST, True),
+         (2, 3, 0, 2, batch.KEEP_NONE, False)],
+        [(2, 5, 2, 2, batch.KEEP_NONE, False)],
+    ]
+    assert all(sum(r.rows for r in c) <= 4 for c in calls)
+    # Every row of a request with drafts comes back, whichever call holds it.
+    every = batch.plan([S(0, 3, 3, batch.KEEP_ALL)], rows=2)
+    assert [batch.kept_rows(r) for c in every for r in c] == [2, 1]
+    # A request's known rows come before its device row, which is its last.
+    mixed = batch.plan([S(7, 3, 2, batch.KEEP_LAST)], rows=8)[0]
+    assert [(r.cached, r.rows, r.keep, r.device) for r in mixed] == [(7, 2, batch.KEEP_NONE, False),
+                                                                      (9, 1, batch.KEEP_LAST, True)]
 
 
-def test_batch_copies_tokens_and_derives_history():
-    tokens = [1, 2, 3]
-    parsed = batch.Batch.parse(tokens, [2, 1], [7, 1])
-    tokens[0] = 9
-    assert parsed.tokens == ((1, 2), (3,))
-    assert parsed.cached == (5, 0)
+@pytest.mark.parametrize("bad", [batch.Scheduled(0, 0, 0, 0), batch.Scheduled(0, 3, 1, 1), batch.Scheduled(0, 2, 3, 1)])
+def test_step_plan_refuses_bad_framing(bad):
+    with pytest.raises(batch.Framing):
+        batch.plan([bad], rows=8)
 
 
-@pytest.mark.parametrize(("tokens", "lengths", "totals"), [([1], [2], [2]), ([1, 1], [0, 2], [1, 2]), ([1], [1], [0])])
-def test_batch_refuses_bad_framing(tokens, lengths, totals):
-    with pytest.raises(batch.Framing) as e:
-        batch.Batch.parse(tokens, lengths, totals)
-    restored = pickle.loads(pickle.dumps(e.value))
-    assert (restored.tokens, restored.scheduled) == (e.value.tokens, e.value.scheduled)
+class _FakeTensor:
+    def __init__(self, values):
+        self.values = list(values)
+
+    def __getitem__(self, sl):
+        return _FakeTensor(self.values[sl])
+
+    def numpy(self):
+        import numpy as np
+
+        return np.asarray(self.values, dtype=np.int32)
+
+    def to_host(self):
+        self.reads += 1
+        return self
+
+    reads = 0
+
+
+class _FakeEngine:
+    """Decoder calls on the host: each kept row's token is (its input token + 1)."""
+
+    class HostTensor:
+        @staticmethod
+        def from_dlpack(a):
+            return _FakeHost(a)
+
+    def __init__(self, rows):
+        from types import SimpleNamespace
+
+        self.rows = rows
+        self.calls = []
+        self.dec = SimpleNamespace(
+            Keep=SimpleNamespace(ALL="all", LAST="last", NONE="none"),
+            Request=lambda blocks, cached, tokens, keep, adapter=None: (cached, tokens, keep))
+
+    def forward(self, reqs, cache, adapters=None):
+        assert sum(len(t.values) for _, t, _ in reqs) <= self.rows
+        self.calls.append(reqs)
+        out = []
+        for _, t, keep in reqs:
+            if keep == "all":
+                out += [v + 1 for v in t.values]
+            elif keep == "last":
+                out.append(t.values[-1] + 1)
+        return _FakeTensor(out)
+
+
+class _FakeHost:
+    def __init__(self, a):
+        self.a = a
+
+    def to_hbm(self, device):
+        return _FakeTensor(self.a.tolist())
+
+
+def _runner(rows):
+    from types import SimpleNamespace
+
+    from furiosa_opt_vllm.runner import Runner
+
+    eng = _FakeEngine(rows)
+    r = Runner.__new__(Runner)
+    r.engine, r.dec = SimpleNamespace(HostTensor=_FakeEngine.HostTensor), eng.dec
+    r.model, r.device, r.cache, r.adapters, r.pooling_config, r.pooled, r.states = eng, None, None, None, None, [], {}
+    return r, eng
+
+
+def _sched(new=(), cached=(), counts=None):
+    from types import SimpleNamespace
+
+    cr = SimpleNamespace(req_ids=[c[0] for c in cached], new_block_ids=[None] * len(cached),
+                         num_computed_tokens=[c[1] for c in cached], resumed_req_ids=set(), all_token_ids={})
+    return SimpleNamespace(finished_req_ids=[], scheduled_new_reqs=list(new), scheduled_cached_reqs=cr,
+                           num_scheduled_tokens=counts, scheduled_spec_decode_tokens={})
+
+
+def test_runner_keeps_greedy_tokens_on_the_device_until_collected():
+    """Async scheduling: step n+1 is issued before step n is collected; its input token is step n's
+    device output, and the step is cut into calls of at most `rows` rows."""
+    from types import SimpleNamespace
+
+    runner, eng = _runner(rows=4)
+    new = [SimpleNamespace(req_id=r, prompt_token_ids=p, num_computed_tokens=0, block_ids=([0, 1],))
+           for r, p in (("a", [10, 11, 12]), ("b", [20, 21]))]
+    first = runner.step(_sched(new=new, counts={"a": 3, "b": 2}), collect=False)
+    assert len(eng.calls) == 2  # 5 rows over calls of 4
+    second = runner.step(_sched(cached=[("a", 3), ("b", 2)], counts={"a": 1, "b": 1}), collect=False)
+    # The decode rows read the first step's device outputs (13 and 22), never a host copy.
+    assert [t.values for _, t, _ in eng.calls[-1]] == [[13], [22]]
+    assert first.collect() == (["a", "b"], [[13], [22]])
+    assert second.collect() == (["a", "b"], [[14], [23]])
+    assert runner.states["a"].tokens == [10, 11, 12, 13, 14]
+    third = runner.step(_sched(cached=[("a", 4), ("b", 3)], counts={"a": 1, "b": 1}))
+    assert third == (["a", "b"], [[15], [24]])
 
 
 def test_block_tables_grow_and_resume():
