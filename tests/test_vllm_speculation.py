@@ -52,6 +52,8 @@ class FakeTensor:
 class FakeModel:
     """Greedy token after each kept row: a function of that row's token."""
 
+    rows = 8192  # rows a call takes
+
     def __init__(self, keep):
         self.keep = keep
         self.calls = []
