@@ -811,7 +811,7 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
                                  cfg_.qk_norm ? w(p + "q_norm") : nullptr,
                                  cfg_.qk_norm ? w(p + "k_norm") : nullptr, cfg_.eps,
                                  i32(stage, sg.positions), rope, bf(ws_q_), layer_cache,
-                                 i32(stage, sg.slots), s),
+                                 i32(stage, sg.slots), s, cache.blocks() * 16, st->status),
          "attention front");
     attn.cache = layer_cache;
     if (plan.decode > 0) {

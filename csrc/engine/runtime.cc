@@ -132,10 +132,13 @@ void DeviceState::raise_status(int code) {
                                "an accumulator was never completed",
                                "an accumulator was never released",
                                "a peer rank never raised its flag",
-                               "copies in flight did not land while aborting"};
-  const std::string reason = code > 0 && code < 7 ? what[code] : "unknown";
+                               "copies in flight did not land while aborting",
+                               "a launch argument failed a device-side check",
+                               "an index read from device memory (a block ID or cache slot) was out of range"};
+  const std::string reason = code > 0 && code < 9 ? what[code] : "unknown";
   cudaMemsetAsync(status, 0, sizeof(int), stream);
-  fail("a kernel gave up a bounded wait: " + reason + " (status " + std::to_string(code) + ")");
+  fail(std::string(code >= 7 && code <= 8 ? "a kernel refused its input: " : "a kernel gave up a bounded wait: ") +
+       reason + " (status " + std::to_string(code) + ")");
 }
 
 bool DeviceState::injected(const char* kind) {

@@ -257,7 +257,13 @@ __global__ void __launch_bounds__(32 * kWarps, decode_ctas_per_sm(D, kWarps, kSt
   const int b_first = k0 / 16, b_last = (k1 - 1) / 16;
 
   auto issue = [&](int b, int stage) {
-    const int id = p.table[seg.table_start + b];
+    int id = p.table[seg.table_start + b];
+    // A block ID past the cache (when its size is known) reads zeros and records the bad index.
+    const bool valid = p.cache_blocks <= 0 || (id >= 0 && id < p.cache_blocks);
+    if (!valid) {
+      if (lane == 0) record_status(p.status, kBadIndex);
+      id = 0;
+    }
     const __nv_bfloat16* kp = p.cache + (long)id * page + (long)kvh * 16 * D;
     const __nv_bfloat16* vp = kp + (long)p.kv_heads * 16 * D;
     const uint32_t kt = wbase + stage * 2 * kTile, vt = kt + kTile;
@@ -265,8 +271,8 @@ __global__ void __launch_bounds__(32 * kWarps, decode_ctas_per_sm(D, kWarps, kSt
     for (int i = 0; i < (16 * D / 8) / 32; ++i) {
       const int chunk = lane + i * 32;
       const int r = chunk / (D / 8), c = chunk % (D / 8);
-      cp_async16(kt + swz<D>(r, c), kp + r * D + c * 8, 16);
-      cp_async16(vt + swz<D>(r, c), vp + r * D + c * 8, 16);
+      cp_async16(kt + swz<D>(r, c), kp + r * D + c * 8, valid ? 16 : 0);
+      cp_async16(vt + swz<D>(r, c), vp + r * D + c * 8, valid ? 16 : 0);
     }
     cp_async_commit();
   };
@@ -450,8 +456,13 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention
       const int chunk = threadIdx.x + i * 128;
       const int r = chunk / (D / 8), c = chunk % (D / 8);
       const int blk = kt * 4 + r / 16;
-      const bool ok = blk < seg.nblocks;
-      const int id = ok ? p.table[seg.table_start + blk] : 0;
+      bool ok = blk < seg.nblocks;
+      int id = ok ? p.table[seg.table_start + blk] : 0;
+      if (ok && p.cache_blocks > 0 && (id < 0 || id >= p.cache_blocks)) {
+        record_status(p.status, kBadIndex);  // read as zeros
+        ok = false;
+        id = 0;
+      }
       const __nv_bfloat16* kp = p.cache + (long)id * page + (long)kvh * 16 * D + (r % 16) * D + c * 8;
       const __nv_bfloat16* vp = kp + (long)p.kv_heads * 16 * D;
       cp_async16(ktile + swz<D>(r, c), kp, ok ? 16 : 0);

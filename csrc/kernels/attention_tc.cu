@@ -176,8 +176,12 @@ __global__ void __launch_bounds__(320, 1)
 #pragma unroll
         for (int pg = 0; pg < 8; ++pg) {
           const int b = j * 8 + pg;
-          const bool in = j < ntiles && b * 16 < keys_end && b < seg.nblocks;
+          bool in = j < ntiles && b * 16 < keys_end && b < seg.nblocks;
           const long id = in ? p.table[seg.table_start + b] : 0;
+          if (in && (id < 0 || id >= p.cache_blocks)) {
+            record_status(p.status, kBadIndex);  // the page reads as the box's zero fill
+            in = false;
+          }
           kr[pg] = in ? (int)((id * 2 * p.kv_heads + kvh) * 16) : cache_rows;
           vr[pg] = in ? (int)((id * 2 * p.kv_heads + p.kv_heads + kvh) * 16) : cache_rows;
         }

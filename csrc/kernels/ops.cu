@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
     const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float eps,
     const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, float attn_factor,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
-    const int32_t* __restrict__ slots) {
+    const int32_t* __restrict__ slots, long cache_slots, int* status) {
   pdl_wait();
   pdl_trigger();
   constexpr int E = kHD / 64;  // elements per lane in each half
@@ -259,6 +259,10 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
   }
   const int slot = slots[row];
   if (slot < 0) return;
+  if (cache_slots > 0 && slot >= cache_slots) {  // a slot past the cache: nothing is written
+    if (lane == 0) record_status(status, kBadIndex);
+    return;
+  }
   const int kvh = is_k ? head - q_heads : head - q_heads - kv_heads;
   const long page = 2L * kv_heads * 16 * kHD;
   __nv_bfloat16* dst = cache + (long)(slot / 16) * page + (is_k ? 0 : (long)kv_heads * 16 * kHD) +
@@ -461,7 +465,7 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
                        float eps, const int32_t* positions, RopeTable rope,
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slots,
-                       cudaStream_t stream) {
+                       cudaStream_t stream, long cache_slots, int* status) {
   if (rows <= 0) return 0;
   const long tasks = (long)rows * (q_heads + 2 * kv_heads);
   const int grid = (int)((tasks + 3) / 4);
@@ -469,17 +473,17 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
     case 64:
       launch_pdl(qk_norm_rope_cache_kernel<64>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
-          rope.attention_factor, q_out, cache, slots);
+          rope.attention_factor, q_out, cache, slots, cache_slots, status);
       break;
     case 128:
       launch_pdl(qk_norm_rope_cache_kernel<128>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
-          rope.attention_factor, q_out, cache, slots);
+          rope.attention_factor, q_out, cache, slots, cache_slots, status);
       break;
     case 256:
       launch_pdl(qk_norm_rope_cache_kernel<256>, dim3(grid), dim3(128), 0, stream, 
           qkv, ld_qkv, rows, q_heads, kv_heads, q_norm, k_norm, eps, positions, rope.inv_freq,
-          rope.attention_factor, q_out, cache, slots);
+          rope.attention_factor, q_out, cache, slots, cache_slots, status);
       break;
     default:
       return -2;

@@ -45,12 +45,14 @@ struct RopeTable {
 // cache slot of each row.
 //
 // Cache layout per layer: block b is `page_bytes` bytes holding K[kv_heads][16][head_dim] then
-// V[kv_heads][16][head_dim] in BF16. slot_mapping[r] = block * 16 + offset, or -1 to skip.
+// V[kv_heads][16][head_dim] in BF16. slot_mapping[r] = block * 16 + offset, or -1 to skip. With
+// `cache_slots` > 0 (blocks * 16) a slot at or past it writes nothing and records kBadIndex in
+// `status`.
 int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
                        int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
                        float eps, const int32_t* positions, RopeTable rope,
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slot_mapping,
-                       cudaStream_t stream);
+                       cudaStream_t stream, long cache_slots = 0, int* status = nullptr);
 
 // LoRA: zeroes z[r, 0:cols) (row stride ldz) of every row r whose row_slot[r] is not `slot`.
 int lora_mask(__nv_bfloat16* z, long ldz, int rows, int cols, int slot, const int32_t* row_slot,

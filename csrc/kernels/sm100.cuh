@@ -30,6 +30,7 @@ enum Status : int {
   kTimeoutPeer = 5,         // a peer rank never raised its flag
   kTimeoutDrain = 6,        // copies in flight did not land while aborting
   kBadArgument = 7,         // a launch argument failed a device-side check
+  kBadIndex = 8,            // an index read from device memory (block ID, cache slot) was out of range
 };
 
 __device__ __forceinline__ uint64_t global_ns() {

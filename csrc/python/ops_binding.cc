@@ -303,7 +303,7 @@ void bind_ops(py::module_& m) {
         [](uint64_t qkv, long ld_qkv, int rows, int q_heads, int kv_heads, int head_dim,
            uint64_t q_norm, uint64_t k_norm, float eps, uint64_t positions, uint64_t inv_freq,
            float attention_factor, uint64_t q_out, uint64_t cache, uint64_t slots,
-           uint64_t stream) {
+           uint64_t stream, long cache_slots, uint64_t status) {
           py::gil_scoped_release nogil;
           foa::RopeTable rope{as_ptr<const float>(inv_freq), attention_factor};
           check(foa::qk_norm_rope_cache(
@@ -311,9 +311,13 @@ void bind_ops(py::module_& m) {
                     as_ptr<const __nv_bfloat16>(q_norm), as_ptr<const __nv_bfloat16>(k_norm), eps,
                     as_ptr<const int32_t>(positions), rope, as_ptr<__nv_bfloat16>(q_out),
                     as_ptr<__nv_bfloat16>(cache), as_ptr<const int32_t>(slots),
-                    as_stream(stream)),
+                    as_stream(stream), cache_slots, as_ptr<int>(status)),
                 "qk_norm_rope_cache");
-        });
+        },
+        py::arg("qkv"), py::arg("ld_qkv"), py::arg("rows"), py::arg("q_heads"), py::arg("kv_heads"),
+        py::arg("head_dim"), py::arg("q_norm"), py::arg("k_norm"), py::arg("eps"), py::arg("positions"),
+        py::arg("inv_freq"), py::arg("attention_factor"), py::arg("q_out"), py::arg("cache"),
+        py::arg("slots"), py::arg("stream"), py::arg("cache_slots") = 0, py::arg("status") = 0);
   auto make_attn = [](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
                       int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
                       uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
@@ -342,10 +346,11 @@ void bind_ops(py::module_& m) {
                     int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
                     uint64_t partial_o, uint64_t partial_lse, size_t capacity, int max_keys,
                     int keys_per_split, uint64_t status, uint64_t stream, uint64_t counters, int warps,
-                    int stages) {
+                    int stages, long cache_blocks) {
           auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
                              head_dim, scale, partial_o, partial_lse, capacity, max_keys,
                              keys_per_split, status);
+          a.cache_blocks = cache_blocks;
           a.decode_warps = warps;
           a.decode_stages = stages;
           (void)counters;
@@ -356,7 +361,7 @@ void bind_ops(py::module_& m) {
         py::arg("num_segments"), py::arg("q_heads"), py::arg("kv_heads"), py::arg("head_dim"),
         py::arg("scale"), py::arg("partial_o"), py::arg("partial_lse"), py::arg("capacity"),
         py::arg("max_keys"), py::arg("keys_per_split"), py::arg("status"), py::arg("stream"),
-        py::arg("counters") = 0, py::arg("warps") = 0, py::arg("stages") = 0);
+        py::arg("counters") = 0, py::arg("warps") = 0, py::arg("stages") = 0, py::arg("cache_blocks") = 0);
   m.def("wait_probe",
         [](uint64_t flag, unsigned long long value, uint64_t limit_ns, uint64_t status, uint64_t stream) {
           check(foa::wait_probe(as_ptr<const unsigned long long>(flag), value, limit_ns, as_ptr<int>(status),

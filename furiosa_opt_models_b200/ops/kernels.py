@@ -275,7 +275,8 @@ def qk_norm_rope_cache(qkv, q_heads, kv_heads, head_dim, q_norm, k_norm, eps, po
     native().ops.qk_norm_rope_cache(
         qkv.data_ptr(), qkv.stride(0), rows, q_heads, kv_heads, head_dim, _ptr(q_norm),
         _ptr(k_norm), float(eps), positions.data_ptr(), inv_freq.data_ptr(),
-        float(attention_factor), q.data_ptr(), cache.data_ptr(), slots.data_ptr(), _stream())
+        float(attention_factor), q.data_ptr(), cache.data_ptr(), slots.data_ptr(), _stream(),
+        cache_slots=cache.shape[0] * 16, status=scratch(qkv.device).status.data_ptr())
     return q
 
 
@@ -303,7 +304,7 @@ def paged_decode(q, cache, table, segments, kv_heads, max_keys, scale=None, keys
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(), n,
         q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5), po.data_ptr(),
         pl.data_ptr(), need, int(max_keys), keys_per_split, s.status.data_ptr(), _stream(),
-        0 if counters is None else counters.data_ptr(), warps, stages)
+        0 if counters is None else counters.data_ptr(), warps, stages, cache.shape[0])
     return out
 
 

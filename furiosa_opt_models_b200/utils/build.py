@@ -42,18 +42,17 @@ def _sources() -> tuple[list[Path], list[Path]]:
     return cu, cc
 
 
-def _ninja_file(cu: list[Path], cc: list[Path], debug: bool) -> str:
+def _ninja_file(cu: list[Path], cc: list[Path]) -> str:
     nvcc = CUDA_HOME / "bin" / "nvcc"
     inc = f"-I{CSRC} -I{CSRC / 'kernels'} -I{CSRC / 'engine'} -I{CUDA_HOME / 'include'}"
     pyinc = f"-I{sysconfig.get_paths()['include']} -I{_pybind_include()}"
-    checked = " -DFOA_CHECKED=1" if debug else ""
     lines = [
         "ninja_required_version = 1.5",
         f"nvcc = {nvcc}",
         f"cuflags = {ARCH} -O3 -lineinfo -std=c++17 -Xcompiler -fPIC,-fvisibility=hidden "
-        f"--expt-relaxed-constexpr -Xptxas -v {inc}{checked}",
+        f"--expt-relaxed-constexpr -Xptxas -v {inc}",
         f"ccflags = -O2 -g -std=c++17 -fPIC -fvisibility=hidden -Wall -Wno-unused-function "
-        f"{inc} {pyinc}{checked}",
+        f"{inc} {pyinc}",
         f"ldflags = -shared -L{CUDA_HOME / 'lib64'} -lcudart_static -lrt -ldl -lpthread",
         "rule cu",
         "  command = $nvcc $cuflags -c $in -o $out > $out.ptxas.log 2>&1 || "
@@ -83,13 +82,13 @@ def _ninja_file(cu: list[Path], cc: list[Path], debug: bool) -> str:
     return "\n".join(lines) + "\n"
 
 
-def build(verbose: bool = False, jobs: int | None = None, debug: bool = False) -> Path:
+def build(verbose: bool = False, jobs: int | None = None) -> Path:
     """Compiles and links the extension; returns its path. Raises on a failed build."""
     cu, cc = _sources()
     BUILD.mkdir(exist_ok=True)
     (BUILD / "obj").mkdir(exist_ok=True)
     ninja_file = BUILD / "build.ninja"
-    text = _ninja_file(cu, cc, debug)
+    text = _ninja_file(cu, cc)
     if not ninja_file.exists() or ninja_file.read_text() != text:
         ninja_file.write_text(text)
     ninja = shutil.which("ninja") or str(Path(sys.executable).parent / "ninja")
@@ -109,9 +108,8 @@ def main() -> None:
     parser = argparse.ArgumentParser(description=__doc__)
     parser.add_argument("--verbose", action="store_true")
     parser.add_argument("--jobs", type=int, default=None)
-    parser.add_argument("--checked", action="store_true", help="bounds-checked kernels")
     args = parser.parse_args()
-    print(build(args.verbose, args.jobs, args.checked))
+    print(build(args.verbose, args.jobs))
 
 
 if __name__ == "__main__":

@@ -93,3 +93,32 @@ def test_paged_decode_history_beyond_max_keys():
         s.status.zero_()
         assert torch.count_nonzero(out[2]).item() == 0
         assert (out[:2].float().cpu() - ref[:2]).abs().max().item() < 2e-2
+
+
+def test_block_ids_past_the_cache_are_refused_on_the_device():
+    """A block ID past the cache reads as zeros and records the bad-index status (8) instead of
+    reading outside the cache; the prefill kernels treat it the same way."""
+    from furiosa_opt_models_b200 import ops
+
+    cached = [40, 100]
+    q, cache, table, segs = _setup([1, 1], cached, 16, 8, 128, blocks=64)
+    bad = table.clone()
+    bad[int(segs[1, 3]) + 2] = 64 + 1000  # past the 64 blocks
+    s = ops.scratch(torch.device("cuda", 0))
+    s.status.zero_()
+    out = ops.paged_decode(q.cuda(), cache.cuda(), bad.cuda(), segs.cuda(), 8, max_keys=101)
+    torch.cuda.synchronize()
+    assert int(s.status[0].item()) == 8
+    assert torch.isfinite(out.float()).all()
+    s.status.zero_()
+    lengths, cached = [20, 33], [0, 16]
+    q, cache, table, segs = _setup(lengths, cached, 16, 8, 128, blocks=64)
+    bad = table.clone()
+    bad[-1] = -5
+    work = ops.prefill_work(segs, 2)
+    for tc in (True, False):
+        out = ops.paged_prefill(q.cuda(), cache.cuda(), bad.cuda(), segs.cuda(), 8, work.cuda(), tensor_cores=tc)
+        torch.cuda.synchronize()
+        assert int(s.status[0].item()) == 8, tc
+        assert torch.isfinite(out.float()).all()
+        s.status.zero_()

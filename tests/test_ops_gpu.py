@@ -80,3 +80,25 @@ def test_qk_norm_rope_cache(head_dim):
         b, o = divmod(s, 16)
         assert (c[b, 0, :, o] - rk[r]).abs().max().item() < 5e-2
         assert (c[b, 1, :, o] - rv[r]).abs().max().item() < 2e-2
+
+
+def test_cache_slots_past_the_cache_write_nothing():
+    """A KV write slot at or past blocks * 16 writes nothing and records the bad-index status (8)."""
+    ops = _ops()
+    from furiosa_opt_models_b200.ops import scratch
+
+    rows, qh, kvh, d = 3, 4, 2, 128
+    qkv = torch.randn(rows, (qh + 2 * kvh) * d, device="cuda", dtype=torch.bfloat16)
+    pos = torch.arange(rows, device="cuda", dtype=torch.int32)
+    inv_freq = 1.0 / (1e6 ** (torch.arange(0, d, 2, device="cuda").float() / d))
+    cache = torch.zeros(2, 2, kvh, 16, d, device="cuda", dtype=torch.bfloat16)
+    guard = torch.zeros(1 << 16, device="cuda", dtype=torch.bfloat16)  # memory right after, often
+    slots = torch.tensor([1, 32, 5000], device="cuda", dtype=torch.int32)
+    s = scratch(torch.device("cuda", 0))
+    s.status.zero_()
+    ops.qk_norm_rope_cache(qkv, qh, kvh, d, None, None, 1e-6, pos, inv_freq, 1.0, cache, slots)
+    torch.cuda.synchronize()
+    assert int(s.status[0].item()) == 8
+    s.status.zero_()
+    assert torch.count_nonzero(cache[0, :, :, 1]).item() > 0  # the valid slot was written
+    assert torch.count_nonzero(guard).item() == 0
