@@ -44,8 +44,8 @@ py::object make_range(int64_t a, int64_t b) {
 int process_rank(size_t chips) {
   // A placement of N chips runs as N processes, one per GPU: this process serves chips[rank].
   if (chips <= 1) return 0;
-  py::object dist = py::module_::import("furiosa_opt_models_b200.parallel.dist");
-  return dist.attr("rank_for_chips")(chips).cast<int>();
+  py::object tp = py::module_::import("furiosa_opt_models_b200.parallel.tp");
+  return tp.attr("rank_for_chips")(chips).cast<int>();
 }
 
 // ------------------------------------------------------------------------------------ Placement

@@ -19,6 +19,24 @@ def set_group(group) -> None:
     _group = group
 
 
+def rank_for_chips(chips: int) -> int:
+    """This process's rank among the `chips` processes of a placement (one process per GPU, process
+    `rank` serving `chips[rank]`), from the process group when it is up, else from RANK and
+    WORLD_SIZE; raises when the group's size is not the placement's. `engine.Device` calls it."""
+    import os
+
+    import torch.distributed as dist
+
+    if dist.is_available() and dist.is_initialized():
+        world, rank = dist.get_world_size(_group), dist.get_rank(_group)
+    else:
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+    if world != chips:
+        raise RuntimeError(f"a placement of {chips} chips runs as {chips} processes, one per GPU; this group has {world}")
+    return rank
+
+
 def exchange_handles(handle: bytes) -> list:
     """Every rank's heap handle, in rank order. A rank that has died or never joins ends the
     exchange with the process group's error (its timeout bounds the wait), before any kernel of

@@ -15,18 +15,7 @@ class B200Platform(NvmlCudaPlatform):
     def check_and_update_config(cls, vllm_config) -> None:
         pc = vllm_config.parallel_config
         cc = vllm_config.cache_config
-        admission.options(
-            pipeline=pc.pipeline_parallel_size,
-            tensor=pc.tensor_parallel_size,
-            speculative=(None if vllm_config.speculative_config is None
-                         else str(vllm_config.speculative_config.method)),
-            lora=vllm_config.lora_config is not None,
-            max_loras=getattr(vllm_config.lora_config, "max_loras", 1) or 1,
-            max_lora_rank=getattr(vllm_config.lora_config, "max_lora_rank", 16) or 16,
-            kv_cache_dtype=str(cc.cache_dtype),
-            prefill_context=getattr(pc, "prefill_context_parallel_size", 1),
-            decode_context=getattr(pc, "decode_context_parallel_size", 1),
-        )
+        admission.check(vllm_config)
         from .additional import Section
 
         Section.parse(vllm_config)

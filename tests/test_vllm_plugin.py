@@ -262,3 +262,56 @@ def test_parameters_that_change_the_greedy_token_are_refused():
         with pytest.raises(admission.Refused) as e:
             admission.unmodified(SimpleNamespace(**{name: value}))
         assert e.value.option == name
+
+
+def test_every_contract_names_an_option_of_this_vllm():
+    """Each contract's path exists in vLLM's configuration classes (a renamed option would silently
+    skip its check otherwise). The classes are read from vLLM's sources: importing vllm.config
+    resolves vLLM's platform, which needs a GPU driver."""
+    import ast
+    import importlib.util
+    from pathlib import Path
+
+    spec = importlib.util.find_spec("vllm")
+    if spec is None:
+        pytest.skip("vLLM is not installed")
+    fields: dict[str, set[str]] = {}
+    for src in (Path(spec.origin).parent / "config").glob("*.py"):
+        for node in ast.walk(ast.parse(src.read_text())):
+            if isinstance(node, ast.ClassDef):
+                names = {n.target.id for n in node.body if isinstance(n, ast.AnnAssign) and isinstance(n.target, ast.Name)}
+                fields.setdefault(node.name, set()).update(names)
+    classes = {"parallel_config": "ParallelConfig", "cache_config": "CacheConfig", "model_config": "ModelConfig",
+               "load_config": "LoadConfig", "lora_config": "LoRAConfig", "scheduler_config": "SchedulerConfig",
+               "offload_config": "OffloadConfig"}
+    for c in admission.CONTRACTS:
+        head, _, rest = c.path.partition(".")
+        assert head in fields["VllmConfig"], c.path
+        if rest:
+            assert rest.split(".")[0] in fields[classes[head]], c.path
+
+
+@pytest.mark.parametrize(("path", "bad", "option"), [
+    ("parallel_config.nnodes", 2, "nnodes"),
+    ("cache_config.cache_dtype", "fp8", "kv_cache_dtype"),
+    ("model_config.dtype", "float16", "dtype"),
+    ("model_config.quantization", "awq", "quantization"),
+    ("load_config.load_format", "gguf", "load_format"),
+    ("lora_config.fully_sharded_loras", True, "fully_sharded_loras"),
+])
+def test_contract_table_refuses_each_option(path, bad, option):
+    from types import SimpleNamespace as ns
+
+    def config():
+        return ns(parallel_config=ns(pipeline_parallel_size=1, tensor_parallel_size=1, nnodes=1),
+                  cache_config=ns(cache_dtype="auto"), model_config=ns(dtype="bfloat16", quantization=None),
+                  load_config=ns(load_format="auto"), lora_config=ns(max_loras=1, max_lora_rank=8, fully_sharded_loras=False),
+                  speculative_config=None, ec_transfer_config=None)
+
+    admission.check(config())
+    cfg = config()
+    head, attr = path.split(".")
+    setattr(getattr(cfg, head), attr, bad)
+    with pytest.raises(admission.Refused) as e:
+        admission.check(cfg)
+    assert e.value.option == option
