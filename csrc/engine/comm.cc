@@ -195,6 +195,7 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   a.world = world_;
   a.site = site_++;
   a.two_shot = two_shot(rows) ? 1 : 0;
+  a.gather_residual = moe_rows_ > 0 ? 1 : 0;  // the expert combine reads every row's residual
   a.status = status_;
   a.trace = trace_;
   if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");

@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
         ss += h[i][2 * t] * h[i][2 * t] + h[i][2 * t + 1] * h[i][2 * t + 1];
       }
       const uint4 out = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      if (a.two_shot) {
+      if (a.two_shot && a.gather_residual) {
         for (int p = 0; p < a.world; ++p)
           *reinterpret_cast<uint4*>(a.peers.residual[p] + (long)row * a.cols + v * 8) = out;
       } else {

@@ -40,6 +40,10 @@ struct AddNormArgs {
   // 1: rank r received rows [r * s, (r + 1) * s) at slot rows 0..s-1, s = ceil(rows / world)
   //    (reduce-scatter); it reduces them and stores the results into every rank (all-gather).
   int two_shot;
+  // Reduce-scatter only: 1 stores the owner's residual rows into every rank too (callers that read
+  // every row's residual, such as the mixture-of-experts combine); 0 keeps each residual row on
+  // its owner alone, which is the only rank that adds to it again within the call.
+  int gather_residual;
   int* status;
   // Optional: CTA 0 writes %globaltimer here at entry (after the grid dependency wait), once its
   // row's partials have all landed, and at exit.
@@ -47,7 +51,8 @@ struct AddNormArgs {
 };
 
 // residual = bf16(sum over ranks in rank order of partial + residual); hidden = RMSNorm(residual)
-// * weight; every rank ends with the same residual and hidden rows.
+// * weight; every rank ends with the same hidden rows, and with the same residual rows where it
+// holds them (all of them one-shot; its own slice, or all with gather_residual, two-shot).
 int tp_add_norm(const AddNormArgs& args, cudaStream_t stream);
 
 // Writes the not-yet-written mark (-0.0) over `floats` floats of a receive region.
