@@ -11,7 +11,10 @@ sides, measured with CUDA events on the engine's stream; the reported time is th
 The e2e arm runs the same waves through the public API with every step's inputs copied from pinned
 host memory and every step's output tokens read back to the host.
 
-    python bench.py --gpus N --steps K --warmup W [--impl ours|reference]
+    python bench.py --gpus N --steps K --warmup W [--impl ours|reference|baseline|vllm]
+
+`--impl baseline` runs the waves on eager PyTorch (cuBLAS, SDPA, NCCL); `--impl vllm` on stock
+vLLM, the library serving stack of this image.
 """
 
 from __future__ import annotations
@@ -36,7 +39,7 @@ def parse() -> argparse.Namespace:
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=2)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline"])
+    p.add_argument("--impl", default="ours", choices=["ours", "reference", "baseline", "vllm"])
     p.add_argument("--model", default="qwen3-1.7b")
     p.add_argument("--concurrency", type=int, default=64)
     p.add_argument("--input-len", type=int, default=1024)
@@ -173,10 +176,101 @@ def baseline_arm(args, torch, dist, world, rank, local) -> None:
         }), flush=True)
 
 
+def vllm_arm(args, world: int, rank: int, local: int) -> None:
+    """The same waves through stock vLLM (its own B200 kernels, CUDA graphs, NCCL and custom
+    all-reduce), none of this repository's kernels or engine on the path: the library serving
+    stack the engine is compared with. Weights are vLLM's dummy initialisation of the named
+    geometry (no checkpoint); at N > 1 every torchrun rank is one vLLM tensor-parallel rank
+    (external launcher). Timed on the wall clock around `LLM.generate`, which returns after the
+    device finished, max over ranks."""
+    import tempfile
+
+    import torch
+    import torch.distributed as dist
+
+    from furiosa_opt_models_b200.models import configs, synthetic
+
+    cfg = configs.get(args.model)
+    if cfg.get("weight_format", "bf16") != "bf16":
+        if rank == 0:
+            print(json.dumps({"impl": "vllm", "unavailable": "the vLLM arm serves the BF16 geometries"}))
+        return
+    from vllm import LLM, SamplingParams
+    from vllm.inputs import TokensPrompt
+
+    d = tempfile.mkdtemp(prefix="foa-vllm-")
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(synthetic.hf_config(cfg), f)
+    total = args.input_len + args.output_len
+    llm = LLM(model=d, load_format="dummy", skip_tokenizer_init=True, tensor_parallel_size=world,
+              distributed_executor_backend="external_launcher" if world > 1 else None,
+              max_model_len=total, max_num_seqs=args.concurrency, max_num_batched_tokens=8192,
+              gpu_memory_utilization=0.8, enable_prefix_caching=False, seed=0, disable_log_stats=False)
+    gen = torch.Generator().manual_seed(1234)
+    prompts = [TokensPrompt(prompt_token_ids=torch.randint(0, cfg["vocab"], (args.input_len,), generator=gen).tolist())
+               for _ in range(args.concurrency)]
+    sp = SamplingParams(temperature=0.0, max_tokens=args.output_len, ignore_eos=True, detokenize=False)
+    for _ in range(args.warmup):
+        llm.generate(prompts, sp, use_tqdm=False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    ttfts, tpots = [], []
+    with sampler:
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            outs = llm.generate(prompts, sp, use_tqdm=False)
+            for o in outs:
+                m = o.metrics
+                if m is None:
+                    continue
+                ttfts.append(m.first_token_latency * 1e3)
+                n = len(o.outputs[0].token_ids)
+                if n > 1:
+                    tpots.append((m.last_token_ts - m.first_token_ts) * 1e3 / (n - 1))
+        torch.cuda.synchronize()
+        elapsed = time.perf_counter() - t0
+    stats = torch.tensor([elapsed, statistics.median(ttfts) if ttfts else -1.0,
+                          statistics.median(tpots) if tpots else -1.0], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+    elapsed, ttft, tpot = stats.tolist()
+    if rank == 0:
+        value = args.steps * args.concurrency * args.output_len / elapsed
+        print(json.dumps({
+            "impl": "vllm", "metric": METRIC, "value": round(value, 1), "unit": "output tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(elapsed * 1e3 / args.steps, 3), "higher_is_better": True, "scaling": "strong",
+            "dtype": "bf16", "data": "synthetic: uniform-random prompt token IDs; vLLM dummy weights",
+            "p50_ttft_ms": round(ttft, 3), "p50_tpot_ms": round(tpot, 4),
+            "config": {"model": f"{args.model} (shape of the named checkpoint)", "global_batch": args.concurrency,
+                       "seq_len": total, "parallelism": f"tp{world}",
+                       "stack": "stock vLLM (LLM.generate, its attention backend, CUDA graphs, its all-reduce)",
+                       "timing": "wall clock around LLM.generate, max over ranks"},
+            "clocks": sampler.summary(),
+        }), flush=True)
+
+
 def main() -> None:
     args = parse()
     if args.impl == "reference":
         reference_arm(args)
+        return
+    if args.impl == "vllm":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        if world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                    device_id=torch.device("cuda", local))
+        vllm_arm(args, world, rank, local)
         return
 
     import torch

@@ -47,6 +47,8 @@ class PeerCollectives : public Collectives {
   // after one that keeps a rank from writing into a peer still in its call.
   void gather_rows(const __nv_bfloat16* src, int rows, int cols, bool exchange, __nv_bfloat16* dst,
                    cudaStream_t stream);
+  // Reduce-scatter (two-shot) rather than one-shot for a call of `rows` rows.
+  bool two_shot(int rows) const;
   // Measurement: the add_norm kernels write milestone timestamps here (null: none).
   void set_trace(unsigned long long* trace) { trace_ = trace; }
   // Fault drill (DeviceState::injected "peer"): the next collective reports a silent peer.
@@ -59,13 +61,10 @@ class PeerCollectives : public Collectives {
   int cols_;
   void* heap_ = nullptr;
   size_t heap_bytes_ = 0;
-  // Reduce-scatter (two-shot) rather than one-shot for a call of `rows` rows.
-  bool two_shot(int rows) const;
 
-  size_t off_signal_, off_arrivals_, off_seq_, off_epoch_, off_recv_, off_residual_, off_hidden_,
+  size_t off_signal_, off_arrivals_, off_seq_, off_epoch_, off_partial_, off_residual_, off_hidden_,
       off_gvalue_, off_gindex_, off_moe_;
-  int64_t slot_rows_ = 0;          // rows of one source slot of the receive region
-  size_t one_shot_limit_ = 0;      // bytes a one-shot call may push to its peers
+  size_t one_shot_limit_ = 0;      // partial bytes a one-shot call may read from its peers
   std::vector<void*> peer_base_;   // every rank's heap as mapped here (own heap at rank_)
   std::vector<bool> opened_;
   foa::PeerBuffers peers_{};

@@ -2,19 +2,17 @@
 //
 // The reference's all-reduce is a deterministic FP32 recursive doubling over chip DMA, narrowed
 // to BF16 once at the end (crates/furiosa-opt-models/src/ops/collective/mod.rs:22-141); its
-// all-gather joins parts in chip order (gather.rs:17-99). Here the row-parallel GEMM's epilogue
-// stores its FP32 partial tiles straight into the reducing ranks' receive buffers over NVLink as
-// the tiles finish (GemmPeerOut), and the reducer adds the landed partials in rank order, so every
-// rank computes the same bits; the sum is fused with the residual add (one rounding) and the
-// RMSNorm that follows. Small calls push every row to every rank (one-shot: one NVLink hop, no
-// barrier); large calls push each row to the rank that owns its slice (reduce-scatter), and the
-// owner stores the normed rows into every rank (all-gather) before a closing barrier.
+// all-gather joins parts in chip order (gather.rs:17-99). Here the row-parallel GEMM writes its
+// FP32 partial into this rank's own symmetric buffer; the reducer meets every rank at a barrier,
+// then pulls the rows it reduces from every rank's buffer over NVLink (loads, many in flight) and
+// adds them in rank order, so every rank computes the same bits; the sum is fused with the
+// residual add (one rounding) and the RMSNorm that follows. Small calls reduce every row on every
+// rank (one-shot); large calls reduce each row on the rank that owns its slice (reduce-scatter),
+// which stores the normed rows into every rank (all-gather) before a closing barrier.
 //
-// Arrival is detected without flags: a receive slot holds -0.0 until its value lands (a GEMM
-// never sends -0.0), and the reducer writes -0.0 back after reading. Ranks meet at device-side
-// barriers elsewhere: a rank stores a monotonically increasing value into its slot of every
-// peer's signal array (release, system scope) and waits, bounded, until every slot of its own
-// array has reached the value. A wait that gives up records kTimeoutPeer and returns.
+// Ranks meet at device-side barriers: a rank stores a monotonically increasing value into its slot
+// of every peer's signal array (release, system scope) and waits, bounded, until every slot of its
+// own array has reached the value. A wait that gives up records kTimeoutPeer and returns.
 
 #include <algorithm>
 
@@ -86,73 +84,59 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   return t;
 }
 
-constexpr uint32_t kUnwritten = 0x80000000u;  // -0.0: a receive slot whose value has not landed
-
-__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
-__device__ __forceinline__ bool unwritten(const float4& v) {
-  return (__float_as_uint(v.x) == kUnwritten) | (__float_as_uint(v.y) == kUnwritten) |
-         (__float_as_uint(v.z) == kUnwritten) | (__float_as_uint(v.w) == kUnwritten);
-}
-
-// One CTA of 256 threads per row; each thread holds kVec vectors of 8 columns. The partials were
-// pushed here by the GEMMs of every rank; each thread polls its 8 values of every source slot,
-// adds them in rank order and marks the slot unwritten again.
-// It follows the GEMM that pushes the partials. That GEMM lets this kernel launch only after the
-// kernels before it completed (so the previous reducer's sequence advance and every earlier read of
-// the residual and normed rows are done); the partials themselves are polled for, so this kernel
-// does not wait for the GEMM to finish.
+// One CTA of 256 threads per row this rank reduces; each thread holds kVec vectors of 8 columns.
+// Launched after the GEMM that wrote this rank's FP32 partial locally. Phase 0 is a barrier: every
+// rank announces its partial is complete and waits until all have (so every partial may be read,
+// and every peer has finished reading the previous use of this buffer parity and consuming the
+// normed rows). Phase 1 pulls the row's partials from every rank over NVLink, many 16-byte loads
+// in flight a thread, adds them in rank order in FP32, adds the residual (one rounding) and
+// normalises. Reduce-scatter calls store the normed rows into every rank and end with a second
+// barrier, so the kernel completes only once every row is in place on this rank.
 template <int kVec>
-__global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
+__global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const ReduceNormArgs a) {
+  pdl_wait();  // this rank's partial (the previous kernel) is complete
   pdl_trigger();
   __shared__ float red[8];
-  const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
-  const int slot_row = blockIdx.x;
-  const int row = a.two_shot ? a.rank * rs + slot_row : slot_row;
-  float* recv = a.recv + (long)(__ldcg(a.seq) & 1u) * a.buf_stride + (long)slot_row * a.cols;
-  const int nvec = a.cols / 8;
+  __shared__ int ok_s;
   const bool tracer = a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
   if (tracer) a.trace[0] = global_ns();
-  if (row < a.rows) {
-    const uint64_t start = global_ns();
-    bool late = false;
+  if (threadIdx.x == 0) {
+    const unsigned long long v = barrier_value(a.epoch, a.site, 0);
+    if (blockIdx.x == 0) signal_all(a.peers, a.rank, a.world, v);
+    ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
+  }
+  __syncthreads();
+  if (tracer) a.trace[1] = global_ns();
+  const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
+  const int row = a.two_shot ? a.rank * rs + (int)blockIdx.x : (int)blockIdx.x;
+  const long par = (long)(__ldcg(a.seq) & 1u) * a.buf_stride + (long)row * a.cols;
+  const int nvec = a.cols / 8;
+  if (ok_s && row < a.rows) {
     float h[kVec][8];
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
       const int v = threadIdx.x + i * 256;
       if (v >= nvec) continue;
-      float acc[8];
+      // Every rank's 8 values first (independent loads in flight), then the sum in rank order.
+      float4 x[kMaxRanks][2];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) acc[t] = 0.f;
-      for (int p = 0; p < a.world; ++p) {
-        float* src = recv + (long)p * a.slot_stride + v * 8;
-        float4 x0, x1;
-        uint32_t spins = 0;
-        for (;;) {
-          x0 = ld_volatile_f4(src);
-          x1 = ld_volatile_f4(src + 4);
-          if (!(unwritten(x0) || unwritten(x1)) || late) break;
-          __nanosleep(100);  // polled while the pushing GEMM runs: leave it the issue slots
-          if ((++spins & 63u) == 0 && global_ns() - start > kWaitLimitNs) {
-            record_status(a.status, kTimeoutPeer);
-            late = true;
-          }
+      for (int p = 0; p < kMaxRanks; ++p) {
+        if (p < a.world) {
+          const float4* src = reinterpret_cast<const float4*>(a.peers.partial[p] + par + v * 8);
+          x[p][0] = __ldcg(src);
+          x[p][1] = __ldcg(src + 1);
         }
-        acc[0] += x0.x; acc[1] += x0.y; acc[2] += x0.z; acc[3] += x0.w;
-        acc[4] += x1.x; acc[5] += x1.y; acc[6] += x1.z; acc[7] += x1.w;
-        const float m = __uint_as_float(kUnwritten);
-        reinterpret_cast<float4*>(src)[0] = make_float4(m, m, m, m);
-        reinterpret_cast<float4*>(src)[1] = make_float4(m, m, m, m);
       }
-      const __nv_bfloat16* rp = a.peers.residual[a.rank] + (long)row * a.cols + v * 8;
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int p = 0; p < kMaxRanks; ++p) {
+        if (p < a.world) {
+          acc[0] += x[p][0].x; acc[1] += x[p][0].y; acc[2] += x[p][0].z; acc[3] += x[p][0].w;
+          acc[4] += x[p][1].x; acc[5] += x[p][1].y; acc[6] += x[p][1].z; acc[7] += x[p][1].w;
+        }
+      }
+      __nv_bfloat16* rp = a.peers.residual[a.rank] + (long)row * a.cols + v * 8;
       const uint4 rv = *reinterpret_cast<const uint4*>(rp);
       const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
       uint32_t packed[4];
@@ -168,11 +152,10 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
         for (int p = 0; p < a.world; ++p)
           *reinterpret_cast<uint4*>(a.peers.residual[p] + (long)row * a.cols + v * 8) = out;
       } else {
-        *reinterpret_cast<uint4*>(a.peers.residual[a.rank] + (long)row * a.cols + v * 8) = out;
+        *reinterpret_cast<uint4*>(rp) = out;
       }
     }
     const float total = block_sum(ss, red);
-    if (tracer) a.trace[1] = global_ns();
     const float inv = rsqrtf(total / (float)a.cols + a.eps);
 #pragma unroll
     for (int i = 0; i < kVec; ++i) {
@@ -193,9 +176,8 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
       }
     }
   }
-  // The last CTA to finish advances the receive sequence (every CTA has read it) and, two-shot,
-  // tells every peer its slice has landed and waits until every peer's slice has landed here, so
-  // the kernel ends only with every row in place.
+  // The last CTA to finish advances the partial-buffer sequence (every CTA has read it) and,
+  // reduce-scatter, meets every peer once every CTA's stores into the peers are visible.
   __syncthreads();
   if (threadIdx.x == 0) {
     if (a.two_shot)
@@ -206,7 +188,7 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
     if (done == gridDim.x - 1) {
       *a.arrivals = 0;
       *a.seq += 1u;
-      if (a.two_shot) {
+      if (a.two_shot && ok_s) {
         const unsigned long long v = barrier_value(a.epoch, a.site, 1);
         signal_all(a.peers, a.rank, a.world, v);
         wait_all(a.peers, a.rank, a.world, v, a.status);
@@ -214,11 +196,6 @@ __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
     }
     if (tracer) a.trace[2] = global_ns();
   }
-}
-
-__global__ void fill_u32_kernel(uint32_t* p, size_t n, uint32_t v) {
-  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-    p[i] = v;
 }
 
 template <int kVec>
@@ -383,26 +360,20 @@ int tp_set_epoch(unsigned long long* epoch, unsigned long long value, cudaStream
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
-int tp_add_norm(const AddNormArgs& a, cudaStream_t stream) {
+int tp_reduce_norm(const ReduceNormArgs& a, cudaStream_t stream) {
   if (a.rows <= 0) return 0;
   if (a.world < 1 || a.world > kMaxRanks || a.cols % 8 != 0) return -2;
   const int vec = (a.cols / 8 + 255) / 256;
   const int grid = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
   cudaError_t e;
   switch (vec) {
-    case 1: e = launch_pdl(tp_add_norm_kernel<1>, dim3(grid), dim3(256), 0, stream, a); break;
-    case 2: e = launch_pdl(tp_add_norm_kernel<2>, dim3(grid), dim3(256), 0, stream, a); break;
+    case 1: e = launch_pdl(tp_reduce_norm_kernel<1>, dim3(grid), dim3(256), 0, stream, a); break;
+    case 2: e = launch_pdl(tp_reduce_norm_kernel<2>, dim3(grid), dim3(256), 0, stream, a); break;
     case 3:
-    case 4: e = launch_pdl(tp_add_norm_kernel<4>, dim3(grid), dim3(256), 0, stream, a); break;
+    case 4: e = launch_pdl(tp_reduce_norm_kernel<4>, dim3(grid), dim3(256), 0, stream, a); break;
     default: return -2;
   }
   return e == cudaSuccess ? 0 : -5;
-}
-
-int tp_clear_recv(float* recv, size_t floats, cudaStream_t stream) {
-  if (floats == 0) return 0;
-  fill_u32_kernel<<<296, 256, 0, stream>>>(reinterpret_cast<uint32_t*>(recv), floats, kUnwritten);
-  return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
 int tp_argmax(const ArgmaxArgs& a, cudaStream_t stream) {

@@ -794,8 +794,8 @@ void bind_engine(py::module_& m) {
     r["fused"] = timed(fused);
     r["local"] = timed([&]() { gemm(nullptr); });
     {
-      // The fused pair again with an event between the two kernels: the GEMM's share (with its
-      // peer stores) and the reducer's share (waits for peers included).
+      // The fused pair again with an event between the two kernels: the GEMM's share and the
+      // reducer's share (waits for peers included).
       std::vector<cudaEvent_t> ev(3 * iters);
       for (auto& e : ev) cudaEventCreate(&e);
       coll->begin_call(s);
@@ -824,7 +824,8 @@ void bind_engine(py::module_& m) {
     }
     {
       // Milestones of one launch (global timer, relative to the GEMM's entry, microseconds): the
-      // local GEMM, then the fused pair (GEMM marks 0-7, then the reducer's entry, landed, exit).
+      // local GEMM, then the fused pair (GEMM marks 0-7, then the reducer's entry, barrier passed,
+      // exit).
       auto* pc = dynamic_cast<PeerCollectives*>(coll.get());
       HbmBuffer tr(d.model->device(), 16 * 8);
       std::vector<unsigned long long> h(16);
@@ -848,7 +849,10 @@ void bind_engine(py::module_& m) {
       if (pc) pc->set_trace(nullptr);
       read("trace_fused_", 11);
     }
-    r["two_shot"] = coll->reduce_target(rows, H).owner_rows > 0 ? 1.0 : 0.0;
+    {
+      auto* pc = dynamic_cast<PeerCollectives*>(coll.get());
+      r["two_shot"] = pc != nullptr && pc->two_shot(rows) ? 1.0 : 0.0;
+    }
     return r;
   });
   m.def("_device_trim", [](const Device& d) {

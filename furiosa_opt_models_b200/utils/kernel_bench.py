@@ -176,8 +176,9 @@ def moe(args) -> dict:
 
 def tp_o_proj(args) -> dict:
     """Layer 0's attention output projection under tensor parallelism, device-timed on every rank
-    (the maximum reported): the GEMM pushing FP32 partials over NVLink fused with the rank-ordered
-    all-reduce + residual + RMSNorm ("fused"), and the same GEMM writing locally ("local")."""
+    (the maximum reported): the GEMM writing its FP32 partial followed by the rank-ordered
+    all-reduce + residual + RMSNorm that pulls every rank's partial over NVLink ("fused"), and the
+    GEMM alone ("local")."""
     import datetime
     import os
 
@@ -208,10 +209,10 @@ def tp_o_proj(args) -> dict:
     tp.detach(model)
     dist.destroy_process_group()
     one_shot = r["two_shot"] == 0
-    # Bytes each rank must move across NVLink: FP32 partials out (every row to every peer, or each
-    # row to its owner), plus (two-shot) the BF16 residual and normed rows of its slice to every peer.
+    # Bytes each rank must move across NVLink: FP32 partials read from the peers (every row, or the
+    # rows of its slice), plus (two-shot) its slice's BF16 normed rows stored into every peer.
     nvlink = (args.rows * H * 4 * (world - 1) if one_shot
-              else args.rows * H * 4 * (world - 1) / world + 2 * args.rows * H * 2 * (world - 1) / world)
+              else args.rows * H * 4 * (world - 1) / world + args.rows * H * 2 * (world - 1) / world)
     peaks = _peaks()
     roof = {"nvlink_us": nvlink / 770e3,
             "weights_us": H * K * 2 / (peaks["hbm_gbs"] * 1e3),
