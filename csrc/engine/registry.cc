@@ -91,6 +91,7 @@ const KnownSize kSizes[] = {
     {"llama", "8B", 4096, 14336, 32, 32, 8},    {"llama", "70B", 8192, 28672, 80, 64, 8},
     {"mistral", "7B", 4096, 14336, 32, 32, 8},  {"mistral", "12B", 5120, 14336, 40, 32, 8},
     {"qwen3_moe", "30B-A3B", 2048, 6144, 48, 32, 4}, {"qwen3_moe", "235B-A22B", 4096, 12288, 94, 64, 4},
+    {"mixtral", "8x7B", 4096, 14336, 32, 32, 8},  {"mixtral", "8x22B", 6144, 16384, 56, 48, 8},
 };
 
 std::string size_of(const std::string& family, const ModelConfig& m) {
@@ -195,6 +196,25 @@ ModelConfig qwen3_moe_scope(const Checkpoint& ck) {
   return m;
 }
 
+// Mixtral: Llama attention (no QK-norm) and a routed SwiGLU of num_local_experts experts a layer,
+// softmax over every expert then the top num_experts_per_tok renormalised (the routing of the MoE
+// line with its top-k weights normalised); intermediate_size is an expert's width.
+ModelConfig mixtral_scope(const Checkpoint& ck) {
+  ModelConfig m = decoder_config(ck, "mixtral", 1000000.0, 1e-5f);
+  const Json& c = ck.config();
+  if (c["sliding_window"].is_number()) unsupported("sliding_window", "Mixtral attends the whole history here");
+  m.experts = static_cast<int>(need_int(c, "num_local_experts"));
+  m.top_k = static_cast<int>(need_int(c, "num_experts_per_tok"));
+  m.expert_intermediate = m.intermediate;
+  m.norm_topk = true;
+  if (m.expert_intermediate % 128 != 0) unsupported("intermediate_size", "not a multiple of 128");
+  if (get_num(c, "router_jitter_noise", 0.0) != 0.0) unsupported("router_jitter_noise", "routing is deterministic here");
+  if (!ck.declaration().is_null()) unsupported("quantization_config", "the MoE line reads BF16 checkpoints");
+  m.size = size_of("mixtral", m);
+  m.precision = "bfloat16";
+  return m;
+}
+
 Implementation make(const char* family, const char* cls, const char* form, Output out,
                     std::function<ModelConfig(const Checkpoint&)> scope) {
   Implementation i;
@@ -204,7 +224,8 @@ Implementation make(const char* family, const char* cls, const char* form, Outpu
   i.output = out;
   i.scope = std::move(scope);
   // Dense BF16 decoders take LoRA adapters (two slots a call).
-  i.adapters = (std::string(form) == "bf16" && std::string(family) != "qwen3_moe" && out != Output::Scores) ? 2 : 0;
+  const bool moe = std::string(family) == "qwen3_moe" || std::string(family) == "mixtral";
+  i.adapters = (std::string(form) == "bf16" && !moe && out != Output::Scores) ? 2 : 0;
   return i;
 }
 
@@ -234,6 +255,8 @@ const std::map<std::string, std::vector<Implementation>>& served() {
                                     [](const Checkpoint& c) { return llama_scope(c, "mistral", "bf16"); })};
     t["Qwen3MoeForCausalLM"] = {make("qwen3_moe", "qwen3_moe.ForCausalLM", "bf16", Output::Tokens,
                                      [](const Checkpoint& c) { return qwen3_moe_scope(c); })};
+    t["MixtralForCausalLM"] = {make("mixtral", "mixtral.ForCausalLM", "bf16", Output::Tokens,
+                                    [](const Checkpoint& c) { return mixtral_scope(c); })};
     // Gemma 4 unified's media embedders, loaded alone (registry.rs:571): an Encoder.
     t["Gemma4UnifiedForConditionalGeneration"] = {
         make("gemma4_unified", "Encoder", "bf16", Output::Hidden, [](const Checkpoint& c) {
@@ -779,7 +802,14 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       // Router (every expert) and this rank's experts, gate/up interleaved in 128-row blocks.
       const int E = cfg.experts, El = model.experts_local(), e0 = model.expert_first();
       const int64_t I = cfg.expert_intermediate;
-      if (auto* t = take(hf + "mlp.gate.weight", {E, H})) {
+      // Expert block names: Qwen3-MoE `mlp.gate`, `mlp.experts.e.{gate,up,down}_proj`; Mixtral
+      // `block_sparse_moe.gate`, `block_sparse_moe.experts.e.{w1,w3,w2}`.
+      const bool mixtral = cfg.family == "mixtral";
+      const std::string block = hf + (mixtral ? "block_sparse_moe." : "mlp.");
+      const char* gate_name = mixtral ? "w1.weight" : "gate_proj.weight";
+      const char* up_name = mixtral ? "w3.weight" : "up_proj.weight";
+      const char* down_name = mixtral ? "w2.weight" : "down_proj.weight";
+      if (auto* t = take(block + "gate.weight", {E, H})) {
         image(en + "router");
         copy_rows(Source(t), 0, E, 0, 0, H, H);
         upload(en + "router");
@@ -787,9 +817,9 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       image(en + "experts_gate_up");
       bool complete = true;
       for (int x = 0; x < El; ++x) {
-        const std::string ep = hf + "mlp.experts." + std::to_string(e0 + x) + ".";
-        const auto* g = take(ep + "gate_proj.weight", {I, H});
-        const auto* u = take(ep + "up_proj.weight", {I, H});
+        const std::string ep = block + "experts." + std::to_string(e0 + x) + ".";
+        const auto* g = take(ep + gate_name, {I, H});
+        const auto* u = take(ep + up_name, {I, H});
         if (!g || !u) {
           complete = false;
           continue;
@@ -805,8 +835,8 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       image(en + "experts_down");
       complete = true;
       for (int x = 0; x < El; ++x) {
-        const std::string ep = hf + "mlp.experts." + std::to_string(e0 + x) + ".";
-        if (auto* t = take(ep + "down_proj.weight", {H, I}))
+        const std::string ep = block + "experts." + std::to_string(e0 + x) + ".";
+        if (auto* t = take(ep + down_name, {H, I}))
           copy_rows(Source(t), 0, H, static_cast<int64_t>(x) * H, 0, I, I);
         else
           complete = false;
@@ -815,8 +845,8 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
       // Other ranks' experts are theirs to load.
       for (int x = 0; x < E; ++x) {
         if (x >= e0 && x < e0 + El) continue;
-        const std::string ep = hf + "mlp.experts." + std::to_string(x) + ".";
-        for (const char* n : {"gate_proj.weight", "up_proj.weight", "down_proj.weight"})
+        const std::string ep = block + "experts." + std::to_string(x) + ".";
+        for (const char* n : {gate_name, up_name, down_name})
           if (used.count(ep + n)) used[ep + n] = true;
       }
     }

@@ -199,6 +199,7 @@ void bind_engine(py::module_& m) {
   py::module_ llama = m.def_submodule("llama", "Llama decoders.");
   py::module_ mistral = m.def_submodule("mistral", "Mistral decoders.");
   py::module_ qwen3_moe = m.def_submodule("qwen3_moe", "Qwen3 mixture-of-experts decoders.");
+  py::module_ mixtral = m.def_submodule("mixtral", "Mixtral mixture-of-experts decoders.");
 
   // ---------------------------------------------------------------- Placement / Device
   py::class_<Placement>(m, "Placement", "Physical chips, in rank order, and the PEs used on each.")
@@ -609,6 +610,7 @@ void bind_engine(py::module_& m) {
   py::class_<PyMistralForCausalLM, PyDecoder>(mistral, "ForCausalLM", "HF MistralForCausalLM, loaded on a device.");
   py::class_<PyQwen3MoeForCausalLM, PyDecoder>(qwen3_moe, "ForCausalLM",
                                                "HF Qwen3MoeForCausalLM, loaded on a device.");
+  py::class_<PyMixtralForCausalLM, PyDecoder>(mixtral, "ForCausalLM", "HF MixtralForCausalLM, loaded on a device.");
 
   // Builds a decoder of `config` (a dict of geometry) with N(0, std) weights: synthetic models
   // of a named architecture for benchmarks and tests.
@@ -630,6 +632,8 @@ void bind_engine(py::module_& m) {
     };
     if (cfg.family == "llama") { PyLlamaForCausalLM d; fill(d); return py::cast(d); }
     if (cfg.family == "mistral") { PyMistralForCausalLM d; fill(d); return py::cast(d); }
+    if (cfg.family == "qwen3_moe") { PyQwen3MoeForCausalLM d; fill(d); return py::cast(d); }
+    if (cfg.family == "mixtral") { PyMixtralForCausalLM d; fill(d); return py::cast(d); }
     if (cfg.output == Output::Hidden) { PyQwen3Model d; fill(d); return py::cast(d); }
     if (cfg.output == Output::Scores) { PyQwen3ForSequenceClassification d; fill(d); return py::cast(d); }
     PyQwen3ForCausalLM d;

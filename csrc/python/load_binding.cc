@@ -57,6 +57,16 @@ py::object make_decoder(const Selection& s, std::shared_ptr<DecoderModel> model,
     fill(d);
     return py::cast(d);
   }
+  if (cls == "qwen3_moe.ForCausalLM") {
+    PyQwen3MoeForCausalLM d;
+    fill(d);
+    return py::cast(d);
+  }
+  if (cls == "mixtral.ForCausalLM") {
+    PyMixtralForCausalLM d;
+    fill(d);
+    return py::cast(d);
+  }
   PyQwen3ForCausalLM d;
   fill(d);
   return py::cast(d);

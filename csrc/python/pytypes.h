@@ -21,6 +21,7 @@ struct PyQwen3Model : PyDecoder {};
 struct PyLlamaForCausalLM : PyDecoder {};
 struct PyMistralForCausalLM : PyDecoder {};
 struct PyQwen3MoeForCausalLM : PyDecoder {};
+struct PyMixtralForCausalLM : PyDecoder {};
 // A media encoder (a load of a vision-language model's encoder alone).
 struct PyEncoder {
   std::shared_ptr<foa::engine::MediaEncoder> encoder;

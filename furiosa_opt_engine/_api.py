@@ -20,9 +20,10 @@ qwen3 = _native.qwen3
 llama = _native.llama
 mistral = _native.mistral
 qwen3_moe = _native.qwen3_moe
+mixtral = _native.mixtral
 vision_language = _native.vision_language
 
-for _name in ("decoder", "qwen3", "llama", "mistral", "qwen3_moe", "vision_language"):
+for _name in ("decoder", "qwen3", "llama", "mistral", "qwen3_moe", "mixtral", "vision_language"):
     _sys.modules[f"furiosa_opt_engine.{_name}"] = getattr(_native, _name)
 
 if _native._trace_level() != "off":
@@ -46,6 +47,7 @@ __all__ = [
     "decoder",
     "llama",
     "mistral",
+    "mixtral",
     "qwen3",
     "qwen3_moe",
     "vision_language",

@@ -67,6 +67,19 @@ CONFIGS: dict[str, dict] = {
         qk_norm=True, tied=False, rope=QWEN3_ROPE, window=40960, rows=8192, experts=128, top_k=8,
         expert_intermediate=768, norm_topk=True,
     ),
+    # A tiny Mixtral geometry (8 experts, top-2) that splits over 2/4/8 chips.
+    "tiny-mixtral": dict(
+        architecture="MixtralForCausalLM", family="mixtral", size="tiny", hidden=256, intermediate=256,
+        layers=2, q_heads=8, kv_heads=2, head_dim=64, vocab=1024, eps=1e-5, qk_norm=False, tied=False,
+        rope={"type": "default", "theta": 1_000_000.0}, window=4096, rows=8192, experts=8, top_k=2,
+        expert_intermediate=256, norm_topk=True,
+    ),
+    "mixtral-8x7b": dict(
+        architecture="MixtralForCausalLM", family="mixtral", size="8x7B", hidden=4096, intermediate=14336,
+        layers=32, q_heads=32, kv_heads=8, head_dim=128, vocab=32000, eps=1e-5, qk_norm=False, tied=False,
+        rope={"type": "default", "theta": 1_000_000.0}, window=32768, rows=8192, experts=8, top_k=2,
+        expert_intermediate=14336, norm_topk=True,
+    ),
 }
 
 

@@ -16,7 +16,8 @@ def hf_config(cfg: dict) -> dict:
     """The HF config.json of an engine geometry."""
     out = {
         "architectures": [cfg["architecture"]],
-        "model_type": {"qwen3": "qwen3", "llama": "llama", "mistral": "mistral", "qwen3_moe": "qwen3_moe"}[cfg["family"]],
+        "model_type": {"qwen3": "qwen3", "llama": "llama", "mistral": "mistral", "qwen3_moe": "qwen3_moe",
+                       "mixtral": "mixtral"}[cfg["family"]],
         "hidden_size": cfg["hidden"],
         "intermediate_size": cfg["intermediate"],
         "num_hidden_layers": cfg["layers"],
@@ -42,11 +43,19 @@ def hf_config(cfg: dict) -> dict:
         out["rope_scaling"] = scaling
     if cfg["family"] == "qwen3":
         out["use_sliding_window"] = False
+    if cfg["family"] == "mixtral":
+        out.update(num_local_experts=cfg["experts"], num_experts_per_tok=cfg["top_k"],
+                   intermediate_size=cfg["expert_intermediate"], sliding_window=None, router_jitter_noise=0.0)
     if cfg["family"] == "qwen3_moe":
         out.update(num_experts=cfg["experts"], num_experts_per_tok=cfg["top_k"],
                    moe_intermediate_size=cfg["expert_intermediate"], norm_topk_prob=cfg["norm_topk"],
                    decoder_sparse_step=1, mlp_only_layers=[])
     return out
+
+
+# HF names of a mixture-of-experts block: (prefix under the layer, gate, up, down projections).
+MOE_NAMES = {"qwen3_moe": ("mlp.", "gate_proj", "up_proj", "down_proj"),
+             "mixtral": ("block_sparse_moe.", "w1", "w3", "w2")}
 
 
 def hf_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict[str, torch.Tensor]:
@@ -75,13 +84,14 @@ def hf_weights(cfg: dict, seed: int = 0, std: float = 0.02) -> dict[str, torch.T
         if cfg.get("qk_norm"):
             w[p + "self_attn.q_norm.weight"] = ones(D)
             w[p + "self_attn.k_norm.weight"] = ones(D)
-        if cfg["family"] == "qwen3_moe":
+        if cfg["family"] in MOE_NAMES:
             E, Ie = cfg["experts"], cfg["expert_intermediate"]
-            w[p + "mlp.gate.weight"] = rnd(E, H)
+            block, gname, uname, dname = MOE_NAMES[cfg["family"]]
+            w[p + block + "gate.weight"] = rnd(E, H)
             for e in range(E):
-                w[p + f"mlp.experts.{e}.gate_proj.weight"] = rnd(Ie, H)
-                w[p + f"mlp.experts.{e}.up_proj.weight"] = rnd(Ie, H)
-                w[p + f"mlp.experts.{e}.down_proj.weight"] = rnd(H, Ie)
+                w[p + f"{block}experts.{e}.{gname}.weight"] = rnd(Ie, H)
+                w[p + f"{block}experts.{e}.{uname}.weight"] = rnd(Ie, H)
+                w[p + f"{block}experts.{e}.{dname}.weight"] = rnd(H, Ie)
         else:
             w[p + "mlp.gate_proj.weight"] = rnd(I, H)
             w[p + "mlp.up_proj.weight"] = rnd(I, H)
@@ -134,13 +144,15 @@ def engine_weights(cfg: dict, hf: dict[str, torch.Tensor]) -> dict[str, torch.Te
         if p + "mlp.gate_proj.weight" in hf:
             out[e + "gate_up"] = interleave_gate_up(hf[p + "mlp.gate_proj.weight"], hf[p + "mlp.up_proj.weight"])
             out[e + "down"] = hf[p + "mlp.down_proj.weight"]
-        if p + "mlp.gate.weight" in hf:
+        if cfg.get("experts"):
             E = cfg["experts"]
-            out[e + "router"] = hf[p + "mlp.gate.weight"]
+            block, gname, uname, dname = MOE_NAMES[cfg["family"]]
+            q = p + block
+            out[e + "router"] = hf[q + "gate.weight"]
             out[e + "experts_gate_up"] = torch.cat([
-                interleave_gate_up(hf[p + f"mlp.experts.{x}.gate_proj.weight"], hf[p + f"mlp.experts.{x}.up_proj.weight"])
+                interleave_gate_up(hf[q + f"experts.{x}.{gname}.weight"], hf[q + f"experts.{x}.{uname}.weight"])
                 for x in range(E)])
-            out[e + "experts_down"] = torch.cat([hf[p + f"mlp.experts.{x}.down_proj.weight"] for x in range(E)])
+            out[e + "experts_down"] = torch.cat([hf[q + f"experts.{x}.{dname}.weight"] for x in range(E)])
     return out
 
 
@@ -277,13 +289,14 @@ def hf_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
         if cfg.get("qk_norm"):
             out[p + "self_attn.q_norm.weight"] = (D,)
             out[p + "self_attn.k_norm.weight"] = (D,)
-        if cfg["family"] == "qwen3_moe":
+        if cfg["family"] in MOE_NAMES:
             E, Ie = cfg["experts"], cfg["expert_intermediate"]
-            out[p + "mlp.gate.weight"] = (E, H)
+            block, gname, uname, dname = MOE_NAMES[cfg["family"]]
+            out[p + block + "gate.weight"] = (E, H)
             for e in range(E):
-                out[p + f"mlp.experts.{e}.gate_proj.weight"] = (Ie, H)
-                out[p + f"mlp.experts.{e}.up_proj.weight"] = (Ie, H)
-                out[p + f"mlp.experts.{e}.down_proj.weight"] = (H, Ie)
+                out[p + f"{block}experts.{e}.{gname}.weight"] = (Ie, H)
+                out[p + f"{block}experts.{e}.{uname}.weight"] = (Ie, H)
+                out[p + f"{block}experts.{e}.{dname}.weight"] = (H, Ie)
         else:
             out[p + "mlp.gate_proj.weight"] = (I, H)
             out[p + "mlp.up_proj.weight"] = (I, H)

@@ -289,3 +289,41 @@ def test_lora_adapters_in_two_slots(tmp_path):
     with pytest.raises(ValueError):
         model.forward([dec.Request([seqs[0].blocks], 0, seqs[0].prompt, dec.Keep.LAST, adapter=1)], cache,
                       [adapters[0], None])
+
+
+def test_mixtral_checkpoint_loads_strictly_and_matches_dense(tmp_path):
+    """A tiny Mixtral checkpoint (block_sparse_moe names, 8 experts, top-2 renormalised) loads
+    through LoadOptions as mixtral.ForCausalLM and decodes the dense forward's greedy tokens."""
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-mixtral")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=5, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine.LoadOptions().load(engine.Checkpoint(str(tmp_path / "m")), device)
+    assert isinstance(model, engine.mixtral.ForCausalLM)
+    gen = torch.Generator().manual_seed(8)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen, dtype=torch.int32) for n in (6, 25, 48)]
+    cache = dec.Cache(model.cache, 32)
+    alloc = serving.BlockAllocator(32)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(p).to_hbm(device), len(p), alloc.take(6))
+            for p in prompts]
+    steps = 5
+    out = serving.prefill(model, cache, seqs, list(range(len(seqs))))
+    tokens = [[t] for t in out.to_host().numpy().tolist()]
+    for _ in range(steps):
+        out = serving.decode(model, cache, seqs)
+        for i, t in enumerate(out.to_host().numpy().tolist()):
+            tokens[i].append(t)
+    device.synchronize()
+    for i, p in enumerate(prompts):
+        seq = p.clone()
+        for step in range(steps + 1):
+            logits = dense.forward(w, cfg, seq)[-1]
+            top = torch.topk(logits, 2).values
+            pick = tokens[i][step]
+            assert logits[pick] >= top[0] - 5e-2 * max(1.0, abs(top[0].item())), (i, step)
+            seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
