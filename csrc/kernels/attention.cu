@@ -434,12 +434,13 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const PagedAttention
   }, lane);
   // Key limits (inclusive) of this thread's two rows, and of the warp and CTA.
   const int pr0 = wm + g, pr1 = wm + g + 8;
-  const int lim0 = pr0 < total ? seg.cached + pr0 / G : -1;
-  const int lim1 = pr1 < total ? seg.cached + pr1 / G : -1;
+  const int all = seg.cached + seg.len - 1;  // bidirectional: every row attends every key
+  const int lim0 = pr0 < total ? (p.bidirectional ? all : seg.cached + pr0 / G) : -1;
+  const int lim1 = pr1 < total ? (p.bidirectional ? all : seg.cached + pr1 / G) : -1;
   const int last_pair = min(m0 + 63, total - 1);
-  const int keys_end = seg.cached + last_pair / G + 1;
+  const int keys_end = p.bidirectional ? all + 1 : seg.cached + last_pair / G + 1;
   const int warp_last = min(wm + 15, total - 1);
-  const int warp_end = wm < total ? seg.cached + warp_last / G + 1 : 0;
+  const int warp_end = wm < total ? (p.bidirectional ? all + 1 : seg.cached + warp_last / G + 1) : 0;
 
   Flash<D> f;
   f.init();

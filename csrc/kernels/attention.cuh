@@ -42,6 +42,9 @@ struct PagedAttention {
   // in flight (2 or 3; 0 takes the default of 2).
   int decode_warps = 0;
   int decode_stages = 0;
+  // Prefill: 0 causal (row i of a segment attends keys 0 .. cached + i); 1 bidirectional (every
+  // row attends all cached + len keys of its segment: encoders, dense attention over visible keys).
+  int bidirectional = 0;
 };
 
 // Decode: every segment appends one row (len == 1) and attends its whole history. A segment whose

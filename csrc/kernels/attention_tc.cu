@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(320, 1)
   const int tok_per_tile = kRowsTc / G;
   const int tok0 = tile * tok_per_tile;                   // first token of the tile in the segment
   const int last_tok = min(seg.len, tok0 + tok_per_tile) - 1;
-  const int keys_end = seg.cached + last_tok + 1;         // keys any row of the tile attends
+  // Keys any row of the tile attends (every key of the segment when bidirectional).
+  const int keys_end = p.bidirectional ? seg.cached + seg.len : seg.cached + last_tok + 1;
   const int ntiles = (keys_end + kKeysTc - 1) / kKeysTc;
 
   if (threadIdx.x == 0) {
@@ -272,9 +273,10 @@ __global__ void __launch_bounds__(320, 1)
     const uint32_t lane_base = tmem + ((uint32_t)(q * 32) << 16);
     const int tok = tok0 + row / G, head = row % G;
     const bool valid = tok < seg.len;
-    const int qpos = valid ? seg.cached + tok : -1;  // the last key this row attends
-    // Keys every row of the tile attends: tiles below this need no mask.
-    const int unmasked_end = seg.cached + tok0 + 1;
+    // The last key this row attends, and the keys every row of the tile attends (tiles below
+    // need no mask).
+    const int qpos = !valid ? -1 : p.bidirectional ? seg.cached + seg.len - 1 : seg.cached + tok;
+    const int unmasked_end = p.bidirectional ? seg.cached + seg.len : seg.cached + tok0 + 1;
     const float scale = p.scale * kLog2eTc;
     float m_use = -INFINITY, l = 0.f;
     bool ok = true;

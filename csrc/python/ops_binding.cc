@@ -375,11 +375,12 @@ void bind_ops(py::module_& m) {
         [make_attn](uint64_t q, uint64_t o, uint64_t cache, uint64_t table, uint64_t segments,
                     int num_segments, int q_heads, int kv_heads, int head_dim, float scale,
                     uint64_t work, int num_work, uint64_t status, uint64_t stream, int rows,
-                    long cache_blocks) {
+                    long cache_blocks, bool bidirectional) {
           auto a = make_attn(q, o, cache, table, segments, num_segments, q_heads, kv_heads,
                              head_dim, scale, 0, 0, 0, 1, 512, status);
           a.rows = rows;
           a.cache_blocks = cache_blocks;
+          a.bidirectional = bidirectional ? 1 : 0;
           py::gil_scoped_release nogil;
           check(foa::paged_prefill(a, as_ptr<const int32_t>(work), num_work, as_stream(stream)),
                 "paged_prefill");
@@ -387,5 +388,5 @@ void bind_ops(py::module_& m) {
         py::arg("q"), py::arg("o"), py::arg("cache"), py::arg("table"), py::arg("segments"),
         py::arg("num_segments"), py::arg("q_heads"), py::arg("kv_heads"), py::arg("head_dim"),
         py::arg("scale"), py::arg("work"), py::arg("num_work"), py::arg("status"), py::arg("stream"),
-        py::arg("rows") = 0, py::arg("cache_blocks") = 0);
+        py::arg("rows") = 0, py::arg("cache_blocks") = 0, py::arg("bidirectional") = false);
 }

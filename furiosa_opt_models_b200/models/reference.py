@@ -65,11 +65,13 @@ def gather_kv(cache: torch.Tensor, table, table_start: int, keys: int):
     return k.float(), v.float()
 
 
-def paged_attention(q: torch.Tensor, cache: torch.Tensor, table, segments, scale: float | None = None):
-    """Causal GQA attention of every segment's rows over its paged history, in FP32.
+def paged_attention(q: torch.Tensor, cache: torch.Tensor, table, segments, scale: float | None = None,
+                    causal: bool = True):
+    """GQA attention of every segment's rows over its paged history, in FP32.
 
     ``q`` [rows, q_heads, d]; ``segments`` rows of (row_start, len, cached, table_start, nblocks).
-    Row i of a segment is position cached + i and attends keys 0..cached + i."""
+    Row i of a segment is position cached + i and attends keys 0..cached + i (causal), or every
+    key 0..cached + len - 1 of its segment (``causal=False``)."""
     rows, q_heads, d = q.shape
     kv_heads = cache.shape[2]
     group = q_heads // kv_heads
@@ -83,7 +85,7 @@ def paged_attention(q: torch.Tensor, cache: torch.Tensor, table, segments, scale
         qs = q[row_start : row_start + length].float()  # [len, q_heads, d]
         s = torch.einsum("lhd,khd->hlk", qs, k) * scale
         pos = torch.arange(length)[:, None] + cached
-        mask = torch.arange(keys)[None, :] <= pos
+        mask = torch.arange(keys)[None, :] <= (pos if causal else torch.full_like(pos, keys - 1))
         s = s.masked_fill(~mask[None], float("-inf"))
         out[row_start : row_start + length] = torch.einsum("hlk,khd->lhd", torch.softmax(s, -1), v)
     return out

@@ -320,9 +320,11 @@ def prefill_work(segments_cpu, group: int) -> torch.Tensor:
     return torch.tensor(work, dtype=torch.int32).reshape(-1, 2)
 
 
-def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=None, tensor_cores=True):
-    """Causal attention of segments' rows over their history and themselves (128-row query tiles
-    of ``prefill_work``). ``cache`` is the layer's pages [blocks, 2, kv_heads, 16, d];
+def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=None, tensor_cores=True,
+                  causal=True):
+    """Attention of segments' rows over their history and themselves (128-row query tiles of
+    ``prefill_work``): causal, or with ``causal=False`` bidirectional (every row attends every key
+    of its segment, as encoders do). ``cache`` is the layer's pages [blocks, 2, kv_heads, 16, d];
     ``tensor_cores=False`` runs the mma.sync kernel."""
     _attn_common(segments)
     rows, q_heads, d = q.shape
@@ -332,7 +334,8 @@ def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=Non
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(),
         segments.shape[0], q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5),
         work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream(),
-        rows=rows if tensor_cores else 0, cache_blocks=cache.shape[0] if tensor_cores else 0)
+        rows=rows if tensor_cores else 0, cache_blocks=cache.shape[0] if tensor_cores else 0,
+        bidirectional=not causal)
     return out
 
 

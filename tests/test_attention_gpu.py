@@ -122,3 +122,23 @@ def test_block_ids_past_the_cache_are_refused_on_the_device():
         assert int(s.status[0].item()) == 8, tc
         assert torch.isfinite(out.float()).all()
         s.status.zero_()
+
+
+@pytest.mark.parametrize("tensor_cores", [True, False], ids=["tcgen05", "mma_sync"])
+@pytest.mark.parametrize("q_heads,kv_heads,d", [(16, 8, 128), (8, 8, 64), (32, 4, 64)])
+def test_bidirectional_prefill(q_heads, kv_heads, d, tensor_cores):
+    """Dense attention over every visible key of a segment (encoders): each row attends the whole
+    history and every row of its own chunk, against the FP32 reference without the causal mask."""
+    from furiosa_opt_models_b200 import ops
+    from furiosa_opt_models_b200.models import reference
+
+    lengths = [7, 64, 130, 200, 1]
+    cached = [0, 16, 0, 33, 90]
+    q, cache, table, segs = _setup(lengths, cached, q_heads, kv_heads, d)
+    ref = reference.paged_attention(q, cache, table, segs, causal=False)
+    work = ops.prefill_work(segs, q_heads // kv_heads)
+    out = ops.paged_prefill(q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), kv_heads, work.cuda(),
+                            tensor_cores=tensor_cores, causal=False)
+    torch.cuda.synchronize()
+    err = (out.float().cpu() - ref).abs().max().item()
+    assert err < 2e-2, err
