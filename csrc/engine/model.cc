@@ -12,6 +12,7 @@
 #include "kernels/moe.cuh"
 #include "kernels/ops.cuh"
 #include "lora.h"
+#include "modules.h"
 
 namespace foa::engine {
 
@@ -636,18 +637,65 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
   return result;
 }
 
-int DecoderModel::launch(const Plan& plan, const Cache& cache) {
-  auto st = device_.state();
-  cudaStream_t s = st->stream;
-  const int H = cfg_.hidden, D = cfg_.head_dim;
-  const int64_t T = plan.rows_padded;
-  const Staged& sg = plan.staged;
-  const HbmBuffer& stage = ws_stage_;
+// ------------------------------------------------------------------------------------ launch
+// One call's launch state: the plan and its staged operands, the stream, the activation buffers
+// and the kernel accounting (count, per-kernel trace spans, host-side fault drills).
+struct Launch {
+  DecoderModel& m;
+  const Plan& plan;
+  const Cache& cache;
+  DeviceState* st;
+  cudaStream_t s;
+  const ModelConfig& cfg;
+  int H, D;
+  int64_t T;
+  const Staged& sg;
+  const HbmBuffer& stage;
   int kernels = 0;
-  // Per-kernel device spans (trace level): an event after every launch.
-  const bool per_kernel = trace_level() >= TraceLevel::Trace;
-  cudaEvent_t prev = per_kernel ? Tracer::get().record(st->ordinal, s) : nullptr;
-  auto fail = [&](int rc, const char* what) {
+  bool per_kernel;
+  cudaEvent_t prev = nullptr;
+  __nv_bfloat16* x;  // residual stream [T, H]
+  __nv_bfloat16* h;  // normed rows [T, H]
+  foa::PagedAttention attn;
+  foa::RopeTable rope;
+
+  Launch(DecoderModel& model, const Plan& p, const Cache& c)
+      : m(model), plan(p), cache(c), st(model.device_.state().get()), s(st->stream), cfg(model.cfg_),
+        H(cfg.hidden), D(cfg.head_dim), T(p.rows_padded), sg(p.staged), stage(model.ws_stage_),
+        per_kernel(trace_level() >= TraceLevel::Trace) {
+    if (per_kernel) prev = Tracer::get().record(st->ordinal, s);
+    // Tensor-parallel ranks keep the residual stream and the normed rows in the symmetric heap,
+    // where the fused collectives write them.
+    x = m.coll_ ? m.coll_->residual_buffer() : bf(m.ws_x_);
+    h = m.coll_ ? m.coll_->hidden_buffer() : bf(m.ws_h_);
+    attn.q = bf(m.ws_q_);
+    attn.o = bf(m.ws_attn_);
+    attn.table = op(sg.table);
+    attn.segments = reinterpret_cast<const foa::Segment*>(op(sg.segments));
+    attn.q_heads = m.qh_l_;
+    attn.kv_heads = m.kvh_l_;
+    attn.head_dim = D;
+    attn.scale = 1.0f / std::sqrt(static_cast<float>(D));
+    attn.partial_o = static_cast<float*>(m.ws_part_o_.data());
+    attn.partial_lse = static_cast<float*>(m.ws_part_lse_.data());
+    attn.partial_capacity = static_cast<size_t>(m.ws_decode_ * m.qh_l_ * m.ws_splits_);
+    attn.max_keys = static_cast<int>(p.max_keys);
+    attn.keys_per_split = m.keys_per_split_;
+    attn.decode_warps = m.decode_warps_;
+    attn.status = st->status;
+    attn.rows = static_cast<int>(T);
+    attn.cache_blocks = c.blocks();
+    rope = foa::RopeTable{static_cast<const float*>(m.inv_freq_.data()), m.attention_factor_};
+  }
+
+  int32_t* op(size_t off) const { return i32(stage, off); }
+  const WeightSlot& w(const std::string& n) const { return m.weights_.at(n); }
+  __nv_bfloat16* wp(const std::string& n) const { return m.weights_.at(n).ptr; }
+  bool tp() const { return m.tp_ > 1; }
+
+  // Accounts for one enqueued kernel (`rc` its launcher's code): a rejected launch poisons the
+  // device; at trace level the kernel gets its own device span.
+  void done(int rc, const char* what) {
     if (rc == 0 && st->injected("launch")) rc = -5;
     if (rc != 0) st->fail(std::string(what) + " launch rejected (" + std::to_string(rc) + ")");
     ++kernels;
@@ -656,11 +704,12 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
       Tracer::get().device_span(what, "GPU", st->ordinal, prev, now);
       prev = now;
     }
-  };
-  const char* gemm_name = "gemm";  // the projection's name in per-kernel traces
-  auto gemm = [&](const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c, long ldc,
-                  int epi, const void* res, int lora_layer = -1, int lora_module = 0,
-                  const foa::GemmPeerOut* peer = nullptr) {
+  }
+
+  // One projection C = epilogue(A W^T) in the weight's format, with this call's LoRA segments.
+  void gemm(const char* gemm_name, const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c,
+            long ldc, int epi, const void* res, int lora_layer = -1, int lora_module = 0,
+            const foa::GemmPeerOut* peer = nullptr) {
     foa::GemmArgs g;
     if (peer != nullptr) g.peer = *peer;
     // LoRA slots: Z_s = X A_s^T (its rows zeroed outside slot s), added as extra K segments
@@ -668,13 +717,13 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     int nseg = 0;
     if (lora_layer >= 0) {
       int kpad = 0;
-      for (const auto& ad : call_adapters_)
+      for (const auto& ad : m.call_adapters_)
         if (ad) kpad = std::max(kpad, ad->factor(lora_layer, lora_module).kpad);
       if (kpad > 0) {
-        __nv_bfloat16* z = bf(ws_lora_z_);
+        __nv_bfloat16* z = bf(m.ws_lora_z_);
         const int ldz = 2 * 128;
-        for (size_t slot = 0; slot < call_adapters_.size(); ++slot) {
-          const auto& ad = call_adapters_[slot];
+        for (size_t slot = 0; slot < m.call_adapters_.size(); ++slot) {
+          const auto& ad = m.call_adapters_[slot];
           if (!ad) continue;
           const LoraFactor& f = ad->factor(lora_layer, lora_module);
           if (f.kpad == 0) continue;
@@ -689,17 +738,17 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
           sh.c = z + slot * 128;
           sh.ldc = ldz;
           sh.status = st->status;
-          sh.workspace = static_cast<float*>(ws_gemm_.data());
-          sh.workspace_bytes = ws_gemm_.size();
-          sh.counters = i32(ws_counters_);
+          sh.workspace = static_cast<float*>(m.ws_gemm_.data());
+          sh.workspace_bytes = m.ws_gemm_.size();
+          sh.counters = i32(m.ws_counters_);
           sh.counters_len = 32768;
-          if (batch_invariant_) {
+          if (m.batch_invariant_) {
             sh.mode = foa::kModeRows;
             sh.splits = 1;
           }
-          fail(foa::gemm_bf16(sh, s), "lora shrink");
-          fail(foa::lora_mask(z + slot * 128, ldz, M, f.kpad, static_cast<int>(slot),
-                              i32(stage, plan.staged.adapters), s),
+          done(foa::gemm_bf16(sh, s), "lora shrink");
+          done(foa::lora_mask(z + slot * 128, ldz, M, f.kpad, static_cast<int>(slot),
+                              op(sg.adapters), s),
                "lora mask");
           g.seg[nseg].a = z + slot * 128;
           g.seg[nseg].lda = ldz;
@@ -722,21 +771,21 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     if (w.format == foa::kWeightFp8A8) {
       // Inputs quantized per (row, 128-input group) ahead of the FP8 MMA.
       const int pad = (M + 127) / 128 * 128;
-      fail(foa::quantize_fp8_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, u8(ws_qa_), K,
-                                 static_cast<float*>(ws_qs_.data()), pad, s),
+      done(foa::quantize_fp8_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, u8(m.ws_qa_), K,
+                                 static_cast<float*>(m.ws_qs_.data()), pad, s),
            "input quantization");
-      g.a = ws_qa_.data();
+      g.a = m.ws_qa_.data();
       g.lda = K;
-      g.a_scale = ws_qs_.data();
+      g.a_scale = m.ws_qs_.data();
       g.a_scale_ld = pad;
     } else if (w.format == foa::kWeightNvfp4A4) {
       // Inputs quantized under the projection's input scale ahead of the block-scaled MMA.
-      fail(foa::quantize_nvfp4_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, 1.f / w.input_scale,
-                                   u8(ws_qa_), K / 2, u8(ws_qs_), s),
+      done(foa::quantize_nvfp4_act(static_cast<const __nv_bfloat16*>(a), lda, M, K, 1.f / w.input_scale,
+                                   u8(m.ws_qa_), K / 2, u8(m.ws_qs_), s),
            "input quantization");
-      g.a = ws_qa_.data();
+      g.a = m.ws_qa_.data();
       g.lda = K;
-      g.a_scale = ws_qs_.data();
+      g.a_scale = m.ws_qs_.data();
       g.w_tensor_scale = w.input_scale * w.tensor_scale;
     }
     g.M = M;
@@ -747,201 +796,309 @@ int DecoderModel::launch(const Plan& plan, const Cache& cache) {
     g.residual = res;
     g.ldr = ldc;
     g.epilogue = epi;
-    g.workspace = static_cast<float*>(ws_gemm_.data());
-    g.workspace_bytes = ws_gemm_.size();
-    g.counters = i32(ws_counters_);
+    g.workspace = static_cast<float*>(m.ws_gemm_.data());
+    g.workspace_bytes = m.ws_gemm_.size();
+    g.counters = i32(m.ws_counters_);
     g.counters_len = 32768;  // the first half; the second serves the attention merge
     g.status = st->status;
-    if (batch_invariant_) {
+    if (m.batch_invariant_) {
       // W8A8 SwiGLU tiles only on the swap mapping; its sums do not depend on the tile shape.
       g.mode = (w.format == foa::kWeightFp8A8 && epi == foa::kEpiSwiGLU) ? foa::kModeSwap : foa::kModeRows;
       g.splits = 1;
     }
-    fail(foa::gemm_bf16(g, s), gemm_name);
-  };
-  const int qkv_cols = (qh_l_ + 2 * kvh_l_) * D;
-  // Tensor-parallel ranks keep the residual stream and the normed rows in the symmetric heap,
-  // where the fused collectives write them.
-  __nv_bfloat16* x = coll_ ? coll_->residual_buffer() : bf(ws_x_);
-  __nv_bfloat16* h = coll_ ? coll_->hidden_buffer() : bf(ws_h_);
-  const auto& W = weights_;
-  auto w = [&](const std::string& n) -> __nv_bfloat16* { return W.at(n).ptr; };
-  auto ws = [&](const std::string& n) -> const WeightSlot& { return W.at(n); };
-  const int64_t count = std::max<int64_t>(plan.requests, plan.rows_padded);
+    done(foa::gemm_bf16(g, s), gemm_name);
+  }
+};
 
-  // Tokens: padded rows read ID 0 (zeroed by the staging), the requests' IDs are gathered.
-  fail(foa::gather_tokens(i32(stage, sg.sources), static_cast<int>(count), i32(stage, sg.tokens), s),
-       "gather tokens");
-  // The embedding table is whole on every chip (the head is vocabulary-parallel).
-  fail(foa::embedding(i32(stage, sg.tokens), w("embed"), H, 0, cfg_.vocab, x, H,
-                      static_cast<int>(T), H, s),
-       "embedding");
-  const bool tp = tp_ > 1;
-  foa::PagedAttention attn;
-  attn.q = bf(ws_q_);
-  attn.o = bf(ws_attn_);
-  attn.table = i32(stage, sg.table);
-  attn.segments = reinterpret_cast<const foa::Segment*>(i32(stage, sg.segments));
-  attn.q_heads = qh_l_;
-  attn.kv_heads = kvh_l_;
-  attn.head_dim = D;
-  attn.scale = 1.0f / std::sqrt(static_cast<float>(D));
-  attn.partial_o = static_cast<float*>(ws_part_o_.data());
-  attn.partial_lse = static_cast<float*>(ws_part_lse_.data());
-  attn.partial_capacity = static_cast<size_t>(ws_decode_ * qh_l_ * ws_splits_);
-  attn.max_keys = static_cast<int>(plan.max_keys);
-  attn.keys_per_split = keys_per_split_;
-  attn.decode_warps = decode_warps_;
-  attn.status = st->status;
-  attn.rows = static_cast<int>(T);
-  attn.cache_blocks = cache.blocks();
-  foa::RopeTable rope{static_cast<const float*>(inv_freq_.data()), attention_factor_};
+namespace {
 
-  for (int l = 0; l < cfg_.layers; ++l) {
-    const std::string p = "layers." + std::to_string(l) + ".";
-    if (l == 0)
-      fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "in_norm"), h, H, nullptr, 0, static_cast<int>(T),
-                        H, cfg_.eps, s),
+std::string layer_prefix(int l) { return "layers." + std::to_string(l) + "."; }
+// The norm after layer l's last block: the next layer's input norm, or the final norm.
+std::string next_norm(int l, int layers) { return l + 1 < layers ? layer_prefix(l + 1) + "in_norm" : "final_norm"; }
+
+}  // namespace
+
+// The leaf modules of the decoder families (friends of DecoderModel: they read its workspace).
+struct DecoderBlocks {
+// Token IDs gathered into the call's rows (padded rows read ID 0), then their embedding rows. The
+// table is whole on every chip (the head is vocabulary-parallel).
+class Embed final : public Module {
+ public:
+  void forward(Launch& e) const override {
+    const int64_t count = std::max<int64_t>(e.plan.requests, e.plan.rows_padded);
+    e.done(foa::gather_tokens(e.op(e.sg.sources), static_cast<int>(count), e.op(e.sg.tokens), e.s), "gather tokens");
+    e.done(foa::embedding(e.op(e.sg.tokens), e.wp("embed"), e.H, 0, e.cfg.vocab, e.x, e.H, static_cast<int>(e.T),
+                          e.H, e.s),
+           "embedding");
+  }
+  std::string name() const override { return "Embed"; }
+};
+
+// h = RMSNorm(x) * weight.
+class Norm final : public Module {
+ public:
+  explicit Norm(std::string weight) : weight_(std::move(weight)) {}
+  void forward(Launch& e) const override {
+    e.done(foa::rmsnorm(e.x, e.H, nullptr, 0, e.wp(weight_), e.h, e.H, nullptr, 0, static_cast<int>(e.T), e.H,
+                        e.cfg.eps, e.s),
            "rmsnorm");
-    gemm_name = "gemm qkv";
-    gemm(h, H, ws(p + "qkv"), static_cast<int>(T), qkv_cols, H, ws_qkv_.data(), qkv_cols, foa::kEpiBf16,
-         nullptr, l, LoraAdapter::kQkv);
-    __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(cache.layers()[l].data());
-    fail(foa::qk_norm_rope_cache(bf(ws_qkv_), qkv_cols, static_cast<int>(T), qh_l_, kvh_l_, D,
-                                 cfg_.qk_norm ? w(p + "q_norm") : nullptr,
-                                 cfg_.qk_norm ? w(p + "k_norm") : nullptr, cfg_.eps,
-                                 i32(stage, sg.positions), rope, bf(ws_q_), layer_cache,
-                                 i32(stage, sg.slots), s, cache.blocks() * 16, st->status),
-         "attention front");
-    attn.cache = layer_cache;
-    if (plan.decode > 0) {
-      attn.num_segments = static_cast<int>(plan.prefill > 0 ? plan.decode : plan.segments_padded);
-      fail(foa::paged_decode(attn, s), "decode attention");
-      if (plan.max_keys > attn.keys_per_split) ++kernels;  // the split merge
+  }
+  std::string name() const override { return "Norm " + weight_; }
+
+ private:
+  std::string weight_;
+};
+
+// Packed q/k/v projection of h, then QK-norm, RoPE and the paged K/V store of layer l.
+class AttentionFront final : public Module {
+ public:
+  explicit AttentionFront(int l) : l_(l) {}
+  void forward(Launch& e) const override {
+    const std::string p = layer_prefix(l_);
+    const int cols = (e.m.qh_l_ + 2 * e.m.kvh_l_) * e.D;
+    e.gemm("gemm qkv", e.h, e.H, e.w(p + "qkv"), static_cast<int>(e.T), cols, e.H, e.m.ws_qkv_.data(), cols,
+           foa::kEpiBf16, nullptr, l_, LoraAdapter::kQkv);
+    __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(e.cache.layers()[l_].data());
+    e.done(foa::qk_norm_rope_cache(bf(e.m.ws_qkv_), cols, static_cast<int>(e.T), e.m.qh_l_, e.m.kvh_l_, e.D,
+                                   e.cfg.qk_norm ? e.wp(p + "q_norm") : nullptr,
+                                   e.cfg.qk_norm ? e.wp(p + "k_norm") : nullptr, e.cfg.eps, e.op(e.sg.positions),
+                                   e.rope, bf(e.m.ws_q_), layer_cache, e.op(e.sg.slots), e.s,
+                                   e.cache.blocks() * 16, e.st->status),
+           "attention front");
+    e.attn.cache = layer_cache;
+  }
+  std::string name() const override { return "AttentionFront (q/k/v, QK-norm, RoPE, KV store)"; }
+
+ private:
+  int l_;
+};
+
+// Split-KV flash decoding of the call's one-row segments (they come first in the call).
+class DecodeAttention final : public Module {
+ public:
+  void forward(Launch& e) const override {
+    e.attn.num_segments = static_cast<int>(e.plan.prefill > 0 ? e.plan.decode : e.plan.segments_padded);
+    e.done(foa::paged_decode(e.attn, e.s), "decode attention");
+    if (e.plan.max_keys > e.attn.keys_per_split) ++e.kernels;  // the split merge
+  }
+  std::string name() const override { return "DecodeAttention"; }
+};
+
+// Causal attention of the call's prompt chunks over their history and themselves.
+class PrefillAttention final : public Module {
+ public:
+  void forward(Launch& e) const override {
+    e.attn.num_segments = static_cast<int>(e.plan.decode + e.plan.prefill);
+    e.done(foa::paged_prefill(e.attn, e.op(e.sg.work), static_cast<int>(e.plan.work), e.s), "prefill attention");
+  }
+  std::string name() const override { return "PrefillAttention"; }
+};
+
+// A row-parallel projection whose output is added to the residual stream and normalised:
+// x += A W^T (one rounding), h = RMSNorm(x) * norm. One chip: the GEMM's residual epilogue and a
+// norm. Tensor parallelism: the GEMM writes its FP32 partial and the fused collective adds every
+// rank's partial in rank order with the residual and the norm.
+class ResidualProjection final : public Module {
+ public:
+  ResidualProjection(const char* trace_name, int l, std::string weight, int lora_module, std::string norm,
+                     bool input_is_attention)
+      : trace_(trace_name), l_(l), weight_(std::move(weight)), lora_(lora_module), norm_(std::move(norm)),
+        attention_(input_is_attention) {}
+  void forward(Launch& e) const override {
+    const void* a = attention_ ? e.m.ws_attn_.data() : e.m.ws_act_.data();
+    const int K = attention_ ? e.m.qh_l_ * e.D : e.m.inter_l_;
+    const int M = static_cast<int>(e.T);
+    if (!e.tp()) {
+      e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, e.x, e.H, foa::kEpiBf16, e.x, l_, lora_);
+      e.done(foa::rmsnorm(e.x, e.H, nullptr, 0, e.wp(norm_), e.h, e.H, nullptr, 0, M, e.H, e.cfg.eps, e.s),
+             "rmsnorm");
+      return;
     }
-    if (plan.prefill > 0) {
-      attn.num_segments = static_cast<int>(plan.decode + plan.prefill);
-      fail(foa::paged_prefill(attn, i32(stage, sg.work), static_cast<int>(plan.work), s),
-           "prefill attention");
-    }
-    const std::string next_norm =
-        l + 1 < cfg_.layers ? "layers." + std::to_string(l + 1) + ".in_norm" : "final_norm";
-    // Attention output projection, then the post-attention RMSNorm (fused with the cross-rank
-    // sum under tensor parallelism).
-    if (!tp) {
-      gemm_name = "gemm o";
-      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, x, H,
-           foa::kEpiBf16, x, l, LoraAdapter::kO);
-      fail(foa::rmsnorm(x, H, nullptr, 0, w(p + "post_norm"), h, H, nullptr, 0, static_cast<int>(T),
-                        H, cfg_.eps, s),
-           "rmsnorm");
-    } else {
-      const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
-      gemm_name = "gemm o (peer push)";
-      gemm(ws_attn_.data(), qh_l_ * D, ws(p + "o"), static_cast<int>(T), H, qh_l_ * D, nullptr, H,
-           foa::kEpiF32, nullptr, l, LoraAdapter::kO, &target);
-      coll_->add_norm(x, w(p + "post_norm"), cfg_.eps, h, static_cast<int>(T), H, s);
-      fail(0, "tp add_norm");
-    }
-    if (cfg_.experts > 0) {
-      // Mixture of experts (rows replicated on every rank; this rank's experts only): router,
-      // routing, grouping by expert, grouped gate/up + SwiGLU and down GEMMs, then the combine
-      // in choice order fused with the next RMSNorm (over NVLink under expert parallelism).
-      const int E = cfg_.experts, Kc = cfg_.top_k, I = cfg_.expert_intermediate;
-      const int tile = moe_tile(T);
-      const int64_t cap = moe_capacity(T);
-      gemm_name = "gemm router";
-      gemm(h, H, ws(p + "router"), static_cast<int>(T), E, H, ws_logits_e_.data(), E, foa::kEpiBf16, nullptr);
-      fail(foa::moe_route(bf(ws_logits_e_), E, static_cast<int>(T), E, Kc, cfg_.norm_topk, i32(ws_ids_),
-                          static_cast<float*>(ws_rw_.data()), s),
+    const foa::GemmPeerOut target = e.m.coll_->reduce_target(M, e.H);
+    e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, nullptr, e.H, foa::kEpiF32, nullptr, l_, lora_, &target);
+    e.m.coll_->add_norm(e.x, e.wp(norm_), e.cfg.eps, e.h, M, e.H, e.s);
+    e.done(0, "tp add_norm");
+  }
+  std::string name() const override {
+    return std::string("ResidualProjection ") + weight_ + " + norm " + norm_ + " (rank-ordered all-reduce under TP)";
+  }
+
+ private:
+  const char* trace_;
+  int l_;
+  std::string weight_;
+  int lora_;
+  std::string norm_;
+  bool attention_;
+};
+
+// gate/up projection of h with the SwiGLU epilogue (act = silu(gate) * up, the intermediate rows).
+class GateUp final : public Module {
+ public:
+  explicit GateUp(int l) : l_(l) {}
+  void forward(Launch& e) const override {
+    const int I = e.m.inter_l_;
+    e.gemm("gemm gate_up", e.h, e.H, e.w(layer_prefix(l_) + "gate_up"), static_cast<int>(e.T), 2 * I, e.H,
+           e.m.ws_act_.data(), I, foa::kEpiSwiGLU, nullptr, l_, LoraAdapter::kGateUp);
+  }
+  std::string name() const override { return "GateUp (SwiGLU epilogue)"; }
+
+ private:
+  int l_;
+};
+
+// Routed experts of layer l: router GEMM, top-k routing, grouping by expert, the grouped gate/up
+// (SwiGLU) and down GEMMs of this rank's experts, then the combine in choice order fused with the
+// residual add and the next norm (reading the peers' expert rows under expert parallelism).
+class Experts final : public Module {
+ public:
+  Experts(int l, std::string norm) : l_(l), norm_(std::move(norm)) {}
+  void forward(Launch& e) const override {
+    DecoderModel& m = e.m;
+    const std::string p = layer_prefix(l_);
+    const int E = e.cfg.experts, Kc = e.cfg.top_k, I = e.cfg.expert_intermediate, H = e.H;
+    const int T = static_cast<int>(e.T);
+    const int tile = m.moe_tile(e.T);
+    const int64_t cap = m.moe_capacity(e.T);
+    e.gemm("gemm router", e.h, H, e.w(p + "router"), T, E, H, m.ws_logits_e_.data(), E, foa::kEpiBf16, nullptr);
+    e.done(foa::moe_route(bf(m.ws_logits_e_), E, T, E, Kc, e.cfg.norm_topk, i32(m.ws_ids_),
+                          static_cast<float*>(m.ws_rw_.data()), e.s),
            "moe route");
-      fail(foa::moe_align_ranks(i32(ws_ids_), static_cast<int>(T), Kc, E, 0, experts_l_, tp_, rank_, tile,
-                                static_cast<int>(cap), i32(ws_pos_), i32(ws_src_), i32(ws_tile_e_),
-                                i32(ws_tiles_), s),
+    e.done(foa::moe_align_ranks(i32(m.ws_ids_), T, Kc, E, 0, m.experts_l_, m.tp_, m.rank_, tile, static_cast<int>(cap),
+                                i32(m.ws_pos_), i32(m.ws_src_), i32(m.ws_tile_e_), i32(m.ws_tiles_), e.s),
            "moe align");
-      fail(foa::moe_gather(h, H, i32(ws_src_), i32(ws_tiles_), tile, static_cast<int>(cap), H, bf(ws_xs_), s),
+    e.done(foa::moe_gather(e.h, H, i32(m.ws_src_), i32(m.ws_tiles_), tile, static_cast<int>(cap), H, bf(m.ws_xs_), e.s),
            "moe gather");
-      __nv_bfloat16* y = tp ? coll_->moe_rows(l & 1, static_cast<size_t>(cap)) : bf(ws_y_);
-      auto grouped = [&](const void* a, const WeightSlot& wt, int N, int Kd, void* c, int ldc, int epi) {
-        foa::GemmArgs g;
-        g.a = a;
-        g.lda = Kd;
-        g.w = wt.ptr;
-        g.ldw = Kd;
-        g.M = static_cast<int>(cap);
-        g.N = N;
-        g.K = Kd;
-        g.c = c;
-        g.ldc = ldc;
-        g.epilogue = epi;
-        g.mode = foa::kModeSwap;
-        g.status = st->status;
-        g.group_tiles = i32(ws_tiles_);
-        g.tile_group = i32(ws_tile_e_);
-        g.group_tile = tile;
-        g.groups = experts_l_;
-        fail(foa::gemm_bf16(g, s), "grouped gemm");
-      };
-      grouped(ws_xs_.data(), W.at(p + "experts_gate_up"), 2 * I, H, ws_eact_.data(), I, foa::kEpiSwiGLU);
-      grouped(ws_eact_.data(), W.at(p + "experts_down"), H, I, y, H, foa::kEpiBf16);
-      if (!tp) {
-        fail(foa::moe_combine_norm(y, H, i32(ws_pos_), static_cast<float*>(ws_rw_.data()), static_cast<int>(T),
-                                   Kc, H, x, H, w(next_norm), cfg_.eps, h, H, s),
+    __nv_bfloat16* y = e.tp() ? m.coll_->moe_rows(l_ & 1, static_cast<size_t>(cap)) : bf(m.ws_y_);
+    auto grouped = [&](const char* what, const void* a, const WeightSlot& wt, int N, int Kd, void* c, int ldc,
+                       int epi) {
+      foa::GemmArgs g;
+      g.a = a;
+      g.lda = Kd;
+      g.w = wt.ptr;
+      g.ldw = Kd;
+      g.M = static_cast<int>(cap);
+      g.N = N;
+      g.K = Kd;
+      g.c = c;
+      g.ldc = ldc;
+      g.epilogue = epi;
+      g.mode = foa::kModeSwap;
+      g.status = e.st->status;
+      g.group_tiles = i32(m.ws_tiles_);
+      g.tile_group = i32(m.ws_tile_e_);
+      g.group_tile = tile;
+      g.groups = m.experts_l_;
+      e.done(foa::gemm_bf16(g, e.s), what);
+    };
+    grouped("grouped gemm gate_up", m.ws_xs_.data(), e.w(p + "experts_gate_up"), 2 * I, H, m.ws_eact_.data(), I,
+            foa::kEpiSwiGLU);
+    grouped("grouped gemm down", m.ws_eact_.data(), e.w(p + "experts_down"), H, I, y, H, foa::kEpiBf16);
+    if (!e.tp()) {
+      e.done(foa::moe_combine_norm(y, H, i32(m.ws_pos_), static_cast<float*>(m.ws_rw_.data()), T, Kc, H, e.x, H,
+                                   e.wp(norm_), e.cfg.eps, e.h, H, e.s),
              "moe combine");
-      } else {
-        coll_->moe_combine_norm(l & 1, i32(ws_pos_), i32(ws_ids_), static_cast<float*>(ws_rw_.data()),
-                                experts_l_, w(next_norm), cfg_.eps, static_cast<int>(T), Kc, H, s);
-        fail(0, "tp moe combine");
-      }
-    } else if (!tp) {
-      gemm_name = "gemm gate_up";
-      gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
-           foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
-      gemm_name = "gemm down";
-      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, x, H,
-           foa::kEpiBf16, x, l, LoraAdapter::kDown);
-      fail(foa::rmsnorm(x, H, nullptr, 0, w(next_norm), h, H, nullptr, 0, static_cast<int>(T), H,
-                        cfg_.eps, s),
-           "rmsnorm");
     } else {
-      gemm_name = "gemm gate_up";
-      gemm(h, H, ws(p + "gate_up"), static_cast<int>(T), 2 * inter_l_, H, ws_act_.data(), inter_l_,
-           foa::kEpiSwiGLU, nullptr, l, LoraAdapter::kGateUp);
-      const foa::GemmPeerOut target = coll_->reduce_target(static_cast<int>(T), H);
-      gemm_name = "gemm down (peer push)";
-      gemm(ws_act_.data(), inter_l_, ws(p + "down"), static_cast<int>(T), H, inter_l_, nullptr, H,
-           foa::kEpiF32, nullptr, l, LoraAdapter::kDown, &target);
-      coll_->add_norm(x, w(next_norm), cfg_.eps, h, static_cast<int>(T), H, s);
-      fail(0, "tp add_norm");
+      m.coll_->moe_combine_norm(l_ & 1, i32(m.ws_pos_), i32(m.ws_ids_), static_cast<float*>(m.ws_rw_.data()),
+                                m.experts_l_, e.wp(norm_), e.cfg.eps, T, Kc, H, e.s);
+      e.done(0, "tp moe combine");
     }
   }
+  std::string name() const override { return "Experts (route, group, grouped SwiGLU GEMMs, combine + norm " + norm_ + ")"; }
 
-  const int K = static_cast<int>(std::max<int64_t>(plan.kept_padded, 0));
-  if (K == 0) return kernels;
-  fail(foa::gather_rows(h, H, i32(stage, sg.kept), K, bf(ws_hk_), H, H, s), "gather rows");
-  if (cfg_.output == Output::Hidden) return kernels;
-  if (cfg_.output == Output::Scores) {
-    gemm_name = "gemm score";
-    gemm(ws_hk_.data(), H, ws("score"), K, cfg_.labels, H, ws_logits_.data(), cfg_.labels,
-         foa::kEpiF32, nullptr);
-    return kernels;
+ private:
+  int l_;
+  std::string norm_;
+};
+
+// The kept rows' outputs: final-normed hidden rows, label scores, or the first-maximum token of
+// the vocabulary-parallel head (candidates exchanged across ranks under tensor parallelism).
+class Head final : public Module {
+ public:
+  explicit Head(Output output) : output_(output) {}
+  void forward(Launch& e) const override {
+    DecoderModel& m = e.m;
+    const int K = static_cast<int>(std::max<int64_t>(e.plan.kept_padded, 0));
+    if (K == 0) return;
+    e.done(foa::gather_rows(e.h, e.H, e.op(e.sg.kept), K, bf(m.ws_hk_), e.H, e.H, e.s), "gather rows");
+    if (output_ == Output::Hidden) return;
+    if (output_ == Output::Scores) {
+      e.gemm("gemm score", m.ws_hk_.data(), e.H, e.w("score"), K, e.cfg.labels, e.H, m.ws_logits_.data(),
+             e.cfg.labels, foa::kEpiF32, nullptr);
+      return;
+    }
+    e.gemm("gemm lm_head", m.ws_hk_.data(), e.H, e.w("lm_head"), K, m.vocab_l_, e.H, m.ws_logits_.data(), m.vocab_l_,
+           foa::kEpiF32, nullptr);
+    const int valid = m.vocab_end_ - m.vocab_begin_;
+    if (!e.tp()) {
+      e.done(foa::argmax_rows(static_cast<float*>(m.ws_logits_.data()), m.vocab_l_, K, m.vocab_l_, valid, 0,
+                              i32(m.ws_tokens_), nullptr, e.s),
+             "argmax");
+      return;
+    }
+    e.done(foa::argmax_rows(static_cast<float*>(m.ws_logits_.data()), m.vocab_l_, K, m.vocab_l_, valid,
+                            m.vocab_begin_, i32(m.ws_idx_), static_cast<float*>(m.ws_val_.data()), e.s),
+           "argmax");
+    m.coll_->argmax(static_cast<float*>(m.ws_val_.data()), i32(m.ws_idx_), K, i32(m.ws_tokens_), e.s);
+    e.done(0, "tp argmax");
   }
-  gemm_name = "gemm lm_head";
-  gemm(ws_hk_.data(), H, ws("lm_head"), K, vocab_l_, H, ws_logits_.data(), vocab_l_, foa::kEpiF32,
-       nullptr);
-  const int valid = vocab_end_ - vocab_begin_;
-  if (!tp) {
-    fail(foa::argmax_rows(static_cast<float*>(ws_logits_.data()), vocab_l_, K, vocab_l_, valid, 0,
-                          i32(ws_tokens_), nullptr, s),
-         "argmax");
-  } else {
-    fail(foa::argmax_rows(static_cast<float*>(ws_logits_.data()), vocab_l_, K, vocab_l_, valid,
-                          vocab_begin_, i32(ws_idx_), static_cast<float*>(ws_val_.data()), s),
-         "argmax");
-    coll_->argmax(static_cast<float*>(ws_val_.data()), i32(ws_idx_), K, i32(ws_tokens_), s);
-    fail(0, "tp argmax");
+  std::string name() const override {
+    return output_ == Output::Hidden ? "Head (hidden rows)"
+           : output_ == Output::Scores ? "Head (label scores)"
+                                       : "Head (vocabulary-parallel greedy token)";
   }
-  return kernels;
+
+ private:
+  Output output_;
+};
+
+  static ModulePtr build(const ModelConfig& cfg);
+};
+
+// The decoder families' launch program: embedding, then per layer the attention block (front,
+// decode and prefill attention as the call holds them, output projection + residual + norm) and
+// the feed-forward block (SwiGLU MLP, or routed experts), then the head.
+ModulePtr DecoderBlocks::build(const ModelConfig& cfg) {
+  auto prog = std::make_unique<Sequential>(cfg.family + " decoder");
+  prog->then(std::make_unique<Embed>());
+  prog->then(std::make_unique<Norm>("layers.0.in_norm"));
+  prog->then(std::make_unique<Layers>(cfg.layers, [&](int l) -> ModulePtr {
+    const std::string p = layer_prefix(l), next = next_norm(l, cfg.layers);
+    auto layer = std::make_unique<Sequential>("Layer");
+    auto attention = std::make_unique<Sequential>("Attention");
+    attention->then(std::make_unique<AttentionFront>(l));
+    attention->then(std::make_unique<Choice>(
+        "decode rows", [](const Launch& e) { return e.plan.decode > 0; }, std::make_unique<DecodeAttention>()));
+    attention->then(std::make_unique<Choice>(
+        "prompt chunks", [](const Launch& e) { return e.plan.prefill > 0; }, std::make_unique<PrefillAttention>()));
+    attention->then(std::make_unique<ResidualProjection>("gemm o", l, p + "o", LoraAdapter::kO, p + "post_norm", true));
+    layer->then(std::move(attention));
+    if (cfg.experts > 0) {
+      layer->then(std::make_unique<Experts>(l, next));
+    } else {
+      auto mlp = std::make_unique<Sequential>("MLP");
+      mlp->then(std::make_unique<GateUp>(l));
+      mlp->then(std::make_unique<ResidualProjection>("gemm down", l, p + "down", LoraAdapter::kDown, next, false));
+      layer->then(std::move(mlp));
+    }
+    return layer;
+  }));
+  prog->then(std::make_unique<Head>(cfg.output));
+  return prog;
+}
+
+int DecoderModel::launch(const Plan& plan, const Cache& cache) {
+  if (!program_) program_ = DecoderBlocks::build(cfg_);
+  Launch env(*this, plan, cache);
+  program_->forward(env);
+  return env.kernels;
+}
+
+std::string DecoderModel::describe() const {
+  std::string out;
+  if (program_) program_->describe(out, 0);
+  else DecoderBlocks::build(cfg_)->describe(out, 0);
+  return out;
 }
 
 }  // namespace foa::engine

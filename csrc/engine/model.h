@@ -111,6 +111,9 @@ struct WeightSlot {
 };
 
 class LoraAdapter;
+class Module;
+struct Launch;
+struct DecoderBlocks;
 
 class DecoderModel {
  public:
@@ -173,6 +176,8 @@ class DecoderModel {
   // replays count every kernel node).
   const Plan& last_plan() const { return last_plan_; }
   uint64_t kernel_launches() const { return launches_; }
+  // The launch program's module tree, one line a module.
+  std::string describe() const;
 
  private:
   void allocate_weights();
@@ -236,6 +241,10 @@ class DecoderModel {
   uint64_t launches_ = 0;
   void clear_graphs();
   Plan last_plan_;
+  // The launch program (modules.h), built at the first call from the configuration.
+  std::unique_ptr<Module> program_;
+  friend struct Launch;
+  friend struct DecoderBlocks;
 };
 
 }  // namespace foa::engine

@@ -561,6 +561,8 @@ void bind_engine(py::module_& m) {
       .def("set_graphs", [](PyDecoder& d, bool on) { d.model->set_graphs(on); })
       .def_property_readonly("weight_bytes", [](const PyDecoder& d) { return d.model->weight_bytes(); })
       .def_property_readonly("kernel_launches", [](const PyDecoder& d) { return d.model->kernel_launches(); })
+      .def_property_readonly("program", [](const PyDecoder& d) { return d.model->describe(); },
+                             "The decoder's launch program: its module tree, one line a module.")
       .def_property_readonly("last_staged_bytes", [](const PyDecoder& d) { return d.model->last_plan().staged.bytes; })
       .def("weight", [](const PyDecoder& d, const std::string& name) {
         const auto& w = d.model->weights().at(name);

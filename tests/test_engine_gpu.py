@@ -327,3 +327,14 @@ def test_mixtral_checkpoint_loads_strictly_and_matches_dense(tmp_path):
             pick = tokens[i][step]
             assert logits[pick] >= top[0] - 5e-2 * max(1.0, abs(top[0].item())), (i, step)
             seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
+
+
+def test_launch_program_is_a_module_tree():
+    """The decoder's launch program is composed of modules: per-layer attention and feed-forward
+    blocks under a Layers combinator, the experts block in place of the MLP for a MoE family."""
+    _, _, _, dense_model = _build()
+    tree = dense_model.program
+    assert tree.splitlines()[0] == "qwen3 decoder"
+    assert "Layers x2" in tree and "GateUp" in tree and "Choice decode rows" in tree and "Experts" not in tree
+    _, _, _, moe = _build("tiny-qwen3-moe")
+    assert "Experts" in moe.program and "GateUp" not in moe.program
