@@ -177,6 +177,7 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   a.peers = peers_;
   a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
   a.arrivals = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_arrivals_);
+  a.announced = reinterpret_cast<unsigned long long*>(static_cast<char*>(heap_) + off_arrivals_ + 8);
   a.seq = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_seq_);
   a.buf_stride = static_cast<long>(rows_) * cols_;
   a.weight = weight;

@@ -101,8 +101,10 @@ __global__ void __launch_bounds__(256) tp_reduce_norm_kernel(const ReduceNormArg
   const bool tracer = a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
   if (tracer) a.trace[0] = global_ns();
   if (threadIdx.x == 0) {
+    // The first CTA to arrive announces this rank (whichever CTAs the GPU schedules first), so
+    // the barrier never depends on one particular CTA being resident.
     const unsigned long long v = barrier_value(a.epoch, a.site, 0);
-    if (blockIdx.x == 0) signal_all(a.peers, a.rank, a.world, v);
+    if (atomicMax(a.announced, v) < v) signal_all(a.peers, a.rank, a.world, v);
     ok_s = wait_all(a.peers, a.rank, a.world, v, a.status);
   }
   __syncthreads();

@@ -27,6 +27,7 @@ struct ReduceNormArgs {
   PeerBuffers peers;
   const unsigned long long* epoch;  // this call's epoch (device memory, written per call)
   unsigned int* arrivals;           // this rank's CTA arrival counter (zero between calls)
+  unsigned long long* announced;    // the last barrier value this rank announced (starts at 0)
   unsigned int* seq;                // this rank's partial-buffer sequence
   long buf_stride;                  // floats between the two partial buffers
   const __nv_bfloat16* weight;
