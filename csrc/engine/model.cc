@@ -207,7 +207,9 @@ void DecoderModel::allocate_weights() {
     }
   }
   const std::string& wf = cfg_.weight_format;
-  const bool per_row = wf == "fp8_channel" || wf == "fp8_tensor";
+  // FP8 codes with one FP32 scale per weight row: quantized at load per channel or per tensor,
+  // or read from a static per-tensor FP8 checkpoint (each projection's scale on its rows).
+  const bool per_row = wf == "fp8_channel" || wf == "fp8_tensor" || wf == "fp8_static";
   const int format = wf == "fp8_block" ? foa::kWeightFp8A8
                      : per_row          ? foa::kWeightFp8Block
                      : wf == "nvfp4"   ? foa::kWeightNvfp4

@@ -174,6 +174,15 @@ ModelConfig llama_scope(const Checkpoint& ck, const std::string& family, const s
       invalid("config.json:quantization_config", "not a block-scaled FP8 declaration");
     m.precision = "float8_e4m3fn";
   }
+  if (form == "fp8_static") {
+    // Static per-tensor FP8 (Mistral NeMo FP8 and the like): E4M3 codes with one weight_scale a
+    // projection; the input_scale a static scheme calibrates is read and the inputs stay BF16.
+    const bool fp8 = q.is_object() && q["quant_method"].is_string() && q["quant_method"].as_string() == "fp8";
+    if (!fp8 || q["weight_block_size"].is_array() || !q["activation_scheme"].is_string() ||
+        q["activation_scheme"].as_string() != "static")
+      invalid("config.json:quantization_config", "not a static per-tensor FP8 declaration");
+    m.precision = "float8_e4m3fn";
+  }
   if (m.intermediate % 128 != 0) unsupported("intermediate_size", "not a multiple of 128");
   m.size = size_of(family, m);
   return m;
@@ -250,9 +259,15 @@ const std::map<std::string, std::vector<Implementation>>& served() {
              [](const Checkpoint& c) { return llama_scope(c, "llama", "nvfp4"); }),
         make("llama", "llama.ForCausalLM", "fp8_block", Output::Tokens,
              [](const Checkpoint& c) { return llama_scope(c, "llama", "fp8_block"); }),
+        make("llama", "llama.ForCausalLM", "fp8_static", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "llama", "fp8_static"); }),
     };
-    t["MistralForCausalLM"] = {make("mistral", "mistral.ForCausalLM", "bf16", Output::Tokens,
-                                    [](const Checkpoint& c) { return llama_scope(c, "mistral", "bf16"); })};
+    t["MistralForCausalLM"] = {
+        make("mistral", "mistral.ForCausalLM", "bf16", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "mistral", "bf16"); }),
+        make("mistral", "mistral.ForCausalLM", "fp8_static", Output::Tokens,
+             [](const Checkpoint& c) { return llama_scope(c, "mistral", "fp8_static"); }),
+    };
     t["Qwen3MoeForCausalLM"] = {make("qwen3_moe", "qwen3_moe.ForCausalLM", "bf16", Output::Tokens,
                                      [](const Checkpoint& c) { return qwen3_moe_scope(c); })};
     t["MixtralForCausalLM"] = {make("mixtral", "mixtral.ForCausalLM", "bf16", Output::Tokens,
@@ -383,6 +398,7 @@ Selection select(const LoadOptions& o, const Checkpoint& ck) {
     s.config.weight_format = *o.quantization == "fp8_per_tensor" ? "fp8_tensor" : "fp8_channel";
   }
   if (s.implementation->form == "fp8_block") s.config.weight_format = "fp8_block";
+  if (s.implementation->form == "fp8_static") s.config.weight_format = "fp8_static";
   if (s.implementation->form == "nvfp4") {
     // ModelOpt NVFP4 checkpoints with calibrated input scales run W4A4 on the block-scaled MMA;
     // without them (or with FOA_NVFP4_W4A16=1) the inputs stay BF16 (W4A16).
@@ -621,6 +637,27 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
   auto load_quantized = [&](const std::string& slot, const std::vector<Part>& parts, int64_t c0, int64_t nc) {
     WeightSlot& w = model.weight_slot(slot);
     const int64_t R = w.shape[0], C = w.shape[1];
+    if (w.format == foa::kWeightFp8Block && w.scale_rows == 1) {
+      // Static per-tensor FP8: each part's codes, and its weight_scale on every one of its rows.
+      std::vector<uint8_t> codes(static_cast<size_t>(R * C), 0);
+      std::vector<float> rows_scale(static_cast<size_t>(R), 0.f);
+      for (const Part& p : parts) {
+        const StoredTensor* wt = take(p.base + ".weight", {p.rows, p.cols});
+        if (wt && wt->dtype != StDType::F8_E4M3)
+          invalid(p.base + ".weight", std::string("codes of dtype ") + st_dtype_name(wt->dtype) + " are not F8_E4M3");
+        const float ws = scalar(p.base + ".weight_scale");
+        if (ck.get(p.base + ".input_scale")) scalar(p.base + ".input_scale");  // calibrated, inputs stay BF16
+        for (int64_t i = 0; i < p.n; ++i) {
+          const int64_t d = p.blocked ? p.dst[i / 128] + i % 128 : p.dst[0] + i;
+          if (wt) std::memcpy(codes.data() + d * C, wt->data() + (p.r0 + i) * p.cols + c0, C);
+          rows_scale[static_cast<size_t>(d)] = ws;
+        }
+      }
+      st->check_cuda(cudaMemcpy(w.codes, codes.data(), codes.size(), cudaMemcpyHostToDevice), "weight upload");
+      st->check_cuda(cudaMemcpy(w.scales, rows_scale.data(), rows_scale.size() * 4, cudaMemcpyHostToDevice),
+                     "weight upload");
+      return;
+    }
     const bool fp8 = w.format == foa::kWeightFp8A8;
     const int64_t code_bytes = fp8 ? C : C / 2;
     std::vector<uint8_t> codes(static_cast<size_t>(R * code_bytes), 0);
@@ -701,7 +738,7 @@ void load_weights(DecoderModel& model, const Checkpoint& ck) {
   };
   // Checkpoints that hold their own codes and scales (load-time FP8 reads BF16 and quantizes).
   const bool quantized = cfg.weight_format == "fp8_block" || cfg.weight_format == "nvfp4" ||
-                         cfg.weight_format == "nvfp4_a4";
+                         cfg.weight_format == "nvfp4_a4" || cfg.weight_format == "fp8_static";
 
   // Names under "model." (a causal or classifier checkpoint); a base model saved on its own
   // (sentence-embedding checkpoints) names its tensors from the root.

@@ -89,6 +89,17 @@ CONFIGS["llama-3.1-8b-fp8"] = dict(CONFIGS["llama-3.1-8b"], precision="float8_e4
 CONFIGS["llama-3.3-70b-nvfp4"] = dict(CONFIGS["llama-3.3-70b"], precision="uint8", weight_format="nvfp4_a4")
 CONFIGS["llama-3.1-8b-nvfp4"] = dict(CONFIGS["llama-3.1-8b"], precision="uint8", weight_format="nvfp4_a4")
 CONFIGS["qwen3-8b-fp8"] = dict(CONFIGS["qwen3-8b"], precision="float8_e4m3fn", weight_format="fp8_block")
+# Mistral NeMo 12B (head_dim 128 below hidden / heads) and its static per-tensor FP8 checkpoint.
+CONFIGS["mistral-nemo-12b"] = dict(
+    architecture="MistralForCausalLM", family="mistral", size="12B", hidden=5120, intermediate=14336, layers=40,
+    q_heads=32, kv_heads=8, head_dim=128, vocab=131072, eps=1e-5, qk_norm=False, tied=False,
+    rope={"type": "default", "theta": 1_000_000.0}, window=131072, rows=8192)
+CONFIGS["mistral-nemo-12b-fp8"] = dict(CONFIGS["mistral-nemo-12b"], precision="float8_e4m3fn",
+                                       weight_format="fp8_static")
+CONFIGS["tiny-mistral"] = dict(
+    architecture="MistralForCausalLM", family="mistral", size="tiny", hidden=256, intermediate=768, layers=2,
+    q_heads=4, kv_heads=2, head_dim=64, vocab=1024, eps=1e-5, qk_norm=False, tied=False,
+    rope={"type": "default", "theta": 1_000_000.0}, window=4096, rows=8192)
 
 
 def get(name: str, **overrides) -> dict:

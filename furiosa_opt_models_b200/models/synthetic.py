@@ -304,6 +304,40 @@ def hf_shapes(cfg: dict) -> dict[str, tuple[int, ...]]:
     return out
 
 
+# The quantization declaration of a static per-tensor FP8 checkpoint (Mistral NeMo FP8 style).
+STATIC_FP8 = {"quant_method": "fp8", "activation_scheme": "static"}
+
+
+def quantize_static_fp8(hf: dict[str, torch.Tensor], amax_in: float = 4.0) -> dict[str, torch.Tensor]:
+    """HF-named BF16 weights as a static per-tensor FP8 checkpoint: each projection's E4M3 codes
+    of w / weight_scale (weight_scale = amax / 448), its FP32 weight_scale and a calibrated
+    input_scale (`amax_in` / 448); other tensors unchanged."""
+    out = {}
+    for name, w in hf.items():
+        if not name.endswith("_proj.weight"):
+            out[name] = w
+            continue
+        base = name[: -len(".weight")]
+        scale = max(float(w.float().abs().max()), 1e-12) / 448.0
+        out[name] = (w.float() / scale).to(torch.float8_e4m3fn)
+        out[base + ".weight_scale"] = torch.tensor(scale, dtype=torch.float32)
+        out[base + ".input_scale"] = torch.tensor(amax_in / 448.0, dtype=torch.float32)
+    return out
+
+
+def dequantize_static_fp8(q: dict[str, torch.Tensor]) -> dict[str, torch.Tensor]:
+    """The BF16 weights a static FP8 checkpoint restores: bf16(code * weight_scale)."""
+    out = {}
+    for name, t in q.items():
+        if name.endswith(".weight_scale") or name.endswith(".input_scale"):
+            continue
+        if t.dtype == torch.float8_e4m3fn:
+            out[name] = (t.float() * q[name[: -len(".weight")] + ".weight_scale"]).bfloat16()
+        else:
+            out[name] = t
+    return out
+
+
 def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
     """A checkpoint of the geometry's full size that holds only headers: config.json and a
     safetensors file whose header declares every tensor (offsets as if the data followed) but
@@ -323,6 +357,8 @@ def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
                                        "weight_block_size": [128, 128]}
     elif fmt in ("nvfp4", "nvfp4_a4"):
         conf["quantization_config"] = {"quant_method": "modelopt", "quant_algo": "NVFP4", "group_size": 16}
+    elif fmt == "fp8_static":
+        conf["quantization_config"] = STATIC_FP8
     with open(os.path.join(directory, "config.json"), "w") as f:
         json.dump(conf, f)
     shapes = dict(hf_shapes(cfg))
@@ -336,6 +372,10 @@ def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
                 dtypes[name] = "F8_E4M3"
                 shapes[base + ".weight_scale_inv"] = (-(-R // 128), -(-C // 128))
                 dtypes[base + ".weight_scale_inv"] = "F32"
+            elif fmt == "fp8_static":
+                dtypes[name] = "F8_E4M3"
+                for s in ("weight_scale", "input_scale"):
+                    shapes[f"{base}.{s}"], dtypes[f"{base}.{s}"] = (), "F32"
             else:
                 shapes[name], dtypes[name] = (R, C // 2), "U8"
                 shapes[base + ".weight_scale"], dtypes[base + ".weight_scale"] = (R, C // 16), "F8_E4M3"

@@ -37,6 +37,7 @@ def test_full_size_checkpoints_select_from_headers(tmp_path, name, cls, size):
     ("llama-3.1-8b-fp8", "8B", "float8_e4m3fn"),
     ("qwen3-8b-fp8", "8B", "float8_e4m3fn"),
     ("llama-3.3-70b-nvfp4", "70B", "uint8"),
+    ("mistral-nemo-12b-fp8", "12B", "float8_e4m3fn"),
 ])
 def test_quantized_full_size_checkpoints_select_their_format(tmp_path, name, size, precision):
     """The BASELINE-shaped quantized checkpoints (block-FP8 8B, NVFP4 70B), declared in their

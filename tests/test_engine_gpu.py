@@ -338,3 +338,50 @@ def test_launch_program_is_a_module_tree():
     assert "Layers x2" in tree and "GateUp" in tree and "Choice decode rows" in tree and "Experts" not in tree
     _, _, _, moe = _build("tiny-qwen3-moe")
     assert "Experts" in moe.program and "GateUp" not in moe.program
+
+
+def test_static_fp8_checkpoint_matches_its_restored_weights(tmp_path):
+    """A static per-tensor FP8 checkpoint (Mistral NeMo FP8 style: E4M3 codes, one weight_scale
+    and one input_scale a projection) loads as mistral.ForCausalLM with FP8 precision and decodes
+    the dense forward's greedy tokens of the restored weights bf16(code * weight_scale)."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200 import serving
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-mistral")
+    hf = synthetic.hf_weights(cfg, seed=9, std=0.05)
+    q = synthetic.quantize_static_fp8(hf)
+    d = str(tmp_path / "m")
+    os.makedirs(d)
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(dict(synthetic.hf_config(cfg), quantization_config=synthetic.STATIC_FP8), f)
+    save_file(q, os.path.join(d, "model.safetensors"))
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, synthetic.dequantize_static_fp8(q)).items()}
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine.LoadOptions().load(engine.Checkpoint(d), device)
+    assert isinstance(model, engine.mistral.ForCausalLM) and model.precision == "float8_e4m3fn"
+    gen = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen, dtype=torch.int32) for n in (9, 40)]
+    cache = dec.Cache(model.cache, 16)
+    alloc = serving.BlockAllocator(16)
+    seqs = [serving.Sequence(engine.HostTensor.from_dlpack(p).to_hbm(device), len(p), alloc.take(5)) for p in prompts]
+    out = serving.prefill(model, cache, seqs, [0, 1])
+    tokens = [[t] for t in out.to_host().numpy().tolist()]
+    for _ in range(4):
+        out = serving.decode(model, cache, seqs)
+        for i, t in enumerate(out.to_host().numpy().tolist()):
+            tokens[i].append(t)
+    for i, p in enumerate(prompts):
+        seq = p.clone()
+        for step in range(5):
+            logits = dense.forward(w, cfg, seq)[-1]
+            top = torch.topk(logits, 2).values
+            pick = tokens[i][step]
+            assert logits[pick] >= top[0] - 1e-2 * max(1.0, abs(top[0].item())), (i, step)
+            seq = torch.cat([seq, torch.tensor([pick], dtype=torch.int32)])
