@@ -43,6 +43,37 @@ def test_vllm_generates_through_the_engine(tmp_path):
         assert json.load(f) is True
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_vllm_tensor_parallel_matches_the_dense_forward(tmp_path):
+    """The parallelism contract through vLLM: the same checkpoint served at tensor_parallel_size 2
+    (vLLM's multiprocess executor, one engine rank a worker) gives greedy tokens that are the dense
+    forward's argmax at every step (within BF16 near-ties), as at TP=1."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3-tp")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=13, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    gen = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (5, 30)]
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", NCCL_NVLS_ENABLE="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    runs = {}
+    for tp in (1, 2):
+        out = str(tmp_path / f"tp{tp}.json")
+        subprocess.run(["timeout", "-k", "30", "600", sys.executable, WORKER, str(tmp_path / "m"), out,
+                        json.dumps(prompts), str(tp)], check=True, env=env, cwd=ROOT)
+        with open(out) as f:
+            runs[tp] = json.load(f)
+    for tp, tokens in runs.items():
+        for p, toks in zip(prompts, tokens):
+            seq = torch.tensor(p, dtype=torch.int32)
+            for t in toks:
+                logits = dense.forward(w, cfg, seq)[-1]
+                assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item())), tp
+                seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+
+
 def test_vllm_sleep_mode_frees_and_restores(tmp_path):
     """vLLM's sleep mode through the plugin: level 1 keeps the host copy, level 2 reads the files,
     reload_weights loads them again; the continuations are the same each time, and sleeping

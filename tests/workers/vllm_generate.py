@@ -15,9 +15,10 @@ def main() -> None:
     from vllm.inputs import TokensPrompt
 
     path, out, prompts = sys.argv[1], sys.argv[2], json.loads(sys.argv[3])
+    tp = int(sys.argv[4]) if len(sys.argv) > 4 else 1
     llm = LLM(model=path, skip_tokenizer_init=True, gpu_memory_utilization=0.3, max_model_len=1024,
               max_num_seqs=8, max_num_batched_tokens=1024, enforce_eager=True, dtype="bfloat16",
-              num_gpu_blocks_override=256, enable_prefix_caching=False)
+              num_gpu_blocks_override=256, enable_prefix_caching=False, tensor_parallel_size=tp)
     params = SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True, detokenize=False)
     outs = llm.generate([TokensPrompt(prompt_token_ids=p) for p in prompts], params)
     with open(out, "w") as f:
