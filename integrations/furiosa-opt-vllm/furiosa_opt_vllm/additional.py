@@ -4,8 +4,8 @@ the same strict parsing, with this engine's options).
 
 - `cuda_graphs` (default true): decode calls replay CUDA graphs the engine captured per call
   shape; false runs every call eagerly (for profiling).
-- `draft_placement` (the reference's chips for a draft model): draft models are not served, so
-  setting it is refused.
+- `draft_placement` (the reference's chips for a draft model): a draft model runs beside the
+  target on the worker's GPU, so another placement is refused.
 """
 
 from __future__ import annotations
@@ -61,5 +61,6 @@ class Section(BaseModel):
             path = ".".join(map(str, ("additional_config", "furiosa", *d["loc"])))
             raise Refused(path, d["msg"]) from None
         if section.draft_placement is not None:
-            raise Refused("additional_config.furiosa.draft_placement", "draft models are not served")
+            raise Refused("additional_config.furiosa.draft_placement",
+                          "a draft model runs beside the target on the worker's GPU")
         return section

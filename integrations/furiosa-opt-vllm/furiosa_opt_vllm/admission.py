@@ -28,7 +28,7 @@ class Refused(ValueError):
 CHIPS = (1, 2, 4, 8)
 
 # Speculative methods served: drafts the target verifies greedily (furiosa_opt_vllm.speculation).
-SPECULATIVE_METHODS = ("ngram",)
+SPECULATIVE_METHODS = ("ngram", "draft_model")
 
 # The engine's adapter slots a call holds and the rank every update holds (decoder.AdapterSpec).
 LORA_SLOTS = 2
@@ -100,7 +100,10 @@ CONTRACTS: tuple[Contract, ...] = (
              "communication inside its kernels"),
     # Speculation: n-gram drafts verified greedily.
     Contract("speculative_config", lambda v, _c: v is None or str(getattr(v, "method", None)) in SPECULATIVE_METHODS,
-             "drafts come from n-gram prompt lookup (method 'ngram'); draft models are not served"),
+             "drafts come from n-gram prompt lookup (method 'ngram') or a draft model (method 'draft_model')"),
+    Contract("speculative_config", lambda v, cfg: v is None or str(getattr(v, "method", None)) != "draft_model"
+             or _tensor(cfg) == 1, "a draft model runs beside the target on one GPU a replica",
+             refuse_as="speculative_config.method"),
     # LoRA: the engine's two slots, rank 32, one GPU a replica.
     Contract("lora_config.max_loras", _at_most(LORA_SLOTS), f"an engine call holds {LORA_SLOTS} adapters"),
     Contract("lora_config.max_lora_rank", _at_most(LORA_RANK), f"the engine serves ranks up to {LORA_RANK}"),

@@ -81,7 +81,12 @@ class Worker(WorkerBase):
 
         if not Section.parse(self.vllm_config).cuda_graphs:
             self.model.set_graphs(False)
-        if self.vllm_config.speculative_config is not None:
+        sc = self.vllm_config.speculative_config
+        if sc is not None and str(sc.method) == "draft_model":
+            # The draft decoder beside the target on this worker's GPU.
+            self.proposer = speculation.DraftModel(
+                self.vllm_config, lambda path: load.load_from(load.checkpoint(path), self.device, 1))
+        elif sc is not None:
             self.proposer = speculation.Proposer(self.vllm_config)
         if self.lora_config is not None:
             self.adapters = lora.Adapters(self.lora_config.max_loras, self.lora_config.max_cpu_loras,
@@ -113,7 +118,13 @@ class Worker(WorkerBase):
         budget = int(total * self.cache_config.gpu_memory_utilization) - (total - free)
         # The engine addresses each layer's cache with 32-bit byte offsets.
         layers = len(self.model.cache.groups[0].layers)
-        return max(min(budget, layers * ((1 << 31) - (1 << 20))), 0)
+        budget = max(min(budget, layers * ((1 << 31) - (1 << 20))), 0)
+        if isinstance(self.proposer, speculation.DraftModel):
+            # vLLM sizes the target's blocks; the draft's cache takes as many blocks of its own size.
+            page = int(self.model.cache.pools[0].bytes) * layers
+            draft = self.proposer.page_bytes() * len(self.proposer.model.cache.groups[0].layers)
+            budget = budget * page // (page + draft)
+        return budget
 
     def get_kv_cache_spec(self):
         return kv.spec(self.model, self.model_config)
@@ -123,6 +134,8 @@ class Worker(WorkerBase):
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
         self.runner = Runner(self.model, self.device, self.cache, self.adapters, self.pooling_config())
+        if self.proposer is not None:
+            self.proposer.attach(self.runner, int(kv_cache_config.num_blocks))
 
     # ------------------------------------------------------------------------ LoRA
     def add_lora(self, lora_request) -> bool:
@@ -207,8 +220,7 @@ class Worker(WorkerBase):
         if self.proposer is not None:
             from vllm.v1.outputs import DraftTokenIds
 
-            histories = [self.runner.states[r].tokens for r in ids]
-            self.drafts = DraftTokenIds(ids, self.proposer.propose(sampled, histories))
+            self.drafts = DraftTokenIds(ids, self.proposer.propose(ids, sampled, self.runner))
         return None
 
     def asynchronous(self) -> bool:

@@ -244,7 +244,7 @@ def test_additional_config_section():
     with pytest.raises(admission.Refused) as e:
         Section.parse(SimpleNamespace(additional_config={"furiosa": {"cuda_graphs": "yes"}}))
     assert e.value.option == "additional_config.furiosa.cuda_graphs"
-    with pytest.raises(admission.Refused, match="draft models are not served"):
+    with pytest.raises(admission.Refused, match="beside the target"):
         Section.parse(SimpleNamespace(additional_config={"furiosa": {"draft_placement": {"chips": [1]}}}))
     with pytest.raises(admission.Refused) as e:
         Section.parse(SimpleNamespace(additional_config={"furiosa": {"draft_placement": {"chips": [1, 1]}}}))

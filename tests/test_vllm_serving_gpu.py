@@ -161,6 +161,36 @@ def test_vllm_ngram_speculation_is_exact(tmp_path):
         assert drafts > 0
 
 
+def test_vllm_draft_model_speculation_is_exact(tmp_path):
+    """Draft-model speculative decoding through the plugin: a smaller decoder of the same vocabulary
+    (one layer, other weights) drafts beside the target; the target's greedy verification keeps the
+    continuations equal to the dense forward of the target's weights."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=13, std=0.05)
+    synthetic.write(str(tmp_path / "d"), configs.get("tiny-qwen3", layers=1), seed=14, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    gen = torch.Generator().manual_seed(7)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (9, 23)]
+    out = str(tmp_path / "draft.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable,
+                    os.path.join(ROOT, "tests", "workers", "vllm_speculate.py"), str(tmp_path / "m"), out,
+                    json.dumps(prompts), str(tmp_path / "d")], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        got = json.load(f)
+    assert [len(t) for t in got["tokens"]] == [24, 24]
+    for p, toks in zip(prompts, got["tokens"]):
+        seq = torch.tensor(p, dtype=torch.int32)
+        for t in toks:
+            logits = dense.forward(w, cfg, seq)[-1]
+            assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+            seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+
+
 @pytest.mark.parametrize("mode", ["embed", "classify"])
 def test_vllm_pooling_through_the_engine(tmp_path, mode):
     """vLLM's pooling runner through the plugin: `embed` on a causal checkpoint served as its base

@@ -21,9 +21,12 @@ def test_accept():
         speculation.accept([1, 2], [1, 2])
 
 
-def test_admission_serves_ngram_only():
+def test_admission_serves_ngram_and_draft_models():
     admission.options(pipeline=1, tensor=1, speculative="ngram", lora=False, kv_cache_dtype="auto")
-    for method in ("eagle", "draft_model", "mtp", "suffix"):
+    admission.options(pipeline=1, tensor=1, speculative="draft_model", lora=False, kv_cache_dtype="auto")
+    with pytest.raises(admission.Refused, match="one GPU a replica"):
+        admission.options(pipeline=1, tensor=2, speculative="draft_model", lora=False, kv_cache_dtype="auto")
+    for method in ("eagle", "mtp", "suffix"):
         with pytest.raises(admission.Refused, match="n-gram prompt lookup"):
             admission.options(pipeline=1, tensor=1, speculative=method, lora=False, kv_cache_dtype="auto")
 
@@ -139,3 +142,57 @@ def test_drafts_after_a_stale_history_are_refused():
     r.step(sched(new=[new], counts={"a": 2}))  # a prompt chunk: nothing sampled
     with pytest.raises(ValueError, match="drafts scheduled before the newest token"):
         r.step(sched(cached=[("a", 1)], counts={"a": 2}, spec={"a": [5]}))
+
+
+def test_draft_model_feeds_only_what_changed_and_output_stays_greedy():
+    """The draft model's proposer on a host fake: its first call feeds the prompt, later calls feed
+    the accepted tokens from the first difference with what it fed, each further draft one row;
+    with the target verifying, the output is exactly the greedy continuation."""
+    r, target = make_runner()
+    draft_calls = []
+
+    class FakeDraft(FakeModel):
+        """Agrees with the target except after token 7 (so some drafts are rejected)."""
+
+        cache = SimpleNamespace(pools=[SimpleNamespace(bytes=64)], groups=[SimpleNamespace(layers=[0])])
+
+        def forward(self, reqs, cache, adapters=None):
+            draft_calls.append([(q.cached, q.tokens.a.tolist()) for q in reqs])
+            out = []
+            for q in reqs:
+                t = q.tokens.a.tolist()[-1]
+                out.append((nxt(t) + (1 if t == 7 else 0)) % 50)
+            return FakeTensor(out)
+
+    r.dec.Cache = lambda spec, n: ("draft cache", n)
+    cfg = SimpleNamespace(speculative_config=SimpleNamespace(num_speculative_tokens=3, model="draft"))
+    prop = speculation.DraftModel(cfg, lambda path: FakeDraft(r.dec.Keep))
+    prop.attach(r, 64)
+    prompt = [3, 11, 4]
+    new = SimpleNamespace(req_id="a", prompt_token_ids=prompt, num_computed_tokens=0, block_ids=([0, 1],),
+                          lora_request=None)
+    ids, out = r.step(sched(new=[new], counts={"a": 3}))
+    drafts = prop.propose(ids, out, r)
+    # The whole prompt and the first sampled token, then one row a further draft.
+    assert draft_calls[0] == [(0, prompt + out[0])]
+    assert [c[0][0] for c in draft_calls[1:]] == [4, 5]
+    produced, computed = list(out[0]), 3
+    greedy, t = [], prompt[-1]
+    for _ in range(20):
+        t = nxt(t)
+        greedy.append(t)
+    while len(produced) < 12:
+        d = drafts[0]
+        n = 1 + len(d)
+        before = len(draft_calls)
+        ids, out = r.step(sched(cached=[("a", computed)], counts={"a": n}, spec={"a": d}))
+        got = out[0]
+        assert got == greedy[len(produced):len(produced) + len(got)]
+        computed += n - (len(d) - (len(got) - 1))
+        produced += got
+        drafts = prop.propose(ids, out, r)
+        # The first draft call starts at the first token the draft has not fed as known.
+        first = draft_calls[before][0]
+        assert first[0] <= len(r.states["a"].tokens) - 1
+        assert first[1] == r.states["a"].tokens[first[0]:]
+    assert produced == greedy[:len(produced)]

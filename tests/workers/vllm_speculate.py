@@ -1,5 +1,6 @@
-"""Worker of the vLLM speculative-decoding test: vLLM's LLM with n-gram speculation through the
-plugin; writes the greedy continuations and vLLM's draft counters to a JSON file."""
+"""Worker of the vLLM speculative-decoding tests: vLLM's LLM with n-gram speculation, or with a
+draft model (its checkpoint the fourth argument), through the plugin; writes the greedy
+continuations and vLLM's draft counters to a JSON file."""
 
 import json
 import os
@@ -15,11 +16,13 @@ def main() -> None:
     from vllm.inputs import TokensPrompt
 
     path, out, prompts = sys.argv[1], sys.argv[2], json.loads(sys.argv[3])
+    draft = sys.argv[4] if len(sys.argv) > 4 else None
+    spec = ({"method": "draft_model", "model": draft, "num_speculative_tokens": 3} if draft else
+            {"method": "ngram", "num_speculative_tokens": 3, "prompt_lookup_max": 3, "prompt_lookup_min": 1})
     llm = LLM(model=path, skip_tokenizer_init=True, gpu_memory_utilization=0.3, max_model_len=1024,
               max_num_seqs=8, max_num_batched_tokens=1024, enforce_eager=True, dtype="bfloat16",
               num_gpu_blocks_override=256, enable_prefix_caching=False, disable_log_stats=False,
-              speculative_config={"method": "ngram", "num_speculative_tokens": 3,
-                                  "prompt_lookup_max": 3, "prompt_lookup_min": 1})
+              speculative_config=spec)
     params = SamplingParams(temperature=0.0, max_tokens=24, ignore_eos=True, detokenize=False)
     outs = llm.generate([TokensPrompt(prompt_token_ids=p) for p in prompts], params)
     counters = {}
