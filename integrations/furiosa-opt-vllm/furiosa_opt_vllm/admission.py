@@ -129,8 +129,12 @@ CONTRACTS: tuple[Contract, ...] = (
     Contract("model_config.enable_return_routed_experts", _unset, "routing stays on the device"),
     Contract("model_config.override_attention_dtype", _unset, "attention runs in BF16"),
     Contract("load_config.load_format", _is("auto", "safetensors"), "the engine loads safetensors checkpoints"),
-    # Transfers the engine does not take part in.
+    # Transfers: KV offloading to host memory through the plugin's connector, nothing else.
     Contract("ec_transfer_config", lambda v, _c: v is None, "encoder caches are not exchanged"),
+    Contract("kv_transfer_config.kv_connector", lambda v, _c: v in (None, "FuriosaOffloadingConnector"),
+             "KV caches move only to host memory, through FuriosaOffloadingConnector"),
+    Contract("kv_transfer_config.kv_load_failure_policy", _is("fail", None),
+             "a failed load from host memory fails its requests (the offloaded memory is poisoned)"),
 )
 
 

@@ -23,11 +23,14 @@ class Collected(AsyncModelRunnerOutput):
 
     def __init__(self, pending):
         self.pending = pending
+        self.output = ModelRunnerOutput(req_ids=[], req_id_to_index={})  # filled by get_output
 
     def get_output(self) -> ModelRunnerOutput:
         ids, sampled = self.pending.collect()
-        return ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
-                                 sampled_token_ids=sampled)
+        self.output.req_ids = ids
+        self.output.req_id_to_index = {r: i for i, r in enumerate(ids)}
+        self.output.sampled_token_ids = sampled
+        return self.output
 
 
 class Worker(WorkerBase):
@@ -136,6 +139,15 @@ class Worker(WorkerBase):
         self.runner = Runner(self.model, self.device, self.cache, self.adapters, self.pooling_config())
         if self.proposer is not None:
             self.proposer.attach(self.runner, int(kv_cache_config.num_blocks))
+        if self.vllm_config.kv_transfer_config is not None:
+            # KV offloading: vLLM's connector over the engine's cache pages.
+            from vllm.distributed.kv_transfer import ensure_kv_transfer_initialized, get_kv_transfer_group
+
+            from . import offload
+
+            offload.attach(self.cache)
+            ensure_kv_transfer_initialized(self.vllm_config, kv_cache_config)
+            get_kv_transfer_group().register_kv_caches({})
 
     # ------------------------------------------------------------------------ LoRA
     def add_lora(self, lora_request) -> bool:
@@ -204,15 +216,49 @@ class Worker(WorkerBase):
         self.model = self.runner = self.cache = None
 
     # ------------------------------------------------------------------------ steps
+    def connector(self):
+        """vLLM's KV connector of this worker (KV offloading), or None."""
+        if self.vllm_config.kv_transfer_config is None:
+            return None
+        from vllm.distributed.kv_transfer import get_kv_transfer_group, has_kv_transfer_group
+
+        return get_kv_transfer_group() if has_kv_transfer_group() else None
+
     def execute_model(self, scheduler_output):
+        conn = self.connector()
+        meta = getattr(scheduler_output, "kv_connector_metadata", None)
+        if conn is not None and meta is not None:
+            # Loads from host memory go on the engine's stream ahead of this step's calls.
+            conn.handle_preemptions(meta)
+            conn.bind_connector_metadata(meta)
+            conn.start_load_kv(None)
+        try:
+            self._run(scheduler_output)
+        finally:
+            if conn is not None and meta is not None:
+                # Stores of the blocks this step filled follow its calls on the same stream.
+                from vllm.v1.outputs import KVConnectorOutput
+
+                conn.wait_for_save()
+                sending, recving = conn.get_finished(scheduler_output.finished_req_ids)
+                kvo = KVConnectorOutput(finished_sending=sending, finished_recving=recving,
+                                        kv_connector_stats=conn.get_kv_connector_stats(),
+                                        kv_connector_worker_meta=conn.build_connector_worker_meta())
+                conn.clear_connector_metadata()
+                target = self.pending.output if isinstance(self.pending, Collected) else self.pending
+                if target is not None:
+                    target.kv_connector_output = kvo
+        return None
+
+    def _run(self, scheduler_output) -> None:
         if scheduler_output.total_num_scheduled_tokens == 0:
             self.runner.update(scheduler_output)
             self.pending = ModelRunnerOutput(req_ids=[], req_id_to_index={})
-            return None
+            return
         if self.asynchronous():
             # The tokens stay on the device; vLLM collects them after it has issued the next step.
             self.pending = Collected(self.runner.step(scheduler_output, collect=False))
-            return None
+            return
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
                                          sampled_token_ids=sampled,
@@ -221,7 +267,6 @@ class Worker(WorkerBase):
             from vllm.v1.outputs import DraftTokenIds
 
             self.drafts = DraftTokenIds(ids, self.proposer.propose(ids, sampled, self.runner))
-        return None
 
     def asynchronous(self) -> bool:
         """Greedy steps under vLLM's async scheduling: no pooling, no drafts to propose."""

@@ -283,7 +283,7 @@ def test_every_contract_names_an_option_of_this_vllm():
                 fields.setdefault(node.name, set()).update(names)
     classes = {"parallel_config": "ParallelConfig", "cache_config": "CacheConfig", "model_config": "ModelConfig",
                "load_config": "LoadConfig", "lora_config": "LoRAConfig", "scheduler_config": "SchedulerConfig",
-               "offload_config": "OffloadConfig"}
+               "offload_config": "OffloadConfig", "kv_transfer_config": "KVTransferConfig"}
     for c in admission.CONTRACTS:
         head, _, rest = c.path.partition(".")
         assert head in fields["VllmConfig"], c.path
@@ -315,3 +315,72 @@ def test_contract_table_refuses_each_option(path, bad, option):
     with pytest.raises(admission.Refused) as e:
         admission.check(cfg)
     assert e.value.option == option
+
+
+class _Transfer:
+    def __init__(self, fn, fail=False):
+        self.fn, self.fail, self.ran = fn, fail, False
+
+    def done(self):
+        return True
+
+    def wait(self):
+        if not self.ran:
+            self.ran = True
+            self.fn()
+        if self.fail:
+            raise RuntimeError("copy failed")
+
+
+class _Buf:
+    """A byte range of a bytearray standing for a device or pinned host buffer."""
+
+    def __init__(self, data, off=0, n=None, fail=None):
+        self.data, self.off, self.n, self.fail = data, off, len(data) - off if n is None else n, fail
+
+    def slice(self, off, n):
+        return _Buf(self.data, self.off + off, n, self.fail)
+
+    def _to(self, other):
+        def run():
+            other.data[other.off : other.off + self.n] = self.data[self.off : self.off + self.n]
+        return _Transfer(run, fail=self.fail is not None and self.fail())
+
+    to_host = _to
+    to_hbm = _to
+
+
+def test_offload_pages_round_trip_and_poison_on_failure():
+    """The KV offload handlers copy whole engine pages of every layer to host slots and back; a
+    failed copy fails its job only once all its copies ended, and poisons later jobs."""
+    from types import SimpleNamespace
+
+    from furiosa_opt_vllm import offload
+
+    page, layers, blocks = 8, 2, 4
+    dev = [bytearray(bytes(range(l * 100, l * 100 + blocks * page))) for l in range(layers)]
+    cache = SimpleNamespace(layers=[_Buf(d) for d in dev])
+    host = bytearray(blocks * layers * page)
+    pool = SimpleNamespace(page=page, layers=layers, poisoned=False,
+                           slot=lambda b, l: _Buf(host, (b * layers + l) * page, page))
+    store, load = offload.PageCopies(cache, pool, True), offload.PageCopies(cache, pool, False)
+    ids = lambda *b: SimpleNamespace(block_ids=list(b))  # noqa: E731
+    assert store.transfer_async(1, (ids(2, 0), ids(0, 3)))
+    [r] = store.get_finished()
+    assert (r.job_id, r.success, r.transfer_size) == (1, True, 2 * layers * page)
+    want = [bytes(dev[l][2 * page : 3 * page]) for l in range(layers)]
+    for l in range(layers):
+        dev[l][2 * page : 3 * page] = bytes(page)  # the device block is reused
+    assert load.transfer_async(2, (ids(0), ids(2)))
+    load.wait({2})
+    assert [bytes(dev[l][2 * page : 3 * page]) for l in range(layers)] == want
+    assert [r.job_id for r in load.get_finished()] == [2]
+    # A failing copy: the job fails after every copy ran, and the memory is poisoned afterwards.
+    bad = SimpleNamespace(layers=[_Buf(d, fail=lambda: True) for d in dev])
+    failing = offload.PageCopies(bad, pool, True)
+    failing.transfer_async(3, (ids(1), ids(1)))
+    with pytest.raises(RuntimeError, match="poisoned"):
+        failing.wait({3})
+    assert failing.get_finished()[0].success is False and pool.poisoned
+    store.transfer_async(4, (ids(0), ids(0)))
+    assert store.get_finished()[0].success is False

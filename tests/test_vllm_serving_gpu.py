@@ -191,6 +191,35 @@ def test_vllm_draft_model_speculation_is_exact(tmp_path):
             seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
 
 
+def test_vllm_kv_offload_stores_and_loads_engine_pages(tmp_path):
+    """KV offloading through the engine's connector: a prompt's pages go to host memory, other
+    prompts evict them from the GPU, and the repeated prompt loads them back; its continuation is
+    the same and the dense forward's."""
+    pytest.importorskip("vllm")
+    from furiosa_opt_models_b200.models import configs, dense, synthetic
+
+    cfg = configs.get("tiny-qwen3")
+    hf = synthetic.write(str(tmp_path / "m"), cfg, seed=15, std=0.05)
+    w = {k: v.float() for k, v in synthetic.engine_weights(cfg, hf).items()}
+    gen = torch.Generator().manual_seed(9)
+    prompts = [torch.randint(0, cfg["vocab"], (256,), generator=gen).tolist() for _ in range(4)]
+    out = str(tmp_path / "offload.json")
+    env = dict(os.environ, VLLM_PLUGINS="furiosa", VLLM_ENABLE_V1_MULTIPROCESSING="0",
+               PYTHONPATH=os.pathsep.join([ROOT, os.path.join(ROOT, "integrations", "furiosa-opt-vllm")]))
+    subprocess.run(["timeout", "-k", "30", "600", sys.executable,
+                    os.path.join(ROOT, "tests", "workers", "vllm_offload.py"), str(tmp_path / "m"), out,
+                    json.dumps(prompts)], check=True, env=env, cwd=ROOT)
+    with open(out) as f:
+        got = json.load(f)
+    assert got["first"] == got["again"], got
+    assert got["stats"]["stored_blocks"] > 0 and got["stats"]["loaded_blocks"] > 0, got["stats"]
+    seq = torch.tensor(prompts[0], dtype=torch.int32)
+    for t in got["first"]:
+        logits = dense.forward(w, cfg, seq)[-1]
+        assert logits[t] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+        seq = torch.cat([seq, torch.tensor([t], dtype=torch.int32)])
+
+
 @pytest.mark.parametrize("mode", ["embed", "classify"])
 def test_vllm_pooling_through_the_engine(tmp_path, mode):
     """vLLM's pooling runner through the plugin: `embed` on a causal checkpoint served as its base
