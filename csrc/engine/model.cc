@@ -687,6 +687,8 @@ struct Launch {
     attn.status = st->status;
     attn.rows = static_cast<int>(T);
     attn.cache_blocks = c.blocks();
+    // The second half of the counters (the GEMMs use the first): the decode splits' merge.
+    attn.merge_counters = i32(m.ws_counters_) + 32768;
     rope = foa::RopeTable{static_cast<const float*>(m.inv_freq_.data()), m.attention_factor_};
   }
 
@@ -880,8 +882,14 @@ class DecodeAttention final : public Module {
  public:
   void forward(Launch& e) const override {
     e.attn.num_segments = static_cast<int>(e.plan.prefill > 0 ? e.plan.decode : e.plan.segments_padded);
+    // The splits merge in the decode kernel while the counters cover the call, else by a second
+    // kernel (very large eager calls).
+    const bool fused = static_cast<int64_t>(e.attn.num_segments) * e.m.kvh_l_ <= 32768;
+    int* counters = e.attn.merge_counters;
+    if (!fused) e.attn.merge_counters = nullptr;
     e.done(foa::paged_decode(e.attn, e.s), "decode attention");
-    if (e.plan.max_keys > e.attn.keys_per_split) ++e.kernels;  // the split merge
+    if (!fused && e.plan.max_keys > e.attn.keys_per_split) ++e.kernels;  // the split merge
+    e.attn.merge_counters = counters;
   }
   std::string name() const override { return "DecodeAttention"; }
 };

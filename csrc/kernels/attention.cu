@@ -374,6 +374,33 @@ __global__ void __launch_bounds__(32 * kWarps, decode_ctas_per_sm(D, kWarps, kSt
       if (c == 0) p.partial_lse[idx] = mm + log2f(ll);
     }
   }
+  if (nsplit == 1 || p.merge_counters == nullptr) return;
+  // The last split of this (segment, key/value head) to finish merges the group's heads, in split
+  // order as the separate merge kernel does (the same bits), and leaves its counter at zero.
+  __shared__ int last_s;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int* counter = p.merge_counters + seg_index * p.kv_heads + kvh;
+    last_s = atomicAdd(counter, 1) == nsplit - 1;
+    if (last_s) *counter = 0;
+  }
+  __syncthreads();
+  if (!last_s) return;
+  __threadfence();
+  for (int i = threadIdx.x; i < G * D; i += 32 * kWarps) {
+    const int r = i / D, c = i % D;
+    const long base = ((long)seg_index * p.q_heads + kvh * G + r) * max_splits;
+    float mx = -INFINITY;
+    for (int sp = 0; sp < nsplit; ++sp) mx = fmaxf(mx, __ldcg(p.partial_lse + base + sp));
+    float num = 0.f, den = 0.f;
+    for (int sp = 0; sp < nsplit; ++sp) {
+      const float w = exp2f(__ldcg(p.partial_lse + base + sp) - mx);
+      num += w * __ldcg(p.partial_o + (base + sp) * D + c);
+      den += w;
+    }
+    p.o[((long)row * p.q_heads + kvh * G + r) * D + c] = __float2bfloat16_rn(num / den);
+  }
 }
 
 // Merges the 2048-key splits of each (segment, head) by log-sum-exp, in split order.
@@ -544,7 +571,7 @@ int decode_launch(const PagedAttention& p, cudaStream_t stream) {
   }
   dim3 grid(p.num_segments * p.kv_heads, max_splits);
   launch_pdl(kernel, dim3(grid), dim3(32 * warps), smem, stream, p, max_splits);
-  if (max_splits > 1)
+  if (max_splits > 1 && p.merge_counters == nullptr)
     launch_pdl(decode_merge_kernel<D>, dim3(p.num_segments, p.q_heads), dim3(D), 0, stream, p, max_splits);
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }

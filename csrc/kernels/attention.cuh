@@ -42,6 +42,10 @@ struct PagedAttention {
   // in flight (2 or 3; 0 takes the default of 2).
   int decode_warps = 0;
   int decode_stages = 0;
+  // Decode: one zeroed counter per (segment, key/value head) (num_segments * kv_heads of them);
+  // given, the last split of each merges the splits in the decode kernel (no merge launch), and
+  // the counters are zero again afterwards. Null: a separate merge kernel.
+  int* merge_counters = nullptr;
   // Prefill: 0 causal (row i of a segment attends keys 0 .. cached + i); 1 bidirectional (every
   // row attends all cached + len keys of its segment: encoders, dense attention over visible keys).
   int bidirectional = 0;

@@ -353,7 +353,7 @@ void bind_ops(py::module_& m) {
           a.cache_blocks = cache_blocks;
           a.decode_warps = warps;
           a.decode_stages = stages;
-          (void)counters;
+          a.merge_counters = as_ptr<int>(counters);
           py::gil_scoped_release nogil;
           check(foa::paged_decode(a, as_stream(stream)), "paged_decode");
         },

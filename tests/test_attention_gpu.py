@@ -142,3 +142,20 @@ def test_bidirectional_prefill(q_heads, kv_heads, d, tensor_cores):
     torch.cuda.synchronize()
     err = (out.float().cpu() - ref).abs().max().item()
     assert err < 2e-2, err
+
+
+def test_decode_splits_merged_in_kernel_match_the_merge_kernel():
+    """With merge counters the last split of each (segment, key/value head) merges in the decode
+    kernel: the same bits as the separate merge kernel, and the counters end at zero."""
+    from furiosa_opt_models_b200 import ops
+
+    cached = [0, 100, 255, 256, 700, 1500, 3000]
+    q, cache, table, segs = _setup([1] * len(cached), cached, 16, 8, 128)
+    args = (q.cuda(), cache.cuda(), table.cuda(), segs.cuda(), 8)
+    separate = ops.paged_decode(*args, max_keys=max(cached) + 1, keys_per_split=256)
+    counters = torch.zeros(len(cached) * 8, dtype=torch.int32, device="cuda")
+    for _ in range(2):
+        fused = ops.paged_decode(*args, max_keys=max(cached) + 1, keys_per_split=256, counters=counters)
+        torch.cuda.synchronize()
+        assert torch.equal(fused, separate)
+        assert torch.count_nonzero(counters).item() == 0
