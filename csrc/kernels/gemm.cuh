@@ -136,6 +136,12 @@ enum GemmWeightFormat : int {
 // -4 tensor-map encoding failed, -5 launch failed.
 int gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 
+// Projections of at most 8 rows of BF16 weights (mode and splits left to the plan, no extra K
+// segment, no group, an unquantized weight): `gemm_bf16` runs them as a weight stream on the CUDA
+// cores (gemv.cu), whose FP32 sums run in another order than the tensor-core GEMM's.
+bool gemv_applies(const GemmArgs& args);
+int gemv_bf16(const GemmArgs& args, cudaStream_t stream);
+
 // Scratch the launch of `args` needs: FP32 workspace bytes and counter entries.
 void gemm_bf16_scratch(const GemmArgs& args, size_t* workspace_bytes, int* counters);
 

@@ -134,3 +134,24 @@ def test_gemm_extra_k_segments(M, mode, epi):
     else:
         ref = full
     _close(out, ref, 2e-2 if epi != 1 else 1e-3)
+
+
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
+@pytest.mark.parametrize("N,K", [(512, 2048), (770, 264), (4096, 768)])
+def test_small_row_projections_stream_weights(M, N, K):
+    """At most 8 rows run as a weight stream (gemv.cu): BF16 with a residual, FP32 and SwiGLU
+    outputs against the FP32 reference."""
+    ops = _ops()
+    from furiosa_opt_models_b200.models import dense, reference
+
+    torch.manual_seed(M * 7 + N)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    w = (torch.randn(N, K, device="cuda") * 0.05).bfloat16()
+    res = torch.randn(M, N, device="cuda").bfloat16()
+    ref = _ref(a, w)
+    _close(ops.gemm(a, w, epilogue=ops.EPI_F32), ref, 1e-3)
+    _close(ops.gemm(a, w, epilogue=ops.EPI_BF16, residual=res), ref + res.float())
+    if N % 256 == 0:
+        g, u = dense.split_gate_up(w)  # 128-row blocks alternate gate and up
+        want = reference.swiglu(_ref(a, g), _ref(a, u))
+        _close(ops.gemm(a, w, epilogue=ops.EPI_SWIGLU), want)
