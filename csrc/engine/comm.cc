@@ -25,11 +25,15 @@ PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int6
   off = align_to(off + 64, 256);
   off_epoch_ = off;
   off = align_to(off + 64, 256);
-  // Partial region: [2 buffers][rows][cols] FP32, this rank's row-parallel GEMM output that
-  // every rank's reducer reads.
+  // Receive region: [2 buffers][world source slots][slot rows][cols] FP32. One-shot calls use
+  // `rows` slot rows of every slot, reduce-scatter calls ceil(rows / world).
+  slot_rows_ = (rows + world - 1) / world;
+  off_recv_ = off;
+  const size_t recv_floats = 2 * static_cast<size_t>(world) * slot_rows_ * cols;
+  off = align_to(off + recv_floats * sizeof(float), 4096);
+  // This rank's FP32 partial [rows][cols]: the row-parallel GEMM's local output, scattered from.
   off_partial_ = off;
-  const size_t partial_floats = 2 * static_cast<size_t>(rows) * cols;
-  off = align_to(off + partial_floats * sizeof(float), 4096);
+  off = align_to(off + static_cast<size_t>(rows) * cols * sizeof(float), 4096);
   off_residual_ = off;
   off = align_to(off + static_cast<size_t>(rows) * cols * 2, 4096);
   off_hidden_ = off;
@@ -43,11 +47,16 @@ PeerCollectives::PeerCollectives(const Device& device, int world, int rank, int6
   heap_bytes_ = off;
   st->check_cuda(cudaMalloc(&heap_, heap_bytes_), "tensor-parallel heap");
   st->check_cuda(cudaMemset(heap_, 0, heap_bytes_), "tensor-parallel heap");
+  // Every receive slot starts unwritten; peers write into it only after `connect`.
+  if (foa::tp_clear_recv(reinterpret_cast<float*>(static_cast<char*>(heap_) + off_recv_), recv_floats,
+                         st->stream) != 0)
+    st->fail("receive region launch failed");
   st->check_cuda(cudaStreamSynchronize(st->stream), "tensor-parallel heap");
   const char* lim = std::getenv("FOA_TP_ONESHOT_BYTES");
-  // One-shot reads (world - 1) copies of every partial on every rank; reduce-scatter reads 1/world
-  // of them and stores the normed rows into every rank behind a second barrier.
-  one_shot_limit_ = lim ? static_cast<size_t>(std::strtoull(lim, nullptr, 10)) : (size_t{1} << 20);
+  // One-shot pushes (world - 1) copies of the call's partials; up to 4 MiB of them it beats the
+  // reduce-scatter's second hop and barrier (2 B200s, Qwen3-1.7B o_proj: 256 rows 17.6 against
+  // 28.0 us; 1024 rows 61.8 against 43.2 us).
+  one_shot_limit_ = lim ? static_cast<size_t>(std::strtoull(lim, nullptr, 10)) : (size_t{4} << 20);
   peer_base_.assign(world, nullptr);
   opened_.assign(world, false);
   peer_base_[rank] = heap_;
@@ -88,7 +97,7 @@ void PeerCollectives::connect(const std::vector<std::string>& handles) {
   for (int p = 0; p < world_; ++p) {
     char* b = static_cast<char*>(peer_base_[p]);
     peers_.signal[p] = reinterpret_cast<unsigned long long*>(b + off_signal_);
-    peers_.partial[p] = reinterpret_cast<float*>(b + off_partial_);
+    peers_.recv[p] = reinterpret_cast<float*>(b + off_recv_);
     peers_.residual[p] = reinterpret_cast<__nv_bfloat16*>(b + off_residual_);
     peers_.hidden[p] = reinterpret_cast<__nv_bfloat16*>(b + off_hidden_);
     peers_.gather_value[p] = reinterpret_cast<float*>(b + off_gvalue_);
@@ -106,25 +115,15 @@ void PeerCollectives::begin_call(cudaStream_t stream) {
 }
 
 bool PeerCollectives::two_shot(int rows) const {
-  // Little data: every rank reads every row's partials (one barrier). More: each rank reduces its
-  // slice of rows and stores the normed rows into every rank (1/world of the reads, a second barrier).
+  // Little data: every rank receives every row (one NVLink hop, no barrier). More: each row goes
+  // to the rank that reduces its slice, which stores the results into every rank (1/world of the
+  // traffic, plus a closing barrier).
   const size_t one_shot_bytes = static_cast<size_t>(rows) * cols_ * 4 * (world_ - 1);
-  return one_shot_bytes > one_shot_limit_;
+  return one_shot_bytes > one_shot_limit_ || rows > slot_rows_;
 }
 
-foa::GemmPeerOut PeerCollectives::reduce_target(int rows, int cols) {
-  if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
-  if (cols != cols_ || rows > rows_) throw ValueError("call exceeds the tensor-parallel heap");
-  // The GEMM writes this rank's own partial region, buffer (seq & 1), read by every reducer.
-  foa::GemmPeerOut t;
-  t.dst[0] = peers_.partial[rank_];
-  t.world = 1;
-  t.rank = 0;
-  t.owner_rows = 0;
-  t.slot_stride = 0;
-  t.buf_stride = static_cast<long>(rows_) * cols_;
-  t.seq = reinterpret_cast<const unsigned int*>(static_cast<char*>(heap_) + off_seq_);
-  return t;
+float* PeerCollectives::partial_buffer() {
+  return reinterpret_cast<float*>(static_cast<char*>(heap_) + off_partial_);
 }
 
 __nv_bfloat16* PeerCollectives::residual_buffer() {
@@ -173,13 +172,29 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   if (residual != residual_buffer() || out != hidden_buffer())
     throw DeviceError("tensor-parallel add_norm takes the heap's own buffers");
   if (cols != cols_ || rows > rows_) throw ValueError("call exceeds the tensor-parallel heap");
-  foa::ReduceNormArgs a{};
+  if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
+  // The partial the GEMM wrote here goes out to the reducing ranks from every SM ...
+  foa::ScatterArgs sc{};
+  sc.peers = peers_;
+  sc.partial = partial_buffer();
+  sc.rows = rows;
+  sc.cols = cols;
+  sc.rank = rank_;
+  sc.world = world_;
+  sc.owner_rows = two_shot(rows) ? (rows + world_ - 1) / world_ : 0;
+  sc.slot_stride = static_cast<long>(slot_rows_) * cols_;
+  sc.buf_stride = sc.slot_stride * world_;
+  sc.seq = reinterpret_cast<const unsigned int*>(static_cast<char*>(heap_) + off_seq_);
+  if (foa::tp_scatter(sc, stream) != 0) device_.state()->fail("tensor-parallel scatter launch failed");
+  // ... while the reducer, launched behind it, polls for what lands.
+  foa::AddNormArgs a{};
   a.peers = peers_;
   a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
   a.arrivals = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_arrivals_);
-  a.announced = reinterpret_cast<unsigned long long*>(static_cast<char*>(heap_) + off_arrivals_ + 8);
   a.seq = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_seq_);
-  a.buf_stride = static_cast<long>(rows_) * cols_;
+  a.recv = peers_.recv[rank_];
+  a.slot_stride = static_cast<long>(slot_rows_) * cols_;
+  a.buf_stride = a.slot_stride * world_;
   a.weight = weight;
   a.eps = eps;
   a.rows = rows;
@@ -191,7 +206,7 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   a.gather_residual = moe_rows_ > 0 ? 1 : 0;  // the expert combine reads every row's residual
   a.status = status_;
   a.trace = trace_;
-  if (foa::tp_reduce_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
+  if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
   inject_peer(stream);
 }
 

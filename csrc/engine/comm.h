@@ -27,7 +27,7 @@ class PeerCollectives : public Collectives {
   int rank() const override { return rank_; }
   int world() const override { return world_; }
   void begin_call(cudaStream_t stream) override;
-  foa::GemmPeerOut reduce_target(int rows, int cols) override;
+  float* partial_buffer() override;
   void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
                 __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) override;
   void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
@@ -62,9 +62,10 @@ class PeerCollectives : public Collectives {
   void* heap_ = nullptr;
   size_t heap_bytes_ = 0;
 
-  size_t off_signal_, off_arrivals_, off_seq_, off_epoch_, off_partial_, off_residual_, off_hidden_,
+  size_t off_signal_, off_arrivals_, off_seq_, off_epoch_, off_recv_, off_partial_, off_residual_, off_hidden_,
       off_gvalue_, off_gindex_, off_moe_;
-  size_t one_shot_limit_ = 0;      // partial bytes a one-shot call may read from its peers
+  int64_t slot_rows_ = 0;          // rows of one source slot of the receive region
+  size_t one_shot_limit_ = 0;      // bytes a one-shot call may push to its peers
   std::vector<void*> peer_base_;   // every rank's heap as mapped here (own heap at rank_)
   std::vector<bool> opened_;
   foa::PeerBuffers peers_{};

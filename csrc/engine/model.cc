@@ -712,10 +712,8 @@ struct Launch {
 
   // One projection C = epilogue(A W^T) in the weight's format, with this call's LoRA segments.
   void gemm(const char* gemm_name, const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c,
-            long ldc, int epi, const void* res, int lora_layer = -1, int lora_module = 0,
-            const foa::GemmPeerOut* peer = nullptr) {
+            long ldc, int epi, const void* res, int lora_layer = -1, int lora_module = 0) {
     foa::GemmArgs g;
-    if (peer != nullptr) g.peer = *peer;
     // LoRA slots: Z_s = X A_s^T (its rows zeroed outside slot s), added as extra K segments
     // Z_s B_s^T into the projection's FP32 sums.
     int nseg = 0;
@@ -924,13 +922,15 @@ class ResidualProjection final : public Module {
              "rmsnorm");
       return;
     }
-    const foa::GemmPeerOut target = e.m.coll_->reduce_target(M, e.H);
-    e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, nullptr, e.H, foa::kEpiF32, nullptr, l_, lora_, &target);
+    e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, e.m.coll_->partial_buffer(), e.H, foa::kEpiF32, nullptr, l_,
+           lora_);
     e.m.coll_->add_norm(e.x, e.wp(norm_), e.cfg.eps, e.h, M, e.H, e.s);
+    e.done(0, "tp scatter");
     e.done(0, "tp add_norm");
   }
   std::string name() const override {
-    return std::string("ResidualProjection ") + weight_ + " + norm " + norm_ + " (rank-ordered all-reduce under TP)";
+    return std::string("ResidualProjection ") + weight_ + " + norm " + norm_ +
+           " (under TP: local FP32 partial, scatter to the reducing ranks, rank-ordered sum)";
   }
 
  private:

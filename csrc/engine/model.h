@@ -71,12 +71,12 @@ class Collectives {
   virtual ~Collectives() = default;
   virtual int rank() const = 0;
   virtual int world() const = 0;
-  // Where a row-parallel GEMM of `rows` x `cols` FP32 partials stores them (this rank's own
-  // symmetric buffer, which every rank's reducer reads) ahead of the add_norm of the same shape.
-  virtual foa::GemmPeerOut reduce_target(int rows, int cols) = 0;
-  // Sums every rank's FP32 partial [rows, cols] (written by the GEMM given reduce_target) in rank
-  // order, adds the BF16 residual (updated in place, rounded once) and writes
-  // RMSNorm(residual) * weight to `out` on every rank.
+  // Where a row-parallel GEMM writes its FP32 partial [rows, cols] (row stride cols) ahead of the
+  // add_norm of the same shape.
+  virtual float* partial_buffer() = 0;
+  // Sums every rank's FP32 partial [rows, cols] (written to partial_buffer) in rank order, adds
+  // the BF16 residual (updated in place, rounded once) and writes RMSNorm(residual) * weight to
+  // `out` on every rank. Launches two kernels: the partial's scatter to the peers and the reducer.
   virtual void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
                         __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) = 0;
   // The first maximum over ranks of (value, token) candidates [rows]: tokens into `out`.

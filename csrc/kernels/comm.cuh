@@ -12,7 +12,7 @@ constexpr int kMaxRanks = 8;
 
 // Every rank's symmetric buffers, as this rank addresses them (peer pointers through CUDA IPC).
 struct PeerBuffers {
-  float* partial[kMaxRanks];            // FP32 partials of the row-parallel GEMMs (see ReduceNormArgs)
+  float* recv[kMaxRanks];               // FP32 partial receive regions (see AddNormArgs)
   __nv_bfloat16* residual[kMaxRanks];   // the residual stream [rows, cols]
   __nv_bfloat16* hidden[kMaxRanks];     // normed rows [rows, cols]
   unsigned long long* signal[kMaxRanks];  // barrier slots: slot i is written by rank i
@@ -20,36 +20,55 @@ struct PeerBuffers {
   int32_t* gather_index[kMaxRanks];
 };
 
-// Every rank's row-parallel GEMM writes its FP32 partial [rows, cols] into its own partial
-// region, buffer (*seq & 1) of two (`buf_stride` floats apart); `seq` advances once per reduction
-// (by the reducer's last CTA) on every rank alike, so consecutive reductions alternate buffers.
-struct ReduceNormArgs {
+// The FP32 partial sums arrive in this rank's receive region, pushed there over NVLink by every
+// rank's scatter (tp_scatter): [2 buffers][world source slots][slot rows][cols], the buffer
+// picked by the low bit of `seq`. A slot holds -0.0 until its value lands; the reducer polls
+// (bounded) until none of the values it needs is -0.0, then writes -0.0 back. `seq` advances once
+// per call (by the last CTA to finish), so consecutive calls alternate buffers and a rank that
+// runs ahead writes the buffer its peer is not reading.
+struct AddNormArgs {
   PeerBuffers peers;
   const unsigned long long* epoch;  // this call's epoch (device memory, written per call)
   unsigned int* arrivals;           // this rank's CTA arrival counter (zero between calls)
-  unsigned long long* announced;    // the last barrier value this rank announced (starts at 0)
-  unsigned int* seq;                // this rank's partial-buffer sequence
-  long buf_stride;                  // floats between the two partial buffers
+  unsigned int* seq;                // this rank's receive sequence
+  float* recv;                      // this rank's receive region
+  long slot_stride, buf_stride;     // floats between source slots, between buffers
   const __nv_bfloat16* weight;
   float eps;
   int rows, cols, rank, world, site;
-  // 0: every rank reduces every row (one-shot all-reduce).
-  // 1: rank r reduces rows [r * s, (r + 1) * s), s = ceil(rows / world) (reduce-scatter), and stores
-  //    the normed rows into every rank (all-gather).
+  // 0: every rank received every row (one-shot all-reduce) at slot row = row.
+  // 1: rank r received rows [r * s, (r + 1) * s) at slot rows 0..s-1, s = ceil(rows / world)
+  //    (reduce-scatter); it reduces them and stores the results into every rank (all-gather).
   int two_shot;
   // Reduce-scatter only: 1 stores the owner's residual rows into every rank too (callers that read
   // every row's residual, such as the mixture-of-experts combine); 0 keeps each residual row on
   // its owner alone, which is the only rank that adds to it again within the call.
   int gather_residual;
   int* status;
-  // Optional: CTA 0 writes %globaltimer here at entry, past the first barrier, and at exit.
+  // Optional: CTA 0 writes %globaltimer here at entry (after the grid dependency wait), once its
+  // row's partials have all landed, and at exit.
   unsigned long long* trace;
 };
 
 // residual = bf16(sum over ranks in rank order of partial + residual); hidden = RMSNorm(residual)
 // * weight; every rank ends with the same hidden rows, and with the same residual rows where it
 // holds them (all of them one-shot; its own slice, or all with gather_residual, two-shot).
-int tp_reduce_norm(const ReduceNormArgs& args, cudaStream_t stream);
+int tp_add_norm(const AddNormArgs& args, cudaStream_t stream);
+
+// Stores this rank's FP32 partial [rows, cols] (cols a multiple of 4) into the receive slots that
+// AddNormArgs describes: slot `rank` of buffer (*seq & 1) of every rank (owner_rows == 0), or of
+// rank r / owner_rows at slot row r % owner_rows (reduce-scatter).
+struct ScatterArgs {
+  PeerBuffers peers;
+  const float* partial;
+  int rows, cols, rank, world, owner_rows;
+  long slot_stride, buf_stride;
+  const unsigned int* seq;
+};
+int tp_scatter(const ScatterArgs& args, cudaStream_t stream);
+
+// Writes the not-yet-written mark (-0.0) over `floats` floats of a receive region.
+int tp_clear_recv(float* recv, size_t floats, cudaStream_t stream);
 
 struct ArgmaxArgs {
   PeerBuffers peers;

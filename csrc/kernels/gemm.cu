@@ -84,7 +84,6 @@ struct KParams {
   const int* group_tiles;  // number of token tiles (device), or null
   const int* tile_group;   // group of each token tile (device)
   long group_rows;
-  GemmPeerOut peer;        // tensor-parallel reduction target (peer.world > 0), kEpiF32 only
 };
 
 // Weight formats a GEMM reads: BF16; FP8 block-scaled or NVFP4 codes dequantized to BF16 in
@@ -189,113 +188,11 @@ __device__ __forceinline__ float silu_bf16_times(float g_acc, float u_acc) {
 
 // Stores 16 consecutive output values of one output row (rows mapping) or one output column
 // (swap mapping), applying the residual add and the output type of the epilogue.
-// Tensor-parallel reduction target: where this rank's partial of output row `row` goes on rank q
-// (`poff` is the buffer and source-slot offset, see peer_offset).
-__device__ __forceinline__ float* peer_dst(const KParams& p, long poff, int q, int row) {
-  return p.peer.dst[q] + poff + (long)row * p.ldc;
-}
-
-// -0.0 marks an unwritten receive slot: a -0.0 partial is sent as +0.0 (the sum is unchanged).
-__device__ __forceinline__ float peer_value(float v) {
-  return __float_as_uint(v) == 0x80000000u ? 0.f : v;
-}
-
-__device__ __forceinline__ void peer_store_one(const KParams& p, long poff, int row, int col, float v) {
-  v = peer_value(v);
-  if (p.peer.owner_rows > 0) {
-    const int q = row / p.peer.owner_rows;
-    peer_dst(p, poff, q, row - q * p.peer.owner_rows)[col] = v;
-    return;
-  }
-  for (int q = 0; q < p.peer.world; ++q) peer_dst(p, poff, q, row)[col] = v;
-}
-
-// Buffer and source-slot offset of this launch's peer stores (read after the grid dependency
-// wait: the reducer of the previous call advanced `seq`).
-__device__ __forceinline__ long peer_offset(const KParams& p) {
-  if (p.peer.world == 0) return 0;
-  return (long)(__ldcg(p.peer.seq) & 1u) * p.peer.buf_stride + (long)p.peer.rank * p.peer.slot_stride;
-}
-
 template <int kEpi>
 __device__ __forceinline__ void store16(const KParams& p, int row, int col, const float (&v)[16],
-                                        bool along_row, long poff = 0) {
+                                        bool along_row) {
   // along_row: the 16 values are C[row, col + t]; otherwise C[row + t, col].
   if (p.debug & 1) return;
-  if (kEpi == kEpiF32 && p.peer.world > 0) {
-    if (along_row) {
-      // Rows mapping: lane L holds row `row` (consecutive lanes, consecutive rows). Four lanes
-      // transpose their 4 x 4 float4 blocks so that each store instruction writes 64 contiguous
-      // bytes of a row per lane group instead of 16 bytes a lane (peer stores travel as NVLink
-      // packets of what one instruction covers). Every lane takes part in the shuffles.
-      const int k = threadIdx.x & 3;
-      float4 t4[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        t4[j] = make_float4(peer_value(v[4 * j]), peer_value(v[4 * j + 1]), peer_value(v[4 * j + 2]),
-                            peer_value(v[4 * j + 3]));
-      // Butterfly transpose of the lanes' 4 x 4 float4 blocks: exchange across lane bit 0, then
-      // across lane bit 1 (selects on the lane bits only, so the blocks stay in registers).
-      auto xchg = [](float4 x, int m) {
-        return make_float4(__shfl_xor_sync(0xffffffffu, x.x, m), __shfl_xor_sync(0xffffffffu, x.y, m),
-                           __shfl_xor_sync(0xffffffffu, x.z, m), __shfl_xor_sync(0xffffffffu, x.w, m));
-      };
-      {
-        const bool odd = k & 1;
-        const float4 r0 = xchg(odd ? t4[0] : t4[1], 1);
-        const float4 r1 = xchg(odd ? t4[2] : t4[3], 1);
-        if (odd) {
-          t4[0] = r0;
-          t4[2] = r1;
-        } else {
-          t4[1] = r0;
-          t4[3] = r1;
-        }
-      }
-      {
-        const bool hi = k & 2;
-        const float4 r0 = xchg(hi ? t4[0] : t4[2], 2);
-        const float4 r1 = xchg(hi ? t4[1] : t4[3], 2);
-        if (hi) {
-          t4[0] = r0;
-          t4[1] = r1;
-        } else {
-          t4[2] = r0;
-          t4[3] = r1;
-        }
-      }
-      // t4[i]: columns col + 4k .. + 3 of row (row - k + i).
-      const int c = col + 4 * k;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int ri = row - k + i;
-        if (ri >= p.out_rows || c >= p.out_cols) continue;
-        int q0 = 0, q1 = p.peer.world, r = ri;
-        if (p.peer.owner_rows > 0) {
-          q0 = ri / p.peer.owner_rows;
-          q1 = q0 + 1;
-          r = ri - q0 * p.peer.owner_rows;
-        }
-        const float w[4] = {t4[i].x, t4[i].y, t4[i].z, t4[i].w};
-        for (int q = q0; q < q1; ++q) {
-          float* dst = peer_dst(p, poff, q, r) + c;
-          if (c + 4 <= p.out_cols) {
-            *reinterpret_cast<float4*>(dst) = t4[i];
-          } else {
-#pragma unroll
-            for (int t = 0; t < 4; ++t)
-              if (c + t < p.out_cols) dst[t] = w[t];
-          }
-        }
-      }
-    } else {
-      if (col >= p.out_cols) return;
-#pragma unroll
-      for (int t = 0; t < 16; ++t)
-        if (row + t < p.out_rows) peer_store_one(p, poff, row + t, col, v[t]);
-    }
-    return;
-  }
   if (kEpi == kEpiF32) {
     float* c = static_cast<float*>(p.c);
     if (along_row) {
@@ -359,12 +256,8 @@ __device__ __forceinline__ void store16(const KParams& p, int row, int col, cons
 enum : int { kRedNone = 0, kRedGlobal = 1, kRedCluster = 2 };
 
 template <int kEpi>
-__device__ __forceinline__ void store_one(const KParams& p, int row, int col, float v, long poff = 0) {
+__device__ __forceinline__ void store_one(const KParams& p, int row, int col, float v) {
   if (row >= p.out_rows || col >= p.out_cols) return;
-  if (kEpi == kEpiF32 && p.peer.world > 0) {
-    peer_store_one(p, poff, row, col, v);
-    return;
-  }
   if (kEpi == kEpiF32) {
     static_cast<float*>(p.c)[(long)row * p.ldc + col] = v;
     return;
@@ -376,31 +269,9 @@ __device__ __forceinline__ void store_one(const KParams& p, int row, int col, fl
 // Stores 8 consecutive output values C[row, col .. col + 7] (col a multiple of 8), applying the
 // residual add and the output type of the epilogue; the cluster split-K reduction's store.
 template <int kEpi>
-__device__ __forceinline__ void store8(const KParams& p, int row, int col, const float (&v)[8], long poff) {
+__device__ __forceinline__ void store8(const KParams& p, int row, int col, const float (&v)[8]) {
   if (row >= p.out_rows || col >= p.out_cols) return;
   const bool whole = col + 8 <= p.out_cols;
-  if (kEpi == kEpiF32 && p.peer.world > 0) {
-    if (!whole) {
-#pragma unroll
-      for (int t = 0; t < 8; ++t)
-        if (col + t < p.out_cols) peer_store_one(p, poff, row, col + t, v[t]);
-      return;
-    }
-    const float4 lo = make_float4(peer_value(v[0]), peer_value(v[1]), peer_value(v[2]), peer_value(v[3]));
-    const float4 hi = make_float4(peer_value(v[4]), peer_value(v[5]), peer_value(v[6]), peer_value(v[7]));
-    int q0 = 0, q1 = p.peer.world, r = row;
-    if (p.peer.owner_rows > 0) {
-      q0 = row / p.peer.owner_rows;
-      q1 = q0 + 1;
-      r = row - q0 * p.peer.owner_rows;
-    }
-    for (int q = q0; q < q1; ++q) {
-      float4* dst = reinterpret_cast<float4*>(peer_dst(p, poff, q, r) + col);
-      dst[0] = lo;
-      dst[1] = hi;
-    }
-    return;
-  }
   if (kEpi == kEpiF32) {
     float* dst = static_cast<float*>(p.c) + (long)row * p.ldc + col;
     if (whole) {
@@ -482,7 +353,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   // A GEMM with a tensor-parallel reduction target lets its reducer launch only once the kernels
   // before it have completed (the trigger follows the producer's grid-dependency wait): the
   // reducer then skips its own wait and polls for the partials while this GEMM still runs.
-  if (p.peer.world == 0) pdl_trigger();
+  pdl_trigger();
   if (threadIdx.x == 0) mark(p, 0);
   // A grouped launch learns its token tiles from the routing kernel before it.
   int units = p.units;
@@ -628,12 +499,10 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           load_w(i, kb0 + i, tp, tq);
         }
         pdl_wait();
-        if (p.peer.world > 0) pdl_trigger();
         mark(p, 2);
         for (int i = 0; i < pre; ++i) load_a(i, kb0 + i, tp, tq);
       } else {
         pdl_wait();
-        if (p.peer.world > 0) pdl_trigger();
       }
       for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
         const int tile = u / p.splits, split = u % p.splits;
@@ -832,7 +701,6 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int lrow = q * 32 + lane;
     pdl_wait();  // the residual and the output may be earlier kernels' memory
-    const long poff = kEpi == kEpiF32 ? peer_offset(p) : 0;
     uint32_t tc = 0;
     uint32_t kit = 0;  // W8A8: k-blocks consumed (stage and buffer sequence of the MMA warp)
     uint32_t xfer_count = 0;  // W8A8: hand-overs between the two scaling streams
@@ -1036,9 +904,9 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
             get16(mb, c0, v);
             const int j = tq * kBN + c0;
             if (!p.swap)
-              store16<kEpi>(p, i, j, v, true, poff);
+              store16<kEpi>(p, i, j, v, true);
             else
-              store16<kEpi>(p, j, i, v, false, poff);
+              store16<kEpi>(p, j, i, v, false);
           }
         }
       }
@@ -1117,8 +985,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       const int rs = slice_rows(rows_here, S);
       const int r0 = rank * rs;
       const int groups = max(0, min(rs, rows_here - r0)) / 8;
-      const long poff = kEpi == kEpiF32 ? peer_offset(p) : 0;
-      for (int e = tid; e < groups * kBN; e += 128) {
+        for (int e = tid; e < groups * kBN; e += 128) {
         const int g = e % groups, c = e / groups;
         if (kEpi == kEpiSwiGLU) {
           float gs[8], us[8];
@@ -1136,7 +1003,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           float o[8];
 #pragma unroll
           for (int t = 0; t < 8; ++t) o[t] = silu_bf16_times(gs[t], us[t]);
-          store8<kEpiBf16>(p, tq * kBN + c, tp * 128 + r0 + g * 8, o, 0);
+          store8<kEpiBf16>(p, tq * kBN + c, tp * 128 + r0 + g * 8, o);
         } else {
           float v[8];
 #pragma unroll
@@ -1147,7 +1014,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
             v[0] += x0.x; v[1] += x0.y; v[2] += x0.z; v[3] += x0.w;
             v[4] += x1.x; v[5] += x1.y; v[6] += x1.z; v[7] += x1.w;
           }
-          store8<kEpi>(p, tq * kBN + c, tp * C::kPRows + r0 + g * 8, v, poff);
+          store8<kEpi>(p, tq * kBN + c, tp * C::kPRows + r0 + g * 8, v);
         }
       }
     }
@@ -1537,18 +1404,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (gemv_applies(a)) return gemv_bf16(a, stream);
   if (a.epilogue == kEpiSwiGLU && (a.N % 256 != 0 || a.residual != nullptr)) return -2;
   if (a.epilogue != kEpiF32 && (a.ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
-  const GemmPeerOut& po = a.peer;
-  if (po.world > 0) {
-    // Peer stores replace `c`: every destination, stride and buffer offset 16-byte aligned.
-    if (a.epilogue != kEpiF32 || po.world > 8 || po.rank < 0 || po.rank >= po.world ||
-        po.seq == nullptr || po.owner_rows < 0 || a.ldc % 4 != 0 || po.slot_stride % 4 != 0 ||
-        po.buf_stride % 4 != 0)
-      return -2;
-    for (int q = 0; q < po.world; ++q)
-      if (po.dst[q] == nullptr || (reinterpret_cast<uintptr_t>(po.dst[q]) & 15)) return -1;
-  } else if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) {
-    return -1;
-  }
+  if (a.epilogue == kEpiF32 && (a.ldc % 4 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
   if (a.residual != nullptr && a.epilogue != kEpiBf16) return -2;
   if (a.w_format != kWBf16 && a.w_scale == nullptr) return -2;
   if (a.w_format == kWNvfp4 && a.K % 64 != 0) return -2;
@@ -1623,7 +1479,6 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     kp.tile_group = a.tile_group;
     kp.group_rows = a.N;
   }
-  kp.peer = a.peer;
   kp.acc_scale = (a.w_format == kWNvfp4 || nvf4) ? a.w_tensor_scale : 1.0f;
   if (nvf4) {
     const long atoms = (long)(a.K / 64) * 512;  // bytes of one 128-row block of scale atoms

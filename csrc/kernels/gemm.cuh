@@ -31,25 +31,6 @@ struct GemmSegment {
   int K = 0;
 };
 
-// Tensor-parallel reduction target of a kEpiF32 GEMM (the row-parallel projections: o_proj and
-// down_proj). With `world` > 0 the FP32 partial sums do not go to `c`: the epilogue stores them
-// over NVLink straight into the receive buffers of the ranks that reduce them, tile by tile as
-// the tiles finish. Rank q's copy lands at dst[q] + (*seq & 1) * buf_stride + rank * slot_stride
-// + r * ldc + col, where r is
-//   owner_rows == 0: the output row itself, on every rank (one-shot all-reduce), or
-//   owner_rows > 0:  row i % owner_rows on rank i / owner_rows only (reduce-scatter).
-// -0.0 marks a receive slot not yet written (the reducer polls until every value it needs has
-// changed, then writes the mark back), so a -0.0 sum is stored as +0.0.
-struct GemmPeerOut {
-  float* dst[8] = {};
-  int world = 0;
-  int rank = 0;
-  int owner_rows = 0;
-  long slot_stride = 0;            // floats between two source slots of a buffer
-  long buf_stride = 0;             // floats between the two buffers
-  const unsigned int* seq = nullptr;  // device word; its low bit picks the buffer
-};
-
 struct GemmArgs {
   const void* a = nullptr;  // activations [M, K] BF16, row stride lda elements
   long lda = 0;
@@ -115,8 +96,6 @@ struct GemmArgs {
   int groups = 0;
   // Up to two extra K segments (BF16 weights, not grouped): C = epilogue(A.W^T + A1.W1^T + A2.W2^T).
   GemmSegment seg[2];
-  // Optional tensor-parallel reduction target (kEpiF32 only); see GemmPeerOut.
-  GemmPeerOut peer;
   // Measurement only (kernel_bench): how split-K partials meet (0 the plan's choice, 1 global
   // scratch, 2 cluster shared memory) and work left out (bit 0 no output stores, bit 1 no TMEM loads).
   int reduction = 0;

@@ -35,9 +35,6 @@ struct GemvArgs {
   const __nv_bfloat16* res;
   long ldr;
   int epilogue;
-  // FP32 output into the tensor-parallel partial buffer (seq & 1) of this rank, or null.
-  const unsigned int* seq;
-  long buf_stride;
 };
 
 __device__ __forceinline__ uint4 ld_stream(const void* p) {
@@ -135,7 +132,6 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const GemvArgs p)
             __float2bfloat16_rn(silu_times(acc[0][m], acc[1][m]));
     } else if (p.epilogue == kEpiF32) {
       float* c = static_cast<float*>(p.c);
-      if (p.seq != nullptr) c += (long)(__ldcg(p.seq) & 1u) * p.buf_stride;
       if (ok0) c[(long)m * p.ldc + r0] = acc[0][m];
       if (ok1) c[(long)m * p.ldc + r1] = acc[1][m];
     } else {
@@ -156,11 +152,10 @@ __global__ void __launch_bounds__(32 * kGemvWarps) gemv_kernel(const GemvArgs p)
 bool gemv_applies(const GemmArgs& a) {
   const bool aligned = (reinterpret_cast<uintptr_t>(a.a) | reinterpret_cast<uintptr_t>(a.w)) % 16 == 0 &&
                        a.lda % 8 == 0 && a.ldw % 8 == 0;
-  const bool local_peer = a.peer.world == 0 || (a.peer.world == 1 && a.peer.owner_rows == 0 && a.peer.slot_stride == 0);
   const bool epi = a.epilogue == kEpiBf16 || a.epilogue == kEpiF32 ||
                    (a.epilogue == kEpiSwiGLU && a.N % 256 == 0);
   return a.M >= 1 && a.M <= 8 && a.mode == kModeAuto && a.splits == 0 && a.w_format == 0 && a.K % 8 == 0 &&
-         aligned && local_peer && epi && a.seg[0].K == 0 && a.group_tiles == nullptr && a.trace == nullptr &&
+         aligned && epi && a.seg[0].K == 0 && a.group_tiles == nullptr && a.trace == nullptr &&
          a.cta_trace == nullptr && a.debug == 0 && a.reduction == 0 && (a.epilogue != kEpiSwiGLU || a.residual == nullptr);
 }
 
@@ -173,13 +168,11 @@ int gemv_bf16(const GemmArgs& a, cudaStream_t stream) {
   p.M = a.M;
   p.N = a.N;
   p.K = a.K;
-  p.c = a.peer.world == 1 ? static_cast<void*>(a.peer.dst[0]) : a.c;
+  p.c = a.c;
   p.ldc = a.ldc;
   p.res = static_cast<const __nv_bfloat16*>(a.residual);
   p.ldr = a.ldr;
   p.epilogue = a.epilogue;
-  p.seq = a.peer.world == 1 ? a.peer.seq : nullptr;
-  p.buf_stride = a.peer.world == 1 ? a.peer.buf_stride : 0;
   const int units = a.epilogue == kEpiSwiGLU ? a.N / 2 : (a.N + 1) / 2;
   const dim3 grid((units + kGemvWarps - 1) / kGemvWarps), block(32 * kGemvWarps);
   cudaError_t e;

@@ -751,7 +751,7 @@ void bind_engine(py::module_& m) {
     HbmBuffer counters(d.model->device(), 32768 * 4);
     unsigned long long* trace_gemm_ = nullptr;
     st->check_cuda(cudaMemsetAsync(counters.data(), 0, 32768 * 4, s), "counters");
-    auto gemm = [&](const foa::GemmPeerOut* peer) {
+    auto gemm = [&](float* partial) {
       foa::GemmArgs g;
       g.a = reinterpret_cast<const void*>(a);
       g.lda = K;
@@ -760,7 +760,7 @@ void bind_engine(py::module_& m) {
       g.M = rows;
       g.N = H;
       g.K = K;
-      g.c = peer ? nullptr : out.data();
+      g.c = partial ? static_cast<void*>(partial) : out.data();
       g.ldc = H;
       g.epilogue = foa::kEpiF32;
       g.workspace = static_cast<float*>(ws.data());
@@ -768,13 +768,11 @@ void bind_engine(py::module_& m) {
       g.counters = static_cast<int*>(counters.data());
       g.counters_len = 32768;
       g.status = st->status;
-      if (peer) g.peer = *peer;
       g.trace = trace_gemm_;
       if (foa::gemm_bf16(g, s) != 0) st->fail("benchmark gemm launch failed");
     };
     auto fused = [&]() {
-      const foa::GemmPeerOut t = coll->reduce_target(rows, H);
-      gemm(&t);
+      gemm(coll->partial_buffer());
       coll->add_norm(coll->residual_buffer(), d.model->weights().at("final_norm").ptr, cfg.eps,
                      coll->hidden_buffer(), rows, H, s);
     };
@@ -799,16 +797,20 @@ void bind_engine(py::module_& m) {
     std::map<std::string, double> r;
     r["fused"] = timed(fused);
     r["local"] = timed([&]() { gemm(nullptr); });
+    // The scatter and reducer alone on a partial already in place (the collective's own cost).
+    r["collective"] = timed([&]() {
+      coll->add_norm(coll->residual_buffer(), d.model->weights().at("final_norm").ptr, cfg.eps, coll->hidden_buffer(),
+                     rows, H, s);
+    });
     {
-      // The fused pair again with an event between the two kernels: the GEMM's share and the
-      // reducer's share (waits for peers included).
+      // The fused pair again with an event between the GEMM and the collective: the GEMM's share
+      // and the scatter + reducer's share (waits for peers included).
       std::vector<cudaEvent_t> ev(3 * iters);
       for (auto& e : ev) cudaEventCreate(&e);
       coll->begin_call(s);
       for (int i = 0; i < iters; ++i) {
-        const foa::GemmPeerOut t = coll->reduce_target(rows, H);
         cudaEventRecord(ev[3 * i], s);
-        gemm(&t);
+        gemm(coll->partial_buffer());
         cudaEventRecord(ev[3 * i + 1], s);
         coll->add_norm(coll->residual_buffer(), d.model->weights().at("final_norm").ptr, cfg.eps,
                        coll->hidden_buffer(), rows, H, s);

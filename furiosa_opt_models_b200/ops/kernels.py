@@ -334,8 +334,7 @@ def paged_prefill(q, cache, table, segments, kv_heads, work, scale=None, out=Non
         q.data_ptr(), out.data_ptr(), cache.data_ptr(), table.data_ptr(), segments.data_ptr(),
         segments.shape[0], q_heads, kv_heads, d, float(scale if scale is not None else d ** -0.5),
         work.data_ptr(), work.shape[0], s.status.data_ptr(), _stream(),
-        rows=rows if tensor_cores else 0, cache_blocks=cache.shape[0] if tensor_cores else 0,
-        bidirectional=not causal)
+        rows=rows if tensor_cores else 0, cache_blocks=cache.shape[0], bidirectional=not causal)
     return out
 
 

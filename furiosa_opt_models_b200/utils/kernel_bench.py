@@ -176,9 +176,10 @@ def moe(args) -> dict:
 
 def tp_o_proj(args) -> dict:
     """Layer 0's attention output projection under tensor parallelism, device-timed on every rank
-    (the maximum reported): the GEMM writing its FP32 partial followed by the rank-ordered
-    all-reduce + residual + RMSNorm that pulls every rank's partial over NVLink ("fused"), and the
-    GEMM alone ("local")."""
+    (the maximum reported): the GEMM writing its FP32 partial locally, the scatter kernel storing it
+    over NVLink into the reducing ranks' receive slots and the rank-ordered reducer + residual +
+    RMSNorm polling for it ("fused"); the GEMM alone ("local"); the scatter and reducer alone on a
+    partial already in place ("collective")."""
     import datetime
     import os
 
@@ -202,15 +203,16 @@ def tp_o_proj(args) -> dict:
     K = cfg["q_heads"] // world * D
     a = torch.randn(args.rows, K, device="cuda").bfloat16()
     r = _native._tp_bench_o_proj(model, args.rows, a.data_ptr(), args.iters)
-    t = torch.tensor([r["fused"], r["local"], r["split_gemm"], r["split_norm"]], dtype=torch.float64, device="cuda")
+    t = torch.tensor([r["fused"], r["local"], r["split_gemm"], r["split_norm"], r["collective"]],
+                     dtype=torch.float64, device="cuda")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    fused_us, local_us = t[0].item() * 1000.0, t[1].item() * 1000.0
-    split = {"gemm_us": round(t[2].item() * 1000.0, 2), "reduce_norm_us": round(t[3].item() * 1000.0, 2)}
+    fused_us, local_us, coll_us = t[0].item() * 1000.0, t[1].item() * 1000.0, t[4].item() * 1000.0
+    split = {"gemm_us": round(t[2].item() * 1000.0, 2), "scatter_reduce_norm_us": round(t[3].item() * 1000.0, 2)}
     tp.detach(model)
     dist.destroy_process_group()
     one_shot = r["two_shot"] == 0
-    # Bytes each rank must move across NVLink: FP32 partials read from the peers (every row, or the
-    # rows of its slice), plus (two-shot) its slice's BF16 normed rows stored into every peer.
+    # Bytes each rank must move across NVLink: FP32 partials stored into the peers (every row, or
+    # each peer's slice), plus (two-shot) its slice's BF16 normed rows stored into every peer.
     nvlink = (args.rows * H * 4 * (world - 1) if one_shot
               else args.rows * H * 4 * (world - 1) / world + args.rows * H * 2 * (world - 1) / world)
     peaks = _peaks()
@@ -220,7 +222,8 @@ def tp_o_proj(args) -> dict:
     bound = max(roof.values())
     return dict(kernel="tp_o_proj_add_norm", world=world, rows=args.rows, hidden=H, K=K,
                 mode="one-shot" if one_shot else "two-shot", fused_us=round(fused_us, 2),
-                local_gemm_us=round(local_us, 2), collective_us=round(fused_us - local_us, 2),
+                local_gemm_us=round(local_us, 2), collective_us=round(coll_us, 2),
+                overlap_us=round(local_us + coll_us - fused_us, 2),
                 events_between_kernels=split,
                 trace_local_us=[round(r[f"trace_local_{i}"], 2) for i in range(8)],
                 trace_fused_us=[round(r[f"trace_fused_{i}"], 2) for i in range(11)],

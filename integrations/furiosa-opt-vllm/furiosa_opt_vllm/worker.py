@@ -248,6 +248,10 @@ class Worker(WorkerBase):
                 target = self.pending.output if isinstance(self.pending, Collected) else self.pending
                 if target is not None:
                     target.kv_connector_output = kvo
+        if scheduler_output.total_num_scheduled_tokens == 0:
+            # Nothing ran: vLLM takes this call's return as the step's output (no sampling).
+            out, self.pending = self.pending, None
+            return out
         return None
 
     def _run(self, scheduler_output) -> None:

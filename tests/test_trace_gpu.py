@@ -39,7 +39,7 @@ def test_trace_level_records_kernel_spans(tmp_path):
     assert len(calls) == 2 and len(device_calls) == 2
     assert all(e["dur"] > 0 for e in device_calls)
     # Every layer launches its projections: at least 4 GEMM spans a layer a call.
-    assert sum(e["name"] == "gemm" for e in kernels) >= 2 * 4 * cfg["layers"]
+    assert sum(e["name"].startswith("gemm") for e in kernels) >= 2 * 4 * cfg["layers"]
     assert all(e["dur"] >= 0 for e in kernels)
     # The kernels of a call lie within its device span.
     first = device_calls[0]
