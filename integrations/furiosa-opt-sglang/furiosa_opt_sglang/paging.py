@@ -30,3 +30,14 @@ def blocks(slots, positions: int) -> list[int]:
 def check_page_size(page_size: int) -> None:
     if page_size != PAGE:
         raise ValueError(f"page_size {page_size}: the engine's cache pages hold {PAGE} tokens")
+
+
+def assign(req_pool_indices, req_to_token, start_offset, end_offset, out_cache_loc, batch_size: int) -> None:
+    """Writes each request's new token slots into its row of the host request table (SGLang's
+    `assign_req_to_token_pool_func` contract: request i's slots for positions start..end follow
+    the earlier requests' in `out_cache_loc`)."""
+    at = 0
+    for i in range(int(batch_size)):
+        start, end = int(start_offset[i]), int(end_offset[i])
+        req_to_token[int(req_pool_indices[i]), start:end] = out_cache_loc[at : at + end - start]
+        at += end - start

@@ -38,6 +38,21 @@ def check(tp_size: int = 1, pp_size: int = 1, dp_size: int = 1, page_size: int =
         raise Refused("page_size", str(e)) from None
 
 
+# Request fields whose inputs the engine's calls do not take (token IDs only) or whose outputs they
+# do not return (scores).
+UNSERVED_INPUTS = ("input_embeds", "image_data", "video_data", "audio_data")
+
+
+def validate_request(_manager, obj, *args, **kwargs) -> None:
+    """Before SGLang's `TokenizerManager._validate_one_request`: refuse a request the plugin does
+    not serve, naming the field."""
+    for field in UNSERVED_INPUTS:
+        if getattr(obj, field, None):
+            raise Refused(field, "the engine's decoders take token IDs only")
+    if getattr(obj, "return_logprob", False):
+        raise Refused("return_logprob", "the engine's decoder calls return tokens, not scores")
+
+
 class Platform:
     """The class SGLang's platform entry point names: CUDA devices, the plugin's checks."""
 

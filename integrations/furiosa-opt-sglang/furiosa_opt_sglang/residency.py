@@ -30,6 +30,7 @@ class Served:
     `load(source, device)` loads a decoder from a checkpoint or its host copy, `checkpoint(path)`
     opens the files and `host_copy(path)` reads them into host memory; `cache(spec, blocks)`
     allocates a KV cache; `trim(device)` returns the engine's cached device blocks to the driver.
+    `blocks` is the cache's block count, or a function of the loaded decoder that sizes it.
     """
 
     def __init__(self, path, device, blocks: int, *, load, checkpoint, host_copy, cache, trim,
@@ -40,7 +41,9 @@ class Served:
         self.memory_saver, self.cpu_backup = memory_saver, cpu_backup
         self.copy = host_copy(path) if cpu_backup else None
         self.model = load(self.copy if self.copy is not None else checkpoint(path), device)
-        self.kv = cache(self.model.cache, blocks)
+        if callable(blocks):
+            self.blocks = blocks(self.model)
+        self.kv = cache(self.model.cache, self.blocks)
         self.released: set[str] = set()
 
     def _tags(self, tags) -> list[str]:
@@ -75,3 +78,27 @@ class Served:
                 raise RuntimeError("the KV cache resumes after the weights it follows")
             self.kv = self._cache(self.model.cache, self.blocks)
             self.released.discard("kv_cache")
+
+
+def _rebind(model_runner) -> None:
+    """Points the plugin's runner and SGLang's token pool at what the served objects hold now."""
+    served = model_runner.served
+    model_runner.engine_runner.model = served.model
+    model_runner.engine_runner.cache = served.kv
+    pool = getattr(model_runner, "token_to_kv_pool", None)
+    if pool is not None and hasattr(pool, "storage"):
+        pool.storage = served.kv
+
+
+def released(_result, updater, request) -> None:
+    """After SGLang's `release_memory_occupation`: release the request's tags on the engine."""
+    model_runner = updater.tp_worker.model_runner
+    model_runner.served.release(getattr(request, "tags", None))
+    _rebind(model_runner)
+
+
+def resumed(_result, updater, request) -> None:
+    """After SGLang's `resume_memory_occupation`: load or allocate the request's tags again."""
+    model_runner = updater.tp_worker.model_runner
+    model_runner.served.resume(getattr(request, "tags", None))
+    _rebind(model_runner)

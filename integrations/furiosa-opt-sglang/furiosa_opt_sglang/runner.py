@@ -1,11 +1,12 @@
-"""Runs SGLang-shaped forward batches through the engine: one engine call per batch, the batch's
-new tokens staged in one host-to-device copy, kept rows' greedy tokens returned in batch order."""
+"""Runs SGLang-shaped forward batches through the engine: the batch's new tokens staged in one
+host-to-device copy a call, kept rows' greedy tokens returned in batch order. `issue` runs SGLang's
+scheduled batches themselves (overlap schedule, tokens kept on the device: `steps`)."""
 
 from __future__ import annotations
 
 import numpy as np
 
-from . import batch
+from . import batch, paging, steps
 
 
 class Runner:
@@ -15,6 +16,16 @@ class Runner:
 
         self.engine, self.dec = engine, dec
         self.model, self.device, self.cache = model, device, cache
+        self.steps = steps.State()
+
+    def blocks(self, req_to_token, slot: int, positions: int) -> list[int]:
+        """The engine blocks of a request-pool row's first `positions` positions."""
+        return paging.blocks(req_to_token[slot], positions)
+
+    def issue(self, schedule_batch, req_to_token, overlap: bool = True):
+        """A scheduled generation batch (SGLang's ScheduleBatch fields) as engine calls; returns the
+        step's result with its tokens still on the device (`steps.issue`)."""
+        return steps.issue(self, schedule_batch, req_to_token, overlap=overlap)
 
     def forward(self, parts: list[batch.Part], tokens, req_to_token) -> list[int]:
         """Runs `parts` (new tokens in `tokens`, flat) and returns the next token of each kept
