@@ -106,25 +106,41 @@ __device__ __forceinline__ uint4 dequant_fp8x8(uint2 v, float scale) {
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
-// BF16 bits of an E2M1 code: +-{0, 0.5, 1, 1.5, 2, 3, 4, 6}.
-__device__ __forceinline__ uint32_t e2m1_bf16_bits(uint32_t code) {
-  const uint32_t c = code & 7u;
-  const uint32_t mag = c == 0 ? 0u : c == 1 ? 0x3F00u : (((126u + (c >> 1)) << 7) | ((c & 1u) << 6));
-  return mag | ((code & 8u) << 12);
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
 }
 
-// Eight E2M1 codes (low nibble first) times their E4M3 scale: exact in BF16.
-__device__ __forceinline__ uint4 dequant_e2m1x8(uint32_t v, uint8_t scale_byte) {
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// An E4M3 scale as two BF16 copies (exact: E4M3 values are BF16 values).
+__device__ __forceinline__ uint32_t e4m3_bf16x2(uint8_t scale_byte) {
   const __half_raw hs = __nv_cvt_fp8_to_halfraw(scale_byte, __NV_E4M3);
-  const float s = __half2float(__half(hs));
-  uint32_t w[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float lo = __uint_as_float(e2m1_bf16_bits(v >> (8 * i)) << 16) * s;
-    const float hi = __uint_as_float(e2m1_bf16_bits(v >> (8 * i + 4)) << 16) * s;
-    w[i] = pack_bf16x2(lo, hi);
-  }
-  return make_uint4(w[0], w[1], w[2], w[3]);
+  const uint32_t b = __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__half(hs))));
+  return b | (b << 16);
+}
+
+// Eight E2M1 codes (low nibble first) times their scale (`scale2`, two BF16 copies), by byte
+// permutes: each 3-bit magnitude indexes the high and the low BF16 bytes of {0, 0.5, 1, 1.5, 2, 3,
+// 4, 6} (high {00 3F 3F 3F 40 40 40 40}, low {00 00 80 C0 00 40 80 C0}), the sign bits move into the
+// high bytes, and the bytes interleave into BF16 pairs. The products are exact in BF16.
+__device__ __forceinline__ uint4 dequant_e2m1x8_permute(uint32_t v, uint32_t scale2) {
+  const uint32_t m = v & 0x77777777u;
+  const uint32_t hi_a = prmt(0x3F3F3F00u, 0x40404040u, m);
+  const uint32_t lo_a = prmt(0xC0800000u, 0xC0804000u, m);
+  const uint32_t hi_b = prmt(0x3F3F3F00u, 0x40404040u, m >> 16);
+  const uint32_t lo_b = prmt(0xC0800000u, 0xC0804000u, m >> 16);
+  // Byte i of `even` / `odd` holds the sign of code 2i / 2i + 1 in its top bit.
+  const uint32_t even = (v << 4) & 0x80808080u, odd = v & 0x80808080u;
+  const uint32_t h0 = hi_a | prmt(even, odd, 0x5140u);
+  const uint32_t h1 = hi_b | prmt(even, odd, 0x7362u);
+  return make_uint4(mul_bf16x2(prmt(lo_a, h0, 0x5140u), scale2), mul_bf16x2(prmt(lo_a, h0, 0x7362u), scale2),
+                    mul_bf16x2(prmt(lo_b, h1, 0x5140u), scale2), mul_bf16x2(prmt(lo_b, h1, 0x7362u), scale2));
 }
 
 __device__ __forceinline__ void mark(const KParams& p, int i) {
@@ -166,8 +182,11 @@ struct Cfg {
   static constexpr int kBarrierBytes = 512;
   static constexpr int kSmemBytes =
       kStages * (kStageBytes + kRawBytes + kSfBytes + kAscBytes) + kBarrierBytes + 1024;
-  // Converter warps (kWF 1, 2) or a second stream of scaling warps (kWF 4) take warps 6-9.
-  static constexpr int kThreadsCta = (kWF == kWFp8Block || kWF == kWNvfp4 || kWF == kWFp8A8) ? 320 : 192;
+  // Converter warps (kWF 1, 2: warps 6-13) or a second stream of scaling warps (kWF 4: warps 6-9).
+  static constexpr int kConvWarps = (kWF == kWFp8Block || kWF == kWNvfp4) ? 8 : 0;
+  static constexpr int kThreadsCta = kConvWarps ? 192 + 32 * kConvWarps : kWF == kWFp8A8 ? 320 : 192;
+  // Items of 8 codes a converter thread expands a stage (weight rows x 8 column groups).
+  static constexpr int kConvItems = kConvWarps ? (kWRows * 8) / (32 * kConvWarps) : 1;
   static_assert(kColsRaw <= 512, "accumulators exceed TMEM");
   static_assert(kSmemBytes <= 232448, "stages exceed shared memory");
   static_assert(kBN % 16 == 0 && kBN >= 16 && kBN <= 256, "invalid MMA N");
@@ -364,9 +383,9 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      // A stage is full when its TMA bytes land and, for quantized weights, the four converter
-      // warps have written the weight tile.
-      mbar_init(full + s, (kWF == kWFp8Block || kWF == kWNvfp4) ? 5 : 1);
+      // A stage is full when its TMA bytes land and, for quantized weights, every converter warp
+      // has written its share of the weight tile.
+      mbar_init(full + s, 1 + C::kConvWarps);
       // W8A8: a stage is free once its MMAs completed and the eight scaling warps read its scales.
       mbar_init(empty + s, kWF == kWFp8A8 ? 9 : 1);
       mbar_init(rawfull + s, 1);
@@ -645,11 +664,16 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       }
     }
   } else if ((kWF == kWFp8Block || kWF == kWNvfp4) && warp >= 6) {
-    // ----------------------------------------------------------------- weight converters (4 warps)
+    // ----------------------------------------------------------------- weight converters (8 warps)
     // Expand each raw weight tile into the BF16 128-byte-swizzled layout the MMA reads: FP8 codes
     // times their 128x128 block scale (rounded once to BF16), or E2M1 codes times their E4M3
-    // 16-element scale (exact in BF16; the tensor scale multiplies the FP32 sums later).
+    // 16-element scale (exact in BF16; the tensor scale multiplies the FP32 sums later). A thread
+    // converts items of 8 codes (rows r = its row + 32 j, column group c); each k-block's scales
+    // are fetched from global memory while the previous k-block converts.
+    constexpr int kConvThreads = 32 * (C::kConvWarps ? C::kConvWarps : 1);
+    constexpr int kItems = C::kConvItems;  // most items a thread converts a stage
     const int ct = threadIdx.x - 192;
+    const int c = ct & 7, r0 = ct >> 3;
     const int wrows_total = p.swap ? p.Mp : p.Nq;
     uint32_t it = 0;
     bool ok = true;
@@ -660,9 +684,28 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       const int kb1 = min(kb0 + p.kb_per_split, p.kblocks);
       const int rows = p.swap ? C::kPRows : kBN;
       const int wrow0 = p.swap ? tp * C::kPRows : tq * kBN;
+      // Scales of one k-block for this thread's items (FP8: float bits; NVFP4: BF16 pairs).
+      auto fetch = [&](int kb, uint32_t (&sv)[C::kConvItems]) {
+#pragma unroll
+        for (int j = 0; j < kItems; ++j) {
+          const int r = r0 + j * (kConvThreads / 8), grow = wrow0 + r;
+          sv[j] = 0;
+          if (r < rows && grow < wrows_total) {
+            if constexpr (kWF == kWFp8Block)
+              sv[j] = __float_as_uint(__ldg(static_cast<const float*>(p.wscale) +
+                                            (long)(grow >> p.wscale_row_shift) * p.wscale_ld +
+                                            (kb >> p.wscale_k_shift)));
+            else
+              sv[j] = __ldg(static_cast<const uint8_t*>(p.wscale) + (long)grow * p.wscale_ld + kb * 4 + (c >> 1));
+          }
+        }
+      };
+      uint32_t cur[kItems], nxt[kItems];
+      if (kb0 < kb1) fetch(kb0, cur);
       for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1;
+        if (kb + 1 < kb1) fetch(kb + 1, nxt);
         int got = 1;
         if (lane == 0) got = mbar_wait(rawfull + s, ph, p.status, kTimeoutTmaFull, abort);
         got = __shfl_sync(0xffffffffu, got, 0);
@@ -672,21 +715,18 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         }
         const uint8_t* src = raw + s * C::kRawBytes;
         uint8_t* dst = smem + s * C::kStageBytes + (p.swap ? 0 : C::kPBytes);
-        for (int id = ct; id < rows * 8; id += 128) {
-          const int r = id >> 3, c = id & 7;
-          const int grow = wrow0 + r;
+#pragma unroll
+        for (int j = 0; j < kItems; ++j) {
+          const int r = r0 + j * (kConvThreads / 8);
+          if (r >= rows) break;
           uint4 out = make_uint4(0, 0, 0, 0);
-          if (grow < wrows_total) {
+          if (wrow0 + r < wrows_total) {
             if constexpr (kWF == kWFp8Block) {
               const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-              const float sc = static_cast<const float*>(
-                  p.wscale)[(long)(grow >> p.wscale_row_shift) * p.wscale_ld + (kb >> p.wscale_k_shift)];
-              out = dequant_fp8x8(v, sc);
+              out = dequant_fp8x8(v, __uint_as_float(cur[j]));
             } else {
               const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * 32 + c * 4);
-              const uint8_t sb =
-                  static_cast<const uint8_t*>(p.wscale)[(long)grow * p.wscale_ld + kb * 4 + (c >> 1)];
-              out = dequant_e2m1x8(v, sb);
+              out = dequant_e2m1x8_permute(v, e4m3_bf16x2(static_cast<uint8_t>(cur[j])));
             }
           }
           *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = out;
@@ -694,6 +734,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         fence_proxy_async();  // the tile is read by the tensor cores (async proxy)
         __syncwarp();
         if (lane == 0) mbar_arrive(full + s);
+#pragma unroll
+        for (int j = 0; j < kItems; ++j) cur[j] = nxt[j];
       }
     }
   } else {

@@ -50,10 +50,17 @@ def gemm(args) -> dict:
         w = (torch.randn(N, K, device="cuda") * 0.02).bfloat16()
         if fmt == "fp8":
             w = ops.quantize_fp8_block(w)
+        elif fmt == "fp8_w8a16":
+            import dataclasses
+
+            w = dataclasses.replace(ops.quantize_fp8_block(w), format="fp8_block_w8a16")
+        elif fmt == "nvfp4":
+            w = ops.quantize_nvfp4(w)  # W4A16: BF16 inputs, E2M1 weights expanded on the fly
         elif fmt == "nvfp4a4":
             w = ops.nvfp4_w4a4(ops.quantize_nvfp4(w), float(a.float().abs().max()) / 2688)
         ws.append(w)
-    wbytes = N * K * ({"fp8": 1 + 1 / 4096, "nvfp4a4": 0.5 + 1 / 16}.get(fmt, 2))
+    wbytes = N * K * ({"fp8": 1 + 1 / 4096, "fp8_w8a16": 1 + 1 / 4096, "nvfp4": 0.5 + 1 / 16,
+                       "nvfp4a4": 0.5 + 1 / 16}.get(fmt, 2))
     epi = {"bf16": ops.EPI_BF16, "f32": ops.EPI_F32, "swiglu": ops.EPI_SWIGLU}[args.epilogue]
     out = {}
     if copies == 1:
@@ -250,7 +257,7 @@ def main() -> None:
     g.add_argument("--M", type=int, default=64)
     g.add_argument("--N", type=int, default=4096)
     g.add_argument("--K", type=int, default=4096)
-    g.add_argument("--format", default="bf16", choices=["bf16", "fp8", "nvfp4a4"])
+    g.add_argument("--format", default="bf16", choices=["bf16", "fp8", "fp8_w8a16", "nvfp4", "nvfp4a4"])
     g.add_argument("--epilogue", default="bf16", choices=["bf16", "f32", "swiglu"])
     g.add_argument("--splits", type=int, default=0)
     g.add_argument("--rotate", type=int, default=1)

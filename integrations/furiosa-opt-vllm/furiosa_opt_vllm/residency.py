@@ -64,7 +64,7 @@ def _drop_model(worker) -> None:
 def _trim(worker) -> None:
     from furiosa_opt_engine import _native
 
-    _native._device_trim(worker.device)
+    _native._device_trim(worker.engine_device)
 
 
 def sleep(worker, level: int) -> None:
@@ -138,7 +138,7 @@ def _load(worker, source) -> None:
     from . import load, lora
 
     lora_config = getattr(worker, "lora_config", None)
-    worker.model = load.load_from(source, worker.device, worker.parallel_config.tensor_parallel_size,
+    worker.model = load.load_from(source, worker.engine_device, worker.parallel_config.tensor_parallel_size,
                                   adapters=lora_config is not None, architecture=getattr(worker, "architecture", None))
     if lora_config is not None:
         worker.adapters = lora.Adapters(lora_config.max_loras, lora_config.max_cpu_loras, worker.model.adapters)
@@ -150,5 +150,5 @@ def _load(worker, source) -> None:
 def check_health(worker) -> None:
     """Raises when the worker's engine device failed (its poison makes every later call raise, a
     synchronization included); a worker that has not opened its device yet is healthy."""
-    if getattr(worker, "device", None) is not None:
-        worker.device.synchronize()
+    if getattr(worker, "engine_device", None) is not None:
+        worker.engine_device.synchronize()

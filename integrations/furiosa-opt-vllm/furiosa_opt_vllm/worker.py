@@ -38,7 +38,9 @@ class Worker(WorkerBase):
                  is_driver_worker: bool = False, **kwargs):
         super().__init__(vllm_config=vllm_config, local_rank=local_rank, rank=rank,
                          distributed_init_method=distributed_init_method, is_driver_worker=is_driver_worker)
-        self.model = self.device = self.cache = self.runner = None
+        self.model = self.engine_device = self.cache = self.runner = None
+        # vLLM's executor threads set this as their CUDA device; the engine's Device is engine_device.
+        self.device = None
         self.copy = None  # sleep mode: the host copy of the checkpoint the weights loaded from
         self.adapters = None  # lora.Adapters when vLLM serves LoRA
         self.asleep: dict = {}
@@ -52,6 +54,7 @@ class Worker(WorkerBase):
         from vllm.distributed import ensure_model_parallel_initialized, init_distributed_environment
 
         torch.cuda.set_device(self.local_rank)
+        self.device = torch.device("cuda", self.local_rank)
         pc = self.parallel_config
         init_distributed_environment(pc.world_size, self.rank, self.distributed_init_method, self.local_rank,
                                      backend="nccl")
@@ -76,7 +79,7 @@ class Worker(WorkerBase):
                 raise admission.Refused("runner", f"pooling serves Qwen3 causal and classifier checkpoints, "
                                                   f"not {', '.join(declared)}")
         self.architecture = architecture
-        self.model, self.device, self.copy = load.load(
+        self.model, self.engine_device, self.copy = load.load(
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
             chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
             adapters=self.lora_config is not None, architecture=architecture)
@@ -88,7 +91,7 @@ class Worker(WorkerBase):
         if sc is not None and str(sc.method) == "draft_model":
             # The draft decoder beside the target on this worker's GPU.
             self.proposer = speculation.DraftModel(
-                self.vllm_config, lambda path: load.load_from(load.checkpoint(path), self.device, 1))
+                self.vllm_config, lambda path: load.load_from(load.checkpoint(path), self.engine_device, 1))
         elif sc is not None:
             self.proposer = speculation.Proposer(self.vllm_config)
         if self.lora_config is not None:
@@ -136,7 +139,7 @@ class Worker(WorkerBase):
         from furiosa_opt_engine import decoder as dec
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
-        self.runner = Runner(self.model, self.device, self.cache, self.adapters, self.pooling_config())
+        self.runner = Runner(self.model, self.engine_device, self.cache, self.adapters, self.pooling_config())
         if self.proposer is not None:
             self.proposer.attach(self.runner, int(kv_cache_config.num_blocks))
         if self.vllm_config.kv_transfer_config is not None:

@@ -36,7 +36,7 @@ def worker(monkeypatch):
     monkeypatch.setattr(load, "checkpoint", lambda path: f"files of {path}")
     monkeypatch.setattr(dec, "Cache", FakeCache)
     w = SimpleNamespace(model_config=SimpleNamespace(enable_sleep_mode=True, model="/m"),
-                        parallel_config=SimpleNamespace(tensor_parallel_size=1), device="dev", runner=None,
+                        parallel_config=SimpleNamespace(tensor_parallel_size=1), engine_device="dev", runner=None,
                         model=FakeModel("copy of /m"), cache=FakeCache("spec", 64), copy="copy of /m", asleep={})
     w.trims = trims
     return w
@@ -88,16 +88,16 @@ def test_refusals(worker):
 def test_health_check_raises_on_a_failed_device():
     from types import SimpleNamespace
 
-    w = SimpleNamespace(device=None)
+    w = SimpleNamespace(engine_device=None)
     residency.check_health(w)  # before load: nothing to check
     calls = []
-    w.device = SimpleNamespace(synchronize=lambda: calls.append(1))
+    w.engine_device = SimpleNamespace(synchronize=lambda: calls.append(1))
     residency.check_health(w)
     assert calls == [1]
 
     def failed():
         raise RuntimeError("the device failed earlier: launch failed")
 
-    w.device = SimpleNamespace(synchronize=failed)
+    w.engine_device = SimpleNamespace(synchronize=failed)
     with pytest.raises(RuntimeError, match="failed earlier"):
         residency.check_health(w)
