@@ -130,7 +130,10 @@ CONTRACTS: tuple[Contract, ...] = (
     Contract("model_config.override_attention_dtype", _unset, "attention runs in BF16"),
     Contract("load_config.load_format", _is("auto", "safetensors"), "the engine loads safetensors checkpoints"),
     # Transfers: KV offloading to host memory through the plugin's connector, nothing else.
-    Contract("ec_transfer_config", lambda v, _c: v is None, "encoder caches are not exchanged"),
+    Contract("ec_transfer_config", lambda v, cfg: v is None or (
+        _get(cfg, "model_config.multimodal_config.mm_encoder_only") is True
+        and bool(getattr(v, "is_ec_producer", False))),
+             "encoder caches are produced only by a media-encoder instance (mm_encoder_only, an EC producer)"),
     Contract("kv_transfer_config.kv_connector", lambda v, _c: v in (None, "FuriosaOffloadingConnector"),
              "KV caches move only to host memory, through FuriosaOffloadingConnector"),
     Contract("kv_transfer_config.kv_load_failure_policy", _is("fail", None),

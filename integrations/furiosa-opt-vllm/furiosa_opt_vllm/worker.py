@@ -11,7 +11,7 @@ import torch
 from vllm.v1.outputs import AsyncModelRunnerOutput, ModelRunnerOutput
 from vllm.v1.worker.worker_base import WorkerBase
 
-from . import admission, lora, pooling, residency, speculation
+from . import admission, lora, media, pooling, residency, speculation
 from . import cache as kv
 from . import load
 from .runner import Runner
@@ -48,6 +48,7 @@ class Worker(WorkerBase):
         self.proposer = None  # speculation.Proposer when vLLM speculates
         self.pooling = getattr(self.model_config, "runner_type", "generate") == "pooling"
         self.drafts = None  # the drafts proposed after the last step, for take_draft_token_ids
+        self.media = None  # media.Media when vLLM runs this instance as a media encoder alone
 
     # ------------------------------------------------------------------------ life cycle
     def init_device(self) -> None:
@@ -70,6 +71,16 @@ class Worker(WorkerBase):
         tp_rank = get_tensor_model_parallel_rank() if tp_size > 1 else 0
         chips = load.replica_chips(self.local_rank, tp_rank, tp_size, getattr(pc, "data_parallel_rank", 0) or 0,
                                    os.environ.get("FURIOSA_VISIBLE_CHIPS"))
+        if media.encoder_only(self.model_config):
+            # An encoder-only instance: the checkpoint's media encoder alone, no KV cache.
+            import furiosa_opt_engine as engine
+
+            if tp_size > 1:
+                raise admission.Refused("tensor_parallel_size", "the media encoder runs on one GPU")
+            self.engine_device = engine.Device(engine.Placement(chips, range(8)))
+            encoder = engine.LoadOptions().encoder().load(load.checkpoint(self.model_config.model), self.engine_device)
+            self.media = media.Media(engine, encoder, self.engine_device)
+            return
         architecture = None
         if self.pooling:
             declared = load.architectures(self.model_config.model)
@@ -120,6 +131,8 @@ class Worker(WorkerBase):
         residency.reload(self)
 
     def determine_available_memory(self) -> int:
+        if self.media is not None:
+            return 0  # an encoder-only instance caches no keys or values
         free, total = torch.cuda.mem_get_info()
         budget = int(total * self.cache_config.gpu_memory_utilization) - (total - free)
         # The engine addresses each layer's cache with 32-bit byte offsets.
@@ -133,10 +146,19 @@ class Worker(WorkerBase):
         return budget
 
     def get_kv_cache_spec(self):
+        if self.media is not None:
+            return {}
         return kv.spec(self.model, self.model_config)
 
     def initialize_from_config(self, kv_cache_config) -> None:
         from furiosa_opt_engine import decoder as dec
+
+        if self.media is not None:
+            if self.vllm_config.ec_transfer_config is not None:
+                from vllm.distributed.ec_transfer import ensure_ec_transfer_initialized
+
+                ensure_ec_transfer_initialized(self.vllm_config)
+            return
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
         self.runner = Runner(self.model, self.engine_device, self.cache, self.adapters, self.pooling_config())
@@ -171,6 +193,8 @@ class Worker(WorkerBase):
         return CompilationTimes(0.0, 0.0)
 
     def get_supported_tasks(self):
+        if media.encoder_only(self.model_config):
+            return ("generate",)
         if not self.pooling:
             return ("generate",)
         if self.model is not None:
@@ -228,6 +252,8 @@ class Worker(WorkerBase):
         return get_kv_transfer_group() if has_kv_transfer_group() else None
 
     def execute_model(self, scheduler_output):
+        if self.media is not None:
+            return media.execute(self.media, scheduler_output)
         conn = self.connector()
         meta = getattr(scheduler_output, "kv_connector_metadata", None)
         if conn is not None and meta is not None:

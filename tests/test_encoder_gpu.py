@@ -74,3 +74,31 @@ def test_call_refusals(tmp_path):
     big = _hbm(engine, device, torch.zeros(2305, 640).bfloat16())
     with pytest.raises(NotImplementedError, match="item 0 holds 2305 rows; a launch takes at most 2304"):
         enc.audio([engine.vision_language.Audio(big)])
+
+
+def test_vllm_media_step_matches_the_encoder(tmp_path):
+    """The vLLM encoder-only step (furiosa_opt_vllm.media) on the real encoder: an image with the
+    processor's padding patches and an audio clip with padded frames give the rows of the encoder
+    called on the valid patches and frames alone."""
+    from types import SimpleNamespace as ns
+
+    from furiosa_opt_vllm import media
+
+    engine, device, enc, w, cfg = _load(tmp_path)
+    g = torch.Generator().manual_seed(3)
+    pix = torch.randn(6, 6912, generator=g).bfloat16()
+    pos = torch.tensor([[0, 0], [1, 0], [2, 1], [3, 1], [-1, -1], [-1, -1]])
+    frames = torch.randn(9, 640, generator=g).bfloat16()
+    mask = torch.tensor([1] * 7 + [0] * 2)
+    image = ns(identifier="i", modality="image", data={"pixel_values": pix, "pixel_position_ids": pos},
+               mm_position=ns(get_num_embeds=lambda: 4))
+    audio = ns(identifier="a", modality="audio", data={"input_features_padded": frames, "input_features_mask": mask},
+               mm_position=ns(get_num_embeds=lambda: 7))
+    m = media.Media(engine, enc, device)
+    so = ns(finished_req_ids=set(), free_encoder_mm_hashes=[], scheduled_new_reqs=[ns(req_id="r", mm_features=[image, audio])],
+            scheduled_encoder_inputs={"r": [0, 1]})
+    assert m.step(so) == ["i", "a"]
+    (want_i,) = enc.vision([engine.vision_language.Image(_hbm(engine, device, pix[:4]), pos[:4].tolist())])
+    (want_a,) = enc.audio([engine.vision_language.Audio(_hbm(engine, device, frames[:7]))])
+    assert torch.equal(m.host["i"].float(), torch.from_numpy(want_i.to_host().numpy()))
+    assert torch.equal(m.host["a"].float(), torch.from_numpy(want_a.to_host().numpy()))

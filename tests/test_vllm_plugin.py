@@ -384,3 +384,93 @@ def test_offload_pages_round_trip_and_poison_on_failure():
     assert failing.get_finished()[0].success is False and pool.poisoned
     store.transfer_async(4, (ids(0), ids(0)))
     assert store.get_finished()[0].success is False
+
+
+def test_encoder_caches_only_from_a_media_encoder_instance():
+    from types import SimpleNamespace as ns
+
+    def config(encoder_only, producer):
+        return ns(parallel_config=ns(pipeline_parallel_size=1, tensor_parallel_size=1, nnodes=1),
+                  cache_config=ns(cache_dtype="auto"),
+                  model_config=ns(dtype="bfloat16", quantization=None,
+                                  multimodal_config=ns(mm_encoder_only=encoder_only)),
+                  load_config=ns(load_format="auto"), speculative_config=None,
+                  ec_transfer_config=ns(is_ec_producer=producer))
+
+    admission.check(config(True, True))
+    for args in ((False, True), (True, False)):
+        with pytest.raises(admission.Refused) as e:
+            admission.check(config(*args))
+        assert e.value.option == "ec_transfer_config"
+
+
+class _Rows:
+    def __init__(self, values):
+        self.values = values
+        self.shape = values.shape
+
+    def to_host(self):
+        return self
+
+    def numpy(self):
+        return self.values.float().numpy()
+
+
+def test_media_step_embeds_each_item_once_and_frees_hashes():
+    """An encoder-only step: scheduled images, video frames and audio embed through the engine's
+    encoder with the processor's padding left out, each hash once, saved through the connector
+    callback; freed hashes leave both caches."""
+    from types import SimpleNamespace as ns
+
+    import torch
+
+    from furiosa_opt_vllm import media
+
+    calls = []
+
+    class Encoder:
+        def vision(self, images):
+            (im,) = images
+            calls.append(("vision", im.pixels.shape[0], im.positions))
+            return [_Rows(im.pixels * 2)]
+
+        def audio(self, clips):
+            (clip,) = clips
+            calls.append(("audio", clip.frames.shape[0]))
+            return [_Rows(clip.frames[:, :4])]
+
+    class Host:
+        @staticmethod
+        def from_dlpack(t):
+            return ns(to_hbm=lambda device: t)
+
+    engine = ns(HostTensor=Host, vision_language=ns(Image=lambda pixels, positions: ns(pixels=pixels, positions=positions),
+                                                   Audio=lambda frames: ns(frames=frames)))
+    m = media.Media(engine, Encoder(), device=None)
+    pix = torch.arange(12, dtype=torch.float32).reshape(3, 4)
+    pos = torch.tensor([[0, 0], [1, 0], [-1, -1]])
+    image = ns(identifier="img", modality="image", data={"pixel_values": pix, "pixel_position_ids": pos},
+               mm_position=ns(get_num_embeds=lambda: 2))
+    video = ns(identifier="vid", modality="video",
+               data={"pixel_values_videos": torch.ones(2, 2, 4), "pixel_position_ids_videos": torch.zeros(2, 2, 2, dtype=torch.long)},
+               mm_position=ns(get_num_embeds=lambda: 4))
+    audio = ns(identifier="aud", modality="audio",
+               data={"input_features_padded": torch.ones(5, 8), "input_features_mask": torch.tensor([1, 1, 1, 0, 0])},
+               mm_position=ns(get_num_embeds=lambda: 3))
+    so = ns(finished_req_ids=set(), free_encoder_mm_hashes=[],
+            scheduled_new_reqs=[ns(req_id="a", mm_features=[image, video]), ns(req_id="b", mm_features=[audio, image])],
+            scheduled_encoder_inputs={"a": [0, 1], "b": [0, 1]})
+    saved = []
+    done = m.step(so, save=lambda cache, h: saved.append((h, cache[h].dtype)))
+    assert done == ["img", "vid", "aud"]  # the second request's image hash was embedded already
+    assert saved == [("img", torch.bfloat16), ("vid", torch.bfloat16), ("aud", torch.bfloat16)]
+    assert calls[0] == ("vision", 2, [[0, 0], [1, 0]]) and calls[1][:2] == ("vision", 4) and calls[2] == ("audio", 3)
+    assert torch.equal(m.host["img"].float(), pix[:2] * 2)
+    so2 = ns(finished_req_ids={"a"}, free_encoder_mm_hashes=["img", "vid"], scheduled_new_reqs=[],
+             scheduled_encoder_inputs={})
+    assert m.step(so2) == []
+    assert set(m.host) == {"aud"} and set(m.rows) == {"aud"} and set(m.features) == {"b"}
+    bad = ns(identifier="x", modality="image", data={"pixel_values": pix, "pixel_position_ids": pos},
+             mm_position=ns(get_num_embeds=lambda: 3))
+    with pytest.raises(ValueError, match="placeholders"):
+        m.embed(bad)
