@@ -240,6 +240,7 @@ __device__ __forceinline__ void store16(const KParams& p, int row, int col, cons
     for (int t = 0; t < 16; ++t) w[t] = v[t];
     if (p.res != nullptr) {
       const __nv_bfloat16* r = p.res + (long)row * p.ldr + col;
+#pragma unroll
       for (int t = 0; t < 16; ++t)
         if (col + t < p.out_cols) w[t] += __bfloat162float(r[t]);
     }
@@ -369,9 +370,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
-  // A GEMM with a tensor-parallel reduction target lets its reducer launch only once the kernels
-  // before it have completed (the trigger follows the producer's grid-dependency wait): the
-  // reducer then skips its own wait and polls for the partials while this GEMM still runs.
+  // The next kernel may launch at once; its own grid-dependency wait orders it after this one.
   pdl_trigger();
   if (threadIdx.x == 0) mark(p, 0);
   // A grouped launch learns its token tiles from the routing kernel before it.
@@ -936,6 +935,38 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
 #pragma unroll
             for (int t = 0; t < 16; ++t) v[t] = silu_bf16_times(g[t], v[t]);
             store16<kEpiBf16>(p, tq * kBN + c0, feature, v, false);
+          }
+        }
+      } else if (kEpi == kEpiBf16 && kMB == 1 && kBN % 64 == 0 && !p.swap && p.res != nullptr &&
+                 (tq + 1) * kBN <= p.out_cols &&
+                 ((reinterpret_cast<uintptr_t>(p.res) | reinterpret_cast<uintptr_t>(p.c)) & 15) == 0 &&
+                 ((p.ldr | p.ldc) & 7) == 0) {
+        // Rows mapping with a residual (o_proj, down_proj at one chip): each thread owns one output
+        // row; the residual of 64 columns is loaded with eight 16-byte loads in flight before the
+        // accumulator columns are read, so the tile pays the load latency once per 64 columns.
+        const int i = tp * C::kPRows + lrow;
+        const bool in = i < p.out_rows;
+        for (int c0 = 0; c0 < kBN; c0 += 64) {
+          const int j0 = tq * kBN + c0;
+          uint4 rr[8];
+          const uint4* rsrc = reinterpret_cast<const uint4*>(p.res + (long)i * p.ldr + j0);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) rr[q] = in ? __ldcs(rsrc + q) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int c1 = 0; c1 < 64; c1 += 16) {
+            float v[16];
+            get16(0, c0 + c1, v);
+            const uint32_t rw[8] = {rr[c1 / 8].x, rr[c1 / 8].y, rr[c1 / 8].z, rr[c1 / 8].w,
+                                    rr[c1 / 8 + 1].x, rr[c1 / 8 + 1].y, rr[c1 / 8 + 1].z, rr[c1 / 8 + 1].w};
+            uint32_t out[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              out[t] = pack_bf16x2(v[2 * t] + __uint_as_float(rw[t] << 16), v[2 * t + 1] + __uint_as_float(rw[t] & 0xFFFF0000u));
+            if (in && !(p.debug & 1)) {
+              uint4* dst = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.c) + (long)i * p.ldc + j0 + c1);
+              dst[0] = make_uint4(out[0], out[1], out[2], out[3]);
+              dst[1] = make_uint4(out[4], out[5], out[6], out[7]);
+            }
           }
         }
       } else {

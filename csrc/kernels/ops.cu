@@ -274,6 +274,110 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
   }
 }
 
+// Row-per-CTA form of the same operation for 16-byte aligned operands (a CTA: one row, a group of
+// its heads): the row's rotation (cos, sin) pairs are computed once into shared memory and shared
+// by the group's heads; a head is kHD / 8 lanes of 8 consecutive elements (16-byte loads and
+// stores), so a warp handles 256 / kHD heads at once; the partner of element j (j + d/2) sits
+// kHD / 16 lanes away.
+template <int kHD>
+__global__ void __launch_bounds__(128) qk_norm_rope_cache_rows_kernel(
+    const __nv_bfloat16* __restrict__ qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
+    const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float eps,
+    const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, float attn_factor,
+    __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
+    const int32_t* __restrict__ slots, long cache_slots, int* status) {
+  constexpr int kLanes = kHD / 8;        // lanes of one head
+  constexpr int kPerWarp = 32 / kLanes;  // heads of one warp pass
+  constexpr int kHalf = kLanes / 2;      // lane distance of the rotation partner
+  __shared__ float cs[kHD / 2], sn[kHD / 2];
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  if (row >= rows) return;
+  const float pos = (float)positions[row];
+  for (int j = threadIdx.x; j < kHD / 2; j += blockDim.x) {
+    float sv, cv;
+    sincosf(pos * inv_freq[j], &sv, &cv);
+    cs[j] = cv * attn_factor;
+    sn[j] = sv * attn_factor;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane / kLanes, hl = lane % kLanes;
+  const bool second = hl >= kHalf;
+  const int j0 = (hl % kHalf) * 8;  // frequency index of this lane's first element
+  const int heads = q_heads + 2 * kv_heads;
+  const int slot = slots[row];
+  const bool bad_slot = slot >= 0 && cache_slots > 0 && slot >= cache_slots;
+  if (bad_slot && threadIdx.x == 0 && blockIdx.y == 0) record_status(status, kBadIndex);  // nothing of the row is cached
+  // blockIdx.y picks the row's group of kGroup heads; a warp takes kPasses passes of kPerWarp
+  // heads, with every pass's load issued before the first is processed.
+  constexpr int kPasses = 4;
+  constexpr int kGroup = 4 * kPerWarp * kPasses;
+  uint4 raws[kPasses];
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps) {
+    const int head = blockIdx.y * kGroup + (ps * 4 + warp) * kPerWarp + sub;
+    raws[ps] = head < heads ? __ldcs(reinterpret_cast<const uint4*>(qkv + (long)row * ld_qkv + (long)head * kHD) + hl)
+                            : make_uint4(0, 0, 0, 0);
+  }
+#pragma unroll
+  for (int ps = 0; ps < kPasses; ++ps) {
+    const int head = blockIdx.y * kGroup + (ps * 4 + warp) * kPerWarp + sub;
+    const bool valid = head < heads;
+    const uint4 raw = raws[ps];
+    const uint32_t rw[4] = {raw.x, raw.y, raw.z, raw.w};
+    float x[8];
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      x[2 * t] = __uint_as_float(rw[t] << 16);
+      x[2 * t + 1] = __uint_as_float(rw[t] & 0xFFFF0000u);
+    }
+    const bool is_q = head < q_heads;
+    const bool is_k = !is_q && head < q_heads + kv_heads;
+    const bool roped = valid && (is_q || is_k);
+    const __nv_bfloat16* nw = is_q ? q_norm : k_norm;
+    // Every lane takes part in the shuffles; only a roped head's lanes use them.
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += x[e] * x[e];
+#pragma unroll
+    for (int o = kHalf; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (roped && nw != nullptr) {
+      const float inv = rsqrtf(ss / (float)kHD + eps);
+      const uint4 wv = __ldg(reinterpret_cast<const uint4*>(nw) + hl);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        x[2 * t] = __bfloat162float(__float2bfloat16_rn(x[2 * t] * inv * __uint_as_float(ww[t] << 16)));
+        x[2 * t + 1] =
+            __bfloat162float(__float2bfloat16_rn(x[2 * t + 1] * inv * __uint_as_float(ww[t] & 0xFFFF0000u)));
+      }
+    }
+    float y[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const float partner = __shfl_xor_sync(0xffffffffu, x[e], kHalf);
+      const float c = cs[j0 + e], sv = sn[j0 + e];
+      // First half: x1 c - x2 s; second half: x2 c + x1 s.
+      y[e] = roped ? (second ? x[e] * c + partner * sv : x[e] * c - partner * sv) : x[e];
+    }
+    if (!valid) continue;
+    const uint4 out = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]), pack_bf16x2(y[4], y[5]),
+                                 pack_bf16x2(y[6], y[7]));
+    if (is_q) {
+      reinterpret_cast<uint4*>(q_out + ((long)row * q_heads + head) * kHD)[hl] = out;
+      continue;
+    }
+    if (slot < 0 || bad_slot) continue;
+    const int kvh = is_k ? head - q_heads : head - q_heads - kv_heads;
+    const long page = 2L * kv_heads * 16 * kHD;
+    __nv_bfloat16* dst = cache + (long)(slot / 16) * page + (is_k ? 0 : (long)kv_heads * 16 * kHD) +
+                         ((long)kvh * 16 + slot % 16) * kHD;
+    reinterpret_cast<uint4*>(dst)[hl] = out;
+  }
+}
+
 // ------------------------------------------------------------------------------------ init / gather
 // SplitMix64-style mixing of (seed, index) into 64 random bits.
 __device__ __forceinline__ uint64_t mix64(uint64_t x) {
@@ -467,6 +571,20 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slots,
                        cudaStream_t stream, long cache_slots, int* status) {
   if (rows <= 0) return 0;
+  const bool aligned = ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_out) |
+                         reinterpret_cast<uintptr_t>(cache) | reinterpret_cast<uintptr_t>(q_norm) |
+                         reinterpret_cast<uintptr_t>(k_norm)) & 15) == 0 && ld_qkv % 8 == 0;
+  if (aligned && (head_dim == 64 || head_dim == 128 || head_dim == 256)) {
+    // Row-per-CTA kernel: shared rotation table, 16-byte accesses.
+    const auto kernel = head_dim == 64    ? qk_norm_rope_cache_rows_kernel<64>
+                        : head_dim == 128 ? qk_norm_rope_cache_rows_kernel<128>
+                                          : qk_norm_rope_cache_rows_kernel<256>;
+    const int group = 16 * (256 / head_dim);  // heads of one CTA: 4 warps x 4 passes
+    const int groups = (q_heads + 2 * kv_heads + group - 1) / group;
+    return launch_pdl(kernel, dim3(rows, groups), dim3(128), 0, stream, qkv, ld_qkv, rows, q_heads, kv_heads, q_norm,
+                      k_norm, eps, positions, rope.inv_freq, rope.attention_factor, q_out, cache, slots,
+                      cache_slots, status) == cudaSuccess ? 0 : -5;
+  }
   const long tasks = (long)rows * (q_heads + 2 * kv_heads);
   const int grid = (int)((tasks + 3) / 4);
   switch (head_dim) {
