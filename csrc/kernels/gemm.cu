@@ -668,7 +668,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
     // times their 128x128 block scale (rounded once to BF16), or E2M1 codes times their E4M3
     // 16-element scale (exact in BF16; the tensor scale multiplies the FP32 sums later). A thread
     // converts items of 8 codes (rows r = its row + 32 j, column group c); each k-block's scales
-    // are fetched from global memory while the previous k-block converts.
+    // are fetched from global memory four k-blocks ahead.
     constexpr int kConvThreads = 32 * (C::kConvWarps ? C::kConvWarps : 1);
     constexpr int kItems = C::kConvItems;  // most items a thread converts a stage
     const int ct = threadIdx.x - 192;
@@ -699,42 +699,51 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
           }
         }
       };
-      uint32_t cur[kItems], nxt[kItems];
-      if (kb0 < kb1) fetch(kb0, cur);
-      for (int kb = kb0; kb < kb1; ++kb, ++it) {
-        const int s = it % kStages;
-        const uint32_t ph = (it / kStages) & 1;
-        if (kb + 1 < kb1) fetch(kb + 1, nxt);
-        int got = 1;
-        if (lane == 0) got = mbar_wait(rawfull + s, ph, p.status, kTimeoutTmaFull, abort);
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) {
-          ok = false;
-          break;
-        }
-        const uint8_t* src = raw + s * C::kRawBytes;
-        uint8_t* dst = smem + s * C::kStageBytes + (p.swap ? 0 : C::kPBytes);
+      // A ring of kAhead k-blocks' scales: the loads for k-block kb + kAhead go out when kb's
+      // scales are used, so their latency hides behind kAhead conversions.
+      constexpr int kAhead = 4;
+      uint32_t sv[kAhead][kItems];
 #pragma unroll
-        for (int j = 0; j < kItems; ++j) {
-          const int r = r0 + j * (kConvThreads / 8);
-          if (r >= rows) break;
-          uint4 out = make_uint4(0, 0, 0, 0);
-          if (wrow0 + r < wrows_total) {
-            if constexpr (kWF == kWFp8Block) {
-              const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
-              out = dequant_fp8x8(v, __uint_as_float(cur[j]));
-            } else {
-              const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * 32 + c * 4);
-              out = dequant_e2m1x8_permute(v, e4m3_bf16x2(static_cast<uint8_t>(cur[j])));
-            }
+      for (int d = 0; d < kAhead; ++d)
+        if (kb0 + d < kb1) fetch(kb0 + d, sv[d]);
+      for (int kbb = kb0; kbb < kb1 && ok; kbb += kAhead) {
+#pragma unroll
+        for (int d = 0; d < kAhead; ++d) {
+          const int kb = kbb + d;
+          if (kb >= kb1) break;
+          const int s = it % kStages;
+          const uint32_t ph = (it / kStages) & 1;
+          int got = 1;
+          if (lane == 0) got = mbar_wait(rawfull + s, ph, p.status, kTimeoutTmaFull, abort);
+          got = __shfl_sync(0xffffffffu, got, 0);
+          if (!got) {
+            ok = false;
+            break;
           }
-          *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = out;
-        }
-        fence_proxy_async();  // the tile is read by the tensor cores (async proxy)
-        __syncwarp();
-        if (lane == 0) mbar_arrive(full + s);
+          const uint8_t* src = raw + s * C::kRawBytes;
+          uint8_t* dst = smem + s * C::kStageBytes + (p.swap ? 0 : C::kPBytes);
 #pragma unroll
-        for (int j = 0; j < kItems; ++j) cur[j] = nxt[j];
+          for (int j = 0; j < kItems; ++j) {
+            const int r = r0 + j * (kConvThreads / 8);
+            if (r >= rows) break;
+            uint4 out = make_uint4(0, 0, 0, 0);
+            if (wrow0 + r < wrows_total) {
+              if constexpr (kWF == kWFp8Block) {
+                const uint2 v = *reinterpret_cast<const uint2*>(src + r * 64 + c * 8);
+                out = dequant_fp8x8(v, __uint_as_float(sv[d][j]));
+              } else {
+                const uint32_t v = *reinterpret_cast<const uint32_t*>(src + r * 32 + c * 4);
+                out = dequant_e2m1x8_permute(v, e4m3_bf16x2(static_cast<uint8_t>(sv[d][j])));
+              }
+            }
+            *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = out;
+          }
+          fence_proxy_async();  // the tile is read by the tensor cores (async proxy)
+          __syncwarp();
+          if (lane == 0) mbar_arrive(full + s);
+          ++it;
+          if (kb + kAhead < kb1) fetch(kb + kAhead, sv[d]);
+        }
       }
     }
   } else {
