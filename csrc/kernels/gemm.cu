@@ -49,6 +49,7 @@ struct KParams {
   int splits, kblocks, kb_per_split;
   int units;                  // tiles * splits
   int swap;                   // 1: C[j, i] (N-side rows are output rows)
+  int tma_store;              // rows mapping, BF16 output through shared memory and TMA stores
   void* c;
   long ldc;
   const __nv_bfloat16* res;
@@ -180,8 +181,10 @@ struct Cfg {
                                    : kColsRaw <= 256 ? 256
                                                      : 512;
   static constexpr int kBarrierBytes = 512;
+  // BF16 rows-mapping output staging: one 32 x 64 box (4 KiB) for each epilogue warp.
+  static constexpr int kOutStage = (kWF == kWBf16 && kMB == 1) ? 4 * 4096 : 0;
   static constexpr int kSmemBytes =
-      kStages * (kStageBytes + kRawBytes + kSfBytes + kAscBytes) + kBarrierBytes + 1024;
+      kStages * (kStageBytes + kRawBytes + kSfBytes + kAscBytes) + kOutStage + kBarrierBytes + 1024;
   // Converter warps (kWF 1, 2: warps 6-13) or a second stream of scaling warps (kWF 4: warps 6-9).
   static constexpr int kConvWarps = (kWF == kWFp8Block || kWF == kWNvfp4) ? 8 : 0;
   static constexpr int kThreadsCta = kConvWarps ? 192 + 32 * kConvWarps : kWF == kWFp8A8 ? 320 : 192;
@@ -343,6 +346,7 @@ __device__ __forceinline__ int slice_rows(int rows, int splits) {
 struct AuxMaps {
   CUtensorMap w;
   CUtensorMap p1, q1, p2, q2;
+  CUtensorMap c;  // BF16 output [rows, cols], boxes of 32 rows x 64 columns (TMA stores)
 };
 
 template <int kMB, int kBN, int kStages, int kAcc, int kEpi, int kRed, int kWF = kWBf16>
@@ -358,7 +362,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
   uint8_t* raw = smem + kStages * C::kStageBytes;  // quantized weight ring (kWF 1, 2)
   uint8_t* sfr = raw + kStages * C::kRawBytes;      // scale-atom ring (kWF 3)
   uint8_t* asr = sfr + kStages * C::kSfBytes;       // activation-scale ring (kWF 4)
-  uint64_t* full = reinterpret_cast<uint64_t*>(asr + kStages * C::kAscBytes);
+  uint8_t* outst = asr + kStages * C::kAscBytes;  // output staging (kOutStage bytes, 1 KiB aligned)
+  uint64_t* full = reinterpret_cast<uint64_t*>(outst + C::kOutStage);
   uint64_t* empty = full + kStages;
   uint64_t* rawfull = empty + kStages;
   uint64_t* tfull = rawfull + kStages;
@@ -922,7 +927,80 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         }
       };
 
-      if (kEpi == kEpiSwiGLU) {
+      // Rows mapping, BF16 output through this warp's 32 x 64 staging box and a TMA store: the
+      // thread of row r writes its 16 values of columns c1 .. c1 + 15 as two 16-byte chunks into
+      // the 128-byte-swizzled box; `flush` stores the box at output column x, and `reuse` waits
+      // until the previous box has been read before the box is written again.
+      uint8_t* box = outst + (size_t)q * 4096;
+      auto reuse = [&]() {
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+      };
+      auto stage16 = [&](int c1, const uint32_t (&w)[8]) {
+        const int ch = c1 / 8;
+        *reinterpret_cast<uint4*>(box + lane * 128 + (((ch) ^ (lane & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(box + lane * 128 + (((ch + 1) ^ (lane & 7)) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+      };
+      auto flush = [&](int x) {
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&aux.c, box, x, tp * C::kPRows + q * 32);
+          bulk_commit();
+        }
+      };
+      const bool staged = C::kOutStage > 0 && p.tma_store && !p.swap && !(p.debug & 1);
+      if (kEpi == kEpiSwiGLU && staged) {
+        // Rows mapping: the tile's first kBN/2 columns are gate rows, the rest up rows.
+        for (int c0 = 0; c0 < kBN / 2; c0 += 64) {
+          reuse();
+#pragma unroll
+          for (int c1 = 0; c1 < 64; c1 += 16) {
+            float g[16], v[16];
+            get16(0, c0 + c1, g);
+            get16(0, c0 + c1 + kBN / 2, v);
+            uint32_t w[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              w[t] = pack_bf16x2(silu_bf16_times(g[2 * t], v[2 * t]), silu_bf16_times(g[2 * t + 1], v[2 * t + 1]));
+            stage16(c1, w);
+          }
+          flush(tq * (kBN / 2) + c0);
+        }
+      } else if (kEpi == kEpiBf16 && staged && kMB == 1 && kBN % 64 == 0 &&
+                 (p.res == nullptr ||
+                  ((tq + 1) * kBN <= p.out_cols && (reinterpret_cast<uintptr_t>(p.res) & 15) == 0 && (p.ldr & 7) == 0))) {
+        // Rows mapping, BF16 output (o_proj and down_proj at one chip add the residual: 64 of its
+        // columns load with eight 16-byte loads in flight before the accumulator columns are read).
+        const int i = tp * C::kPRows + lrow;
+        const bool in = i < p.out_rows;
+        for (int c0 = 0; c0 < kBN; c0 += 64) {
+          const int j0 = tq * kBN + c0;
+          uint4 rr[8];
+          if (p.res != nullptr) {
+            const uint4* rsrc = reinterpret_cast<const uint4*>(p.res + (long)i * p.ldr + j0);
+#pragma unroll
+            for (int qq = 0; qq < 8; ++qq) rr[qq] = in ? __ldcs(rsrc + qq) : make_uint4(0, 0, 0, 0);
+          } else {
+#pragma unroll
+            for (int qq = 0; qq < 8; ++qq) rr[qq] = make_uint4(0, 0, 0, 0);
+          }
+          reuse();
+#pragma unroll
+          for (int c1 = 0; c1 < 64; c1 += 16) {
+            float v[16];
+            get16(0, c0 + c1, v);
+            const uint32_t rw[8] = {rr[c1 / 8].x, rr[c1 / 8].y, rr[c1 / 8].z, rr[c1 / 8].w,
+                                    rr[c1 / 8 + 1].x, rr[c1 / 8 + 1].y, rr[c1 / 8 + 1].z, rr[c1 / 8 + 1].w};
+            uint32_t w[8];
+#pragma unroll
+            for (int t = 0; t < 8; ++t)
+              w[t] = pack_bf16x2(v[2 * t] + __uint_as_float(rw[t] << 16), v[2 * t + 1] + __uint_as_float(rw[t] & 0xFFFF0000u));
+            stage16(c1, w);
+          }
+          flush(j0);
+        }
+      } else if (kEpi == kEpiSwiGLU) {
         if (!p.swap) {
           // Rows mapping: the tile's first kBN/2 columns are gate rows, the rest up rows.
           const int row = tp * C::kPRows + lrow;
@@ -997,6 +1075,7 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         mbar_arrive(tempty + b);
       }
     }
+    if (lane == 0) bulk_wait_all();  // the output boxes stored by TMA have landed
     if (lrow == 0) mark(p, 6);
   }
 
@@ -1153,7 +1232,8 @@ struct Shape {
   static constexpr int kRaw = (kMB * 128 > kBN ? kMB * 128 : kBN) * (kWF == 1 ? 64 : kWF == 2 ? 32 : 0);
   static constexpr int kSfGroups = kWF == 3 ? kMB + (kBN + 127) / 128 : 0;
   static constexpr int kAsc = kWF == 4 ? 4 * (kBN > 128 ? kBN : 128) + 16 * kMB : 0;
-  static constexpr int kFit = (220 * 1024 - 2048) / (kStage + kRaw + kSfGroups * 2048 + kAsc);
+  static constexpr int kOut = (kWF == 0 && kMB == 1) ? 4 * 4096 : 0;  // output staging (Cfg::kOutStage)
+  static constexpr int kFit = (220 * 1024 - 2048 - kOut) / (kStage + kRaw + kSfGroups * 2048 + kAsc);
   static constexpr int kStages = kFit > 8 ? 8 : kFit;
   // W8A8 keeps up to eight per-block partial sums in flight so the MMAs run ahead of the scaling.
   static constexpr int kAccW8 = 512 / (kMB * kBN) > 8 ? 8 : 512 / (kMB * kBN);
@@ -1165,7 +1245,8 @@ int swap_ring_bytes(int mb, int kbn, int wf) {
   const int stage = 128 * mb * 128 + kbn * 128;
   const int raw = (mb * 128 > kbn ? mb * 128 : kbn) * (wf == 1 ? 64 : wf == 2 ? 32 : 0);
   const int sf = wf == 3 ? (mb + (kbn + 127) / 128) * 2048 : wf == 4 ? 4 * std::max(kbn, 128) + 16 * mb : 0;
-  int stages = (220 * 1024 - 2048) / (stage + raw + sf);
+  const int out = (wf == 0 && mb == 1) ? 4 * 4096 : 0;
+  int stages = (220 * 1024 - 2048 - out) / (stage + raw + sf);
   if (stages > 8) stages = 8;
   return stage * stages;
 }
@@ -1185,6 +1266,9 @@ Plan make_plan(const GemmArgs& a, int num_sms, size_t ws_bytes, int counters_len
   if (!swap) {
     pl.mb = 1;
     pl.kbn = a.w_format == kWFp8A8 ? 128 : 256;  // W8A8 sums a tile row in registers
+    // (128-column BF16 tiles against wave quantization measured slower: down_proj of 8192 rows
+    // 183 -> 214 us.)
+
     pl.tiles_p = (a.M + 127) / 128;
     pl.tiles_q = (a.N + pl.kbn - 1) / pl.kbn;
   } else {
@@ -1591,6 +1675,14 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     if (!encode_tmap_2d(&tw.w, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, a.w, a.N, row_bytes, ld_bytes,
                         wrows_box, box_bytes, CU_TENSOR_MAP_SWIZZLE_NONE))
       return -4;
+  }
+  // Rows mapping with BF16 weights: BF16 outputs leave through shared memory as TMA stores of
+  // 32 x 64 boxes (whole 128-byte row segments instead of one 16-byte store a row and a thread).
+  kp.tma_store = 0;
+  if (!pl.swap && a.w_format == kWBf16 && (a.epilogue == kEpiBf16 || a.epilogue == kEpiSwiGLU) && a.debug == 0 &&
+      a.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15) == 0) {
+    const long out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
+    if (encode_tmap_bf16_kmajor(&tw.c, a.c, a.M, out_cols, a.ldc, 32)) kp.tma_store = 1;
   }
   // Operand maps: BF16 rows of 64 elements, or packed E2M1 rows of 128 bytes (256 elements).
   auto operand = [&](CUtensorMap* m, const void* base, long rows, long ld, int box) {

@@ -42,9 +42,10 @@ void bind_ops(py::module_& m) {
          int w_format, uint64_t w_scale, long w_scale_ld, float w_tensor_scale, uint64_t a_scale,
          long a_scale_ld, uint64_t group_tiles, uint64_t tile_group, int group_tile, int groups,
          int w_scale_rows, const std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>& segments,
-         uint64_t cta_trace, int reduction) {
+         uint64_t cta_trace, int reduction, int debug) {
         foa::GemmArgs g;
         g.reduction = reduction;
+        g.debug = debug;
         g.cta_trace = reinterpret_cast<unsigned long long*>(cta_trace);
         g.w_scale_rows = w_scale_rows;
         if (segments.size() > 2) throw std::runtime_error("gemm: at most two extra K segments");
@@ -98,7 +99,7 @@ void bind_ops(py::module_& m) {
       py::arg("a_scale_ld") = 0, py::arg("group_tiles") = 0, py::arg("tile_group") = 0,
       py::arg("group_tile") = 0, py::arg("groups") = 0, py::arg("w_scale_rows") = 128,
       py::arg("segments") = std::vector<std::tuple<uint64_t, long, uint64_t, long, int>>{},
-      py::arg("cta_trace") = 0, py::arg("reduction") = 0);
+      py::arg("cta_trace") = 0, py::arg("reduction") = 0, py::arg("debug") = 0);
 
   m.def(
       "quantize_fp8_rows",

@@ -162,6 +162,7 @@ def gemm(
     segments: list | None = None,
     cta_trace: torch.Tensor | None = None,
     reduction: int = 0,
+    debug: int = 0,
 ) -> torch.Tensor:
     """``epilogue(a @ w.T)`` on the tcgen05 GEMM: a [M, K] BF16, w [N, K] BF16.
 
@@ -173,7 +174,8 @@ def gemm(
     ``segments`` [(a1 [M, k1], w1 [N, k1]), ...] (at most two, k a multiple of 64) add
     ``a1 @ w1.T`` and so on into the same FP32 sums before the epilogue (LoRA updates).
     ``trace`` (int64 [8]) and ``cta_trace`` (int64 [4 x CTAs]) receive global-timer milestones.
-    ``reduction`` (measurements) makes split-K partials meet in global scratch (1) or the cluster (2).
+    ``reduction`` (measurements) makes split-K partials meet in global scratch (1) or the cluster (2);
+    ``debug`` (measurements) leaves out the output stores (1) and the accumulator reads (2).
     """
     _rowmajor(a, "a")
     M, K = a.shape
@@ -224,7 +226,7 @@ def gemm(
         s.counters.data_ptr(), s.counters.numel(), s.status.data_ptr(), _stream(),
         0 if trace is None else trace.data_ptr(), **qargs,
         segments=[(sa.data_ptr(), sa.stride(0), sw.data_ptr(), sw.stride(0), sa.shape[1]) for sa, sw in (segments or [])],
-        cta_trace=0 if cta_trace is None else cta_trace.data_ptr(), reduction=reduction,
+        cta_trace=0 if cta_trace is None else cta_trace.data_ptr(), reduction=reduction, debug=debug,
     )
     return out
 

@@ -64,7 +64,8 @@ def gemm(args) -> dict:
     epi = {"bf16": ops.EPI_BF16, "f32": ops.EPI_F32, "swiglu": ops.EPI_SWIGLU}[args.epilogue]
     out = {}
     if copies == 1:
-        us = _time(lambda: ops.gemm(a, ws[0], epilogue=epi, splits=args.splits, reduction=args.reduction),
+        us = _time(lambda: ops.gemm(a, ws[0], epilogue=epi, splits=args.splits, reduction=args.reduction,
+                                    debug=args.debug, mode=args.mode),
                    args.warmup, args.iters)
     else:
         # Two traced launches in the middle of the loop: launch `mid` and the one after it.
@@ -77,7 +78,8 @@ def gemm(args) -> dict:
                     torch.matmul(a, w.t())  # the library reference point (BF16 only)
                     continue
                 t = tr[i - mid] if trace and i in (mid, mid + 1) else None
-                ops.gemm(a, w, epilogue=epi, splits=args.splits, cta_trace=t, reduction=args.reduction)
+                ops.gemm(a, w, epilogue=epi, splits=args.splits, cta_trace=t, reduction=args.reduction,
+                         debug=args.debug, mode=args.mode)
 
         for _ in range(args.warmup):
             loop()
@@ -264,6 +266,10 @@ def main() -> None:
     g.add_argument("--cta-trace", action="store_true")
     g.add_argument("--graph", action="store_true")
     g.add_argument("--impl", default="engine", choices=["engine", "cublas"])
+    g.add_argument("--mode", type=int, default=0, choices=[0, 1, 2],
+                   help="0: the plan's choice (CUDA-core weight stream up to 8 rows), 1: rows mapping, 2: swap mapping")
+    g.add_argument("--debug", type=int, default=0, choices=[0, 1, 2, 3],
+                   help="leave out the output stores (1), the accumulator reads (2) or both (measurement)")
     g.add_argument("--reduction", type=int, default=0, choices=[0, 1, 2],
                    help="split-K partials meet by the plan's choice (0), global scratch (1) or the cluster (2)")
     d = sub.add_parser("decode-attn")

@@ -155,3 +155,25 @@ def test_small_row_projections_stream_weights(M, N, K):
         g, u = dense.split_gate_up(w)  # 128-row blocks alternate gate and up
         want = reference.swiglu(_ref(a, g), _ref(a, u))
         _close(ops.gemm(a, w, epilogue=ops.EPI_SWIGLU), want)
+
+
+@pytest.mark.parametrize("M,N,K", [(1000, 2048, 512), (777, 1000, 320), (4096, 2048, 1024)])
+def test_gemm_rows_tma_store_with_residual(M, N, K):
+    """Row counts above 256 on the rows mapping, BF16 output through shared memory and TMA stores
+    (partial tiles clipped at the matrix edge), with and without the residual; a second call into
+    a larger output leaves the columns past N untouched."""
+    ops = _ops()
+    a = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.05
+    res = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+    out = ops.gemm(a, w, splits=1)
+    torch.cuda.synchronize()
+    _close(out, _ref(a, w))
+    out = ops.gemm(a, w, residual=res, splits=1)
+    torch.cuda.synchronize()
+    _close(out, _ref(a, w) + res.float())
+    wide = torch.full((M, N + 64), 7.0, device="cuda", dtype=torch.bfloat16)
+    ops.gemm(a, w, residual=res, splits=1, out=wide[:, :N])
+    torch.cuda.synchronize()
+    assert torch.equal(wide[:, :N], out)
+    assert bool((wide[:, N:] == 7.0).all())
