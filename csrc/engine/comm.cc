@@ -167,13 +167,26 @@ void PeerCollectives::moe_combine_norm(int which, const int32_t* pos_all, const 
   if (foa::tp_moe_combine_norm(a, stream) != 0) device_.state()->fail("expert-parallel combine launch failed");
 }
 
-void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
-                               __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) {
+bool PeerCollectives::inline_scatter(int rows) const {
+  const int grid = two_shot(rows) ? (rows + world_ - 1) / world_ : rows;
+  return grid <= foa::kInlineScatterCtas;
+}
+
+int PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+                              __nv_bfloat16* out, int rows, int cols, cudaStream_t stream,
+                              const foa::GemmSplits* splits) {
   if (residual != residual_buffer() || out != hidden_buffer())
     throw DeviceError("tensor-parallel add_norm takes the heap's own buffers");
   if (cols != cols_ || rows > rows_) throw ValueError("call exceeds the tensor-parallel heap");
   if (!connected_) throw DeviceError("tensor-parallel peers are not connected");
-  // The partial the GEMM wrote here goes out to the reducing ranks from every SM ...
+  const bool two = two_shot(rows);
+  // Small calls (decode): each reducer CTA first stores its rows of this rank's partial into the
+  // peers, all CTAs resident at once, which saves the scatter's launch. Larger calls: the
+  // partial goes out from every SM in a scatter kernel, and the reducer behind it polls.
+  const bool inline_scatter = this->inline_scatter(rows);
+  if (splits != nullptr && splits->splits > 1 && !inline_scatter)
+    throw DeviceError("GEMM K splits reach add_norm only in calls whose reducer scatters");
+  if (!inline_scatter) {
   foa::ScatterArgs sc{};
   sc.peers = peers_;
   sc.partial = partial_buffer();
@@ -181,13 +194,15 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   sc.cols = cols;
   sc.rank = rank_;
   sc.world = world_;
-  sc.owner_rows = two_shot(rows) ? (rows + world_ - 1) / world_ : 0;
+  sc.owner_rows = two ? (rows + world_ - 1) / world_ : 0;
   sc.slot_stride = static_cast<long>(slot_rows_) * cols_;
   sc.buf_stride = sc.slot_stride * world_;
   sc.seq = reinterpret_cast<const unsigned int*>(static_cast<char*>(heap_) + off_seq_);
   if (foa::tp_scatter(sc, stream) != 0) device_.state()->fail("tensor-parallel scatter launch failed");
-  // ... while the reducer, launched behind it, polls for what lands.
+  }
   foa::AddNormArgs a{};
+  a.partial = inline_scatter ? partial_buffer() : nullptr;
+  if (inline_scatter && splits != nullptr && splits->splits > 1) a.splits = *splits;
   a.peers = peers_;
   a.epoch = reinterpret_cast<const unsigned long long*>(static_cast<char*>(heap_) + off_epoch_);
   a.arrivals = reinterpret_cast<unsigned int*>(static_cast<char*>(heap_) + off_arrivals_);
@@ -202,12 +217,13 @@ void PeerCollectives::add_norm(__nv_bfloat16* residual, const __nv_bfloat16* wei
   a.rank = rank_;
   a.world = world_;
   a.site = site_++;
-  a.two_shot = two_shot(rows) ? 1 : 0;
+  a.two_shot = two ? 1 : 0;
   a.gather_residual = moe_rows_ > 0 ? 1 : 0;  // the expert combine reads every row's residual
   a.status = status_;
   a.trace = trace_;
   if (foa::tp_add_norm(a, stream) != 0) device_.state()->fail("tensor-parallel add_norm launch failed");
   inject_peer(stream);
+  return inline_scatter ? 1 : 2;
 }
 
 void PeerCollectives::inject_peer(cudaStream_t stream) {

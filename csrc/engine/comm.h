@@ -28,8 +28,10 @@ class PeerCollectives : public Collectives {
   int world() const override { return world_; }
   void begin_call(cudaStream_t stream) override;
   float* partial_buffer() override;
-  void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
-                __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) override;
+  int add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+               __nv_bfloat16* out, int rows, int cols, cudaStream_t stream,
+               const foa::GemmSplits* splits = nullptr) override;
+  bool inline_scatter(int rows) const override;
   void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
               cudaStream_t stream) override;
   __nv_bfloat16* residual_buffer() override;

@@ -711,8 +711,12 @@ struct Launch {
   }
 
   // One projection C = epilogue(A W^T) in the weight's format, with this call's LoRA segments.
+  // `external` (non-null): when the plan splits K (decode rows on the swap mapping), the splits'
+  // FP32 partials stay in the GEMM workspace for the next kernel to add (*external describes them,
+  // splits > 1) and `c` is not written; otherwise *external has one split and the GEMM stores `c`.
   void gemm(const char* gemm_name, const void* a, long lda, const WeightSlot& w, int M, int N, int K, void* c,
-            long ldc, int epi, const void* res, int lora_layer = -1, int lora_module = 0) {
+            long ldc, int epi, const void* res, int lora_layer = -1, int lora_module = 0,
+            foa::GemmSplits* external = nullptr) {
     foa::GemmArgs g;
     // LoRA slots: Z_s = X A_s^T (its rows zeroed outside slot s), added as extra K segments
     // Z_s B_s^T into the projection's FP32 sums.
@@ -808,6 +812,10 @@ struct Launch {
       g.mode = (w.format == foa::kWeightFp8A8 && epi == foa::kEpiSwiGLU) ? foa::kModeSwap : foa::kModeRows;
       g.splits = 1;
     }
+    if (external != nullptr) {
+      *external = foa::gemm_bf16_splits(g);
+      g.external_splits = external->splits > 1 ? 1 : 0;
+    }
     done(foa::gemm_bf16(g, s), gemm_name);
   }
 };
@@ -858,14 +866,16 @@ class AttentionFront final : public Module {
   void forward(Launch& e) const override {
     const std::string p = layer_prefix(l_);
     const int cols = (e.m.qh_l_ + 2 * e.m.kvh_l_) * e.D;
+    // Decode rows: the GEMM's K splits are added by the next kernel as it reads them.
+    foa::GemmSplits sp;
     e.gemm("gemm qkv", e.h, e.H, e.w(p + "qkv"), static_cast<int>(e.T), cols, e.H, e.m.ws_qkv_.data(), cols,
-           foa::kEpiBf16, nullptr, l_, LoraAdapter::kQkv);
+           foa::kEpiBf16, nullptr, l_, LoraAdapter::kQkv, &sp);
     __nv_bfloat16* layer_cache = static_cast<__nv_bfloat16*>(e.cache.layers()[l_].data());
     e.done(foa::qk_norm_rope_cache(bf(e.m.ws_qkv_), cols, static_cast<int>(e.T), e.m.qh_l_, e.m.kvh_l_, e.D,
                                    e.cfg.qk_norm ? e.wp(p + "q_norm") : nullptr,
                                    e.cfg.qk_norm ? e.wp(p + "k_norm") : nullptr, e.cfg.eps, e.op(e.sg.positions),
                                    e.rope, bf(e.m.ws_q_), layer_cache, e.op(e.sg.slots), e.s,
-                                   e.cache.blocks() * 16, e.st->status),
+                                   e.cache.blocks() * 16, e.st->status, sp.splits > 1 ? &sp : nullptr),
            "attention front");
     e.attn.cache = layer_cache;
   }
@@ -917,15 +927,23 @@ class ResidualProjection final : public Module {
     const int K = attention_ ? e.m.qh_l_ * e.D : e.m.inter_l_;
     const int M = static_cast<int>(e.T);
     if (!e.tp()) {
-      e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, e.x, e.H, foa::kEpiBf16, e.x, l_, lora_);
-      e.done(foa::rmsnorm(e.x, e.H, nullptr, 0, e.wp(norm_), e.h, e.H, nullptr, 0, M, e.H, e.cfg.eps, e.s),
-             "rmsnorm");
+      // Decode rows: the norm adds the GEMM's K splits and the residual as it reads them.
+      foa::GemmSplits sp;
+      e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, e.x, e.H, foa::kEpiBf16, e.x, l_, lora_, &sp);
+      if (sp.splits > 1)
+        e.done(foa::rmsnorm_splits(sp, e.x, e.H, e.wp(norm_), e.h, e.H, M, e.H, e.cfg.eps, e.s), "rmsnorm");
+      else
+        e.done(foa::rmsnorm(e.x, e.H, nullptr, 0, e.wp(norm_), e.h, e.H, nullptr, 0, M, e.H, e.cfg.eps, e.s),
+               "rmsnorm");
       return;
     }
+    // Decode rows: the reducer adds the GEMM's K splits as it scatters them to the peers.
+    foa::GemmSplits sp;
+    const bool inline_scatter = e.m.coll_->inline_scatter(M);
     e.gemm(trace_, a, K, e.w(weight_), M, e.H, K, e.m.coll_->partial_buffer(), e.H, foa::kEpiF32, nullptr, l_,
-           lora_);
-    e.m.coll_->add_norm(e.x, e.wp(norm_), e.cfg.eps, e.h, M, e.H, e.s);
-    e.done(0, "tp scatter");
+           lora_, inline_scatter ? &sp : nullptr);
+    if (e.m.coll_->add_norm(e.x, e.wp(norm_), e.cfg.eps, e.h, M, e.H, e.s, sp.splits > 1 ? &sp : nullptr) > 1)
+      e.done(0, "tp scatter");
     e.done(0, "tp add_norm");
   }
   std::string name() const override {

@@ -76,9 +76,16 @@ class Collectives {
   virtual float* partial_buffer() = 0;
   // Sums every rank's FP32 partial [rows, cols] (written to partial_buffer) in rank order, adds
   // the BF16 residual (updated in place, rounded once) and writes RMSNorm(residual) * weight to
-  // `out` on every rank. Launches two kernels: the partial's scatter to the peers and the reducer.
-  virtual void add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
-                        __nv_bfloat16* out, int rows, int cols, cudaStream_t stream) = 0;
+  // `out` on every rank. Returns the kernels it launched: the reducer, which scatters the partial
+  // itself in small calls, or the partial's scatter to the peers and then the reducer. `splits`
+  // (small calls only, see inline_scatter): the partial is the sum of a GEMM's K splits left in
+  // its workspace, added in split order by the reducer as it scatters them.
+  virtual int add_norm(__nv_bfloat16* residual, const __nv_bfloat16* weight, float eps,
+                       __nv_bfloat16* out, int rows, int cols, cudaStream_t stream,
+                       const foa::GemmSplits* splits = nullptr) = 0;
+  // Whether add_norm of `rows` rows scatters the partial from the reducer itself (and so may take
+  // a GEMM's K splits in place of the partial).
+  virtual bool inline_scatter(int rows) const = 0;
   // The first maximum over ranks of (value, token) candidates [rows]: tokens into `out`.
   virtual void argmax(const float* value, const int32_t* index, int rows, int32_t* out,
                       cudaStream_t stream) = 0;

@@ -5,7 +5,9 @@
 // all-gather joins parts in chip order (gather.rs:17-99). Here the row-parallel GEMM writes its FP32
 // partial into this rank's memory at full speed; a scatter kernel on every SM then stores it over
 // NVLink into the receive buffers of the reducing ranks, and the reducer (launched while the
-// scatter runs) adds the landed partials in rank order, so every rank computes the same bits; the
+// scatter runs) adds the landed partials in rank order, so every rank computes the same bits (in
+// small calls, whose reducer CTAs are all resident at once, each reducer CTA first stores its own
+// rows to the peers, with no scatter launch); the
 // sum is fused with the residual add (one rounding) and the RMSNorm that follows. Small calls push
 // every row to every rank (one-shot: one NVLink hop, no barrier); large calls push each row to the
 // rank that owns its slice (reduce-scatter), and the owner stores the normed rows into every rank
@@ -111,12 +113,51 @@ __device__ __forceinline__ bool unwritten(const float4& v) {
 // partials themselves are polled for, so this kernel does not wait for the scatter to finish.
 template <int kVec>
 __global__ void __launch_bounds__(256) tp_add_norm_kernel(const AddNormArgs a) {
+  if (a.partial != nullptr) pdl_wait();  // inline scatter: this rank's partial is complete
   pdl_trigger();
   __shared__ float red[8];
   const int rs = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
   const int slot_row = blockIdx.x;
   const int row = a.two_shot ? a.rank * rs + slot_row : slot_row;
-  float* recv = a.recv + (long)(__ldcg(a.seq) & 1u) * a.buf_stride + (long)slot_row * a.cols;
+  const unsigned int parity = __ldcg(a.seq) & 1u;
+  if (a.partial != nullptr) {
+    // Every rank's CTA `slot_row` reduces slot row `slot_row`: store this rank's rows of it there
+    // (one-shot: row slot_row to every rank; two-shot: row q * rs + slot_row to rank q), -0.0 as
+    // +0.0 so the unwritten mark stays unambiguous.
+    const long off = (long)parity * a.buf_stride + (long)a.rank * a.slot_stride + (long)slot_row * a.cols;
+    for (int q = 0; q < a.world; ++q) {
+      const int src_row = a.two_shot ? q * rs + slot_row : slot_row;
+      if (src_row >= a.rows) continue;
+      const float4* src = reinterpret_cast<const float4*>(a.partial + (long)src_row * a.cols);
+      float4* dst = reinterpret_cast<float4*>(a.peers.recv[q] + off);
+      for (int v = threadIdx.x; v < a.cols / 4; v += blockDim.x) {
+        float4 x;
+        if (a.splits.splits > 1) {
+          // The GEMM's K splits, added in split order (what its reduction would have stored); the
+          // loads all go out first.
+          float4 p[GemmSplits::kMax];
+#pragma unroll
+          for (int s = 0; s < GemmSplits::kMax; ++s)
+            if (s < a.splits.splits)
+              p[s] = __ldcg(reinterpret_cast<const float4*>(a.splits.ws + a.splits.at(s, src_row, 4L * v)));
+          x = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int s = 0; s < GemmSplits::kMax; ++s)
+            if (s < a.splits.splits) {
+              x.x += p[s].x; x.y += p[s].y; x.z += p[s].z; x.w += p[s].w;
+            }
+        } else {
+          x = __ldcg(src + v);
+        }
+        x.x = __float_as_uint(x.x) == kUnwritten ? 0.f : x.x;
+        x.y = __float_as_uint(x.y) == kUnwritten ? 0.f : x.y;
+        x.z = __float_as_uint(x.z) == kUnwritten ? 0.f : x.z;
+        x.w = __float_as_uint(x.w) == kUnwritten ? 0.f : x.w;
+        dst[v] = x;
+      }
+    }
+  }
+  float* recv = a.recv + (long)parity * a.buf_stride + (long)slot_row * a.cols;
   const int nvec = a.cols / 8;
   const bool tracer = a.trace != nullptr && blockIdx.x == 0 && threadIdx.x == 0;
   if (tracer) a.trace[0] = global_ns();
@@ -416,6 +457,8 @@ int tp_add_norm(const AddNormArgs& a, cudaStream_t stream) {
   if (a.world < 1 || a.world > kMaxRanks || a.cols % 8 != 0) return -2;
   const int vec = (a.cols / 8 + 255) / 256;
   const int grid = a.two_shot ? (a.rows + a.world - 1) / a.world : a.rows;
+  if (a.partial != nullptr && (grid > kInlineScatterCtas || a.cols % 4 != 0 || a.splits.splits > GemmSplits::kMax))
+    return -2;
   cudaError_t e;
   switch (vec) {
     case 1: e = launch_pdl(tp_add_norm_kernel<1>, dim3(grid), dim3(256), 0, stream, a); break;

@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "gemm.cuh"
+
 namespace foa {
 
 constexpr int kMaxRanks = 8;
@@ -48,7 +50,18 @@ struct AddNormArgs {
   // Optional: CTA 0 writes %globaltimer here at entry (after the grid dependency wait), once its
   // row's partials have all landed, and at exit.
   unsigned long long* trace;
+  // Small calls (the grid at most kInlineScatterCtas CTAs): this rank's FP32 partial [rows, cols],
+  // which each CTA first stores into the receive slots of the rows it reduces on every rank (the
+  // scatter of tp_scatter, without its launch). Null: the partials arrive from tp_scatter.
+  const float* partial;
+  // With `partial` and splits.splits > 1: this rank's partial is the sum, in split order, of a
+  // GEMM's K splits in its workspace (GemmSplits layout); `partial` is then not read.
+  GemmSplits splits;
 };
+
+// The largest grid whose CTAs push their own rows before polling (they must all be resident, on
+// every rank, at once).
+constexpr int kInlineScatterCtas = 148;
 
 // residual = bf16(sum over ranks in rank order of partial + residual); hidden = RMSNorm(residual)
 // * weight; every rank ends with the same hidden rows, and with the same residual rows where it

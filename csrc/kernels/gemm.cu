@@ -50,6 +50,7 @@ struct KParams {
   int units;                  // tiles * splits
   int swap;                   // 1: C[j, i] (N-side rows are output rows)
   int tma_store;              // rows mapping, BF16 output through shared memory and TMA stores
+  int external;               // split partials stay in ws for the next kernel (GemmSplits layout)
   void* c;
   long ldc;
   const __nv_bfloat16* res;
@@ -888,6 +889,20 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
       };
       if (kRed == kRedCluster) continue;  // pushed after the cluster barrier below
       bool from_ws = false;
+      if (kRed == kRedGlobal && p.splits > 1 && p.external) {
+        // The next kernel adds the splits: store this split's partial and take the next unit.
+#pragma unroll 1
+        for (int mb = 0; mb < kMB; ++mb)
+          for (int c0 = 0; c0 < kBN; c0 += 16) {
+            float v[16];
+            tmem16(mb, c0, v);
+#pragma unroll
+            for (int t = 0; t < 16; ++t) __stcg(ws_at(split, mb, c0 + t), v[t]);
+          }
+        tc_fence_before();
+        mbar_arrive(tempty + b);
+        continue;
+      }
       if (kRed == kRedGlobal && p.splits > 1) {
         for (int mb = 0; mb < kMB; ++mb)
           for (int c0 = 0; c0 < kBN; c0 += 16) {
@@ -927,8 +942,8 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
         }
       };
 
-      // Rows mapping, BF16 output through this warp's 32 x 64 staging box and a TMA store: the
-      // thread of row r writes its 16 values of columns c1 .. c1 + 15 as two 16-byte chunks into
+      // Rows mapping, output through this warp's staging box (32 rows of 128 bytes: 64 BF16 or 32
+      // FP32 values) and a TMA store: the thread of row r writes its values as 16-byte chunks into
       // the 128-byte-swizzled box; `flush` stores the box at output column x, and `reuse` waits
       // until the previous box has been read before the box is written again.
       uint8_t* box = outst + (size_t)q * 4096;
@@ -966,6 +981,23 @@ __global__ void __launch_bounds__((Cfg<kMB, kBN, kStages, kAcc, kWF>::kThreadsCt
             stage16(c1, w);
           }
           flush(tq * (kBN / 2) + c0);
+        }
+      } else if (kEpi == kEpiF32 && staged && kMB == 1 && kBN % 32 == 0) {
+        // Rows mapping, FP32 output (a tensor-parallel partial): 32 x 32 boxes of 128-byte rows.
+        for (int c0 = 0; c0 < kBN; c0 += 32) {
+          reuse();
+#pragma unroll
+          for (int c1 = 0; c1 < 32; c1 += 16) {
+            float v[16];
+            get16(0, c0 + c1, v);
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const int ch = c1 / 4 + t;
+              *reinterpret_cast<float4*>(box + lane * 128 + ((ch ^ (lane & 7)) << 4)) =
+                  make_float4(v[4 * t], v[4 * t + 1], v[4 * t + 2], v[4 * t + 3]);
+            }
+          }
+          flush(tq * kBN + c0);
         }
       } else if (kEpi == kEpiBf16 && staged && kMB == 1 && kBN % 64 == 0 &&
                  (p.res == nullptr ||
@@ -1562,6 +1594,32 @@ void gemm_bf16_scratch(const GemmArgs& args, size_t* workspace_bytes, int* count
   *counters = global ? pl.tiles_p * pl.tiles_q : 0;
 }
 
+namespace {
+// The plan of an external-splits GEMM: the split count the plan picks for the shape (before any
+// cluster-residency shrink), every split's partial kept in global scratch.
+bool external_plan(const GemmArgs& a, int sms, Plan* out) {
+  if (a.w_format != kWBf16 || a.epilogue == kEpiSwiGLU || a.group_tiles != nullptr || gemv_applies(a)) return false;
+  Plan pl = make_plan(a, sms, ~size_t(0) >> 1, 1 << 30, nullptr);
+  if (!pl.swap || pl.mb != 1 || pl.splits <= 1) return false;
+  pl.red = 1;
+  pl.grid = std::min(pl.units, sms);
+  *out = pl;
+  return true;
+}
+}  // namespace
+
+GemmSplits gemm_bf16_splits(const GemmArgs& a) {
+  GemmSplits l;
+  l.ws = a.workspace;
+  Plan pl{};
+  if (a.M > 0 && a.N > 0 && a.K > 0 && external_plan(a, a.num_sms > 0 ? a.num_sms : device_sms(), &pl)) {
+    l.splits = pl.splits;
+    l.kbn = pl.kbn;
+    l.tiles_p = pl.tiles_p;
+  }
+  return l;
+}
+
 int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return -2;
   if (a.K % 8 != 0 || a.lda % 8 != 0 || a.ldw % 8 != 0) return -1;
@@ -1608,8 +1666,14 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
 
   const int sms = a.num_sms > 0 ? a.num_sms : device_sms();
   g_cluster_wf = a.w_format;
-  const Plan pl = make_plan(a, sms, a.workspace ? a.workspace_bytes : 0,
-                            a.counters ? a.counters_len : 0);
+  Plan pl{};
+  if (a.external_splits) {
+    // The next kernel adds the splits: they stay in the workspace in the GemmSplits layout.
+    if (!external_plan(a, sms, &pl) || a.workspace == nullptr) return -2;
+    if ((size_t)pl.tiles_p * pl.tiles_q * pl.splits * 128 * pl.kbn * 4 > a.workspace_bytes) return -3;
+  } else {
+    pl = make_plan(a, sms, a.workspace ? a.workspace_bytes : 0, a.counters ? a.counters_len : 0);
+  }
 
   KParams kp{};
   kp.tiles_p = pl.tiles_p;
@@ -1629,6 +1693,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   kp.trace = a.trace;
   kp.cta_trace = a.cta_trace;
   kp.debug = a.debug;
+  kp.external = a.external_splits ? 1 : 0;
   kp.out_rows = a.M;
   kp.out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
   kp.wscale = a.w_scale;
@@ -1659,7 +1724,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
     kp.ascale = static_cast<const float*>(a.a_scale);
     kp.ascale_ld = a.a_scale_ld;
   }
-  if (pl.red == 1 && (a.workspace == nullptr || a.counters == nullptr)) return -3;
+  if (pl.red == 1 && (a.workspace == nullptr || (a.counters == nullptr && !a.external_splits))) return -3;
 
   CUtensorMap tp, tq;
   AuxMaps tw;
@@ -1679,10 +1744,16 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   // Rows mapping with BF16 weights: BF16 outputs leave through shared memory as TMA stores of
   // 32 x 64 boxes (whole 128-byte row segments instead of one 16-byte store a row and a thread).
   kp.tma_store = 0;
-  if (!pl.swap && a.w_format == kWBf16 && (a.epilogue == kEpiBf16 || a.epilogue == kEpiSwiGLU) && a.debug == 0 &&
-      a.ldc % 8 == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15) == 0) {
-    const long out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
-    if (encode_tmap_bf16_kmajor(&tw.c, a.c, a.M, out_cols, a.ldc, 32)) kp.tma_store = 1;
+  if (!pl.swap && a.w_format == kWBf16 && a.debug == 0 && (reinterpret_cast<uintptr_t>(a.c) & 15) == 0) {
+    if ((a.epilogue == kEpiBf16 || a.epilogue == kEpiSwiGLU) && a.ldc % 8 == 0) {
+      const long out_cols = a.epilogue == kEpiSwiGLU ? a.N / 2 : a.N;
+      if (encode_tmap_bf16_kmajor(&tw.c, a.c, a.M, out_cols, a.ldc, 32)) kp.tma_store = 1;
+    } else if (a.epilogue == kEpiF32 && a.ldc % 4 == 0) {
+      // FP32 rows of 32 elements (128 bytes) a box, 32 rows.
+      if (encode_tmap_2d(&tw.c, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, a.c, a.M, a.N, a.ldc, 32, 32,
+                         CU_TENSOR_MAP_SWIZZLE_128B))
+        kp.tma_store = 1;
+    }
   }
   // Operand maps: BF16 rows of 64 elements, or packed E2M1 rows of 128 bytes (256 elements).
   auto operand = [&](CUtensorMap* m, const void* base, long rows, long ld, int box) {

@@ -44,6 +44,9 @@ struct GemmArgs {
   int epilogue = kEpiBf16;
   int mode = kModeAuto;
   int splits = 0;  // K splits; 0 chooses
+  // Swap mapping, splits > 1, BF16 weights: the K splits' FP32 partials stay in `workspace` for the
+  // next kernel to add (GemmSplits describes where); the GEMM neither reduces nor writes `c`.
+  int external_splits = 0;
   // Scratch for split-K partial sums: FP32 partials and one arrival counter per output tile.
   // The counters must be zero before the first launch; every launch leaves them zero.
   float* workspace = nullptr;
@@ -115,11 +118,28 @@ enum GemmWeightFormat : int {
 // -4 tensor-map encoding failed, -5 launch failed.
 int gemm_bf16(const GemmArgs& args, cudaStream_t stream);
 
-// Projections of at most 8 rows of BF16 weights (mode and splits left to the plan, no extra K
+// Projections of one row (K <= 4096, N <= 16384) of BF16 weights (mode and splits left to the plan, no extra K
 // segment, no group, an unquantized weight): `gemm_bf16` runs them as a weight stream on the CUDA
 // cores (gemv.cu), whose FP32 sums run in another order than the tensor-core GEMM's.
 bool gemv_applies(const GemmArgs& args);
 int gemv_bf16(const GemmArgs& args, cudaStream_t stream);
+
+// Where a GEMM with external_splits leaves its K splits' FP32 partials: the partial of split s,
+// token t (an A row) and feature f (a W row) sits at
+//   ws[((f / 128 + (t / kbn) * tiles_p) * splits + s) * 128 * kbn + (t % kbn) * 128 + f % 128],
+// so a token's 128 features of one split are contiguous.
+struct GemmSplits {
+  static constexpr int kMax = 8;  // the plan splits K at most 8 ways
+  const float* ws = nullptr;
+  int splits = 1, kbn = 0, tiles_p = 0;
+  __host__ __device__ long at(int s, long t, long f) const {
+    return ((f / 128 + (t / kbn) * (long)tiles_p) * splits + s) * 128L * kbn + (t % kbn) * 128 + f % 128;
+  }
+};
+
+// The split layout the plan of `args` (mode and splits as given) would use: splits > 1 only when
+// it runs on the swap mapping with a split K and no weight stream; otherwise splits == 1.
+GemmSplits gemm_bf16_splits(const GemmArgs& args);
 
 // Scratch the launch of `args` needs: FP32 workspace bytes and counter entries.
 void gemm_bf16_scratch(const GemmArgs& args, size_t* workspace_bytes, int* counters);

@@ -11,7 +11,10 @@
 //
 // Set-up: the first call on each device, with that device current, looks up the device address of
 // the scratch array with cudaGetSymbolAddress and keeps it for later calls on that device. Make
-// that first call before capturing any stream into a graph.
+// that first call before capturing any stream into a graph. The address belongs to the device's
+// current context: after cudaDeviceReset (or any teardown of the primary context) the module is
+// loaded again at another address, so a process that resets a device must not call this entry
+// point on that device afterwards (the kept address would be stale).
 //
 // Sharing: every call on a device uses the same scratch array, and the array keeps whatever the
 // last call left in it. Nothing in it has to start at zero: each call writes every partial before

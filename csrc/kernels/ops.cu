@@ -279,13 +279,13 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
 // by the group's heads; a head is kHD / 8 lanes of 8 consecutive elements (16-byte loads and
 // stores), so a warp handles 256 / kHD heads at once; the partner of element j (j + d/2) sits
 // kHD / 16 lanes away.
-template <int kHD>
+template <int kHD, int kPasses>
 __global__ void __launch_bounds__(128) qk_norm_rope_cache_rows_kernel(
     const __nv_bfloat16* __restrict__ qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
     const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float eps,
     const int32_t* __restrict__ positions, const float* __restrict__ inv_freq, float attn_factor,
     __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ cache,
-    const int32_t* __restrict__ slots, long cache_slots, int* status) {
+    const int32_t* __restrict__ slots, long cache_slots, int* status, const GemmSplits sp) {
   constexpr int kLanes = kHD / 8;        // lanes of one head
   constexpr int kPerWarp = 32 / kLanes;  // heads of one warp pass
   constexpr int kHalf = kLanes / 2;      // lane distance of the rotation partner
@@ -312,14 +312,35 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_rows_kernel(
   if (bad_slot && threadIdx.x == 0 && blockIdx.y == 0) record_status(status, kBadIndex);  // nothing of the row is cached
   // blockIdx.y picks the row's group of kGroup heads; a warp takes kPasses passes of kPerWarp
   // heads, with every pass's load issued before the first is processed.
-  constexpr int kPasses = 4;
   constexpr int kGroup = 4 * kPerWarp * kPasses;
   uint4 raws[kPasses];
 #pragma unroll
   for (int ps = 0; ps < kPasses; ++ps) {
     const int head = blockIdx.y * kGroup + (ps * 4 + warp) * kPerWarp + sub;
-    raws[ps] = head < heads ? __ldcs(reinterpret_cast<const uint4*>(qkv + (long)row * ld_qkv + (long)head * kHD) + hl)
-                            : make_uint4(0, 0, 0, 0);
+    if (head >= heads) {
+      raws[ps] = make_uint4(0, 0, 0, 0);
+    } else if (sp.splits > 1) {
+      // The projection's K splits, added in split order and rounded once.
+      float4 p0[GemmSplits::kMax], p1[GemmSplits::kMax];
+#pragma unroll
+      for (int s2 = 0; s2 < GemmSplits::kMax; ++s2)
+        if (s2 < sp.splits) {
+          const float4* src = reinterpret_cast<const float4*>(sp.ws + sp.at(s2, row, (long)head * kHD + hl * 8));
+          p0[s2] = __ldcg(src);
+          p1[s2] = __ldcg(src + 1);
+        }
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s2 = 0; s2 < GemmSplits::kMax; ++s2)
+        if (s2 < sp.splits) {
+          acc[0] += p0[s2].x; acc[1] += p0[s2].y; acc[2] += p0[s2].z; acc[3] += p0[s2].w;
+          acc[4] += p1[s2].x; acc[5] += p1[s2].y; acc[6] += p1[s2].z; acc[7] += p1[s2].w;
+        }
+      raws[ps] = make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
+                            pack_bf16x2(acc[6], acc[7]));
+    } else {
+      raws[ps] = __ldcs(reinterpret_cast<const uint4*>(qkv + (long)row * ld_qkv + (long)head * kHD) + hl);
+    }
   }
 #pragma unroll
   for (int ps = 0; ps < kPasses; ++ps) {
@@ -503,6 +524,91 @@ int gather_rows(const __nv_bfloat16* in, long ldi, const int32_t* rows, int n, _
   return cudaGetLastError() == cudaSuccess ? 0 : -5;
 }
 
+// One CTA of 128 threads per row, as rmsnorm_kernel; each 8-column vector first adds the K
+// splits' FP32 partials (two 16-byte loads a split) and the residual.
+template <int kVec>
+__global__ void __launch_bounds__(128) rmsnorm_splits_kernel(const GemmSplits sp, __nv_bfloat16* x, long ldx,
+                                                             const __nv_bfloat16* __restrict__ weight,
+                                                             __nv_bfloat16* __restrict__ out, long ldo, int cols,
+                                                             float eps) {
+  pdl_wait();
+  pdl_trigger();
+  const int row = blockIdx.x;
+  const int nvec = cols / 8;
+  float h[kVec][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = threadIdx.x + i * 128;
+    if (v < nvec) {
+      // Every split's two 16-byte loads go out before the sum (in split order) starts.
+      float4 p0[GemmSplits::kMax], p1[GemmSplits::kMax];
+#pragma unroll
+      for (int s = 0; s < GemmSplits::kMax; ++s)
+        if (s < sp.splits) {
+          const float4* src = reinterpret_cast<const float4*>(sp.ws + sp.at(s, row, (long)v * 8));
+          p0[s] = __ldcg(src);
+          p1[s] = __ldcg(src + 1);
+        }
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int s = 0; s < GemmSplits::kMax; ++s)
+        if (s < sp.splits) {
+          acc[0] += p0[s].x; acc[1] += p0[s].y; acc[2] += p0[s].z; acc[3] += p0[s].w;
+          acc[4] += p1[s].x; acc[5] += p1[s].y; acc[6] += p1[s].z; acc[7] += p1[s].w;
+        }
+      const uint4 rv = *reinterpret_cast<const uint4*>(x + (long)row * ldx + v * 8);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+      uint32_t packed[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        packed[t] = pack_bf16x2(acc[2 * t] + bf16_lo(rw[t]), acc[2 * t + 1] + bf16_hi(rw[t]));
+        h[i][2 * t] = bf16_lo(packed[t]);
+        h[i][2 * t + 1] = bf16_hi(packed[t]);
+        ss += h[i][2 * t] * h[i][2 * t] + h[i][2 * t + 1] * h[i][2 * t + 1];
+      }
+      *reinterpret_cast<uint4*>(x + (long)row * ldx + v * 8) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  }
+  __shared__ float red[4];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  const float total = red[0] + red[1] + red[2] + red[3];
+  const float inv = rsqrtf(total / (float)cols + eps);
+#pragma unroll
+  for (int i = 0; i < kVec; ++i) {
+    const int v = threadIdx.x + i * 128;
+    if (v < nvec) {
+      const uint4 wv = *reinterpret_cast<const uint4*>(weight + v * 8);
+      const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int t = 0; t < 4; ++t)
+        o[t] = pack_bf16x2(h[i][2 * t] * inv * bf16_lo(ww[t]), h[i][2 * t + 1] * inv * bf16_hi(ww[t]));
+      *reinterpret_cast<uint4*>(out + (long)row * ldo + v * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
+int rmsnorm_splits(const GemmSplits& sp, __nv_bfloat16* x, long ldx, const __nv_bfloat16* weight,
+                   __nv_bfloat16* out, long ldo, int rows, int cols, float eps, cudaStream_t stream) {
+  if (rows <= 0) return 0;
+  if (cols % 8 != 0 || cols > 16384 || sp.ws == nullptr || sp.splits < 1 || sp.splits > GemmSplits::kMax ||
+      sp.kbn <= 0)
+    return -2;
+  const int vec = (cols / 8 + 127) / 128;
+  cudaError_t e;
+  switch (vec) {
+    case 1: e = launch_pdl(rmsnorm_splits_kernel<1>, dim3(rows), dim3(128), 0, stream, sp, x, ldx, weight, out, ldo, cols, eps); break;
+    case 2: e = launch_pdl(rmsnorm_splits_kernel<2>, dim3(rows), dim3(128), 0, stream, sp, x, ldx, weight, out, ldo, cols, eps); break;
+    case 3: case 4: e = launch_pdl(rmsnorm_splits_kernel<4>, dim3(rows), dim3(128), 0, stream, sp, x, ldx, weight, out, ldo, cols, eps); break;
+    case 5: case 6: case 7: case 8: e = launch_pdl(rmsnorm_splits_kernel<8>, dim3(rows), dim3(128), 0, stream, sp, x, ldx, weight, out, ldo, cols, eps); break;
+    default: e = launch_pdl(rmsnorm_splits_kernel<16>, dim3(rows), dim3(128), 0, stream, sp, x, ldx, weight, out, ldo, cols, eps); break;
+  }
+  return e == cudaSuccess ? 0 : -5;
+}
+
 int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, long ldr,
             const __nv_bfloat16* weight, __nv_bfloat16* out, long ldo,
             __nv_bfloat16* residual_out, long ldro, int rows, int cols, float eps,
@@ -569,22 +675,34 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
                        float eps, const int32_t* positions, RopeTable rope,
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slots,
-                       cudaStream_t stream, long cache_slots, int* status) {
+                       cudaStream_t stream, long cache_slots, int* status, const GemmSplits* splits) {
   if (rows <= 0) return 0;
+  GemmSplits sp;
+  if (splits != nullptr && splits->splits > 1) {
+    sp = *splits;
+    if (sp.ws == nullptr || (reinterpret_cast<uintptr_t>(sp.ws) & 15) || head_dim % 8 != 0 ||
+        sp.splits > GemmSplits::kMax)
+      return -2;
+  } else {
+    sp.splits = 0;
+  }
   const bool aligned = ((reinterpret_cast<uintptr_t>(qkv) | reinterpret_cast<uintptr_t>(q_out) |
                          reinterpret_cast<uintptr_t>(cache) | reinterpret_cast<uintptr_t>(q_norm) |
                          reinterpret_cast<uintptr_t>(k_norm)) & 15) == 0 && ld_qkv % 8 == 0;
   if (aligned && (head_dim == 64 || head_dim == 128 || head_dim == 256)) {
     // Row-per-CTA kernel: shared rotation table, 16-byte accesses.
-    const auto kernel = head_dim == 64    ? qk_norm_rope_cache_rows_kernel<64>
-                        : head_dim == 128 ? qk_norm_rope_cache_rows_kernel<128>
-                                          : qk_norm_rope_cache_rows_kernel<256>;
-    const int group = 16 * (256 / head_dim);  // heads of one CTA: 4 warps x 4 passes
+    // Many rows: four passes a warp (more loads in flight); few rows (decode): one pass, more CTAs.
+    const bool many = rows >= 148;
+    const auto kernel = head_dim == 64    ? (many ? qk_norm_rope_cache_rows_kernel<64, 4> : qk_norm_rope_cache_rows_kernel<64, 1>)
+                        : head_dim == 128 ? (many ? qk_norm_rope_cache_rows_kernel<128, 4> : qk_norm_rope_cache_rows_kernel<128, 1>)
+                                          : (many ? qk_norm_rope_cache_rows_kernel<256, 4> : qk_norm_rope_cache_rows_kernel<256, 1>);
+    const int group = (many ? 16 : 4) * (256 / head_dim);  // heads of one CTA: 4 warps x passes
     const int groups = (q_heads + 2 * kv_heads + group - 1) / group;
     return launch_pdl(kernel, dim3(rows, groups), dim3(128), 0, stream, qkv, ld_qkv, rows, q_heads, kv_heads, q_norm,
                       k_norm, eps, positions, rope.inv_freq, rope.attention_factor, q_out, cache, slots,
-                      cache_slots, status) == cudaSuccess ? 0 : -5;
+                      cache_slots, status, sp) == cudaSuccess ? 0 : -5;
   }
+  if (sp.splits > 1) return -2;  // split partials are read by the row kernel only
   const long tasks = (long)rows * (q_heads + 2 * kv_heads);
   const int grid = (int)((tasks + 3) / 4);
   switch (head_dim) {

@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "gemm.cuh"
+
 namespace foa {
 
 // h = x (+ residual), FP32 sum rounded once to BF16 into residual_out (when given);
@@ -15,6 +17,12 @@ int rmsnorm(const __nv_bfloat16* x, long ldx, const __nv_bfloat16* residual, lon
             const __nv_bfloat16* weight, __nv_bfloat16* out, long ldo,
             __nv_bfloat16* residual_out, long ldro, int rows, int cols, float eps,
             cudaStream_t stream);
+
+// x = BF16(sum of the GEMM's K splits in split order (FP32) + x), in place, then
+// out = BF16(x * weight / sqrt(mean(x^2) + eps)): the residual projection's split reduction, its
+// residual add and the norm after it in one kernel (`splits` from gemm_bf16_splits).
+int rmsnorm_splits(const GemmSplits& splits, __nv_bfloat16* x, long ldx, const __nv_bfloat16* weight,
+                   __nv_bfloat16* out, long ldo, int rows, int cols, float eps, cudaStream_t stream);
 
 // out[r, :] = table[ids[r], :] for r < rows, BF16 rows of `cols` elements. Rows of the table
 // outside [row_begin, row_end) (a vocabulary shard) give zeros, and ids are shifted by row_begin.
@@ -52,7 +60,12 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
                        int head_dim, const __nv_bfloat16* q_norm, const __nv_bfloat16* k_norm,
                        float eps, const int32_t* positions, RopeTable rope,
                        __nv_bfloat16* q_out, __nv_bfloat16* cache, const int32_t* slot_mapping,
-                       cudaStream_t stream, long cache_slots = 0, int* status = nullptr);
+                       cudaStream_t stream, long cache_slots = 0, int* status = nullptr,
+                       const GemmSplits* splits = nullptr);
+
+// With `splits` (from gemm_bf16_splits of the q/k/v GEMM, more than one split) the projection is
+// read as the sum of its K splits' FP32 partials in split order, rounded once to BF16 (what the
+// GEMM would have stored), and `qkv` is not read.
 
 // LoRA: zeroes z[r, 0:cols) (row stride ldz) of every row r whose row_slot[r] is not `slot`.
 int lora_mask(__nv_bfloat16* z, long ldz, int rows, int cols, int slot, const int32_t* row_slot,

@@ -240,7 +240,14 @@ void bind_engine(py::module_& m) {
       .def("synchronize", [](const Device& d) {
         py::gil_scoped_release nogil;
         d.synchronize();
-      });
+      })
+      .def("check", [](const Device& d) {
+        // Without waiting: raises when an earlier failure poisoned the device, or when the stream
+        // reports an error (a fault of work already finished); work still running is not waited for.
+        d.state()->check();
+        const cudaError_t e = cudaStreamQuery(d.state()->stream);
+        if (e != cudaSuccess && e != cudaErrorNotReady) d.state()->check_cuda(e, "device health check");
+      }, "Raises when the device failed, without waiting for the work in flight.");
 
   // ---------------------------------------------------------------- buffers / transfers
   py::class_<Transfer>(m, "Transfer", "A submitted copy between a HostBuffer and an HbmBuffer.")

@@ -148,7 +148,11 @@ def _load(worker, source) -> None:
 
 
 def check_health(worker) -> None:
-    """Raises when the worker's engine device failed (its poison makes every later call raise, a
-    synchronization included); a worker that has not opened its device yet is healthy."""
-    if getattr(worker, "engine_device", None) is not None:
-        worker.engine_device.synchronize()
+    """Raises when the worker's engine device failed (its poison makes every later call raise);
+    a worker that has not opened its device yet is healthy. The check does not wait for the steps
+    in flight (`Device.check`): a failure inside them shows at the next check after they end, and
+    a bounded device wait that gives up ends its step with an error, which poisons the device."""
+    device = getattr(worker, "engine_device", None)
+    if device is None:
+        return
+    (device.check if hasattr(device, "check") else device.synchronize)()

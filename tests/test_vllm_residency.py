@@ -94,6 +94,10 @@ def test_health_check_raises_on_a_failed_device():
     w.engine_device = SimpleNamespace(synchronize=lambda: calls.append(1))
     residency.check_health(w)
     assert calls == [1]
+    # A device that can be checked without waiting is not synchronized.
+    w.engine_device = SimpleNamespace(check=lambda: calls.append(2), synchronize=lambda: calls.append(3))
+    residency.check_health(w)
+    assert calls == [1, 2]
 
     def failed():
         raise RuntimeError("the device failed earlier: launch failed")
