@@ -16,12 +16,22 @@ from .request import State
 
 
 class Pending:
-    """A step's sampled tokens, still on the device until `collect()` reads them (once)."""
+    """A step's sampled tokens, still on the device until `collect()` reads them (once; later calls
+    return the same result)."""
 
     def __init__(self, runner: "Runner", order, drafts, kept):
         self.runner, self.order, self.drafts, self.kept = runner, order, drafts, kept
+        self.result = None
 
     def collect(self) -> tuple[list[str], list[list[int]]]:
+        if self.result is not None:
+            return self.result
+        if self in self.runner.uncollected:
+            self.runner.uncollected.remove(self)
+        self.result = self._read()
+        return self.result
+
+    def _read(self) -> tuple[list[str], list[list[int]]]:
         host: dict[int, list[int]] = {}  # one device-to-host read per engine call
         sampled = []
         for rid, d, runs in zip(self.order, self.drafts, self.kept):
@@ -58,6 +68,11 @@ class Runner:
         self.pooling_config = pooling_config
         self.pooled: list = []  # each request's pooled output of the last step (None: not yet)
         self.states: dict[str, State] = {}
+        # Steps whose tokens are still on the device, oldest first. vLLM collects a step before it
+        # issues the second one after it on the driver rank; the other tensor-parallel ranks are
+        # never asked, so a step collects every older step but the newest itself (their tokens
+        # are long complete) and the newest feeds the next step from the device.
+        self.uncollected: list[Pending] = []
 
     # -------------------------------------------------------------------- scheduler bookkeeping
     def update(self, so) -> None:
@@ -99,6 +114,8 @@ class Runner:
         model the tokens are empty and `pooled` holds each request's output."""
         if self.pooling_config is not None:
             return self.pool_step(so)
+        while len(self.uncollected) > 1 or (self.uncollected and collect):
+            self.uncollected[0].collect()
         self.update(so)
         order = list(so.num_scheduled_tokens.keys())
         if not order:
@@ -162,7 +179,10 @@ class Runner:
             # The newest sampled token stays on the device until collected; the next step reads it.
             st.tail = (kept[i][-1][0], kept[i][-1][1] + kept[i][-1][2] - 1) if kept[i] and not d else None
         pending = Pending(self, order, drafts, kept)
-        return pending.collect() if collect else pending
+        if collect:
+            return pending.collect()
+        self.uncollected.append(pending)
+        return pending
 
     def pool_step(self, so) -> tuple[list[str], list[list[int]]]:
         """A step of a pooling model: prompt chunks whose kept rows (hidden values or label

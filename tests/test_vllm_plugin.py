@@ -98,6 +98,7 @@ def _runner(rows):
     r = Runner.__new__(Runner)
     r.engine, r.dec = SimpleNamespace(HostTensor=_FakeEngine.HostTensor), eng.dec
     r.model, r.device, r.cache, r.adapters, r.pooling_config, r.pooled, r.states = eng, None, None, None, None, [], {}
+    r.uncollected = []
     return r, eng
 
 
@@ -128,6 +129,22 @@ def test_runner_keeps_greedy_tokens_on_the_device_until_collected():
     assert runner.states["a"].tokens == [10, 11, 12, 13, 14]
     third = runner.step(_sched(cached=[("a", 4), ("b", 3)], counts={"a": 1, "b": 1}))
     assert third == (["a", "b"], [[15], [24]])
+
+
+def test_runner_of_a_rank_vllm_never_asks_collects_old_steps_itself():
+    """Tensor-parallel ranks other than the driver are never asked for their tokens: each step
+    collects every older step but the newest (whose token feeds it from the device)."""
+    from types import SimpleNamespace
+
+    runner, eng = _runner(rows=4)
+    new = [SimpleNamespace(req_id="a", prompt_token_ids=[10, 11, 12], num_computed_tokens=0, block_ids=([0, 1],))]
+    runner.step(_sched(new=new, counts={"a": 3}), collect=False)
+    for i in range(4):
+        runner.step(_sched(cached=[("a", 3 + i)], counts={"a": 1}), collect=False)
+        assert len(runner.uncollected) <= 2
+    # Every step's token came from the device; the tokens of all but the last two steps are known.
+    assert runner.states["a"].tokens == [10, 11, 12, 13, 14, 15]
+    assert [t.values for _, t, _ in eng.calls[-1]] == [[16]]
 
 
 def test_block_tables_grow_and_resume():
