@@ -279,7 +279,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_kernel(
 // by the group's heads; a head is kHD / 8 lanes of 8 consecutive elements (16-byte loads and
 // stores), so a warp handles 256 / kHD heads at once; the partner of element j (j + d/2) sits
 // kHD / 16 lanes away.
-template <int kHD, int kPasses>
+template <int kHD, int kPasses, bool kSplits>
 __global__ void __launch_bounds__(128) qk_norm_rope_cache_rows_kernel(
     const __nv_bfloat16* __restrict__ qkv, long ld_qkv, int rows, int q_heads, int kv_heads,
     const __nv_bfloat16* __restrict__ q_norm, const __nv_bfloat16* __restrict__ k_norm, float eps,
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(128) qk_norm_rope_cache_rows_kernel(
     const int head = blockIdx.y * kGroup + (ps * 4 + warp) * kPerWarp + sub;
     if (head >= heads) {
       raws[ps] = make_uint4(0, 0, 0, 0);
-    } else if (sp.splits > 1) {
+    } else if constexpr (kSplits) {
       // The projection's K splits, added in split order and rounded once.
       float4 p0[GemmSplits::kMax], p1[GemmSplits::kMax];
 #pragma unroll
@@ -692,10 +692,16 @@ int qk_norm_rope_cache(const __nv_bfloat16* qkv, long ld_qkv, int rows, int q_he
   if (aligned && (head_dim == 64 || head_dim == 128 || head_dim == 256)) {
     // Row-per-CTA kernel: shared rotation table, 16-byte accesses.
     // Many rows: four passes a warp (more loads in flight); few rows (decode): one pass, more CTAs.
-    const bool many = rows >= 148;
-    const auto kernel = head_dim == 64    ? (many ? qk_norm_rope_cache_rows_kernel<64, 4> : qk_norm_rope_cache_rows_kernel<64, 1>)
-                        : head_dim == 128 ? (many ? qk_norm_rope_cache_rows_kernel<128, 4> : qk_norm_rope_cache_rows_kernel<128, 1>)
-                                          : (many ? qk_norm_rope_cache_rows_kernel<256, 4> : qk_norm_rope_cache_rows_kernel<256, 1>);
+    // Only the one-pass form reads GEMM splits (the split partials exist for decode rows only).
+    const bool many = rows >= 148 && sp.splits <= 1;
+    const bool split = sp.splits > 1;
+    const auto kernel =
+        head_dim == 64    ? (many ? qk_norm_rope_cache_rows_kernel<64, 4, false>
+                                  : split ? qk_norm_rope_cache_rows_kernel<64, 1, true> : qk_norm_rope_cache_rows_kernel<64, 1, false>)
+        : head_dim == 128 ? (many ? qk_norm_rope_cache_rows_kernel<128, 4, false>
+                                  : split ? qk_norm_rope_cache_rows_kernel<128, 1, true> : qk_norm_rope_cache_rows_kernel<128, 1, false>)
+                          : (many ? qk_norm_rope_cache_rows_kernel<256, 4, false>
+                                  : split ? qk_norm_rope_cache_rows_kernel<256, 1, true> : qk_norm_rope_cache_rows_kernel<256, 1, false>);
     const int group = (many ? 16 : 4) * (256 / head_dim);  // heads of one CTA: 4 warps x passes
     const int groups = (q_heads + 2 * kv_heads + group - 1) / group;
     return launch_pdl(kernel, dim3(rows, groups), dim3(128), 0, stream, qkv, ld_qkv, rows, q_heads, kv_heads, q_norm,
