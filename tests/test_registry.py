@@ -120,3 +120,23 @@ def test_media_encoder_refuses_odd_widths(tmp_path):
     del broken["vision_config"]["mm_embed_dim"]
     with pytest.raises(ValueError, match="vision_config.mm_embed_dim"):
         engine.LoadOptions().encoder().parse(_ckpt(tmp_path / "b", broken))
+
+
+@pytest.mark.parametrize("name,cls,size", [("mixtral-8x7b", "mixtral.ForCausalLM", "8x7B"),
+                                           ("tiny-mixtral", "mixtral.ForCausalLM", "custom"),
+                                           ("tiny-qwen3-moe", "qwen3_moe.ForCausalLM", "custom")])
+def test_mixture_of_experts_families_load_from_the_config(tmp_path, name, cls, size):
+    """Weightless loads of the mixture-of-experts families: the class, size and precision come from
+    config.json alone."""
+    sel = engine.LoadOptions().select(_ckpt(tmp_path, synthetic.hf_config(configs.get(name))))
+    assert sel["class"] == cls and sel["size"] == size and sel["precision"] == "bfloat16"
+
+
+def test_mixture_of_experts_refusals(tmp_path):
+    base = synthetic.hf_config(configs.get("mixtral-8x7b"))
+    with pytest.raises(NotImplementedError, match="sliding_window"):
+        engine.LoadOptions().parse(_ckpt(tmp_path, dict(base, sliding_window=4096)))
+    # Listed upstream but without an implementation: refused as not served, before any weight.
+    for arch in ("OlmoeForCausalLM", "DeepseekV2ForCausalLM"):
+        with pytest.raises(NotImplementedError, match=f"{arch}: no model type is implemented"):
+            engine.LoadOptions().parse(_ckpt(tmp_path / arch, dict(base, architectures=[arch])))
