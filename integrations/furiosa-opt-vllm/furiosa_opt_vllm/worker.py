@@ -21,12 +21,19 @@ class Collected(AsyncModelRunnerOutput):
     """A greedy step's output whose tokens are still on the device: `get_output` reads them (vLLM
     calls it after issuing the next step, so the device works while the host schedules)."""
 
-    def __init__(self, pending):
-        self.pending = pending
+    def __init__(self, pending, worker=None):
+        self.pending, self.worker = pending, worker
         self.output = ModelRunnerOutput(req_ids=[], req_id_to_index={})  # filled by get_output
 
     def get_output(self) -> ModelRunnerOutput:
-        ids, sampled = self.pending.collect()
+        try:
+            ids, sampled = self.pending.collect()
+        except Exception as error:
+            # vLLM has issued the next step already; it raises this failure, since its requests
+            # lack the tokens this step failed to read.
+            if self.worker is not None:
+                self.worker.failure = error
+            raise
         self.output.req_ids = ids
         self.output.req_id_to_index = {r: i for i, r in enumerate(ids)}
         self.output.sampled_token_ids = sampled
@@ -49,6 +56,7 @@ class Worker(WorkerBase):
         self.pooling = getattr(self.model_config, "runner_type", "generate") == "pooling"
         self.drafts = None  # the drafts proposed after the last step, for take_draft_token_ids
         self.media = None  # media.Media when vLLM runs this instance as a media encoder alone
+        self.failure: BaseException | None = None  # the first step whose tokens could not be read
 
     # ------------------------------------------------------------------------ life cycle
     def init_device(self) -> None:
@@ -252,6 +260,8 @@ class Worker(WorkerBase):
         return get_kv_transfer_group() if has_kv_transfer_group() else None
 
     def execute_model(self, scheduler_output):
+        if self.failure is not None:
+            raise RuntimeError("an earlier step's tokens could not be read") from self.failure
         if self.media is not None:
             return media.execute(self.media, scheduler_output)
         conn = self.connector()
@@ -290,7 +300,7 @@ class Worker(WorkerBase):
             return
         if self.asynchronous():
             # The tokens stay on the device; vLLM collects them after it has issued the next step.
-            self.pending = Collected(self.runner.step(scheduler_output, collect=False))
+            self.pending = Collected(self.runner.step(scheduler_output, collect=False), self)
             return
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},
