@@ -2,9 +2,11 @@
 
 Each rank (one process per GPU) allocates a symmetric heap for the fused collectives, exports it
 as a CUDA IPC handle, and opens every peer's handle after an all-gather over the process group.
-From then on the decoder's row-parallel projections end in a fused kernel that reads the peers'
-FP32 partial sums over NVLink, adds them in rank order with the residual and applies the next
-RMSNorm; the vocabulary-parallel head ends in an exchange of (value, token) candidates.
+From then on each row-parallel projection writes its FP32 partial locally, the partial is stored
+over NVLink into the receive slots of the ranks that reduce it (by a scatter kernel, or in small
+calls by the reducer itself), and the reducer adds the ranks' partials in rank order with the
+residual and applies the next RMSNorm; the vocabulary-parallel head ends in an exchange of
+(value, token) candidates. `emulate.py` runs the same schedule on the host as its oracle.
 """
 
 from __future__ import annotations
