@@ -1624,7 +1624,7 @@ int gemm_bf16(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return -2;
   if (a.K % 8 != 0 || a.lda % 8 != 0 || a.ldw % 8 != 0) return -1;
   if ((reinterpret_cast<uintptr_t>(a.a) & 15) || (reinterpret_cast<uintptr_t>(a.w) & 15)) return -1;
-  // At most 8 rows of BF16 weights: a weight stream without the tensor-core pipeline (gemv.cu).
+  // One row of BF16 weights: a weight stream without the tensor-core pipeline (gemv.cu).
   if (gemv_applies(a)) return gemv_bf16(a, stream);
   if (a.epilogue == kEpiSwiGLU && (a.N % 256 != 0 || a.residual != nullptr)) return -2;
   if (a.epilogue != kEpiF32 && (a.ldc % 8 != 0 || (reinterpret_cast<uintptr_t>(a.c) & 15))) return -1;
