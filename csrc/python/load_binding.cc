@@ -5,6 +5,7 @@
 #include "engine/lora.h"
 #include <pybind11/stl.h>
 
+#include "engine/catalog.h"
 #include "engine/checkpoint.h"
 #include "engine/encoder.h"
 #include "engine/registry.h"
@@ -194,6 +195,25 @@ void bind_checkpoint_and_load(py::module_& m) {
       }, py::arg("checkpoint"), py::arg("device"));
 
   m.def("_architectures", []() { return architecture_names(); });
+  m.def("_catalog_composes", [](const std::string& architecture) { return catalog::composes(architecture); });
+  // The catalog composition of a checkpoint's config (family, module tree, weights and tied
+  // aliases by name and shape), checked strictly against its tensors when `check`.
+  m.def("_catalog", [](const PyCheckpoint& c, bool check) {
+    const catalog::Composition comp = catalog::compose(*c.ck);
+    if (check) catalog::check(comp, *c.ck);
+    auto table = [](const std::vector<catalog::Weight>& ws) {
+      py::dict d;
+      for (const auto& w : ws) d[py::str(w.name)] = py::tuple(py::cast(w.shape));
+      return d;
+    };
+    py::dict out;
+    out["family"] = comp.family;
+    out["architecture"] = comp.architecture;
+    out["tree"] = comp.tree;
+    out["weights"] = table(comp.weights);
+    out["aliases"] = table(comp.aliases);
+    return out;
+  }, py::arg("checkpoint"), py::arg("check") = true);
   // The native checkpoint behind a Checkpoint object (for the engine's own classes).
   m.def("_checkpoint_ptr", [](const PyCheckpoint& c) { return reinterpret_cast<uintptr_t>(c.ck.get()); });
 }

@@ -343,8 +343,6 @@ def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
     safetensors file whose header declares every tensor (offsets as if the data followed) but
     stores no data, for `Checkpoint.declared` (loading checks of models too large to write).
     Returns the declared shapes."""
-    import struct
-
     cfg = configs.get(name_or_cfg) if isinstance(name_or_cfg, str) else name_or_cfg
     os.makedirs(directory, exist_ok=True)
     fmt = cfg.get("weight_format", "bf16")
@@ -363,7 +361,6 @@ def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
         json.dump(conf, f)
     shapes = dict(hf_shapes(cfg))
     dtypes = {name: "BF16" for name in shapes}
-    size = {"BF16": 2, "F32": 4, "F8_E4M3": 1, "U8": 1}
     if fmt != "bf16":
         for name in [n for n in shapes if n.endswith("_proj.weight")]:
             R, C = shapes[name]
@@ -381,15 +378,26 @@ def write_declared(directory: str, name_or_cfg) -> dict[str, tuple[int, ...]]:
                 shapes[base + ".weight_scale"], dtypes[base + ".weight_scale"] = (R, C // 16), "F8_E4M3"
                 for s in ("weight_scale_2", "input_scale"):
                     shapes[f"{base}.{s}"], dtypes[f"{base}.{s}"] = (), "F32"
+    write_headers(directory, shapes, dtypes)
+    return shapes
+
+
+def write_headers(directory: str, shapes: dict, dtypes: dict | None = None) -> None:
+    """Writes `model.safetensors` holding only a header that declares `shapes` (BF16 unless
+    `dtypes` names another type), offsets as if the data followed."""
+    import struct
+
+    size = {"BF16": 2, "F32": 4, "F8_E4M3": 1, "U8": 1}
+    dtypes = dtypes or {}
     header, at = {}, 0
     for name in sorted(shapes):
-        n = size[dtypes[name]]
+        dt = dtypes.get(name, "BF16")
+        n = size[dt]
         for d in shapes[name]:
             n *= d
-        header[name] = {"dtype": dtypes[name], "shape": list(shapes[name]), "data_offsets": [at, at + n]}
+        header[name] = {"dtype": dt, "shape": list(shapes[name]), "data_offsets": [at, at + n]}
         at += n
     raw = json.dumps(header).encode()
     raw += b" " * (-len(raw) % 8)
     with open(os.path.join(directory, "model.safetensors"), "wb") as f:
         f.write(struct.pack("<Q", len(raw)) + raw)
-    return shapes
