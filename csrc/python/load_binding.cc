@@ -196,8 +196,9 @@ void bind_checkpoint_and_load(py::module_& m) {
 
   m.def("_architectures", []() { return architecture_names(); });
   m.def("_catalog_composes", [](const std::string& architecture) { return catalog::composes(architecture); });
-  // The catalog composition of a checkpoint's config (family, module tree, weights and tied
-  // aliases by name and shape), checked strictly against its tensors when `check`.
+  m.def("_catalog_architectures", []() { return catalog::architectures(); });
+  // The catalog composition of a checkpoint's config (family, module tree, weights and optional
+  // weights by name and shape, ignored names), checked strictly against its tensors when `check`.
   m.def("_catalog", [](const PyCheckpoint& c, bool check) {
     const catalog::Composition comp = catalog::compose(*c.ck);
     if (check) catalog::check(comp, *c.ck);
@@ -211,7 +212,8 @@ void bind_checkpoint_and_load(py::module_& m) {
     out["architecture"] = comp.architecture;
     out["tree"] = comp.tree;
     out["weights"] = table(comp.weights);
-    out["aliases"] = table(comp.aliases);
+    out["optional"] = table(comp.optional);
+    out["ignored"] = comp.ignored;
     return out;
   }, py::arg("checkpoint"), py::arg("check") = true);
   // The native checkpoint behind a Checkpoint object (for the engine's own classes).

@@ -1,16 +1,18 @@
 """Catalog compositions: model families that the registry lists but that no kernels serve yet.
 
 Each family is a typed composition built natively from config.json (csrc/engine/catalog.cc): the
-module tree and every weight it reads, by checkpoint name and shape, plus the tied copies a
-checkpoint may hold or leave out. A checkpoint, or only its safetensors headers
+module tree and every weight it reads, by checkpoint name and shape, plus the weights a checkpoint
+may hold or leave out (tied copies, unused parts) and the names nothing reads (old buffers,
+pretraining heads). A checkpoint, or only its safetensors headers
 (`Checkpoint.declared`), is checked strictly against it: a missing, misshaped or unread tensor is
 refused by name. Loading such a model is still refused by the registry (`NotImplementedError`), as
 the reference refuses its catalog families
-(crates/furiosa-opt-models/src/models/{encoder,encoder_decoder,decoder/recurrent}).
+(crates/furiosa-opt-models/src/models/{encoder,encoder_decoder,vision_language,decoder/recurrent,
+decoder/hybrid,decoder/attention}).
 
-Families: BERT (`BertModel`), T5 and mT5 (`T5ForConditionalGeneration`,
-`MT5ForConditionalGeneration`), Whisper (`WhisperForConditionalGeneration`), Mamba-2
-(`Mamba2ForCausalLM`) and Gemma-3 text (`Gemma3ForCausalLM`).
+Families (`architectures()` lists every name): BERT and its classification and masked-LM heads,
+XLM-RoBERTa (BGE-M3, rerankers), CLIP and SigLIP, T5 / mT5, Whisper, Mamba, Mamba-2, Bamba,
+Gemma-3 and Gemma-4 text, OLMoE, DeepSeek-V2, LLaVA, Mllama and Qwen3-VL.
 """
 
 from __future__ import annotations
@@ -24,7 +26,8 @@ class Composition:
     architecture: str
     tree: tuple[str, ...]
     weights: dict[str, tuple[int, ...]]
-    aliases: dict[str, tuple[int, ...]]
+    optional: dict[str, tuple[int, ...]]
+    ignored: tuple[str, ...]
 
     def describe(self) -> str:
         return "\n".join(self.tree)
@@ -45,6 +48,12 @@ def composes(architecture: str) -> bool:
     return bool(_native._catalog_composes(architecture))
 
 
+def architectures() -> list[str]:
+    from furiosa_opt_engine import _native
+
+    return list(_native._catalog_architectures())
+
+
 def compose(checkpoint, check: bool = True) -> Composition:
     """The composition of `checkpoint`'s config (a `furiosa_opt_engine.Checkpoint`), checked
     against its tensors unless `check` is False. Raises ValueError naming the config key or tensor
@@ -52,4 +61,5 @@ def compose(checkpoint, check: bool = True) -> Composition:
     from furiosa_opt_engine import _native
 
     d = _native._catalog(checkpoint, check)
-    return Composition(d["family"], d["architecture"], tuple(d["tree"]), dict(d["weights"]), dict(d["aliases"]))
+    return Composition(d["family"], d["architecture"], tuple(d["tree"]), dict(d["weights"]), dict(d["optional"]),
+                       tuple(d["ignored"]))
