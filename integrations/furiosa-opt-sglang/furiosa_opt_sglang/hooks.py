@@ -47,6 +47,12 @@ def _validate():
     return validate_request
 
 
+def _speculative():
+    from .speculative import create_worker
+
+    return create_worker
+
+
 def _released():
     from .residency import released
 
@@ -65,6 +71,9 @@ HOOKS = (
          "pools over the engine cache"),
     Hook("sglang.srt.managers.scheduler.Scheduler.process_batch_result", "BEFORE", _collect,
          "an overlapped greedy step's tokens are read from the device before SGLang processes it"),
+    Hook("sglang.srt.speculative.spec_info.SpeculativeAlgorithm.create_worker", "REPLACE", _speculative,
+         "SGLang's speculative workers run torch draft models; the engine drafts (n-grams or a draft "
+         "model) and verifies"),
     Hook("sglang.srt.mem_cache.allocation.assign_req_to_token_pool_func", "REPLACE", _assign,
          "the request-to-token table lives in host memory; SGLang's own writer is a device kernel"),
     Hook("sglang.srt.managers.tokenizer_manager.TokenizerManager._validate_one_request", "BEFORE", _validate,

@@ -19,7 +19,8 @@ class Refused(ValueError):
 
 def check(tp_size: int = 1, pp_size: int = 1, dp_size: int = 1, page_size: int = 16,
           speculative: str | None = None, lora: bool = False, attn_cp_size: int = 1,
-          kv_cache_dtype: str = "auto", sampling_backend: str | None = None) -> None:
+          kv_cache_dtype: str = "auto", sampling_backend: str | None = None, draft_model: str | None = None,
+          draft_topk: int | None = None) -> None:
     if pp_size != 1:
         raise Refused("pp_size", "pipeline parallelism is not served; use tensor parallelism")
     if tp_size not in (1, 2, 4, 8):
@@ -27,7 +28,14 @@ def check(tp_size: int = 1, pp_size: int = 1, dp_size: int = 1, page_size: int =
     if attn_cp_size != 1:
         raise Refused("attn_cp_size", "context parallelism is not served")
     if speculative:
-        raise Refused("speculative_algorithm", "speculative decoding is not served")
+        algorithm = str(speculative).upper()
+        if algorithm not in ("NGRAM", "STANDALONE"):
+            raise Refused("speculative_algorithm", f"{speculative}: the engine drafts by n-grams (NGRAM) or with a "
+                          "draft model (STANDALONE); EAGLE and MTP drafts read the target's hidden rows")
+        if algorithm == "STANDALONE" and not draft_model:
+            raise Refused("speculative_draft_model_path", "STANDALONE drafting loads a draft model")
+        if draft_topk not in (None, 1):
+            raise Refused("speculative_eagle_topk", "verification runs one chain of drafts a request")
     if lora:
         raise Refused("enable_lora", "adapters are not served through this plugin")
     if kv_cache_dtype not in ("auto", "bfloat16"):
@@ -66,4 +74,6 @@ class Platform:
               speculative=getattr(args, "speculative_algorithm", None),
               lora=bool(getattr(args, "enable_lora", False)),
               attn_cp_size=getattr(args, "attn_cp_size", 1) or 1,
-              kv_cache_dtype=str(getattr(args, "kv_cache_dtype", "auto")))
+              kv_cache_dtype=str(getattr(args, "kv_cache_dtype", "auto")),
+              draft_model=getattr(args, "speculative_draft_model_path", None),
+              draft_topk=getattr(args, "speculative_eagle_topk", None))

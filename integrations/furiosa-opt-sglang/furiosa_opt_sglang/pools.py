@@ -165,11 +165,17 @@ def bind(model_runner) -> None:
         tensor_parallel.set_group(None)  # SGLang's default process group holds its TP ranks
         opts = opts.chips(tp)
     plan: list = []
+    algorithm = str(getattr(args, "speculative_algorithm", None) or "").upper()
+    # A draft model loads first, so that the target's cache is sized from what it leaves free.
+    draft = opts.load(engine.Checkpoint(args.speculative_draft_model_path), device) if algorithm == "STANDALONE" else None
+
+    def block_bytes_of(spec) -> int:
+        # One block of every layer: each group's layers take a page of their pool's format.
+        return sum(int(spec.pools[g.pool].bytes) * len(g.layers) for g in spec.groups)
 
     def blocks(decoder) -> int:
-        # One block of every layer: each group's layers take a page of their pool's format.
-        spec = decoder.cache
-        block_bytes = sum(int(spec.pools[g.pool].bytes) * len(g.layers) for g in spec.groups)
+        # The draft's cache has the target's block count, so a block costs both.
+        block_bytes = block_bytes_of(decoder.cache) + (block_bytes_of(draft.cache) if draft is not None else 0)
         plan.append(Sizes.plan(int(device.available), int(device.capacity), float(model_runner.mem_fraction_static),
                                max(block_bytes, 1), int(decoder.rows), getattr(args, "max_total_tokens", None),
                                getattr(args, "max_running_requests", None)))
@@ -184,6 +190,13 @@ def bind(model_runner) -> None:
     sizes, storage = plan[-1], served.kv
     model_runner.served = served
     model_runner.engine_runner = Runner(served.model, device, storage)
+    if algorithm:
+        from . import speculative
+
+        width = speculative.width_of(args)
+        proposer = (speculative.ngram_of(args, width) if algorithm == "NGRAM" else
+                    speculative.DraftModel(draft, dec.Cache(draft.cache, sizes.blocks), width - 1))
+        model_runner.engine_runner.speculation = speculative.Speculation(proposer, width)
     model_runner.max_total_num_tokens = sizes.tokens
     model_runner.max_running_requests = sizes.requests
     model_runner.kv_cache_dtype = torch.bfloat16

@@ -17,6 +17,7 @@ class Runner:
         self.engine, self.dec = engine, dec
         self.model, self.device, self.cache = model, device, cache
         self.steps = steps.State()
+        self.speculation = None  # speculative.Speculation when SGLang runs a speculative schedule
 
     def blocks(self, req_to_token, slot: int, positions: int) -> list[int]:
         """The engine blocks of a request-pool row's first `positions` positions."""

@@ -80,6 +80,17 @@ class EmbeddingPoolerOutput:
         self.embeddings = embeddings
 
 
+class BaseSpecWorker:
+    def __init__(self):
+        pass
+
+
+class NgramVerifyInput:
+    def __init__(self, draft_token_num, new_seq_lens, accept_tokens, accept_lens):
+        self.draft_token_num, self.new_seq_lens = draft_token_num, new_seq_lens
+        self.accept_tokens, self.accept_lens = accept_tokens, accept_lens
+
+
 class HookType:
     REPLACE, BEFORE, AFTER, AROUND = "replace", "before", "after", "around"
 
@@ -102,13 +113,15 @@ MODULES = {
     "sglang.srt.mem_cache.pool_host": {"HostKVCache": HostKVCache},
     "sglang.srt.layers.pooler": {"EmbeddingPoolerOutput": EmbeddingPoolerOutput},
     "sglang.srt.plugins.hook_registry": {"HookRegistry": HookRegistry, "HookType": HookType},
+    "sglang.srt.speculative.base_spec_worker": {"BaseSpecWorker": BaseSpecWorker},
+    "sglang.srt.speculative.ngram_info": {"NgramVerifyInput": NgramVerifyInput},
 }
 
 
 def install(monkeypatch) -> None:
     """Puts the stand-in modules (and their parent packages) into sys.modules and clears the
     plugin's caches of classes made over SGLang's, for the duration of one test."""
-    from furiosa_opt_sglang import hicache, pools, steps, worker
+    from furiosa_opt_sglang import hicache, pools, speculative, steps, worker
 
     HookRegistry.installed = []
     for name, members in MODULES.items():
@@ -125,3 +138,4 @@ def install(monkeypatch) -> None:
     monkeypatch.setattr(worker, "_made", {})
     monkeypatch.setattr(pools, "_made", {})
     monkeypatch.setattr(hicache, "_made", {})
+    monkeypatch.setattr(speculative, "_made", {})

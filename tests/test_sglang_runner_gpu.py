@@ -135,3 +135,62 @@ def test_host_tier_round_trip_through_the_engine_cache():
         assert np.array_equal(got[4 * page : 7 * page], data[4 * page : 7 * page])
         assert np.array_equal(got[10 * page : 13 * page], data[4 * page : 7 * page])
         assert np.array_equal(got[: 4 * page], data[: 4 * page])
+
+
+@pytest.mark.parametrize("proposer", ["ngram", "draft_same", "draft_other"])
+def test_speculative_steps_commit_greedy_tokens(proposer):
+    """SGLang's speculative schedule through the engine: n-gram drafts, a draft model equal to the
+    target (every draft accepted) and an unrelated one (most rejected); every committed token is the
+    dense forward's greedy token."""
+    from types import SimpleNamespace
+
+    import furiosa_opt_engine as engine
+    from furiosa_opt_engine import decoder as dec
+    from furiosa_opt_models_b200.models import configs, dense
+    from furiosa_opt_sglang import speculative
+    from furiosa_opt_sglang.runner import Runner
+
+    from test_engine_gpu import _weights
+
+    cfg = configs.get("tiny-qwen3")
+    device = engine.Device(engine.Placement([0], range(8)))
+    model = engine._native._synthetic_decoder(device, cfg, seed=9, std=0.05)
+    runner = Runner(model, device, dec.Cache(model.cache, 64))
+    if proposer == "ngram":
+        propose = speculative.Ngram(k=3)
+    else:
+        draft = engine._native._synthetic_decoder(device, cfg, seed=9 if proposer == "draft_same" else 4, std=0.05)
+        propose = speculative.DraftModel(draft, dec.Cache(draft.cache, 64), k=3)
+    spec = speculative.Speculation(propose, width=4)
+    gen = torch.Generator().manual_seed(6)
+    prompts = [torch.randint(0, cfg["vocab"], (n,), generator=gen).tolist() for n in (12, 35)]
+    prompts[0] = (prompts[0][:6] * 2)  # a repeat for the n-gram drafts to find
+    req_to_token = torch.zeros(2, 256, dtype=torch.int64)
+    req_to_token[0] = torch.arange(5 * 16, 5 * 16 + 256)
+    req_to_token[1] = torch.arange(20 * 16, 20 * 16 + 256)
+    table = req_to_token.tolist()
+    reqs = [SimpleNamespace(rid=str(i), origin_input_ids=p, output_ids=[]) for i, p in enumerate(prompts)]
+    extend = _batch([0, 1], [12, 35], prompts[0] + prompts[1], extend_lens=[12, 35])
+    extend.reqs = reqs
+    first = speculative.forward(runner, spec, extend, table, context=256)
+    for r, t in zip(reqs, first.next_token_ids.view(2, 4)[:, 0].tolist()):
+        r.output_ids.append(int(t))
+    accepted = 0
+    while min(len(r.output_ids) for r in reqs) < 10:
+        b = _batch([0, 1], [len(r.origin_input_ids) + len(r.output_ids) - 1 for r in reqs], [0, 0])
+        b.reqs = reqs
+        result = speculative.forward(runner, spec, b, table, context=256)
+        packed = result.next_token_ids.view(2, 4)
+        for i, r in enumerate(reqs):
+            n = int(result.accept_lens[i])
+            accepted += n - 1
+            r.output_ids += packed[i, :n].tolist()
+    device.synchronize()
+    w = _weights(model)
+    for r in reqs:
+        s = r.origin_input_ids + r.output_ids
+        for i in range(len(r.origin_input_ids), len(s)):
+            logits = dense.forward(w, cfg, torch.tensor(s[:i], dtype=torch.int32))[-1]
+            assert logits[s[i]] >= logits.max() - 1e-2 * max(1.0, abs(logits.max().item()))
+    if proposer == "draft_same":
+        assert accepted > 0

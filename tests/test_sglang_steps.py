@@ -51,9 +51,11 @@ class Decoder:
         self.calls.append([(r.rows[0], r.cached, r.tokens.values.tolist(), r.keep) for r in reqs])
         out = []
         for r in reqs:
+            t = r.tokens.values.tolist()
             if r.keep == "last":
-                t = r.tokens.values.tolist()
                 out.append(next_token(int(t[-1]), r.cached + len(t) - 1))
+            elif r.keep == "all":
+                out += [next_token(int(x), r.cached + i) for i, x in enumerate(t)]
         return Tensor(np.array(out, dtype=np.int32))
 
 
