@@ -1108,9 +1108,241 @@ Composition qwen3_vl(const Json& j, const std::string& arch, const Checkpoint&) 
   return b.c;
 }
 
-// ---- Dispatch --------------------------------------------------------------------------------
+// ---- Diffusion: AutoencoderKL, DiT, FLUX, pipelines -----------------------------------------
+
+void conv(Builder& b, const std::string& p, int64_t out, int64_t in, int64_t k) {
+  b.weight(p + ".weight", {out, in, k, k});
+  b.weight(p + ".bias", {out});
+}
+
+// A ResNet block of the autoencoder: GroupNorm, SiLU, 3x3 convolution, twice; a 1x1 shortcut
+// when the width changes.
+void resnet(Builder& b, const std::string& p, int64_t in, int64_t out) {
+  b.norm(p + "norm1", in, true);
+  conv(b, p + "conv1", out, in, 3);
+  b.norm(p + "norm2", out, true);
+  conv(b, p + "conv2", out, out, 3);
+  if (in != out) conv(b, p + "conv_shortcut", out, in, 1);
+}
+
+// The autoencoder's middle block: a ResNet block, one-head self-attention over the spatial
+// positions (GroupNorm, q/k/v and output projections), a ResNet block.
+void vae_middle(Builder& b, const std::string& p, int64_t c, bool attention) {
+  resnet(b, p + "resnets.0.", c, c);
+  if (attention) {
+    b.norm(p + "attentions.0.group_norm", c, true);
+    for (const char* n : {"to_q", "to_k", "to_v"}) b.linear(p + "attentions.0." + n, c, c, true);
+    b.linear(p + "attentions.0.to_out.0", c, c, true);
+  }
+  resnet(b, p + "resnets.1.", c, c);
+}
+
+// The KL autoencoder of latent diffusion (Stable Diffusion, FLUX): a convolutional encoder to the
+// latent's mean and log-variance, a decoder back to pixels.
+Composition autoencoder_kl(const Json& j, const std::string& arch, const Checkpoint&) {
+  const Config cfg(j, "");
+  const int64_t in = cfg.get("in_channels", 3), out = cfg.get("out_channels", 3), latent = cfg.get("latent_channels", 4),
+                layers = cfg.get("layers_per_block", 1), groups = cfg.get("norm_num_groups", 32);
+  const std::vector<int64_t> widths = cfg.ints("block_out_channels", {64});
+  if (widths.empty()) refuse(cfg.key("block_out_channels") + ": at least one block");
+  for (auto w : widths)
+    if (w <= 0 || w % groups != 0) refuse(cfg.key("block_out_channels") + ": " + str(w) + " channels in groups of " + str(groups));
+  auto types = [&](const char* key, const char* want) {
+    const Json& v = cfg[key];
+    if (v.is_null()) return;
+    if (!v.is_array() || v.size() != widths.size()) refuse(cfg.key(key) + ": one a block");
+    for (const auto& t : v.items())
+      if (!t.is_string() || t.as_string() != want) refuse(cfg.key(key) + ": every block is " + std::string(want));
+  };
+  types("down_block_types", "DownEncoderBlock2D");
+  types("up_block_types", "UpDecoderBlock2D");
+  const bool quant = cfg.flag("use_quant_conv", true), post = cfg.flag("use_post_quant_conv", true),
+             mid_attention = cfg.flag("mid_block_add_attention", true);
+  const int64_t n = static_cast<int64_t>(widths.size()), top = widths.back();
+  Builder b = start("autoencoder_kl", arch);
+  std::string chans;
+  for (auto w : widths) chans += (chans.empty() ? "" : ", ") + str(w);
+  b.nest(arch + " (" + str(latent) + " latent channels, blocks of " + chans + ", " + str(layers) +
+             " ResNet blocks each, GroupNorm " + str(groups) + ")",
+         [&] {
+           b.nest("Encoder (downsampling by " + str(int64_t{1} << (n - 1)) + "; mean and log-variance out)", [&] {
+             conv(b, "encoder.conv_in", widths[0], in, 3);
+             for (int64_t i = 0; i < n; ++i) {
+               const std::string p = "encoder.down_blocks." + str(i) + ".";
+               const int64_t from = i == 0 ? widths[0] : widths[i - 1];
+               for (int64_t r = 0; r < layers; ++r) resnet(b, p + "resnets." + str(r) + ".", r == 0 ? from : widths[i], widths[i]);
+               if (i + 1 < n) conv(b, p + "downsamplers.0.conv", widths[i], widths[i], 3);
+             }
+             vae_middle(b, "encoder.mid_block.", top, mid_attention);
+             b.norm("encoder.conv_norm_out", top, true);
+             conv(b, "encoder.conv_out", 2 * latent, top, 3);
+             if (quant) conv(b, "quant_conv", 2 * latent, 2 * latent, 1);
+           });
+           b.nest("Decoder (upsampling, " + str(layers + 1) + " ResNet blocks a level)", [&] {
+             if (post) conv(b, "post_quant_conv", latent, latent, 1);
+             conv(b, "decoder.conv_in", top, latent, 3);
+             vae_middle(b, "decoder.mid_block.", top, mid_attention);
+             int64_t prev = top;
+             for (int64_t i = 0; i < n; ++i) {
+               const std::string p = "decoder.up_blocks." + str(i) + ".";
+               const int64_t w = widths[n - 1 - i];
+               for (int64_t r = 0; r <= layers; ++r) resnet(b, p + "resnets." + str(r) + ".", r == 0 ? prev : w, w);
+               if (i + 1 < n) conv(b, p + "upsamplers.0.conv", w, w, 3);
+               prev = w;
+             }
+             b.norm("decoder.conv_norm_out", widths[0], true);
+             conv(b, "decoder.conv_out", out, widths[0], 3);
+           });
+         });
+  return b.c;
+}
+
+// A timestep (or guidance) embedding: sinusoidal features of 256, linear, SiLU, linear.
+void timestep_embedder(Builder& b, const std::string& p, int64_t d, int64_t in = 256) {
+  b.linear(p + ".linear_1", d, in, true);
+  b.linear(p + ".linear_2", d, d, true);
+}
+
+// DiT: patch embedding, transformer blocks modulated by the timestep and class (adaLN-Zero, each
+// block with its own embedders), a modulated linear head to the patch's noise and variance.
+Composition dit(const Json& j, const std::string& arch, const Checkpoint&) {
+  const Config cfg(j, "");
+  const std::string norm = cfg.text("norm_type", "ada_norm_zero");
+  if (norm != "ada_norm_zero")
+    refuse(cfg.key("norm_type") + ": " + norm + "; DiT modulates its norms by the timestep and class (ada_norm_zero)");
+  const int64_t heads = cfg.get("num_attention_heads", 16), hd = cfg.get("attention_head_dim", 72),
+                in = cfg.get("in_channels", 4), out = cfg.get("out_channels", in), L = cfg.get("num_layers", 28),
+                patch = cfg.get("patch_size", 2), classes = cfg.get("num_embeds_ada_norm", 1000),
+                sample = cfg.get("sample_size", 32);
+  if (patch <= 0 || sample % patch != 0) refuse(cfg.key("patch_size") + ": does not divide sample_size");
+  const int64_t d = heads * hd, ff = cfg.get("ff_inner_dim", 4 * d);
+  Builder b = start("dit", arch);
+  b.nest(arch + " x " + str(L) + " (" + str(sample) + "x" + str(sample) + " latents in patches of " + str(patch) + ", " +
+             str(heads) + " heads of " + str(hd) + ", " + str(classes) + " classes and a null class)",
+         [&] {
+           conv(b, "pos_embed.proj", d, in, patch);
+           b.ignore("pos_embed.pos_embed");
+           b.leaf("Block: adaLN-Zero (timestep and class embedded, SiLU, linear to 6 modulations), "
+                  "self-attention, tanh-GELU MLP " + str(ff));
+           for (int64_t l = 0; l < L; ++l) {
+             const std::string p = "transformer_blocks." + str(l) + ".";
+             timestep_embedder(b, p + "norm1.emb.timestep_embedder", d);
+             b.weight(p + "norm1.emb.class_embedder.embedding_table", {classes + 1, d});
+             b.linear(p + "norm1.linear", 6 * d, d, true);
+             for (const char* n : {"to_q", "to_k", "to_v"}) b.linear(p + "attn1." + n, d, d, true);
+             b.linear(p + "attn1.to_out.0", d, d, true);
+             b.linear(p + "ff.net.0.proj", ff, d, true);
+             b.linear(p + "ff.net.2", d, ff, true);
+           }
+           b.nest("Head: modulated LayerNorm, linear to " + str(patch) + "x" + str(patch) + "x" + str(out), [&] {
+             b.linear("proj_out_1", 2 * d, d, true);
+             b.linear("proj_out_2", patch * patch * out, d, true);
+           });
+         });
+  return b.c;
+}
+
+// FLUX.1's transformer: double-stream blocks (image and text rows with their own modulations,
+// projections and MLPs, attending jointly with QK RMSNorm and 3-axis RoPE), then single-stream
+// blocks over the joined rows (parallel attention and MLP), a modulated head.
+Composition flux(const Json& j, const std::string& arch, const Checkpoint&) {
+  const Config cfg(j, "");
+  const int64_t heads = cfg.get("num_attention_heads", 24), hd = cfg.get("attention_head_dim", 128),
+                in = cfg.get("in_channels", 64), out = cfg.get("out_channels", in), patch = cfg.get("patch_size", 1),
+                L = cfg.get("num_layers", 19), Ls = cfg.get("num_single_layers", 38),
+                joint = cfg.get("joint_attention_dim", 4096), pooled = cfg.get("pooled_projection_dim", 768);
+  const bool guidance = cfg.flag("guidance_embeds", false);
+  const std::vector<int64_t> axes = cfg.ints("axes_dims_rope", {16, 56, 56});
+  int64_t rope = 0;
+  for (auto a : axes) rope += a;
+  if (rope != hd) refuse(cfg.key("axes_dims_rope") + ": the axes rotate " + str(rope) + " of a head's " + str(hd));
+  const int64_t d = heads * hd, mlp = 4 * d;
+  Builder b = start("flux", arch);
+  b.nest(arch + " (" + str(L) + " double-stream + " + str(Ls) + " single-stream blocks, " + str(heads) + " heads of " +
+             str(hd) + (guidance ? ", guidance embedded" : "") + ")",
+         [&] {
+           b.nest("Embeddings: image rows, text rows, timestep" + std::string(guidance ? " + guidance" : "") +
+                      " + pooled text",
+                  [&] {
+                    b.linear("x_embedder", d, in * patch * patch, true);
+                    b.linear("context_embedder", d, joint, true);
+                    timestep_embedder(b, "time_text_embed.timestep_embedder", d);
+                    if (guidance) timestep_embedder(b, "time_text_embed.guidance_embedder", d);
+                    b.linear("time_text_embed.text_embedder.linear_1", d, pooled, true);
+                    b.linear("time_text_embed.text_embedder.linear_2", d, d, true);
+                  });
+           b.leaf("Double-stream block: per stream adaLN-Zero (6 modulations), q/k/v with RMSNorm of q and k, "
+                  "joint attention, output projection, tanh-GELU MLP " + str(mlp));
+           for (int64_t l = 0; l < L; ++l) {
+             const std::string p = "transformer_blocks." + str(l) + ".";
+             b.linear(p + "norm1.linear", 6 * d, d, true);
+             b.linear(p + "norm1_context.linear", 6 * d, d, true);
+             for (const char* n : {"to_q", "to_k", "to_v", "add_q_proj", "add_k_proj", "add_v_proj"})
+               b.linear(p + "attn." + n, d, d, true);
+             for (const char* n : {"norm_q", "norm_k", "norm_added_q", "norm_added_k"}) b.weight(p + "attn." + n + ".weight", {hd});
+             b.linear(p + "attn.to_out.0", d, d, true);
+             b.linear(p + "attn.to_add_out", d, d, true);
+             for (const char* s : {"ff", "ff_context"}) {
+               b.linear(p + s + ".net.0.proj", mlp, d, true);
+               b.linear(p + s + ".net.2", d, mlp, true);
+             }
+           }
+           b.leaf("Single-stream block: adaLN-Zero (3 modulations), q/k/v with RMSNorm and a parallel MLP " +
+                  str(mlp) + ", one output projection of both");
+           for (int64_t l = 0; l < Ls; ++l) {
+             const std::string p = "single_transformer_blocks." + str(l) + ".";
+             b.linear(p + "norm.linear", 3 * d, d, true);
+             for (const char* n : {"to_q", "to_k", "to_v"}) b.linear(p + "attn." + n, d, d, true);
+             b.weight(p + "attn.norm_q.weight", {hd});
+             b.weight(p + "attn.norm_k.weight", {hd});
+             b.linear(p + "proj_mlp", mlp, d, true);
+             b.linear(p + "proj_out", d, d + mlp, true);
+           }
+           b.nest("Head: modulated LayerNorm, linear to the patch's " + str(out * patch * patch) + " channels", [&] {
+             b.linear("norm_out.linear", 2 * d, d, true);
+             b.linear("proj_out", patch * patch * out, d, true);
+           });
+         });
+  return b.c;
+}
+
+// The class a (component) config names: diffusers' `_class_name`, else its first architecture.
+std::string class_of(const Json& cfg) {
+  if (cfg["_class_name"].is_string()) return cfg["_class_name"].as_string();
+  const Json& a = cfg["architectures"];
+  if (a.is_array() && a.size() > 0 && a.at(0).is_string()) return a.at(0).as_string();
+  return "";
+}
 
 using Maker = Composition (*)(const Json&, const std::string&, const Checkpoint&);
+const std::map<std::string, Maker>& makers();
+
+// A diffusers pipeline: each component folder with a config composes on its own, its tensors
+// under the folder's name (the tokenizers and the scheduler hold no weights).
+Composition pipeline(const Json& j, const std::string& arch, const Checkpoint& ck) {
+  Builder b = start("pipeline", arch);
+  b.nest(arch, [&] {
+    for (const auto& [name, v] : j.members()) {
+      if (!v.is_object()) continue;
+      const std::string cls = class_of(v);
+      if (cls.empty()) continue;
+      const auto it = makers().find(cls);
+      if (it == makers().end() || it->second == pipeline)
+        refuse("config.json:" + name + ": " + cls + " has no catalog composition");
+      const Composition c = it->second(v, cls, ck);
+      b.module(name + ": " + c.family);
+      for (const auto& line : c.tree) b.c.tree.push_back(std::string(2 * (b.depth + 1), ' ') + line);
+      const std::string p = name + ".";
+      for (const auto& w : c.weights) b.weight(p + w.name, w.shape);
+      for (const auto& w : c.optional) b.optional(p + w.name, w.shape);
+      for (const auto& n : c.ignored) b.ignore(p + n);
+    }
+  });
+  return b.c;
+}
+
+// ---- Dispatch --------------------------------------------------------------------------------
+
 
 const std::map<std::string, Maker>& makers() {
   static const std::map<std::string, Maker> m = {
@@ -1141,6 +1373,12 @@ const std::map<std::string, Maker>& makers() {
       {"LlavaForConditionalGeneration", llava},
       {"MllamaForConditionalGeneration", mllama},
       {"Qwen3VLForConditionalGeneration", qwen3_vl},
+      {"AutoencoderKL", autoencoder_kl},
+      {"DiTTransformer2DModel", dit},
+      {"Transformer2DModel", dit},
+      {"FluxTransformer2DModel", flux},
+      {"FluxPipeline", pipeline},
+      {"DiTPipeline", pipeline},
   };
   return m;
 }
@@ -1169,6 +1407,11 @@ Composition compose(const Checkpoint& ck) {
     if (!a.is_string()) continue;
     const auto it = makers().find(a.as_string());
     if (it != makers().end()) return it->second(cfg, a.as_string(), ck);
+  }
+  // Diffusers names a model's (or a pipeline's) class in `_class_name`.
+  if (cfg["_class_name"].is_string()) {
+    const auto it = makers().find(cfg["_class_name"].as_string());
+    if (it != makers().end()) return it->second(cfg, cfg["_class_name"].as_string(), ck);
   }
   refuse("config.json:architectures: no catalog composition");
 }

@@ -298,3 +298,118 @@ def test_every_catalog_architecture_is_a_registry_name():
 
     names = set(_native._architectures())
     assert set(catalog.architectures()) <= names
+
+
+# ---- Diffusion: no diffusers in the image, so the oracle is the published parameter counts ----
+
+SD_VAE = {"_class_name": "AutoencoderKL", "block_out_channels": [128, 256, 512, 512],
+          "down_block_types": ["DownEncoderBlock2D"] * 4, "up_block_types": ["UpDecoderBlock2D"] * 4,
+          "in_channels": 3, "out_channels": 3, "latent_channels": 4, "layers_per_block": 2, "norm_num_groups": 32}
+FLUX_VAE = dict(SD_VAE, latent_channels=16, use_quant_conv=False, use_post_quant_conv=False)
+FLUX_DEV = {"_class_name": "FluxTransformer2DModel", "attention_head_dim": 128, "guidance_embeds": True,
+            "in_channels": 64, "joint_attention_dim": 4096, "num_attention_heads": 24, "num_layers": 19,
+            "num_single_layers": 38, "patch_size": 1, "pooled_projection_dim": 768, "axes_dims_rope": [16, 56, 56]}
+DIT_XL_2 = {"_class_name": "Transformer2DModel", "activation_fn": "gelu-approximate", "attention_bias": True,
+            "attention_head_dim": 72, "in_channels": 4, "norm_type": "ada_norm_zero", "num_attention_heads": 16,
+            "num_embeds_ada_norm": 1000, "num_layers": 28, "out_channels": 8, "patch_size": 2, "sample_size": 32}
+
+
+def _compose_config(tmp_path, name, cfg, check=False):
+    d = tmp_path / name
+    d.mkdir(parents=True, exist_ok=True)
+    (d / "config.json").write_text(json.dumps(cfg))
+    return catalog.compose(engine.Checkpoint.declared(str(d)), check=check)
+
+
+def test_diffusion_compositions_hold_the_published_parameter_counts(tmp_path):
+    assert _compose_config(tmp_path, "sd_vae", SD_VAE).parameters() == 83_653_863  # Stable Diffusion's VAE
+    assert _compose_config(tmp_path, "flux_vae", FLUX_VAE).parameters() == 83_819_683  # FLUX.1's VAE
+    flux = _compose_config(tmp_path, "flux", FLUX_DEV)
+    assert flux.parameters() == 11_901_408_320  # FLUX.1-dev's transformer
+    assert flux.family == "flux" and "transformer_blocks.18.attn.norm_added_k.weight" in flux.weights
+    schnell = _compose_config(tmp_path, "schnell", dict(FLUX_DEV, guidance_embeds=False))
+    assert flux.parameters() - schnell.parameters() == 2 * 3072 + 256 * 3072 + 3072 * 3072
+    # DiT-XL/2: 675,129,632 in the original code, which counts its fixed 256 x 1152 position table
+    # and shares one timestep and class embedder; diffusers gives every block its own embedders.
+    dit = _compose_config(tmp_path, "dit", DIT_XL_2)
+    embedders = (256 * 1152 + 1152 + 1152 * 1152 + 1152) + 1001 * 1152
+    assert dit.parameters() - 27 * embedders + 256 * 1152 == 675_129_632
+    assert "pos_embed.pos_embed" in dit.ignored
+
+
+def test_diffusion_refusals(tmp_path):
+    with pytest.raises(ValueError, match="config.json:norm_type: ada_norm_single"):
+        _compose_config(tmp_path, "a", dict(DIT_XL_2, norm_type="ada_norm_single"))
+    with pytest.raises(ValueError, match="config.json:down_block_types: every block is DownEncoderBlock2D"):
+        _compose_config(tmp_path, "b", dict(SD_VAE, down_block_types=["DownBlock2D"] * 4))
+    with pytest.raises(ValueError, match="config.json:block_out_channels: 100 channels in groups of 32"):
+        _compose_config(tmp_path, "c", dict(SD_VAE, block_out_channels=[128, 100, 512, 512]))
+    with pytest.raises(ValueError, match="config.json:axes_dims_rope"):
+        _compose_config(tmp_path, "d", dict(FLUX_DEV, axes_dims_rope=[16, 56, 48]))
+
+
+def _tiny_flux_pipeline(root):
+    """A FLUX pipeline folder of tiny geometry: model_index.json and four components, each with its
+    config and a header-only safetensors file (text encoders from transformers' modules)."""
+    t = transformers
+    root.mkdir(parents=True, exist_ok=True)
+    (root / "model_index.json").write_text(json.dumps({
+        "_class_name": "FluxPipeline", "scheduler": ["diffusers", "FlowMatchEulerDiscreteScheduler"],
+        "text_encoder": ["transformers", "CLIPTextModel"], "text_encoder_2": ["transformers", "T5EncoderModel"],
+        "tokenizer": ["transformers", "CLIPTokenizer"], "transformer": ["diffusers", "FluxTransformer2DModel"],
+        "vae": ["diffusers", "AutoencoderKL"]}))
+    shapes = {}
+    for name, cfg, cls in [("text_encoder", t.CLIPTextConfig(hidden_size=32, intermediate_size=64, num_hidden_layers=1,
+                                                             num_attention_heads=2, vocab_size=50,
+                                                             max_position_embeddings=16), t.CLIPTextModel),
+                           ("text_encoder_2", t.T5Config(d_model=32, d_kv=8, d_ff=64, num_heads=4, num_layers=1,
+                                                         vocab_size=50), t.T5EncoderModel)]:
+        with torch.device("meta"):
+            model = cls(cfg)
+        conf = json.loads(cfg.to_json_string())
+        conf["architectures"] = [cls.__name__]
+        d = root / name
+        d.mkdir()
+        (d / "config.json").write_text(json.dumps(conf))
+        held = {n: tuple(v.shape) for n, v in model.state_dict().items() if n != "encoder.embed_tokens.weight"}
+        synthetic.write_headers(str(d), held)
+        shapes.update({f"{name}.{n}": s for n, s in held.items()})
+    for name, cfg in [("transformer", dict(FLUX_DEV, num_layers=1, num_single_layers=2, num_attention_heads=2,
+                                           attention_head_dim=16, axes_dims_rope=[4, 6, 6], joint_attention_dim=32,
+                                           pooled_projection_dim=32, in_channels=16)),
+                      ("vae", dict(SD_VAE, block_out_channels=[32, 64], down_block_types=["DownEncoderBlock2D"] * 2,
+                                   up_block_types=["UpDecoderBlock2D"] * 2, latent_channels=4, layers_per_block=1))]:
+        d = root / name
+        d.mkdir()
+        (d / "config.json").write_text(json.dumps(cfg))
+        comp = catalog.compose(engine.Checkpoint.declared(str(d)), check=False)
+        synthetic.write_headers(str(d), comp.weights)
+        shapes.update({f"{name}.{n}": s for n, s in comp.weights.items()})
+    (root / "scheduler").mkdir()
+    (root / "scheduler" / "scheduler_config.json").write_text(json.dumps({"_class_name": "FlowMatchEulerDiscreteScheduler"}))
+    return shapes
+
+
+def test_pipelines_compose_each_component_under_its_folder(tmp_path):
+    shapes = _tiny_flux_pipeline(tmp_path / "flux")
+    comp = catalog.compose(engine.Checkpoint.declared(str(tmp_path / "flux")))
+    assert comp.family == "pipeline" and comp.architecture == "FluxPipeline"
+    assert comp.weights == shapes
+    assert {line.strip().split(":")[0] for line in comp.tree[1:] if line.startswith("  ") and not line.startswith("    ")} \
+        == {"text_encoder", "text_encoder_2", "transformer", "vae"}
+    assert "text_encoder_2.encoder.embed_tokens.weight" in comp.optional
+    with pytest.raises(NotImplementedError, match="FluxPipeline"):
+        engine.LoadOptions().parse(engine.Checkpoint.declared(str(tmp_path / "flux")))
+    # A component whose tensor is missing is refused by its full name.
+    (tmp_path / "flux" / "vae" / "model.safetensors").unlink()
+    with pytest.raises(ValueError, match="vae.encoder.conv_in.weight: missing from the checkpoint"):
+        catalog.compose(engine.Checkpoint.declared(str(tmp_path / "flux")))
+
+
+def test_pipeline_components_without_a_composition_are_refused(tmp_path):
+    shapes = _tiny_flux_pipeline(tmp_path / "p")
+    assert shapes
+    cfg = json.loads((tmp_path / "p" / "vae" / "config.json").read_text())
+    (tmp_path / "p" / "vae" / "config.json").write_text(json.dumps(dict(cfg, _class_name="AutoencoderTiny")))
+    with pytest.raises(ValueError, match="config.json:vae: AutoencoderTiny has no catalog composition"):
+        catalog.compose(engine.Checkpoint.declared(str(tmp_path / "p")))
