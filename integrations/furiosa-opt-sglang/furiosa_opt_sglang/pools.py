@@ -140,6 +140,25 @@ def token_pool_class():
     return Tokens
 
 
+def overridden(model_path: str, overrides) -> dict | None:
+    """The checkpoint's config.json under SGLang's `json_model_override_args` (a JSON object; None
+    without overrides): each key replaces the config's value."""
+    import json
+    import os
+
+    if not overrides:
+        return None
+    extra = json.loads(overrides) if isinstance(overrides, str) else overrides
+    if not isinstance(extra, dict):
+        raise ValueError("json_model_override_args: a JSON object of config keys")
+    if not extra:
+        return None
+    with open(os.path.join(model_path, "config.json")) as f:
+        config = json.load(f)
+    config.update(extra)
+    return config
+
+
 def bind(model_runner) -> None:
     """Loads the engine decoder of `model_runner`'s model on its GPU and sets SGLang's pools, sizes
     and the plugin's `engine_runner` on it."""
@@ -159,6 +178,9 @@ def bind(model_runner) -> None:
     first = int(model_runner.gpu_id) - rank
     device = engine.Device(engine.Placement(list(range(first, first + tp)), range(8)), rank=rank if tp > 1 else 0)
     opts = engine.LoadOptions()
+    if getattr(args, "enable_deterministic_inference", False):
+        opts = opts.batch_invariant()  # a request's tokens keep their bits whatever shares its steps
+    config = overridden(model_runner.model_config.model_path, getattr(args, "json_model_override_args", None))
     if tp > 1:
         from furiosa_opt_models_b200.parallel import tp as tensor_parallel
 
@@ -182,8 +204,9 @@ def bind(model_runner) -> None:
         return plan[-1].blocks
 
     served = residency.Served(
-        model_runner.model_config.model_path, device, blocks, load=opts.load, checkpoint=engine.Checkpoint,
-        host_copy=lambda path: engine.Checkpoint(path).read(), cache=dec.Cache,
+        model_runner.model_config.model_path, device, blocks, load=opts.load,
+        checkpoint=lambda path: engine.Checkpoint(path, config),
+        host_copy=lambda path: engine.Checkpoint(path, config).read(), cache=dec.Cache,
         trim=lambda d: engine._native._device_trim(d),
         memory_saver=bool(getattr(args, "enable_memory_saver", False)),
         cpu_backup=bool(getattr(args, "enable_weights_cpu_backup", False)))

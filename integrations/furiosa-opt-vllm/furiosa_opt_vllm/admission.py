@@ -124,7 +124,8 @@ CONTRACTS: tuple[Contract, ...] = (
              "the engine computes in BF16"),
     Contract("model_config.quantization", _is(*QUANTIZATIONS),
              "the engine reads BF16, block FP8 and NVFP4 checkpoints as published"),
-    Contract("model_config.hf_overrides", lambda v, _c: not v, "the checkpoint's config is read as published"),
+    Contract("model_config.hf_overrides", lambda v, _c: not v or isinstance(v, dict),
+             "overrides are a mapping of config keys applied to config.json; a function of the config is not served"),
     Contract("model_config.enable_prompt_embeds", _unset, "requests carry token IDs"),
     Contract("model_config.enable_return_routed_experts", _unset, "routing stays on the device"),
     Contract("model_config.override_attention_dtype", _unset, "attention runs in BF16"),

@@ -4,15 +4,40 @@
 from __future__ import annotations
 
 
-def checkpoint(model_path: str):
+def checkpoint(model_path: str, config: dict | None = None):
+    """The checkpoint's files, read with `config` instead of its config.json when given."""
     import furiosa_opt_engine as engine
 
-    return engine.Checkpoint(model_path)
+    return engine.Checkpoint(model_path, config)
 
 
-def host_copy(model_path: str):
+def host_copy(model_path: str, config: dict | None = None):
     """The checkpoint with every tensor copied into host memory (sleep mode's copy)."""
-    return checkpoint(model_path).read()
+    return checkpoint(model_path, config).read()
+
+
+def overridden(model_path: str, hf_overrides) -> dict | None:
+    """The checkpoint's config.json under vLLM's `hf_overrides` (None without overrides). As
+    transformers' `PretrainedConfig.update` does, a key replaces the config's value, except that an
+    override of a nested sub-config (a value with its own `model_type`) updates its keys."""
+    import json
+    import os
+
+    from .admission import Refused
+
+    if not hf_overrides:
+        return None
+    if not isinstance(hf_overrides, dict):
+        raise Refused("hf_overrides", "a mapping of config keys; a function of the config is not served")
+    with open(os.path.join(model_path, "config.json")) as f:
+        config = json.load(f)
+    for key, value in hf_overrides.items():
+        old = config.get(key)
+        if isinstance(value, dict) and isinstance(old, dict) and "model_type" in old:
+            config[key] = {**old, **value}
+        else:
+            config[key] = value
+    return config
 
 
 def architectures(model_path: str) -> list[str]:
@@ -24,7 +49,16 @@ def architectures(model_path: str) -> list[str]:
         return list(json.load(f).get("architectures") or [])
 
 
-def load_from(ck, device, world: int, adapters: bool = False, architecture: str | None = None):
+def batch_invariant() -> bool:
+    """Whether vLLM runs batch invariant (`VLLM_BATCH_INVARIANT=1`): a request's tokens and rows
+    then keep their bits whatever other requests share its steps."""
+    import os
+
+    return os.environ.get("VLLM_BATCH_INVARIANT", "0").strip().lower() in ("1", "true")
+
+
+def load_from(ck, device, world: int, adapters: bool = False, architecture: str | None = None,
+              invariant: bool | None = None):
     import furiosa_opt_engine as engine
 
     opts = engine.LoadOptions()
@@ -34,6 +68,8 @@ def load_from(ck, device, world: int, adapters: bool = False, architecture: str 
         opts = opts.chips(world)
     if adapters:
         opts = opts.adapters()
+    if batch_invariant() if invariant is None else invariant:
+        opts = opts.batch_invariant()
     return opts.load(ck, device)
 
 
@@ -56,11 +92,11 @@ def replica_chips(local_rank: int, tp_rank: int, tp: int, dp_rank: int = 0, visi
 
 
 def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips: list | None = None,
-         group=None, adapters: bool = False, architecture: str | None = None):
+         group=None, adapters: bool = False, architecture: str | None = None, config: dict | None = None):
     """(decoder, device, host copy or None): this worker's chip of its replica (`chips`, its
     tensor-parallel `rank` of `world`, joined in `group`); a load under sleep mode keeps the host
     copy it loaded. `architecture` overrides the config's class (a causal checkpoint pooled as its
-    base model)."""
+    base model); `config` replaces the checkpoint's config.json (vLLM's overrides applied)."""
     import furiosa_opt_engine as engine
 
     chips = chips if chips is not None else list(range(world))
@@ -69,5 +105,5 @@ def load(model_path: str, rank: int, world: int, keep_copy: bool = False, chips:
         from furiosa_opt_models_b200.parallel import tp
 
         tp.set_group(group)
-    ck = host_copy(model_path) if keep_copy else checkpoint(model_path)
+    ck = host_copy(model_path, config) if keep_copy else checkpoint(model_path, config)
     return load_from(ck, device, world, adapters, architecture), device, (ck if keep_copy else None)

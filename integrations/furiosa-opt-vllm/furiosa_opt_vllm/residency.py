@@ -106,7 +106,8 @@ def wake_up(worker, tags) -> None:
         if state is None:
             continue
         if isinstance(state, Weights):
-            copy = state.copy if state.copy is not None else load.host_copy(worker.model_config.model)
+            copy = state.copy if state.copy is not None else load.host_copy(worker.model_config.model,
+                                                                             getattr(worker, "checkpoint_config", None))
             _load(worker, copy)
             worker.copy = copy
         else:
@@ -123,8 +124,9 @@ def reload(worker) -> None:
     if "weights" in worker.asleep:
         raise RuntimeError("reload_weights requires awake weights; wake them up first")
     # The files are read before the served weights leave the device.
-    source = load.host_copy(worker.model_config.model) if worker.model_config.enable_sleep_mode else \
-        load.checkpoint(worker.model_config.model)
+    config = getattr(worker, "checkpoint_config", None)
+    source = load.host_copy(worker.model_config.model, config) if worker.model_config.enable_sleep_mode else \
+        load.checkpoint(worker.model_config.model, config)
     _drop_model(worker)
     _trim(worker)
     _load(worker, source)

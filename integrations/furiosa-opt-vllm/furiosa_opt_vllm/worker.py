@@ -98,10 +98,11 @@ class Worker(WorkerBase):
                 raise admission.Refused("runner", f"pooling serves Qwen3 causal and classifier checkpoints, "
                                                   f"not {', '.join(declared)}")
         self.architecture = architecture
+        self.checkpoint_config = load.overridden(self.model_config.model, getattr(self.model_config, "hf_overrides", None))
         self.model, self.engine_device, self.copy = load.load(
             self.model_config.model, tp_rank, tp_size, keep_copy=bool(self.model_config.enable_sleep_mode),
             chips=chips, group=get_tp_group().cpu_group if tp_size > 1 else None,
-            adapters=self.lora_config is not None, architecture=architecture)
+            adapters=self.lora_config is not None, architecture=architecture, config=self.checkpoint_config)
         from .additional import Section
 
         if not Section.parse(self.vllm_config).cuda_graphs:

@@ -337,3 +337,16 @@ def test_host_pool_class_adapts_the_tier(monkeypatch):
     assert log[-1] == ("h2d", "host", 0, 100, ("L1", 100, 100))
     with pytest.raises(ValueError):
         hicache.host_pool_class()(device_pool, 2.0, 0, 32)
+
+
+def test_model_override_args_replace_config_keys(tmp_path):
+    import json
+
+    (tmp_path / "config.json").write_text(json.dumps({"architectures": ["Qwen3ForCausalLM"], "rope_theta": 1e6}))
+    assert pools.overridden(str(tmp_path), None) is None
+    assert pools.overridden(str(tmp_path), "{}") is None
+    got = pools.overridden(str(tmp_path), '{"rope_scaling": {"rope_type": "linear", "factor": 2.0}}')
+    assert got == {"architectures": ["Qwen3ForCausalLM"], "rope_theta": 1e6,
+                   "rope_scaling": {"rope_type": "linear", "factor": 2.0}}
+    with pytest.raises(ValueError, match="json_model_override_args"):
+        pools.overridden(str(tmp_path), "[1, 2]")

@@ -491,3 +491,88 @@ def test_media_step_embeds_each_item_once_and_frees_hashes():
              mm_position=ns(get_num_embeds=lambda: 3))
     with pytest.raises(ValueError, match="placeholders"):
         m.embed(bad)
+
+
+def test_config_overrides_apply_to_the_checkpoint_config(tmp_path):
+    """vLLM's `hf_overrides` (a mapping) replace config.json keys as transformers' update does; a
+    nested sub-config is updated key by key; a function of the config is refused."""
+    import json
+
+    from furiosa_opt_vllm import load
+
+    (tmp_path / "config.json").write_text(json.dumps({
+        "architectures": ["Qwen3ForCausalLM"], "max_position_embeddings": 4096, "rope_theta": 1e6,
+        "rope_scaling": {"rope_type": "linear", "factor": 2.0}, "text_config": {"model_type": "x", "a": 1, "b": 2}}))
+    assert load.overridden(str(tmp_path), None) is None
+    assert load.overridden(str(tmp_path), {}) is None
+    got = load.overridden(str(tmp_path), {"rope_scaling": {"rope_type": "yarn", "factor": 4.0,
+                                                            "original_max_position_embeddings": 4096},
+                                          "max_position_embeddings": 16384, "text_config": {"b": 3}})
+    assert got["rope_scaling"] == {"rope_type": "yarn", "factor": 4.0, "original_max_position_embeddings": 4096}
+    assert got["max_position_embeddings"] == 16384 and got["rope_theta"] == 1e6
+    assert got["text_config"] == {"model_type": "x", "a": 1, "b": 3}
+    with pytest.raises(admission.Refused) as e:
+        load.overridden(str(tmp_path), lambda c: c)
+    assert e.value.option == "hf_overrides"
+
+
+def test_overridden_config_reaches_the_engine_load(tmp_path):
+    """The overridden config is what the registry reads: YaRN scaling selects, a refused scaling is
+    refused by the registry with its key."""
+    import json
+
+    import furiosa_opt_engine as engine
+    from furiosa_opt_models_b200.models import configs, synthetic
+    from furiosa_opt_vllm import load
+
+    (tmp_path / "config.json").write_text(json.dumps(synthetic.hf_config(configs.get("qwen3-1.7b"))))
+    ok = load.overridden(str(tmp_path), {"rope_scaling": {"rope_type": "yarn", "factor": 4.0,
+                                                           "original_max_position_embeddings": 40960}})
+    assert engine.LoadOptions().select(load.checkpoint(str(tmp_path), ok))["class"] == "qwen3.ForCausalLM"
+    bad = load.overridden(str(tmp_path), {"rope_scaling": {"rope_type": "longrope", "factor": 4.0}})
+    with pytest.raises(NotImplementedError, match="rope_scaling"):
+        engine.LoadOptions().select(load.checkpoint(str(tmp_path), bad))
+
+
+def test_batch_invariant_vllm_loads_batch_invariant(monkeypatch):
+    import furiosa_opt_engine as engine
+    from furiosa_opt_vllm import load
+
+    calls = []
+
+    class Options:
+        def __init__(self):
+            self.chain = []
+
+        def __getattr__(self, name):
+            def step(*args):
+                self.chain.append((name, args))
+                return self
+            return step
+
+        def load(self, ck, device):
+            calls.append(self.chain)
+            return "decoder"
+
+    monkeypatch.setattr(engine, "LoadOptions", Options)
+    monkeypatch.setenv("VLLM_BATCH_INVARIANT", "1")
+    assert load.batch_invariant()
+    load.load_from("ck", "dev", 2)
+    monkeypatch.setenv("VLLM_BATCH_INVARIANT", "0")
+    load.load_from("ck", "dev", 1)
+    load.load_from("ck", "dev", 1, invariant=True)
+    assert [[n for n, _ in c] for c in calls] == [["chips", "batch_invariant"], [], ["batch_invariant"]]
+
+
+def test_overrides_contract():
+    from types import SimpleNamespace as ns
+
+    cfg = ns(parallel_config=ns(pipeline_parallel_size=1, tensor_parallel_size=1, nnodes=1),
+             cache_config=ns(cache_dtype="auto"),
+             model_config=ns(dtype="bfloat16", quantization=None, hf_overrides={"max_position_embeddings": 8192}),
+             load_config=ns(load_format="auto"), speculative_config=None, ec_transfer_config=None)
+    admission.check(cfg)
+    cfg.model_config.hf_overrides = lambda c: c
+    with pytest.raises(admission.Refused) as e:
+        admission.check(cfg)
+    assert e.value.option == "hf_overrides"

@@ -32,8 +32,8 @@ def worker(monkeypatch):
     trims = []
     monkeypatch.setattr(_native, "_device_trim", lambda device: trims.append(device))
     monkeypatch.setattr(load, "load_from", lambda ck, device, world, adapters=False, architecture=None: FakeModel(ck))
-    monkeypatch.setattr(load, "host_copy", lambda path: f"copy of {path}")
-    monkeypatch.setattr(load, "checkpoint", lambda path: f"files of {path}")
+    monkeypatch.setattr(load, "host_copy", lambda path, config=None: f"copy of {path}")
+    monkeypatch.setattr(load, "checkpoint", lambda path, config=None: f"files of {path}")
     monkeypatch.setattr(dec, "Cache", FakeCache)
     w = SimpleNamespace(model_config=SimpleNamespace(enable_sleep_mode=True, model="/m"),
                         parallel_config=SimpleNamespace(tensor_parallel_size=1), engine_device="dev", runner=None,
