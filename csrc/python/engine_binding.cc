@@ -378,13 +378,13 @@ void bind_engine(py::module_& m) {
       });
 
   py::class_<PyKind> kind(decoder, "Kind", "What the blocks of a group hold.");
-  py::class_<PyKindPaged, PyKind>(kind, "Paged").def(py::init([]() { return PyKindPaged{{KindTag::Paged, 0}}; }))
+  py::class_<PyKindPaged, PyKind>(kind, "Paged", "Paged keys and values: each block caches a page of consecutive positions, read in the order of the request's block table.").def(py::init([]() { return PyKindPaged{{KindTag::Paged, 0}}; }))
       .def("__eq__", [](const PyKind& a, const py::object& o) {
         return py::isinstance<PyKindPaged>(o);
       });
-  py::class_<PyKindState, PyKind>(kind, "State").def(py::init([]() { return PyKindState{{KindTag::State, 0}}; }))
+  py::class_<PyKindState, PyKind>(kind, "State", "A recurrent state a block (not served by any decoder here).").def(py::init([]() { return PyKindState{{KindTag::State, 0}}; }))
       .def("__eq__", [](const PyKind& a, const py::object& o) { return py::isinstance<PyKindState>(o); });
-  py::class_<PyKindCross, PyKind>(kind, "Cross")
+  py::class_<PyKindCross, PyKind>(kind, "Cross", "Encoder keys and values: `length` positions that one call writes for every later call to read.")
       .def(py::init([](int64_t length) { return PyKindCross{{KindTag::Cross, length}}; }), py::arg("length"))
       .def_property_readonly("length", [](const PyKindCross& k) { return k.length; })
       .def("__eq__", [](const PyKind& a, const py::object& o) {
