@@ -1,5 +1,6 @@
-// Media encoders: a call turns images (merged patches with their positions) or audio frames into
-// rows of the language model's width, which a framework places at the media's placeholder tokens.
+// Media encoders: images (merged patches and their positions) and audio frames in, embedding rows
+// of the language model's hidden size out; the serving framework substitutes those rows for the
+// media placeholder tokens of the prompt.
 //
 // Reference: crates/furiosa-opt-engine/src/vision_language/mod.rs (Image :19-41, Audio :44-60,
 // Encoder :79-94, launches :98-118) and gemma4_unified.rs (vision :42-84, audio :86-103);

@@ -51,7 +51,7 @@ void bind_encoder(py::module_& m) {
              return PyImage{std::move(pixels), positions};
            }),
            py::arg("pixels"), py::arg("positions"),
-           "`pixels` lie on the model's device; `positions` name the valid patches only.\n\n"
+           "`pixels` must be on the model's device; `positions` lists the real patches (padding has none).\n\n"
            "Raises:\n    ValueError: `pixels` are not two-dimensional BF16 rows, one for each position.")
       .def_property_readonly("pixels", [](const PyImage& i) { return i.pixels; })
       .def_property_readonly("positions", [](const PyImage& i) { return i.positions; });
@@ -67,8 +67,8 @@ void bind_encoder(py::module_& m) {
       .def_property_readonly("frames", [](const PyAudio& a) { return a.frames; });
 
   py::class_<PyEncoder>(m, "Encoder",
-                        "A media encoder loaded on a device, whatever its model: its calls turn images, video "
-                        "frames and audio into rows of its language model's width.")
+                        "A loaded media encoder (any supported model): images, video frames and audio in, embedding "
+                        "rows of the language model's hidden size out.")
       .def("vision",
            [](const PyEncoder& e, const std::vector<PyImage>& images) {
              std::vector<ImageInput> in;

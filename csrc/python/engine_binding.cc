@@ -391,7 +391,7 @@ void bind_engine(py::module_& m) {
         return py::isinstance<PyKindCross>(o) && o.cast<const PyKind&>().length == a.length;
       });
 
-  py::class_<Group>(decoder, "Group", "Layers whose cache has one kind and takes its blocks from one pool.")
+  py::class_<Group>(decoder, "Group", "A set of layers sharing one cache kind and drawing blocks from one pool.")
       .def_readonly("pool", &Group::pool)
       .def_property_readonly("layers", [](const Group& g) { return make_range(g.layers_begin, g.layers_end); })
       .def_property_readonly("kind", [](const Group& g) -> py::object {
@@ -426,14 +426,14 @@ void bind_engine(py::module_& m) {
       .value("NONE", PyKeep::NONE)
       .value("LAST", PyKeep::LAST)
       .value("ALL", PyKeep::ALL);
-  py::enum_<PyOutput>(decoder, "Output", "What a decoder's call returns of each kept row.")
+  py::enum_<PyOutput>(decoder, "Output", "The output a decoder produces for each kept row: token, hidden row or scores.")
       .value("TOKENS", PyOutput::TOKENS)
       .value("HIDDEN", PyOutput::HIDDEN)
       .value("SCORES", PyOutput::SCORES);
 
   py::class_<PyAdapterSpec>(decoder, "AdapterSpec",
-                            "The LoRA adapters a loaded decoder's calls run their requests with: RANK, "
-                            "the rank every update holds, and SLOTS, the adapters one call runs with.")
+                            "Adapter limits of a loaded decoder: RANK (the LoRA rank of every update) and SLOTS (how "
+                            "many adapters one call can use).")
       .def_property_readonly_static("RANK", [](py::object) { return LoraAdapter::kRank; })
       .def_property_readonly_static("SLOTS", [](py::object) { return LoraAdapter::kSlots; });
   py::class_<PyAdapter>(decoder, "Adapter",

@@ -77,8 +77,8 @@ py::object make_decoder(const Selection& s, std::shared_ptr<DecoderModel> model,
 
 void bind_checkpoint_and_load(py::module_& m) {
   py::class_<PyCheckpoint>(m, "Checkpoint",
-                           "The tensors of a checkpoint directory, mapped or read into host memory, "
-                           "and the config of its model.")
+                           "A checkpoint directory: its model config and its tensors, memory-mapped or copied into "
+                           "host memory.")
       .def(py::init([](const py::object& path, const py::object& config) {
              const std::string p = py::str(py::module_::import("os").attr("fspath")(path));
              std::optional<Json> cfg;

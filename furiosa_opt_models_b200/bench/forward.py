@@ -14,8 +14,8 @@ Each case runs `warmups` unmeasured calls, then `repetitions` measured ones. A m
 `forward` span (args `case`, `step`) from the call's submission to the device's completion; the
 spans go to `<out>/<org>--<name>/forward.json` together with the engine's own spans (its device
 span per call, and a span per kernel under FURIOSA_OPT_PROFILE=trace), and
-`furiosa_opt_models_b200.bench.metrics` reads step and kernel times from that file. Timing reads
-no cache values, so the histories stay unwritten. The weights are random (N(0, 0.02)) in the shape
+`furiosa_opt_models_b200.bench.metrics` reads step and kernel times from that file. The timed calls
+attend to cache pages that were never filled: timing does not depend on their values. The weights are random (N(0, 0.02)) in the shape
 of the named model.
 
 Reference: crates/furiosa-opt-engine/tests/forward.rs:47-160 (cases, warm-ups, repetitions and

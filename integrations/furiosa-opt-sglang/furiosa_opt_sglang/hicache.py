@@ -1,4 +1,4 @@
-"""SGLang's hierarchical cache over the engine cache: a host tier of the engine's KV pages.
+"""A host-memory tier for SGLang's hierarchical cache, holding copies of the engine's KV pages.
 
 SGLang's cache controller backs evicted radix-tree pages up to a host pool and loads them back
 layer by layer before a request that hits them runs. The engine owns the device pages (one buffer

@@ -5,7 +5,8 @@ integrations/furiosa-opt-sglang/furiosa_opt_sglang/residency.py).
 Device memory is released by dropping what holds it (the loaded decoder, the KV cache) and
 returning the engine's cached device blocks to the driver; resuming loads or allocates it again.
 
-- Only `--enable-memory-saver` releases memory, as with SGLang's own allocator.
+- Releasing needs `--enable-memory-saver`; without it SGLang's own allocator releases nothing
+  either, and so neither does the plugin.
 - With `--enable-weights-cpu-backup` the load keeps a host copy of the checkpoint's tensors
   (`Checkpoint.read()`) and resuming loads from it; without it resuming reads the files again.
 - A released cache keeps its block count and comes back empty (SGLang flushes its radix cache

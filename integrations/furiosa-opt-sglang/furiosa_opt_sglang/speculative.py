@@ -280,14 +280,14 @@ def forward(runner, speculation: Speculation, batch, req_to_token, context: int)
         # the proposer kept of it.
         speculation.proposer.forget(r.rid for r in batch.reqs)
         result = runner.issue(batch, req_to_token, overlap=False)
-        result.collect()
+        result.read()
         committed = [(int(t),) for t in result.next_token_ids.tolist()]
         new_seq_lens = batch.seq_lens
     elif mode.is_decode():
         if not steps.greedy(batch):
             raise NotImplementedError("speculative verification selects greedy tokens; sampling reads scores")
         committed = speculation.decode(runner, batch, req_to_token, context)
-        result = steps.result_class()([], len(committed))
+        result = steps.result_class()((), len(committed))
         new_seq_lens = batch.seq_lens + torch.tensor([len(c) for c in committed], dtype=batch.seq_lens.dtype)
     else:
         raise ValueError(f"speculative decoding schedules no {mode} step")

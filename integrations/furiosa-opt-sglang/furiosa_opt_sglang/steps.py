@@ -84,7 +84,8 @@ _classes: dict = {}
 
 
 def result_class():
-    """The step result class: a subclass of SGLang's GenerationBatchResult (or of `_Record`)."""
+    """The step result class, `DeviceStep`: a subclass of SGLang's GenerationBatchResult (of
+    `_Record` without SGLang)."""
     try:
         from sglang.srt.layers.logits_processor import LogitsProcessorOutput
         from sglang.srt.managers.utils import GenerationBatchResult
@@ -94,49 +95,70 @@ def result_class():
     if key in _classes:
         return _classes[key]
 
-    class Sampled(GenerationBatchResult):
-        """A greedy step whose tokens stay on the device until `collect` (once, before SGLang
-        processes the step). Until then `next_token_ids` holds zeros, which SGLang relays as the
-        next decode rows' inputs; those rows read the device tokens instead."""
+    class DeviceStep(GenerationBatchResult):
+        """A step's selected tokens while they are still on the device. `reads` pairs the batch
+        indices of each engine call's kept rows with the call's output tensor; `read()` copies them
+        to the host once and puts them in `next_token_ids`, which until then holds zeros (SGLang
+        relays those as the next decode rows' inputs, and those rows take the device tokens)."""
 
-        def __init__(self, calls: list, size: int):
+        def __init__(self, reads, size: int, number: int = -1):
             import torch
 
             logits = LogitsProcessorOutput(next_token_logits=None) if LogitsProcessorOutput is not None else None
             super().__init__(logits_output=logits, next_token_ids=torch.zeros(size, dtype=torch.int64),
                              can_run_cuda_graph=False)
-            self.calls = calls  # [(batch indices of the kept rows, the call's device tokens)]
-            self.size = size
+            self.reads = list(reads)
+            self.size, self.number = size, number
 
-        def collect(self) -> None:
+        @property
+        def unread(self) -> bool:
+            return bool(self.reads)
+
+        def read(self) -> None:
             import torch
 
-            if not self.calls:
+            if not self.reads:
                 return
-            ids = torch.zeros(self.size, dtype=torch.int64)
-            for kept, tokens in self.calls:
-                host = np.asarray(tokens.to_host().numpy()).reshape(-1)[: len(kept)]
-                ids[torch.tensor(kept, dtype=torch.int64)] = torch.from_numpy(host.astype(np.int64))
-            self.next_token_ids = ids
-            self.calls = []
+            host = np.zeros(self.size, dtype=np.int64)
+            for where, tokens in self.reads:
+                host[where] = np.asarray(tokens.to_host().numpy()).reshape(-1)[: len(where)]
+            self.next_token_ids = torch.from_numpy(host)
+            self.reads = []
 
-    _classes[key] = Sampled
-    return Sampled
+        collect = read  # the name SGLang-facing code calls
+
+    _classes[key] = DeviceStep
+    return DeviceStep
 
 
 class State:
-    """A runner's step bookkeeping: the results issued and not yet certainly processed (oldest
-    first), and each request-pool row's next input token while a greedy step holds it on the device
-    (the call's token tensor and the row in it)."""
+    """A runner's step bookkeeping: a count of the steps issued, the results not yet read (by step
+    number), and each request-pool row's next input token while a step keeps it on the device
+    (the call's output tensor and the row in it)."""
 
     def __init__(self):
-        self.issued: deque = deque()
+        self.issued_steps = 0
+        self.unread: dict[int, object] = {}
         self.selected: dict[int, tuple] = {}
 
     def release(self, slots) -> None:
         """Drops the device tokens of freed request-pool rows (their requests run no further step)."""
         for s in slots:
             self.selected.pop(int(s), None)
+
+    def begin(self, lag: int) -> int:
+        """The number of the step about to be issued. SGLang reads a step's result before it issues
+        the step `lag + 1` after it (lag 1 under the overlap schedule, 0 without), so any older
+        step still unread is an error."""
+        n = self.issued_steps
+        for k, step in list(self.unread.items()):
+            if not step.unread:
+                del self.unread[k]
+            elif k < n - lag:
+                raise RuntimeError(f"step {k} was issued and never read: SGLang issued step {n} "
+                                   "without collecting its tokens")
+        self.issued_steps = n + 1
+        return n
 
 
 def _ints(x) -> list[int]:
@@ -146,14 +168,11 @@ def _ints(x) -> list[int]:
 
 
 def issue(runner, batch, req_to_token, *, overlap: bool):
-    """Submits a scheduled generation batch's engine calls and returns its `Sampled` result without
-    waiting for them. With `overlap`, SGLang processes the previous step while the device runs
-    this one; either way a step must be collected before the second step after it is issued."""
+    """Submits a scheduled generation batch's engine calls and returns its `DeviceStep` without
+    waiting for them. With `overlap`, SGLang processes the previous step while the device runs this
+    one; either way a step is read before the second step after it is issued."""
     state: State = runner.steps
-    while len(state.issued) > (1 if overlap else 0):
-        old = state.issued.popleft()
-        if old.calls:
-            raise RuntimeError("SGLang processed a greedy step without collecting its tokens")
+    number = state.begin(1 if overlap else 0)
     mode = batch.forward_mode
     extend = mode.is_extend()
     if not (extend or mode.is_decode()):
@@ -164,51 +183,50 @@ def issue(runner, batch, req_to_token, *, overlap: bool):
     seq_lens = _ints(batch.seq_lens)
     lengths = _ints(batch.extend_lens) if extend else [1] * len(slots)
     cached = [t - n for t, n in zip(seq_lens, lengths)]
-    # Decode rows, and the decode requests a mixed extend batch carries, take the token the last
+    # Decode rows, and the decode requests a mixed extend batch carries, take the token an earlier
     # step left on the device; every other row reads the batch's uploaded IDs.
     running = {id(r) for r in (getattr(batch, "decoding_reqs", None) or ())}
-    feed = {}
-    for i, req in enumerate(batch.reqs):
-        if (not extend or id(req) in running) and slots[i] in state.selected:
-            feed[i] = state.selected[slots[i]]
+    from_device = {i: state.selected[slots[i]] for i, req in enumerate(batch.reqs)
+                   if (not extend or id(req) in running) and slots[i] in state.selected}
     ids = np.asarray(_ints(batch.input_ids), dtype=np.int32)
     starts = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
     if len(ids) != starts[-1]:
         raise ValueError(f"{len(ids)} input IDs for {starts[-1]} scheduled rows")
-    calls = []
+    reads = []
     for call in plan(lengths, cached, int(runner.model.rows)):
-        host = [r for r in call if r.seq not in feed]
-        uploaded = None
-        if host:
-            flat = np.concatenate([ids[starts[r.seq] + r.first : starts[r.seq] + r.first + r.count] for r in host])
+        uploaded_runs = [r for r in call if r.seq not in from_device]
+        uploaded, offset = None, 0
+        if uploaded_runs:
+            flat = np.concatenate([ids[starts[r.seq] + r.first : starts[r.seq] + r.first + r.count]
+                                   for r in uploaded_runs])
             uploaded = runner.engine.HostTensor.from_dlpack(np.ascontiguousarray(flat)).to_hbm(runner.device)
-        reqs, at, kept = [], 0, []
+        requests, ends = [], []
         for r in call:
-            if r.seq in feed:
-                src, row = feed[r.seq]
+            if r.seq in from_device:
+                src, row = from_device[r.seq]
                 tokens = src[row : row + 1]
             else:
-                tokens = uploaded[at : at + r.count]
-                at += r.count
+                tokens = uploaded[offset : offset + r.count]
+                offset += r.count
             blocks = runner.blocks(req_to_token, slots[r.seq], r.cached + r.count)
             keep = runner.dec.Keep.LAST if r.last else runner.dec.Keep.NONE
-            reqs.append(runner.dec.Request([blocks], r.cached, tokens, keep))
+            requests.append(runner.dec.Request([blocks], r.cached, tokens, keep))
             if r.last:
-                kept.append(r.seq)
-        out = runner.model.forward(reqs, runner.cache)
-        if kept:
-            calls.append((kept, out))
-            for row, i in enumerate(kept):
-                state.selected[slots[i]] = (out, row)
+                ends.append(r.seq)
+        out = runner.model.forward(requests, runner.cache)
         for r in call:
-            if not r.last:  # a request's earlier runs keep nothing; a stale token must not feed it
+            if r.last:
+                state.selected[slots[r.seq]] = (out, ends.index(r.seq))
+            else:  # an earlier run of a request keeps nothing; its old device token must not feed it
                 state.selected.pop(slots[r.seq], None)
-    result = result_class()(calls, len(slots))
-    state.issued.append(result)
+        if ends:
+            reads.append((np.asarray(ends, dtype=np.int64), out))
+    result = result_class()(reads, len(slots), number)
+    state.unread[number] = result
     return result
 
 
 def collect(_scheduler, _batch, result) -> None:
     """The hook before SGLang's `Scheduler.process_batch_result`: reads a step's device tokens."""
     if isinstance(result, result_class()):
-        result.collect()
+        result.read()

@@ -130,8 +130,8 @@ class Worker(WorkerBase):
 
     def reload_weights(self, weights_iterator: object = None, weights_path: str | None = None,
                        is_checkpoint_format: bool = True) -> None:
-        """Load the weights again from the served checkpoint's files; the engine loads no other
-        source."""
+        """Reads the served checkpoint's files again and swaps the weights in; weights from an
+        iterator or another path are refused (the engine only loads checkpoints)."""
         for name, value, default in (("weights_iterator", weights_iterator, None),
                                      ("weights_path", weights_path, None),
                                      ("is_checkpoint_format", is_checkpoint_format, True)):
