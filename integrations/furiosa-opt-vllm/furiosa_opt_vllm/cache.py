@@ -7,6 +7,9 @@ from __future__ import annotations
 import torch
 
 BLOCK = 16
+# A layer's page holds K[kv_heads][16][head] then V[kv_heads][16][head]: heads outermost, in vLLM's
+# naming the "HND" layout. It is the engine's fixed layout, so it is the only one offered.
+LAYOUTS = ("HND",)
 
 
 def spec(model, model_config) -> dict:

@@ -159,6 +159,14 @@ class Worker(WorkerBase):
             return {}
         return kv.spec(self.model, self.model_config)
 
+    def get_supported_kv_cache_layouts(self) -> list[str]:
+        # No torch attention backend runs here for vLLM to ask; the engine's page layout is fixed.
+        return list(kv.LAYOUTS)
+
+    def get_cache_block_size_bytes(self) -> int:
+        """Bytes of one block across every layer (vLLM's page of each layer's spec)."""
+        return sum(int(s.page_size_bytes) for s in self.get_kv_cache_spec().values())
+
     def initialize_from_config(self, kv_cache_config) -> None:
         from furiosa_opt_engine import decoder as dec
 
