@@ -1,4 +1,5 @@
 #include "batch.h"
+#include "trace.h"
 
 #include "kernels/attention.cuh"
 
@@ -44,6 +45,10 @@ Cache::Cache(const Device& device, const CacheSpec& spec, int64_t blocks)
     layers_.push_back(std::move(b));
   }
   st->check_cuda(cudaStreamSynchronize(st->stream), "cache zero");
+  size_t bytes = 0;
+  for (size_t b : sizes) bytes += b;
+  log_event(LogLevel::Info, "KV cache: " + std::to_string(blocks) + " blocks, " + std::to_string(bytes >> 20) + " MiB on GPU " +
+                          std::to_string(st->ordinal));
 }
 
 void Cache::lend() {

@@ -595,6 +595,8 @@ HbmTensor DecoderModel::forward(const std::vector<Request>& requests, Cache& cac
       cudaGraphDestroy(graph);
       it->second.exec = exec;
       it->second.kernels = kernels;
+      log_event(LogLevel::Debug, "captured a decode graph: " + std::to_string(bucket) + " rows, " +
+                                     std::to_string(kernels) + " kernels");
       st->check_cuda(cudaGraphLaunch(exec, st->stream), "graph launch");
       launches_ += kernels;
     }

@@ -1,5 +1,9 @@
 #include "runtime.h"
 
+#include <cstdio>
+
+#include "trace.h"
+
 #include <cstdlib>
 
 #include <algorithm>
@@ -108,6 +112,7 @@ void DeviceState::check() const {
 }
 
 void DeviceState::fail(const std::string& what) {
+  if (poison.empty()) log_event(LogLevel::Error, "GPU " + std::to_string(ordinal) + " failed: " + what);
   if (poison.empty()) poison = what;
   throw DeviceError(what);
 }
@@ -174,6 +179,18 @@ Device::Device(std::vector<int> chips, int pes_begin, int pes_end, int rank) {
   state_->check_cuda(cudaStreamCreateWithFlags(&state_->stream, cudaStreamNonBlocking), "stream");
   state_->check_cuda(cudaMalloc(&state_->status, 64), "status word");
   state_->check_cuda(cudaMemset(state_->status, 0, 64), "status word");
+  {
+    cudaDeviceProp prop{};
+    size_t free_b = 0, total = 0;
+    if (cudaGetDeviceProperties(&prop, state_->ordinal) == cudaSuccess && cudaMemGetInfo(&free_b, &total) == cudaSuccess) {
+      char line[256];
+      std::snprintf(line, sizeof(line), "GPU %d (%s, %d SMs): %.1f of %.1f GiB free; rank %d of %zu", state_->ordinal,
+                    prop.name, prop.multiProcessorCount, free_b / 1073741824.0, total / 1073741824.0, rank,
+                    chips.size());
+      log_event(LogLevel::Info, line);
+    }
+    cudaGetLastError();
+  }
   if (const char* f = std::getenv("FOA_FAULT")) {
     // <kind>:<countdown>, e.g. "launch:10": the eleventh kernel launch fails.
     const std::string spec(f);

@@ -6,11 +6,45 @@
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
+#include <deque>
 #include <fstream>
 #include <iomanip>
 #include <sstream>
 
 namespace foa::engine {
+
+namespace {
+std::mutex g_log_mu;
+std::deque<std::pair<int, std::string>> g_logs;
+size_t g_dropped = 0;
+std::atomic<bool> g_log_pending{false};
+}  // namespace
+
+void log_event(LogLevel level, std::string message) {
+  std::lock_guard<std::mutex> g(g_log_mu);
+  if (g_logs.size() >= kLogQueue) {
+    g_logs.pop_front();
+    ++g_dropped;
+  }
+  g_logs.emplace_back(static_cast<int>(level), std::move(message));
+  g_log_pending.store(true, std::memory_order_release);
+}
+
+bool logs_pending() { return g_log_pending.load(std::memory_order_acquire); }
+
+std::vector<std::pair<int, std::string>> take_logs() {
+  std::lock_guard<std::mutex> g(g_log_mu);
+  std::vector<std::pair<int, std::string>> out;
+  if (g_dropped > 0) {
+    out.emplace_back(static_cast<int>(LogLevel::Warning),
+                     std::to_string(g_dropped) + " older engine log records were dropped (queue full)");
+    g_dropped = 0;
+  }
+  out.insert(out.end(), std::make_move_iterator(g_logs.begin()), std::make_move_iterator(g_logs.end()));
+  g_logs.clear();
+  g_log_pending.store(false, std::memory_order_release);
+  return out;
+}
 
 namespace {
 
@@ -155,7 +189,12 @@ std::string Tracer::flush(const std::string& path_in) {
     cudaEventDestroy(e);
   }
   events_.clear();
-  return f.good() ? path : "";
+  if (!f.good()) {
+    log_event(LogLevel::Warning, "trace: could not write " + path);
+    return "";
+  }
+  log_event(LogLevel::Info, "trace written to " + path);
+  return path;
 }
 
 TraceScope::TraceScope(const char* name, const char* cat, TraceLevel level)

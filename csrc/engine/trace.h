@@ -26,6 +26,16 @@
 
 namespace foa::engine {
 
+// Engine log records for Python's `logging` (logger "furiosa_opt_engine"). Engine code queues them
+// from any thread and under any lock: queuing calls no Python and takes only the queue's own lock.
+// The binding hands the queue to `logging` on the calling thread when a public call returns or
+// raises. Levels are Python's numbers; the queue keeps the newest kLogQueue records.
+enum class LogLevel : int { Debug = 10, Info = 20, Warning = 30, Error = 40 };
+constexpr size_t kLogQueue = 1024;
+void log_event(LogLevel level, std::string message);
+bool logs_pending();
+std::vector<std::pair<int, std::string>> take_logs();
+
 enum class TraceLevel : int { Off = 0, Info = 1, Debug = 2, Trace = 3 };
 
 TraceLevel trace_level();

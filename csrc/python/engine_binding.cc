@@ -23,6 +23,24 @@
 namespace py = pybind11;
 using namespace foa::engine;
 
+void emit_logs() {
+  if (!logs_pending()) return;
+  const auto records = take_logs();
+  try {
+    py::object logger = py::module_::import("logging").attr("getLogger")("furiosa_opt_engine");
+    for (const auto& [level, message] : records) logger.attr("log")(level, message);
+  } catch (py::error_already_set& e) {
+    e.discard_as_unraisable("furiosa_opt_engine log");
+  }
+}
+
+LogsOnExit::~LogsOnExit() {
+  try {
+    emit_logs();
+  } catch (...) {
+  }
+}
+
 namespace {
 
 // ------------------------------------------------------------------------------------ helpers
@@ -224,6 +242,7 @@ void bind_engine(py::module_& m) {
 
   py::class_<Device>(m, "Device", "An opened device; memory sizes are bytes per chip.")
       .def(py::init([](const Placement& p, std::optional<int> rank) {
+             LogsOnExit logs;
              // The process's rank among the placement's chips: given (a framework that runs several
              // replicas in one process group), else the process group's rank.
              const int r = rank ? *rank : process_rank(p.chips.size());
@@ -412,6 +431,7 @@ void bind_engine(py::module_& m) {
 
   py::class_<PyCache>(decoder, "Cache", "The storage of a CacheSpec on the decoder's device.")
       .def(py::init([](const PyCacheSpec& spec, int64_t blocks) {
+             LogsOnExit logs;
              if (blocks <= 0) throw ValueError("cache blocks must be positive");
              py::gil_scoped_release nogil;
              return PyCache{std::make_shared<Cache>(spec.device, spec.spec, blocks), spec.device};
@@ -504,6 +524,7 @@ void bind_engine(py::module_& m) {
   // ---------------------------------------------------------------- decoders
   auto forward = [](PyDecoder& d, const std::vector<PyRequest*>& requests, PyCache& cache,
                     const py::object& adapters) {
+    LogsOnExit logs;
     std::vector<Request> reqs;
     reqs.reserve(requests.size());
     for (const PyRequest* pr : requests) {
@@ -905,11 +926,18 @@ void bind_engine(py::module_& m) {
      "Adds a host span (the clock of _trace_now_ns) to the trace, for a framework's own phases; "
      "`args` is a JSON object written as the span's args.");
   m.def("_trace_flush", [](const std::string& path) {
+    LogsOnExit logs;
     py::gil_scoped_release nogil;
     return Tracer::get().flush(path);
   }, py::arg("path") = std::string(),
      "Writes the spans so far as Chrome trace JSON (default: FURIOSA_OPT_OUT_DIR/trace-<pid>.json) "
      "and clears them; returns the path, or '' when there was nothing to write.");
+  m.def("_log", [](int level, const std::string& message, int times) {
+    LogsOnExit logs;
+    for (int i = 0; i < times; ++i) log_event(static_cast<LogLevel>(level), message);
+  }, py::arg("level"), py::arg("message"), py::arg("times") = 1,
+     "Queues a record `times` times as engine code does (Python's level numbers); the records reach "
+     "`logging` when this call returns.");
   m.def("_tp_connect", [](PyDecoder& d, const std::vector<py::bytes>& handles) {
     std::vector<std::string> hs;
     for (const auto& h : handles) hs.push_back(std::string(h));

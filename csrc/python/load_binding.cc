@@ -2,6 +2,8 @@
 // weight is read, and the strict load into device memory.
 #include <pybind11/pybind11.h>
 
+#include <chrono>
+
 #include "engine/lora.h"
 #include <pybind11/stl.h>
 
@@ -9,6 +11,7 @@
 #include "engine/checkpoint.h"
 #include "engine/encoder.h"
 #include "engine/registry.h"
+#include "engine/trace.h"
 #include "python/pytypes.h"
 
 namespace py = pybind11;
@@ -83,8 +86,13 @@ void bind_checkpoint_and_load(py::module_& m) {
              const std::string p = py::str(py::module_::import("os").attr("fspath")(path));
              std::optional<Json> cfg;
              if (!config.is_none()) cfg = to_json(config);
-             py::gil_scoped_release nogil;
-             return PyCheckpoint{std::make_shared<Checkpoint>(Checkpoint::open(p, cfg ? &*cfg : nullptr))};
+             LogsOnExit logs;
+             auto ck = [&] {
+               py::gil_scoped_release nogil;
+               return std::make_shared<Checkpoint>(Checkpoint::open(p, cfg ? &*cfg : nullptr));
+             }();
+             log_event(LogLevel::Debug, p + ": " + std::to_string(ck->tensors().size()) + " tensors");
+             return PyCheckpoint{ck};
            }),
            py::arg("path"), py::arg("config") = py::none())
       .def("read", [](const PyCheckpoint& c) {
@@ -167,6 +175,8 @@ void bind_checkpoint_and_load(py::module_& m) {
         return d;
       }, py::arg("checkpoint"))
       .def("load", [](const LoadOptions& o, const PyCheckpoint& c, const Device& device) -> py::object {
+        LogsOnExit logs;
+        const auto t0 = std::chrono::steady_clock::now();
         const Selection s = select(o, *c.ck);
         if (device.chips() != s.chips)
           throw ValueError("the device opens " + std::to_string(device.chips()) + " chips, the load " +
@@ -191,6 +201,10 @@ void bind_checkpoint_and_load(py::module_& m) {
         py::object decoder = make_decoder(s, model, o.batch_invariant);
         if (s.chips > 1)
           py::module_::import("furiosa_opt_models_b200.parallel.tp").attr("attach")(decoder, device);
+        const double secs = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        log_event(LogLevel::Info, s.architecture + " loaded on " + std::to_string(s.chips) + " GPU(s) from " +
+                                      c.ck->directory() + " in " + std::to_string(secs).substr(0, 5) + " s" +
+                                      (o.batch_invariant ? " (batch invariant)" : ""));
         return decoder;
       }, py::arg("checkpoint"), py::arg("device"));
 

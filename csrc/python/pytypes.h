@@ -8,6 +8,14 @@
 #include "engine/lora.h"
 #include "engine/model.h"
 
+// Hands the engine's queued log records to Python's `logging` (logger "furiosa_opt_engine"); the
+// GIL is held. `LogsOnExit` does it when a binding call returns or raises: declare it first in the
+// call's body, so that it runs after any `gil_scoped_release` in the body has ended.
+void emit_logs();
+struct LogsOnExit {
+  ~LogsOnExit();
+};
+
 // A loaded decoder: the model, and its load's descriptive fields.
 struct PyDecoder {
   std::shared_ptr<foa::engine::DecoderModel> model;
