@@ -7,6 +7,7 @@ namespace py = pybind11;
 void bind_ops(py::module_& m);
 void bind_engine(py::module_& m);
 void bind_encoder(py::module_& m);
+void bind_emulate(py::module_& m);
 
 PYBIND11_MODULE(_native, m) {
   m.doc() = "Native engine of furiosa_opt_engine for NVIDIA Blackwell (sm_100a).";
@@ -14,4 +15,5 @@ PYBIND11_MODULE(_native, m) {
   bind_ops(ops);
   bind_engine(m);
   bind_encoder(m);
+  bind_emulate(m);
 }
