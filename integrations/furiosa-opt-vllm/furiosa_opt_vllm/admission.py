@@ -191,7 +191,6 @@ NEUTRAL = (
     ("bad_words", None),
     ("structured_outputs", None),
     ("logprob_token_ids", None),
-    ("thinking_token_budget", None),
     ("extra_args", None),
 )
 

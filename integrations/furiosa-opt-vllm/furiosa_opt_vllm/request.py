@@ -19,6 +19,7 @@ class State:
     pool: object = None  # pooling.Pool of a pooling request, or None
     # The newest sampled token while it is still on the device: (engine output, row), or None.
     tail: tuple | None = None
+    budget: object = None  # thinking.Budget of a request with a thinking-token budget, or None
 
     def scheduled(self, n: int) -> list[int]:
         """The `n` tokens this step feeds (after the history)."""

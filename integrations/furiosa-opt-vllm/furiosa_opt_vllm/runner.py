@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from . import batch, pooling, speculation
+from . import batch, pooling, speculation, thinking
 from .paging import BlockTable, first_group
 from .request import State
 
@@ -50,6 +50,10 @@ class Pending:
                     st.computed -= len(d) - (len(got) - 1)
             else:
                 got = rows
+            if st is not None and st.budget is not None:
+                forced = thinking.apply(st.budget, got)
+                st.computed -= len(got) - len(forced)  # rows verified against a replaced token
+                got = forced
             if st is not None:
                 st.tokens.extend(got)
             sampled.append(got)
@@ -57,7 +61,7 @@ class Pending:
 
 
 class Runner:
-    def __init__(self, model, device, cache, adapters=None, pooling_config=None):
+    def __init__(self, model, device, cache, adapters=None, pooling_config=None, reasoning=None):
         import furiosa_opt_engine as engine
         from furiosa_opt_engine import decoder as dec
 
@@ -67,6 +71,8 @@ class Runner:
         # Pooling models: {"task": "embed" | "classify", "method": pooling type, "labels": n}.
         self.pooling_config = pooling_config
         self.pooled: list = []  # each request's pooled output of the last step (None: not yet)
+        # (start marker IDs, end marker IDs) of a reasoning model (vLLM's reasoning config), or None.
+        self.reasoning = reasoning
         self.states: dict[str, State] = {}
         # Steps whose tokens are still on the device, oldest first. vLLM collects a step before it
         # issues the second one after it on the driver rank; the other tensor-parallel ranks are
@@ -83,6 +89,14 @@ class Runner:
             self.states[nr.req_id] = State(prompt, len(prompt), nr.num_computed_tokens,
                                            BlockTable(first_group(nr.block_ids)),
                                            lora=getattr(nr, "lora_request", None))
+            sampling = getattr(nr, "sampling_params", None)
+            budget = getattr(sampling, "thinking_token_budget", None)
+            if budget is not None:
+                if not getattr(self, "reasoning", None):
+                    raise ValueError(f"{nr.req_id}: thinking_token_budget needs the model's reasoning markers "
+                                     "(start vLLM with --reasoning-parser)")
+                self.states[nr.req_id].budget = thinking.Budget(budget, *self.reasoning)
+                self.states[nr.req_id].budget.reset(prompt)
             params = getattr(nr, "pooling_params", None)
             if self.pooling_config is not None:
                 if params is None:
@@ -99,6 +113,8 @@ class Runner:
                 if rid in all_tokens:
                     st.tokens = list(all_tokens[rid])
                     st.tail = None
+                    if st.budget is not None:
+                        st.budget.reset(st.tokens, st.prompt)
             elif nb is not None:
                 st.table.append(first_group(nb))
             st.computed = cr.num_computed_tokens[i]
@@ -183,6 +199,11 @@ class Runner:
             return pending.collect()
         self.uncollected.append(pending)
         return pending
+
+    def reads_each_step(self, so) -> bool:
+        """Whether a step's tokens must reach the host as it is issued: a scheduled request has a
+        thinking budget, which may replace the engine's token."""
+        return any(getattr(self.states.get(r), "budget", None) is not None for r in so.num_scheduled_tokens)
 
     def pool_step(self, so) -> tuple[list[str], list[list[int]]]:
         """A step of a pooling model: prompt chunks whose kept rows (hidden values or label

@@ -178,7 +178,12 @@ class Worker(WorkerBase):
             return
 
         self.cache = dec.Cache(self.model.cache, int(kv_cache_config.num_blocks))
-        self.runner = Runner(self.model, self.engine_device, self.cache, self.adapters, self.pooling_config())
+        rc = getattr(self.vllm_config, "reasoning_config", None)
+        markers = None
+        if rc is not None and getattr(rc, "reasoning_end_token_ids", None):
+            markers = (list(getattr(rc, "reasoning_start_token_ids", None) or []), list(rc.reasoning_end_token_ids))
+        self.runner = Runner(self.model, self.engine_device, self.cache, self.adapters, self.pooling_config(),
+                             reasoning=markers)
         if self.proposer is not None:
             self.proposer.attach(self.runner, int(kv_cache_config.num_blocks))
         if self.vllm_config.kv_transfer_config is not None:
@@ -309,7 +314,10 @@ class Worker(WorkerBase):
             return
         if self.asynchronous():
             # The tokens stay on the device; vLLM collects them after it has issued the next step.
-            self.pending = Collected(self.runner.step(scheduler_output, collect=False), self)
+            step = self.runner.step(scheduler_output, collect=False)
+            if self.runner.reads_each_step(scheduler_output):
+                step.collect()  # a thinking budget may replace a token: the next step feeds it from the host
+            self.pending = Collected(step, self)
             return
         ids, sampled = self.runner.step(scheduler_output)
         self.pending = ModelRunnerOutput(req_ids=ids, req_id_to_index={r: i for i, r in enumerate(ids)},

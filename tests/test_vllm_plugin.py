@@ -576,3 +576,66 @@ def test_overrides_contract():
     with pytest.raises(admission.Refused) as e:
         admission.check(cfg)
     assert e.value.option == "hf_overrides"
+
+
+def test_thinking_budget_forces_the_end_marker():
+    from furiosa_opt_vllm import thinking
+
+    start, end = [100], [101, 102]
+    b = thinking.Budget(3, start, end)
+    b.reset([5, 6])
+    out = [b.choose(t) for t in [100, 7, 8, 9, 10, 11, 12, 13]]
+    # Three thinking tokens after the start marker, then the two end tokens, then the model again.
+    assert out == [100, 7, 8, 9, 101, 102, 12, 13]
+    b = thinking.Budget(5, start, end)
+    b.reset([5])
+    assert [b.choose(t) for t in [100, 7, 101, 102, 8, 9, 10, 11, 12, 13]] == [100, 7, 101, 102, 8, 9, 10, 11, 12, 13]
+    b = thinking.Budget(0, start, end)
+    b.reset([5, 100], prompt=2)  # the prompt opens the section: no token of thought is allowed
+    assert [b.choose(t) for t in [7, 8, 9]] == [101, 102, 9]
+    b = thinking.Budget(2, [], [101])  # no start marker: thinking from the first token
+    b.reset([1, 2, 3], prompt=3)
+    assert [b.choose(t) for t in [7, 8, 9]] == [7, 8, 101]
+    with pytest.raises(ValueError):
+        thinking.Budget(2, start, [])
+
+
+def test_runner_applies_thinking_budgets_and_feeds_forced_tokens():
+    """The fake engine's token is its input + 1; a budget of 2 after the start marker 13 forces the
+    end marker 50, which the next step feeds from the host."""
+    from types import SimpleNamespace
+
+    runner, eng = _runner(rows=8)
+    runner.reasoning = ([13], [50])
+    new = [SimpleNamespace(req_id="a", prompt_token_ids=[10, 11, 12], num_computed_tokens=0, block_ids=([0, 1],),
+                           sampling_params=SimpleNamespace(thinking_token_budget=2))]
+    got = [runner.step(_sched(new=new, counts={"a": 3}))[1][0]]
+    for i in range(5):
+        got.append(runner.step(_sched(cached=[("a", 3 + i)], counts={"a": 1}))[1][0])
+    # 13 opens thinking; 14 and 15 spend the budget; 50 is forced; 51, 52 follow it.
+    assert [g[0] for g in got] == [13, 14, 15, 50, 51, 52]
+    assert [t.values for _, t, _ in eng.calls[4]] == [[50]]
+    assert runner.states["a"].tokens == [10, 11, 12, 13, 14, 15, 50, 51, 52]
+    assert runner.reads_each_step(_sched(cached=[("a", 9)], counts={"a": 1}))
+
+
+def test_a_forced_token_drops_the_accepted_drafts_after_it():
+    from furiosa_opt_vllm import thinking
+    from furiosa_opt_vllm.request import State
+
+    b = thinking.Budget(1, [13], [50])
+    b.reset([13], prompt=1)
+    st = State([13], 1, 1, None, budget=b)
+    # Speculative step: the engine's tokens 20, 21, 22 were accepted; the budget forces 50 after 20.
+    assert thinking.apply(st.budget, [20, 21, 22]) == [20, 50]
+
+
+def test_budgets_need_reasoning_markers():
+    from types import SimpleNamespace
+
+    runner, _ = _runner(rows=8)
+    runner.reasoning = None
+    new = [SimpleNamespace(req_id="a", prompt_token_ids=[10], num_computed_tokens=0, block_ids=([0],),
+                           sampling_params=SimpleNamespace(thinking_token_budget=2))]
+    with pytest.raises(ValueError, match="reasoning-parser"):
+        runner.step(_sched(new=new, counts={"a": 1}))
