@@ -1,0 +1,41 @@
+"""Host forwards of catalog families against transformers' own modules with the same random
+weights: BERT and XLM-RoBERTa encoders (final hidden rows and pooled rows, padded batches)."""
+
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from furiosa_opt_models_b200.models import catalog_forward  # noqa: E402
+
+
+@pytest.mark.parametrize("family", ["bert", "xlm_roberta"])
+def test_encoder_matches_transformers(tmp_path, family):
+    t = transformers
+    kw = dict(hidden_size=64, num_hidden_layers=2, num_attention_heads=4, intermediate_size=128, vocab_size=100,
+              max_position_embeddings=40)
+    cfg, cls = (t.BertConfig(**kw), t.BertModel) if family == "bert" else (t.XLMRobertaConfig(**kw), t.XLMRobertaModel)
+    torch.manual_seed(0)
+    model = cls(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(3, 100, (2, 9))
+    mask = torch.ones_like(ids)
+    mask[1, 6:] = 0
+    ids[1, 6:] = cfg.pad_token_id
+    types = torch.zeros_like(ids)
+    if family == "bert":
+        types[:, 5:] = 1
+    with torch.no_grad():
+        want = model(input_ids=ids, attention_mask=mask, token_type_ids=types)
+    hidden, pooled = catalog_forward.encoder(str(tmp_path), ids, mask, types)
+    real = mask.bool()
+    torch.testing.assert_close(hidden[real], want.last_hidden_state[real], rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(pooled, want.pooler_output, rtol=1e-4, atol=1e-4)
+
+
+def test_encoder_refuses_other_families(tmp_path):
+    t = transformers
+    cfg = t.MambaConfig(hidden_size=32, num_hidden_layers=1, vocab_size=50, state_size=8)
+    t.MambaForCausalLM(cfg).save_pretrained(str(tmp_path))
+    with pytest.raises(ValueError, match="not a BERT-style encoder"):
+        catalog_forward.encoder(str(tmp_path), torch.zeros(1, 3, dtype=torch.long))
