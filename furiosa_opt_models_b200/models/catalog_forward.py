@@ -4,6 +4,9 @@ will be tested against, and a CPU path for small encoders.
 
 - `encoder`: BERT and XLM-RoBERTa (BGE-M3) encoders, post-norm layers with exact GELU: the final
   hidden rows of each sequence and, where the composition has one, the pooled first row.
+- `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
+  recurrence it is (state[h] <- exp(dt A[h]) state[h] + dt x[h] B^T, y[h] = state[h] C + D[h] x[h]),
+  the oracle of a future chunked (SSD) scan kernel.
 """
 
 from __future__ import annotations
@@ -83,3 +86,70 @@ def encoder(directory: str, input_ids: torch.Tensor, attention_mask: torch.Tenso
                                              p + "pooler.dense.weight" in comp.optional):
         pooled = torch.tanh(x[:, 0] @ t[p + "pooler.dense.weight"].T + t[p + "pooler.dense.bias"])
     return x, pooled
+
+
+def _rms(x, w, eps):
+    return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+
+def mamba2(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a Mamba-2 checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "mamba2":
+        raise ValueError(f"{comp.architecture}: not a Mamba-2 model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    d = int(cfg["hidden_size"])
+    inner = int(cfg.get("expand", 2)) * d
+    heads, groups, state = int(cfg["num_heads"]), int(cfg.get("n_groups", 1)), int(cfg["state_size"])
+    head_dim = inner // heads
+    eps = float(cfg.get("layer_norm_epsilon", 1e-5))
+    lo, hi = (cfg.get("time_step_limit") or (0.0, float("inf")))
+    lo = float(lo) if lo is not None else 0.0
+    hi = float(hi) if isinstance(hi, (int, float)) else float("inf")
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["backbone.embeddings.weight"][ids]
+    for layer in range(int(cfg["num_hidden_layers"])):
+        p = f"backbone.layers.{layer}."
+        m = p + "mixer."
+        h = _rms(x, t[p + "norm.weight"], eps)
+        proj = h @ t[m + "in_proj.weight"].T
+        if m + "in_proj.bias" in t:
+            proj = proj + t[m + "in_proj.bias"]
+        conv_dim = inner + 2 * groups * state
+        z, xbc, dt = proj.split([inner, conv_dim, heads], dim=-1)
+        # Causal depthwise convolution over the tokens, then SiLU.
+        w = t[m + "conv1d.weight"][:, 0, :]  # [conv_dim, kernel]
+        k = w.shape[1]
+        padded = torch.cat([torch.zeros(k - 1, conv_dim), xbc])
+        conv = torch.stack([(padded[i : i + k] * w.T).sum(0) for i in range(n)])
+        if m + "conv1d.bias" in t:
+            conv = conv + t[m + "conv1d.bias"]
+        conv = torch.nn.functional.silu(conv)
+        xs, bs, cs = conv.split([inner, groups * state, groups * state], dim=-1)
+        dt = torch.nn.functional.softplus(dt + t[m + "dt_bias"]).clamp(lo, hi)  # [n, heads]
+        a = -torch.exp(t[m + "A_log"])
+        s = torch.zeros(heads, head_dim, state)
+        ys = []
+        per = heads // groups
+        for i in range(n):
+            xh = xs[i].view(heads, head_dim)
+            b = bs[i].view(groups, state).repeat_interleave(per, dim=0)  # [heads, state]
+            c = cs[i].view(groups, state).repeat_interleave(per, dim=0)
+            s = s * torch.exp(dt[i] * a)[:, None, None] + (dt[i][:, None] * xh)[:, :, None] * b[:, None, :]
+            ys.append((s @ c[:, :, None])[..., 0] + t[m + "D"][:, None] * xh)
+        y = torch.stack(ys).reshape(n, inner)
+        y = _rms(y * torch.nn.functional.silu(z), t[m + "norm.weight"], eps)
+        out = y @ t[m + "out_proj.weight"].T
+        if m + "out_proj.bias" in t:
+            out = out + t[m + "out_proj.bias"]
+        x = x + out
+    x = _rms(x, t["backbone.norm_f.weight"], eps)
+    head = t.get("lm_head.weight", t["backbone.embeddings.weight"])
+    return x @ head.T

@@ -39,3 +39,22 @@ def test_encoder_refuses_other_families(tmp_path):
     t.MambaForCausalLM(cfg).save_pretrained(str(tmp_path))
     with pytest.raises(ValueError, match="not a BERT-style encoder"):
         catalog_forward.encoder(str(tmp_path), torch.zeros(1, 3, dtype=torch.long))
+
+
+def test_mamba2_recurrence_matches_transformers(tmp_path):
+    """The token-by-token selective scan against transformers' chunked scan (its CPU path)."""
+    t = transformers
+    cfg = t.Mamba2Config(hidden_size=32, num_hidden_layers=2, vocab_size=60, state_size=8, n_groups=2, head_dim=8,
+                         num_heads=8, expand=2, chunk_size=4, tie_word_embeddings=False)
+    torch.manual_seed(1)
+    model = t.Mamba2ForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for name, prm in model.named_parameters():
+            if name.endswith(("A_log", "dt_bias", "D")):
+                prm.uniform_(-0.5, 0.5)
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 60, (1, 11))
+    with torch.no_grad():
+        want = model(input_ids=ids).logits[0]
+    got = catalog_forward.mamba2(str(tmp_path), ids[0])
+    torch.testing.assert_close(got, want, rtol=2e-4, atol=2e-4)
