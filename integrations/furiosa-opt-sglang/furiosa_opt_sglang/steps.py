@@ -5,7 +5,9 @@ SGLang's overlap scheduler issues step n+1 before it processes step n's result. 
 here returns once its engine calls are submitted: the selected tokens stay on the device, each
 request's next decode row reads its input token from there (an engine request may take its tokens
 from any device tensor), and the scheduler hook `collect` reads them (one device-to-host copy per
-engine call) just before SGLang processes the step. Steps that need scores (sampling, logprobs,
+engine call) just before SGLang processes the step. Issued steps are numbered: step n is refused
+while step n - 2 (overlap) or n - 1 (synchronous schedule) is still unread, which is SGLang's
+contract broken. Steps that need scores (sampling, logprobs,
 penalties, grammars, logit bias) are refused: the engine's decoder calls return tokens, not logits.
 The reference's contract: integrations/furiosa-opt-sglang/furiosa_opt_sglang/generation/__init__.py
 (`issue`, `Sampled`, `device_argmax`) and generation/sequence.py (calls of at most `rows` rows).
