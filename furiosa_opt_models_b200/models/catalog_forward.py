@@ -4,6 +4,8 @@ will be tested against, and a CPU path for small encoders.
 
 - `encoder`: BERT and XLM-RoBERTa (BGE-M3) encoders, post-norm layers with exact GELU: the final
   hidden rows of each sequence and, where the composition has one, the pooled first row.
+- `clip`: CLIP's text and image embeddings (pre-norm towers with quick-GELU, the text tower's
+  causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
 - `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
   recurrence it is (state[h] <- exp(dt A[h]) state[h] + dt x[h] B^T, y[h] = state[h] C + D[h] x[h]),
   the oracle of a future chunked (SSD) scan kernel.
@@ -153,3 +155,74 @@ def mamba2(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
     x = _rms(x, t["backbone.norm_f.weight"], eps)
     head = t.get("lm_head.weight", t["backbone.embeddings.weight"])
     return x @ head.T
+
+
+def _clip_tower(t, p, cfg, x, causal: bool):
+    """Pre-norm CLIP layers over rows x [batch, n, d]."""
+    heads = int(cfg.get("num_attention_heads", 8))
+    eps = float(cfg.get("layer_norm_eps", 1e-5))
+    act = cfg.get("hidden_act", "quick_gelu")
+    batch, n, d = x.shape
+    hd = d // heads
+    bias = torch.triu(torch.full((n, n), float("-inf")), 1) if causal else None
+    for layer in range(int(cfg["num_hidden_layers"])):
+        q = f"{p}encoder.layers.{layer}."
+
+        def lin(name, v):
+            return v @ t[q + name + ".weight"].T + t[q + name + ".bias"]
+
+        h = _layer_norm(x, t[q + "layer_norm1.weight"], t[q + "layer_norm1.bias"], eps)
+        split = lambda v: v.view(batch, n, heads, hd).transpose(1, 2)  # noqa: E731
+        qs, ks, vs = (split(lin(f"self_attn.{m}_proj", h)) for m in ("q", "k", "v"))
+        scores = qs @ ks.transpose(-1, -2) / math.sqrt(hd)
+        if bias is not None:
+            scores = scores + bias
+        att = (torch.softmax(scores, dim=-1) @ vs).transpose(1, 2).reshape(batch, n, d)
+        x = x + lin("self_attn.out_proj", att)
+        h = _layer_norm(x, t[q + "layer_norm2.weight"], t[q + "layer_norm2.bias"], eps)
+        h = lin("mlp.fc1", h)
+        h = h * torch.sigmoid(1.702 * h) if act == "quick_gelu" else torch.nn.functional.gelu(h)
+        x = x + lin("mlp.fc2", h)
+    return x
+
+
+def clip(directory: str, input_ids: torch.Tensor | None = None, pixels: torch.Tensor | None = None):
+    """(text embeddings [batch, proj] or None, image embeddings [batch, proj] or None) of a
+    `CLIPModel` checkpoint, L2-normalised; `pixels` are [batch, channels, size, size]."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.architecture != "CLIPModel":
+        raise ValueError(f"{comp.architecture}: not a CLIPModel")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    text = image = None
+    if input_ids is not None:
+        tc = cfg.get("text_config", {})
+        ids = input_ids.long()
+        n = ids.shape[1]
+        x = t["text_model.embeddings.token_embedding.weight"][ids] + t["text_model.embeddings.position_embedding.weight"][:n]
+        x = _clip_tower(t, "text_model.", tc, x, causal=True)
+        x = _layer_norm(x, t["text_model.final_layer_norm.weight"], t["text_model.final_layer_norm.bias"],
+                        float(tc.get("layer_norm_eps", 1e-5)))
+        eos = int(tc.get("eos_token_id", 2))
+        # The end-of-text row: the first eos token (the highest id for configs that predate it).
+        rows = (ids == eos).int().argmax(-1) if eos != 2 else ids.argmax(-1)
+        text = x[torch.arange(ids.shape[0]), rows] @ t["text_projection.weight"].T
+        text = torch.nn.functional.normalize(text, dim=-1)
+    if pixels is not None:
+        vc = cfg.get("vision_config", {})
+        w = t["vision_model.embeddings.patch_embedding.weight"]
+        patch = w.shape[-1]
+        x = torch.nn.functional.conv2d(pixels.float(), w, stride=patch).flatten(2).transpose(1, 2)
+        cls = t["vision_model.embeddings.class_embedding"].expand(x.shape[0], 1, -1)
+        x = torch.cat([cls, x], dim=1) + t["vision_model.embeddings.position_embedding.weight"]
+        eps = float(vc.get("layer_norm_eps", 1e-5))
+        x = _layer_norm(x, t["vision_model.pre_layrnorm.weight"], t["vision_model.pre_layrnorm.bias"], eps)
+        x = _clip_tower(t, "vision_model.", vc, x, causal=False)
+        pooled = _layer_norm(x[:, 0], t["vision_model.post_layernorm.weight"], t["vision_model.post_layernorm.bias"], eps)
+        image = torch.nn.functional.normalize(pooled @ t["visual_projection.weight"].T, dim=-1)
+    return text, image

@@ -58,3 +58,24 @@ def test_mamba2_recurrence_matches_transformers(tmp_path):
         want = model(input_ids=ids).logits[0]
     got = catalog_forward.mamba2(str(tmp_path), ids[0])
     torch.testing.assert_close(got, want, rtol=2e-4, atol=2e-4)
+
+
+def test_clip_embeddings_match_transformers(tmp_path):
+    t = transformers
+    cfg = t.CLIPConfig(text_config=dict(hidden_size=32, intermediate_size=64, num_hidden_layers=2,
+                                        num_attention_heads=4, vocab_size=50, max_position_embeddings=12,
+                                        eos_token_id=49),
+                       vision_config=dict(hidden_size=48, intermediate_size=96, num_hidden_layers=2,
+                                          num_attention_heads=4, image_size=16, patch_size=4),
+                       projection_dim=24)
+    torch.manual_seed(3)
+    model = t.CLIPModel(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 48, (2, 7))
+    ids[:, -1] = 49  # end of text
+    pixels = torch.randn(2, 3, 16, 16)
+    with torch.no_grad():
+        want = model(input_ids=ids, pixel_values=pixels)
+    text, image = catalog_forward.clip(str(tmp_path), ids, pixels)
+    torch.testing.assert_close(text, want.text_embeds, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(image, want.image_embeds, rtol=1e-4, atol=1e-4)
