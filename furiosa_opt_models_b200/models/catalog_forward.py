@@ -4,6 +4,9 @@ will be tested against, and a CPU path for small encoders.
 
 - `encoder`: BERT and XLM-RoBERTa (BGE-M3) encoders, post-norm layers with exact GELU: the final
   hidden rows of each sequence and, where the composition has one, the pooled first row.
+- `t5_encoder`: the T5 / mT5 encoder stack (RMSNorm before each block, unscaled attention with
+  bidirectional relative-position buckets from the first block, ReLU or gated-GELU feed-forward):
+  final hidden rows, as a diffusion pipeline's text encoder reads them.
 - `clip`: CLIP's text and image embeddings (pre-norm towers with quick-GELU, the text tower's
   causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
 - `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
@@ -226,3 +229,60 @@ def clip(directory: str, input_ids: torch.Tensor | None = None, pixels: torch.Te
         pooled = _layer_norm(x[:, 0], t["vision_model.post_layernorm.weight"], t["vision_model.post_layernorm.bias"], eps)
         image = torch.nn.functional.normalize(pooled @ t["visual_projection.weight"].T, dim=-1)
     return text, image
+
+
+def _t5_buckets(n: int, buckets: int, max_distance: int) -> torch.Tensor:
+    """Bidirectional relative-position buckets [n, n] (Raffel et al. 2020): half the buckets a
+    direction, exact for small distances, logarithmic up to `max_distance`."""
+    rel = torch.arange(n)[None, :] - torch.arange(n)[:, None]  # key - query
+    half = buckets // 2
+    out = (rel > 0).long() * half
+    dist = rel.abs()
+    exact = half // 2
+    log = exact + (torch.log(dist.float().clamp(min=1) / exact) / math.log(max_distance / exact)
+                   * (half - exact)).long()
+    log = torch.minimum(log, torch.full_like(log, half - 1))
+    return out + torch.where(dist < exact, dist, log)
+
+
+def t5_encoder(directory: str, input_ids: torch.Tensor, attention_mask: torch.Tensor | None = None) -> torch.Tensor:
+    """Final hidden rows [batch, tokens, d_model] of a T5 / mT5 checkpoint's encoder."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "t5":
+        raise ValueError(f"{comp.architecture}: not a T5 model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    heads, dkv = int(cfg["num_heads"]), int(cfg["d_kv"])
+    eps = float(cfg.get("layer_norm_epsilon", 1e-6))
+    gated = str(cfg.get("feed_forward_proj", "relu")).startswith("gated-")
+    ids = input_ids.long()
+    batch, n = ids.shape
+    mask = torch.ones_like(ids) if attention_mask is None else attention_mask.long()
+
+    def norm(x, w):
+        return w * (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps))
+
+    x = t["shared.weight"][ids]
+    rel = t["encoder.block.0.layer.0.SelfAttention.relative_attention_bias.weight"]  # [buckets, heads]
+    buckets = _t5_buckets(n, rel.shape[0], int(cfg.get("relative_attention_max_distance", 128)))
+    bias = rel[buckets].permute(2, 0, 1)[None] + (1.0 - mask[:, None, None, :].float()) * torch.finfo(torch.float32).min
+    for layer in range(int(cfg["num_layers"])):
+        p = f"encoder.block.{layer}.layer."
+        h = norm(x, t[p + "0.layer_norm.weight"])
+        split = lambda v: v.view(batch, n, heads, dkv).transpose(1, 2)  # noqa: E731
+        q, k, v = (split(h @ t[f"{p}0.SelfAttention.{m}.weight"].T) for m in ("q", "k", "v"))
+        att = torch.softmax(q @ k.transpose(-1, -2) + bias, dim=-1) @ v
+        x = x + att.transpose(1, 2).reshape(batch, n, heads * dkv) @ t[p + "0.SelfAttention.o.weight"].T
+        h = norm(x, t[p + "1.layer_norm.weight"])
+        ff = p + "1.DenseReluDense."
+        if gated:
+            mid = torch.nn.functional.gelu(h @ t[ff + "wi_0.weight"].T, approximate="tanh") * (h @ t[ff + "wi_1.weight"].T)
+        else:
+            mid = torch.relu(h @ t[ff + "wi.weight"].T)
+        x = x + mid @ t[ff + "wo.weight"].T
+    return norm(x, t["encoder.final_layer_norm.weight"])

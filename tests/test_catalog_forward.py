@@ -79,3 +79,21 @@ def test_clip_embeddings_match_transformers(tmp_path):
     text, image = catalog_forward.clip(str(tmp_path), ids, pixels)
     torch.testing.assert_close(text, want.text_embeds, rtol=1e-4, atol=1e-4)
     torch.testing.assert_close(image, want.image_embeds, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("ff", ["relu", "gated-gelu"])
+def test_t5_encoder_matches_transformers(tmp_path, ff):
+    t = transformers
+    cfg = t.T5Config(d_model=32, d_kv=8, d_ff=64, num_heads=4, num_layers=2, vocab_size=60, feed_forward_proj=ff,
+                     relative_attention_num_buckets=8, relative_attention_max_distance=20)
+    torch.manual_seed(4)
+    model = t.T5EncoderModel(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 60, (2, 30))
+    mask = torch.ones_like(ids)
+    mask[0, 25:] = 0
+    with torch.no_grad():
+        want = model(input_ids=ids, attention_mask=mask).last_hidden_state
+    got = catalog_forward.t5_encoder(str(tmp_path), ids, mask)
+    real = mask.bool()
+    torch.testing.assert_close(got[real], want[real], rtol=1e-4, atol=1e-4)
