@@ -7,6 +7,8 @@ will be tested against, and a CPU path for small encoders.
 - `t5_encoder`: the T5 / mT5 encoder stack (RMSNorm before each block, unscaled attention with
   bidirectional relative-position buckets from the first block, ReLU or gated-GELU feed-forward):
   final hidden rows, as a diffusion pipeline's text encoder reads them.
+- `whisper_encoder`: Whisper's audio encoder (two convolutions over log-mel frames, learned
+  positions, pre-norm layers, final LayerNorm): the rows its decoder cross-attends.
 - `clip`: CLIP's text and image embeddings (pre-norm towers with quick-GELU, the text tower's
   causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
 - `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
@@ -286,3 +288,42 @@ def t5_encoder(directory: str, input_ids: torch.Tensor, attention_mask: torch.Te
             mid = torch.relu(h @ t[ff + "wi.weight"].T)
         x = x + mid @ t[ff + "wo.weight"].T
     return norm(x, t["encoder.final_layer_norm.weight"])
+
+
+def whisper_encoder(directory: str, features: torch.Tensor) -> torch.Tensor:
+    """Encoder rows [batch, frames / 2, d_model] of a Whisper checkpoint for log-mel `features`
+    [batch, mel bins, frames]."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "whisper":
+        raise ValueError(f"{comp.architecture}: not a Whisper model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    p = "model.encoder."
+    x = torch.nn.functional.gelu(torch.nn.functional.conv1d(features.float(), t[p + "conv1.weight"],
+                                                            t[p + "conv1.bias"], padding=1))
+    x = torch.nn.functional.gelu(torch.nn.functional.conv1d(x, t[p + "conv2.weight"], t[p + "conv2.bias"], stride=2,
+                                                            padding=1))
+    x = x.transpose(1, 2)
+    batch, n, d = x.shape
+    x = x + t[p + "embed_positions.weight"][:n]
+    heads = int(cfg["encoder_attention_heads"])
+    hd = d // heads
+    for layer in range(int(cfg["encoder_layers"])):
+        q = f"{p}layers.{layer}."
+        h = _layer_norm(x, t[q + "self_attn_layer_norm.weight"], t[q + "self_attn_layer_norm.bias"], 1e-5)
+        split = lambda v: v.view(batch, n, heads, hd).transpose(1, 2)  # noqa: E731
+        qs = split(h @ t[q + "self_attn.q_proj.weight"].T + t[q + "self_attn.q_proj.bias"])
+        ks = split(h @ t[q + "self_attn.k_proj.weight"].T)  # keys carry no bias
+        vs = split(h @ t[q + "self_attn.v_proj.weight"].T + t[q + "self_attn.v_proj.bias"])
+        att = torch.softmax(qs @ ks.transpose(-1, -2) / math.sqrt(hd), dim=-1) @ vs
+        att = att.transpose(1, 2).reshape(batch, n, d)
+        x = x + att @ t[q + "self_attn.out_proj.weight"].T + t[q + "self_attn.out_proj.bias"]
+        h = _layer_norm(x, t[q + "final_layer_norm.weight"], t[q + "final_layer_norm.bias"], 1e-5)
+        h = torch.nn.functional.gelu(h @ t[q + "fc1.weight"].T + t[q + "fc1.bias"])
+        x = x + h @ t[q + "fc2.weight"].T + t[q + "fc2.bias"]
+    return _layer_norm(x, t[p + "layer_norm.weight"], t[p + "layer_norm.bias"], 1e-5)

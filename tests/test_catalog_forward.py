@@ -97,3 +97,18 @@ def test_t5_encoder_matches_transformers(tmp_path, ff):
     got = catalog_forward.t5_encoder(str(tmp_path), ids, mask)
     real = mask.bool()
     torch.testing.assert_close(got[real], want[real], rtol=1e-4, atol=1e-4)
+
+
+def test_whisper_encoder_matches_transformers(tmp_path):
+    t = transformers
+    cfg = t.WhisperConfig(d_model=32, encoder_layers=2, decoder_layers=1, encoder_attention_heads=4,
+                          decoder_attention_heads=4, encoder_ffn_dim=64, decoder_ffn_dim=64, vocab_size=60,
+                          num_mel_bins=16, max_source_positions=20, max_target_positions=10, pad_token_id=0,
+                          bos_token_id=1, eos_token_id=2, decoder_start_token_id=1)
+    torch.manual_seed(5)
+    model = t.WhisperForConditionalGeneration(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    features = torch.randn(2, 16, 40)
+    with torch.no_grad():
+        want = model.model.encoder(features).last_hidden_state
+    torch.testing.assert_close(catalog_forward.whisper_encoder(str(tmp_path), features), want, rtol=1e-4, atol=1e-4)
