@@ -11,6 +11,8 @@ will be tested against, and a CPU path for small encoders.
   positions, pre-norm layers, final LayerNorm): the rows its decoder cross-attends.
 - `clip`: CLIP's text and image embeddings (pre-norm towers with quick-GELU, the text tower's
   causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
+- `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
+  recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
 - `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
   recurrence it is (state[h] <- exp(dt A[h]) state[h] + dt x[h] B^T, y[h] = state[h] C + D[h] x[h]),
   the oracle of a future chunked (SSD) scan kernel.
@@ -327,3 +329,56 @@ def whisper_encoder(directory: str, features: torch.Tensor) -> torch.Tensor:
         h = torch.nn.functional.gelu(h @ t[q + "fc1.weight"].T + t[q + "fc1.bias"])
         x = x + h @ t[q + "fc2.weight"].T + t[q + "fc2.bias"]
     return _layer_norm(x, t[p + "layer_norm.weight"], t[p + "layer_norm.bias"], 1e-5)
+
+
+def _causal_conv(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    """Depthwise causal convolution of rows x [n, channels] with kernels w [channels, k], then SiLU."""
+    k = w.shape[1]
+    padded = torch.cat([torch.zeros(k - 1, x.shape[1]), x])
+    out = torch.stack([(padded[i : i + k] * w.T).sum(0) for i in range(x.shape[0])])
+    return torch.nn.functional.silu(out if b is None else out + b)
+
+
+def mamba(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a Mamba checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "mamba":
+        raise ValueError(f"{comp.architecture}: not a Mamba model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    eps = float(cfg.get("layer_norm_epsilon", 1e-5))
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["backbone.embeddings.weight"][ids]
+    for layer in range(int(cfg["num_hidden_layers"])):
+        p = f"backbone.layers.{layer}."
+        m = p + "mixer."
+        h = _rms(x, t[p + "norm.weight"], eps)
+        proj = h @ t[m + "in_proj.weight"].T
+        if m + "in_proj.bias" in t:
+            proj = proj + t[m + "in_proj.bias"]
+        xs, z = proj.chunk(2, dim=-1)
+        xs = _causal_conv(xs, t[m + "conv1d.weight"][:, 0, :], t.get(m + "conv1d.bias"))
+        a = -torch.exp(t[m + "A_log"])  # [inner, state]
+        state = a.shape[1]
+        rank = t[m + "dt_proj.weight"].shape[1]
+        dbc = xs @ t[m + "x_proj.weight"].T
+        dt, b, c = dbc.split([rank, state, state], dim=-1)
+        dt = torch.nn.functional.softplus(dt @ t[m + "dt_proj.weight"].T + t[m + "dt_proj.bias"])  # [n, inner]
+        s = torch.zeros_like(a)
+        ys = []
+        for i in range(n):
+            s = torch.exp(dt[i][:, None] * a) * s + (dt[i] * xs[i])[:, None] * b[i][None, :]
+            ys.append(s @ c[i] + t[m + "D"] * xs[i])
+        y = torch.stack(ys) * torch.nn.functional.silu(z)
+        out = y @ t[m + "out_proj.weight"].T
+        if m + "out_proj.bias" in t:
+            out = out + t[m + "out_proj.bias"]
+        x = x + out
+    x = _rms(x, t["backbone.norm_f.weight"], eps)
+    return x @ t.get("lm_head.weight", t["backbone.embeddings.weight"]).T

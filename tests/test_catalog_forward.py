@@ -112,3 +112,15 @@ def test_whisper_encoder_matches_transformers(tmp_path):
     with torch.no_grad():
         want = model.model.encoder(features).last_hidden_state
     torch.testing.assert_close(catalog_forward.whisper_encoder(str(tmp_path), features), want, rtol=1e-4, atol=1e-4)
+
+
+def test_mamba_selective_scan_matches_transformers(tmp_path):
+    t = transformers
+    cfg = t.MambaConfig(hidden_size=32, num_hidden_layers=2, vocab_size=60, state_size=8, expand=2, conv_kernel=4)
+    torch.manual_seed(6)
+    model = t.MambaForCausalLM(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 60, (1, 9))
+    with torch.no_grad():
+        want = model(input_ids=ids).logits[0]
+    torch.testing.assert_close(catalog_forward.mamba(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
