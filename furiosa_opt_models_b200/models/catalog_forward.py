@@ -13,6 +13,8 @@ will be tested against, and a CPU path for small encoders.
   causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
 - `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
   recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
+- `bamba`: a Bamba hybrid's logits: Mamba-2 mixers, and attention with partial RoPE at the
+  config's layers, each followed by a gated MLP.
 - `mamba2`: a Mamba-2 language model's logits, its selective scan run token by token as the
   recurrence it is (state[h] <- exp(dt A[h]) state[h] + dt x[h] B^T, y[h] = state[h] C + D[h] x[h]),
   the oracle of a future chunked (SSD) scan kernel.
@@ -116,49 +118,13 @@ def mamba2(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
     d = int(cfg["hidden_size"])
     inner = int(cfg.get("expand", 2)) * d
     heads, groups, state = int(cfg["num_heads"]), int(cfg.get("n_groups", 1)), int(cfg["state_size"])
-    head_dim = inner // heads
     eps = float(cfg.get("layer_norm_epsilon", 1e-5))
-    lo, hi = (cfg.get("time_step_limit") or (0.0, float("inf")))
-    lo = float(lo) if lo is not None else 0.0
-    hi = float(hi) if isinstance(hi, (int, float)) else float("inf")
-    ids = input_ids.long().view(-1)
-    n = ids.numel()
-    x = t["backbone.embeddings.weight"][ids]
+    lo, hi = _step_limit(cfg)
+    x = t["backbone.embeddings.weight"][input_ids.long().view(-1)]
     for layer in range(int(cfg["num_hidden_layers"])):
         p = f"backbone.layers.{layer}."
         m = p + "mixer."
-        h = _rms(x, t[p + "norm.weight"], eps)
-        proj = h @ t[m + "in_proj.weight"].T
-        if m + "in_proj.bias" in t:
-            proj = proj + t[m + "in_proj.bias"]
-        conv_dim = inner + 2 * groups * state
-        z, xbc, dt = proj.split([inner, conv_dim, heads], dim=-1)
-        # Causal depthwise convolution over the tokens, then SiLU.
-        w = t[m + "conv1d.weight"][:, 0, :]  # [conv_dim, kernel]
-        k = w.shape[1]
-        padded = torch.cat([torch.zeros(k - 1, conv_dim), xbc])
-        conv = torch.stack([(padded[i : i + k] * w.T).sum(0) for i in range(n)])
-        if m + "conv1d.bias" in t:
-            conv = conv + t[m + "conv1d.bias"]
-        conv = torch.nn.functional.silu(conv)
-        xs, bs, cs = conv.split([inner, groups * state, groups * state], dim=-1)
-        dt = torch.nn.functional.softplus(dt + t[m + "dt_bias"]).clamp(lo, hi)  # [n, heads]
-        a = -torch.exp(t[m + "A_log"])
-        s = torch.zeros(heads, head_dim, state)
-        ys = []
-        per = heads // groups
-        for i in range(n):
-            xh = xs[i].view(heads, head_dim)
-            b = bs[i].view(groups, state).repeat_interleave(per, dim=0)  # [heads, state]
-            c = cs[i].view(groups, state).repeat_interleave(per, dim=0)
-            s = s * torch.exp(dt[i] * a)[:, None, None] + (dt[i][:, None] * xh)[:, :, None] * b[:, None, :]
-            ys.append((s @ c[:, :, None])[..., 0] + t[m + "D"][:, None] * xh)
-        y = torch.stack(ys).reshape(n, inner)
-        y = _rms(y * torch.nn.functional.silu(z), t[m + "norm.weight"], eps)
-        out = y @ t[m + "out_proj.weight"].T
-        if m + "out_proj.bias" in t:
-            out = out + t[m + "out_proj.bias"]
-        x = x + out
+        x = x + _mamba2_mixer(t, m, _rms(x, t[p + "norm.weight"], eps), inner, heads, groups, state, eps, lo, hi)
     x = _rms(x, t["backbone.norm_f.weight"], eps)
     head = t.get("lm_head.weight", t["backbone.embeddings.weight"])
     return x @ head.T
@@ -382,3 +348,106 @@ def mamba(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
         x = x + out
     x = _rms(x, t["backbone.norm_f.weight"], eps)
     return x @ t.get("lm_head.weight", t["backbone.embeddings.weight"]).T
+
+
+def _mamba2_mixer(t, m, h, inner, heads, groups, state, eps, lo, hi):
+    """A Mamba-2 mixer (names under `m`) over normed rows h [n, d]: in_proj to z, x, B, C and dt, a
+    causal depthwise convolution and SiLU over x, B, C, the scan as its recurrence, the gated
+    RMSNorm and out_proj."""
+    n = h.shape[0]
+    head_dim = inner // heads
+    proj = h @ t[m + "in_proj.weight"].T
+    if m + "in_proj.bias" in t:
+        proj = proj + t[m + "in_proj.bias"]
+    conv_dim = inner + 2 * groups * state
+    z, xbc, dt = proj.split([inner, conv_dim, heads], dim=-1)
+    conv = _causal_conv(xbc, t[m + "conv1d.weight"][:, 0, :], t.get(m + "conv1d.bias"))
+    xs, bs, cs = conv.split([inner, groups * state, groups * state], dim=-1)
+    dt = torch.nn.functional.softplus(dt + t[m + "dt_bias"]).clamp(lo, hi)  # [n, heads]
+    a = -torch.exp(t[m + "A_log"])
+    s = torch.zeros(heads, head_dim, state)
+    ys = []
+    per = heads // groups
+    for i in range(n):
+        xh = xs[i].view(heads, head_dim)
+        b = bs[i].view(groups, state).repeat_interleave(per, dim=0)  # [heads, state]
+        c = cs[i].view(groups, state).repeat_interleave(per, dim=0)
+        s = s * torch.exp(dt[i] * a)[:, None, None] + (dt[i][:, None] * xh)[:, :, None] * b[:, None, :]
+        ys.append((s @ c[:, :, None])[..., 0] + t[m + "D"][:, None] * xh)
+    y = torch.stack(ys).reshape(n, inner)
+    y = _rms(y * torch.nn.functional.silu(z), t[m + "norm.weight"], eps)
+    out = y @ t[m + "out_proj.weight"].T
+    if m + "out_proj.bias" in t:
+        out = out + t[m + "out_proj.bias"]
+    return out
+
+
+def _step_limit(cfg) -> tuple[float, float]:
+    """The clamp of a Mamba-2 mixer's dt (`time_step_limit`, unbounded by default)."""
+    lo, hi = cfg.get("time_step_limit") or (0.0, float("inf"))
+    lo = float(lo) if isinstance(lo, (int, float)) else 0.0
+    hi = float(hi) if isinstance(hi, (int, float)) else float("inf")
+    return lo, hi
+
+
+def _rotate(x: torch.Tensor, theta: float, rot: int) -> torch.Tensor:
+    """RoPE (rotate-half pairing) of the first `rot` dims of x [n, heads, head], positions 0..n-1."""
+    inv = 1.0 / theta ** (torch.arange(0, rot, 2).float() / rot)
+    ang = torch.arange(x.shape[0]).float()[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1)[:, None, :]
+    sin = torch.cat([ang.sin(), ang.sin()], -1)[:, None, :]
+    xr, xp = x[..., :rot], x[..., rot:]
+    half = torch.cat([-xr[..., rot // 2 :], xr[..., : rot // 2]], -1)
+    return torch.cat([xr * cos + half * sin, xp], -1)
+
+
+def bamba(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a Bamba checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "bamba":
+        raise ValueError(f"{comp.architecture}: not a Bamba model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    d = int(cfg["hidden_size"])
+    heads = int(cfg["num_attention_heads"])
+    kv = int(cfg.get("num_key_value_heads", heads))
+    hd = d // heads
+    inner = int(cfg.get("mamba_expand", 2)) * d
+    eps = float(cfg.get("rms_norm_eps", 1e-5))
+    rope = cfg.get("rope_parameters") or {}
+    theta = float(rope.get("rope_theta", cfg.get("rope_theta", 10000.0)))
+    # The rotated prefix of each head: `attn_rotary_emb` dims (the original Bamba config key), else
+    # head_dim x partial_rotary_factor (the top-level key, else the one in rope_parameters).
+    factor = cfg.get("partial_rotary_factor", rope.get("partial_rotary_factor", 0.5))
+    rot = int(cfg.get("attn_rotary_emb") or hd * float(factor))
+    attention = set(cfg.get("attn_layer_indices") or [])
+    lo, hi = _step_limit(cfg)
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["model.embed_tokens.weight"][ids]
+    causal = torch.triu(torch.full((n, n), float("-inf")), 1)
+    for layer in range(int(cfg["num_hidden_layers"])):
+        p = f"model.layers.{layer}."
+        h = _rms(x, t[p + "input_layernorm.weight"], eps)
+        if layer in attention:
+            q = _rotate((h @ t[p + "self_attn.q_proj.weight"].T).view(n, heads, hd), theta, rot)
+            k = _rotate((h @ t[p + "self_attn.k_proj.weight"].T).view(n, kv, hd), theta, rot)
+            v = (h @ t[p + "self_attn.v_proj.weight"].T).view(n, kv, hd)
+            k, v = (z.repeat_interleave(heads // kv, dim=1) for z in (k, v))
+            att = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(hd) + causal, dim=-1)
+            out = torch.einsum("hqk,khd->qhd", att, v).reshape(n, heads * hd) @ t[p + "self_attn.o_proj.weight"].T
+        else:
+            out = _mamba2_mixer(t, p + "mamba.", h, inner, int(cfg["mamba_n_heads"]), int(cfg.get("mamba_n_groups", 1)),
+                                int(cfg.get("mamba_d_state", 256)), eps, lo, hi)
+        x = x + out
+        h = _rms(x, t[p + "pre_ff_layernorm.weight"], eps)
+        f = p + "feed_forward."
+        x = x + (torch.nn.functional.silu(h @ t[f + "gate_proj.weight"].T) * (h @ t[f + "up_proj.weight"].T)) @ \
+            t[f + "down_proj.weight"].T
+    x = _rms(x, t["model.final_layernorm.weight"], eps)
+    return x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T

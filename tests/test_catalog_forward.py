@@ -124,3 +124,32 @@ def test_mamba_selective_scan_matches_transformers(tmp_path):
     with torch.no_grad():
         want = model(input_ids=ids).logits[0]
     torch.testing.assert_close(catalog_forward.mamba(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
+
+
+def test_bamba_hybrid_matches_transformers(tmp_path):
+    """transformers (this version) rotates whole heads whatever partial_rotary_factor says, so the
+    checkpoint declares whole-head rotation (attn_rotary_emb = head_dim) for the comparison; the
+    prefix rotation of the published configs is checked on its own below."""
+    t = transformers
+    cfg = t.BambaConfig(hidden_size=32, num_hidden_layers=3, vocab_size=60, num_attention_heads=4, num_key_value_heads=2,
+                        intermediate_size=64, attn_layer_indices=[1], mamba_n_heads=8, mamba_d_head=8, mamba_n_groups=2,
+                        mamba_d_state=8, mamba_expand=2, mamba_chunk_size=4)
+    torch.manual_seed(7)
+    model = t.BambaForCausalLM(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    import json
+
+    conf = json.loads((tmp_path / "config.json").read_text())
+    (tmp_path / "config.json").write_text(json.dumps(dict(conf, attn_rotary_emb=8)))
+    ids = torch.randint(0, 60, (1, 10))
+    with torch.no_grad():
+        want = model(input_ids=ids, use_cache=False).logits[0]
+    torch.testing.assert_close(catalog_forward.bamba(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
+
+
+def test_partial_rotation_rotates_the_prefix_only():
+    x = torch.randn(6, 2, 8)
+    part = catalog_forward._rotate(x, 10000.0, 4)
+    assert torch.equal(part[..., 4:], x[..., 4:])
+    torch.testing.assert_close(part[..., :4], catalog_forward._rotate(x[..., :4].contiguous(), 10000.0, 4))
+    torch.testing.assert_close(part[0], x[0])  # position 0 is not rotated
