@@ -11,6 +11,9 @@ will be tested against, and a CPU path for small encoders.
   positions, pre-norm layers, final LayerNorm): the rows its decoder cross-attends.
 - `clip`: CLIP's text and image embeddings (pre-norm towers with quick-GELU, the text tower's
   causal mask and end-of-text row, the image tower's class row, the projections), L2-normalised.
+- `gemma3`: a Gemma-3 text decoder's logits (scaled embedding, RMSNorms with a (1 + weight) scale
+  around attention and MLP, QK RMSNorm, global layers and sliding-window layers with their own
+  RoPE bases, GeGLU MLP).
 - `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
   recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
 - `bamba`: a Bamba hybrid's logits: Mamba-2 mixers, and attention with partial RoPE at the
@@ -451,3 +454,59 @@ def bamba(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
             t[f + "down_proj.weight"].T
     x = _rms(x, t["model.final_layernorm.weight"], eps)
     return x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
+
+
+def gemma3(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a Gemma-3 text checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "gemma3_text":
+        raise ValueError(f"{comp.architecture}: not a Gemma-3 text model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    d, L = int(cfg["hidden_size"]), int(cfg["num_hidden_layers"])
+    heads = int(cfg["num_attention_heads"])
+    kv = int(cfg.get("num_key_value_heads", heads))
+    hd = int(cfg.get("head_dim", 256))
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    window = int(cfg.get("sliding_window", 4096))
+    scale = float(cfg.get("query_pre_attn_scalar", hd)) ** -0.5
+    rope = cfg.get("rope_parameters") or {}
+    theta = {"full_attention": float((rope.get("full_attention") or {}).get("rope_theta", cfg.get("rope_theta", 1e6))),
+             "sliding_attention": float((rope.get("sliding_attention") or {}).get(
+                 "rope_theta", cfg.get("rope_local_base_freq", 1e4)))}
+    types = cfg.get("layer_types") or ["full_attention" if (i + 1) % int(cfg.get("sliding_window_pattern", 6)) == 0
+                                       else "sliding_attention" for i in range(L)]
+
+    def norm(x, w):
+        return (x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)) * (1.0 + w)
+
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["model.embed_tokens.weight"][ids] * torch.tensor(d ** 0.5)
+    i, j = torch.arange(n)[:, None], torch.arange(n)[None, :]
+    masks = {"full_attention": torch.where(j <= i, 0.0, float("-inf")),
+             "sliding_attention": torch.where((j <= i) & (j > i - window), 0.0, float("-inf"))}
+    for layer in range(L):
+        p = f"model.layers.{layer}."
+        kind = types[layer]
+        h = norm(x, t[p + "input_layernorm.weight"])
+        q = norm((h @ t[p + "self_attn.q_proj.weight"].T).view(n, heads, hd), t[p + "self_attn.q_norm.weight"])
+        k = norm((h @ t[p + "self_attn.k_proj.weight"].T).view(n, kv, hd), t[p + "self_attn.k_norm.weight"])
+        v = (h @ t[p + "self_attn.v_proj.weight"].T).view(n, kv, hd)
+        q, k = _rotate(q, theta[kind], hd), _rotate(k, theta[kind], hd)
+        k, v = (z.repeat_interleave(heads // kv, dim=1) for z in (k, v))
+        att = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) * scale + masks[kind], dim=-1)
+        out = torch.einsum("hqk,khd->qhd", att, v).reshape(n, heads * hd) @ t[p + "self_attn.o_proj.weight"].T
+        x = x + norm(out, t[p + "post_attention_layernorm.weight"])
+        h = norm(x, t[p + "pre_feedforward_layernorm.weight"])
+        mid = torch.nn.functional.gelu(h @ t[p + "mlp.gate_proj.weight"].T, approximate="tanh") * (h @ t[p + "mlp.up_proj.weight"].T)
+        x = x + norm(mid @ t[p + "mlp.down_proj.weight"].T, t[p + "post_feedforward_layernorm.weight"])
+    x = norm(x, t["model.norm.weight"])
+    logits = x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
+    cap = cfg.get("final_logit_softcapping")
+    return logits if not cap else torch.tanh(logits / cap) * cap

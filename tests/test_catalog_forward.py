@@ -153,3 +153,21 @@ def test_partial_rotation_rotates_the_prefix_only():
     assert torch.equal(part[..., 4:], x[..., 4:])
     torch.testing.assert_close(part[..., :4], catalog_forward._rotate(x[..., :4].contiguous(), 10000.0, 4))
     torch.testing.assert_close(part[0], x[0])  # position 0 is not rotated
+
+
+def test_gemma3_text_matches_transformers(tmp_path):
+    t = transformers
+    cfg = t.Gemma3TextConfig(hidden_size=32, num_hidden_layers=4, vocab_size=60, num_attention_heads=4,
+                             num_key_value_heads=2, head_dim=8, intermediate_size=64, sliding_window=4,
+                             layer_types=["sliding_attention", "full_attention"] * 2, max_position_embeddings=64)
+    torch.manual_seed(8)
+    model = t.Gemma3ForCausalLM(cfg).eval()
+    with torch.no_grad():  # norms start at zero scale: give them values
+        for name, prm in model.named_parameters():
+            if "norm" in name:
+                prm.uniform_(-0.5, 0.5)
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 60, (1, 12))
+    with torch.no_grad():
+        want = model(input_ids=ids, use_cache=False).logits[0]
+    torch.testing.assert_close(catalog_forward.gemma3(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
