@@ -14,6 +14,9 @@ will be tested against, and a CPU path for small encoders.
 - `gemma3`: a Gemma-3 text decoder's logits (scaled embedding, RMSNorms with a (1 + weight) scale
   around attention and MLP, QK RMSNorm, global layers and sliding-window layers with their own
   RoPE bases, GeGLU MLP).
+- `gemma4`: a Gemma-4 text decoder's logits (per-layer input embeddings gated into every layer,
+  wider global heads with proportional RoPE, unscaled QK-normed attention, value RMSNorm, keys as
+  values where configured, a learned scalar a layer); the mixture-of-experts block is not covered.
 - `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
   recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
 - `bamba`: a Bamba hybrid's logits: Mamba-2 mixers, and attention with partial RoPE at the
@@ -506,6 +509,100 @@ def gemma3(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
         h = norm(x, t[p + "pre_feedforward_layernorm.weight"])
         mid = torch.nn.functional.gelu(h @ t[p + "mlp.gate_proj.weight"].T, approximate="tanh") * (h @ t[p + "mlp.up_proj.weight"].T)
         x = x + norm(mid @ t[p + "mlp.down_proj.weight"].T, t[p + "post_feedforward_layernorm.weight"])
+    x = norm(x, t["model.norm.weight"])
+    logits = x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
+    cap = cfg.get("final_logit_softcapping")
+    return logits if not cap else torch.tanh(logits / cap) * cap
+
+
+def _rotate_freqs(x: torch.Tensor, inv: torch.Tensor) -> torch.Tensor:
+    """Rotate-half RoPE of x [n, heads, head] with the inverse frequencies `inv` [head / 2]
+    (zeros leave their pairs unrotated), positions 0..n-1."""
+    ang = torch.arange(x.shape[0]).float()[:, None] * inv[None, :]
+    cos = torch.cat([ang.cos(), ang.cos()], -1)[:, None, :]
+    sin = torch.cat([ang.sin(), ang.sin()], -1)[:, None, :]
+    h = x.shape[-1] // 2
+    return x * cos + torch.cat([-x[..., h:], x[..., :h]], -1) * sin
+
+
+def _inv_freq(params: dict, head: int) -> torch.Tensor:
+    theta = float(params.get("rope_theta", 10000.0))
+    if params.get("rope_type", "default") == "proportional":
+        # Only the first partial_rotary_factor of the head's frequencies turn, at the whole head's
+        # spacing; the other pairs keep frequency zero.
+        turning = int(head * float(params.get("partial_rotary_factor", 1.0))) // 2
+        inv = torch.zeros(head // 2)
+        inv[:turning] = 1.0 / theta ** (torch.arange(0, 2 * turning, 2).float() / head)
+        return inv
+    return 1.0 / theta ** (torch.arange(0, head, 2).float() / head)
+
+
+def gemma4(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a Gemma-4 text checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "gemma4_text":
+        raise ValueError(f"{comp.architecture}: not a Gemma-4 text model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    if cfg.get("enable_moe_block"):
+        raise NotImplementedError("enable_moe_block: the host forward does not cover the expert block")
+    t = load_tensors(directory)
+    d, L = int(cfg["hidden_size"]), int(cfg["num_hidden_layers"])
+    heads = int(cfg["num_attention_heads"])
+    kv = int(cfg.get("num_key_value_heads", heads))
+    hd = int(cfg.get("head_dim", 256))
+    ghd = int(cfg.get("global_head_dim") or hd)
+    gkv = int(cfg.get("num_global_key_value_heads") or kv)
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    window = int(cfg.get("sliding_window", 512))
+    k_eq_v = bool(cfg.get("attention_k_eq_v"))
+    ple = int(cfg.get("hidden_size_per_layer_input") or 0)
+    rope = cfg.get("rope_parameters") or {}
+    types = cfg["layer_types"]
+
+    def norm(x, w=None):
+        y = x * (x.pow(2).mean(-1, keepdim=True) + eps) ** -0.5
+        return y if w is None else y * w
+
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["model.embed_tokens.weight"][ids] * torch.tensor(d ** 0.5)
+    if ple:
+        per = t["model.embed_tokens_per_layer.weight"][ids].view(n, L, ple) * torch.tensor(ple ** 0.5)
+        proj = (x @ t["model.per_layer_model_projection.weight"].T * d ** -0.5).view(n, L, ple)
+        per = (norm(proj, t["model.per_layer_projection_norm.weight"]) + per) * 2 ** -0.5
+    i, j = torch.arange(n)[:, None], torch.arange(n)[None, :]
+    masks = {"full_attention": torch.where(j <= i, 0.0, float("-inf")),
+             "sliding_attention": torch.where((j <= i) & (j > i - window), 0.0, float("-inf"))}
+    for layer in range(L):
+        p = f"model.layers.{layer}."
+        kind = types[layer]
+        full = kind == "full_attention"
+        h_dim = ghd if full else hd
+        nkv = gkv if (k_eq_v and full) else kv
+        inv = _inv_freq(rope.get(kind, {}), h_dim)
+        h = norm(x, t[p + "input_layernorm.weight"])
+        q = _rotate_freqs(norm((h @ t[p + "self_attn.q_proj.weight"].T).view(n, heads, h_dim),
+                               t[p + "self_attn.q_norm.weight"]), inv)
+        k_raw = (h @ t[p + "self_attn.k_proj.weight"].T).view(n, nkv, h_dim)
+        v_raw = k_raw if (k_eq_v and full) else (h @ t[p + "self_attn.v_proj.weight"].T).view(n, nkv, h_dim)
+        k = _rotate_freqs(norm(k_raw, t[p + "self_attn.k_norm.weight"]), inv)
+        v = norm(v_raw)
+        k, v = (z.repeat_interleave(heads // nkv, dim=1) for z in (k, v))
+        att = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) + masks[kind], dim=-1)
+        out = torch.einsum("hqk,khd->qhd", att, v).reshape(n, heads * h_dim) @ t[p + "self_attn.o_proj.weight"].T
+        x = x + norm(out, t[p + "post_attention_layernorm.weight"])
+        h = norm(x, t[p + "pre_feedforward_layernorm.weight"])
+        mid = torch.nn.functional.gelu(h @ t[p + "mlp.gate_proj.weight"].T, approximate="tanh") * (h @ t[p + "mlp.up_proj.weight"].T)
+        x = x + norm(mid @ t[p + "mlp.down_proj.weight"].T, t[p + "post_feedforward_layernorm.weight"])
+        if ple:
+            g = torch.nn.functional.gelu(x @ t[p + "per_layer_input_gate.weight"].T, approximate="tanh") * per[:, layer]
+            x = x + norm(g @ t[p + "per_layer_projection.weight"].T, t[p + "post_per_layer_input_norm.weight"])
+        x = x * t[p + "layer_scalar"]
     x = norm(x, t["model.norm.weight"])
     logits = x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
     cap = cfg.get("final_logit_softcapping")

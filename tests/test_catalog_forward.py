@@ -171,3 +171,26 @@ def test_gemma3_text_matches_transformers(tmp_path):
     with torch.no_grad():
         want = model(input_ids=ids, use_cache=False).logits[0]
     torch.testing.assert_close(catalog_forward.gemma3(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
+
+
+@pytest.mark.parametrize("k_eq_v", [False, True])
+def test_gemma4_text_matches_transformers(tmp_path, k_eq_v):
+    t = transformers
+    cfg = t.Gemma4TextConfig(hidden_size=32, num_hidden_layers=4, vocab_size=60, num_attention_heads=4,
+                             num_key_value_heads=2, head_dim=8, global_head_dim=16, intermediate_size=64,
+                             hidden_size_per_layer_input=8, vocab_size_per_layer_input=30, sliding_window=4,
+                             attention_k_eq_v=k_eq_v, num_global_key_value_heads=1 if k_eq_v else None,
+                             layer_types=["sliding_attention", "full_attention"] * 2)
+    torch.manual_seed(9)
+    model = t.Gemma4ForCausalLM(cfg).eval()
+    with torch.no_grad():
+        for name, prm in model.named_parameters():
+            if "norm" in name:
+                prm.uniform_(0.5, 1.5)
+        for layer in model.model.layers:
+            layer.layer_scalar.fill_(0.9)
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 30, (1, 12))
+    with torch.no_grad():
+        want = model(input_ids=ids, use_cache=False).logits[0]
+    torch.testing.assert_close(catalog_forward.gemma4(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
