@@ -17,6 +17,8 @@ will be tested against, and a CPU path for small encoders.
 - `gemma4`: a Gemma-4 text decoder's logits (per-layer input embeddings gated into every layer,
   wider global heads with proportional RoPE, unscaled QK-normed attention, value RMSNorm, keys as
   values where configured, a learned scalar a layer); the mixture-of-experts block is not covered.
+- `olmoe`: an OLMoE mixture-of-experts decoder's logits (RMSNorm over the whole q and k
+  projections, softmax router, top-k experts combined by their probabilities).
 - `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
   recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
 - `bamba`: a Bamba hybrid's logits: Mamba-2 mixers, and attention with partial RoPE at the
@@ -607,3 +609,57 @@ def gemma4(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
     logits = x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
     cap = cfg.get("final_logit_softcapping")
     return logits if not cap else torch.tanh(logits / cap) * cap
+
+
+def olmoe(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of an OLMoE checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "olmoe":
+        raise ValueError(f"{comp.architecture}: not an OLMoE model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    d, L = int(cfg["hidden_size"]), int(cfg["num_hidden_layers"])
+    heads = int(cfg["num_attention_heads"])
+    kv = int(cfg.get("num_key_value_heads", heads))
+    hd = d // heads
+    eps = float(cfg.get("rms_norm_eps", 1e-5))
+    experts, top = int(cfg["num_experts"]), int(cfg.get("num_experts_per_tok", 8))
+    theta = float((cfg.get("rope_parameters") or {}).get("rope_theta", cfg.get("rope_theta", 10000.0)))
+    inv = 1.0 / theta ** (torch.arange(0, hd, 2).float() / hd)
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["model.embed_tokens.weight"][ids]
+    causal = torch.triu(torch.full((n, n), float("-inf")), 1)
+    for layer in range(L):
+        p = f"model.layers.{layer}."
+        h = _rms(x, t[p + "input_layernorm.weight"], eps)
+        q = _rms(h @ t[p + "self_attn.q_proj.weight"].T, t[p + "self_attn.q_norm.weight"], eps).view(n, heads, hd)
+        k = _rms(h @ t[p + "self_attn.k_proj.weight"].T, t[p + "self_attn.k_norm.weight"], eps).view(n, kv, hd)
+        v = (h @ t[p + "self_attn.v_proj.weight"].T).view(n, kv, hd)
+        q, k = _rotate_freqs(q, inv), _rotate_freqs(k, inv)
+        k, v = (z.repeat_interleave(heads // kv, dim=1) for z in (k, v))
+        att = torch.softmax(torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(hd) + causal, dim=-1)
+        x = x + torch.einsum("hqk,khd->qhd", att, v).reshape(n, d) @ t[p + "self_attn.o_proj.weight"].T
+        h = _rms(x, t[p + "post_attention_layernorm.weight"], eps)
+        probs = torch.softmax(h @ t[p + "mlp.gate.weight"].T, dim=-1)
+        weights, chosen = probs.topk(top, dim=-1)
+        if cfg.get("norm_topk_prob"):
+            weights = weights / weights.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for e in range(experts):
+            rows, slot = (chosen == e).nonzero(as_tuple=True)
+            if rows.numel() == 0:
+                continue
+            q_ = f"{p}mlp.experts.{e}."
+            he = h[rows]
+            y = (torch.nn.functional.silu(he @ t[q_ + "gate_proj.weight"].T) * (he @ t[q_ + "up_proj.weight"].T)) @ \
+                t[q_ + "down_proj.weight"].T
+            out.index_add_(0, rows, y * weights[rows, slot][:, None])
+        x = x + out
+    x = _rms(x, t["model.norm.weight"], eps)
+    return x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T

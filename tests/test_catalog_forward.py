@@ -194,3 +194,18 @@ def test_gemma4_text_matches_transformers(tmp_path, k_eq_v):
     with torch.no_grad():
         want = model(input_ids=ids, use_cache=False).logits[0]
     torch.testing.assert_close(catalog_forward.gemma4(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
+
+
+@pytest.mark.parametrize("norm_topk", [False, True])
+def test_olmoe_matches_transformers(tmp_path, norm_topk):
+    t = transformers
+    cfg = t.OlmoeConfig(hidden_size=32, num_hidden_layers=2, vocab_size=50, num_attention_heads=4,
+                        num_key_value_heads=2, intermediate_size=16, num_experts=4, num_experts_per_tok=2,
+                        norm_topk_prob=norm_topk)
+    torch.manual_seed(10)
+    model = t.OlmoeForCausalLM(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 50, (1, 9))
+    with torch.no_grad():
+        want = model(input_ids=ids, use_cache=False).logits[0]
+    torch.testing.assert_close(catalog_forward.olmoe(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
