@@ -19,6 +19,9 @@ will be tested against, and a CPU path for small encoders.
   values where configured, a learned scalar a layer); the mixture-of-experts block is not covered.
 - `olmoe`: an OLMoE mixture-of-experts decoder's logits (RMSNorm over the whole q and k
   projections, softmax router, top-k experts combined by their probabilities).
+- `deepseek_v2`: a DeepSeek-V2 decoder's logits (multi-head latent attention: low-rank KV with a
+  shared rotary key, optional low-rank queries, interleaved RoPE on the rotary dims; routed experts
+  by greedy or group-limited top-k, scaled, plus shared experts after the first dense layers).
 - `mamba`: a Mamba (1) language model's logits, its selective scan run as the per-channel
   recurrence (state[c] <- exp(dt[c] A[c]) state[c] + dt[c] x[c] B, y[c] = state[c] C + D[c] x[c]).
 - `bamba`: a Bamba hybrid's logits: Mamba-2 mixers, and attention with partial RoPE at the
@@ -661,5 +664,89 @@ def olmoe(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
                 t[q_ + "down_proj.weight"].T
             out.index_add_(0, rows, y * weights[rows, slot][:, None])
         x = x + out
+    x = _rms(x, t["model.norm.weight"], eps)
+    return x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T
+
+
+def _rotate_pairs(x: torch.Tensor, inv: torch.Tensor) -> torch.Tensor:
+    """RoPE on adjacent pairs (2i, 2i + 1) of x [n, heads, dims], positions 0..n-1."""
+    ang = torch.arange(x.shape[0]).float()[:, None] * inv[None, :]
+    cos, sin = ang.cos()[:, None, :], ang.sin()[:, None, :]
+    a, b = x[..., 0::2], x[..., 1::2]
+    return torch.stack([a * cos - b * sin, a * sin + b * cos], dim=-1).flatten(-2)
+
+
+def deepseek_v2(directory: str, input_ids: torch.Tensor) -> torch.Tensor:
+    """Logits [tokens, vocab] of a DeepSeek-V2 checkpoint for one sequence of `input_ids`."""
+    import furiosa_opt_engine as engine
+
+    from . import catalog
+
+    comp = catalog.compose(engine.Checkpoint(directory))
+    if comp.family != "deepseek_v2":
+        raise ValueError(f"{comp.architecture}: not a DeepSeek-V2 model")
+    with open(os.path.join(directory, "config.json")) as f:
+        cfg = json.load(f)
+    t = load_tensors(directory)
+    L, heads = int(cfg["num_hidden_layers"]), int(cfg["num_attention_heads"])
+    nope, rope_d, vd = int(cfg["qk_nope_head_dim"]), int(cfg["qk_rope_head_dim"]), int(cfg["v_head_dim"])
+    kv_rank = int(cfg["kv_lora_rank"])
+    eps = float(cfg.get("rms_norm_eps", 1e-6))
+    experts, top = int(cfg.get("n_routed_experts") or 0), int(cfg.get("num_experts_per_tok") or 0)
+    dense, freq = int(cfg.get("first_k_dense_replace") or 0), int(cfg.get("moe_layer_freq") or 1)
+    scale_out = float(cfg.get("routed_scaling_factor") or 1.0)
+    method = cfg.get("topk_method") or "greedy"
+    theta = float((cfg.get("rope_parameters") or {}).get("rope_theta", cfg.get("rope_theta", 10000.0)))
+    inv = 1.0 / theta ** (torch.arange(0, rope_d, 2).float() / rope_d)
+    ids = input_ids.long().view(-1)
+    n = ids.numel()
+    x = t["model.embed_tokens.weight"][ids]
+    causal = torch.triu(torch.full((n, n), float("-inf")), 1)
+
+    def mlp(prefix, h):
+        return (torch.nn.functional.silu(h @ t[prefix + "gate_proj.weight"].T) * (h @ t[prefix + "up_proj.weight"].T)) @ \
+            t[prefix + "down_proj.weight"].T
+
+    for layer in range(L):
+        p = f"model.layers.{layer}."
+        a = p + "self_attn."
+        h = _rms(x, t[p + "input_layernorm.weight"], eps)
+        if a + "q_a_proj.weight" in t:
+            q = _rms(h @ t[a + "q_a_proj.weight"].T, t[a + "q_a_layernorm.weight"], eps) @ t[a + "q_b_proj.weight"].T
+        else:
+            q = h @ t[a + "q_proj.weight"].T
+        q = q.view(n, heads, nope + rope_d)
+        q_nope, q_pe = q.split([nope, rope_d], dim=-1)
+        ckv = h @ t[a + "kv_a_proj_with_mqa.weight"].T
+        latent, k_pe = ckv.split([kv_rank, rope_d], dim=-1)
+        kvb = (_rms(latent, t[a + "kv_a_layernorm.weight"], eps) @ t[a + "kv_b_proj.weight"].T).view(n, heads, nope + vd)
+        k_nope, v = kvb.split([nope, vd], dim=-1)
+        q_pe = _rotate_pairs(q_pe, inv)
+        k_pe = _rotate_pairs(k_pe.view(n, 1, rope_d), inv).expand(n, heads, rope_d)
+        qs, ks = torch.cat([q_nope, q_pe], -1), torch.cat([k_nope, k_pe], -1)
+        att = torch.softmax(torch.einsum("qhd,khd->hqk", qs, ks) / math.sqrt(nope + rope_d) + causal, dim=-1)
+        x = x + torch.einsum("hqk,khd->qhd", att, v).reshape(n, heads * vd) @ t[a + "o_proj.weight"].T
+        h = _rms(x, t[p + "post_attention_layernorm.weight"], eps)
+        if experts and layer >= dense and layer % freq == 0:
+            probs = torch.softmax(h @ t[p + "mlp.gate.weight"].T, dim=-1)
+            if method == "group_limited_greedy":
+                groups, keep = int(cfg["n_group"]), int(cfg["topk_group"])
+                best = probs.view(n, groups, -1).max(-1).values.topk(keep, dim=-1).indices
+                allowed = torch.zeros(n, groups).scatter_(1, best, 1.0).repeat_interleave(experts // groups, dim=1)
+                probs_masked = probs.masked_fill(allowed == 0, 0.0)
+                weights, chosen = probs_masked.topk(top, dim=-1)
+            else:
+                weights, chosen = probs.topk(top, dim=-1)
+            weights = weights * scale_out
+            out = torch.zeros_like(x)
+            for e in range(experts):
+                rows, slot = (chosen == e).nonzero(as_tuple=True)
+                if rows.numel():
+                    out.index_add_(0, rows, mlp(f"{p}mlp.experts.{e}.", h[rows]) * weights[rows, slot][:, None])
+            if p + "mlp.shared_experts.gate_proj.weight" in t:
+                out = out + mlp(p + "mlp.shared_experts.", h)
+            x = x + out
+        else:
+            x = x + mlp(p + "mlp.", h)
     x = _rms(x, t["model.norm.weight"], eps)
     return x @ t.get("lm_head.weight", t["model.embed_tokens.weight"]).T

@@ -209,3 +209,19 @@ def test_olmoe_matches_transformers(tmp_path, norm_topk):
     with torch.no_grad():
         want = model(input_ids=ids, use_cache=False).logits[0]
     torch.testing.assert_close(catalog_forward.olmoe(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
+
+
+@pytest.mark.parametrize("q_rank", [24, None])
+def test_deepseek_v2_matches_transformers(tmp_path, q_rank):
+    t = transformers
+    cfg = t.DeepseekV2Config(hidden_size=32, num_hidden_layers=3, vocab_size=50, num_attention_heads=4,
+                             num_key_value_heads=4, intermediate_size=64, moe_intermediate_size=16, n_routed_experts=4,
+                             n_shared_experts=2, num_experts_per_tok=2, first_k_dense_replace=1, q_lora_rank=q_rank,
+                             kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=4, v_head_dim=8)
+    torch.manual_seed(11)
+    model = t.DeepseekV2ForCausalLM(cfg).eval()
+    model.save_pretrained(str(tmp_path))
+    ids = torch.randint(0, 50, (1, 9))
+    with torch.no_grad():
+        want = model(input_ids=ids, use_cache=False).logits[0]
+    torch.testing.assert_close(catalog_forward.deepseek_v2(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
