@@ -211,13 +211,16 @@ def test_olmoe_matches_transformers(tmp_path, norm_topk):
     torch.testing.assert_close(catalog_forward.olmoe(str(tmp_path), ids[0]), want, rtol=2e-4, atol=2e-4)
 
 
-@pytest.mark.parametrize("q_rank", [24, None])
-def test_deepseek_v2_matches_transformers(tmp_path, q_rank):
+# transformers' own group-limited routing does not run in this version, so only greedy routing has
+# an oracle here.
+@pytest.mark.parametrize(("q_rank", "method"), [(24, "greedy"), (None, "greedy")])
+def test_deepseek_v2_matches_transformers(tmp_path, q_rank, method):
     t = transformers
     cfg = t.DeepseekV2Config(hidden_size=32, num_hidden_layers=3, vocab_size=50, num_attention_heads=4,
-                             num_key_value_heads=4, intermediate_size=64, moe_intermediate_size=16, n_routed_experts=4,
+                             num_key_value_heads=4, intermediate_size=64, moe_intermediate_size=16, n_routed_experts=8,
                              n_shared_experts=2, num_experts_per_tok=2, first_k_dense_replace=1, q_lora_rank=q_rank,
-                             kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=4, v_head_dim=8)
+                             kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=4, v_head_dim=8, topk_method=method,
+                             n_group=4, topk_group=2, routed_scaling_factor=1.5)
     torch.manual_seed(11)
     model = t.DeepseekV2ForCausalLM(cfg).eval()
     model.save_pretrained(str(tmp_path))
